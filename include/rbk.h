@@ -1,0 +1,330 @@
+/*
+ * rbk.h — C ABI of the B200 (sm_100a) backward-pass library for
+ * rubidium-train (librbk.so).
+ *
+ * Conventions (all entry points):
+ *   - extern "C", plain pointers and sizes; device pointers unless stated.
+ *   - every call takes the CUDA stream it launches on (`stream`, a
+ *     cudaStream_t passed as void*; NULL = legacy default stream) and returns
+ *     an int status: RBK_OK (0) or a negative RBK_ERR_* code.  Nothing calls
+ *     exit(); rbk_last_error() holds a message for the calling thread.
+ *   - "half" tensors are IEEE binary16 (the reference's FP16 activations and
+ *     weights, src/model.h:29-55); "float" tensors are FP32.
+ *   - the caller owns every buffer.  Scratch comes from the rbk_ctx, which
+ *     allocates it on first use at a given size (never during a call that
+ *     already had enough) and keeps it until rbk_ctx_destroy.
+ *   - one rbk_ctx per host thread / stream; calls on one ctx are not
+ *     thread-safe.
+ *
+ * Each entry point names the reference interface it replaces; reference paths
+ * are relative to the rubidium-train project.
+ */
+#ifndef RBK_H
+#define RBK_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "rbk_layout.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RBK_OK 0
+#define RBK_ERR_INVALID (-1)      /* bad argument (shape, alignment, null)   */
+#define RBK_ERR_CUDA (-2)         /* a CUDA runtime / driver call failed      */
+#define RBK_ERR_UNSUPPORTED (-3)  /* device is not sm_100 or shape unsupported */
+#define RBK_ERR_TIMEOUT (-4)      /* a bounded device-side wait ran out       */
+#define RBK_ERR_NCCL (-5)         /* an NCCL call failed                      */
+#define RBK_ERR_NOMEM (-6)        /* device allocation failed                 */
+
+typedef struct rbk_ctx rbk_ctx;
+
+/* Message of the last failing call on this thread ("" when none). */
+const char* rbk_last_error(void);
+/* Library ABI version (bumped on incompatible changes). */
+int rbk_version(void);
+
+/* Context: device binding + scratch arena.  Fails with RBK_ERR_UNSUPPORTED on
+ * anything but a compute capability 10.0 device.
+ * Replaces init_handles()/MemPool (src/cuda_kernels.cuh:30,46-57). */
+int rbk_ctx_create(rbk_ctx** out, int device);
+int rbk_ctx_destroy(rbk_ctx* ctx);
+
+/* ------------------------------------------------------------------------
+ * LayerNorm
+ * ------------------------------------------------------------------------ */
+
+/* y = gamma * (x - mean) * rstd + beta, per row of [N, D] half; mean/rstd FP32
+ * [N] out (biased variance, eps).  gamma/beta half [D].  D % 8 == 0, D <= 8192.
+ * Replaces layer_norm_fp16_forward (src/cuda_kernels.cuh:99-101). */
+int rbk_ln_fwd(rbk_ctx* ctx, void* y, float* mean, float* rstd, const void* x, const void* gamma,
+               const void* beta, int N, int D, float eps, void* stream);
+
+#define RBK_LN_REFERENCE_FORMULA 1  /* dx as src/cpu_mat.h:146 (one rstd factor short) */
+
+/* LayerNorm backward over [N, D] half.
+ *   dx      = dres + LN'(dy)      (dres optional: the residual-stream branch)
+ *   dgamma += sum_rows dy * xhat,  dbeta += sum_rows dy        (FP32 [D])
+ *   dbias_out (optional) += sum_rows dx  (FP32 [D]; the bias gradient of the
+ *            linear layer whose output is this residual stream)
+ * dx is the exact gradient unless flags has RBK_LN_REFERENCE_FORMULA.
+ * Column sums are reduced deterministically through ctx scratch.
+ * Replaces layer_norm_fp16_backward (src/cuda_kernels.cuh:102-104). */
+int rbk_ln_bwd(rbk_ctx* ctx, void* dx, float* dgamma, float* dbeta, float* dbias_out, const void* dy,
+               const void* dres, const void* x, const void* gamma, const float* mean, const float* rstd,
+               int N, int D, int flags, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Softmax cross-entropy (LM head loss)
+ * ------------------------------------------------------------------------ */
+
+/* One pass over half logits [N, V] (row stride ld >= V, ld % 8 == 0,
+ * V <= 65536):
+ *   dlogits[i, j] = (softmax(z_i)_j - [j == t_i]) * scale * (*dscale if dscale)
+ * dlogits may alias logits (in place).  Optional output:
+ *   row_loss [N] FP32 = -log(softmax(z_i)_{t_i} + 1e-10)  (src/cpu_mat.h:213)
+ * A target outside [0, V) yields a NaN row loss and a zero gradient row.
+ * The lm_b gradient (column sums of dlogits) comes from the LM-head wgrad
+ * (rbk_gemm_desc.dbias_rows), which reads dlogits anyway.
+ * `scale` carries the 1/N of the mean (src/cpu_mat.h:233) and any upstream
+ * factor; dscale (device FP32, optional) is the dynamic loss scale.
+ * Replaces cross_entropy_fp32_forward/_backward (src/cuda_kernels.cuh:127-128)
+ * and the scale_add that follows them (src/model.cu:348-350). */
+int rbk_softmax_xent_bwd(rbk_ctx* ctx, void* dlogits, const void* logits, int ld, const int* targets, int N,
+                         int V, float scale, const float* dscale, float* row_loss, void* stream);
+
+/* Sum of row_loss[0..N) * scale into *out (device FP32), deterministic. */
+int rbk_sum(rbk_ctx* ctx, float* out, const float* x, int n, float scale, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Attention softmax backward (materialised probabilities)
+ * ------------------------------------------------------------------------ */
+
+/* dS = P * (dP - rowsum(dP * P)) over nmat stacked [T, T] half matrices.
+ * causal != 0: row i covers columns 0..i only; the strict upper triangle of
+ * dS is not written.  T % 8 == 0.
+ * Replaces softmax_fp16_backward / softmax_fp32_backward
+ * (src/cuda_kernels.cuh:120,124). */
+int rbk_attn_softmax_bwd(rbk_ctx* ctx, void* dS, const void* P, const void* dP, int nmat, int T, int causal,
+                         void* stream);
+
+/* ------------------------------------------------------------------------
+ * Embeddings
+ * ------------------------------------------------------------------------ */
+
+/* x[b*S+s] = tok_emb[tokens[b*S+s]] + pos_emb[s]   (half [B*S, D]).
+ * Replaces embedding_fp16_forward + the pos scale_add (src/model.cu:246-248). */
+int rbk_embed_fwd(rbk_ctx* ctx, void* x, const void* tok_emb, const void* pos_emb, const int* tokens, int B,
+                  int S, int D, int V, void* stream);
+
+/* dtok[tokens[i]] += dx[i] (FP32 [V, D]);  dpos[s] += sum_b dx[b*S+s]
+ * (FP32 [S, D]).  Either output may be NULL.
+ * Replaces embedding_fp16_backward (src/cuda_kernels.cuh:112) and adds the
+ * pos_emb gradient the reference never computes. */
+int rbk_embed_bwd(rbk_ctx* ctx, float* dtok, float* dpos, const void* dx, const int* tokens, int B, int S,
+                  int D, int V, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Mixed-precision tail
+ * ------------------------------------------------------------------------ */
+
+/* Dynamic loss-scaler state, resident in device memory (LossScaler,
+ * src/cuda_kernels.cuh:62-73; backoff 0.5, growth 2.0, clamp [1, 65536]). */
+typedef struct rbk_scaler {
+    float scale;          /* current loss scale                                 */
+    int unskipped;        /* clean steps since the last growth / overflow       */
+    int interval;         /* growth interval (2000)                             */
+    int skipped;          /* 1 when the last tail call skipped its update       */
+    int applied_steps;    /* updates applied so far (Adam's t when t <= 0)       */
+    int overflow_steps;   /* total skipped steps                                */
+    int status;           /* 0, or RBK_ERR_TIMEOUT from the tail's grid barrier */
+    int pad;
+} rbk_scaler;
+
+typedef struct rbk_tail_args {
+    float* p32;              /* FP32 masters [n]                                  */
+    float* g;                /* FP32 gradients [n] (scaled by scaler.scale); zeroed */
+    float* m;                /* Adam first moment [n]                             */
+    float* v;                /* Adam second moment [n]                            */
+    void* p16;               /* half copy of the masters [n] (may be NULL)        */
+    int64_t n;
+    /* Optional per-tensor L2 clip (src/model.cu:493-523) of the unscaled
+     * gradients: nseg tensors [seg_off[i], seg_off[i] + seg_len[i]) (host
+     * arrays).  max_norm <= 0 disables clipping. */
+    const int64_t* seg_off;
+    const int64_t* seg_len;
+    int nseg;
+    float max_norm;
+    float lr, beta1, beta2, eps, weight_decay;
+    int t;                   /* 1-based Adam step; <= 0: scaler->applied_steps + 1 */
+    rbk_scaler* scaler;      /* device pointer                                    */
+} rbk_tail_args;
+
+/* One kernel: inf/NaN check of every gradient, unscale by 1/scale, optional
+ * per-tensor clip, L2-coupled AdamW (src/cpu_mat.h:280-292), FP16 copy-out,
+ * gradient zeroing, loss-scaler update and the skip decision.  On overflow the
+ * masters and moments are left untouched and the step is skipped.
+ * Replaces check_overflow_all (src/cuda_kernels.cu:1060-1074),
+ * update_loss_scale (src/model.cu:436-449), optimizer_step (src/model.cu:454-488),
+ * clip_gradients (src/model.cu:493-523) and convert_fp32_to_fp16
+ * (src/cuda_kernels.cuh:186). */
+int rbk_adam_tail(rbk_ctx* ctx, const rbk_tail_args* args, void* stream);
+
+/* ------------------------------------------------------------------------
+ * GEMM (tcgen05 / TMEM, TMA-fed)
+ * ------------------------------------------------------------------------ */
+
+enum {
+    RBK_EPI_STORE_F16 = 0,  /* C16 = alpha*acc [+ bias[n]] [+ aux[m,n]]              */
+    RBK_EPI_BIAS_GELU = 1,  /* C16 = acc + bias[n] (pre-activation); aux_out16 = gelu */
+    RBK_EPI_GELU_BWD = 2,   /* C16 = acc * gelu'(aux[m,n])                           */
+    RBK_EPI_ACC_F32 = 3,    /* C32[m,n] += alpha*acc   (gradient accumulation)       */
+    RBK_EPI_STORE_F32 = 4   /* C32[m,n] = alpha*acc                                  */
+};
+
+/* C[M,N] = op(A)[M,K] . op(B)[N,K]^T in FP32 on the tensor cores, half inputs.
+ *   a_major 0: A(m,k) = A[m*lda + k] (K-major);  1: A(m,k) = A[k*lda + m]
+ *   b_major 0: B(n,k) = B[n*ldb + k] (K-major);  1: B(n,k) = B[k*ldb + n]
+ *   C(m,n) = C[m*ldc + n]; aux/aux_out share ldc unless ld_aux is given.
+ * Leading dimensions must be multiples of 8 elements and base pointers
+ * 16-byte aligned (TMA).  split_k 0 = automatic (only for RBK_EPI_ACC_F32).
+ * Replaces gemm_fp16_tensorcores, gemm_fp16_accum_fp32 and its _backward_dA /
+ * _backward_dB variants, linear_forward_fp16(_to_fp32) and linear_backward_fp16
+ * (src/cuda_kernels.cuh:137-147,190-193), plus the FFN/QKV fusions
+ * (src/cuda_kernels.cuh:153-169). */
+typedef struct rbk_gemm_desc {
+    int M, N, K;
+    const void* A; int lda; int a_major;
+    const void* B; int ldb; int b_major;
+    void* C; int ldc;
+    int epilogue;
+    const void* bias;        /* half [N]                                   */
+    const void* aux;         /* half [M, ld_aux]: residual or pre-activation */
+    int ld_aux;              /* 0 -> ldc                                    */
+    void* aux_out;           /* half [M, ld_aux]: activation output         */
+    float* dbias_rows;       /* ACC_F32 only: FP32 [M] += alpha * row sums of
+                                op(A) over K — the bias gradient of a linear
+                                layer when A = dY^T (one extra N=16 MMA
+                                against a ones tile, issued by the n = 0 tiles) */
+    float alpha;
+    int split_k;
+} rbk_gemm_desc;
+
+int rbk_gemm(rbk_ctx* ctx, const rbk_gemm_desc* d, void* stream);
+
+/* Linear-layer shorthands over the [out, in] weight layout:
+ *   fwd  : Y[N,out] = X[N,in] W^T (+ bias) (+ residual)      -> STORE_F16
+ *   dgrad: dX[N,in] = dY[N,out] W  [* gelu'(gelu_pre)]      -> STORE_F16 or GELU_BWD
+ *   wgrad: dW[out,in] += dY^T X   (FP32 accumulate)          -> ACC_F32 (+ bias grad)
+ * Replaces gemm_fp16_accum_fp32_backward_dA / _dB (src/cuda_kernels.cu:639-665). */
+int rbk_linear_fwd(rbk_ctx* ctx, void* Y, const void* X, const void* W, const void* bias, const void* residual,
+                   int N, int in, int out, void* stream);
+int rbk_gemm_dgrad(rbk_ctx* ctx, void* dX, const void* dY, const void* W, int N, int in, int out,
+                   const void* gelu_pre, void* stream);
+/* dbias (optional, FP32 [out]) += column sums of dY, fused into the wgrad. */
+int rbk_gemm_wgrad(rbk_ctx* ctx, float* dW, float* dbias, const void* dY, const void* X, int N, int in, int out,
+                   void* stream);
+
+/* ------------------------------------------------------------------------
+ * Causal flash attention (d_head 64 or 128)
+ * ------------------------------------------------------------------------ */
+
+/* qkv: half [B*S, 3*H*dh] with q | k | v column blocks (the fused QKV GEMM
+ * output); o: half [B*S, H*dh]; lse: FP32 [B, H, S] (natural-log sum-exp of
+ * the scaled scores).  scale = 1/sqrt(dh) (src/cpu_model.cpp:148).
+ * Replaces the per-(b,h) score GEMMs, apply_causal_mask_fp32 and
+ * softmax_fp32_forward of src/model.cu:262-286. */
+int rbk_attn_fwd(rbk_ctx* ctx, void* o, float* lse, const void* qkv, int B, int S, int H, int dh, float scale,
+                 void* stream);
+
+/* dqkv: half [B*S, 3*H*dh] (dq | dk | dv); dbias_qkv (optional) FP32 [3*H*dh]
+ * += column sums of dqkv (the bq | bk | bv gradients).  The reference never
+ * runs an attention backward (src/model.cu:387-397 sets dQ = dK = dV = dO). */
+int rbk_attn_bwd(rbk_ctx* ctx, void* dqkv, float* dbias_qkv, const void* qkv, const void* o, const void* dout,
+                 const float* lse, int B, int S, int H, int dh, float scale, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Model: the RubidiumTransformer drop-in (src/model.h:112-139)
+ * ------------------------------------------------------------------------ */
+
+typedef struct rbk_model rbk_model;
+
+typedef struct rbk_model_opts {
+    int max_batch;                     /* B of allocate_activations(B*T)            */
+    int max_seq;                       /* S <= cfg.T                                */
+    int use_activation_checkpointing;  /* ModelConfig field, src/model.h:19         */
+    float init_loss_scale;             /* 65536 (src/model.h:120)                   */
+    int growth_interval;               /* 2000                                      */
+    int device;
+} rbk_model_opts;
+
+/* Buffer families of the parameter arena (include/rbk_layout.h). */
+enum { RBK_BUF_P16 = 0, RBK_BUF_P32 = 1, RBK_BUF_GRAD = 2, RBK_BUF_M = 3, RBK_BUF_V = 4 };
+
+int rbk_model_create(rbk_model** out, const rbk_config* cfg, const rbk_model_opts* opts);
+int rbk_model_destroy(rbk_model* m);
+/* Device pointer and element count of one arena family. */
+int rbk_model_buffer(rbk_model* m, int which, void** ptr, int64_t* n);
+/* Device pointer to the loss scaler state (rbk_scaler). */
+int rbk_model_scaler(rbk_model* m, rbk_scaler** dev);
+/* Copy FP32 masters to the FP16 weights (convert_weights_fp32_to_fp16, src/model.h:129). */
+int rbk_model_sync_fp16(rbk_model* m, void* stream);
+/* init_weights (src/model.cu:146-183): seeded N(0, std) matrices and
+ * embeddings, LN gamma 1 / beta 0, biases 0; zero moments and gradients. */
+int rbk_model_init_weights(rbk_model* m, uint64_t seed, float std, void* stream);
+
+/* forward (src/model.h:130): device tokens/targets [B*S] int32.  Writes the
+ * mean loss to *loss_dev (device FP32) when non-NULL; targets may be NULL. */
+int rbk_model_forward(rbk_model* m, const int* tokens, const int* targets, int B, int S, float* loss_dev,
+                      void* stream);
+/* backward (src/model.h:131): accumulates gradients of
+ *   loss * grad_scale * scaler.scale
+ * into the gradient arena (grad_scale is the reference's loss_scale argument,
+ * 1/(BS*GA) in src/main.cpp:158; pass 1 for the plain mean).  Must follow a
+ * forward on the same tokens. */
+int rbk_model_backward(rbk_model* m, const int* tokens, const int* targets, int B, int S, float grad_scale,
+                       void* stream);
+/* optimizer_step (src/model.h:132) fused with the overflow check, unscale,
+ * optional per-tensor clip (max_norm <= 0: off), scaler update and skip. */
+int rbk_model_optimizer_step(rbk_model* m, int t, float lr, float b1, float b2, float eps, float wd,
+                             float max_norm, void* stream);
+
+/* ------------------------------------------------------------------------
+ * LoRA (src/lora.h:13-231): rank-r adapters on the Q and V projections.
+ * ------------------------------------------------------------------------ */
+
+/* Enable adapters: A [L, D, r] ~ N(0, 0.02) (seeded), B [L, r, D] = 0,
+ * scaling alpha / r.  Base weights become frozen: backward produces only the
+ * adapter gradients (plus the dgrads through the frozen base).
+ * Replaces init_lora (src/lora.h:223). */
+int rbk_model_lora_enable(rbk_model* m, int rank, float alpha, uint64_t seed, void* stream);
+/* Device pointers of the adapter arenas: which = RBK_BUF_P32 (A|B masters),
+ * RBK_BUF_GRAD, RBK_BUF_M, RBK_BUF_V.  Layout: Aq [L,D,r] | Bq [L,r,D] |
+ * Av [L,D,r] | Bv [L,r,D]. */
+int rbk_model_lora_buffer(rbk_model* m, int which, void** ptr, int64_t* n);
+/* lora_optimizer_step (src/lora.h:230) with the same fused tail. */
+int rbk_model_lora_step(rbk_model* m, int t, float lr, float b1, float b2, float eps, float wd, void* stream);
+/* Overflow injection for testing the skip path: before the next backward's
+ * LM-head dgrad, set every `stride`-th element of dlogits (starting at
+ * `offset`) to +inf.  stride <= 0 disables. */
+int rbk_model_inject_inf(rbk_model* m, int64_t offset, int64_t stride);
+
+/* ------------------------------------------------------------------------
+ * Data parallel: bucketed NCCL all-reduce of the gradient arena, overlapped
+ * with the backward (no counterpart in the reference, which is single-GPU:
+ * src/main.cpp:54).
+ * ------------------------------------------------------------------------ */
+
+#define RBK_NCCL_ID_BYTES 128
+/* Fill a 128-byte NCCL unique id on the root rank (ncclGetUniqueId). */
+int rbk_dp_unique_id(void* id128);
+/* Join the communicator; bucket_bytes (25 MB) sets the all-reduce granularity. */
+int rbk_model_dp_init(rbk_model* m, const void* id128, int rank, int world, int64_t bucket_bytes);
+int rbk_model_dp_shutdown(rbk_model* m);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RBK_H */

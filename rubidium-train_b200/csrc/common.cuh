@@ -1,0 +1,137 @@
+// common.cuh — shared host/device helpers of librbk (sm_100a only).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+
+#include "rbk.h"
+
+// ----------------------------------------------------------------------------
+// Host-side error plumbing: every entry point returns an int status and leaves
+// a message in a thread-local buffer (rbk_last_error).
+// ----------------------------------------------------------------------------
+namespace rbk {
+
+void set_error(const char* fmt, ...);
+int cuda_fail(cudaError_t e, const char* what, const char* file, int line);
+
+}  // namespace rbk
+
+#define RBK_CUDA(call)                                                              \
+    do {                                                                            \
+        cudaError_t e_ = (call);                                                    \
+        if (e_ != cudaSuccess) return ::rbk::cuda_fail(e_, #call, __FILE__, __LINE__); \
+    } while (0)
+
+#define RBK_LAUNCHED(what)                                                          \
+    do {                                                                            \
+        cudaError_t e_ = cudaGetLastError();                                        \
+        if (e_ != cudaSuccess) return ::rbk::cuda_fail(e_, what, __FILE__, __LINE__); \
+    } while (0)
+
+#define RBK_REQUIRE(cond, ...)                \
+    do {                                      \
+        if (!(cond)) {                        \
+            ::rbk::set_error(__VA_ARGS__);    \
+            return RBK_ERR_INVALID;           \
+        }                                     \
+    } while (0)
+
+#define RBK_TRY(expr)                 \
+    do {                              \
+        int s_ = (expr);              \
+        if (s_ != RBK_OK) return s_;  \
+    } while (0)
+
+// ----------------------------------------------------------------------------
+// Context: device + scratch arena + a small zeroed area for tickets/flags.
+// ----------------------------------------------------------------------------
+struct rbk_ctx {
+    int device = 0;
+    int num_sms = 148;
+    void* scratch = nullptr;
+    size_t scratch_bytes = 0;
+    // Device ints, zero at creation; each user restores its slot to zero.
+    int* tickets = nullptr;
+    static constexpr int kTickets = 64;
+    int* err = nullptr;      // device error word written by bounded waits
+};
+
+namespace rbk {
+
+// Scratch of at least `bytes` (256-byte aligned); grows (cudaFree + cudaMalloc)
+// only when the current arena is too small.
+int ctx_scratch(rbk_ctx* ctx, size_t bytes, void** out);
+
+// out[c] += sum_r part[r*C + c], deterministic (ctx.cu).
+int column_reduce(float* out, const float* part, int R, int C, cudaStream_t st);
+
+// Ticket slots (see rbk_ctx::tickets).
+enum TicketSlot {
+    kTicketSum = 0,
+    kTailOverflow = 8, kTailBarrier = 9, kTailTicket = 10, kTailTimeout = 11,
+    kGemmError = 16,
+};
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ----------------------------------------------------------------------------
+// Device helpers
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// 8 halves <-> 8 floats through one 16-byte vector.
+__device__ __forceinline__ void h8_to_f(const uint4& u, float* f) {
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float2 t = __half22float2(h[i]);
+        f[2 * i] = t.x;
+        f[2 * i + 1] = t.y;
+    }
+}
+__device__ __forceinline__ uint4 f_to_h8(const float* f) {
+    uint4 u;
+    __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+    return u;
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bounded device-side waits give up after this long and report RBK_ERR_TIMEOUT.
+constexpr uint64_t kWaitTimeoutNs = 2000000000ull;   // 2 s
+
+// GPT-2 tanh GELU and its derivative (the FFN activation of this build; the
+// reference's FFN uses ReLU, src/cpu_model.cpp:198-200).
+__device__ __forceinline__ float gelu_f(float x) {
+    const float c = 0.7978845608028654f, a = 0.044715f;
+    return 0.5f * x * (1.0f + tanhf(c * (x + a * x * x * x)));
+}
+__device__ __forceinline__ float gelu_grad_f(float x) {
+    const float c = 0.7978845608028654f, a = 0.044715f;
+    const float t = tanhf(c * (x + a * x * x * x));
+    return 0.5f * (1.0f + t) + 0.5f * x * (1.0f - t * t) * c * (1.0f + 3.0f * a * x * x);
+}
+
+}  // namespace rbk

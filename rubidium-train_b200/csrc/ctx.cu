@@ -1,0 +1,138 @@
+// ctx.cu — context, scratch arena, error strings and the small reductions
+// shared by several entry points.
+#include <cstring>
+#include <string>
+
+#include "common.cuh"
+
+namespace rbk {
+
+static thread_local char g_err[512] = "";
+
+void set_error(const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+}
+
+int cuda_fail(cudaError_t e, const char* what, const char* file, int line) {
+    set_error("%s failed: %s (%s:%d)", what, cudaGetErrorString(e), file, line);
+    return e == cudaErrorMemoryAllocation ? RBK_ERR_NOMEM : RBK_ERR_CUDA;
+}
+
+int ctx_scratch(rbk_ctx* ctx, size_t bytes, void** out) {
+    bytes = (bytes + 255) & ~size_t(255);
+    if (bytes > ctx->scratch_bytes) {
+        if (ctx->scratch) RBK_CUDA(cudaFree(ctx->scratch));
+        ctx->scratch = nullptr;
+        ctx->scratch_bytes = 0;
+        RBK_CUDA(cudaMalloc(&ctx->scratch, bytes));
+        ctx->scratch_bytes = bytes;
+    }
+    *out = ctx->scratch;
+    return RBK_OK;
+}
+
+// out[c] += sum_r part[r*C + c]   (deterministic, fixed order over r)
+__global__ void column_reduce_kernel(float* __restrict__ out, const float* __restrict__ part, int R, int C) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= C) return;
+    float s = 0.0f;
+    for (int r = 0; r < R; ++r) s += part[(size_t)r * C + c];
+    out[c] += s;
+}
+
+int column_reduce(float* out, const float* part, int R, int C, cudaStream_t st) {
+    column_reduce_kernel<<<(C + 255) / 256, 256, 0, st>>>(out, part, R, C);
+    RBK_LAUNCHED("column_reduce_kernel");
+    return RBK_OK;
+}
+
+// Deterministic sum of n floats into *out (times scale): one CTA per 64K-chunk
+// writes a partial, the last CTA (ticket) adds the partials in order.
+__global__ void sum_kernel(float* __restrict__ out, const float* __restrict__ x, int n, float scale,
+                           float* __restrict__ part, int* ticket) {
+    __shared__ float sw[32];
+    __shared__ int last;
+    const int chunk = 65536;
+    const int begin = blockIdx.x * chunk, end = min(n, begin + chunk);
+    float s = 0.0f;
+    for (int i = begin + threadIdx.x; i < end; i += blockDim.x) s += x[i];
+    s = warp_sum(s);
+    if ((threadIdx.x & 31) == 0) sw[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float t = threadIdx.x < (blockDim.x >> 5) ? sw[threadIdx.x] : 0.0f;
+        t = warp_sum(t);
+        if (threadIdx.x == 0) {
+            part[blockIdx.x] = t;
+            __threadfence();
+            last = (atomicAdd(ticket, 1) == (int)gridDim.x - 1);
+        }
+    }
+    __syncthreads();
+    if (last && threadIdx.x == 0) {
+        __threadfence();
+        float tot = 0.0f;
+        for (int b = 0; b < (int)gridDim.x; ++b) tot += ((volatile float*)part)[b];
+        *out = tot * scale;
+        *ticket = 0;
+    }
+}
+
+}  // namespace rbk
+
+using namespace rbk;
+
+extern "C" {
+
+const char* rbk_last_error(void) { return g_err; }
+
+int rbk_version(void) { return 1; }
+
+int rbk_ctx_create(rbk_ctx** out, int device) {
+    RBK_REQUIRE(out != nullptr, "rbk_ctx_create: out is NULL");
+    *out = nullptr;
+    int ndev = 0;
+    RBK_CUDA(cudaGetDeviceCount(&ndev));
+    RBK_REQUIRE(device >= 0 && device < ndev, "rbk_ctx_create: device %d out of range (%d devices)", device, ndev);
+    RBK_CUDA(cudaSetDevice(device));
+    cudaDeviceProp prop;
+    RBK_CUDA(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10 || prop.minor != 0) {
+        set_error("librbk is built for sm_100a (B200); device %d is sm_%d%d", device, prop.major, prop.minor);
+        return RBK_ERR_UNSUPPORTED;
+    }
+    rbk_ctx* c = new rbk_ctx();
+    c->device = device;
+    c->num_sms = prop.multiProcessorCount;
+    cudaError_t e = cudaMalloc(&c->tickets, sizeof(int) * (rbk_ctx::kTickets + 1));
+    if (e != cudaSuccess) { delete c; return cuda_fail(e, "cudaMalloc(tickets)", __FILE__, __LINE__); }
+    e = cudaMemset(c->tickets, 0, sizeof(int) * (rbk_ctx::kTickets + 1));
+    if (e != cudaSuccess) { cudaFree(c->tickets); delete c; return cuda_fail(e, "cudaMemset", __FILE__, __LINE__); }
+    c->err = c->tickets + rbk_ctx::kTickets;
+    *out = c;
+    return RBK_OK;
+}
+
+int rbk_ctx_destroy(rbk_ctx* ctx) {
+    if (!ctx) return RBK_OK;
+    cudaSetDevice(ctx->device);
+    if (ctx->scratch) cudaFree(ctx->scratch);
+    if (ctx->tickets) cudaFree(ctx->tickets);
+    delete ctx;
+    return RBK_OK;
+}
+
+int rbk_sum(rbk_ctx* ctx, float* out, const float* x, int n, float scale, void* stream) {
+    RBK_REQUIRE(ctx && out && x && n > 0, "rbk_sum: bad arguments");
+    const int blocks = (n + 65535) / 65536;
+    void* ws;
+    RBK_TRY(ctx_scratch(ctx, sizeof(float) * blocks, &ws));
+    sum_kernel<<<blocks, 256, 0, as_stream(stream)>>>(out, x, n, scale, (float*)ws, ctx->tickets + kTicketSum);
+    RBK_LAUNCHED("sum_kernel");
+    return RBK_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,622 @@
+// gemm.cu — FP16 x FP16 -> FP32 GEMM on the 5th-generation tensor cores.
+//
+// C[M,N] = op(A)[M,K] . op(B)[N,K]^T with fused epilogues; every dense
+// contraction of the model (forward linears, dgrad, wgrad, LM head) runs here.
+// It replaces the reference's cuBLAS/cuBLASLt wrappers and naive fused kernels
+// (src/cuda_kernels.cu:596-665, 670-784, 1031-1045).
+//
+// Design (one persistent CTA per SM, 192 threads):
+//   warp 0      TMA producer: 128B-swizzled tiles of A (128 x 64) and B
+//               (BN x 64) into a STAGES-deep shared-memory ring (mbarriers with
+//               complete_tx).  K-major operands are one box per tile; MN-major
+//               operands (the transposed reads of dgrad/wgrad) are 64-wide
+//               boxes stacked at the descriptor's leading-byte offset.
+//   warp 1      MMA issuer: tcgen05.mma.cta_group::1.kind::f16, M=128, N=BN,
+//               K=16 per instruction, FP32 accumulator in TMEM, double-buffered
+//               so the epilogue of tile i overlaps the MMAs of tile i+1.
+//               tcgen05.commit releases smem stages and publishes accumulators.
+//   warps 2..5  epilogue: tcgen05.ld 32x32b (one TMEM lane quarter per warp,
+//               one output row per thread), fused bias / residual / GELU /
+//               GELU' / FP32 accumulation, direct 16-byte global stores.
+// Bias gradients (row sums of A over K when A = dY^T) come from one extra
+// N=16 MMA per k-step against a constant ones tile, issued by the n=0 tiles.
+// Every mbarrier wait is bounded (globaltimer); on expiry the kernel records
+// RBK_ERR_TIMEOUT, drains, frees TMEM and returns.
+// No cluster multicast is used anywhere.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace rbk {
+namespace gemm {
+
+constexpr int BM = 128, BK = 64, UMMA_K = 16;
+constexpr int kThreads = 192;
+
+template <int BN>
+struct Cfg {
+    static constexpr int STAGES = BN == 256 ? 4 : 6;
+    static constexpr int A_BYTES = BM * BK * 2;
+    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int ONES_BYTES = 16 * BK * 2;
+    static constexpr int BAR_BYTES = 256;
+    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + ONES_BYTES + BAR_BYTES;
+    static constexpr uint32_t TMEM_COLS = 512;
+    static constexpr int ACC2_COL = 2 * BN;   // ones-MMA accumulators (BN == 128 only)
+};
+
+struct Params {
+    int M, N, K;
+    int m_blocks, n_blocks, k_blocks, splits, kb_per_split, units;
+    int a_mn, b_mn;
+    void* C;
+    int ldc;
+    const half* bias;
+    const half* aux;
+    int ld_aux;
+    half* aux_out;
+    float* dbias_rows;
+    float alpha;
+    int* err;
+};
+
+// ------------------------------------------------------------------ PTX ----
+__device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait. Returns false (and raises the CTA abort flag) on timeout or
+// when another role already aborted.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+    if (mbar_try(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+#pragma unroll 1
+        for (int i = 0; i < 32; ++i)
+            if (mbar_try(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+            *abort_flag = 1;
+            return false;
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* tm, uint32_t bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            dst),
+        "l"(tm), "r"(bar), "r"(x), "r"(y)
+        : "memory");
+}
+
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void mma_f16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// SW128 shared-memory matrix descriptor (version 1 = sm_100).
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr & 0x3FFFFu) >> 4);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+// kind::f16 instruction descriptor: FP16 A/B, FP32 D, M=128.
+__host__ __device__ constexpr uint32_t idesc_f16(int n, int a_mn, int b_mn) {
+    return (1u << 4) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) | ((uint32_t)(n >> 3) << 17) |
+           ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ uint32_t tmem_ld1(uint32_t taddr) {
+    uint32_t r;
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
+    return r;
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
+                 : "memory");
+}
+
+__device__ __forceinline__ void decode_unit(const Params& p, int u, int& m_blk, int& n_blk, int& kb0, int& kb1) {
+    const int split = u % p.splits;
+    const int tile = u / p.splits;
+    constexpr int GM = 8;
+    const int group_size = GM * p.n_blocks;
+    const int group = tile / group_size;
+    const int first_m = group * GM;
+    const int gm = min(GM, p.m_blocks - first_m);
+    const int in_group = tile - group * group_size;
+    m_blk = first_m + in_group % gm;
+    n_blk = in_group / gm;
+    kb0 = split * p.kb_per_split;
+    kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
+}
+
+// ------------------------------------------------------------- epilogue ----
+template <int EPI>
+__device__ __forceinline__ void epilogue_chunk(const Params& p, int m, int n, const uint32_t* r) {
+    // r: 32 FP32 accumulators of row m, columns n .. n+31
+    if (m >= p.M || n >= p.N) return;
+    const bool full = n + 32 <= p.N;
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+
+    if constexpr (EPI == RBK_EPI_ACC_F32 || EPI == RBK_EPI_STORE_F32) {
+        float* c = reinterpret_cast<float*>(p.C) + (size_t)m * p.ldc + n;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] *= p.alpha;
+        if (full) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+                if constexpr (EPI == RBK_EPI_ACC_F32)
+                    red_add_v4(c + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
+                else
+                    *reinterpret_cast<float4*>(c + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                if (n + j < p.N) {
+                    if constexpr (EPI == RBK_EPI_ACC_F32)
+                        atomicAdd(c + j, v[j]);
+                    else
+                        c[j] = v[j];
+                }
+            }
+        }
+        return;
+    } else {
+        half* c = reinterpret_cast<half*>(p.C) + (size_t)m * p.ldc + n;
+        const int lda = p.ld_aux ? p.ld_aux : p.ldc;
+        if constexpr (EPI == RBK_EPI_STORE_F16) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] *= p.alpha;
+        }
+        if (p.bias && EPI != RBK_EPI_GELU_BWD) {
+            if (full) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 8) {
+                    float b[8];
+                    h8_to_f(__ldg(reinterpret_cast<const uint4*>(p.bias + n + j)), b);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) v[j + q] += b[q];
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    if (n + j < p.N) v[j] += __half2float(p.bias[n + j]);
+            }
+        }
+        if (p.aux) {
+            const half* a = p.aux + (size_t)m * lda + n;
+            if (full) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 8) {
+                    float b[8];
+                    h8_to_f(__ldg(reinterpret_cast<const uint4*>(a + j)), b);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        if constexpr (EPI == RBK_EPI_GELU_BWD)
+                            v[j + q] *= gelu_grad_f(b[q]);
+                        else
+                            v[j + q] += b[q];
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    if (n + j < p.N) {
+                        const float b = __half2float(a[j]);
+                        if constexpr (EPI == RBK_EPI_GELU_BWD)
+                            v[j] *= gelu_grad_f(b);
+                        else
+                            v[j] += b;
+                    }
+                }
+            }
+        }
+        if (full) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) *reinterpret_cast<uint4*>(c + j) = f_to_h8(v + j);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (n + j < p.N) c[j] = __float2half_rn(v[j]);
+        }
+        if constexpr (EPI == RBK_EPI_BIAS_GELU) {
+            half* o = p.aux_out + (size_t)m * lda + n;
+            float gl[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) gl[j] = gelu_f(v[j]);
+            if (full) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 8) *reinterpret_cast<uint4*>(o + j) = f_to_h8(gl + j);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    if (n + j < p.N) o[j] = __float2half_rn(gl[j]);
+            }
+        }
+    }
+}
+
+// ----------------------------------------------------------------- kernel ----
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                           const __grid_constant__ CUtensorMap tmB, const Params p) {
+    using C = Cfg<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = su32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t* gbase = smem_raw + (base - raw);
+    const uint32_t sA0 = base;                                       // stage s: A at s*STAGE_BYTES
+    const uint32_t ones = base + C::STAGES * C::STAGE_BYTES;          // 2 KB of fp16 ones
+    const uint32_t bars = ones + C::ONES_BYTES;
+    uint8_t* gbars = gbase + (bars - base);
+    auto full_bar = [&](int s) { return bars + 8u * s; };
+    auto empty_bar = [&](int s) { return bars + 8u * (C::STAGES + s); };
+    auto tfull_bar = [&](int b) { return bars + 8u * (2 * C::STAGES + b); };
+    auto tempty_bar = [&](int b) { return bars + 8u * (2 * C::STAGES + 2 + b); };
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbars + 8 * (2 * C::STAGES + 4));
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(gbars + 8 * (2 * C::STAGES + 4) + 8);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    // ones tile (for the bias-gradient MMA) and barrier init
+    {
+        uint32_t* o = reinterpret_cast<uint32_t*>(gbase + (ones - base));
+        for (int i = threadIdx.x; i < C::ONES_BYTES / 4; i += blockDim.x) o[i] = 0x3C003C00u;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(tfull_bar(b), 1);
+            mbar_init(tempty_bar(b), 4);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0 && lane == 0) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_slot)),
+                     "r"(C::TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------ TMA producer ------------------------
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x) {
+                int mb, nb, kb0, kb1;
+                decode_unit(p, u, mb, nb, kb0, kb1);
+                const int m0 = mb * BM, n0 = nb * BN;
+                for (int kb = kb0; kb < kb1; ++kb) {
+                    if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag)) break;
+                    const uint32_t fb = full_bar(stage);
+                    mbar_expect_tx(fb, C::STAGE_BYTES);
+                    const uint32_t sa = sA0 + stage * C::STAGE_BYTES;
+                    const uint32_t sb = sa + C::A_BYTES;
+                    const int k0 = kb * BK;
+                    if (!p.a_mn) {
+                        tma_load_2d(sa, &tmA, fb, k0, m0);
+                    } else {
+                        tma_load_2d(sa, &tmA, fb, m0, k0);
+                        tma_load_2d(sa + 8192, &tmA, fb, m0 + 64, k0);
+                    }
+                    if (!p.b_mn) {
+                        tma_load_2d(sb, &tmB, fb, k0, n0);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + 8192 * j, &tmB, fb, n0 + 64 * j, k0);
+                    }
+                    if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------ MMA issuer --------------------------
+        if (lane == 0) {
+            const uint32_t idesc = idesc_f16(BN, p.a_mn, p.b_mn);
+            const uint32_t idesc1 = idesc_f16(16, p.a_mn, 0);
+            const uint32_t a_lbo = p.a_mn ? 8192u : 16u, b_lbo = p.b_mn ? 8192u : 16u;
+            const uint32_t a_kstep = p.a_mn ? 2048u : 32u, b_kstep = p.b_mn ? 2048u : 32u;
+            int stage = 0, buf = 0;
+            uint32_t phase = 0, bphase = 0;
+            for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x) {
+                int mb, nb, kb0, kb1;
+                decode_unit(p, u, mb, nb, kb0, kb1);
+                const bool rowsum = EPI == RBK_EPI_ACC_F32 && BN == 128 && p.dbias_rows && nb == 0;
+                if (!mbar_wait(tempty_bar(buf), bphase ^ 1, abort_flag)) break;
+                fence_after();
+                const uint32_t dacc = tmem + buf * BN;
+                const uint32_t dacc2 = tmem + C::ACC2_COL + buf * 16;
+                bool ok = true;
+                for (int kb = kb0; kb < kb1; ++kb) {
+                    if (!mbar_wait(full_bar(stage), phase, abort_flag)) { ok = false; break; }
+                    fence_after();
+                    const uint32_t sa = sA0 + stage * C::STAGE_BYTES;
+                    const uint32_t sb = sa + C::A_BYTES;
+#pragma unroll
+                    for (int k = 0; k < BK / UMMA_K; ++k) {
+                        const uint64_t ad = sdesc(sa + k * a_kstep, a_lbo, 1024);
+                        const uint64_t bd = sdesc(sb + k * b_kstep, b_lbo, 1024);
+                        const uint32_t acc = (kb > kb0 || k > 0) ? 1u : 0u;
+                        mma_f16(dacc, ad, bd, idesc, acc);
+                        if (rowsum) mma_f16(dacc2, ad, sdesc(ones + k * 32, 16, 1024), idesc1, acc);
+                    }
+                    mma_commit(empty_bar(stage));
+                    if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
+                }
+                if (!ok) break;
+                mma_commit(tfull_bar(buf));
+                if (++buf == 2) { buf = 0; bphase ^= 1; }
+            }
+        }
+    } else {
+        // ------------------------------ epilogue ----------------------------
+        const int q = warp & 3;                 // TMEM lane quarter of this warp
+        const int row = q * 32 + lane;
+        int buf = 0;
+        uint32_t bphase = 0;
+        for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+            int mb, nb, kb0, kb1;
+            decode_unit(p, u, mb, nb, kb0, kb1);
+            if (!mbar_wait(tfull_bar(buf), bphase, abort_flag)) break;
+            fence_after();
+            const int m = mb * BM + row;
+            const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + buf * BN;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld32(tbase + c * 32, r);
+                tmem_wait_ld();
+                epilogue_chunk<EPI>(p, m, nb * BN + c * 32, r);
+            }
+            if (EPI == RBK_EPI_ACC_F32 && BN == 128 && p.dbias_rows && nb == 0) {
+                const uint32_t v = tmem_ld1(tmem + ((uint32_t)(q * 32) << 16) + C::ACC2_COL + buf * 16);
+                tmem_wait_ld();
+                if (m < p.M) atomicAdd(p.dbias_rows + m, p.alpha * __uint_as_float(v));
+            }
+            fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty_bar(buf));
+            if (++buf == 2) { buf = 0; bphase ^= 1; }
+        }
+    }
+
+    fence_before();
+    __syncthreads();
+    fence_after();
+    if (threadIdx.x == 0 && *abort_flag) atomicExch(p.err, RBK_ERR_TIMEOUT);
+    if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS));
+}
+
+// ------------------------------------------------------------------- host ----
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q;
+        void* f = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    return fn;
+}
+
+// 2-D FP16 map: inner (contiguous) extent, outer extent, row stride in elements.
+int make_tmap(CUtensorMap* tm, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_in,
+              uint32_t box_out) {
+    auto fn = encode_fn();
+    if (!fn) {
+        set_error("cuTensorMapEncodeTiled unavailable from the driver");
+        return RBK_ERR_CUDA;
+    }
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {ld * 2};
+    cuuint32_t box[2] = {box_in, box_out};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled failed (%d): inner=%llu outer=%llu ld=%llu box=%ux%u", (int)r,
+                  (unsigned long long)inner, (unsigned long long)outer, (unsigned long long)ld, box_in, box_out);
+        return RBK_ERR_CUDA;
+    }
+    return RBK_OK;
+}
+
+template <int BN, int EPI>
+int launch(rbk_ctx* ctx, const rbk_gemm_desc* d, Params& p, cudaStream_t st) {
+    using C = Cfg<BN>;
+    CUtensorMap ta, tb;
+    if (!d->a_major) RBK_TRY(make_tmap(&ta, d->A, d->K, d->M, d->lda, 64, 128));
+    else RBK_TRY(make_tmap(&ta, d->A, d->M, d->K, d->lda, 64, 64));
+    if (!d->b_major) RBK_TRY(make_tmap(&tb, d->B, d->K, d->N, d->ldb, 64, BN));
+    else RBK_TRY(make_tmap(&tb, d->B, d->N, d->K, d->ldb, 64, 64));
+    static int configured_device = -1;   // attribute is per device; one device per process
+    if (configured_device != ctx->device) {
+        RBK_CUDA(cudaFuncSetAttribute(gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        configured_device = ctx->device;
+    }
+    int grid = p.units < ctx->num_sms ? p.units : ctx->num_sms;
+    gemm_kernel<BN, EPI><<<grid, kThreads, C::SMEM, st>>>(ta, tb, p);
+    RBK_LAUNCHED("gemm_kernel");
+    return RBK_OK;
+}
+
+}  // namespace gemm
+}  // namespace rbk
+
+using namespace rbk;
+using namespace rbk::gemm;
+
+extern "C" {
+
+int rbk_gemm(rbk_ctx* ctx, const rbk_gemm_desc* d, void* stream) {
+    RBK_REQUIRE(ctx && d && d->A && d->B && d->C, "rbk_gemm: null pointer");
+    RBK_REQUIRE(d->M > 0 && d->N > 0 && d->K > 0, "rbk_gemm: empty problem (M=%d N=%d K=%d)", d->M, d->N, d->K);
+    RBK_REQUIRE(d->epilogue >= RBK_EPI_STORE_F16 && d->epilogue <= RBK_EPI_STORE_F32, "rbk_gemm: bad epilogue");
+    RBK_REQUIRE(d->lda % 8 == 0 && d->ldb % 8 == 0 && d->ldc % 8 == 0 && (d->ld_aux % 8 == 0),
+                "rbk_gemm: leading dimensions must be multiples of 8 elements");
+    RBK_REQUIRE(aligned16(d->A) && aligned16(d->B) && aligned16(d->C) && (!d->aux || aligned16(d->aux)) &&
+                    (!d->aux_out || aligned16(d->aux_out)) && (!d->bias || aligned16(d->bias)),
+                "rbk_gemm: pointers must be 16-byte aligned");
+    RBK_REQUIRE(d->lda >= (d->a_major ? d->M : d->K) && d->ldb >= (d->b_major ? d->N : d->K),
+                "rbk_gemm: leading dimension smaller than the contiguous extent");
+    RBK_REQUIRE(d->epilogue != RBK_EPI_BIAS_GELU || (d->bias && d->aux_out), "rbk_gemm: BIAS_GELU needs bias and aux_out");
+    RBK_REQUIRE(d->epilogue != RBK_EPI_GELU_BWD || d->aux, "rbk_gemm: GELU_BWD needs aux (pre-activation)");
+    RBK_REQUIRE(!d->dbias_rows || d->epilogue == RBK_EPI_ACC_F32, "rbk_gemm: dbias_rows needs ACC_F32");
+    const int epi = d->epilogue;
+    const bool f32out = epi == RBK_EPI_ACC_F32 || epi == RBK_EPI_STORE_F32;
+    const int BN = (!f32out && d->N >= 512) ? 256 : 128;
+    Params p;
+    p.M = d->M; p.N = d->N; p.K = d->K;
+    p.m_blocks = (d->M + BM - 1) / BM;
+    p.n_blocks = (d->N + BN - 1) / BN;
+    p.k_blocks = (d->K + BK - 1) / BK;
+    int splits = 1;
+    if (epi == RBK_EPI_ACC_F32) {
+        const int tiles = p.m_blocks * p.n_blocks;
+        if (d->split_k > 0) splits = d->split_k;
+        else if (tiles < ctx->num_sms) splits = (ctx->num_sms + tiles - 1) / tiles;
+        int max_split = p.k_blocks / 4 > 0 ? p.k_blocks / 4 : 1;
+        if (splits > max_split) splits = max_split;
+        if (splits < 1) splits = 1;
+    }
+    p.kb_per_split = (p.k_blocks + splits - 1) / splits;
+    p.splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;
+    p.units = p.m_blocks * p.n_blocks * p.splits;
+    p.a_mn = d->a_major ? 1 : 0;
+    p.b_mn = d->b_major ? 1 : 0;
+    p.C = d->C; p.ldc = d->ldc;
+    p.bias = (const half*)d->bias;
+    p.aux = (const half*)d->aux;
+    p.ld_aux = d->ld_aux;
+    p.aux_out = (half*)d->aux_out;
+    p.dbias_rows = d->dbias_rows;
+    p.alpha = d->alpha;
+    p.err = ctx->tickets + kGemmError;
+    cudaStream_t st = as_stream(stream);
+    if (BN == 256) {
+        switch (epi) {
+            case RBK_EPI_STORE_F16: return launch<256, RBK_EPI_STORE_F16>(ctx, d, p, st);
+            case RBK_EPI_BIAS_GELU: return launch<256, RBK_EPI_BIAS_GELU>(ctx, d, p, st);
+            default: return launch<256, RBK_EPI_GELU_BWD>(ctx, d, p, st);
+        }
+    }
+    switch (epi) {
+        case RBK_EPI_STORE_F16: return launch<128, RBK_EPI_STORE_F16>(ctx, d, p, st);
+        case RBK_EPI_BIAS_GELU: return launch<128, RBK_EPI_BIAS_GELU>(ctx, d, p, st);
+        case RBK_EPI_GELU_BWD: return launch<128, RBK_EPI_GELU_BWD>(ctx, d, p, st);
+        case RBK_EPI_ACC_F32: return launch<128, RBK_EPI_ACC_F32>(ctx, d, p, st);
+        default: return launch<128, RBK_EPI_STORE_F32>(ctx, d, p, st);
+    }
+}
+
+int rbk_linear_fwd(rbk_ctx* ctx, void* Y, const void* X, const void* W, const void* bias, const void* residual,
+                   int N, int in, int out, void* stream) {
+    rbk_gemm_desc d = {};
+    d.M = N; d.N = out; d.K = in;
+    d.A = X; d.lda = in; d.a_major = 0;
+    d.B = W; d.ldb = in; d.b_major = 0;
+    d.C = Y; d.ldc = out;
+    d.epilogue = RBK_EPI_STORE_F16;
+    d.bias = bias;
+    d.aux = residual;
+    d.alpha = 1.0f;
+    return rbk_gemm(ctx, &d, stream);
+}
+
+int rbk_gemm_dgrad(rbk_ctx* ctx, void* dX, const void* dY, const void* W, int N, int in, int out,
+                   const void* gelu_pre, void* stream) {
+    rbk_gemm_desc d = {};
+    d.M = N; d.N = in; d.K = out;
+    d.A = dY; d.lda = out; d.a_major = 0;
+    d.B = W; d.ldb = in; d.b_major = 1;      // B(n=in, k=out) = W[out, in]
+    d.C = dX; d.ldc = in;
+    d.epilogue = gelu_pre ? RBK_EPI_GELU_BWD : RBK_EPI_STORE_F16;
+    d.aux = gelu_pre;
+    d.alpha = 1.0f;
+    return rbk_gemm(ctx, &d, stream);
+}
+
+int rbk_gemm_wgrad(rbk_ctx* ctx, float* dW, float* dbias, const void* dY, const void* X, int N, int in, int out,
+                   void* stream) {
+    rbk_gemm_desc d = {};
+    d.M = out; d.N = in; d.K = N;
+    d.A = dY; d.lda = out; d.a_major = 1;    // A(m=out, k=token) = dY[token, out]
+    d.B = X; d.ldb = in; d.b_major = 1;      // B(n=in, k=token) = X[token, in]
+    d.C = dW; d.ldc = in;
+    d.epilogue = RBK_EPI_ACC_F32;
+    d.dbias_rows = dbias;
+    d.alpha = 1.0f;
+    return rbk_gemm(ctx, &d, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,269 @@
+// ln.cu — LayerNorm forward and backward over FP16 rows (HBM-bound).
+//
+// Forward: one warp per row, the row held in registers (16-byte vectors), two
+// passes over registers for mean and biased variance, as
+// layer_norm_fp16_fwd_kernel / cpuops::layer_norm (reference
+// src/cuda_kernels.cu:183-225, src/cpu_mat.h:98-123).
+//
+// Backward: each thread owns 8 adjacent columns for every row its CTA visits,
+// so the dgamma / dbeta (/ dbias) column partials live in registers for the
+// whole kernel instead of the reference's per-element half atomics
+// (src/cuda_kernels.cu:279-282).  A CTA takes ROWS rows at a time (8 x 16 B of
+// dy and of x in flight per thread), reduces the two row sums across its warps
+// through shared memory, writes dx, and accumulates the partials.  The CTA
+// partials are reduced in a second, column-parallel launch in fixed order, so
+// the result is bitwise reproducible.
+#include "common.cuh"
+
+namespace rbk {
+namespace {
+
+template <int NV>
+__global__ void __launch_bounds__(256) ln_fwd_kernel(half* __restrict__ y, float* __restrict__ mean,
+                                                     float* __restrict__ rstd, const half* __restrict__ x,
+                                                     const half* __restrict__ g, const half* __restrict__ b, int N,
+                                                     int D, float eps) {
+    const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+    const int nvec = D >> 3;
+    const float invD = 1.0f / (float)D;
+    for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < N; row += gridDim.x * warps) {
+        const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * D);
+        float v[NV][8];
+        float s = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int c = lane + 32 * i;
+            if (c < nvec) {
+                h8_to_f(__ldg(xr + c), v[i]);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) s += v[i][j];
+            }
+        }
+        const float m = warp_sum(s) * invD;
+        float q = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int c = lane + 32 * i;
+            if (c < nvec) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) { const float d = v[i][j] - m; q += d * d; }
+            }
+        }
+        const float r = 1.0f / sqrtf(warp_sum(q) * invD + eps);
+        uint4* yr = reinterpret_cast<uint4*>(y + (size_t)row * D);
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int c = lane + 32 * i;
+            if (c < nvec) {
+                float gf[8], bf[8], o[8];
+                h8_to_f(__ldg(reinterpret_cast<const uint4*>(g) + c), gf);
+                h8_to_f(__ldg(reinterpret_cast<const uint4*>(b) + c), bf);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) o[j] = gf[j] * (v[i][j] - m) * r + bf[j];
+                yr[c] = f_to_h8(o);
+            }
+        }
+        if (lane == 0) { mean[row] = m; rstd[row] = r; }
+    }
+}
+
+constexpr int kLnRows = 4;   // rows per CTA iteration in the backward
+
+// part layout: [gridDim.x][3][D]  (dgamma | dbeta | dbias partials)
+template <bool kRefFormula, bool kRes, bool kBias>
+__global__ void __launch_bounds__(512) ln_bwd_kernel(half* __restrict__ dx, float* __restrict__ part,
+                                                      const half* __restrict__ dy, const half* __restrict__ dres,
+                                                      const half* __restrict__ x, const half* __restrict__ g,
+                                                      const float* __restrict__ mean, const float* __restrict__ rstd,
+                                                      int N, int D) {
+    constexpr int R = kLnRows;
+    __shared__ float red[2][2 * R][32];   // [buffer][row-sum][warp]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+    const int nvec = D >> 3;
+    const bool own = tid < nvec;          // this thread owns columns [8 tid, 8 tid + 8)
+    const float invD = 1.0f / (float)D;
+    float gam[8], pg[8], pb[8], pd[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { pg[j] = 0.0f; pb[j] = 0.0f; pd[j] = 0.0f; gam[j] = 0.0f; }
+    if (own) h8_to_f(__ldg(reinterpret_cast<const uint4*>(g) + tid), gam);
+
+    int buf = 0;
+    const int ngroups = (N + R - 1) / R;
+    for (int grp = blockIdx.x; grp < ngroups; grp += gridDim.x, buf ^= 1) {
+        const int row0 = grp * R;
+        uint4 dyv[R], xv[R];
+        float mr[R], rr[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int row = row0 + r;
+            const bool ok = own && row < N;
+            dyv[r] = ok ? __ldg(reinterpret_cast<const uint4*>(dy + (size_t)row * D) + tid) : make_uint4(0, 0, 0, 0);
+            xv[r] = ok ? __ldg(reinterpret_cast<const uint4*>(x + (size_t)row * D) + tid) : make_uint4(0, 0, 0, 0);
+            mr[r] = row < N ? __ldg(mean + row) : 0.0f;
+            rr[r] = row < N ? __ldg(rstd + row) : 0.0f;
+        }
+        // Row sums: ts1 = sum dy*g, ts2 = sum dy*g*(x - mean).
+        float ts[2 * R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            float d[8], xx[8];
+            h8_to_f(dyv[r], d);
+            h8_to_f(xv[r], xx);
+            float s1 = 0.0f, s2 = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float dg = d[j] * gam[j];
+                s1 += dg;
+                s2 += dg * (xx[j] - mr[r]);
+            }
+            ts[2 * r] = warp_sum(s1);
+            ts[2 * r + 1] = warp_sum(s2);
+        }
+        if (lane == 0) {
+#pragma unroll
+            for (int k = 0; k < 2 * R; ++k) red[buf][k][warp] = ts[k];
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 2 * R; ++k) {
+            float s = 0.0f;
+            for (int w = 0; w < nwarps; ++w) s += red[buf][k][w];
+            ts[k] = s;
+        }
+        // (the other buffer is written next iteration; the barrier above orders
+        //  this iteration's reads of `buf` before the iteration after next)
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int row = row0 + r;
+            if (!own || row >= N) continue;
+            float d[8], xx[8], o[8];
+            h8_to_f(dyv[r], d);
+            h8_to_f(xv[r], xx);
+            float rs[8];
+            if (kRes) h8_to_f(__ldg(reinterpret_cast<const uint4*>(dres + (size_t)row * D) + tid), rs);
+            const float inv = rr[r];
+            const float c2 = kRefFormula ? inv : inv * inv;
+            const float t1 = ts[2 * r], t2 = ts[2 * r + 1];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float xm = xx[j] - mr[r];
+                float v = inv * (d[j] * gam[j] - (t1 + xm * c2 * t2) * invD);
+                if (kRes) v += rs[j];
+                o[j] = v;
+                pg[j] += d[j] * xm * inv;
+                pb[j] += d[j];
+                if (kBias) pd[j] += v;
+            }
+            reinterpret_cast<uint4*>(dx + (size_t)row * D)[tid] = f_to_h8(o);
+        }
+    }
+    if (own) {
+        float* pr = part + (size_t)blockIdx.x * 3 * D + 8 * tid;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            pr[j] = pg[j];
+            pr[D + j] = pb[j];
+            pr[2 * D + j] = pd[j];
+        }
+    }
+}
+
+// dgamma[c] += sum_b part[b][0][c]; dbeta[c] += sum_b part[b][1][c]; dbias likewise.
+__global__ void ln_bwd_reduce_kernel(float* __restrict__ dg, float* __restrict__ db, float* __restrict__ dbias,
+                                     const float* __restrict__ part, int nblk, int D) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    const int which = blockIdx.y;
+    if (c >= D) return;
+    float* out = which == 0 ? dg : which == 1 ? db : dbias;
+    if (!out) return;
+    float s = 0.0f;
+    for (int b = 0; b < nblk; ++b) s += part[(size_t)b * 3 * D + (size_t)which * D + c];
+    out[c] += s;
+}
+
+template <int NV>
+void launch_fwd(int blocks, cudaStream_t st, half* y, float* mean, float* rstd, const half* x, const half* g,
+                const half* b, int N, int D, float eps) {
+    ln_fwd_kernel<NV><<<blocks, 256, 0, st>>>(y, mean, rstd, x, g, b, N, D, eps);
+}
+
+}  // namespace
+}  // namespace rbk
+
+using namespace rbk;
+
+extern "C" {
+
+int rbk_ln_fwd(rbk_ctx* ctx, void* y, float* mean, float* rstd, const void* x, const void* gamma, const void* beta,
+               int N, int D, float eps, void* stream) {
+    RBK_REQUIRE(ctx && y && mean && rstd && x && gamma && beta, "rbk_ln_fwd: null pointer");
+    RBK_REQUIRE(N > 0 && D > 0 && D % 8 == 0 && D <= 8192, "rbk_ln_fwd: need D %% 8 == 0 and D <= 8192 (D=%d)", D);
+    RBK_REQUIRE(aligned16(y) && aligned16(x) && aligned16(gamma) && aligned16(beta),
+                "rbk_ln_fwd: tensors must be 16-byte aligned");
+    const int nv = (D / 8 + 31) / 32;
+    const int rows_per_block = 8;
+    int blocks = (N + rows_per_block - 1) / rows_per_block;
+    blocks = blocks < ctx->num_sms * 16 ? blocks : ctx->num_sms * 16;
+    cudaStream_t st = as_stream(stream);
+    auto Y = (half*)y;
+    auto X = (const half*)x;
+    auto G = (const half*)gamma;
+    auto Bt = (const half*)beta;
+    switch (nv) {
+        case 1: launch_fwd<1>(blocks, st, Y, mean, rstd, X, G, Bt, N, D, eps); break;
+        case 2: launch_fwd<2>(blocks, st, Y, mean, rstd, X, G, Bt, N, D, eps); break;
+        case 3: launch_fwd<3>(blocks, st, Y, mean, rstd, X, G, Bt, N, D, eps); break;
+        case 4: launch_fwd<4>(blocks, st, Y, mean, rstd, X, G, Bt, N, D, eps); break;
+        case 5: case 6: launch_fwd<6>(blocks, st, Y, mean, rstd, X, G, Bt, N, D, eps); break;
+        case 7: case 8: launch_fwd<8>(blocks, st, Y, mean, rstd, X, G, Bt, N, D, eps); break;
+        case 9: case 10: case 11: case 12: launch_fwd<12>(blocks, st, Y, mean, rstd, X, G, Bt, N, D, eps); break;
+        case 13: case 14: case 15: case 16: launch_fwd<16>(blocks, st, Y, mean, rstd, X, G, Bt, N, D, eps); break;
+        default: launch_fwd<32>(blocks, st, Y, mean, rstd, X, G, Bt, N, D, eps); break;
+    }
+    RBK_LAUNCHED("ln_fwd_kernel");
+    return RBK_OK;
+}
+
+int rbk_ln_bwd(rbk_ctx* ctx, void* dx, float* dgamma, float* dbeta, float* dbias_out, const void* dy,
+               const void* dres, const void* x, const void* gamma, const float* mean, const float* rstd, int N,
+               int D, int flags, void* stream) {
+    RBK_REQUIRE(ctx && dx && dgamma && dbeta && dy && x && gamma && mean && rstd, "rbk_ln_bwd: null pointer");
+    RBK_REQUIRE(N > 0 && D > 0 && D % 8 == 0 && D <= 4096, "rbk_ln_bwd: need D %% 8 == 0 and D <= 4096 (D=%d)", D);
+    RBK_REQUIRE(aligned16(dx) && aligned16(dy) && aligned16(x) && aligned16(gamma) && (!dres || aligned16(dres)),
+                "rbk_ln_bwd: tensors must be 16-byte aligned");
+    const int threads = ((D / 8 + 31) / 32) * 32;
+    const int ngroups = (N + kLnRows - 1) / kLnRows;
+    int per_sm = 2048 / threads;
+    if (per_sm > 4) per_sm = 4;
+    if (per_sm < 1) per_sm = 1;
+    int blocks = ctx->num_sms * per_sm;
+    if (blocks > ngroups) blocks = ngroups;
+    void* ws;
+    RBK_TRY(ctx_scratch(ctx, sizeof(float) * 3 * (size_t)D * blocks, &ws));
+    float* part = (float*)ws;
+    cudaStream_t st = as_stream(stream);
+    const bool ref = (flags & RBK_LN_REFERENCE_FORMULA) != 0;
+    const bool res = dres != nullptr, bias = dbias_out != nullptr;
+    auto DX = (half*)dx;
+    auto DY = (const half*)dy;
+    auto DR = (const half*)dres;
+    auto X = (const half*)x;
+    auto G = (const half*)gamma;
+#define RBK_LN_BWD(R_, S_, B_) \
+    ln_bwd_kernel<R_, S_, B_><<<blocks, threads, 0, st>>>(DX, part, DY, DR, X, G, mean, rstd, N, D)
+    if (ref) {
+        if (res) { if (bias) RBK_LN_BWD(true, true, true); else RBK_LN_BWD(true, true, false); }
+        else { if (bias) RBK_LN_BWD(true, false, true); else RBK_LN_BWD(true, false, false); }
+    } else {
+        if (res) { if (bias) RBK_LN_BWD(false, true, true); else RBK_LN_BWD(false, true, false); }
+        else { if (bias) RBK_LN_BWD(false, false, true); else RBK_LN_BWD(false, false, false); }
+    }
+#undef RBK_LN_BWD
+    RBK_LAUNCHED("ln_bwd_kernel");
+    dim3 rg((D + 255) / 256, bias ? 3 : 2);
+    ln_bwd_reduce_kernel<<<rg, 256, 0, st>>>(dgamma, dbeta, dbias_out, part, blocks, D);
+    RBK_LAUNCHED("ln_bwd_reduce_kernel");
+    return RBK_OK;
+}
+
+}  // extern "C"

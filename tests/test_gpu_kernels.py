@@ -1,0 +1,353 @@
+"""Parity of the sm_100a kernels with the CPU oracle (and float64 torch for GEMMs).
+
+Inputs are seeded; the oracle receives exactly the FP16-rounded values the GPU
+reads.  Tolerances (relative L2 unless stated):
+  FP16 outputs 3e-3 (one FP16 rounding ~ 2.4e-4 rms plus FP32 summation order),
+  FP32 reductions 1e-4.
+"""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+F16_TOL = 3e-3
+F32_TOL = 1e-4
+
+
+def rel(a, b):
+    a = np.asarray(a, np.float64); b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from rbk import ops as o
+    return o
+
+
+def h(a, dev="cuda"):
+    return torch.from_numpy(np.ascontiguousarray(a, np.float16)).to(dev)
+
+
+def f(t):
+    return t.float().cpu().numpy()
+
+
+# ------------------------------------------------------------------ LayerNorm --
+
+@pytest.mark.parametrize("N,D", [(300, 256), (257, 768), (64, 1024), (33, 2048)])
+def test_ln_fwd(ops, ora, N, D):
+    rng = np.random.default_rng(N + D)
+    x = (rng.standard_normal((N, D)) * 0.5 + 0.1).astype(np.float16)
+    g = (1 + 0.1 * rng.standard_normal(D)).astype(np.float16)
+    b = (0.1 * rng.standard_normal(D)).astype(np.float16)
+    y, mean, rstd = ops.ln_fwd(h(x), h(g), h(b))
+    ye, me, re_ = ora.ln_fwd(x.astype(np.float32), g.astype(np.float32), b.astype(np.float32))
+    assert rel(f(y), ye) < F16_TOL
+    assert rel(mean.cpu().numpy(), me) < 1e-5 and rel(rstd.cpu().numpy(), re_) < 1e-5
+
+
+@pytest.mark.parametrize("N,D,res,bias", [(300, 256, False, False), (257, 768, True, True), (129, 1024, True, False),
+                                          (40, 2048, False, True)])
+def test_ln_bwd_exact(ops, ora, N, D, res, bias):
+    rng = np.random.default_rng(7 * N + D)
+    x = (0.05 * rng.standard_normal((N, D))).astype(np.float16)     # small variance: rstd ~ 20
+    g = (1 + 0.02 * rng.standard_normal(D)).astype(np.float16)
+    dy = rng.standard_normal((N, D)).astype(np.float16)
+    dres = rng.standard_normal((N, D)).astype(np.float16) if res else None
+    _, mean, rstd = ops.ln_fwd(h(x), h(g), h(np.zeros(D, np.float16)))
+    dx, dg, db, dbias = ops.ln_bwd(h(dy), h(x), h(g), mean, rstd, dres=None if dres is None else h(dres),
+                                   want_dbias=bias)
+    ex, eg, eb = ora.ln_bwd(dy.astype(np.float32), x.astype(np.float32), g.astype(np.float32),
+                            mean.cpu().numpy(), rstd.cpu().numpy(),
+                            dres=None if dres is None else dres.astype(np.float32))
+    assert rel(f(dx), ex) < F16_TOL
+    assert rel(dg.cpu().numpy(), eg) < F32_TOL and rel(db.cpu().numpy(), eb) < F32_TOL
+    if bias:
+        assert rel(dbias.cpu().numpy(), ex.sum(0)) < 2e-3
+
+
+def test_ln_bwd_reference_formula_matches_reference_engine(ops, ora):
+    """RBK_LN_REFERENCE_FORMULA reproduces cpuops::layer_norm_backward's golden vectors."""
+    import os
+    gold = np.load(os.path.join(os.path.dirname(__file__), "golden", "ref_ops.npz"))
+    x16 = gold["ln_x"].astype(np.float16); dy16 = gold["ln_dy"].astype(np.float16)
+    g16 = gold["ln_g"].astype(np.float16)
+    mean = torch.from_numpy(gold["ln_mean"]).cuda(); rstd = torch.from_numpy(gold["ln_rstd"]).cuda()
+    dx, dg, db, _ = ops.ln_bwd(h(dy16), h(x16), h(g16), mean, rstd, ref_formula=True)
+    # inputs were rounded to FP16 for the GPU: compare against the oracle on the same rounded inputs,
+    # and against the reference's own vectors with the rounding tolerance.
+    ex, eg, eb = ora.ln_bwd(dy16.astype(np.float32), x16.astype(np.float32), g16.astype(np.float32),
+                            gold["ln_mean"], gold["ln_rstd"], ref_formula=True)
+    assert rel(f(dx), ex) < F16_TOL
+    assert rel(f(dx), gold["ln_dx"]) < 5e-3
+    assert rel(dg.cpu().numpy(), gold["ln_dg"]) < 5e-3 and rel(db.cpu().numpy(), gold["ln_db"]) < 5e-3
+
+
+def test_ln_bwd_config_2a_full_size(ops, ora):
+    """[16384, 1024] FP16, x~N(0,1), dy~N(0,1), gamma~N(1,0.02): full-size parity."""
+    rng = np.random.default_rng(2)
+    N, D = 16384, 1024
+    x = rng.standard_normal((N, D), dtype=np.float32).astype(np.float16)
+    dy = rng.standard_normal((N, D), dtype=np.float32).astype(np.float16)
+    g = (1 + 0.02 * rng.standard_normal(D)).astype(np.float16)
+    _, mean, rstd = ops.ln_fwd(h(x), h(g), h(np.zeros(D, np.float16)))
+    dx, dg, db, _ = ops.ln_bwd(h(dy), h(x), h(g), mean, rstd)
+    ex, eg, eb = ora.ln_bwd(dy.astype(np.float32), x.astype(np.float32), g.astype(np.float32),
+                            mean.cpu().numpy(), rstd.cpu().numpy())
+    assert rel(f(dx), ex) < F16_TOL
+    assert rel(dg.cpu().numpy(), eg) < F32_TOL and rel(db.cpu().numpy(), eb) < F32_TOL
+    # deterministic column reduction: bitwise-identical rerun
+    dx2, dg2, db2, _ = ops.ln_bwd(h(dy), h(x), h(g), mean, rstd)
+    assert torch.equal(dx, dx2) and torch.equal(dg, dg2) and torch.equal(db, db2)
+
+
+# ------------------------------------------------------------- cross entropy --
+
+@pytest.mark.parametrize("N,V,ld", [(64, 4096, 4096), (37, 1000, 1008), (16, 50257, 50264), (8, 65536, 65536)])
+def test_softmax_xent(ops, ora, N, V, ld):
+    rng = np.random.default_rng(V)
+    z = np.zeros((N, ld), np.float16)
+    z[:, :V] = (2.0 * rng.standard_normal((N, V))).astype(np.float16)
+    t = rng.integers(0, V, N).astype(np.int32)
+    scale = 65536.0 / N
+    d, rl = ops.softmax_xent_bwd(h(z), torch.from_numpy(t).cuda(), scale=scale, V=V)
+    z32 = z[:, :V].astype(np.float32)
+    e = ora.ce_bwd(z32, t, scale * N)           # oracle divides by N itself
+    assert rel(f(d)[:, :V], e) < F16_TOL
+    _, erl, _ = ora.ce_fwd(z32, t)
+    assert rel(rl.cpu().numpy(), erl) < 1e-4
+
+
+def test_softmax_xent_inplace_and_bad_target(ops, ora):
+    rng = np.random.default_rng(1)
+    N, V = 12, 777
+    ld = 784
+    z = np.zeros((N, ld), np.float16)
+    z[:, :V] = rng.standard_normal((N, V)).astype(np.float16)
+    t = rng.integers(0, V, N).astype(np.int32)
+    t[3] = V + 5
+    zt = h(z)
+    d, rl = ops.softmax_xent_bwd(zt, torch.from_numpy(t).cuda(), scale=1.0, V=V, out=zt)
+    assert d.data_ptr() == zt.data_ptr()
+    rl = rl.cpu().numpy()
+    assert np.isnan(rl[3]) and np.all(np.isfinite(np.delete(rl, 3)))
+    assert np.all(f(d)[3, :V] == 0)
+    good = np.delete(np.arange(N), 3)
+    e = ora.ce_bwd(z[good, :V].astype(np.float32), t[good], len(good))
+    assert rel(f(d)[good, :V], e) < F16_TOL
+
+
+def test_softmax_xent_config_2b_full_size(ops, ora):
+    """[8192, 32000] FP16 logits ~N(0,2): rows sum to zero; 256 rows vs the oracle.
+    The gradient carries the loss scale 65536 (as in training): unscaled (p - y)/N
+    would sit in FP16's subnormal range."""
+    rng = np.random.default_rng(3)
+    N, V = 8192, 32000
+    scale = 65536.0 / N
+    z = (2.0 * rng.standard_normal((N, V), dtype=np.float32)).astype(np.float16)
+    t = rng.integers(0, V, N).astype(np.int32)
+    d, rl = ops.softmax_xent_bwd(h(z), torch.from_numpy(t).cuda(), scale=scale)
+    rows = np.sort(rng.choice(N, 256, replace=False))
+    dd = d[torch.from_numpy(rows).cuda()].float().cpu().numpy()
+    e = ora.ce_bwd(z[rows].astype(np.float32), t[rows], scale * len(rows))
+    assert rel(dd, e) < F16_TOL
+    rowsum = d.float().sum(1).abs().max().item()
+    assert rowsum < 0.01 * scale
+    _, erl, _ = ora.ce_fwd(z[rows].astype(np.float32), t[rows])
+    assert rel(rl.cpu().numpy()[rows], erl) < 1e-4
+
+
+# ---------------------------------------------------- attention softmax bwd --
+
+def _softmax_causal(rng, nmat, T):
+    s = rng.standard_normal((nmat, T, T)).astype(np.float32)
+    mask = np.tril(np.ones((T, T), bool))
+    s = np.where(mask, s, -1e9)
+    p = np.exp(s - s.max(-1, keepdims=True))
+    return (p / p.sum(-1, keepdims=True)).astype(np.float16), mask
+
+
+@pytest.mark.parametrize("nmat,T", [(3, 136), (2, 1024), (1, 64)])
+def test_attn_softmax_bwd(ops, ora, nmat, T):
+    rng = np.random.default_rng(T)
+    P, mask = _softmax_causal(rng, nmat, T)
+    dP = rng.standard_normal((nmat, T, T)).astype(np.float16)
+    sentinel = torch.full((nmat, T, T), 7.0, dtype=torch.float16, device="cuda")
+    dS = ops.attn_softmax_bwd(h(P), h(dP), causal=True, out=sentinel)
+    e = ora.causal_softmax_bwd(dP.astype(np.float32), P.astype(np.float32))
+    got = f(dS)
+    assert rel(got[:, mask], e[:, mask]) < F16_TOL
+    assert np.all(got[:, ~mask] == 7.0)          # strict upper triangle untouched
+
+
+def test_attn_softmax_bwd_config_2c_full_size(ops, ora):
+    """B=8, H=16, T=1024 causal: rows of dS sum to ~0 everywhere; 2 matrices vs the oracle."""
+    rng = np.random.default_rng(4)
+    nmat, T = 8 * 16, 1024
+    s = torch.randn(nmat, T, T, device="cuda")
+    s = s.masked_fill(torch.triu(torch.ones(T, T, dtype=torch.bool, device="cuda"), 1), -1e9)
+    P = torch.softmax(s, -1).half()
+    dP = torch.randn(nmat, T, T, device="cuda").half()
+    dS = ops.attn_softmax_bwd(P, dP, causal=True)
+    mask = torch.tril(torch.ones(T, T, dtype=torch.bool, device="cuda"))
+    rs = (dS.float() * mask).sum(-1)
+    # sum_j dS_ij = dot - dot * sum_j P_ij ~ 0 (FP16 P sums to 1 within ~1e-3)
+    assert rs.abs().max().item() < 0.05 * (dP.float().abs().max().item())
+    for i in (0, nmat - 1):
+        e = ora.causal_softmax_bwd(dP[i:i + 1].float().cpu().numpy(), P[i:i + 1].float().cpu().numpy())
+        m = mask.cpu().numpy()
+        assert rel(dS[i:i + 1].float().cpu().numpy()[:, m], e[:, m]) < F16_TOL
+
+
+# --------------------------------------------------------------- embeddings --
+
+def test_embeddings(ops):
+    rng = np.random.default_rng(5)
+    V, T, D, B, S = 97, 40, 64, 3, 32
+    tok_emb = rng.standard_normal((V, D)).astype(np.float16)
+    pos_emb = rng.standard_normal((T, D)).astype(np.float16)
+    tokens = rng.integers(0, V, B * S).astype(np.int32)
+    x = ops.embed_fwd(h(tok_emb), h(pos_emb), torch.from_numpy(tokens).cuda(), B, S)
+    ex = tok_emb.astype(np.float32)[tokens] + np.tile(pos_emb[:S].astype(np.float32), (B, 1))
+    assert rel(f(x), ex) < F16_TOL
+    dx = rng.standard_normal((B * S, D)).astype(np.float16)
+    dtok, dpos = ops.embed_bwd(h(dx), torch.from_numpy(tokens).cuda(), B, S, V)
+    et = np.zeros((V, D), np.float32)
+    np.add.at(et, tokens, dx.astype(np.float32))
+    ep = dx.astype(np.float32).reshape(B, S, D).sum(0)
+    assert rel(dtok.cpu().numpy(), et) < 1e-6 and rel(dpos.cpu().numpy(), ep) < 1e-6
+
+
+# --------------------------------------------------------------------- tail --
+
+@pytest.mark.parametrize("overflow,clip", [(False, False), (True, False), (False, True)])
+def test_adam_tail(ops, ora, overflow, clip):
+    rng = np.random.default_rng(6 + overflow + 2 * clip)
+    segs = [(0, 4096), (4096, 64), (4160, 100000 - 4160 - 64), (100000 - 64, 64)]
+    n = 100000
+    p = (0.02 * rng.standard_normal(n)).astype(np.float32)
+    m = (1e-3 * rng.standard_normal(n)).astype(np.float32)
+    v = np.abs(1e-6 * rng.standard_normal(n)).astype(np.float32)
+    g = (65536.0 * 1e-3 * rng.standard_normal(n)).astype(np.float32)
+    if overflow:
+        g[77777] = np.inf
+    sc = ops.new_scaler(65536.0, 2000)
+    tp, tg, tm, tv = (torch.from_numpy(a.copy()).cuda() for a in (p, g, m, v))
+    p16 = torch.empty(n, dtype=torch.float16, device="cuda")
+    so = [s for s, _ in segs]; sl = [l for _, l in segs]
+    ops.adam_tail(tp, tg, tm, tv, p16, sc, lr=3e-4, b1=0.9, b2=0.999, eps=1e-8, wd=0.1, t=3,
+                  seg_off=so if clip else None, seg_len=sl if clip else None, max_norm=0.05 if clip else 0.0)
+    st = ops.read_scaler(sc)
+    osc = ora.Scaler(65536.0, 0, 2000)
+    ep, eg, em, ev = p.copy(), g.copy(), m.copy(), v.copy()
+    skip = ora.adam_tail(ep, eg, em, ev, so, sl, 3e-4, 0.9, 0.999, 1e-8, 0.1, 3, osc, 0.05 if clip else 0.0)
+    assert st.skipped == skip == int(overflow)
+    assert st.scale == osc.scale and st.unskipped == osc.unskipped and st.status == 0
+    assert torch.count_nonzero(tg).item() == 0
+    assert rel(tp.cpu().numpy(), ep) < 1e-6 and rel(tm.cpu().numpy(), em) < 1e-5
+    assert rel(tv.cpu().numpy(), ev) < 1e-5
+    if not overflow:
+        assert rel(p16.float().cpu().numpy(), ep) < 1e-3
+    else:
+        assert np.array_equal(tp.cpu().numpy(), p)
+
+
+def test_adam_tail_growth_and_device_step_counter(ops):
+    n = 4096
+    sc = ops.new_scaler(1024.0, 3)
+    tp = torch.zeros(n, device="cuda"); tm = torch.zeros(n, device="cuda"); tv = torch.zeros(n, device="cuda")
+    for k in range(3):
+        tg = torch.ones(n, device="cuda")
+        ops.adam_tail(tp, tg, tm, tv, None, sc, lr=1e-3, t=0)
+    st = ops.read_scaler(sc)
+    assert st.applied_steps == 3 and st.scale == 2048.0 and st.unskipped == 0
+
+
+# --------------------------------------------------------------------- GEMM --
+
+def _ref_gemm(A, B, a_major, b_major):
+    A = torch.from_numpy(A.astype(np.float32)); B = torch.from_numpy(B.astype(np.float32))
+    Am = A.T if a_major else A
+    Bm = B.T if b_major else B
+    return (Am.double() @ Bm.double().T).numpy()
+
+
+def _mk(rng, rows, cols, ld=None):
+    ld = ld or cols
+    a = np.zeros((rows, ld), np.float16)
+    a[:, :cols] = (rng.standard_normal((rows, cols)) * 0.5).astype(np.float16)
+    return a
+
+
+@pytest.mark.parametrize("M,N,K,a_major,b_major", [
+    (256, 384, 192, 0, 0),     # forward linear (both K-major)
+    (200, 72, 100, 0, 0),      # ragged M, N, K (K padded to ld=104)
+    (300, 136, 200, 0, 1),     # dgrad: B MN-major
+    (192, 160, 1000, 1, 1),    # wgrad shape: both MN-major
+    (256, 640, 128, 0, 0),     # BN=256 path
+    (384, 1024, 320, 0, 1),    # BN=256 with MN-major B
+    (128, 512, 64, 1, 0),      # A MN-major, BN=256
+])
+def test_gemm_store(ops, M, N, K, a_major, b_major):
+    rng = np.random.default_rng(M * 7 + N + K)
+    kpad = (K + 7) // 8 * 8
+    A = _mk(rng, K, M, (M + 7) // 8 * 8) if a_major else _mk(rng, M, K, kpad)
+    B = _mk(rng, K, N, (N + 7) // 8 * 8) if b_major else _mk(rng, N, K, kpad)
+    ref = _ref_gemm(A[:, :M] if a_major else A[:, :K], B[:, :N] if b_major else B[:, :K], a_major, b_major)
+    ldc = (N + 7) // 8 * 8
+    Cg = torch.full((M, ldc), 5.0, dtype=torch.float16, device="cuda")
+    ops.gemm(h(A), h(B), M, N, K, a_major, b_major, C_out=Cg, ldc=ldc)
+    got = f(Cg)
+    assert rel(got[:, :N], ref) < F16_TOL
+    if ldc > N:
+        assert np.all(got[:, N:] == 5.0)
+    C32 = torch.zeros((M, ldc), dtype=torch.float32, device="cuda")
+    ops.gemm(h(A), h(B), M, N, K, a_major, b_major, C_out=C32, ldc=ldc, epilogue=ops.EPI_STORE_F32)
+    assert rel(C32.cpu().numpy()[:, :N], ref) < F32_TOL
+
+
+def test_gemm_bias_residual_gelu(ops):
+    rng = np.random.default_rng(11)
+    M, N, K = 320, 768, 256
+    X = _mk(rng, M, K); W = _mk(rng, N, K) * np.float16(0.1)
+    b = (0.1 * rng.standard_normal(N)).astype(np.float16)
+    R = _mk(rng, M, N)
+    ref = _ref_gemm(X, W, 0, 0) + b.astype(np.float64)
+    Y = ops.linear_fwd(h(X), h(W), bias=h(b), residual=h(R))
+    assert rel(f(Y), ref + R.astype(np.float64)) < F16_TOL
+    pre = torch.empty(M, N, dtype=torch.float16, device="cuda")
+    act = torch.empty(M, N, dtype=torch.float16, device="cuda")
+    ops.gemm(h(X), h(W), M, N, K, C_out=pre, epilogue=ops.EPI_BIAS_GELU, bias=h(b), aux_out=act)
+    assert rel(f(pre), ref) < F16_TOL
+    import oracle
+    assert rel(f(act), oracle.act_fwd(f(pre))) < F16_TOL
+
+
+def test_gemm_dgrad_gelu_bwd(ops, ora):
+    rng = np.random.default_rng(12)
+    Ntok, fin, out = 260, 192, 320
+    dY = _mk(rng, Ntok, out)
+    W = _mk(rng, out, fin)
+    pre = _mk(rng, Ntok, fin)
+    dX = ops.gemm_dgrad(h(dY), h(W), gelu_pre=h(pre))
+    ref = (dY.astype(np.float64) @ W.astype(np.float64)) * ora.act_grad(pre.astype(np.float32)).astype(np.float64)
+    assert rel(f(dX), ref) < F16_TOL
+    dX2 = ops.gemm_dgrad(h(dY), h(W))
+    assert rel(f(dX2), dY.astype(np.float64) @ W.astype(np.float64)) < F16_TOL
+
+
+@pytest.mark.parametrize("Ntok,fin,out", [(1000, 160, 192), (4096, 768, 2304), (333, 64, 136)])
+def test_gemm_wgrad_with_bias_grad(ops, Ntok, fin, out):
+    rng = np.random.default_rng(Ntok + fin)
+    dY = _mk(rng, Ntok, out)
+    X = _mk(rng, Ntok, fin)
+    dW0 = rng.standard_normal((out, fin)).astype(np.float32)
+    db0 = rng.standard_normal(out).astype(np.float32)
+    dW = torch.from_numpy(dW0.copy()).cuda(); db = torch.from_numpy(db0.copy()).cuda()
+    ops.gemm_wgrad(h(dY), h(X), dW=dW, dbias=db)
+    ref = dW0 + dY.astype(np.float64).T @ X.astype(np.float64)
+    assert rel(dW.cpu().numpy(), ref) < F32_TOL
+    assert rel(db.cpu().numpy(), db0 + dY.astype(np.float64).sum(0)) < F32_TOL
