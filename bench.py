@@ -1,0 +1,421 @@
+"""Benchmark: one rubidium-train training step (forward + backward + fused
+Adam tail) per step on synthetic data, through librbk's sm_100a kernels.
+
+Default workload (N=1): the GPT-2-small-shaped decoder — 12 layers, d=768,
+12 heads, FFN 3072 (GELU), vocab 50257, seq 1024, micro-batch 16 per GPU,
+FP16 activations / FP32 masters, dynamic loss scale from 65536, per-layer
+activation checkpointing, random init N(0, 0.02), uniform random tokens.
+With --gpus N (torchrun, one rank per GPU) the same per-GPU work runs data
+parallel with bucketed (25 MB) NCCL all-reduce overlapped with the backward
+("scaling": "weak").  --workload 1.3b selects the 1.3B decoder (24 x 2048,
+16 heads, FFN 8192, seq 2048, micro-batch 8).
+
+Printed by rank 0: one JSON line (see the keys below).  Timing: CUDA events
+on the launching stream, barrier + synchronize around the timed region, max
+over ranks.  Weights, activations and logits exceed the 126 MB L2, so no L2
+flush is needed between steps.  --impl reference times the CPU restatement
+of the same step (the reference's own engine cannot run a backward) on the
+host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "rubidium-train_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "train tokens/s/GPU (fwd+bwd+Adam), backward ms/step, % of TC/HBM roofline"
+
+WORKLOADS = {
+    "gpt2-small": dict(cfg=dict(V=50257, T=1024, D=768, H=12, L=12, FF=3072), batch=16, seq=1024,
+                       name="GPT-2-small decoder (L12 d768 H12 FF3072 V50257), seq 1024, micro-batch 16/GPU"),
+    "1.3b": dict(cfg=dict(V=50257, T=2048, D=2048, H=16, L=24, FF=8192), batch=8, seq=2048,
+                 name="1.3B decoder (L24 d2048 H16 FF8192 V50257), seq 2048, micro-batch 8/GPU"),
+    "tiny": dict(cfg=dict(V=4096, T=128, D=256, H=4, L=4, FF=1024), batch=8, seq=128,
+                 name="tiny decoder (L4 d256 H4 FF1024 V4096), seq 128, batch 8"),
+}
+
+CAT_NAMES = ["gemm", "attn_fwd", "attn_bwd", "ln_fwd", "ln_bwd", "softmax_xent", "adam_tail", "embedding", "other"]
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), float(p["bf16_tflops_sustained"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def mm_params(cfg):
+    D, F, L, V = cfg["D"], cfg["FF"], cfg["L"], cfg["V"]
+    return L * (4 * D * D + 2 * D * F) + V * D
+
+
+def gemm_flops_per_step(cfg, ntok, ckpt=True):
+    """Algorithmic tensor-core FLOPs of the GEMMs in one step: forward 2 P, backward
+    4 P per token (P = matmul parameters), plus the checkpoint recompute of the
+    QKV and W1 projections."""
+    D, F, L = cfg["D"], cfg["FF"], cfg["L"]
+    P = mm_params(cfg)
+    rec = L * (3 * D * D + D * F) if ckpt else 0
+    return 2.0 * ntok * (3 * P + rec)
+
+
+def train_flops_per_token(cfg, seq):
+    """6 P + 6 L T D (causal attention), recompute excluded (the published convention)."""
+    return 6.0 * mm_params(cfg) + 6.0 * cfg["L"] * seq * cfg["D"]
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.dev = device_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.dev}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r.split(",") for r in out.strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
+        loaded = [s for s in sm if s > 0.5 * (max(mx) if mx else 1)] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------- CPU legs ----
+
+def cpu_sample(workload, seq=128):
+    """The CPU restatement (oracle) of one fwd+bwd+AdamW step of the same model
+    at micro-batch 1 over `seq` tokens; returns (tokens/s, seconds, threads)."""
+    import numpy as np
+    import oracle
+    cfg = dict(WORKLOADS[workload]["cfg"])
+    rng = np.random.default_rng(0)
+    params = oracle.init_params(cfg, seed=1)
+    tok = rng.integers(0, cfg["V"], seq).astype(np.int32)
+    tgt = rng.integers(0, cfg["V"], seq).astype(np.int32)
+    m = np.zeros_like(params); v = np.zeros_like(params)
+    t0 = time.perf_counter()
+    _, g, _ = oracle.model_loss_grad(cfg, params, tok, tgt, 1, seq)
+    oracle.adamw(params, g, m, v, 3e-4, 0.9, 0.999, 1e-8, 0.0, 1)
+    dt = time.perf_counter() - t0
+    return seq / dt, dt, oracle.num_threads()
+
+
+def run_reference(args):
+    """--impl reference: the CPU restatement of the step on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    wl = WORKLOADS[args.workload]
+    seq = 128
+    vals = []
+    for i in range(args.warmup + args.steps):
+        tps, dt, cores = cpu_sample(args.workload, seq)
+        if i >= args.warmup:
+            vals.append(tps)
+    v = statistics.median(vals)
+    out = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * seq / v, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "config": {"workload": wl["name"] + f"; CPU sample: micro-batch 1 x {seq} tokens per step"},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"one fwd+bwd+AdamW step over 1 x {seq} tokens of the same model (oracle)"},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------- microbench ----
+
+def microbench(ops, torch, hbm_peak, reps=20):
+    """HBM-bound backward kernels at their configured shapes (GB/s of algorithmic bytes)."""
+    res = {}
+    dev = "cuda"
+
+    def timeit(fn, n=reps):
+        for _ in range(3):
+            fn(0)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        s.record()
+        for i in range(n):
+            fn(i)
+        e.record()
+        torch.cuda.synchronize()
+        return s.elapsed_time(e) / n
+
+    g = torch.Generator(device=dev).manual_seed(0)
+    # (a) LN backward [16384, 1024]: 4 input sets rotate so the 64 MB per set is not L2-resident
+    N, D = 16384, 1024
+    sets = []
+    for k in range(4):
+        x = torch.randn(N, D, device=dev, generator=g).half()
+        dy = torch.randn(N, D, device=dev, generator=g).half()
+        sets.append((x, dy))
+    gam = (1 + 0.02 * torch.randn(D, device=dev, generator=g)).half()
+    mean = torch.empty(N, device=dev); rstd = torch.empty(N, device=dev)
+    _, mean, rstd = ops.ln_fwd(sets[0][0], gam, torch.zeros(D, device=dev).half())
+    dx = torch.empty(N, D, device=dev, dtype=torch.float16)
+    dg = torch.zeros(D, device=dev); db = torch.zeros(D, device=dev)
+    C = ops.ctx()
+    import ctypes
+    from rbk._lib import call
+
+    def ln(i):
+        x, dy = sets[i % 4]
+        call("rbk_ln_bwd", C.handle, ctypes.c_void_p(dx.data_ptr()), ctypes.c_void_p(dg.data_ptr()),
+             ctypes.c_void_p(db.data_ptr()), None, ctypes.c_void_p(dy.data_ptr()), None,
+             ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(gam.data_ptr()), ctypes.c_void_p(mean.data_ptr()),
+             ctypes.c_void_p(rstd.data_ptr()), N, D, 0, ops._s())
+    ms = timeit(ln)
+    by = N * D * 6 + N * 8 + D * 10
+    res["ln_bwd_16384x1024"] = {"ms": ms, "GB/s": by / ms / 1e6, "frac_of_hbm": by / ms / 1e6 / hbm_peak,
+                                "algorithmic_bytes": by}
+    del sets
+    # (b) softmax-CE backward [8192, 32000] FP16 logits ~N(0,2), uniform targets (524 MB in, 524 MB out)
+    N, V = 8192, 32000
+    z = (2.0 * torch.randn(N, V, device=dev, generator=g)).half()
+    t = torch.randint(0, V, (N,), device=dev, generator=g, dtype=torch.int32)
+    d = torch.empty_like(z)
+
+    def ce(i):
+        call("rbk_softmax_xent_bwd", C.handle, ctypes.c_void_p(d.data_ptr()), ctypes.c_void_p(z.data_ptr()), V,
+             ctypes.c_void_p(t.data_ptr()), N, V, ctypes.c_float(65536.0 / N), None, None, ops._s())
+    ms = timeit(ce)
+    by = N * V * 4 + N * 4
+    res["softmax_xent_bwd_8192x32000"] = {"ms": ms, "GB/s": by / ms / 1e6, "frac_of_hbm": by / ms / 1e6 / hbm_peak,
+                                          "algorithmic_bytes": by}
+    del z, d
+    # (c) causal attention-softmax backward B8 H16 T1024 (P, dP in, dS out over the lower triangle)
+    nm, T = 8 * 16, 1024
+    P = torch.rand(nm, T, T, device=dev, generator=g).half()
+    dP = torch.randn(nm, T, T, device=dev, generator=g).half()
+    dS = torch.empty_like(P)
+
+    def sm(i):
+        call("rbk_attn_softmax_bwd", C.handle, ctypes.c_void_p(dS.data_ptr()), ctypes.c_void_p(P.data_ptr()),
+             ctypes.c_void_p(dP.data_ptr()), nm, T, 1, ops._s())
+    ms = timeit(sm)
+    by = nm * T * (T + 1) // 2 * 6
+    res["attn_softmax_bwd_B8H16T1024"] = {"ms": ms, "GB/s": by / ms / 1e6, "frac_of_hbm": by / ms / 1e6 / hbm_peak,
+                                          "algorithmic_bytes": by}
+    del P, dP, dS
+    torch.cuda.empty_cache()
+    return res
+
+
+# ------------------------------------------------------------------ GPU leg ----
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=40)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="rbk", choices=["rbk", "reference"])
+    ap.add_argument("--workload", default="gpt2-small", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-ckpt", action="store_true", help="disable activation checkpointing")
+    ap.add_argument("--no-micro", action="store_true", help="skip the HBM-bound kernel microbench")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--bucket-mb", type=float, default=25.0)
+    args = ap.parse_args()
+    assert args.warmup >= 3 or args.impl == "reference" or os.environ.get("RBK_BENCH_ALLOW_FEW_WARMUP"), \
+        "at least 3 warm-up steps"
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    from rbk import lib, ops
+    from rbk.model import ModelConfig, RubidiumTransformer, dp_unique_id
+
+    hbm_peak, tc_burst, tc_sustained, peak_kind = peaks()
+    wl = WORKLOADS[args.workload]
+    cfg = wl["cfg"]
+    B, S = wl["batch"], wl["seq"]
+    ntok = B * S
+    ckpt = not args.no_ckpt
+    model = RubidiumTransformer(ModelConfig(**cfg, use_activation_checkpointing=ckpt), max_batch=B, max_seq=S)
+    model.init_weights(seed=42, std=0.02)
+    if world > 1:
+        uid = [dp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        model.dp_init(rank, world, uid[0], int(args.bucket_mb * (1 << 20)))
+
+    g = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    tokens = torch.randint(0, cfg["V"], (B, S), device="cuda", dtype=torch.int32, generator=g)
+    targets = torch.randint(0, cfg["V"], (B, S), device="cuda", dtype=torch.int32, generator=g)
+    stream = torch.cuda.current_stream()
+
+    def step(t):
+        model.forward(tokens, targets, B, S)
+        model.backward(tokens, targets, B, S, 1.0)
+        model.optimizer_step(t, 3e-4, 0.9, 0.999, 1e-8, 0.0)
+
+    for i in range(args.warmup):
+        step(0)
+    torch.cuda.synchronize()
+
+    # ---------------- timed region (device events, max over ranks) ----------
+    import ctypes
+    mctx = ctypes.c_void_p()
+    lib().rbk_model_ctx(model.handle, ctypes.byref(mctx))
+    lib().rbk_ctx_profile(mctx, 1)
+    clocks = Clocks(local)
+    clocks.start()
+    time.sleep(0.5)   # let the sampler come up before the timed region
+    bw_s = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    bw_e = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    launches0 = lib().rbk_launch_count()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(args.steps):
+        model.forward(tokens, targets, B, S)
+        bw_s[i].record(stream)
+        model.backward(tokens, targets, B, S, 1.0)
+        bw_e[i].record(stream)
+        model.optimizer_step(0, 3e-4, 0.9, 0.999, 1e-8, 0.0)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    launches = lib().rbk_launch_count() - launches0
+    clk = clocks.stop()
+    ms = t_start.elapsed_time(t_end)
+    bwd_ms = statistics.median(bw_s[i].elapsed_time(bw_e[i]) for i in range(args.steps))
+    cat_ms = (ctypes.c_double * 9)(); cat_w = (ctypes.c_double * 9)(); cat_n = (ctypes.c_int * 9)()
+    lib().rbk_ctx_profile_read(mctx, cat_ms, cat_w, cat_n, 9)
+    lib().rbk_ctx_profile(mctx, 0)
+    if world > 1:
+        t = torch.tensor([ms, bwd_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, bwd_ms = float(t[0]), float(t[1])
+    ms_step = ms / args.steps
+    value = world * ntok / (ms_step / 1000.0)
+
+    # ---------------- end-to-end through the public API with host buffers ----
+    h_tok = torch.empty((B, S), dtype=torch.int32, pin_memory=True)
+    h_tgt = torch.empty((B, S), dtype=torch.int32, pin_memory=True)
+    h_tok.copy_(tokens.cpu()); h_tgt.copy_(targets.cpu())
+    d_tok = torch.empty_like(tokens); d_tgt = torch.empty_like(targets)
+    h_loss = torch.empty(1, dtype=torch.float32, pin_memory=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    w0 = time.perf_counter()
+    for i in range(args.steps):
+        d_tok.copy_(h_tok, non_blocking=True)
+        d_tgt.copy_(h_tgt, non_blocking=True)
+        loss = model.forward(d_tok, d_tgt, B, S)
+        model.backward(d_tok, d_tgt, B, S, 1.0)
+        model.optimizer_step(0, 3e-4, 0.9, 0.999, 1e-8, 0.0)
+        h_loss.copy_(loss.view(1), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        _ = float(h_loss[0])
+    e2e_s = time.perf_counter() - w0
+    if world > 1:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t[0])
+    e2e = world * ntok * args.steps / e2e_s
+
+    # ---------------- roofline of the dominant kernel (the tcgen05 GEMM) ----
+    per_cat = {CAT_NAMES[c]: {"ms_per_step": cat_ms[c] / args.steps, "launches_per_step": cat_n[c] / args.steps,
+                              "share": cat_ms[c] / max(sum(cat_ms), 1e-9)} for c in range(9) if cat_n[c]}
+    gemm_tflops = cat_w[0] / (cat_ms[0] * 1e-3) / 1e12 if cat_ms[0] > 0 else 0.0
+    roofline = {"bound": "tensor", "kernel": "gemm_kernel (tcgen05, all GEMMs of the step)",
+                "achieved": gemm_tflops, "peak": tc_sustained, "unit": "TFLOP/s",
+                "frac": gemm_tflops / tc_sustained, "traffic": None,
+                "peak_source": f"{peak_kind} bf16_tflops_sustained (FP16 and BF16 share the dense tensor rate)",
+                "gemm_flops_per_launch": cat_w[0] / max(cat_n[0], 1),
+                "gemm_ms_per_launch": cat_ms[0] / max(cat_n[0], 1)}
+
+    extra = {}
+    if rank == 0 and not args.no_micro:
+        try:
+            extra["microbench"] = microbench(ops, torch, hbm_peak)
+        except Exception as exc:   # report, never hide
+            extra["microbench"] = {"error": repr(exc)}
+    cpu = None
+    if rank == 0 and not args.no_cpu:
+        tps, dt, cores = cpu_sample(args.workload, 128)
+        cpu = {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"oracle fwd+bwd+AdamW of the same model over 1 x 128 tokens ({dt:.1f} s)"}
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp16", "data": "synthetic (uniform random tokens, N(0,0.02) weights)",
+            "config": {"workload": wl["name"], "global_batch": B * world, "seq_len": S,
+                       "parallelism": f"dp{world}", "activation_checkpointing": ckpt,
+                       "loss_scale_init": 65536, "l2": "no flush: weights/activations/logits exceed 126 MB L2"},
+            "tokens_per_s_per_gpu": value / world,
+            "backward_ms_per_step": bwd_ms,
+            "train_tflops_per_gpu": train_flops_per_token(cfg, S) * ntok / (ms_step / 1000.0) / 1e12,
+            "gemm_flops_per_step": gemm_flops_per_step(cfg, ntok, ckpt),
+            "roofline": roofline,
+            "kernels": per_cat,
+            "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 2 * ntok * 4, "d2h_bytes_per_step": 4},
+            "gpu_launches": int(launches),
+            "clocks": clk,
+            "cpu_baseline": cpu,
+            "loss_scale": model.loss_scale,
+        }
+        out.update(extra)
+        print(json.dumps(out), flush=True)
+    model.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -52,6 +52,25 @@ int rbk_version(void);
 int rbk_ctx_create(rbk_ctx** out, int device);
 int rbk_ctx_destroy(rbk_ctx* ctx);
 
+/* Instrumentation (no counterpart in the reference, which times steps with
+ * clock(), src/main.cpp:123,178):
+ *   rbk_launch_count   kernels launched by librbk since load (all contexts);
+ *   rbk_ctx_profile    enable (1) / disable (0) per-entry-point CUDA-event
+ *                      timing on ctx and clear its records;
+ *   rbk_ctx_profile_read  synchronise and sum per category (>= RBK_PROF_NCAT
+ *                      slots): milliseconds, algorithmic work (GEMM and
+ *                      attention FLOPs, bytes for the others) and launches.
+ *                      Categories: 0 GEMM, 1 attention fwd, 2 attention bwd,
+ *                      3 LN fwd, 4 LN bwd, 5 softmax-CE, 6 Adam tail,
+ *                      7 embeddings, 8 other;
+ *   rbk_ctx_device_error  read and clear the status word that bounded
+ *                      device-side waits set (0 or RBK_ERR_TIMEOUT). */
+#define RBK_PROF_NCAT 9
+long long rbk_launch_count(void);
+int rbk_ctx_profile(rbk_ctx* ctx, int enable);
+int rbk_ctx_profile_read(rbk_ctx* ctx, double* ms, double* work, int* launches, int ncat);
+int rbk_ctx_device_error(rbk_ctx* ctx, int* status);
+
 /* ------------------------------------------------------------------------
  * LayerNorm
  * ------------------------------------------------------------------------ */
@@ -83,7 +102,7 @@ int rbk_ln_bwd(rbk_ctx* ctx, void* dx, float* dgamma, float* dbeta, float* dbias
 /* One pass over half logits [N, V] (row stride ld >= V, ld % 8 == 0,
  * V <= 65536):
  *   dlogits[i, j] = (softmax(z_i)_j - [j == t_i]) * scale * (*dscale if dscale)
- * dlogits may alias logits (in place).  Optional output:
+ * dlogits may alias logits (in place), or be NULL for a loss-only pass.  Output:
  *   row_loss [N] FP32 = -log(softmax(z_i)_{t_i} + 1e-10)  (src/cpu_mat.h:213)
  * A target outside [0, V) yields a NaN row loss and a zero gradient row.
  * The lm_b gradient (column sums of dlogits) comes from the LM-head wgrad
@@ -260,11 +279,16 @@ typedef struct rbk_model_opts {
     int device;
 } rbk_model_opts;
 
-/* Buffer families of the parameter arena (include/rbk_layout.h). */
-enum { RBK_BUF_P16 = 0, RBK_BUF_P32 = 1, RBK_BUF_GRAD = 2, RBK_BUF_M = 3, RBK_BUF_V = 4 };
+/* Buffer families of the parameter arena (include/rbk_layout.h), plus the
+ * model's device loss scalar (FP32, n = 1) and its logits / dlogits buffer
+ * (half [max_batch * max_seq, round_up(V, 8)]). */
+enum { RBK_BUF_P16 = 0, RBK_BUF_P32 = 1, RBK_BUF_GRAD = 2, RBK_BUF_M = 3, RBK_BUF_V = 4,
+       RBK_BUF_LOSS = 5, RBK_BUF_LOGITS = 6 };
 
 int rbk_model_create(rbk_model** out, const rbk_config* cfg, const rbk_model_opts* opts);
 int rbk_model_destroy(rbk_model* m);
+/* The model's own context (for rbk_ctx_profile / rbk_ctx_device_error). */
+int rbk_model_ctx(rbk_model* m, rbk_ctx** ctx);
 /* Device pointer and element count of one arena family. */
 int rbk_model_buffer(rbk_model* m, int which, void** ptr, int64_t* n);
 /* Device pointer to the loss scaler state (rbk_scaler). */

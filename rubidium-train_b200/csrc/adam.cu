@@ -291,7 +291,10 @@ extern "C" int rbk_adam_tail(rbk_ctx* ctx, const rbk_tail_args* a, void* stream)
     int grid = ctx->num_sms * (occ > 0 ? occ : 1);
     if (grid > P.nchunks) grid = P.nchunks;
     void* args[] = {&P};
+    // algorithmic bytes: read g, p, m, v; write p, m, v, g (zero), p16
+    ProfScope prof(ctx, as_stream(stream), kCatTail, (double)a->n * (a->p16 ? 34.0 : 32.0));
     RBK_CUDA(cudaLaunchCooperativeKernel((const void*)adam_tail_kernel, dim3(grid), dim3(512), args, 0,
                                          as_stream(stream)));
+    count_launch();
     return RBK_OK;
 }

@@ -7,6 +7,7 @@
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
+#include <vector>
 
 #include "rbk.h"
 
@@ -18,6 +19,7 @@ namespace rbk {
 
 void set_error(const char* fmt, ...);
 int cuda_fail(cudaError_t e, const char* what, const char* file, int line);
+void count_launch();   // every kernel launched by librbk is counted (rbk_launch_count)
 
 }  // namespace rbk
 
@@ -31,6 +33,7 @@ int cuda_fail(cudaError_t e, const char* what, const char* file, int line);
     do {                                                                            \
         cudaError_t e_ = cudaGetLastError();                                        \
         if (e_ != cudaSuccess) return ::rbk::cuda_fail(e_, what, __FILE__, __LINE__); \
+        ::rbk::count_launch();                                                      \
     } while (0)
 
 #define RBK_REQUIRE(cond, ...)                \
@@ -50,6 +53,14 @@ int cuda_fail(cudaError_t e, const char* what, const char* file, int line);
 // ----------------------------------------------------------------------------
 // Context: device + scratch arena + a small zeroed area for tickets/flags.
 // ----------------------------------------------------------------------------
+// Optional per-category kernel timing (CUDA events around each entry point).
+struct rbk_prof {
+    bool on = false;
+    std::vector<cudaEvent_t> pool;     // start/stop pairs
+    struct Rec { int cat; double work; };
+    std::vector<Rec> recs;             // recs[i] uses pool[2i], pool[2i+1]
+};
+
 struct rbk_ctx {
     int device = 0;
     int num_sms = 148;
@@ -59,9 +70,23 @@ struct rbk_ctx {
     int* tickets = nullptr;
     static constexpr int kTickets = 64;
     int* err = nullptr;      // device error word written by bounded waits
+    rbk_prof prof;
 };
 
 namespace rbk {
+
+// Timing categories (rbk_ctx_profile_read).
+enum ProfCat { kCatGemm = 0, kCatAttnFwd, kCatAttnBwd, kCatLnFwd, kCatLnBwd, kCatXent, kCatTail, kCatEmbed,
+               kCatOther, kNumCats };
+
+// Records start/stop events around one entry point when profiling is on.
+struct ProfScope {
+    rbk_ctx* ctx;
+    cudaStream_t st;
+    int idx = -1;
+    ProfScope(rbk_ctx* c, cudaStream_t s, int cat, double work);
+    ~ProfScope();
+};
 
 // Scratch of at least `bytes` (256-byte aligned); grows (cudaFree + cudaMalloc)
 // only when the current arena is too small.

@@ -1,5 +1,6 @@
 // ctx.cu — context, scratch arena, error strings and the small reductions
 // shared by several entry points.
+#include <atomic>
 #include <cstring>
 #include <string>
 
@@ -8,6 +9,32 @@
 namespace rbk {
 
 static thread_local char g_err[512] = "";
+static std::atomic<long long> g_launches{0};
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+constexpr int kProfPairs = 8192;
+
+ProfScope::ProfScope(rbk_ctx* c, cudaStream_t s, int cat, double work) : ctx(c), st(s) {
+    if (!c || !c->prof.on) return;
+    rbk_prof& p = c->prof;
+    const int i = (int)p.recs.size();
+    if (i >= kProfPairs) return;
+    if ((int)p.pool.size() < 2 * (i + 1)) {
+        for (int k = 0; k < 2; ++k) {
+            cudaEvent_t e;
+            if (cudaEventCreate(&e) != cudaSuccess) return;
+            p.pool.push_back(e);
+        }
+    }
+    p.recs.push_back({cat, work});
+    cudaEventRecord(p.pool[2 * i], s);
+    idx = i;
+}
+
+ProfScope::~ProfScope() {
+    if (idx >= 0) cudaEventRecord(ctx->prof.pool[2 * idx + 1], st);
+}
 
 void set_error(const char* fmt, ...) {
     va_list ap;
@@ -121,7 +148,51 @@ int rbk_ctx_destroy(rbk_ctx* ctx) {
     cudaSetDevice(ctx->device);
     if (ctx->scratch) cudaFree(ctx->scratch);
     if (ctx->tickets) cudaFree(ctx->tickets);
+    for (cudaEvent_t e : ctx->prof.pool) cudaEventDestroy(e);
     delete ctx;
+    return RBK_OK;
+}
+
+long long rbk_launch_count(void) { return g_launches.load(); }
+
+int rbk_ctx_profile(rbk_ctx* ctx, int enable) {
+    RBK_REQUIRE(ctx, "rbk_ctx_profile: null ctx");
+    ctx->prof.on = enable != 0;
+    ctx->prof.recs.clear();
+    // create the event pool up front so no event is created inside a timed region
+    while (enable && ctx->prof.pool.size() < 2 * (size_t)kProfPairs) {
+        cudaEvent_t e;
+        RBK_CUDA(cudaEventCreate(&e));
+        ctx->prof.pool.push_back(e);
+    }
+    return RBK_OK;
+}
+
+int rbk_ctx_profile_read(rbk_ctx* ctx, double* ms, double* work, int* launches, int ncat) {
+    RBK_REQUIRE(ctx && ms && work && launches && ncat >= kNumCats, "rbk_ctx_profile_read: bad arguments");
+    for (int c = 0; c < ncat; ++c) { ms[c] = 0.0; work[c] = 0.0; launches[c] = 0; }
+    rbk_prof& p = ctx->prof;
+    for (size_t i = 0; i < p.recs.size(); ++i) {
+        RBK_CUDA(cudaEventSynchronize(p.pool[2 * i + 1]));
+        float t = 0.0f;
+        RBK_CUDA(cudaEventElapsedTime(&t, p.pool[2 * i], p.pool[2 * i + 1]));
+        const int c = p.recs[i].cat;
+        ms[c] += t;
+        work[c] += p.recs[i].work;
+        launches[c] += 1;
+    }
+    return RBK_OK;
+}
+
+int rbk_ctx_device_error(rbk_ctx* ctx, int* status) {
+    RBK_REQUIRE(ctx && status, "rbk_ctx_device_error: bad arguments");
+    int v[rbk_ctx::kTickets] = {};
+    RBK_CUDA(cudaMemcpy(v, ctx->tickets, sizeof(v), cudaMemcpyDeviceToHost));
+    *status = v[kGemmError];
+    if (v[kGemmError]) {
+        const int zero = 0;
+        RBK_CUDA(cudaMemcpy(ctx->tickets + kGemmError, &zero, sizeof(int), cudaMemcpyHostToDevice));
+    }
     return RBK_OK;
 }
 

@@ -103,6 +103,7 @@ int rbk_embed_bwd(rbk_ctx* ctx, float* dtok, float* dpos, const void* dx, const 
                 "rbk_embed_bwd: 16-byte alignment");
     const int N = B * S;
     cudaStream_t st = as_stream(stream);
+    ProfScope prof(ctx, st, kCatEmbed, (double)N * D * (2.0 + 8.0));
     if (dtok) {
         embed_tok_bwd_kernel<<<grid_for((long)N * (D / 8), ctx->num_sms), 256, 0, st>>>(dtok, (const half*)dx,
                                                                                        tokens, N, D, V);

@@ -563,6 +563,7 @@ int rbk_gemm(rbk_ctx* ctx, const rbk_gemm_desc* d, void* stream) {
     p.alpha = d->alpha;
     p.err = ctx->tickets + kGemmError;
     cudaStream_t st = as_stream(stream);
+    ProfScope prof(ctx, st, kCatGemm, 2.0 * d->M * (double)d->N * d->K);
     if (BN == 256) {
         switch (epi) {
             case RBK_EPI_STORE_F16: return launch<256, RBK_EPI_STORE_F16>(ctx, d, p, st);

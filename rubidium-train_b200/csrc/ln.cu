@@ -205,6 +205,7 @@ int rbk_ln_fwd(rbk_ctx* ctx, void* y, float* mean, float* rstd, const void* x, c
     int blocks = (N + rows_per_block - 1) / rows_per_block;
     blocks = blocks < ctx->num_sms * 16 ? blocks : ctx->num_sms * 16;
     cudaStream_t st = as_stream(stream);
+    ProfScope prof(ctx, st, kCatLnFwd, 4.0 * N * D + 8.0 * N + 4.0 * D);
     auto Y = (half*)y;
     auto X = (const half*)x;
     auto G = (const half*)gamma;
@@ -242,6 +243,9 @@ int rbk_ln_bwd(rbk_ctx* ctx, void* dx, float* dgamma, float* dbeta, float* dbias
     RBK_TRY(ctx_scratch(ctx, sizeof(float) * 3 * (size_t)D * blocks, &ws));
     float* part = (float*)ws;
     cudaStream_t st = as_stream(stream);
+    // algorithmic bytes: x, dy, dx (+ dres) half rows, mean/rstd, gamma, FP32 column sums
+    ProfScope prof(ctx, st, kCatLnBwd,
+                   (double)N * D * (6.0 + (dres ? 2.0 : 0.0)) + 8.0 * N + (double)D * (2.0 + 8.0 + (dbias_out ? 4.0 : 0.0)));
     const bool ref = (flags & RBK_LN_REFERENCE_FORMULA) != 0;
     const bool res = dres != nullptr, bias = dbias_out != nullptr;
     auto DX = (half*)dx;

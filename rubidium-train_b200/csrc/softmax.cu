@@ -88,6 +88,8 @@ extern "C" int rbk_attn_softmax_bwd(rbk_ctx* ctx, void* dS, const void* P, const
     const long cap = (long)ctx->num_sms * 8;
     const int grid = (int)(g < cap ? g : cap);
     cudaStream_t st = as_stream(stream);
+    const double elems = causal ? (double)nmat * T * (T + 1) / 2.0 : (double)nmat * T * T;
+    ProfScope prof(ctx, st, kCatOther, 6.0 * elems);
     auto o = (half*)dS;
     auto p = (const half*)P;
     auto d = (const half*)dP;

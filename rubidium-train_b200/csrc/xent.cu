@@ -95,6 +95,7 @@ __global__ void __launch_bounds__(512) xent_kernel(half* dl, const half* lg, int
             if (tvalid) l = -logf(__expf(__half2float(z[t]) - mx) * inv + 1e-10f);
             row_loss[row] = l;
         }
+        if (!dl) continue;   // loss-only mode
         const float g = tvalid ? gs : 0.0f;
         half* d = dl + (size_t)row * ld;
 #pragma unroll
@@ -133,10 +134,11 @@ using namespace rbk;
 
 extern "C" int rbk_softmax_xent_bwd(rbk_ctx* ctx, void* dlogits, const void* logits, int ld, const int* targets,
                                     int N, int V, float scale, const float* dscale, float* row_loss, void* stream) {
-    RBK_REQUIRE(ctx && dlogits && logits && targets, "rbk_softmax_xent_bwd: null pointer");
+    RBK_REQUIRE(ctx && logits && targets && (dlogits || row_loss), "rbk_softmax_xent_bwd: null pointer");
     RBK_REQUIRE(N > 0 && V > 0 && V <= 65536 && ld >= V && ld % 8 == 0,
                 "rbk_softmax_xent_bwd: need 0 < V <= 65536, ld >= V, ld %% 8 == 0 (V=%d ld=%d)", V, ld);
-    RBK_REQUIRE(aligned16(dlogits) && aligned16(logits), "rbk_softmax_xent_bwd: tensors must be 16-byte aligned");
+    RBK_REQUIRE((!dlogits || aligned16(dlogits)) && aligned16(logits),
+                "rbk_softmax_xent_bwd: tensors must be 16-byte aligned");
     int nt = ((V + 63) / 64 + 31) / 32 * 32;
     nt = nt < 128 ? 128 : nt > 512 ? 512 : nt;
     const int e = (V + 8 * nt - 1) / (8 * nt);
@@ -144,6 +146,8 @@ extern "C" int rbk_softmax_xent_bwd(rbk_ctx* ctx, void* dlogits, const void* log
     int grid = ctx->num_sms * per_sm;
     if (grid > N) grid = N;
     cudaStream_t st = as_stream(stream);
+    ProfScope prof(ctx, st, kCatXent,
+                   (double)N * V * (dlogits ? 4.0 : 2.0) + 4.0 * N + (row_loss ? 4.0 * N : 0.0));
     auto DL = (half*)dlogits;
     auto LG = (const half*)logits;
     if (e <= 1) launch<1>(grid, nt, st, DL, LG, ld, targets, N, V, scale, dscale, row_loss);

@@ -62,6 +62,11 @@ _SIGS = {
     "rbk_version": (i32, []),
     "rbk_ctx_create": (i32, [C.POINTER(vp), i32]),
     "rbk_ctx_destroy": (i32, [vp]),
+    "rbk_launch_count": (C.c_longlong, []),
+    "rbk_ctx_profile": (i32, [vp, i32]),
+    "rbk_ctx_profile_read": (i32, [vp, C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(i32), i32]),
+    "rbk_ctx_device_error": (i32, [vp, C.POINTER(i32)]),
+    "rbk_model_ctx": (i32, [vp, C.POINTER(vp)]),
     "rbk_ln_fwd": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, f32, vp]),
     "rbk_ln_bwd": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, vp]),
     "rbk_softmax_xent_bwd": (i32, [vp, vp, vp, i32, vp, i32, i32, f32, vp, vp, vp]),

@@ -1,0 +1,198 @@
+"""Attention and whole-model parity on the B200 against the CPU oracle.
+
+Acceptance (BASELINE): loss within 1e-3 relative; per-tensor gradient relative
+L2 error <= 2e-2 (FP16 path vs FP32 oracle, absolute floor for tensors whose
+exact gradient is ~0, e.g. the key bias); identical overflow / skip decisions.
+"""
+import math
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+GRAD_TOL = 2e-2
+LOSS_TOL = 1e-3
+CFG1 = dict(V=4096, T=128, D=256, H=4, L=4, FF=1024)
+
+
+def rel(a, b, floor=0.0):
+    a = np.asarray(a, np.float64); b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), floor, 1e-30))
+
+
+# ------------------------------------------------------------------ attention --
+
+@pytest.mark.parametrize("B,S,H,dh", [(2, 128, 3, 64), (1, 256, 2, 128), (3, 64, 1, 64)])
+def test_flash_attention_fwd_bwd(ora, B, S, H, dh):
+    from rbk import ops
+    rng = np.random.default_rng(S + dh)
+    D = H * dh
+    qkv = (rng.standard_normal((B * S, 3 * D)) * 0.7).astype(np.float16)
+    dout = rng.standard_normal((B * S, D)).astype(np.float16)
+    t_qkv = torch.from_numpy(qkv).cuda()
+    o, lse = ops.attn_fwd(t_qkv, B, S, H, dh)
+    q32, k32, v32 = (qkv[:, i * D:(i + 1) * D].astype(np.float32) for i in range(3))
+    eo, P = ora.attn_fwd(q32, k32, v32, B, S, H)
+    assert rel(o.float().cpu().numpy(), eo) < 3e-3
+    # reference lse from float64 scores
+    qh = q32.reshape(B, S, H, dh).transpose(0, 2, 1, 3).astype(np.float64)
+    kh = k32.reshape(B, S, H, dh).transpose(0, 2, 1, 3).astype(np.float64)
+    sc = qh @ kh.transpose(0, 1, 3, 2) / math.sqrt(dh)
+    sc = np.where(np.tril(np.ones((S, S), bool)), sc, -np.inf)
+    e_lse = np.log(np.exp(sc - sc.max(-1, keepdims=True)).sum(-1)) + sc.max(-1)
+    assert rel(lse.cpu().numpy(), e_lse) < 1e-4
+    dbias = torch.zeros(3 * D, dtype=torch.float32, device="cuda")
+    dqkv = ops.attn_bwd(t_qkv, o, torch.from_numpy(dout).cuda(), lse, B, S, H, dh, dbias=dbias)
+    edq, edk, edv = ora.attn_bwd(dout.astype(np.float32), P, q32, k32, v32, B, S, H)
+    g = dqkv.float().cpu().numpy()
+    assert rel(g[:, :D], edq) < 5e-3
+    assert rel(g[:, D:2 * D], edk) < 5e-3
+    assert rel(g[:, 2 * D:], edv) < 5e-3
+    # q|k|v bias gradients = column sums (rows of the dk block sum to ~0 exactly)
+    db = dbias.cpu().numpy()
+    assert rel(db[:D], g[:, :D].sum(0)) < 5e-3
+    assert rel(db[2 * D:], g[:, 2 * D:].sum(0)) < 5e-3
+    assert np.abs(db[D:2 * D] - g[:, D:2 * D].sum(0)).max() < 1e-2
+
+
+def test_flash_attention_config_shape(ora):
+    """GPT-2-small attention shape (B16 H12 S1024 dh64): lse and output sanity + a slice vs the oracle."""
+    from rbk import ops
+    B, S, H, dh = 16, 1024, 12, 64
+    D = H * dh
+    g = torch.Generator(device="cuda").manual_seed(0)
+    qkv = (torch.randn(B * S, 3 * D, device="cuda", generator=g) * 0.5).half()
+    o, lse = ops.attn_fwd(qkv, B, S, H, dh)
+    assert torch.isfinite(o.float()).all() and torch.isfinite(lse).all()
+    # batch 0 vs the oracle
+    sl = qkv[:S].float().cpu().numpy()
+    eo, _ = ora.attn_fwd(sl[:, :D], sl[:, D:2 * D], sl[:, 2 * D:], 1, S, H)
+    assert rel(o[:S].float().cpu().numpy(), eo) < 3e-3
+
+
+# ----------------------------------------------------------------- whole model --
+
+def _setup(ora, cfg, B, S, seed, ckpt=True):
+    from rbk.model import ModelConfig, RubidiumTransformer
+    rng = np.random.default_rng(seed)
+    params = ora.init_params(cfg, seed=seed)
+    for name, off, r, c in ora.param_table(cfg):
+        base = name.split(".")[-1]
+        if base in ("ln1_w", "ln2_w", "ln_f_w"):
+            params[off:off + r * c] += (0.05 * rng.standard_normal(r * c)).astype(np.float32)
+        elif base in ("ln1_b", "ln2_b", "ln_f_b", "bq", "bk", "bv", "bo", "b1", "b2", "lm_b"):
+            params[off:off + r * c] = (0.02 * rng.standard_normal(r * c)).astype(np.float32)
+    tok = rng.integers(0, cfg["V"], B * S).astype(np.int32)
+    tgt = rng.integers(0, cfg["V"], B * S).astype(np.int32)
+    mc = ModelConfig(**cfg, use_activation_checkpointing=ckpt)
+    m = RubidiumTransformer(mc, max_batch=B, max_seq=S)
+    m.load_params(torch.from_numpy(params))
+    return m, params, tok, tgt
+
+
+def _grad_errors(ora, cfg, m, params, tok, tgt, B, S):
+    tt = torch.from_numpy(tok).cuda().view(B, S)
+    tg = torch.from_numpy(tgt).cuda().view(B, S)
+    loss = m.forward(tt, tg, B, S).item()
+    scale = m.loss_scale
+    m.backward(tt, tg, B, S, loss_scale=1.0)
+    g = m.grad.cpu().numpy() / scale
+    el, eg, _ = ora.model_loss_grad(cfg, params, tok, tgt, B, S, grad_scale=1.0)
+    # absolute floor: 1% of the median per-tensor gradient norm.  It only matters for the key
+    # bias, whose exact gradient is identically 0 (adding a constant to every key of a head shifts
+    # all scores of a query row equally), so both sides are rounding noise there.
+    norms = [np.linalg.norm(eg[off:off + r * c]) for _, off, r, c in ora.param_table(cfg)]
+    floor = 1e-2 * float(np.median(norms))
+    errs = {name: rel(g[off:off + r * c], eg[off:off + r * c], floor)
+            for name, off, r, c in ora.param_table(cfg)}
+    return loss, el, errs
+
+
+@pytest.mark.parametrize("ckpt", [True, False])
+def test_config1_loss_and_grads_match_oracle(ora, ckpt):
+    """Config 1 (L4 D256 H4 FF1024 V4096, B8 S128): one fwd+bwd vs the FP32 oracle."""
+    B, S = 8, 128
+    m, params, tok, tgt = _setup(ora, CFG1, B, S, seed=1, ckpt=ckpt)
+    loss, el, errs = _grad_errors(ora, CFG1, m, params, tok, tgt, B, S)
+    assert abs(loss - el) <= LOSS_TOL * abs(el), (loss, el)
+    bad = {k: v for k, v in errs.items() if v > GRAD_TOL}
+    assert not bad, bad
+    m.close()
+
+
+def test_config1_full_step_matches_oracle(ora):
+    """fwd + bwd + fused Adam tail (lr 3e-4): post-step masters vs the oracle's."""
+    B, S = 8, 128
+    m, params, tok, tgt = _setup(ora, CFG1, B, S, seed=2)
+    tt = torch.from_numpy(tok).cuda().view(B, S); tg = torch.from_numpy(tgt).cuda().view(B, S)
+    m.forward(tt, tg, B, S)
+    m.backward(tt, tg, B, S)
+    m.optimizer_step(1, 3e-4, 0.9, 0.999, 1e-8, 0.0)
+    st = m.scaler()
+    assert st.skipped == 0 and st.applied_steps == 1
+    _, eg, _ = ora.model_loss_grad(CFG1, params, tok, tgt, B, S)
+    ep, em, ev = ora.adamw(params, eg, np.zeros_like(params), np.zeros_like(params), 3e-4, 0.9, 0.999, 1e-8, 0.0, 1)
+    p_gpu = m.p32.cpu().numpy()
+    # the first Adam step moves each weight by ~lr * sign(g): compare the updates where the
+    # oracle gradient is well above FP16 noise, and the moments everywhere
+    big = np.abs(eg) > 1e-3 * np.abs(eg).max()
+    upd_gpu, upd_ora = p_gpu - params, ep - params
+    assert np.mean(np.sign(upd_gpu[big]) == np.sign(upd_ora[big])) > 0.99
+    assert rel(upd_gpu, upd_ora) < 0.1
+    assert rel(m._bufs[3].cpu().numpy(), em) < GRAD_TOL
+    assert torch.count_nonzero(m.grad).item() == 0
+    assert rel(m.p16.float().cpu().numpy(), p_gpu) < 1e-3
+    m.close()
+
+
+def test_overflow_injection_skips_step(ora):
+    """Inf planted in dlogits: the tail skips, halves the scale, keeps masters, zeroes grads."""
+    B, S = 2, 128
+    m, params, tok, tgt = _setup(ora, CFG1, B, S, seed=3)
+    tt = torch.from_numpy(tok).cuda().view(B, S); tg = torch.from_numpy(tgt).cuda().view(B, S)
+    p0 = m.p32.clone()
+    m.forward(tt, tg, B, S)
+    m.inject_inf(offset=123, stride=100000)
+    m.backward(tt, tg, B, S)
+    m.optimizer_step(1, 3e-4, 0.9, 0.999, 1e-8, 0.0)
+    st = m.scaler()
+    assert st.skipped == 1 and st.scale == 32768.0 and st.overflow_steps == 1 and st.applied_steps == 0
+    assert torch.equal(m.p32, p0)
+    assert torch.count_nonzero(m.grad).item() == 0
+    # next clean step applies with t = 1 and the halved scale
+    m.forward(tt, tg, B, S)
+    m.backward(tt, tg, B, S)
+    m.optimizer_step(0, 3e-4, 0.9, 0.999, 1e-8, 0.0)
+    st = m.scaler()
+    assert st.skipped == 0 and st.applied_steps == 1 and st.scale == 32768.0
+    m.close()
+
+
+def test_lora_grads_match_oracle(ora):
+    """Rank-16 Q/V adapters on a frozen base: dA, dB vs the oracle (B nonzero so dA != 0)."""
+    B, S, r, alpha = 2, 128, 16, 32.0
+    m, params, tok, tgt = _setup(ora, CFG1, B, S, seed=4)
+    m.init_lora(rank=r, alpha=alpha)
+    Aq, Bq, Av, Bv = m.lora_tensors("p32")
+    g = torch.Generator(device="cuda").manual_seed(5)
+    Bq.copy_(0.02 * torch.randn(Bq.shape, device="cuda", generator=g))
+    Bv.copy_(0.02 * torch.randn(Bv.shape, device="cuda", generator=g))
+    m.lora_sync_fp16()
+    tt = torch.from_numpy(tok).cuda().view(B, S); tg = torch.from_numpy(tgt).cuda().view(B, S)
+    loss = m.forward(tt, tg, B, S).item()
+    m.backward(tt, tg, B, S)
+    scale = m.loss_scale
+    dAq, dBq, dAv, dBv = (t.cpu().numpy() / scale for t in m.lora_tensors("grad"))
+    el, eAq, eBq, eAv, eBv = ora.model_lora_grad(CFG1, params, Aq.cpu().numpy(), Bq.cpu().numpy(), Av.cpu().numpy(),
+                                                 Bv.cpu().numpy(), r, alpha, tok, tgt, B, S)
+    assert abs(loss - el) <= LOSS_TOL * abs(el)
+    for got, exp in ((dAq, eAq), (dBq, eBq), (dAv, eAv), (dBv, eBv)):
+        assert rel(got, exp) < GRAD_TOL
+    # base gradients are not produced under LoRA
+    assert torch.count_nonzero(m.grad).item() == 0
+    m.lora_optimizer_step(1, 1e-3)
+    assert m.scaler().applied_steps == 1
+    m.close()
