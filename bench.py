@@ -242,6 +242,92 @@ def microbench(ops, torch, hbm_peak, reps=20):
     return res
 
 
+def kernel_loop(name, reps, torch, ops):
+    """One kernel at a representative GPT-2-small shape, `reps` launches (for ncu
+    captures and tuning).  Prints per-launch time and the achieved rate."""
+    g = torch.Generator(device="cuda").manual_seed(0)
+    hbm, tc, tcs, _ = peaks()
+    N, D, F, V = 16384, 768, 3072, 50257
+    if name.startswith("gemm"):
+        shapes = {  # (M, N, K, a_major, b_major, epilogue)
+            "gemm_fwd_w1": (N, F, D, 0, 0, ops.EPI_BIAS_GELU),
+            "gemm_fwd_qkv": (N, 3 * D, D, 0, 0, ops.EPI_STORE_F16),
+            "gemm_dgrad_w2": (N, F, D, 0, 1, ops.EPI_GELU_BWD),
+            "gemm_dgrad_w1": (N, D, F, 0, 1, ops.EPI_STORE_F16),
+            "gemm_wgrad_w1": (F, D, N, 1, 1, ops.EPI_ACC_F32),
+            "gemm_lm_fwd": (N, V, D, 0, 0, ops.EPI_STORE_F16),
+        }
+        M, Nn, K, am, bm, epi = shapes[name]
+        A = torch.randn(K if am else M, M if am else K, device="cuda", generator=g).half()
+        B = torch.randn(K if bm else Nn, (Nn + 7) // 8 * 8 if bm else K, device="cuda", generator=g).half()
+        ldc = (Nn + 7) // 8 * 8
+        f32 = epi == ops.EPI_ACC_F32
+        Cm = torch.zeros(M, ldc, device="cuda", dtype=torch.float32 if f32 else torch.float16)
+        bias = torch.randn(ldc, device="cuda", generator=g).half()
+        aux = torch.randn(M, ldc, device="cuda", generator=g).half() if epi in (ops.EPI_GELU_BWD,) else None
+        aux_out = torch.empty(M, ldc, device="cuda", dtype=torch.float16) if epi == ops.EPI_BIAS_GELU else None
+        dbias = torch.zeros(M, device="cuda") if f32 else None
+
+        def fn():
+            ops.gemm(A, B, M, Nn, K, am, bm, C_out=Cm, ldc=ldc, epilogue=epi,
+                     bias=bias if epi in (ops.EPI_BIAS_GELU,) else None, aux=aux, aux_out=aux_out,
+                     dbias_rows=dbias, ldb=B.shape[1])
+        work, unit, peak = 2.0 * M * Nn * K, "TFLOP/s", tc
+    elif name == "ln_bwd":
+        x = torch.randn(16384, 1024, device="cuda", generator=g).half()
+        dy = torch.randn(16384, 1024, device="cuda", generator=g).half()
+        gam = torch.ones(1024, device="cuda").half()
+        _, mean, rstd = ops.ln_fwd(x, gam, torch.zeros(1024, device="cuda").half())
+
+        def fn():
+            ops.ln_bwd(dy, x, gam, mean, rstd)
+        work, unit, peak = 16384 * 1024 * 6 + 16384 * 8 + 1024 * 10, "GB/s", hbm
+    elif name == "xent":
+        z = (2 * torch.randn(8192, 32000, device="cuda", generator=g)).half()
+        t = torch.randint(0, 32000, (8192,), device="cuda", dtype=torch.int32, generator=g)
+
+        def fn():
+            ops.softmax_xent_bwd(z, t, scale=8.0, out=z, want_loss=False)
+        work, unit, peak = 8192 * 32000 * 4 + 8192 * 4, "GB/s", hbm
+    elif name in ("attn_fwd", "attn_bwd"):
+        qkv = (0.5 * torch.randn(N, 3 * D, device="cuda", generator=g)).half()
+        o, lse = ops.attn_fwd(qkv, 16, 1024, 12, 64)
+        do = torch.randn(N, D, device="cuda", generator=g).half()
+        tri = 16 * 12 * 1024 * 1025 / 2 * 64
+
+        def fn():
+            if name == "attn_fwd":
+                ops.attn_fwd(qkv, 16, 1024, 12, 64)
+            else:
+                ops.attn_bwd(qkv, o, do, lse, 16, 1024, 12, 64)
+        work, unit, peak = (4 if name == "attn_fwd" else 8) * tri, "TFLOP/s", tc
+    elif name == "adam_tail":
+        n = 163_000_000 // 64 * 64
+        p, gr, m, v = (torch.zeros(n, device="cuda") for _ in range(4))
+        p16 = torch.empty(n, device="cuda", dtype=torch.float16)
+        sc = ops.new_scaler()
+
+        def fn():
+            ops.adam_tail(p, gr, m, v, p16, sc, lr=1e-4)
+        work, unit, peak = 34.0 * n, "GB/s", hbm
+    else:
+        raise SystemExit(f"unknown kernel {name}")
+    for _ in range(3):
+        fn()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    s.record()
+    for _ in range(reps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / reps
+    rate = work / (ms * 1e-3) / (1e12 if unit == "TFLOP/s" else 1e9)
+    print(json.dumps({"kernel": name, "ms_per_launch": ms, "achieved": rate, "unit": unit, "peak": peak,
+                      "frac": rate / peak}), flush=True)
+    return 0
+
+
 # ------------------------------------------------------------------ GPU leg ----
 
 def main():
@@ -255,7 +341,15 @@ def main():
     ap.add_argument("--no-micro", action="store_true", help="skip the HBM-bound kernel microbench")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--bucket-mb", type=float, default=25.0)
+    ap.add_argument("--kernel", default=None,
+                    help="loop one kernel instead of the training step (gemm_fwd_w1, gemm_fwd_qkv, gemm_dgrad_w2, "
+                         "gemm_dgrad_w1, gemm_wgrad_w1, gemm_lm_fwd, ln_bwd, xent, attn_fwd, attn_bwd, adam_tail)")
     args = ap.parse_args()
+    if args.kernel:
+        import torch
+        from rbk import ops
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        return kernel_loop(args.kernel, args.steps, torch, ops)
     assert args.warmup >= 3 or args.impl == "reference" or os.environ.get("RBK_BENCH_ALLOW_FEW_WARMUP"), \
         "at least 3 warm-up steps"
     if args.impl == "reference":

@@ -5,14 +5,15 @@
 // layer_norm_fp16_fwd_kernel / cpuops::layer_norm (reference
 // src/cuda_kernels.cu:183-225, src/cpu_mat.h:98-123).
 //
-// Backward: each thread owns 8 adjacent columns for every row its CTA visits,
-// so the dgamma / dbeta (/ dbias) column partials live in registers for the
-// whole kernel instead of the reference's per-element half atomics
-// (src/cuda_kernels.cu:279-282).  A CTA takes ROWS rows at a time (8 x 16 B of
-// dy and of x in flight per thread), reduces the two row sums across its warps
-// through shared memory, writes dx, and accumulates the partials.  The CTA
-// partials are reduced in a second, column-parallel launch in fixed order, so
-// the result is bitwise reproducible.
+// Backward: a "team" of D/8 threads covers one row, each thread owning 8
+// adjacent columns, and several teams share a CTA.  A thread keeps its
+// columns' dgamma / dbeta (/ dbias) partial sums in registers for every row
+// its team visits, instead of the reference's per-element half atomics
+// (src/cuda_kernels.cu:279-282).  Teams take kLnRows rows at a time (that
+// many 16-byte loads of dy and of x in flight per thread) and reduce their two
+// row sums through shared memory.  At the end the teams of a CTA fold their
+// partials in shared memory, and one small column-parallel launch sums the
+// per-CTA partials in a fixed order, so results are bitwise reproducible.
 #include "common.cuh"
 
 namespace rbk {
@@ -67,40 +68,51 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(half* __restrict__ y, float
     }
 }
 
-constexpr int kLnRows = 4;   // rows per CTA iteration in the backward
+constexpr int kLnRows = 4;       // rows per team iteration in the backward
+constexpr int kLnMaxTeams = 8;
 
-// part layout: [gridDim.x][3][D]  (dgamma | dbeta | dbias partials)
+// Dynamic shared memory: red[2][teams][2R][warps per team] then part[teams][3][D].
+// part (global) layout: [gridDim.x][3][D]  (dgamma | dbeta | dbias partials)
 template <bool kRefFormula, bool kRes, bool kBias>
 __global__ void __launch_bounds__(512) ln_bwd_kernel(half* __restrict__ dx, float* __restrict__ part,
                                                       const half* __restrict__ dy, const half* __restrict__ dres,
                                                       const half* __restrict__ x, const half* __restrict__ g,
                                                       const float* __restrict__ mean, const float* __restrict__ rstd,
-                                                      int N, int D) {
+                                                      int N, int D, int teams) {
     constexpr int R = kLnRows;
-    __shared__ float red[2][2 * R][32];   // [buffer][row-sum][warp]
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+    extern __shared__ float lsm[];
+    const int tpt = blockDim.x / teams;                 // threads per team
+    const int wpt = tpt >> 5;                           // warps per team
+    const int tid = threadIdx.x, team = tid / tpt, ttid = tid - team * tpt;
+    const int lane = tid & 31, twarp = ttid >> 5;
+    float* red = lsm;                                   // [2][teams][2R][wpt]
+    float* tpart = lsm + 2 * teams * 2 * R * wpt;       // [teams][3][D]
     const int nvec = D >> 3;
-    const bool own = tid < nvec;          // this thread owns columns [8 tid, 8 tid + 8)
+    const bool own = ttid < nvec;                       // columns [8 ttid, 8 ttid + 8)
     const float invD = 1.0f / (float)D;
     float gam[8], pg[8], pb[8], pd[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) { pg[j] = 0.0f; pb[j] = 0.0f; pd[j] = 0.0f; gam[j] = 0.0f; }
-    if (own) h8_to_f(__ldg(reinterpret_cast<const uint4*>(g) + tid), gam);
+    if (own) h8_to_f(__ldg(reinterpret_cast<const uint4*>(g) + ttid), gam);
 
-    int buf = 0;
     const int ngroups = (N + R - 1) / R;
-    for (int grp = blockIdx.x; grp < ngroups; grp += gridDim.x, buf ^= 1) {
+    const int stride = gridDim.x * teams;
+    const int iters = (ngroups + stride - 1) / stride;
+    for (int it = 0; it < iters; ++it) {
+        const int buf = it & 1;
+        const int grp = it * stride + blockIdx.x * teams + team;
         const int row0 = grp * R;
         uint4 dyv[R], xv[R];
         float mr[R], rr[R];
 #pragma unroll
         for (int r = 0; r < R; ++r) {
             const int row = row0 + r;
-            const bool ok = own && row < N;
-            dyv[r] = ok ? __ldg(reinterpret_cast<const uint4*>(dy + (size_t)row * D) + tid) : make_uint4(0, 0, 0, 0);
-            xv[r] = ok ? __ldg(reinterpret_cast<const uint4*>(x + (size_t)row * D) + tid) : make_uint4(0, 0, 0, 0);
-            mr[r] = row < N ? __ldg(mean + row) : 0.0f;
-            rr[r] = row < N ? __ldg(rstd + row) : 0.0f;
+            const bool rowok = grp < ngroups && row < N;
+            const bool ok = own && rowok;
+            dyv[r] = ok ? __ldg(reinterpret_cast<const uint4*>(dy + (size_t)row * D) + ttid) : make_uint4(0, 0, 0, 0);
+            xv[r] = ok ? __ldg(reinterpret_cast<const uint4*>(x + (size_t)row * D) + ttid) : make_uint4(0, 0, 0, 0);
+            mr[r] = rowok ? __ldg(mean + row) : 0.0f;
+            rr[r] = rowok ? __ldg(rstd + row) : 0.0f;
         }
         // Row sums: ts1 = sum dy*g, ts2 = sum dy*g*(x - mean).
         float ts[2 * R];
@@ -119,72 +131,101 @@ __global__ void __launch_bounds__(512) ln_bwd_kernel(half* __restrict__ dx, floa
             ts[2 * r] = warp_sum(s1);
             ts[2 * r + 1] = warp_sum(s2);
         }
+        float* rb = red + ((size_t)buf * teams + team) * 2 * R * wpt;
         if (lane == 0) {
 #pragma unroll
-            for (int k = 0; k < 2 * R; ++k) red[buf][k][warp] = ts[k];
+            for (int k = 0; k < 2 * R; ++k) rb[k * wpt + twarp] = ts[k];
         }
         __syncthreads();
 #pragma unroll
         for (int k = 0; k < 2 * R; ++k) {
             float s = 0.0f;
-            for (int w = 0; w < nwarps; ++w) s += red[buf][k][w];
+            for (int w = 0; w < wpt; ++w) s += rb[k * wpt + w];
             ts[k] = s;
         }
-        // (the other buffer is written next iteration; the barrier above orders
-        //  this iteration's reads of `buf` before the iteration after next)
+        // (the other buffer is written next iteration; this barrier orders the
+        //  reads of `buf` before the iteration after next overwrites it)
 #pragma unroll
         for (int r = 0; r < R; ++r) {
             const int row = row0 + r;
-            if (!own || row >= N) continue;
-            float d[8], xx[8], o[8];
-            h8_to_f(dyv[r], d);
-            h8_to_f(xv[r], xx);
-            float rs[8];
-            if (kRes) h8_to_f(__ldg(reinterpret_cast<const uint4*>(dres + (size_t)row * D) + tid), rs);
-            const float inv = rr[r];
-            const float c2 = kRefFormula ? inv : inv * inv;
-            const float t1 = ts[2 * r], t2 = ts[2 * r + 1];
+            if (own && grp < ngroups && row < N) {
+                float d[8], xx[8], o[8];
+                h8_to_f(dyv[r], d);
+                h8_to_f(xv[r], xx);
+                float rs[8];
+                if (kRes) h8_to_f(__ldg(reinterpret_cast<const uint4*>(dres + (size_t)row * D) + ttid), rs);
+                const float inv = rr[r];
+                const float c2 = kRefFormula ? inv : inv * inv;
+                const float t1 = ts[2 * r], t2 = ts[2 * r + 1];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float xm = xx[j] - mr[r];
-                float v = inv * (d[j] * gam[j] - (t1 + xm * c2 * t2) * invD);
-                if (kRes) v += rs[j];
-                o[j] = v;
-                pg[j] += d[j] * xm * inv;
-                pb[j] += d[j];
-                if (kBias) pd[j] += v;
+                for (int j = 0; j < 8; ++j) {
+                    const float xm = xx[j] - mr[r];
+                    float v = inv * (d[j] * gam[j] - (t1 + xm * c2 * t2) * invD);
+                    if (kRes) v += rs[j];
+                    o[j] = v;
+                    pg[j] += d[j] * xm * inv;
+                    pb[j] += d[j];
+                    if (kBias) pd[j] += v;
+                }
+                reinterpret_cast<uint4*>(dx + (size_t)row * D)[ttid] = f_to_h8(o);
             }
-            reinterpret_cast<uint4*>(dx + (size_t)row * D)[tid] = f_to_h8(o);
         }
     }
+    // fold the teams' partials in shared memory, then one CTA partial to global
     if (own) {
-        float* pr = part + (size_t)blockIdx.x * 3 * D + 8 * tid;
+        float* tp = tpart + (size_t)team * 3 * D + 8 * ttid;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            pr[j] = pg[j];
-            pr[D + j] = pb[j];
-            pr[2 * D + j] = pd[j];
+            tp[j] = pg[j];
+            tp[D + j] = pb[j];
+            tp[2 * D + j] = pd[j];
         }
+    }
+    __syncthreads();
+    for (int i = tid; i < 3 * D; i += blockDim.x) {
+        float s = 0.0f;
+        for (int t = 0; t < teams; ++t) s += tpart[(size_t)t * 3 * D + i];
+        part[(size_t)blockIdx.x * 3 * D + i] = s;
     }
 }
 
-// dgamma[c] += sum_b part[b][0][c]; dbeta[c] += sum_b part[b][1][c]; dbias likewise.
-__global__ void ln_bwd_reduce_kernel(float* __restrict__ dg, float* __restrict__ db, float* __restrict__ dbias,
-                                     const float* __restrict__ part, int nblk, int D) {
-    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+// out_w[c] += sum_b part[b][w][c] for w in {dgamma, dbeta, dbias}: 32 columns per
+// CTA (one per lane), the 8 warps split the partial rows, fixed summation order.
+__global__ void __launch_bounds__(256) ln_bwd_reduce_kernel(float* __restrict__ dg, float* __restrict__ db,
+                                                            float* __restrict__ dbias,
+                                                            const float* __restrict__ part, int nblk, int D) {
+    __shared__ float s[8][33];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int c = blockIdx.x * 32 + lane;
     const int which = blockIdx.y;
-    if (c >= D) return;
     float* out = which == 0 ? dg : which == 1 ? db : dbias;
-    if (!out) return;
-    float s = 0.0f;
-    for (int b = 0; b < nblk; ++b) s += part[(size_t)b * 3 * D + (size_t)which * D + c];
-    out[c] += s;
+    float acc = 0.0f;
+    if (c < D)
+        for (int b = warp; b < nblk; b += 8) acc += part[(size_t)b * 3 * D + (size_t)which * D + c];
+    s[warp][lane] = acc;
+    __syncthreads();
+    if (warp == 0 && c < D && out) {
+        float t = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) t += s[w][lane];
+        out[c] += t;
+    }
 }
 
 template <int NV>
 void launch_fwd(int blocks, cudaStream_t st, half* y, float* mean, float* rstd, const half* x, const half* g,
                 const half* b, int N, int D, float eps) {
     ln_fwd_kernel<NV><<<blocks, 256, 0, st>>>(y, mean, rstd, x, g, b, N, D, eps);
+}
+
+template <bool A, bool B, bool C>
+int launch_bwd(int blocks, int threads, int teams, size_t smem, cudaStream_t st, half* dx, float* part,
+               const half* dy, const half* dres, const half* x, const half* g, const float* mean, const float* rstd,
+               int N, int D) {
+    if (smem > 48 * 1024) RBK_CUDA(cudaFuncSetAttribute(ln_bwd_kernel<A, B, C>,
+                                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    ln_bwd_kernel<A, B, C><<<blocks, threads, smem, st>>>(dx, part, dy, dres, x, g, mean, rstd, N, D, teams);
+    return RBK_OK;
 }
 
 }  // namespace
@@ -232,13 +273,15 @@ int rbk_ln_bwd(rbk_ctx* ctx, void* dx, float* dgamma, float* dbeta, float* dbias
     RBK_REQUIRE(N > 0 && D > 0 && D % 8 == 0 && D <= 4096, "rbk_ln_bwd: need D %% 8 == 0 and D <= 4096 (D=%d)", D);
     RBK_REQUIRE(aligned16(dx) && aligned16(dy) && aligned16(x) && aligned16(gamma) && (!dres || aligned16(dres)),
                 "rbk_ln_bwd: tensors must be 16-byte aligned");
-    const int threads = ((D / 8 + 31) / 32) * 32;
+    const int tpt = ((D / 8 + 31) / 32) * 32;            // threads per team
+    int teams = 512 / tpt;
+    teams = teams < 1 ? 1 : teams > kLnMaxTeams ? kLnMaxTeams : teams;
+    const int threads = teams * tpt;
     const int ngroups = (N + kLnRows - 1) / kLnRows;
-    int per_sm = 2048 / threads;
-    if (per_sm > 4) per_sm = 4;
-    if (per_sm < 1) per_sm = 1;
-    int blocks = ctx->num_sms * per_sm;
-    if (blocks > ngroups) blocks = ngroups;
+    int blocks = ctx->num_sms;                            // 512 threads x ~128 registers: one CTA per SM
+    const int need = (ngroups + teams - 1) / teams;
+    if (blocks > need) blocks = need;
+    const size_t smem = sizeof(float) * ((size_t)2 * teams * 2 * kLnRows * (tpt / 32) + (size_t)teams * 3 * D);
     void* ws;
     RBK_TRY(ctx_scratch(ctx, sizeof(float) * 3 * (size_t)D * blocks, &ws));
     float* part = (float*)ws;
@@ -254,7 +297,7 @@ int rbk_ln_bwd(rbk_ctx* ctx, void* dx, float* dgamma, float* dbeta, float* dbias
     auto X = (const half*)x;
     auto G = (const half*)gamma;
 #define RBK_LN_BWD(R_, S_, B_) \
-    ln_bwd_kernel<R_, S_, B_><<<blocks, threads, 0, st>>>(DX, part, DY, DR, X, G, mean, rstd, N, D)
+    RBK_TRY((launch_bwd<R_, S_, B_>(blocks, threads, teams, smem, st, DX, part, DY, DR, X, G, mean, rstd, N, D)))
     if (ref) {
         if (res) { if (bias) RBK_LN_BWD(true, true, true); else RBK_LN_BWD(true, true, false); }
         else { if (bias) RBK_LN_BWD(true, false, true); else RBK_LN_BWD(true, false, false); }
@@ -264,7 +307,7 @@ int rbk_ln_bwd(rbk_ctx* ctx, void* dx, float* dgamma, float* dbeta, float* dbias
     }
 #undef RBK_LN_BWD
     RBK_LAUNCHED("ln_bwd_kernel");
-    dim3 rg((D + 255) / 256, bias ? 3 : 2);
+    dim3 rg((D + 31) / 32, bias ? 3 : 2);
     ln_bwd_reduce_kernel<<<rg, 256, 0, st>>>(dgamma, dbeta, dbias_out, part, blocks, D);
     RBK_LAUNCHED("ln_bwd_reduce_kernel");
     return RBK_OK;

@@ -1,10 +1,14 @@
 // xent.cu — fused softmax-cross-entropy forward + backward (HBM-bound).
 //
-// One CTA owns a row: the row is read once into registers (16-byte vectors,
-// kept as half2), reduced for its max and sum of exponentials, and the
-// gradient (softmax - onehot) * scale is written from the same registers, in
-// place if the caller wishes.  The reference reads the whole row twice per
-// element (src/cuda_kernels.cu:533-551, O(N V^2)); cpuops does three passes
+// One CTA owns a row at a time.  Pass 1 streams the row once from HBM with
+// 16-byte loads (4 in flight per thread) and keeps an online (max, sum of
+// exp) per thread, merged across the CTA; pass 2 re-reads the same row — a
+// few tens of KB that the CTA touched microseconds earlier, so it comes from
+// L2 — and writes (softmax - onehot) * scale, in place if the caller wishes.
+// DRAM therefore sees one read and one write per logit.  The number of rows in
+// flight (grid x row bytes) is capped well below the 126 MB L2 so pass 2 hits.
+// The reference instead rescans the whole row for every element
+// (src/cuda_kernels.cu:533-551, O(N V^2)); cpuops does three passes
 // (src/cpu_mat.h:220-236).  Per-row loss follows src/cpu_mat.h:213
 // (-log(p_t + 1e-10)).
 #include <cfloat>
@@ -14,117 +18,102 @@
 namespace rbk {
 namespace {
 
-__device__ __forceinline__ float block_reduce_max(float v, float* sh) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    v = warp_max(v);
-    if (lane == 0) sh[warp] = v;
-    __syncthreads();
-    float r = lane < nw ? sh[lane] : -FLT_MAX;
-    r = warp_max(r);
-    __syncthreads();
-    return r;
-}
-__device__ __forceinline__ float block_reduce_sum(float v, float* sh) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    v = warp_sum(v);
-    if (lane == 0) sh[warp] = v;
-    __syncthreads();
-    float r = lane < nw ? sh[lane] : 0.0f;
-    r = warp_sum(r);
-    __syncthreads();
-    return r;
+constexpr int kThreads = 512;
+constexpr int kUnroll = 4;
+
+// Merge two (max, sum) online-softmax states.
+__device__ __forceinline__ void merge(float& m, float& s, float m2, float s2) {
+    const float mn = fmaxf(m, m2);
+    s = (m == -INFINITY ? 0.0f : s * __expf(m - mn)) + (m2 == -INFINITY ? 0.0f : s2 * __expf(m2 - mn));
+    m = mn;
 }
 
-template <int E>
-__global__ void __launch_bounds__(512) xent_kernel(half* dl, const half* lg, int ld, const int* __restrict__ tgt,
-                                                   int N, int V, float scale, const float* __restrict__ dscale,
-                                                   float* __restrict__ row_loss) {
-    __shared__ float sh[32];
+__device__ __forceinline__ void add8(float& m, float& s, const uint4& u) {
+    float f[8];
+    h8_to_f(u, f);
+    float mv = f[0];
+#pragma unroll
+    for (int j = 1; j < 8; ++j) mv = fmaxf(mv, f[j]);
+    if (mv > m) {
+        s = (m == -INFINITY) ? 0.0f : s * __expf(m - mv);
+        m = mv;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s += __expf(f[j] - m);
+}
+
+__global__ void __launch_bounds__(kThreads) xent_kernel(half* dl, const half* lg, int ld, const int* __restrict__ tgt,
+                                                        int N, int V, float scale, const float* __restrict__ dscale,
+                                                        float* __restrict__ row_loss) {
+    __shared__ float sm_m[kThreads / 32], sm_s[kThreads / 32];
+    __shared__ float s_row[2];
     const float gs = scale * (dscale ? __ldg(dscale) : 1.0f);
-    const int nt = blockDim.x, tid = threadIdx.x;
-    const half NEG = __float2half(-65504.0f);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nvec = V >> 3;                       // full 8-element vectors
     for (int row = blockIdx.x; row < N; row += gridDim.x) {
         const half* z = lg + (size_t)row * ld;
-        uint4 raw[E];
-        float mx = -FLT_MAX;
-#pragma unroll
-        for (int k = 0; k < E; ++k) {
-            const int c = tid + k * nt;
-            const int col = 8 * c;
-            if (col + 8 <= V) {
-                raw[k] = *reinterpret_cast<const uint4*>(z + col);
-            } else {
-                half h[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) h[j] = (col + j < V) ? z[col + j] : NEG;
-                raw[k] = *reinterpret_cast<uint4*>(h);
-            }
-            if (col < V) {
-                const __half2* h2 = reinterpret_cast<const __half2*>(&raw[k]);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    float2 f = __half22float2(h2[j]);
-                    mx = fmaxf(mx, fmaxf(f.x, f.y));
-                }
-            }
-        }
-        mx = block_reduce_max(mx, sh);
-        // exponentials kept as float pairs would double the registers; keep the
-        // raw logits and recompute exp in the write pass only where needed.
-        float s = 0.0f;
-#pragma unroll
-        for (int k = 0; k < E; ++k) {
-            const int col = 8 * (tid + k * nt);
-            if (col < V) {
-                const __half2* h2 = reinterpret_cast<const __half2*>(&raw[k]);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    float2 f = __half22float2(h2[j]);
-                    const float e0 = (col + 2 * j < V) ? __expf(f.x - mx) : 0.0f;
-                    const float e1 = (col + 2 * j + 1 < V) ? __expf(f.y - mx) : 0.0f;
-                    s += e0 + e1;
-                }
-            }
-        }
-        s = block_reduce_sum(s, sh);
-        const float inv = 1.0f / s;
+        const uint4* z4 = reinterpret_cast<const uint4*>(z);
         const int t = __ldg(tgt + row);
         const bool tvalid = t >= 0 && t < V;
+        // the target logit is read before any thread can overwrite the row in place
+        const float zt = (row_loss && tid == 0 && tvalid) ? __half2float(z[t]) : 0.0f;
+        // ---------------- pass 1: online max / sum ----------------
+        float m = -INFINITY, s = 0.0f;
+        int c = tid;
+        for (; c + (kUnroll - 1) * kThreads < nvec; c += kUnroll * kThreads) {
+            uint4 u[kUnroll];
+#pragma unroll
+            for (int k = 0; k < kUnroll; ++k) u[k] = __ldcg(z4 + c + k * kThreads);
+#pragma unroll
+            for (int k = 0; k < kUnroll; ++k) add8(m, s, u[k]);
+        }
+        for (; c < nvec; c += kThreads) add8(m, s, __ldcg(z4 + c));
+        for (int j = nvec * 8 + tid; j < V; j += kThreads) {
+            const float f = __half2float(z[j]);
+            if (f > m) { s = (m == -INFINITY) ? 0.0f : s * __expf(m - f); m = f; }
+            s += __expf(f - m);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
+            merge(m, s, m2, s2);
+        }
+        if (lane == 0) { sm_m[warp] = m; sm_s[warp] = s; }
+        __syncthreads();
+        if (warp == 0) {
+            m = lane < kThreads / 32 ? sm_m[lane] : -INFINITY;
+            s = lane < kThreads / 32 ? sm_s[lane] : 0.0f;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
+                merge(m, s, m2, s2);
+            }
+            if (lane == 0) { s_row[0] = m; s_row[1] = s; }
+        }
+        __syncthreads();
+        const float mx = s_row[0], inv = 1.0f / s_row[1];
         if (row_loss && tid == 0) {
             float l = __int_as_float(0x7fc00000);   // NaN for an invalid target
-            if (tvalid) l = -logf(__expf(__half2float(z[t]) - mx) * inv + 1e-10f);
+            if (tvalid) l = -logf(__expf(zt - mx) * inv + 1e-10f);
             row_loss[row] = l;
         }
-        if (!dl) continue;   // loss-only mode
-        const float g = tvalid ? gs : 0.0f;
-        half* d = dl + (size_t)row * ld;
+        if (dl) {
+            // ---------------- pass 2: gradient (row re-read from L2) --------
+            const float g = tvalid ? gs : 0.0f;
+            half* d = dl + (size_t)row * ld;
+            uint4* d4 = reinterpret_cast<uint4*>(d);
+            for (int v = tid; v < nvec; v += kThreads) {
+                float f[8];
+                h8_to_f(__ldcg(z4 + v), f);
 #pragma unroll
-        for (int k = 0; k < E; ++k) {
-            const int col = 8 * (tid + k * nt);
-            if (col >= V) continue;
-            const __half2* h2 = reinterpret_cast<const __half2*>(&raw[k]);
-            float o[8];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                float2 f = __half22float2(h2[j]);
-                o[2 * j] = (__expf(f.x - mx) * inv - (col + 2 * j == t ? 1.0f : 0.0f)) * g;
-                o[2 * j + 1] = (__expf(f.y - mx) * inv - (col + 2 * j + 1 == t ? 1.0f : 0.0f)) * g;
+                for (int j = 0; j < 8; ++j) f[j] = (__expf(f[j] - mx) * inv - (8 * v + j == t ? 1.0f : 0.0f)) * g;
+                d4[v] = f_to_h8(f);
             }
-            if (col + 8 <= V) {
-                *reinterpret_cast<uint4*>(d + col) = f_to_h8(o);
-            } else {
-#pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    if (col + j < V) d[col + j] = __float2half_rn(o[j]);
-            }
+            for (int j = nvec * 8 + tid; j < V; j += kThreads)
+                d[j] = __float2half_rn((__expf(__half2float(z[j]) - mx) * inv - (j == t ? 1.0f : 0.0f)) * g);
         }
+        __syncthreads();   // s_row / sm_* reuse by the next row
     }
-}
-
-template <int E>
-void launch(int grid, int nt, cudaStream_t st, half* dl, const half* lg, int ld, const int* tgt, int N, int V,
-            float scale, const float* dscale, float* row_loss) {
-    xent_kernel<E><<<grid, nt, 0, st>>>(dl, lg, ld, tgt, N, V, scale, dscale, row_loss);
 }
 
 }  // namespace
@@ -135,27 +124,21 @@ using namespace rbk;
 extern "C" int rbk_softmax_xent_bwd(rbk_ctx* ctx, void* dlogits, const void* logits, int ld, const int* targets,
                                     int N, int V, float scale, const float* dscale, float* row_loss, void* stream) {
     RBK_REQUIRE(ctx && logits && targets && (dlogits || row_loss), "rbk_softmax_xent_bwd: null pointer");
-    RBK_REQUIRE(N > 0 && V > 0 && V <= 65536 && ld >= V && ld % 8 == 0,
-                "rbk_softmax_xent_bwd: need 0 < V <= 65536, ld >= V, ld %% 8 == 0 (V=%d ld=%d)", V, ld);
+    RBK_REQUIRE(N > 0 && V > 0 && V <= (1 << 24) && ld >= V && ld % 8 == 0,
+                "rbk_softmax_xent_bwd: need 0 < V, ld >= V, ld %% 8 == 0 (V=%d ld=%d)", V, ld);
     RBK_REQUIRE((!dlogits || aligned16(dlogits)) && aligned16(logits),
                 "rbk_softmax_xent_bwd: tensors must be 16-byte aligned");
-    int nt = ((V + 63) / 64 + 31) / 32 * 32;
-    nt = nt < 128 ? 128 : nt > 512 ? 512 : nt;
-    const int e = (V + 8 * nt - 1) / (8 * nt);
-    const int per_sm = 2048 / nt;
+    // rows in flight (one per CTA) are kept to <= 40 MB so the second pass hits L2
+    const double row_bytes = 2.0 * V;
+    int per_sm = (int)(40e6 / (row_bytes * ctx->num_sms));
+    per_sm = per_sm < 1 ? 1 : per_sm > 4 ? 4 : per_sm;
     int grid = ctx->num_sms * per_sm;
     if (grid > N) grid = N;
     cudaStream_t st = as_stream(stream);
     ProfScope prof(ctx, st, kCatXent,
                    (double)N * V * (dlogits ? 4.0 : 2.0) + 4.0 * N + (row_loss ? 4.0 * N : 0.0));
-    auto DL = (half*)dlogits;
-    auto LG = (const half*)logits;
-    if (e <= 1) launch<1>(grid, nt, st, DL, LG, ld, targets, N, V, scale, dscale, row_loss);
-    else if (e <= 2) launch<2>(grid, nt, st, DL, LG, ld, targets, N, V, scale, dscale, row_loss);
-    else if (e <= 4) launch<4>(grid, nt, st, DL, LG, ld, targets, N, V, scale, dscale, row_loss);
-    else if (e <= 8) launch<8>(grid, nt, st, DL, LG, ld, targets, N, V, scale, dscale, row_loss);
-    else if (e <= 12) launch<12>(grid, nt, st, DL, LG, ld, targets, N, V, scale, dscale, row_loss);
-    else launch<16>(grid, nt, st, DL, LG, ld, targets, N, V, scale, dscale, row_loss);
+    xent_kernel<<<grid, kThreads, 0, st>>>((half*)dlogits, (const half*)logits, ld, targets, N, V, scale, dscale,
+                                           row_loss);
     RBK_LAUNCHED("xent_kernel");
     return RBK_OK;
 }
