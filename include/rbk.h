@@ -342,6 +342,11 @@ int rbk_model_inject_inf(rbk_model* m, int64_t offset, int64_t stride);
  * ------------------------------------------------------------------------ */
 
 #define RBK_NCCL_ID_BYTES 128
+/* The all-reduce schedule (host only, no GPU needed): *count buckets, each
+ * out[3i..3i+2] = {backward unit after which it is launched (0 = LN_f + LM
+ * head, 1..L = layers L-1..0, L+1 = embeddings), arena begin, arena end}.
+ * Buckets tile the arena exactly once, in descending address order. */
+int rbk_dp_plan(const rbk_config* cfg, int64_t bucket_bytes, int64_t* out, int max, int* count);
 /* Fill a 128-byte NCCL unique id on the root rank (ncclGetUniqueId). */
 int rbk_dp_unique_id(void* id128);
 /* Join the communicator; bucket_bytes (25 MB) sets the all-reduce granularity. */

@@ -361,26 +361,43 @@ static void unit_range(rbk_model* m, int u, int64_t* b, int64_t* e) {
     *e = (l + 1 < L) ? m->tab[rbk_layer_tensor(l + 1, 0)].offset : m->tab[rbk_tail_tensor(&m->lay, 0)].offset;
 }
 
+// Bucket plan: walk the units in backward order, growing a pending range
+// downwards through the arena, and close a bucket once it holds at least
+// bucket_elems (the embeddings unit always closes the last one).  Pure host
+// code: identical on every rank for the same configuration.
+std::vector<DpBucket> dp_plan(const rbk_config* c, int64_t bucket_elems) {
+    rbk_model tmp;
+    tmp.lay = *c;
+    tmp.cfg.L = c->L;
+    tmp.tab.resize(rbk_num_tensors(c));
+    tmp.n = rbk_param_table(c, tmp.tab.data());
+    std::vector<DpBucket> out;
+    int64_t pend_end = tmp.n;
+    for (int u = 0; u <= c->L + 1; ++u) {
+        int64_t b, e;
+        unit_range(&tmp, u, &b, &e);
+        if (pend_end - b >= bucket_elems || u == c->L + 1) {
+            out.push_back(DpBucket{u, b, pend_end});
+            pend_end = b;
+        }
+    }
+    return out;
+}
+
 static int dp_unit_done(rbk_model* m, int u, cudaStream_t st) {
     DpState& d = m->dp;
-    static thread_local int64_t pend_end = -1;
-    static thread_local int64_t pend_begin = -1;
-    int64_t b, e;
-    unit_range(m, u, &b, &e);
-    if (u == 0) { pend_end = e; pend_begin = b; }
-    else pend_begin = b;
-    const bool last = (u == m->cfg.L + 1);
-    if (!last && pend_end - pend_begin < d.bucket_elems) return RBK_OK;
-    RBK_CUDA(cudaEventRecord(d.layer_done[u], st));
-    RBK_CUDA(cudaStreamWaitEvent(d.stream, d.layer_done[u], 0));
-    ncclResult_t r = ncclAllReduce(m->grad + pend_begin, m->grad + pend_begin, (size_t)(pend_end - pend_begin),
-                                   ncclFloat32, ncclSum, d.comm, d.stream);
-    if (r != ncclSuccess) {
-        set_error("ncclAllReduce failed: %s", ncclGetErrorString(r));
-        return RBK_ERR_NCCL;
+    for (const DpBucket& bk : d.plan) {
+        if (bk.unit != u) continue;
+        RBK_CUDA(cudaEventRecord(d.layer_done[u], st));
+        RBK_CUDA(cudaStreamWaitEvent(d.stream, d.layer_done[u], 0));
+        ncclResult_t r = ncclAllReduce(m->grad + bk.begin, m->grad + bk.begin, (size_t)(bk.end - bk.begin),
+                                       ncclFloat32, ncclSum, d.comm, d.stream);
+        if (r != ncclSuccess) {
+            set_error("ncclAllReduce failed: %s", ncclGetErrorString(r));
+            return RBK_ERR_NCCL;
+        }
     }
-    pend_end = pend_begin;
-    if (last) {
+    if (u == m->cfg.L + 1) {
         RBK_CUDA(cudaEventRecord(d.all_done, d.stream));
         RBK_CUDA(cudaStreamWaitEvent(st, d.all_done, 0));
     }
@@ -607,6 +624,18 @@ int rbk_model_inject_inf(rbk_model* m, int64_t offset, int64_t stride) {
     return RBK_OK;
 }
 
+int rbk_dp_plan(const rbk_config* cfg, int64_t bucket_bytes, int64_t* out, int max, int* count) {
+    RBK_REQUIRE(cfg && count && rbk_config_check(cfg) == 0 && bucket_bytes > 0, "rbk_dp_plan: bad arguments");
+    const std::vector<DpBucket> p = dp_plan(cfg, std::max<int64_t>(bucket_bytes / 4, 1));
+    *count = (int)p.size();
+    for (int i = 0; i < (int)p.size() && i < max && out; ++i) {
+        out[3 * i] = p[i].unit;
+        out[3 * i + 1] = p[i].begin;
+        out[3 * i + 2] = p[i].end;
+    }
+    return RBK_OK;
+}
+
 int rbk_dp_unique_id(void* id128) {
     RBK_REQUIRE(id128, "rbk_dp_unique_id: null pointer");
     static_assert(sizeof(ncclUniqueId) == RBK_NCCL_ID_BYTES, "NCCL unique id size");
@@ -636,6 +665,7 @@ int rbk_model_dp_init(rbk_model* m, const void* id128, int rank, int world, int6
     for (auto& e : m->dp.layer_done) RBK_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     RBK_CUDA(cudaEventCreateWithFlags(&m->dp.all_done, cudaEventDisableTiming));
     m->dp.bucket_elems = std::max<int64_t>(bucket_bytes / 4, 1);
+    m->dp.plan = dp_plan(&m->lay, m->dp.bucket_elems);
     m->dp.rank = rank;
     m->dp.world = world;
     m->dp.on = true;

@@ -81,12 +81,20 @@ struct LoraState {
     half *dyb = nullptr;            // [N, r] scratch
 };
 
+// One gradient all-reduce: fired after backward unit `unit` (0 = head,
+// 1..L = layers L-1..0, L+1 = embeddings), covering arena [begin, end).
+struct DpBucket {
+    int unit;
+    int64_t begin, end;
+};
+
 struct DpState {
     bool on = false;
     int rank = 0, world = 1;
     ncclComm_t comm = nullptr;
     cudaStream_t stream = nullptr;
     int64_t bucket_elems = 0;
+    std::vector<DpBucket> plan;
     std::vector<cudaEvent_t> layer_done;   // recorded after each layer's grads are final
     cudaEvent_t head_done = nullptr, all_done = nullptr;
 };

@@ -226,6 +226,16 @@ class RubidiumTransformer:
             pass
 
 
+def dp_plan(cfg: ModelConfig, bucket_bytes: int = 25 << 20):
+    """The gradient all-reduce schedule librbk uses: [(unit, begin, end)] (host only)."""
+    c = Config(cfg.V, cfg.T, cfg.D, cfg.H, cfg.L, cfg.FF)
+    cnt = C.c_int()
+    call("rbk_dp_plan", C.byref(c), C.c_int64(bucket_bytes), None, 0, C.byref(cnt))
+    buf = (C.c_int64 * (3 * cnt.value))()
+    call("rbk_dp_plan", C.byref(c), C.c_int64(bucket_bytes), buf, cnt.value, C.byref(cnt))
+    return [(buf[3 * i], buf[3 * i + 1], buf[3 * i + 2]) for i in range(cnt.value)]
+
+
 def dp_unique_id() -> bytes:
     buf = C.create_string_buffer(128)
     call("rbk_dp_unique_id", buf)

@@ -1,0 +1,103 @@
+"""Data-parallel host logic on CPU: two gloo ranks (world_size 2), no GPU.
+
+Checks the all-reduce schedule librbk builds (rbk_dp_plan) and the semantics
+the GPU path relies on, reproduced with gloo collectives on the same buckets:
+  - every rank derives the same plan; buckets tile the arena exactly once, in
+    backward (descending address) order, each >= the bucket size but the last;
+  - summing the pre-divided (1/world) per-rank gradients bucket by bucket gives
+    the gradient of the global mean loss;
+  - a non-finite value on one rank reaches every rank through the sum, so the
+    overflow / skip decision is identical everywhere.
+"""
+import os
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+import torch.distributed as dist  # noqa: E402
+import torch.multiprocessing as mp  # noqa: E402
+
+GPT2S = dict(V=50257, T=1024, D=768, H=12, L=12, FF=3072)
+TINY = dict(V=4096, T=128, D=256, H=4, L=4, FF=1024)
+
+
+def _plan(cfg, bucket_bytes):
+    from rbk.model import ModelConfig, dp_plan
+    return dp_plan(ModelConfig(**cfg), bucket_bytes)
+
+
+def _arena(cfg):
+    from rbk.model import ModelConfig, param_table
+    return param_table(ModelConfig(**cfg))
+
+
+@pytest.mark.parametrize("cfg,bucket_mb", [(GPT2S, 25), (TINY, 1), (TINY, 1000)])
+def test_plan_tiles_arena(cfg, bucket_mb):
+    table, n = _arena(cfg)
+    plan = _plan(cfg, bucket_mb << 20)
+    assert plan[0][2] == n and plan[-1][1] == 0
+    for (u0, b0, e0), (u1, b1, e1) in zip(plan, plan[1:]):
+        assert e1 == b0 and u1 > u0                     # contiguous, descending, in backward order
+    elems = (bucket_mb << 20) // 4
+    assert all(e - b >= elems for _, b, e in plan[:-1])
+    assert plan[-1][0] == cfg["L"] + 1                  # the embeddings close the last bucket
+    # the head (LM head, ln_f) is the first unit the backward finishes
+    lm_off = [off for name, off, r, c in table if name == "ln_f_w"][0]
+    assert plan[0][1] <= lm_off
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        cfg = TINY
+        plan = _plan(cfg, 1 << 20)
+        # all ranks agree on the plan
+        plans = [None] * world
+        dist.all_gather_object(plans, plan)
+        same = all(p == plans[0] for p in plans)
+        _, n = _arena(cfg)
+        rng = np.random.default_rng(100 + rank)
+        local = rng.standard_normal(n).astype(np.float32)       # this rank's mean-loss gradient
+        g = torch.from_numpy(local / world)                     # seed pre-divided by world
+        for _, b, e in plan:                                    # bucketed sum all-reduce, plan order
+            seg = g[b:e].clone()
+            dist.all_reduce(seg, op=dist.ReduceOp.SUM)
+            g[b:e] = seg
+        allg = [torch.zeros(n) for _ in range(world)]
+        dist.all_gather(allg, torch.from_numpy(local))
+        expect = torch.stack(allg).mean(0)
+        ok_sum = torch.allclose(g, expect, rtol=1e-5, atol=1e-6)
+        # overflow agreement: rank 1 plants an inf in the last bucket
+        h = torch.ones(n)
+        if rank == 1:
+            h[plan[-1][1] + 3] = float("inf")
+        for _, b, e in plan:
+            seg = h[b:e].clone()
+            dist.all_reduce(seg, op=dist.ReduceOp.SUM)
+            h[b:e] = seg
+        skip = torch.tensor([int(not torch.isfinite(h).all())])
+        skips = [torch.zeros(1, dtype=torch.long) for _ in range(world)]
+        dist.all_gather(skips, skip)
+        q.put((rank, same, ok_sum, [int(s) for s in skips]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_gloo_bucketed_allreduce_semantics():
+    world = 2
+    port = 29500 + (os.getpid() % 1000)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, same, ok_sum, skips in res:
+        assert same, "ranks derived different all-reduce plans"
+        assert ok_sum, "bucketed sum of pre-divided gradients != mean gradient"
+        assert skips == [1, 1], "overflow decision differs across ranks"
