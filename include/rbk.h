@@ -95,6 +95,27 @@ int rbk_ln_bwd(rbk_ctx* ctx, void* dx, float* dgamma, float* dbeta, float* dbias
                const void* dres, const void* x, const void* gamma, const float* mean, const float* rstd,
                int N, int D, int flags, void* stream);
 
+/* rbk_ln_bwd for callers that cannot allocate device memory: no rbk_ctx, no
+ * cudaMalloc / cudaFree or allocating library call.  No counterpart in the
+ * reference.  Meant for hosts whose device memory is all owned by their own
+ * pool (as the reference trainer's fixed MemPool arena) or that cannot take
+ * the device-wide synchronisation an allocation costs inside a step loop.
+ * Same arguments and results as rbk_ln_bwd (identical launch shape).
+ *   - Scratch: one fixed array of RBK_LN_BWD_NOALLOC_SCRATCH_BYTES (4 MiB) in
+ *     device memory, reserved once by every GPU that loads the library and
+ *     held until the process exits; enough for D <= 2048 on a 148-SM B200.
+ *     Larger needs are rejected with RBK_ERR_INVALID (use rbk_ln_bwd).
+ *   - The first call on each device looks up that array's device address
+ *     (with the device current); make that first call before any stream
+ *     capture.
+ *   - Every call shares the one array.  Each call overwrites the whole part it
+ *     uses, so nothing carries over, but calls that overlap on the GPU (other
+ *     streams, other threads) race on it: serialise them. */
+#define RBK_LN_BWD_NOALLOC_SCRATCH_BYTES (4u << 20)
+int rbk_ln_bwd_noalloc(void* dx, float* dgamma, float* dbeta, float* dbias_out, const void* dy, const void* dres,
+                       const void* x, const void* gamma, const float* mean, const float* rstd, int N, int D,
+                       int flags, void* stream);
+
 /* ------------------------------------------------------------------------
  * Softmax cross-entropy (LM head loss)
  * ------------------------------------------------------------------------ */

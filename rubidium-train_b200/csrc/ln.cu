@@ -314,3 +314,110 @@ int rbk_ln_bwd(rbk_ctx* ctx, void* dx, float* dgamma, float* dbeta, float* dbias
 }
 
 }  // extern "C"
+
+// ----------------------------------------------------------------------------
+// LayerNorm backward for callers that cannot allocate device memory.
+//
+// Some callers own every byte of device memory through their own pool (the
+// reference trainer reserves a fixed arena up front, src/cuda_kernels.cuh:46-57),
+// or cannot afford an allocation — cudaMalloc / cudaFree synchronise the device
+// — inside their step loop.  They cannot create an rbk_ctx either, because the
+// context allocates its flags and scratch.  This variant needs no context: its
+// column partials live in the fixed array below, which the library reserves
+// once per GPU that loads it and holds until the process exits.
+// ----------------------------------------------------------------------------
+#include <mutex>
+
+namespace rbk {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = RBK_LN_BWD_NOALLOC_SCRATCH_BYTES;
+static __device__ __align__(256) float g_ln_bwd_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[kNoAllocMaxDevices] = {};   // device address of the array, per device
+int g_noalloc_sms[kNoAllocMaxDevices] = {};
+
+// Set-up on the first call on a device (with that device current): the host
+// name of a __device__ array is only a host-side stand-in, so the kernel must
+// be given the address the runtime reports for this device.
+int noalloc_setup(int* dev_out, float** ptr, int* sms) {
+    int dev = 0;
+    RBK_CUDA(cudaGetDevice(&dev));
+    RBK_REQUIRE(dev >= 0 && dev < kNoAllocMaxDevices, "rbk_ln_bwd_noalloc: device %d beyond %d", dev,
+                kNoAllocMaxDevices);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        cudaDeviceProp prop;
+        RBK_CUDA(cudaGetDeviceProperties(&prop, dev));
+        if (prop.major != 10 || prop.minor != 0) {
+            set_error("librbk is built for sm_100a (B200); device %d is sm_%d%d", dev, prop.major, prop.minor);
+            return RBK_ERR_UNSUPPORTED;
+        }
+        void* p = nullptr;
+        RBK_CUDA(cudaGetSymbolAddress(&p, g_ln_bwd_noalloc_scratch));
+        g_noalloc_sms[dev] = prop.multiProcessorCount;
+        g_noalloc_ptr[dev] = static_cast<float*>(p);
+    }
+    *dev_out = dev;
+    *ptr = g_noalloc_ptr[dev];
+    *sms = g_noalloc_sms[dev];
+    return RBK_OK;
+}
+
+}  // namespace
+}  // namespace rbk
+
+extern "C" int rbk_ln_bwd_noalloc(void* dx, float* dgamma, float* dbeta, float* dbias_out, const void* dy,
+                                  const void* dres, const void* x, const void* gamma, const float* mean,
+                                  const float* rstd, int N, int D, int flags, void* stream) {
+    RBK_REQUIRE(dx && dgamma && dbeta && dy && x && gamma && mean && rstd, "rbk_ln_bwd_noalloc: null pointer");
+    RBK_REQUIRE(N > 0 && D > 0 && D % 8 == 0 && D <= 4096,
+                "rbk_ln_bwd_noalloc: need D %% 8 == 0 and D <= 4096 (D=%d)", D);
+    RBK_REQUIRE(aligned16(dx) && aligned16(dy) && aligned16(x) && aligned16(gamma) && (!dres || aligned16(dres)),
+                "rbk_ln_bwd_noalloc: tensors must be 16-byte aligned");
+    int dev = 0, sms = 0;
+    float* part = nullptr;
+    RBK_TRY(noalloc_setup(&dev, &part, &sms));
+    // Same launch shape as rbk_ln_bwd, so both entry points give identical results.
+    const int tpt = ((D / 8 + 31) / 32) * 32;
+    int teams = 512 / tpt;
+    teams = teams < 1 ? 1 : teams > kLnMaxTeams ? kLnMaxTeams : teams;
+    const int threads = teams * tpt;
+    const int ngroups = (N + kLnRows - 1) / kLnRows;
+    int blocks = sms;
+    const int need = (ngroups + teams - 1) / teams;
+    if (blocks > need) blocks = need;
+    const size_t scratch = sizeof(float) * 3 * (size_t)D * blocks;
+    if (scratch > kNoAllocScratchBytes) {
+        set_error("rbk_ln_bwd_noalloc: needs %zu bytes of scratch (3 x D=%d x %d CTAs x 4 B) but the fixed "
+                  "array holds %zu; use rbk_ln_bwd for this size",
+                  scratch, D, blocks, kNoAllocScratchBytes);
+        return RBK_ERR_INVALID;
+    }
+    const size_t smem = sizeof(float) * ((size_t)2 * teams * 2 * kLnRows * (tpt / 32) + (size_t)teams * 3 * D);
+    cudaStream_t st = as_stream(stream);
+    const bool ref = (flags & RBK_LN_REFERENCE_FORMULA) != 0;
+    const bool res = dres != nullptr, bias = dbias_out != nullptr;
+    auto DX = (half*)dx;
+    auto DY = (const half*)dy;
+    auto DR = (const half*)dres;
+    auto X = (const half*)x;
+    auto G = (const half*)gamma;
+#define RBK_LN_BWD(R_, S_, B_) \
+    RBK_TRY((launch_bwd<R_, S_, B_>(blocks, threads, teams, smem, st, DX, part, DY, DR, X, G, mean, rstd, N, D)))
+    if (ref) {
+        if (res) { if (bias) RBK_LN_BWD(true, true, true); else RBK_LN_BWD(true, true, false); }
+        else { if (bias) RBK_LN_BWD(true, false, true); else RBK_LN_BWD(true, false, false); }
+    } else {
+        if (res) { if (bias) RBK_LN_BWD(false, true, true); else RBK_LN_BWD(false, true, false); }
+        else { if (bias) RBK_LN_BWD(false, false, true); else RBK_LN_BWD(false, false, false); }
+    }
+#undef RBK_LN_BWD
+    RBK_LAUNCHED("ln_bwd_kernel (no-alloc)");
+    dim3 rg((D + 31) / 32, bias ? 3 : 2);
+    ln_bwd_reduce_kernel<<<rg, 256, 0, st>>>(dgamma, dbeta, dbias_out, part, blocks, D);
+    RBK_LAUNCHED("ln_bwd_reduce_kernel (no-alloc)");
+    return RBK_OK;
+}

@@ -69,6 +69,7 @@ _SIGS = {
     "rbk_model_ctx": (i32, [vp, C.POINTER(vp)]),
     "rbk_ln_fwd": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, f32, vp]),
     "rbk_ln_bwd": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, vp]),
+    "rbk_ln_bwd_noalloc": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, vp]),
     "rbk_softmax_xent_bwd": (i32, [vp, vp, vp, i32, vp, i32, i32, f32, vp, vp, vp]),
     "rbk_sum": (i32, [vp, vp, vp, i32, f32, vp]),
     "rbk_attn_softmax_bwd": (i32, [vp, vp, vp, vp, i32, i32, i32, vp]),
