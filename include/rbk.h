@@ -321,7 +321,11 @@ int rbk_model_sync_fp16(rbk_model* m, void* stream);
 int rbk_model_init_weights(rbk_model* m, uint64_t seed, float std, void* stream);
 
 /* forward (src/model.h:130): device tokens/targets [B*S] int32.  Writes the
- * mean loss to *loss_dev (device FP32) when non-NULL; targets may be NULL. */
+ * mean loss to *loss_dev (device FP32) when non-NULL; targets may be NULL.
+ * In training mode (the default) the pass that computes the loss also writes
+ * dlogits over the logits buffer for the following backward; in eval mode
+ * (rbk_model_set_training(m, 0)) the logits are left intact and backward
+ * recomputes dlogits from them. */
 int rbk_model_forward(rbk_model* m, const int* tokens, const int* targets, int B, int S, float* loss_dev,
                       void* stream);
 /* backward (src/model.h:131): accumulates gradients of
@@ -331,6 +335,8 @@ int rbk_model_forward(rbk_model* m, const int* tokens, const int* targets, int B
  * forward on the same tokens. */
 int rbk_model_backward(rbk_model* m, const int* tokens, const int* targets, int B, int S, float grad_scale,
                        void* stream);
+/* Training (1, default) / eval (0) mode, see rbk_model_forward. */
+int rbk_model_set_training(rbk_model* m, int training);
 /* optimizer_step (src/model.h:132) fused with the overflow check, unscale,
  * optional per-tensor clip (max_norm <= 0: off), scaler update and skip. */
 int rbk_model_optimizer_step(rbk_model* m, int t, float lr, float b1, float b2, float eps, float wd,

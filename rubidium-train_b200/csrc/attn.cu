@@ -218,29 +218,39 @@ __global__ void __launch_bounds__(128) flash_fwd_kernel(half* __restrict__ O, fl
 // ------------------------------------------------------------------ backward --
 
 // Dot[bh, s] = sum_d dO[s, d] O[s, d]  and zero the FP32 dQ accumulator.
+// One thread per 16-byte chunk (coalesced); the HD/8 threads of a head reduce
+// by shuffles (they are adjacent lanes of one warp since HD/8 divides 32).
 template <int HD>
 __global__ void flash_bwd_pre_kernel(float* __restrict__ Dot, float* __restrict__ dq_acc, const half* __restrict__ O,
                                      const half* __restrict__ dO, int BS, int S, int H) {
-    const long total = (long)BS * H;
+    constexpr int G = HD / 8;            // chunks per (row, head)
     const int D = H * HD;
-    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-        const int n = (int)(i / H), h = (int)(i % H);
-        const uint4* o4 = reinterpret_cast<const uint4*>(O + (size_t)n * D + h * HD);
-        const uint4* d4 = reinterpret_cast<const uint4*>(dO + (size_t)n * D + h * HD);
+    const long total = (long)BS * (D / 8);
+    const long stride = (long)gridDim.x * blockDim.x;
+    // every lane of a warp runs the same number of iterations (shuffles below)
+    const long iters = (total + stride - 1) / stride;
+    for (long it = 0; it < iters; ++it) {
+        const long i = it * stride + blockIdx.x * (long)blockDim.x + threadIdx.x;
+        const bool ok = i < total;
         float acc = 0.0f;
-#pragma unroll
-        for (int c = 0; c < HD / 8; ++c) {
+        if (ok) {
             float a[8], bb[8];
-            h8_to_f(__ldg(o4 + c), a);
-            h8_to_f(__ldg(d4 + c), bb);
+            h8_to_f(__ldg(reinterpret_cast<const uint4*>(O) + i), a);
+            h8_to_f(__ldg(reinterpret_cast<const uint4*>(dO) + i), bb);
 #pragma unroll
             for (int k = 0; k < 8; ++k) acc += a[k] * bb[k];
+            float4* z = reinterpret_cast<float4*>(dq_acc) + 2 * i;
+            z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+            z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        const int b = n / S, s = n % S;
-        Dot[((size_t)b * H + h) * S + s] = acc;
-        float4* z = reinterpret_cast<float4*>(dq_acc + (size_t)n * D + h * HD);
 #pragma unroll
-        for (int c = 0; c < HD / 4; ++c) z[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int o = 1; o < G; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (ok && (threadIdx.x & (G - 1)) == 0) {
+            const long n = i / (D / 8);
+            const int h = (int)((i % (D / 8)) / G);
+            const long b = n / S, s = n % S;
+            Dot[((size_t)b * H + h) * S + s] = acc;
+        }
     }
 }
 
@@ -480,7 +490,7 @@ int bwd(rbk_ctx* ctx, void* dqkv, float* dbias, const void* qkv, const void* o, 
     float* Dot = (float*)ws;
     float* dq_acc = (float*)((char*)ws + dot_bytes);
     {
-        const long work = (long)BS * H;
+        const long work = (long)BS * (D / 8);
         long gsz = (work + 255) / 256;
         if (gsz > ctx->num_sms * 16) gsz = ctx->num_sms * 16;
         flash_bwd_pre_kernel<HD><<<(int)gsz, 256, 0, st>>>(Dot, dq_acc, (const half*)o, (const half*)dout, (int)BS, S, H);
@@ -496,7 +506,8 @@ int bwd(rbk_ctx* ctx, void* dqkv, float* dbias, const void* qkv, const void* o, 
     flash_bwd_kernel<HD><<<grid, 128, SMEM, st>>>((half*)dqkv, dq_acc, dbias, (const half*)qkv, (const half*)dout,
                                                   lse, Dot, S, H, scale, scale * kLog2e);
     RBK_LAUNCHED("flash_bwd_kernel");
-    const int rows_per_block = 256;
+    // enough CTAs to stream the FP32 accumulator at full bandwidth (>= 4 per SM)
+    const int rows_per_block = 32;
     dim3 pg((D / 8 + 127) / 128, (int)((BS + rows_per_block - 1) / rows_per_block));
     flash_bwd_post_kernel<<<pg, 128, 0, st>>>((half*)dqkv, dbias, dq_acc, (int)BS, D, rows_per_block);
     RBK_LAUNCHED("flash_bwd_post_kernel");

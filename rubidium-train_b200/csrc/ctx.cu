@@ -13,7 +13,7 @@ static std::atomic<long long> g_launches{0};
 
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
-constexpr int kProfPairs = 8192;
+constexpr int kProfPairs = 32768;   // ~130 timed steps of the 12-layer model
 
 ProfScope::ProfScope(rbk_ctx* c, cudaStream_t s, int cat, double work) : ctx(c), st(s) {
     if (!c || !c->prof.on) return;

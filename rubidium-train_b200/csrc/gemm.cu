@@ -34,19 +34,41 @@ namespace rbk {
 namespace gemm {
 
 constexpr int BM = 128, BK = 64, UMMA_K = 16;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;                  // two warps per TMEM lane quarter, split by columns
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kStageRow = 80;                 // epilogue staging tile: 32 rows x (64 B + 16 B pad)
+constexpr int kStageBytes = 32 * kStageRow;
+
+// GELU with the hardware tanh (tanh.approx.f32, ~2^-11 relative error: the
+// size of the FP16 rounding that follows).  GPT-2 tanh form, as the oracle.
+__device__ __forceinline__ float tanh_fast(float x) {
+    float y;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float gelu_fast(float x) {
+    const float c = 0.7978845608028654f, a = 0.044715f;
+    return 0.5f * x * (1.0f + tanh_fast(c * (x + a * x * x * x)));
+}
+__device__ __forceinline__ float gelu_grad_fast(float x) {
+    const float c = 0.7978845608028654f, a = 0.044715f;
+    const float t = tanh_fast(c * (x + a * x * x * x));
+    return 0.5f * (1.0f + t) + 0.5f * x * (1.0f - t * t) * c * (1.0f + 3.0f * a * x * x);
+}
 
 template <int BN>
 struct Cfg {
-    static constexpr int STAGES = BN == 256 ? 4 : 6;
+    static constexpr int STAGES = BN == 256 ? 4 : BN == 192 ? 5 : 6;
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int ONES_BYTES = 16 * BK * 2;
     static constexpr int BAR_BYTES = 256;
-    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + ONES_BYTES + BAR_BYTES;
+    static constexpr int EPI_BYTES = kEpiWarps * kStageBytes;
+    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + ONES_BYTES + EPI_BYTES + BAR_BYTES;
     static constexpr uint32_t TMEM_COLS = 512;
-    static constexpr int ACC2_COL = 2 * BN;   // ones-MMA accumulators (BN == 128 only)
+    static constexpr int ACC2_COL = 2 * BN;   // ones-MMA accumulators (BN <= 192 only)
+    static constexpr bool ROWSUM_OK = 2 * BN + 32 <= (int)TMEM_COLS;
 };
 
 struct Params {
@@ -182,48 +204,127 @@ __device__ __forceinline__ void decode_unit(const Params& p, int u, int& m_blk, 
 }
 
 // ------------------------------------------------------------- epilogue ----
+// Every epilogue warp owns a 32-row x 32-column chunk at a time (thread =
+// row, as tcgen05.ld 32x32b delivers it).  Global traffic goes through a
+// private shared tile (32 rows x 80 B: 64 B of data + 16 B pad, so each
+// 8-thread phase of a 16-byte access hits distinct banks) and is issued
+// row-segment-wise: lane -> (row lane/4 + 8i, 16-byte piece lane%4), i.e. each
+// instruction covers 8 full 64-byte row segments instead of 32 scattered
+// 16-byte pieces.
+// Coalesced loads of a 32 x 32 half tile (row pitch ld) into registers: lane
+// holds pieces (row lane/4 + 8i, 16-byte piece lane%4).  Issued one chunk
+// ahead so the HBM latency overlaps the previous chunk (or the MMAs).
+__device__ __forceinline__ void prefetch_h(uint4* pf, const half* g, int ld, int m0, int n, const Params& p,
+                                           int lane) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int rr = i * 8 + (lane >> 2), pc = lane & 3;
+        const int m = m0 + rr, col = n + 8 * pc;
+        uint4 u = make_uint4(0, 0, 0, 0);
+        if (m < p.M && col < p.N) {
+            const half* src = g + (size_t)m * ld + col;
+            if (col + 8 <= p.N) {
+                u = __ldg(reinterpret_cast<const uint4*>(src));
+            } else {
+                half h[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) h[e] = col + e < p.N ? src[e] : __float2half(0.0f);
+                u = *reinterpret_cast<uint4*>(h);
+            }
+        }
+        pf[i] = u;
+    }
+}
+__device__ __forceinline__ void stage_in_h(uint8_t* st, const uint4* pf, int lane) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        *reinterpret_cast<uint4*>(st + (i * 8 + (lane >> 2)) * kStageRow + (lane & 3) * 16) = pf[i];
+}
+// Coalesced stage -> global for a 32 x 32 half tile.
+__device__ __forceinline__ void stage_out_h(const uint8_t* st, half* g, int ld, int m0, int n, const Params& p,
+                                            int lane) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int rr = i * 8 + (lane >> 2), pc = lane & 3;
+        const int m = m0 + rr, col = n + 8 * pc;
+        if (m >= p.M || col >= p.N) continue;
+        const uint4 u = *reinterpret_cast<const uint4*>(st + rr * kStageRow + pc * 16);
+        half* dst = g + (size_t)m * ld + col;
+        if (col + 8 <= p.N) {
+            *reinterpret_cast<uint4*>(dst) = u;
+        } else {
+            const half* h = reinterpret_cast<const half*>(&u);
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+                if (col + e < p.N) dst[e] = h[e];
+        }
+    }
+}
+// Own row (thread = row) <-> stage, 32 halves as 4 x 16 B.
+__device__ __forceinline__ void row_to_stage_h(uint8_t* st, int lane, const float* v) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) *reinterpret_cast<uint4*>(st + lane * kStageRow + k * 16) = f_to_h8(v + 8 * k);
+}
+__device__ __forceinline__ void row_from_stage_h(const uint8_t* st, int lane, float* v) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) h8_to_f(*reinterpret_cast<const uint4*>(st + lane * kStageRow + k * 16), v + 8 * k);
+}
+
+// r: 32 FP32 accumulators of row m0 + lane, columns n .. n+31.
+// pf: this chunk's aux pieces (prefetch_h), used when p.aux is set.
 template <int EPI>
-__device__ __forceinline__ void epilogue_chunk(const Params& p, int m, int n, const uint32_t* r) {
-    // r: 32 FP32 accumulators of row m, columns n .. n+31
-    if (m >= p.M || n >= p.N) return;
-    const bool full = n + 32 <= p.N;
+__device__ __forceinline__ void epilogue_chunk(const Params& p, int m0, int n, const uint32_t* r, uint8_t* st,
+                                               int lane, const uint4* pf) {
+    if (n >= p.N || m0 >= p.M) return;                     // warp-uniform: nothing of this chunk is in C
     float v[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
 
     if constexpr (EPI == RBK_EPI_ACC_F32 || EPI == RBK_EPI_STORE_F32) {
-        float* c = reinterpret_cast<float*>(p.C) + (size_t)m * p.ldc + n;
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] *= p.alpha;
-        if (full) {
+        float* C = reinterpret_cast<float*>(p.C);
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-                if constexpr (EPI == RBK_EPI_ACC_F32)
-                    red_add_v4(c + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
-                else
-                    *reinterpret_cast<float4*>(c + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-            }
-        } else {
+        for (int hh = 0; hh < 2; ++hh) {             // 16 FP32 columns (64 B per row) at a time
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                if (n + j < p.N) {
-                    if constexpr (EPI == RBK_EPI_ACC_F32)
-                        atomicAdd(c + j, v[j]);
-                    else
-                        c[j] = v[j];
+            for (int k = 0; k < 4; ++k)
+                *reinterpret_cast<float4*>(st + lane * kStageRow + k * 16) =
+                    make_float4(v[16 * hh + 4 * k], v[16 * hh + 4 * k + 1], v[16 * hh + 4 * k + 2],
+                                v[16 * hh + 4 * k + 3]);
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int rr = i * 8 + (lane >> 2), pc = lane & 3;
+                const int m = m0 + rr, col = n + 16 * hh + 4 * pc;
+                if (m < p.M && col < p.N) {
+                    const float4 f = *reinterpret_cast<const float4*>(st + rr * kStageRow + pc * 16);
+                    float* dst = C + (size_t)m * p.ldc + col;
+                    if (col + 4 <= p.N) {
+                        if constexpr (EPI == RBK_EPI_ACC_F32) red_add_v4(dst, f.x, f.y, f.z, f.w);
+                        else *reinterpret_cast<float4*>(dst) = f;
+                    } else {
+                        const float fv[4] = {f.x, f.y, f.z, f.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            if (col + e < p.N) {
+                                if constexpr (EPI == RBK_EPI_ACC_F32) atomicAdd(dst + e, fv[e]);
+                                else dst[e] = fv[e];
+                            }
+                        }
+                    }
                 }
             }
+            __syncwarp();
         }
         return;
     } else {
-        half* c = reinterpret_cast<half*>(p.C) + (size_t)m * p.ldc + n;
         const int lda = p.ld_aux ? p.ld_aux : p.ldc;
         if constexpr (EPI == RBK_EPI_STORE_F16) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] *= p.alpha;
         }
-        if (p.bias && EPI != RBK_EPI_GELU_BWD) {
-            if (full) {
+        if (p.bias && EPI != RBK_EPI_GELU_BWD) {          // one 64-byte bias row, broadcast to all lanes
+            if (n + 32 <= p.N) {
 #pragma unroll
                 for (int j = 0; j < 32; j += 8) {
                     float b[8];
@@ -237,55 +338,29 @@ __device__ __forceinline__ void epilogue_chunk(const Params& p, int m, int n, co
                     if (n + j < p.N) v[j] += __half2float(p.bias[n + j]);
             }
         }
-        if (p.aux) {
-            const half* a = p.aux + (size_t)m * lda + n;
-            if (full) {
+        if (p.aux) {                                       // residual or GELU pre-activation
+            stage_in_h(st, pf, lane);
+            __syncwarp();
+            float b[32];
+            row_from_stage_h(st, lane, b);
+            __syncwarp();
 #pragma unroll
-                for (int j = 0; j < 32; j += 8) {
-                    float b[8];
-                    h8_to_f(__ldg(reinterpret_cast<const uint4*>(a + j)), b);
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        if constexpr (EPI == RBK_EPI_GELU_BWD)
-                            v[j + q] *= gelu_grad_f(b[q]);
-                        else
-                            v[j + q] += b[q];
-                    }
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    if (n + j < p.N) {
-                        const float b = __half2float(a[j]);
-                        if constexpr (EPI == RBK_EPI_GELU_BWD)
-                            v[j] *= gelu_grad_f(b);
-                        else
-                            v[j] += b;
-                    }
-                }
+            for (int j = 0; j < 32; ++j) {
+                if constexpr (EPI == RBK_EPI_GELU_BWD) v[j] *= gelu_grad_fast(b[j]);
+                else v[j] += b[j];
             }
         }
-        if (full) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 8) *reinterpret_cast<uint4*>(c + j) = f_to_h8(v + j);
-        } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-                if (n + j < p.N) c[j] = __float2half_rn(v[j]);
-        }
+        row_to_stage_h(st, lane, v);
+        __syncwarp();
+        stage_out_h(st, reinterpret_cast<half*>(p.C), p.ldc, m0, n, p, lane);
+        __syncwarp();
         if constexpr (EPI == RBK_EPI_BIAS_GELU) {
-            half* o = p.aux_out + (size_t)m * lda + n;
-            float gl[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) gl[j] = gelu_f(v[j]);
-            if (full) {
-#pragma unroll
-                for (int j = 0; j < 32; j += 8) *reinterpret_cast<uint4*>(o + j) = f_to_h8(gl + j);
-            } else {
-#pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    if (n + j < p.N) o[j] = __float2half_rn(gl[j]);
-            }
+            for (int j = 0; j < 32; ++j) v[j] = gelu_fast(v[j]);
+            row_to_stage_h(st, lane, v);
+            __syncwarp();
+            stage_out_h(st, p.aux_out, lda, m0, n, p, lane);
+            __syncwarp();
         }
     }
 }
@@ -301,7 +376,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     uint8_t* gbase = smem_raw + (base - raw);
     const uint32_t sA0 = base;                                       // stage s: A at s*STAGE_BYTES
     const uint32_t ones = base + C::STAGES * C::STAGE_BYTES;          // 2 KB of fp16 ones
-    const uint32_t bars = ones + C::ONES_BYTES;
+    const uint32_t epi_stage = ones + C::ONES_BYTES;                 // kEpiWarps x kStageBytes
+    const uint32_t bars = epi_stage + C::EPI_BYTES;
     uint8_t* gbars = gbase + (bars - base);
     auto full_bar = [&](int s) { return bars + 8u * s; };
     auto empty_bar = [&](int s) { return bars + 8u * (C::STAGES + s); };
@@ -325,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(tfull_bar(b), 1);
-            mbar_init(tempty_bar(b), 4);
+            mbar_init(tempty_bar(b), kEpiWarps);
         }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -388,7 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x) {
                 int mb, nb, kb0, kb1;
                 decode_unit(p, u, mb, nb, kb0, kb1);
-                const bool rowsum = EPI == RBK_EPI_ACC_F32 && BN == 128 && p.dbias_rows && nb == 0;
+                const bool rowsum = EPI == RBK_EPI_ACC_F32 && C::ROWSUM_OK && p.dbias_rows && nb == 0;
                 if (!mbar_wait(tempty_bar(buf), bphase ^ 1, abort_flag)) break;
                 fence_after();
                 const uint32_t dacc = tmem + buf * BN;
@@ -418,24 +494,36 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     } else {
         // ------------------------------ epilogue ----------------------------
         const int q = warp & 3;                 // TMEM lane quarter of this warp
+        const int half_id = (warp - 2) / 4;     // which half of the tile's columns
+        constexpr int kChunks = BN / 32;
+        const int c0 = half_id * (kChunks / 2), c1 = half_id ? kChunks : kChunks / 2;
         const int row = q * 32 + lane;
+        uint8_t* my_stage = gbase + (epi_stage - base) + (warp - 2) * kStageBytes;
         int buf = 0;
         uint32_t bphase = 0;
         for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
             int mb, nb, kb0, kb1;
             decode_unit(p, u, mb, nb, kb0, kb1);
+            const int m0 = mb * BM + q * 32;
+            // residual / pre-activation of the first chunk: fetched while the MMAs run
+            constexpr bool kAux = EPI == RBK_EPI_STORE_F16 || EPI == RBK_EPI_BIAS_GELU || EPI == RBK_EPI_GELU_BWD;
+            const int lda = p.ld_aux ? p.ld_aux : p.ldc;
+            uint4 pf[4];
+            if (kAux && p.aux) prefetch_h(pf, p.aux, lda, m0, nb * BN + c0 * 32, p, lane);
             if (!mbar_wait(tfull_bar(buf), bphase, abort_flag)) break;
             fence_after();
             const int m = mb * BM + row;
             const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + buf * BN;
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
+            for (int c = c0; c < c1; ++c) {
                 uint32_t r[32];
                 tmem_ld32(tbase + c * 32, r);
+                uint4 cur[4] = {pf[0], pf[1], pf[2], pf[3]};
+                if (kAux && p.aux && c + 1 < c1) prefetch_h(pf, p.aux, lda, m0, nb * BN + (c + 1) * 32, p, lane);
                 tmem_wait_ld();
-                epilogue_chunk<EPI>(p, m, nb * BN + c * 32, r);
+                epilogue_chunk<EPI>(p, m0, nb * BN + c * 32, r, my_stage, lane, cur);
             }
-            if (EPI == RBK_EPI_ACC_F32 && BN == 128 && p.dbias_rows && nb == 0) {
+            if (EPI == RBK_EPI_ACC_F32 && C::ROWSUM_OK && p.dbias_rows && nb == 0 && half_id == 0) {
                 const uint32_t v = tmem_ld1(tmem + ((uint32_t)(q * 32) << 16) + C::ACC2_COL + buf * 16);
                 tmem_wait_ld();
                 if (m < p.M) atomicAdd(p.dbias_rows + m, p.alpha * __uint_as_float(v));
@@ -533,8 +621,14 @@ int rbk_gemm(rbk_ctx* ctx, const rbk_gemm_desc* d, void* stream) {
     RBK_REQUIRE(d->epilogue != RBK_EPI_GELU_BWD || d->aux, "rbk_gemm: GELU_BWD needs aux (pre-activation)");
     RBK_REQUIRE(!d->dbias_rows || d->epilogue == RBK_EPI_ACC_F32, "rbk_gemm: dbias_rows needs ACC_F32");
     const int epi = d->epilogue;
-    const bool f32out = epi == RBK_EPI_ACC_F32 || epi == RBK_EPI_STORE_F32;
-    const int BN = (!f32out && d->N >= 512) ? 256 : 128;
+    // Tile width: N=256 tiles amortise each A tile over the most MMA columns; the
+    // wgrad with a fused bias gradient uses N=192 so that two accumulators plus
+    // the ones-MMA accumulator fit the 512 TMEM columns; narrow problems use 128.
+    int BN;
+    if (epi == RBK_EPI_ACC_F32)
+        BN = d->N <= 128 ? 128 : (d->dbias_rows || d->N < 256) ? 192 : 256;
+    else
+        BN = d->N >= 512 ? 256 : 128;
     Params p;
     p.M = d->M; p.N = d->N; p.K = d->K;
     p.m_blocks = (d->M + BM - 1) / BM;
@@ -542,10 +636,25 @@ int rbk_gemm(rbk_ctx* ctx, const rbk_gemm_desc* d, void* stream) {
     p.k_blocks = (d->K + BK - 1) / BK;
     int splits = 1;
     if (epi == RBK_EPI_ACC_F32) {
+        // Split K (FP32 accumulation makes the splits add up) so the persistent
+        // grid's waves are nearly full: take the fewest splits whose wave
+        // efficiency units / (ceil(units / SMs) * SMs) is >= 90%, else the best.
         const int tiles = p.m_blocks * p.n_blocks;
-        if (d->split_k > 0) splits = d->split_k;
-        else if (tiles < ctx->num_sms) splits = (ctx->num_sms + tiles - 1) / tiles;
-        int max_split = p.k_blocks / 4 > 0 ? p.k_blocks / 4 : 1;
+        const int max_split = p.k_blocks / 8 > 0 ? p.k_blocks / 8 : 1;
+        if (d->split_k > 0) {
+            splits = d->split_k;
+        } else {
+            double best = -1.0;
+            for (int s = 1; s <= max_split && s <= 64; ++s) {
+                const int kbps = (p.k_blocks + s - 1) / s;
+                const int real = (p.k_blocks + kbps - 1) / kbps;
+                const long units = (long)tiles * real;
+                const long waves = (units + ctx->num_sms - 1) / ctx->num_sms;
+                const double eff = (double)units / (double)(waves * ctx->num_sms);
+                if (eff > best + 1e-9) { best = eff; splits = s; }
+                if (eff >= 0.9) break;
+            }
+        }
         if (splits > max_split) splits = max_split;
         if (splits < 1) splits = 1;
     }
@@ -568,9 +677,12 @@ int rbk_gemm(rbk_ctx* ctx, const rbk_gemm_desc* d, void* stream) {
         switch (epi) {
             case RBK_EPI_STORE_F16: return launch<256, RBK_EPI_STORE_F16>(ctx, d, p, st);
             case RBK_EPI_BIAS_GELU: return launch<256, RBK_EPI_BIAS_GELU>(ctx, d, p, st);
-            default: return launch<256, RBK_EPI_GELU_BWD>(ctx, d, p, st);
+            case RBK_EPI_GELU_BWD: return launch<256, RBK_EPI_GELU_BWD>(ctx, d, p, st);
+            case RBK_EPI_ACC_F32: return launch<256, RBK_EPI_ACC_F32>(ctx, d, p, st);
+            default: return launch<256, RBK_EPI_STORE_F32>(ctx, d, p, st);
         }
     }
+    if (BN == 192) return launch<192, RBK_EPI_ACC_F32>(ctx, d, p, st);
     switch (epi) {
         case RBK_EPI_STORE_F16: return launch<128, RBK_EPI_STORE_F16>(ctx, d, p, st);
         case RBK_EPI_BIAS_GELU: return launch<128, RBK_EPI_BIAS_GELU>(ctx, d, p, st);

@@ -245,10 +245,17 @@ static int forward(rbk_model* m, const int* tokens, const int* targets, int B, i
     RBK_TRY(rbk_ln_fwd(m->ctx, m->act.hf, m->act.ln_f_mean, m->act.ln_f_inv_std, m->act.x_out, m->w.ln_f_w,
                        m->w.ln_f_b, N, D, 1e-5f, st));
     RBK_TRY(g.fwd(m->act.logits, m->ldV, m->act.hf, D, m->w.lm_w, N, D, V, m->w.lm_b));
+    m->dlogits_ready = false;
     if (targets) {
-        RBK_TRY(rbk_softmax_xent_bwd(m->ctx, nullptr, m->act.logits, m->ldV, targets, N, V, 0.0f, nullptr,
-                                     m->act.row_loss, st));
+        // Training mode: the same pass that produces the loss writes dlogits over
+        // the logits (without backward's upstream factor, applied later as the
+        // LM-head GEMMs' alpha), saving a second read of [N, V].
+        const float world = m->dp.on ? (float)m->dp.world : 1.0f;
+        const bool fuse = m->fused_ce;
+        RBK_TRY(rbk_softmax_xent_bwd(m->ctx, fuse ? m->act.logits : nullptr, m->act.logits, m->ldV, targets, N, V,
+                                     1.0f / (N * world), fuse ? &m->scaler->scale : nullptr, m->act.row_loss, st));
         RBK_TRY(rbk_sum(m->ctx, loss_dev ? loss_dev : m->loss_dev, m->act.row_loss, N, 1.0f / N, st));
+        m->dlogits_ready = fuse;
     }
     return RBK_OK;
 }
@@ -265,9 +272,16 @@ static int backward(rbk_model* m, const int* tokens, const int* targets, int B, 
     G g{m->ctx, st};
     Activations& a = m->act;
     const float world = m->dp.on ? (float)m->dp.world : 1.0f;
-    // dlogits = (softmax - onehot) * grad_scale / (N * world) * loss_scale, in place
-    RBK_TRY(rbk_softmax_xent_bwd(m->ctx, a.logits, a.logits, m->ldV, targets, N, V, grad_scale / (N * world),
-                                 &m->scaler->scale, nullptr, st));
+    // dlogits = (softmax - onehot) * grad_scale / (N * world) * loss_scale, in place.  When the
+    // forward already wrote it (training mode), grad_scale rides on the LM-head GEMMs' alpha.
+    float head_alpha = 1.0f;
+    if (m->dlogits_ready) {
+        head_alpha = grad_scale;
+        m->dlogits_ready = false;
+    } else {
+        RBK_TRY(rbk_softmax_xent_bwd(m->ctx, a.logits, a.logits, m->ldV, targets, N, V, grad_scale / (N * world),
+                                     &m->scaler->scale, nullptr, st));
+    }
     if (m->inject_pending) {
         inject_inf_kernel<<<grid_for((int64_t)N * V / std::max<int64_t>(m->inject_stride, 1), m->ctx->num_sms), 256,
                             0, st>>>(a.logits, N, V, m->ldV, m->inject_offset, m->inject_stride);
@@ -275,8 +289,11 @@ static int backward(rbk_model* m, const int* tokens, const int* targets, int B, 
         m->inject_pending = false;
     }
     // LM head
-    RBK_TRY(g.dgrad(a.dh, D, a.logits, m->ldV, m->w.lm_w, N, D, V));
-    if (base) RBK_TRY(g.wgrad(m->w.g_lm_w, m->w.g_lm_b, a.logits, m->ldV, a.hf, D, N, D, V));
+    RBK_TRY(g.raw(N, D, V, a.logits, m->ldV, 0, m->w.lm_w, D, 1, a.dh, D, RBK_EPI_STORE_F16, nullptr, nullptr, 0,
+                  nullptr, nullptr, head_alpha));
+    if (base)
+        RBK_TRY(g.raw(V, D, N, a.logits, m->ldV, 1, a.hf, D, 1, m->w.g_lm_w, D, RBK_EPI_ACC_F32, nullptr, nullptr, 0,
+                      nullptr, m->w.g_lm_b, head_alpha));
     // final LN (under LoRA the LN parameters are frozen: their gradients go to a sink)
     float* sk = a.sink;
     half* gcur = a.g0;
@@ -614,6 +631,13 @@ int rbk_model_lora_step(rbk_model* m, int t, float lr, float b1, float b2, float
     a.lr = lr; a.beta1 = b1; a.beta2 = b2; a.eps = eps; a.weight_decay = wd; a.t = t;
     a.scaler = m->scaler;
     return rbk_adam_tail(m->ctx, &a, stream);
+}
+
+int rbk_model_set_training(rbk_model* m, int training) {
+    RBK_REQUIRE(m, "rbk_model_set_training: null model");
+    m->fused_ce = training != 0;
+    m->dlogits_ready = false;
+    return RBK_OK;
 }
 
 int rbk_model_inject_inf(rbk_model* m, int64_t offset, int64_t stride) {

@@ -120,5 +120,7 @@ struct rbk_model {
     std::vector<int64_t> seg_off, seg_len;
     int64_t inject_offset = 0, inject_stride = 0;
     bool inject_pending = false;
+    bool fused_ce = true;           // forward writes dlogits in place (training mode)
+    bool dlogits_ready = false;     // set by a training-mode forward, consumed by backward
     std::vector<void*> allocs;
 };

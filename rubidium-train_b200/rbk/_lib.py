@@ -95,6 +95,7 @@ _SIGS = {
     "rbk_model_lora_buffer": (i32, [vp, i32, C.POINTER(vp), C.POINTER(i64)]),
     "rbk_model_lora_step": (i32, [vp, i32, f32, f32, f32, f32, f32, vp]),
     "rbk_model_inject_inf": (i32, [vp, i64, i64]),
+    "rbk_model_set_training": (i32, [vp, i32]),
     "rbk_dp_unique_id": (i32, [vp]),
     "rbk_dp_plan": (i32, [C.POINTER(Config), i64, C.POINTER(i64), i32, C.POINTER(i32)]),
     "rbk_model_dp_init": (i32, [vp, vp, i32, i32, i64]),

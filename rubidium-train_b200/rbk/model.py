@@ -163,6 +163,11 @@ class RubidiumTransformer:
         call("rbk_model_backward", self.handle, C.c_void_p(tokens.data_ptr()), C.c_void_p(targets.data_ptr()), B, T,
              C.c_float(loss_scale), _s())
 
+    def set_training(self, training: bool = True):
+        """Training mode: forward also writes dlogits (one pass over the logits);
+        eval mode keeps the logits intact."""
+        call("rbk_model_set_training", self.handle, int(bool(training)))
+
     def clip_gradients(self, max_norm: float):
         """Per-tensor clip (src/model.cu:493-523), fused into the next optimizer_step."""
         self._pending_clip = float(max_norm)

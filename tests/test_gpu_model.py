@@ -148,6 +148,27 @@ def test_config1_full_step_matches_oracle(ora):
     m.close()
 
 
+def test_training_and_eval_mode_agree_with_grad_scale(ora):
+    """Training mode (dlogits written by forward, upstream factor as GEMM alpha) and eval mode
+    (dlogits recomputed in backward) give the same gradients; two accumulated backwards with
+    the reference's 1/GA factor equal one plain backward (src/main.cpp:158)."""
+    B, S = 4, 128
+    m, params, tok, tgt = _setup(ora, CFG1, B, S, seed=9)
+    tt = torch.from_numpy(tok).cuda().view(B, S); tg = torch.from_numpy(tgt).cuda().view(B, S)
+    m.forward(tt, tg, B, S); m.backward(tt, tg, B, S, 1.0)
+    g1 = m.grad.clone(); m.grad.zero_()
+    for _ in range(2):                                # GA = 2 in training mode
+        m.forward(tt, tg, B, S); m.backward(tt, tg, B, S, 0.5)
+    g2 = m.grad.clone(); m.grad.zero_()
+    m.set_training(False)
+    for _ in range(2):                                # GA = 2 in eval mode
+        m.forward(tt, tg, B, S); m.backward(tt, tg, B, S, 0.5)
+    g3 = m.grad.clone()
+    assert rel(g2.cpu().numpy(), g1.cpu().numpy()) < 2e-3
+    assert rel(g3.cpu().numpy(), g1.cpu().numpy()) < 2e-3
+    m.close()
+
+
 def test_overflow_injection_skips_step(ora):
     """Inf planted in dlogits: the tail skips, halves the scale, keeps masters, zeroes grads."""
     B, S = 2, 128
