@@ -515,6 +515,11 @@ int bwd(rbk_ctx* ctx, void* dqkv, float* dbias, const void* qkv, const void* o, 
 }
 
 }  // namespace attn
+
+// tcgen05 forward for d_head 64, S % 128 == 0 (attn_tc.cu).
+int attn_fwd_tc(rbk_ctx* ctx, void* o, float* lse, const void* qkv, int B, int S, int H, float scale,
+                cudaStream_t st);
+
 }  // namespace rbk
 
 using namespace rbk;
@@ -530,6 +535,13 @@ int rbk_attn_fwd(rbk_ctx* ctx, void* o, float* lse, const void* qkv, int B, int 
     cudaStream_t st = as_stream(stream);
     // causal: QK^T and PV over S(S+1)/2 score entries per (b, h)
     ProfScope prof(ctx, st, kCatAttnFwd, 4.0 * B * H * ((double)S * (S + 1) / 2.0) * dh);
+    // tcgen05 kernel (attn_tc.cu) for d_head 64 and 128-multiple lengths;
+    // RBK_ATTN_LEGACY=1 forces the mma.sync kernel (A/B comparisons).
+    static const bool legacy = [] {
+        const char* e = getenv("RBK_ATTN_LEGACY");
+        return e && e[0] == '1';
+    }();
+    if (dh == 64 && S % 128 == 0 && !legacy) return attn_fwd_tc(ctx, o, lse, qkv, B, S, H, scale, st);
     return dh == 64 ? attn::fwd<64>(ctx, o, lse, qkv, B, S, H, scale, st)
                     : attn::fwd<128>(ctx, o, lse, qkv, B, S, H, scale, st);
 }
