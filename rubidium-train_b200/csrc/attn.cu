@@ -20,6 +20,11 @@
 #include "common.cuh"
 
 namespace rbk {
+
+// tcgen05 main backward pass for d_head 64, S % 128 == 0 (attn_bwd_tc.cu).
+int attn_bwd_tc(rbk_ctx* ctx, void* dqkv, float* dq_acc, float* dbias, const void* qkv, const void* dout,
+                const float* NL2, const float* Dot, int B, int S, int H, float scale, cudaStream_t st);
+
 namespace attn {
 
 __device__ __forceinline__ uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -217,11 +222,13 @@ __global__ void __launch_bounds__(128) flash_fwd_kernel(half* __restrict__ O, fl
 
 // ------------------------------------------------------------------ backward --
 
-// Dot[bh, s] = sum_d dO[s, d] O[s, d]  and zero the FP32 dQ accumulator.
+// Dot[bh, s] = sum_d dO[s, d] O[s, d]  and zero the FP32 dQ accumulator; with
+// NL2 also NL2[bh, s] = -LSE[bh, s] * log2 e (the tcgen05 main pass reads it).
 // One thread per 16-byte chunk (coalesced); the HD/8 threads of a head reduce
 // by shuffles (they are adjacent lanes of one warp since HD/8 divides 32).
 template <int HD>
-__global__ void flash_bwd_pre_kernel(float* __restrict__ Dot, float* __restrict__ dq_acc, const half* __restrict__ O,
+__global__ void flash_bwd_pre_kernel(float* __restrict__ Dot, float* __restrict__ dq_acc, float* __restrict__ NL2,
+                                     const float* __restrict__ LSE, const half* __restrict__ O,
                                      const half* __restrict__ dO, int BS, int S, int H) {
     constexpr int G = HD / 8;            // chunks per (row, head)
     const int D = H * HD;
@@ -249,7 +256,9 @@ __global__ void flash_bwd_pre_kernel(float* __restrict__ Dot, float* __restrict_
             const long n = i / (D / 8);
             const int h = (int)((i % (D / 8)) / G);
             const long b = n / S, s = n % S;
-            Dot[((size_t)b * H + h) * S + s] = acc;
+            const size_t idx = ((size_t)b * H + h) * S + s;
+            Dot[idx] = acc;
+            if (NL2) NL2[idx] = -LSE[idx] * kLog2e;
         }
     }
 }
@@ -481,31 +490,37 @@ int fwd(rbk_ctx* ctx, void* o, float* lse, const void* qkv, int B, int S, int H,
 
 template <int HD>
 int bwd(rbk_ctx* ctx, void* dqkv, float* dbias, const void* qkv, const void* o, const void* dout, const float* lse,
-        int B, int S, int H, float scale, cudaStream_t st) {
+        int B, int S, int H, float scale, bool tc, cudaStream_t st) {
     const int D = H * HD;
     const size_t BS = (size_t)B * S;
     const size_t dot_bytes = ((sizeof(float) * BS * H) + 255) & ~size_t(255);
     void* ws;
-    RBK_TRY(ctx_scratch(ctx, dot_bytes + sizeof(float) * BS * D, &ws));
+    RBK_TRY(ctx_scratch(ctx, 2 * dot_bytes + sizeof(float) * BS * D, &ws));
     float* Dot = (float*)ws;
-    float* dq_acc = (float*)((char*)ws + dot_bytes);
+    float* NL2 = (float*)((char*)ws + dot_bytes);
+    float* dq_acc = (float*)((char*)ws + 2 * dot_bytes);
     {
         const long work = (long)BS * (D / 8);
         long gsz = (work + 255) / 256;
         if (gsz > ctx->num_sms * 16) gsz = ctx->num_sms * 16;
-        flash_bwd_pre_kernel<HD><<<(int)gsz, 256, 0, st>>>(Dot, dq_acc, (const half*)o, (const half*)dout, (int)BS, S, H);
+        flash_bwd_pre_kernel<HD><<<(int)gsz, 256, 0, st>>>(Dot, dq_acc, tc ? NL2 : nullptr, lse, (const half*)o,
+                                                           (const half*)dout, (int)BS, S, H);
         RBK_LAUNCHED("flash_bwd_pre_kernel");
     }
-    constexpr int SMEM = 6 * BLK * HD * 2 + BLK * BLK * 2 + 4 * BLK * 4;
-    static int set_dev = -1;
-    if (set_dev != ctx->device) {
-        RBK_CUDA(cudaFuncSetAttribute(flash_bwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
-        set_dev = ctx->device;
+    if (tc) {
+        RBK_TRY(attn_bwd_tc(ctx, dqkv, dq_acc, dbias, qkv, dout, NL2, Dot, B, S, H, scale, st));
+    } else {
+        constexpr int SMEM = 6 * BLK * HD * 2 + BLK * BLK * 2 + 4 * BLK * 4;
+        static int set_dev = -1;
+        if (set_dev != ctx->device) {
+            RBK_CUDA(cudaFuncSetAttribute(flash_bwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+            set_dev = ctx->device;
+        }
+        dim3 grid(S / BLK, B * H);
+        flash_bwd_kernel<HD><<<grid, 128, SMEM, st>>>((half*)dqkv, dq_acc, dbias, (const half*)qkv,
+                                                      (const half*)dout, lse, Dot, S, H, scale, scale * kLog2e);
+        RBK_LAUNCHED("flash_bwd_kernel");
     }
-    dim3 grid(S / BLK, B * H);
-    flash_bwd_kernel<HD><<<grid, 128, SMEM, st>>>((half*)dqkv, dq_acc, dbias, (const half*)qkv, (const half*)dout,
-                                                  lse, Dot, S, H, scale, scale * kLog2e);
-    RBK_LAUNCHED("flash_bwd_kernel");
     // enough CTAs to stream the FP32 accumulator at full bandwidth (>= 4 per SM)
     const int rows_per_block = 32;
     dim3 pg((D / 8 + 127) / 128, (int)((BS + rows_per_block - 1) / rows_per_block));
@@ -524,6 +539,15 @@ int attn_fwd_tc(rbk_ctx* ctx, void* o, float* lse, const void* qkv, int B, int S
 
 using namespace rbk;
 
+// RBK_ATTN_LEGACY=1 forces the mma.sync kernels for every shape (A/B comparisons).
+static bool attn_legacy() {
+    static const bool legacy = [] {
+        const char* e = getenv("RBK_ATTN_LEGACY");
+        return e && e[0] == '1';
+    }();
+    return legacy;
+}
+
 extern "C" {
 
 int rbk_attn_fwd(rbk_ctx* ctx, void* o, float* lse, const void* qkv, int B, int S, int H, int dh, float scale,
@@ -535,13 +559,8 @@ int rbk_attn_fwd(rbk_ctx* ctx, void* o, float* lse, const void* qkv, int B, int 
     cudaStream_t st = as_stream(stream);
     // causal: QK^T and PV over S(S+1)/2 score entries per (b, h)
     ProfScope prof(ctx, st, kCatAttnFwd, 4.0 * B * H * ((double)S * (S + 1) / 2.0) * dh);
-    // tcgen05 kernel (attn_tc.cu) for d_head 64 and 128-multiple lengths;
-    // RBK_ATTN_LEGACY=1 forces the mma.sync kernel (A/B comparisons).
-    static const bool legacy = [] {
-        const char* e = getenv("RBK_ATTN_LEGACY");
-        return e && e[0] == '1';
-    }();
-    if (dh == 64 && S % 128 == 0 && !legacy) return attn_fwd_tc(ctx, o, lse, qkv, B, S, H, scale, st);
+    // tcgen05 kernel (attn_tc.cu) for d_head 64 and 128-multiple lengths
+    if (dh == 64 && S % 128 == 0 && !attn_legacy()) return attn_fwd_tc(ctx, o, lse, qkv, B, S, H, scale, st);
     return dh == 64 ? attn::fwd<64>(ctx, o, lse, qkv, B, S, H, scale, st)
                     : attn::fwd<128>(ctx, o, lse, qkv, B, S, H, scale, st);
 }
@@ -555,8 +574,9 @@ int rbk_attn_bwd(rbk_ctx* ctx, void* dqkv, float* dbias_qkv, const void* qkv, co
     cudaStream_t st = as_stream(stream);
     // algorithmic: dV, dP, dQ, dK products over the causal triangle (score recompute excluded)
     ProfScope prof(ctx, st, kCatAttnBwd, 8.0 * B * H * ((double)S * (S + 1) / 2.0) * dh);
-    return dh == 64 ? attn::bwd<64>(ctx, dqkv, dbias_qkv, qkv, o, dout, lse, B, S, H, scale, st)
-                    : attn::bwd<128>(ctx, dqkv, dbias_qkv, qkv, o, dout, lse, B, S, H, scale, st);
+    const bool tc = dh == 64 && S % 128 == 0 && !attn_legacy();
+    return dh == 64 ? attn::bwd<64>(ctx, dqkv, dbias_qkv, qkv, o, dout, lse, B, S, H, scale, tc, st)
+                    : attn::bwd<128>(ctx, dqkv, dbias_qkv, qkv, o, dout, lse, B, S, H, scale, false, st);
 }
 
 }  // extern "C"

@@ -43,6 +43,14 @@ class Context:
             pass
 
 
+def device_error() -> int:
+    """Read and clear the context's device status word (0, or RBK_ERR_TIMEOUT after a bounded wait gave up)."""
+    torch.cuda.synchronize()
+    st = C.c_int(0)
+    call("rbk_ctx_device_error", ctx().handle, C.byref(st))
+    return st.value
+
+
 def ctx() -> Context:
     dev = torch.cuda.current_device()
     cache = getattr(_tls, "ctxs", None)

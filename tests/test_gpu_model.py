@@ -25,7 +25,8 @@ def rel(a, b, floor=0.0):
 
 # ------------------------------------------------------------------ attention --
 
-@pytest.mark.parametrize("B,S,H,dh", [(2, 128, 3, 64), (1, 256, 2, 128), (3, 64, 1, 64)])
+@pytest.mark.parametrize("B,S,H,dh", [(2, 128, 3, 64), (1, 256, 2, 128), (3, 64, 1, 64), (2, 384, 2, 64),
+                                       (1, 512, 3, 64)])
 def test_flash_attention_fwd_bwd(ora, B, S, H, dh):
     from rbk import ops
     rng = np.random.default_rng(S + dh)
@@ -56,6 +57,7 @@ def test_flash_attention_fwd_bwd(ora, B, S, H, dh):
     assert rel(db[:D], g[:, :D].sum(0)) < 5e-3
     assert rel(db[2 * D:], g[:, 2 * D:].sum(0)) < 5e-3
     assert np.abs(db[D:2 * D] - g[:, D:2 * D].sum(0)).max() < 1e-2
+    assert ops.device_error() == 0
 
 
 def test_flash_attention_config_shape(ora):
@@ -71,6 +73,35 @@ def test_flash_attention_config_shape(ora):
     sl = qkv[:S].float().cpu().numpy()
     eo, _ = ora.attn_fwd(sl[:, :D], sl[:, D:2 * D], sl[:, 2 * D:], 1, S, H)
     assert rel(o[:S].float().cpu().numpy(), eo) < 3e-3
+
+
+def test_flash_attention_bwd_config_shape_vs_torch():
+    """Backward at the GPT-2-small head shape (S 1024, 12 heads, d_head 64) against an FP32
+    torch autograd reference of the same causal attention (2 sequences)."""
+    from rbk import ops
+    B, S, H, dh = 2, 1024, 12, 64
+    D = H * dh
+    g = torch.Generator(device="cuda").manual_seed(1)
+    qkv = (torch.randn(B * S, 3 * D, device="cuda", generator=g) * 0.6).half()
+    dout = torch.randn(B * S, D, device="cuda", generator=g).half()
+    o, lse = ops.attn_fwd(qkv, B, S, H, dh)
+    dbias = torch.zeros(3 * D, dtype=torch.float32, device="cuda")
+    dqkv = ops.attn_bwd(qkv, o, dout, lse, B, S, H, dh, dbias=dbias).float()
+    x = qkv.float().requires_grad_(True)
+    q, k, v = (x[:, i * D:(i + 1) * D].view(B, S, H, dh).transpose(1, 2) for i in range(3))
+    sc = (q @ k.transpose(-1, -2)) / math.sqrt(dh)
+    sc = sc.masked_fill(~torch.tril(torch.ones(S, S, dtype=torch.bool, device="cuda")), float("-inf"))
+    ref_o = (torch.softmax(sc, -1) @ v).transpose(1, 2).reshape(B * S, D)
+    ref_o.backward(dout.float())
+    ref = x.grad
+    for i in range(3):
+        sl = slice(i * D, (i + 1) * D)
+        err = float((dqkv[:, sl] - ref[:, sl]).norm() / ref[:, sl].norm())
+        assert err < 5e-3, (i, err)
+    colsum = ref.sum(0)
+    assert float((dbias[:D] - colsum[:D]).norm() / colsum[:D].norm()) < 5e-3
+    assert float((dbias[2 * D:] - colsum[2 * D:]).norm() / colsum[2 * D:].norm()) < 5e-3
+    assert ops.device_error() == 0
 
 
 # ----------------------------------------------------------------- whole model --
