@@ -13,20 +13,24 @@
 //   dV    += P^T_i dO_i       dK    += dS^T_i Q_i     (TMEM accumulators)
 // and for every pair of sub-tiles (128 queries)
 //   dQ     = dS K            (M = 128 queries, K = 128 keys) -> TMA reduce-add
-// into the FP32 accumulator.  P^T and dS^T go to shared memory as FP16 in the
-// 128B-swizzled layout: K-major for the dV / dK products and, read the other
-// way, MN-major for the dQ product, so one copy serves both.
+// into the FP32 accumulator.  P^T goes back to TMEM as FP16 and is the A
+// operand of the dV product straight from there; dS^T goes to shared memory as
+// FP16 in the 128B-swizzled layout: K-major for the dK product and, read the
+// other way, MN-major for the dQ product, so one copy serves both.
 //
-// Roles (448 threads):
-//   warp 0      TMA: K and V once, then Q_i, dO_i and the per-query rows
-//               (-LSE log2 e, Dot) through a 3-stage ring
-//   warp 1      MMA issue (one thread)
-//   warps 2-9   P / dS: warp w owns TMEM lanes 32 (w % 4) .. +31 and query
-//               columns 32 ((w - 2) / 4) .. +31 of each sub-tile
-//   warps 10-13 dQ drain (TMEM -> swizzled FP32 staging -> reduce-add), then
-//               the dK / dV epilogue (FP16 stores, k/v bias column sums)
-// TMEM (512 columns): S^T[2] 0/64, dP^T[2] 128/192, dK 256, dV 320, dQ 384.
-// Every wait is bounded; no cluster multicast.
+// Roles (736 threads):
+//   warp 0       TMA: K and V once, then Q_i, dO_i and the per-query rows
+//                (-LSE log2 e, Dot) through a 5-stage ring
+//   warp 1       MMA issue, producer side: S^T_i and dP^T_i
+//   warp 2       MMA issue, consumer side: dV, dK and dQ.  Two issuing
+//                threads in different warps: a single issuer that also waits
+//                on barriers leaves the tensor pipe idle for each wait.
+//   warps 3-18   P / dS: warp w owns TMEM lanes 32 (w % 4) .. +31 and query
+//                columns 16 ((w - 3) / 4) .. +15 of each sub-tile
+//   warps 19-22  dQ drain (TMEM -> swizzled FP32 staging -> reduce-add), then
+//                the dK / dV epilogue (FP16 stores, k/v bias column sums)
+// TMEM (512 columns): S^T[2] 0/64, dP^T[2] 128/192, dK 256, dV 320, dQ 384,
+// P^T[2] (FP16 pairs) 448/480.  Every wait is bounded; no cluster multicast.
 #include <type_traits>
 
 #include "tc.cuh"
@@ -37,20 +41,23 @@ namespace attn_tc_bwd {
 using namespace tc;
 
 constexpr int BK = 128, BQ = 64, HD = 64;
-constexpr int QS = 3;                       // Q / dO ring depth
-constexpr int kThreads = 14 * 32;
+constexpr int QS = 5;                       // Q / dO ring depth
+constexpr int NE = 16;                      // P / dS warps
+constexpr int WE = 3;                       // first P / dS warp
+constexpr int WD = WE + NE;                 // first drain warp
+constexpr int kThreads = (WD + 4) * 32;
 constexpr int KT_BYTES = BK * HD * 2;       // 16 KB  K or V block
 constexpr int QT_BYTES = BQ * HD * 2;       // 8 KB   Q or dO sub-tile
-constexpr int PT_BYTES = BK * BQ * 2;       // 16 KB  P^T / dS^T sub-tile
+constexpr int PT_BYTES = BK * BQ * 2;       // 16 KB  dS^T sub-tile
 constexpr int DQ_BYTES = 128 * HD * 4;      // 32 KB  FP32 dQ staging (two 128 B-wide swizzled boxes)
 constexpr int ROW_BYTES = 2 * BQ * 4;       // -LSE log2e | Dot of one sub-tile
 constexpr int OFF_K = 0, OFF_V = OFF_K + KT_BYTES, OFF_Q = OFF_V + KT_BYTES, OFF_DO = OFF_Q + QS * QT_BYTES,
-              OFF_P = OFF_DO + QS * QT_BYTES, OFF_DS = OFF_P + 2 * PT_BYTES, OFF_DQ = OFF_DS + 4 * PT_BYTES,
-              OFF_ROW = OFF_DQ + DQ_BYTES, OFF_BAR = OFF_ROW + QS * ROW_BYTES;
-constexpr int NBARS = 1 + 2 * QS + 2 + 2 + 2 + 2 + 2 + 1;
+              OFF_DS = OFF_DO + QS * QT_BYTES, OFF_DQ = OFF_DS + 4 * PT_BYTES, OFF_ROW = OFF_DQ + DQ_BYTES,
+              OFF_BAR = OFF_ROW + QS * ROW_BYTES;
+constexpr int NBARS = 1 + 2 * QS + 2 + 2 + 2 + 2 + 2 + 1 + 2;
 constexpr int SMEM = 1024 + OFF_BAR + NBARS * 8 + 16;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t S_COL = 0, DP_COL = 128, DK_COL = 256, DV_COL = 320, DQ_COL = 384;
+constexpr uint32_t S_COL = 0, DP_COL = 128, DK_COL = 256, DV_COL = 320, DQ_COL = 384, P_COL = 448;
 static_assert(SMEM <= 232448, "shared memory budget");
 
 __device__ __forceinline__ float ex2(float x) {
@@ -94,7 +101,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto sQ = [&](int s) { return base + OFF_Q + (uint32_t)s * QT_BYTES; };
     auto sdO = [&](int s) { return base + OFF_DO + (uint32_t)s * QT_BYTES; };
     auto sRow = [&](int s) { return base + OFF_ROW + (uint32_t)s * ROW_BYTES; };
-    auto sP = [&](int s) { return base + OFF_P + (uint32_t)s * PT_BYTES; };
     auto sdS = [&](int s) { return base + OFF_DS + (uint32_t)s * PT_BYTES; };
     const uint32_t bars = base + OFF_BAR;
     const uint32_t kv_full = bars;
@@ -102,10 +108,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto q_empty = [&](int s) { return bars + 8 + 8 * QS + 8 * s; };
     const uint32_t b2 = bars + 8 + 16 * QS;
     auto s_full = [&](int s) { return b2 + 8 * s; };        // S^T_i, dP^T_i in TMEM buffer i & 1
-    auto p_full = [&](int s) { return b2 + 16 + 8 * s; };   // P^T_i, dS^T_i in shared memory (8 warps)
+    auto p_full = [&](int s) { return b2 + 16 + 8 * s; };   // P^T_i in TMEM, dS^T_i in shared memory (NE warps)
     auto p_free = [&](int s) { return b2 + 32 + 8 * s; };   // dV_i, dK_i done: P^T buffer i & 1 reusable
     auto ds_free = [&](int s) { return b2 + 48 + 8 * s; };  // dQ of a pair done: its two dS^T buffers reusable
     const uint32_t dq_full = b2 + 64, dq_free = b2 + 72, acc_done = b2 + 80;
+    auto s_free = [&](int s) { return b2 + 88 + 8 * s; };   // S^T_i, dP^T_i read out of TMEM buffer i & 1
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + OFF_BAR + NBARS * 8);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + OFF_BAR + NBARS * 8 + 8);
 
@@ -119,12 +126,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) {
         mbar_init(kv_full, 1);
-        for (int s = 0; s < QS; ++s) { mbar_init(q_full(s), 1); mbar_init(q_empty(s), 9); }
+        for (int s = 0; s < QS; ++s) { mbar_init(q_full(s), 1); mbar_init(q_empty(s), NE + 2); }
         for (int s = 0; s < 2; ++s) {
             mbar_init(s_full(s), 1);
-            mbar_init(p_full(s), 8);
+            mbar_init(p_full(s), NE);
             mbar_init(p_free(s), 1);
             mbar_init(ds_free(s), 1);
+            mbar_init(s_free(s), NE);
         }
         mbar_init(dq_full, 1);
         mbar_init(dq_free, 4);
@@ -164,14 +172,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else if (warp == 1) {
-        // ---------------------------------------------------------- MMA ----
+        // ------------------------------------------- MMA: S^T, dP^T producer ----
         if (lane == 0) {
             const uint32_t id_s = idesc_f16(BQ, 0, 0);    // K (K-major) x Q^T (K-major): N = 64 queries
-            const uint32_t id_kv = idesc_f16(HD, 0, 1);   // P^T / dS^T (K-major) x dO / Q (MN-major): N = 64
-            const uint32_t id_q = idesc_f16(HD, 1, 1);    // dS (MN-major) x K (MN-major): N = 64
-            auto issue_sdp = [&](int j) -> bool {
+            bool ok = mbar_wait(kv_full, 0, abort_flag);
+            for (int j = 0; ok && j < n; ++j) {
                 const int s = j % QS;
-                if (!mbar_wait(q_full(s), (j / QS) & 1, abort_flag)) return false;
+                ok = mbar_wait(q_full(s), (j / QS) & 1, abort_flag) &&
+                     (j < 2 || mbar_wait(s_free(j & 1), ((j >> 1) & 1) ^ 1, abort_flag));
+                if (!ok) break;
                 fence_after();
                 const uint32_t bcol = (uint32_t)(j & 1) * BQ;
 #pragma unroll
@@ -183,19 +192,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mma_f16(tmem + DP_COL + bcol, sdesc(sV + k * 32, 16, 1024), sdesc(sdO(s) + k * 32, 16, 1024),
                             id_s, k > 0);
                 mma_commit(s_full(j & 1));
-                return true;
-            };
-            bool ok = mbar_wait(kv_full, 0, abort_flag) && issue_sdp(0) && issue_sdp(1);
+                mma_commit(q_empty(s));
+            }
+        }
+    } else if (warp == 2) {
+        // ------------------------------------------- MMA: dV, dK, dQ consumer ----
+        if (lane == 0) {
+            const uint32_t id_kv = idesc_f16(HD, 0, 1);   // P^T (TMEM) / dS^T (K-major) x dO / Q (MN-major): N = 64
+            const uint32_t id_q = idesc_f16(HD, 1, 1);    // dS (MN-major) x K (MN-major): N = 64
+            bool ok = mbar_wait(kv_full, 0, abort_flag);  // K is an operand of dQ
             for (int i = 0; ok && i < n; ++i) {
                 const int s = i % QS, pb = i & 1;
                 if (!mbar_wait(p_full(pb), (i >> 1) & 1, abort_flag)) { ok = false; break; }
                 fence_after();
-                // S / dP buffer pb was read out before p_full: the next-but-one sub-tile may overwrite it
-                if (i + 2 < n && !issue_sdp(i + 2)) { ok = false; break; }
 #pragma unroll
                 for (int k = 0; k < BQ / 16; ++k)
-                    mma_f16(tmem + DV_COL, sdesc(sP(pb) + k * 32, 16, 1024), sdesc(sdO(s) + k * 2048, 8192, 1024),
-                            id_kv, (i > 0 || k > 0) ? 1u : 0u);
+                    mma_f16_ts(tmem + DV_COL, tmem + P_COL + (uint32_t)(pb * 32 + k * 8),
+                               sdesc(sdO(s) + k * 2048, 8192, 1024), id_kv, (i > 0 || k > 0) ? 1u : 0u);
 #pragma unroll
                 for (int k = 0; k < BQ / 16; ++k)
                     mma_f16(tmem + DK_COL, sdesc(sdS(i & 3) + k * 32, 16, 1024), sdesc(sQ(s) + k * 2048, 8192, 1024),
@@ -217,28 +230,31 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (ok) mma_commit(acc_done);
         }
-    } else if (warp < 10) {
+    } else if (warp < WD) {
         // ------------------------------------------------------ P / dS ----
-        const int lg = warp & 3, half_ = (warp - 2) >> 2;
+        const int lg = warp & 3, quarter = (warp - WE) >> 2;
         const int r = lg * 32 + lane;                         // key row inside the block
         const uint32_t lane_off = (uint32_t)(lg * 32) << 16;
-        const int c0 = half_ * 32;                            // first query column of this warp
+        const int c0 = quarter * 16;                          // first query column of this warp
         for (int i = 0; i < n; ++i) {
             const int s = i % QS, pb = i & 1;
             bool ok = mbar_wait(s_full(pb), (i >> 1) & 1, abort_flag) && mbar_wait(q_full(s), (i / QS) & 1, abort_flag);
             if (!__all_sync(0xffffffffu, ok)) break;
             fence_after();
-            uint32_t sr[32], dr[32];
-            tmem_ld32(tmem + lane_off + S_COL + (uint32_t)pb * BQ + c0, sr);
-            tmem_ld32(tmem + lane_off + DP_COL + (uint32_t)pb * BQ + c0, dr);
+            uint32_t sr[16], dr[16];
+            tmem_ld16(tmem + lane_off + S_COL + (uint32_t)pb * BQ + c0, sr);
+            tmem_ld16(tmem + lane_off + DP_COL + (uint32_t)pb * BQ + c0, dr);
             tmem_wait_ld();
+            fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(s_free(pb));          // the producer may overwrite this buffer
             const uint32_t rowp = sRow(s);
-            uint32_t pk[16], dk[16];
+            uint32_t pk[8], dk[8];
             // masked: the two sub-tiles that overlap the diagonal; columns e < lim lie above it
             auto compute = [&](auto masked) {
                 const int lim = r - BQ * i - c0;
 #pragma unroll
-                for (int q4 = 0; q4 < 8; ++q4) {
+                for (int q4 = 0; q4 < 4; ++q4) {
                     const float4 nl = ld_shared_f4(rowp + (uint32_t)(c0 + 4 * q4) * 4);
                     const float4 dt = ld_shared_f4(rowp + BQ * 4 + (uint32_t)(c0 + 4 * q4) * 4);
                     const float nlv[4] = {nl.x, nl.y, nl.z, nl.w}, dtv[4] = {dt.x, dt.y, dt.z, dt.w};
@@ -264,13 +280,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (i >= 2) ok = mbar_wait(p_free(pb), ((i >> 1) & 1) ^ 1, abort_flag);
             if (ok && i >= 4 && !(i & 1)) ok = mbar_wait(ds_free((i >> 1) & 1), ((i >> 2) & 1) ^ 1, abort_flag);
             if (!__all_sync(0xffffffffu, ok)) break;
-            const uint32_t prow = sP(pb) + (uint32_t)r * 128u, drow = sdS(i & 3) + (uint32_t)r * 128u;
+            fence_after();
+            tmem_st8(tmem + lane_off + P_COL + (uint32_t)(pb * 32 + quarter * 8), pk);
+            const uint32_t drow = sdS(i & 3) + (uint32_t)r * 128u;
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {                     // 16-byte chunk = 8 queries, 128B swizzle
+            for (int c = 0; c < 2; ++c) {                     // 16-byte chunk = 8 queries, 128B swizzle
                 const uint32_t sw = (uint32_t)((((c0 >> 3) + c) ^ (r & 7)) << 4);
-                st_shared_v4(prow + sw, pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
                 st_shared_v4(drow + sw, dk[4 * c], dk[4 * c + 1], dk[4 * c + 2], dk[4 * c + 3]);
             }
+            tmem_wait_st();
             fence_proxy_async();
             fence_before();
             __syncwarp();
@@ -284,29 +302,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int lg = warp & 3;
         const int r = lg * 32 + lane;                         // query row of the pair / key row at the end
         const uint32_t lane_off = (uint32_t)(lg * 32) << 16;
-        const bool elected = warp == 10 && lane == 0;
+        const bool elected = warp == WD && lane == 0;
+        const int tid = (int)threadIdx.x - WD * 32;           // 0..127
         bool ok = true;
         for (int p = 0; p < n / 2; ++p) {
             ok = __all_sync(0xffffffffu, ok && mbar_wait(dq_full, p & 1, abort_flag));
-            uint32_t a[64];
-            if (ok) {
-                fence_after();
-                tmem_ld32(tmem + lane_off + DQ_COL, a);
-                tmem_ld32(tmem + lane_off + DQ_COL + 32, a + 32);
-                tmem_wait_ld();
-                fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(dq_free);
-            }
+            if (ok) fence_after();
             if (elected) bulk_wait_read0();                   // staging free again
             named_sync(1, 128);
-            if (ok) {
+#pragma unroll 1
+            for (int hc = 0; hc < 2; ++hc) {                  // 32 columns at a time
+                uint32_t a[32];
+                if (ok) {
+                    tmem_ld32(tmem + lane_off + DQ_COL + hc * 32, a);
+                    tmem_wait_ld();
+                    if (hc == 1) {
+                        fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(dq_free);
+                    }
 #pragma unroll
-                for (int c = 0; c < 16; ++c)
-                    st_shared_v4(stage_addr(sDQ, r, c), __float_as_uint(__uint_as_float(a[4 * c]) * scale),
-                                 __float_as_uint(__uint_as_float(a[4 * c + 1]) * scale),
-                                 __float_as_uint(__uint_as_float(a[4 * c + 2]) * scale),
-                                 __float_as_uint(__uint_as_float(a[4 * c + 3]) * scale));
+                    for (int c = 0; c < 8; ++c)
+                        st_shared_v4(stage_addr(sDQ, r, hc * 8 + c), __float_as_uint(__uint_as_float(a[4 * c]) * scale),
+                                     __float_as_uint(__uint_as_float(a[4 * c + 1]) * scale),
+                                     __float_as_uint(__uint_as_float(a[4 * c + 2]) * scale),
+                                     __float_as_uint(__uint_as_float(a[4 * c + 3]) * scale));
+                }
             }
             fence_proxy_async();
             named_sync(1, 128);
@@ -317,35 +338,39 @@ __global__ void __launch_bounds__(kThreads, 1)
                 bulk_commit();
             }
         }
-        if (elected) bulk_wait0();                            // last reduce has read the staging
+        if (elected) bulk_wait_read0();                       // last reduce has read the staging
         named_sync(1, 128);
         ok = __all_sync(0xffffffffu, ok && mbar_wait(acc_done, 0, abort_flag));
-        // dK (scaled) then dV: FP16 rows to dqkv, FP32 rows to staging for the bias column sums
+        if (ok) fence_after();
+        // dK (scaled) then dV, 32 columns at a time: FP16 rows to dqkv, FP32 to staging for the bias sums
+#pragma unroll 1
         for (int t = 0; t < 2; ++t) {
-            uint32_t a[64];
-            if (ok) {
-                fence_after();
-                tmem_ld32(tmem + lane_off + (t ? DV_COL : DK_COL), a);
-                tmem_ld32(tmem + lane_off + (t ? DV_COL : DK_COL) + 32, a + 32);
-                tmem_wait_ld();
-                const float f = t ? 1.0f : scale;
-                float v[64];
+#pragma unroll 1
+            for (int hc = 0; hc < 2; ++hc) {
+                if (ok) {
+                    uint32_t a[32];
+                    tmem_ld32(tmem + lane_off + (t ? DV_COL : DK_COL) + hc * 32, a);
+                    tmem_wait_ld();
+                    const float f = t ? 1.0f : scale;
+                    float v[32];
 #pragma unroll
-                for (int e = 0; e < 64; ++e) v[e] = __uint_as_float(a[e]) * f;
-                half* row = dqkv + (size_t)(krow0 + r) * (3 * D) + (t + 1) * D + h * HD;
+                    for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(a[e]) * f;
+                    half* row = dqkv + (size_t)(krow0 + r) * (3 * D) + (t + 1) * D + h * HD + hc * 32;
 #pragma unroll
-                for (int g = 0; g < 8; ++g) reinterpret_cast<uint4*>(row)[g] = f_to_h8(v + 8 * g);
-                if (dbias) {
+                    for (int g = 0; g < 4; ++g) reinterpret_cast<uint4*>(row)[g] = f_to_h8(v + 8 * g);
+                    if (dbias) {
 #pragma unroll
-                    for (int c = 0; c < 16; ++c)
-                        st_shared_v4(stage_addr(sDQ, r, c), __float_as_uint(v[4 * c]), __float_as_uint(v[4 * c + 1]),
-                                     __float_as_uint(v[4 * c + 2]), __float_as_uint(v[4 * c + 3]));
+                        for (int c = 0; c < 8; ++c)
+                            st_shared_v4(stage_addr(sDQ, r, hc * 8 + c), __float_as_uint(v[4 * c]),
+                                         __float_as_uint(v[4 * c + 1]), __float_as_uint(v[4 * c + 2]),
+                                         __float_as_uint(v[4 * c + 3]));
+                    }
                 }
             }
             if (dbias) {
                 named_sync(1, 128);
                 if (ok) {
-                    const int tid = threadIdx.x - 320, col = tid & 63, rh = tid >> 6;
+                    const int col = tid & 63, rh = tid >> 6;
                     float acc = 0.0f;
 #pragma unroll 8
                     for (int rr = rh * 64; rr < rh * 64 + 64; ++rr)
@@ -355,6 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 named_sync(1, 128);
             }
         }
+        if (elected) bulk_wait0();
     }
     fence_before();
     __syncthreads();
