@@ -22,8 +22,8 @@
 namespace rbk {
 
 // tcgen05 main backward pass for d_head 64, S % 128 == 0 (attn_bwd_tc.cu).
-int attn_bwd_tc(rbk_ctx* ctx, void* dqkv, float* dq_acc, float* dbias, const void* qkv, const void* dout,
-                const float* NL2, const float* Dot, int B, int S, int H, float scale, cudaStream_t st);
+int attn_bwd_tc(rbk_ctx* ctx, void* dqkv, float* dq_acc, const void* qkv, const void* dout, const float* NL2,
+                const float* Dot, int B, int S, int H, float scale, cudaStream_t st);
 
 namespace attn {
 
@@ -453,13 +453,17 @@ __global__ void __launch_bounds__(128) flash_bwd_kernel(half* __restrict__ dqkv,
     }
 }
 
-// dqkv[:, q block] = half(dq_acc); dbias[q block] += column sums.
+// dqkv[:, q block] = half(dq_acc); dbias[q block] += column sums.  With dO
+// (the tcgen05 path, whose main pass writes no bias terms) also
+// dbias[v block] += column sums of dO: sum_keys dV = sum_queries dO because
+// every row of P sums to 1 (the k block stays untouched: its gradient is 0).
 __global__ void flash_bwd_post_kernel(half* __restrict__ dqkv, float* __restrict__ dbias,
-                                      const float* __restrict__ dq_acc, int BS, int D, int rows_per_block) {
+                                      const float* __restrict__ dq_acc, const half* __restrict__ dO, int BS, int D,
+                                      int rows_per_block) {
     const int c8 = blockIdx.x * blockDim.x + threadIdx.x;   // 8-column group
     if (c8 * 8 >= D) return;
     const int r0 = blockIdx.y * rows_per_block, r1 = min(BS, r0 + rows_per_block);
-    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0}, accv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int r = r0; r < r1; ++r) {
         const float4* src = reinterpret_cast<const float4*>(dq_acc + (size_t)r * D + c8 * 8);
         const float4 u = src[0], v = src[1];
@@ -467,10 +471,20 @@ __global__ void flash_bwd_post_kernel(half* __restrict__ dqkv, float* __restrict
 #pragma unroll
         for (int k = 0; k < 8; ++k) acc[k] += x[k];
         *reinterpret_cast<uint4*>(dqkv + (size_t)r * 3 * D + c8 * 8) = f_to_h8(x);
+        if (dO && dbias) {
+            float y[8];
+            h8_to_f(__ldg(reinterpret_cast<const uint4*>(dO + (size_t)r * D + c8 * 8)), y);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) accv[k] += y[k];
+        }
     }
     if (dbias) {
 #pragma unroll
         for (int k = 0; k < 8; ++k) atomicAdd(dbias + c8 * 8 + k, acc[k]);
+        if (dO) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) atomicAdd(dbias + 2 * D + c8 * 8 + k, accv[k]);
+        }
     }
 }
 
@@ -508,7 +522,7 @@ int bwd(rbk_ctx* ctx, void* dqkv, float* dbias, const void* qkv, const void* o, 
         RBK_LAUNCHED("flash_bwd_pre_kernel");
     }
     if (tc) {
-        RBK_TRY(attn_bwd_tc(ctx, dqkv, dq_acc, dbias, qkv, dout, NL2, Dot, B, S, H, scale, st));
+        RBK_TRY(attn_bwd_tc(ctx, dqkv, dq_acc, qkv, dout, NL2, Dot, B, S, H, scale, st));
     } else {
         constexpr int SMEM = 6 * BLK * HD * 2 + BLK * BLK * 2 + 4 * BLK * 4;
         static int set_dev = -1;
@@ -524,7 +538,8 @@ int bwd(rbk_ctx* ctx, void* dqkv, float* dbias, const void* qkv, const void* o, 
     // enough CTAs to stream the FP32 accumulator at full bandwidth (>= 4 per SM)
     const int rows_per_block = 32;
     dim3 pg((D / 8 + 127) / 128, (int)((BS + rows_per_block - 1) / rows_per_block));
-    flash_bwd_post_kernel<<<pg, 128, 0, st>>>((half*)dqkv, dbias, dq_acc, (int)BS, D, rows_per_block);
+    flash_bwd_post_kernel<<<pg, 128, 0, st>>>((half*)dqkv, dbias, dq_acc, tc ? (const half*)dout : nullptr, (int)BS,
+                                              D, rows_per_block);
     RBK_LAUNCHED("flash_bwd_post_kernel");
     return RBK_OK;
 }

@@ -2,11 +2,11 @@
 // tensor cores (d_head 64, sequence length a multiple of 128): the tcgen05
 // replacement of the mma.sync main kernel in attn.cu.  The pre pass (Dot =
 // rowsum(dO * O), -LSE * log2 e, zeroed FP32 dQ accumulator) and the post pass
-// (dQ -> FP16, q-bias column sums) are shared with the mma.sync path.
+// (dQ -> FP16, q- and v-bias column sums) are shared with the mma.sync path.
 //
-// One CTA = one (batch, head, 128-key block); it walks the 64-query sub-tiles
-// from the diagonal to the end of the sequence.  Per sub-tile i (TMEM lane =
-// key, column = query):
+// Work item = one (batch, head, 128-key block): it walks the 64-query
+// sub-tiles from the diagonal to the end of the sequence.  Per sub-tile i
+// (TMEM lane = key, column = query):
 //   S^T_i  = K Q_i^T          dP^T_i = V dO_i^T       (N = 64, double-buffered)
 //   P^T_i  = exp2(S^T * scale * log2 e - LSE * log2 e)     (0 above the diagonal)
 //   dS^T_i = P^T_i * (dP^T_i - Dot)
@@ -16,10 +16,19 @@
 // into the FP32 accumulator.  P^T goes back to TMEM as FP16 and is the A
 // operand of the dV product straight from there; dS^T goes to shared memory as
 // FP16 in the 128B-swizzled layout: K-major for the dK product and, read the
-// other way, MN-major for the dQ product, so one copy serves both.
+// other way, MN-major for the dQ product, so one copy serves both.  Once dQ of
+// a pair is in TMEM, the pair's two dS^T tiles are the FP32 staging buffer of
+// its reduce-add.
+//
+// The kernel is persistent: one CTA per SM takes work items round-robin from
+// a longest-first order; K and V are double-buffered so the next item's tiles
+// load while the current one finishes, and the dK / dV epilogue of one item
+// overlaps the start of the next: the accumulators are read out of TMEM as
+// FP16 into the item's own K / V tiles (no longer needed once its last MMA is
+// done) and leave by TMA store.
 //
 // Roles (736 threads):
-//   warp 0       TMA: K and V once, then Q_i, dO_i and the per-query rows
+//   warp 0       TMA: K and V per item, then Q_i, dO_i and the per-query rows
 //                (-LSE log2 e, Dot) through a 5-stage ring
 //   warp 1       MMA issue, producer side: S^T_i and dP^T_i
 //   warp 2       MMA issue, consumer side: dV, dK and dQ.  Two issuing
@@ -28,11 +37,15 @@
 //   warps 3-18   P / dS: warp w owns TMEM lanes 32 (w % 4) .. +31 and query
 //                columns 16 ((w - 3) / 4) .. +15 of each sub-tile
 //   warps 19-22  dQ drain (TMEM -> swizzled FP32 staging -> reduce-add), then
-//                the dK / dV epilogue (FP16 stores, k/v bias column sums)
+//                the dK / dV epilogue of each item (TMEM -> K / V tiles -> TMA
+//                store)
 // TMEM (512 columns): S^T[2] 0/64, dP^T[2] 128/192, dK 256, dV 320, dQ 384,
 // P^T[2] (FP16 pairs) 448/480.  Every wait is bounded; no cluster multicast.
-#include <type_traits>
-
+//
+// Bias gradients: the key bias has an exactly zero gradient (it shifts every
+// score of a query row by the same amount, and sum_j dS_ij = Dot_i - Dot_i = 0),
+// and the value bias gradient is sum_j dV_j = sum_i dO_i (rows of P sum to 1);
+// the post pass adds the latter from dO, so this kernel writes no bias terms.
 #include "tc.cuh"
 
 namespace rbk {
@@ -49,12 +62,10 @@ constexpr int kThreads = (WD + 4) * 32;
 constexpr int KT_BYTES = BK * HD * 2;       // 16 KB  K or V block
 constexpr int QT_BYTES = BQ * HD * 2;       // 8 KB   Q or dO sub-tile
 constexpr int PT_BYTES = BK * BQ * 2;       // 16 KB  dS^T sub-tile
-constexpr int DQ_BYTES = 128 * HD * 4;      // 32 KB  FP32 dQ staging (two 128 B-wide swizzled boxes)
 constexpr int ROW_BYTES = 2 * BQ * 4;       // -LSE log2e | Dot of one sub-tile
-constexpr int OFF_K = 0, OFF_V = OFF_K + KT_BYTES, OFF_Q = OFF_V + KT_BYTES, OFF_DO = OFF_Q + QS * QT_BYTES,
-              OFF_DS = OFF_DO + QS * QT_BYTES, OFF_DQ = OFF_DS + 4 * PT_BYTES, OFF_ROW = OFF_DQ + DQ_BYTES,
-              OFF_BAR = OFF_ROW + QS * ROW_BYTES;
-constexpr int NBARS = 1 + 2 * QS + 2 + 2 + 2 + 2 + 2 + 1 + 2;
+constexpr int OFF_K = 0, OFF_V = OFF_K + 2 * KT_BYTES, OFF_Q = OFF_V + 2 * KT_BYTES, OFF_DO = OFF_Q + QS * QT_BYTES,
+              OFF_DS = OFF_DO + QS * QT_BYTES, OFF_ROW = OFF_DS + 4 * PT_BYTES, OFF_BAR = OFF_ROW + QS * ROW_BYTES;
+constexpr int NBARS = 2 * QS + 2 * 6 + 4 + 2 * 2;
 constexpr int SMEM = 1024 + OFF_BAR + NBARS * 8 + 16;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t S_COL = 0, DP_COL = 128, DK_COL = 256, DV_COL = 320, DQ_COL = 384, P_COL = 448;
@@ -77,66 +88,87 @@ __device__ __forceinline__ float4 ld_shared_f4(uint32_t addr) {
     asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
     return v;
 }
-__device__ __forceinline__ float ld_shared_f(uint32_t addr) {
-    float v;
-    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
-    return v;
-}
 
 // FP32 [128 rows][64 cols] staging as two 128B-swizzled boxes of 32 columns.
 __device__ __forceinline__ uint32_t stage_addr(uint32_t s, int row, int chunk /* 16 B = 4 floats, 0..15 */) {
     return s + (uint32_t)(chunk >> 3) * 16384u + (uint32_t)row * 128u + (uint32_t)(((chunk & 7) ^ (row & 7)) << 4);
 }
 
+// Work item u (longest first: all diagonal-0 key blocks, then 1, ...).
+struct Item {
+    int kb, bh, h, n, krow0;
+};
+__device__ __forceinline__ Item item_of(int u, int BH, int H, int S) {
+    Item it;
+    it.kb = u / BH;
+    it.bh = u % BH;
+    it.h = it.bh % H;
+    it.n = 2 * (S / BK - it.kb);
+    it.krow0 = (it.bh / H) * S + it.kb * BK;
+    return it;
+}
+
+struct Masked {
+    static constexpr bool value = true;
+};
+struct Plain {
+    static constexpr bool value = false;
+};
+
 __global__ void __launch_bounds__(kThreads, 1)
     flash_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmkv,
                         const __grid_constant__ CUtensorMap tmdo, const __grid_constant__ CUtensorMap tmdq,
-                        half* __restrict__ dqkv, float* __restrict__ dbias, const float* __restrict__ NL2,
-                        const float* __restrict__ Dot, int S, int H, float scale, float scale_log2, int* err) {
+                        const __grid_constant__ CUtensorMap tmout, const float* __restrict__ NL2,
+                        const float* __restrict__ Dot, int S, int H, int num_items, float scale, float scale_log2,
+                        int* err) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = su32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t* gbase = smem_raw + (base - raw);
-    const uint32_t sK = base + OFF_K, sV = base + OFF_V, sDQ = base + OFF_DQ;
+    auto sK = [&](int s) { return base + OFF_K + (uint32_t)s * KT_BYTES; };
+    auto sV = [&](int s) { return base + OFF_V + (uint32_t)s * KT_BYTES; };
     auto sQ = [&](int s) { return base + OFF_Q + (uint32_t)s * QT_BYTES; };
     auto sdO = [&](int s) { return base + OFF_DO + (uint32_t)s * QT_BYTES; };
     auto sRow = [&](int s) { return base + OFF_ROW + (uint32_t)s * ROW_BYTES; };
     auto sdS = [&](int s) { return base + OFF_DS + (uint32_t)s * PT_BYTES; };
+    // barriers
     const uint32_t bars = base + OFF_BAR;
-    const uint32_t kv_full = bars;
-    auto q_full = [&](int s) { return bars + 8 + 8 * s; };
-    auto q_empty = [&](int s) { return bars + 8 + 8 * QS + 8 * s; };
-    const uint32_t b2 = bars + 8 + 16 * QS;
-    auto s_full = [&](int s) { return b2 + 8 * s; };        // S^T_i, dP^T_i in TMEM buffer i & 1
-    auto p_full = [&](int s) { return b2 + 16 + 8 * s; };   // P^T_i in TMEM, dS^T_i in shared memory (NE warps)
-    auto p_free = [&](int s) { return b2 + 32 + 8 * s; };   // dV_i, dK_i done: P^T buffer i & 1 reusable
-    auto ds_free = [&](int s) { return b2 + 48 + 8 * s; };  // dQ of a pair done: its two dS^T buffers reusable
-    const uint32_t dq_full = b2 + 64, dq_free = b2 + 72, acc_done = b2 + 80;
-    auto s_free = [&](int s) { return b2 + 88 + 8 * s; };   // S^T_i, dP^T_i read out of TMEM buffer i & 1
+    auto q_full = [&](int s) { return bars + 8 * s; };
+    auto q_empty = [&](int s) { return bars + 8 * QS + 8 * s; };
+    const uint32_t b2 = bars + 16 * QS;
+    auto kv_full = [&](int s) { return b2 + 8 * s; };       // K, V of an item in buffer s
+    auto kv_empty = [&](int s) { return b2 + 16 + 8 * s; }; // K / V buffer s free: producer done, dK / dV stored
+    auto s_full = [&](int s) { return b2 + 32 + 8 * s; };   // S^T_i, dP^T_i in TMEM buffer i & 1
+    auto s_free = [&](int s) { return b2 + 48 + 8 * s; };   // S^T_i, dP^T_i read out of TMEM buffer i & 1
+    auto p_full = [&](int s) { return b2 + 64 + 8 * s; };   // P^T_i in TMEM, dS^T_i in shared memory
+    auto p_free = [&](int s) { return b2 + 80 + 8 * s; };   // dV_i, dK_i done: P^T buffer i & 1 reusable
+    const uint32_t dq_full = b2 + 96, dq_free = b2 + 104, acc_done = b2 + 112, acc_free = b2 + 120;
+    auto ds_free = [&](int s) { return b2 + 128 + 8 * s; }; // pair's dS^T tiles (and staging) reusable
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + OFF_BAR + NBARS * 8);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + OFF_BAR + NBARS * 8 + 8);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nkb = S / BK;
-    const int kb = (int)blockIdx.y;                  // y-major launch order: long (low) key blocks first
-    const int bh = (int)blockIdx.x, b = bh / H, h = bh % H;
+    const int BH = num_items / (S / BK);
     const int D = H * HD;
-    const int krow0 = b * S + kb * BK;               // first key row (= first query row of the walk)
-    const int n = 2 * (nkb - kb);                    // 64-query sub-tiles from the diagonal on
 
     if (threadIdx.x == 0) {
-        mbar_init(kv_full, 1);
-        for (int s = 0; s < QS; ++s) { mbar_init(q_full(s), 1); mbar_init(q_empty(s), NE + 2); }
+        for (int s = 0; s < QS; ++s) {
+            mbar_init(q_full(s), 1);
+            mbar_init(q_empty(s), NE + 2);
+        }
         for (int s = 0; s < 2; ++s) {
+            mbar_init(kv_full(s), 1);
+            mbar_init(kv_empty(s), 2);
             mbar_init(s_full(s), 1);
+            mbar_init(s_free(s), NE);
             mbar_init(p_full(s), NE);
             mbar_init(p_free(s), 1);
             mbar_init(ds_free(s), 1);
-            mbar_init(s_free(s), NE);
         }
         mbar_init(dq_full, 1);
         mbar_init(dq_free, 4);
         mbar_init(acc_done, 1);
+        mbar_init(acc_free, 4);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -145,6 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("prefetch.tensormap [%0];" ::"l"(&tmkv) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(&tmdo) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(&tmdq) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmout) : "memory");
     }
     if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
     fence_before();
@@ -155,44 +188,61 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0) {
         // ---------------------------------------------------------- TMA ----
         if (lane == 0) {
-            mbar_expect_tx(kv_full, 2 * KT_BYTES);
-            tma_load_2d(sK, &tmkv, kv_full, D + h * HD, krow0);
-            tma_load_2d(sV, &tmkv, kv_full, 2 * D + h * HD, krow0);
-            const float* nl2 = NL2 + (size_t)bh * S + kb * BK;
-            const float* dot = Dot + (size_t)bh * S + kb * BK;
-            for (int i = 0; i < n; ++i) {
-                const int s = i % QS;
-                if (!mbar_wait(q_empty(s), ((i / QS) & 1) ^ 1, abort_flag)) break;
-                const uint32_t fb = q_full(s);
-                mbar_expect_tx(fb, 2 * QT_BYTES + ROW_BYTES);
-                tma_load_2d(sQ(s), &tmq, fb, h * HD, krow0 + i * BQ);
-                tma_load_2d(sdO(s), &tmdo, fb, h * HD, krow0 + i * BQ);
-                bulk_load(sRow(s), nl2 + i * BQ, BQ * 4, fb);
-                bulk_load(sRow(s) + BQ * 4, dot + i * BQ, BQ * 4, fb);
+            int g = 0;                                       // sub-tile counter of this CTA
+            bool ok = true;
+            for (int t = 0, u = blockIdx.x; ok && u < num_items; ++t, u += gridDim.x) {
+                const Item it = item_of(u, BH, H, S);
+                const int kvb = t & 1;
+                if (!mbar_wait(kv_empty(kvb), ((t >> 1) & 1) ^ 1, abort_flag)) break;
+                mbar_expect_tx(kv_full(kvb), 2 * KT_BYTES);
+                tma_load_2d(sK(kvb), &tmkv, kv_full(kvb), D + it.h * HD, it.krow0);
+                tma_load_2d(sV(kvb), &tmkv, kv_full(kvb), 2 * D + it.h * HD, it.krow0);
+                const float* nl2 = NL2 + (size_t)it.bh * S + it.kb * BK;
+                const float* dot = Dot + (size_t)it.bh * S + it.kb * BK;
+                for (int i = 0; i < it.n; ++i, ++g) {
+                    const int s = g % QS;
+                    if (!mbar_wait(q_empty(s), ((g / QS) & 1) ^ 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t fb = q_full(s);
+                    mbar_expect_tx(fb, 2 * QT_BYTES + ROW_BYTES);
+                    tma_load_2d(sQ(s), &tmq, fb, it.h * HD, it.krow0 + i * BQ);
+                    tma_load_2d(sdO(s), &tmdo, fb, it.h * HD, it.krow0 + i * BQ);
+                    bulk_load(sRow(s), nl2 + i * BQ, BQ * 4, fb);
+                    bulk_load(sRow(s) + BQ * 4, dot + i * BQ, BQ * 4, fb);
+                }
             }
         }
     } else if (warp == 1) {
         // ------------------------------------------- MMA: S^T, dP^T producer ----
         if (lane == 0) {
             const uint32_t id_s = idesc_f16(BQ, 0, 0);    // K (K-major) x Q^T (K-major): N = 64 queries
-            bool ok = mbar_wait(kv_full, 0, abort_flag);
-            for (int j = 0; ok && j < n; ++j) {
-                const int s = j % QS;
-                ok = mbar_wait(q_full(s), (j / QS) & 1, abort_flag) &&
-                     (j < 2 || mbar_wait(s_free(j & 1), ((j >> 1) & 1) ^ 1, abort_flag));
-                if (!ok) break;
-                fence_after();
-                const uint32_t bcol = (uint32_t)(j & 1) * BQ;
+            int g = 0;
+            bool ok = true;
+            for (int t = 0, u = blockIdx.x; ok && u < num_items; ++t, u += gridDim.x) {
+                const int n = item_of(u, BH, H, S).n;
+                const int kvb = t & 1;
+                if (!mbar_wait(kv_full(kvb), (t >> 1) & 1, abort_flag)) break;
+                for (int i = 0; i < n; ++i, ++g) {
+                    const int s = g % QS;
+                    ok = mbar_wait(q_full(s), (g / QS) & 1, abort_flag) &&
+                         (g < 2 || mbar_wait(s_free(g & 1), ((g >> 1) & 1) ^ 1, abort_flag));
+                    if (!ok) break;
+                    fence_after();
+                    const uint32_t bcol = (uint32_t)(g & 1) * BQ;
 #pragma unroll
-                for (int k = 0; k < HD / 16; ++k)
-                    mma_f16(tmem + S_COL + bcol, sdesc(sK + k * 32, 16, 1024), sdesc(sQ(s) + k * 32, 16, 1024), id_s,
-                            k > 0);
+                    for (int k = 0; k < HD / 16; ++k)
+                        mma_f16(tmem + S_COL + bcol, sdesc(sK(kvb) + k * 32, 16, 1024), sdesc(sQ(s) + k * 32, 16, 1024),
+                                id_s, k > 0);
 #pragma unroll
-                for (int k = 0; k < HD / 16; ++k)
-                    mma_f16(tmem + DP_COL + bcol, sdesc(sV + k * 32, 16, 1024), sdesc(sdO(s) + k * 32, 16, 1024),
-                            id_s, k > 0);
-                mma_commit(s_full(j & 1));
-                mma_commit(q_empty(s));
+                    for (int k = 0; k < HD / 16; ++k)
+                        mma_f16(tmem + DP_COL + bcol, sdesc(sV(kvb) + k * 32, 16, 1024),
+                                sdesc(sdO(s) + k * 32, 16, 1024), id_s, k > 0);
+                    mma_commit(s_full(g & 1));
+                    mma_commit(q_empty(s));
+                }
+                if (ok) mma_commit(kv_empty(kvb));
             }
         }
     } else if (warp == 2) {
@@ -200,35 +250,49 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             const uint32_t id_kv = idesc_f16(HD, 0, 1);   // P^T (TMEM) / dS^T (K-major) x dO / Q (MN-major): N = 64
             const uint32_t id_q = idesc_f16(HD, 1, 1);    // dS (MN-major) x K (MN-major): N = 64
-            bool ok = mbar_wait(kv_full, 0, abort_flag);  // K is an operand of dQ
-            for (int i = 0; ok && i < n; ++i) {
-                const int s = i % QS, pb = i & 1;
-                if (!mbar_wait(p_full(pb), (i >> 1) & 1, abort_flag)) { ok = false; break; }
-                fence_after();
-#pragma unroll
-                for (int k = 0; k < BQ / 16; ++k)
-                    mma_f16_ts(tmem + DV_COL, tmem + P_COL + (uint32_t)(pb * 32 + k * 8),
-                               sdesc(sdO(s) + k * 2048, 8192, 1024), id_kv, (i > 0 || k > 0) ? 1u : 0u);
-#pragma unroll
-                for (int k = 0; k < BQ / 16; ++k)
-                    mma_f16(tmem + DK_COL, sdesc(sdS(i & 3) + k * 32, 16, 1024), sdesc(sQ(s) + k * 2048, 8192, 1024),
-                            id_kv, (i > 0 || k > 0) ? 1u : 0u);
-                mma_commit(p_free(pb));
-                mma_commit(q_empty(s));
-                if (i & 1) {
-                    const int p = i >> 1;
-                    if (!mbar_wait(dq_free, (p & 1) ^ 1, abort_flag)) { ok = false; break; }   // pair p-1 drained
+            int g = 0;
+            bool ok = true;
+            for (int t = 0, u = blockIdx.x; ok && u < num_items; ++t, u += gridDim.x) {
+                const int n = item_of(u, BH, H, S).n;
+                const int kvb = t & 1;
+                // K is an operand of dQ; the accumulators must have been read out for the previous item
+                ok = mbar_wait(kv_full(kvb), (t >> 1) & 1, abort_flag) &&
+                     (t == 0 || mbar_wait(acc_free, (t - 1) & 1, abort_flag));
+                if (!ok) break;
+                for (int i = 0; i < n; ++i, ++g) {
+                    const int s = g % QS, pb = g & 1;
+                    if (!mbar_wait(p_full(pb), (g >> 1) & 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
                     fence_after();
-                    const uint32_t a0 = sdS((i - 1) & 3);                      // two adjacent 64-query blocks
 #pragma unroll
-                    for (int k = 0; k < BK / 16; ++k)
-                        mma_f16(tmem + DQ_COL, sdesc(a0 + k * 2048, PT_BYTES, 1024), sdesc(sK + k * 2048, 8192, 1024),
-                                id_q, k > 0);
-                    mma_commit(dq_full);
-                    mma_commit(ds_free(p & 1));
+                    for (int k = 0; k < BQ / 16; ++k)
+                        mma_f16_ts(tmem + DV_COL, tmem + P_COL + (uint32_t)(pb * 32 + k * 8),
+                                   sdesc(sdO(s) + k * 2048, 8192, 1024), id_kv, (i > 0 || k > 0) ? 1u : 0u);
+#pragma unroll
+                    for (int k = 0; k < BQ / 16; ++k)
+                        mma_f16(tmem + DK_COL, sdesc(sdS(g & 3) + k * 32, 16, 1024),
+                                sdesc(sQ(s) + k * 2048, 8192, 1024), id_kv, (i > 0 || k > 0) ? 1u : 0u);
+                    mma_commit(p_free(pb));
+                    mma_commit(q_empty(s));
+                    if (g & 1) {
+                        const int p = g >> 1;
+                        if (!mbar_wait(dq_free, (p & 1) ^ 1, abort_flag)) {   // pair p-1 read out of TMEM
+                            ok = false;
+                            break;
+                        }
+                        fence_after();
+                        const uint32_t a0 = sdS((g - 1) & 3);                  // two adjacent 64-query blocks
+#pragma unroll
+                        for (int k = 0; k < BK / 16; ++k)
+                            mma_f16(tmem + DQ_COL, sdesc(a0 + k * 2048, PT_BYTES, 1024),
+                                    sdesc(sK(kvb) + k * 2048, 8192, 1024), id_q, k > 0);
+                        mma_commit(dq_full);
+                    }
                 }
+                if (ok) mma_commit(acc_done);
             }
-            if (ok) mma_commit(acc_done);
         }
     } else if (warp < WD) {
         // ------------------------------------------------------ P / dS ----
@@ -236,148 +300,158 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int r = lg * 32 + lane;                         // key row inside the block
         const uint32_t lane_off = (uint32_t)(lg * 32) << 16;
         const int c0 = quarter * 16;                          // first query column of this warp
-        for (int i = 0; i < n; ++i) {
-            const int s = i % QS, pb = i & 1;
-            bool ok = mbar_wait(s_full(pb), (i >> 1) & 1, abort_flag) && mbar_wait(q_full(s), (i / QS) & 1, abort_flag);
-            if (!__all_sync(0xffffffffu, ok)) break;
-            fence_after();
-            uint32_t sr[16], dr[16];
-            tmem_ld16(tmem + lane_off + S_COL + (uint32_t)pb * BQ + c0, sr);
-            tmem_ld16(tmem + lane_off + DP_COL + (uint32_t)pb * BQ + c0, dr);
-            tmem_wait_ld();
-            fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(s_free(pb));          // the producer may overwrite this buffer
-            const uint32_t rowp = sRow(s);
-            uint32_t pk[8], dk[8];
-            // masked: the two sub-tiles that overlap the diagonal; columns e < lim lie above it
-            auto compute = [&](auto masked) {
-                const int lim = r - BQ * i - c0;
-#pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4) {
-                    const float4 nl = ld_shared_f4(rowp + (uint32_t)(c0 + 4 * q4) * 4);
-                    const float4 dt = ld_shared_f4(rowp + BQ * 4 + (uint32_t)(c0 + 4 * q4) * 4);
-                    const float nlv[4] = {nl.x, nl.y, nl.z, nl.w}, dtv[4] = {dt.x, dt.y, dt.z, dt.w};
-                    float pv[4], dv[4];
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int e = 4 * q4 + u;
-                        float p = ex2(fmaf(__uint_as_float(sr[e]), scale_log2, nlv[u]));
-                        if (decltype(masked)::value) p = e < lim ? 0.0f : p;
-                        pv[u] = p;
-                        dv[u] = p * (__uint_as_float(dr[e]) - dtv[u]);
-                    }
-                    pk[2 * q4] = pack_h2(pv[0], pv[1]);
-                    pk[2 * q4 + 1] = pack_h2(pv[2], pv[3]);
-                    dk[2 * q4] = pack_h2(dv[0], dv[1]);
-                    dk[2 * q4 + 1] = pack_h2(dv[2], dv[3]);
+        int g = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; ok && u < num_items; u += gridDim.x) {
+            const int n = item_of(u, BH, H, S).n;
+            for (int i = 0; i < n; ++i, ++g) {
+                const int s = g % QS, pb = g & 1;
+                ok = mbar_wait(s_full(pb), (g >> 1) & 1, abort_flag) && mbar_wait(q_full(s), (g / QS) & 1, abort_flag);
+                if (!__all_sync(0xffffffffu, ok)) {
+                    ok = false;
+                    break;
                 }
-            };
-            if (i < 2) compute(std::true_type{});
-            else compute(std::false_type{});
-            // P^T buffer pb was last read by dV_{i-2}; the dS^T pair slot by dQ of pair i/2 - 2
-            ok = true;
-            if (i >= 2) ok = mbar_wait(p_free(pb), ((i >> 1) & 1) ^ 1, abort_flag);
-            if (ok && i >= 4 && !(i & 1)) ok = mbar_wait(ds_free((i >> 1) & 1), ((i >> 2) & 1) ^ 1, abort_flag);
-            if (!__all_sync(0xffffffffu, ok)) break;
-            fence_after();
-            tmem_st8(tmem + lane_off + P_COL + (uint32_t)(pb * 32 + quarter * 8), pk);
-            const uint32_t drow = sdS(i & 3) + (uint32_t)r * 128u;
+                fence_after();
+                uint32_t sr[16], dr[16];
+                tmem_ld16(tmem + lane_off + S_COL + (uint32_t)pb * BQ + c0, sr);
+                tmem_ld16(tmem + lane_off + DP_COL + (uint32_t)pb * BQ + c0, dr);
+                tmem_wait_ld();
+                fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(s_free(pb));      // the producer may overwrite this buffer
+                const uint32_t rowp = sRow(s);
+                uint32_t pk[8], dk[8];
+                // masked: the two sub-tiles that overlap the diagonal; columns e < lim lie above it
+                auto compute = [&](auto masked) {
+                    const int lim = r - BQ * i - c0;
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {                     // 16-byte chunk = 8 queries, 128B swizzle
-                const uint32_t sw = (uint32_t)((((c0 >> 3) + c) ^ (r & 7)) << 4);
-                st_shared_v4(drow + sw, dk[4 * c], dk[4 * c + 1], dk[4 * c + 2], dk[4 * c + 3]);
-            }
-            tmem_wait_st();
-            fence_proxy_async();
-            fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(p_full(pb));
-                mbar_arrive(q_empty(s));
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        const float4 nl = ld_shared_f4(rowp + (uint32_t)(c0 + 4 * q4) * 4);
+                        const float4 dt = ld_shared_f4(rowp + BQ * 4 + (uint32_t)(c0 + 4 * q4) * 4);
+                        const float nlv[4] = {nl.x, nl.y, nl.z, nl.w}, dtv[4] = {dt.x, dt.y, dt.z, dt.w};
+                        float pv[4], dv[4];
+#pragma unroll
+                        for (int e4 = 0; e4 < 4; ++e4) {
+                            const int e = 4 * q4 + e4;
+                            float p = ex2(fmaf(__uint_as_float(sr[e]), scale_log2, nlv[e4]));
+                            if (decltype(masked)::value) p = e < lim ? 0.0f : p;
+                            pv[e4] = p;
+                            dv[e4] = p * (__uint_as_float(dr[e]) - dtv[e4]);
+                        }
+                        pk[2 * q4] = pack_h2(pv[0], pv[1]);
+                        pk[2 * q4 + 1] = pack_h2(pv[2], pv[3]);
+                        dk[2 * q4] = pack_h2(dv[0], dv[1]);
+                        dk[2 * q4 + 1] = pack_h2(dv[2], dv[3]);
+                    }
+                };
+                if (i < 2) compute(Masked{});
+                else compute(Plain{});
+                // P^T buffer pb was last read by dV two sub-tiles back; the dS^T pair slot by the
+                // reduce-add of the pair two pairs back
+                ok = g < 2 || mbar_wait(p_free(pb), ((g >> 1) & 1) ^ 1, abort_flag);
+                if (ok && g >= 4 && !(g & 1)) ok = mbar_wait(ds_free((g >> 1) & 1), ((g >> 2) & 1) ^ 1, abort_flag);
+                if (!__all_sync(0xffffffffu, ok)) {
+                    ok = false;
+                    break;
+                }
+                fence_after();
+                tmem_st8(tmem + lane_off + P_COL + (uint32_t)(pb * 32 + quarter * 8), pk);
+                const uint32_t drow = sdS(g & 3) + (uint32_t)r * 128u;
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {                 // 16-byte chunk = 8 queries, 128B swizzle
+                    const uint32_t sw = (uint32_t)((((c0 >> 3) + c) ^ (r & 7)) << 4);
+                    st_shared_v4(drow + sw, dk[4 * c], dk[4 * c + 1], dk[4 * c + 2], dk[4 * c + 3]);
+                }
+                tmem_wait_st();
+                fence_proxy_async();
+                fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(p_full(pb));
+                    mbar_arrive(q_empty(s));
+                }
             }
         }
     } else {
         // ------------------------------------------- dQ drain, dK / dV out ----
         const int lg = warp & 3;
-        const int r = lg * 32 + lane;                         // query row of the pair / key row at the end
+        const int r = lg * 32 + lane;                         // query row of the pair / key row of the item
         const uint32_t lane_off = (uint32_t)(lg * 32) << 16;
         const bool elected = warp == WD && lane == 0;
-        const int tid = (int)threadIdx.x - WD * 32;           // 0..127
+        int gp = 0;                                           // pair counter of this CTA
         bool ok = true;
-        for (int p = 0; p < n / 2; ++p) {
-            ok = __all_sync(0xffffffffu, ok && mbar_wait(dq_full, p & 1, abort_flag));
-            if (ok) fence_after();
-            if (elected) bulk_wait_read0();                   // staging free again
-            named_sync(1, 128);
-#pragma unroll 1
-            for (int hc = 0; hc < 2; ++hc) {                  // 32 columns at a time
-                uint32_t a[32];
+        for (int t = 0, u = blockIdx.x; u < num_items; ++t, u += gridDim.x) {
+            const Item it = item_of(u, BH, H, S);
+            for (int p = 0; p < it.n / 2; ++p, ++gp) {
+                ok = __all_sync(0xffffffffu, ok && mbar_wait(dq_full, gp & 1, abort_flag));
+                const uint32_t stage = sdS(2 * (gp & 1));    // the pair's dS^T tiles: read by dQ, now free
                 if (ok) {
-                    tmem_ld32(tmem + lane_off + DQ_COL + hc * 32, a);
-                    tmem_wait_ld();
-                    if (hc == 1) {
-                        fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(dq_free);
-                    }
+                    fence_after();
+#pragma unroll 1
+                    for (int hc = 0; hc < 2; ++hc) {          // 32 columns at a time
+                        uint32_t a[32];
+                        tmem_ld32(tmem + lane_off + DQ_COL + hc * 32, a);
+                        tmem_wait_ld();
+                        if (hc == 1) {
+                            fence_before();
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(dq_free);
+                        }
 #pragma unroll
-                    for (int c = 0; c < 8; ++c)
-                        st_shared_v4(stage_addr(sDQ, r, hc * 8 + c), __float_as_uint(__uint_as_float(a[4 * c]) * scale),
-                                     __float_as_uint(__uint_as_float(a[4 * c + 1]) * scale),
-                                     __float_as_uint(__uint_as_float(a[4 * c + 2]) * scale),
-                                     __float_as_uint(__uint_as_float(a[4 * c + 3]) * scale));
+                        for (int c = 0; c < 8; ++c)
+                            st_shared_v4(stage_addr(stage, r, hc * 8 + c),
+                                         __float_as_uint(__uint_as_float(a[4 * c]) * scale),
+                                         __float_as_uint(__uint_as_float(a[4 * c + 1]) * scale),
+                                         __float_as_uint(__uint_as_float(a[4 * c + 2]) * scale),
+                                         __float_as_uint(__uint_as_float(a[4 * c + 3]) * scale));
+                    }
                 }
+                fence_proxy_async();
+                named_sync(1, 128);
+                if (elected && ok) {
+                    const int y = it.krow0 + p * 128;
+                    tma_reduce_add_2d(&tmdq, stage, it.h * HD, y);
+                    tma_reduce_add_2d(&tmdq, stage + 16384, it.h * HD + 32, y);
+                    bulk_commit();
+                    bulk_wait_read0();                        // staging read: the tiles may be rewritten
+                    mbar_arrive(ds_free(gp & 1));
+                }
+            }
+            // dK (scaled) and dV: TMEM -> FP16 in the item's K / V tiles (128B-swizzled rows, the
+            // layout the TMA store reads), then the accumulators are free for the next item
+            ok = __all_sync(0xffffffffu, ok && mbar_wait(acc_done, t & 1, abort_flag));
+            const int kvb = t & 1;
+            if (ok) {
+                fence_after();
+#pragma unroll 1
+                for (int q = 0; q < 4; ++q) {                 // dK lo, dK hi, dV lo, dV hi
+                    const int tv = q >> 1, hc = q & 1;
+                    uint32_t a[32];
+                    tmem_ld32(tmem + lane_off + (tv ? DV_COL : DK_COL) + hc * 32, a);
+                    tmem_wait_ld();
+                    const float f = tv ? 1.0f : scale;
+                    const uint32_t row = (tv ? sV(kvb) : sK(kvb)) + (uint32_t)r * 128u;
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        uint32_t w[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            w[e] = pack_h2(__uint_as_float(a[8 * c + 2 * e]) * f, __uint_as_float(a[8 * c + 2 * e + 1]) * f);
+                        st_shared_v4(row + (uint32_t)((((hc * 4 + c) ^ (r & 7))) << 4), w[0], w[1], w[2], w[3]);
+                    }
+                }
+                fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(acc_free);         // the next item may accumulate again
             }
             fence_proxy_async();
             named_sync(1, 128);
             if (elected && ok) {
-                const int y = krow0 + p * 128;
-                tma_reduce_add_2d(&tmdq, sDQ, h * HD, y);
-                tma_reduce_add_2d(&tmdq, sDQ + 16384, h * HD + 32, y);
+                tma_store_2d(&tmout, sK(kvb), D + it.h * HD, it.krow0);
+                tma_store_2d(&tmout, sV(kvb), 2 * D + it.h * HD, it.krow0);
                 bulk_commit();
-            }
-        }
-        if (elected) bulk_wait_read0();                       // last reduce has read the staging
-        named_sync(1, 128);
-        ok = __all_sync(0xffffffffu, ok && mbar_wait(acc_done, 0, abort_flag));
-        if (ok) fence_after();
-        // dK (scaled) then dV, 32 columns at a time: FP16 rows to dqkv, FP32 to staging for the bias sums
-#pragma unroll 1
-        for (int t = 0; t < 2; ++t) {
-#pragma unroll 1
-            for (int hc = 0; hc < 2; ++hc) {
-                if (ok) {
-                    uint32_t a[32];
-                    tmem_ld32(tmem + lane_off + (t ? DV_COL : DK_COL) + hc * 32, a);
-                    tmem_wait_ld();
-                    const float f = t ? 1.0f : scale;
-                    float v[32];
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(a[e]) * f;
-                    half* row = dqkv + (size_t)(krow0 + r) * (3 * D) + (t + 1) * D + h * HD + hc * 32;
-#pragma unroll
-                    for (int g = 0; g < 4; ++g) reinterpret_cast<uint4*>(row)[g] = f_to_h8(v + 8 * g);
-                    if (dbias) {
-#pragma unroll
-                        for (int c = 0; c < 8; ++c)
-                            st_shared_v4(stage_addr(sDQ, r, hc * 8 + c), __float_as_uint(v[4 * c]),
-                                         __float_as_uint(v[4 * c + 1]), __float_as_uint(v[4 * c + 2]),
-                                         __float_as_uint(v[4 * c + 3]));
-                    }
-                }
-            }
-            if (dbias) {
-                named_sync(1, 128);
-                if (ok) {
-                    const int col = tid & 63, rh = tid >> 6;
-                    float acc = 0.0f;
-#pragma unroll 8
-                    for (int rr = rh * 64; rr < rh * 64 + 64; ++rr)
-                        acc += ld_shared_f(stage_addr(sDQ, rr, col >> 2) + (uint32_t)(col & 3) * 4);
-                    atomicAdd(dbias + (t + 1) * D + h * HD + col, acc);
-                }
-                named_sync(1, 128);
+                bulk_wait_read0();                            // tiles read: the buffer may take new K / V
+                mbar_arrive(kv_empty(kvb));
             }
         }
         if (elected) bulk_wait0();
@@ -392,24 +466,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace attn_tc_bwd
 
 // Main pass of rbk_attn_bwd (attn.cu) when d_head == 64 and S % 128 == 0.
-// dq_acc: FP32 [B*S, H*64], zeroed; NL2 / Dot: [B*H, S].
-int attn_bwd_tc(rbk_ctx* ctx, void* dqkv, float* dq_acc, float* dbias, const void* qkv, const void* dout,
-                const float* NL2, const float* Dot, int B, int S, int H, float scale, cudaStream_t st) {
+// dq_acc: FP32 [B*S, H*64], zeroed; NL2 / Dot: [B*H, S].  Writes the k and v
+// sections of dqkv and adds dQ into dq_acc.
+int attn_bwd_tc(rbk_ctx* ctx, void* dqkv, float* dq_acc, const void* qkv, const void* dout, const float* NL2,
+                const float* Dot, int B, int S, int H, float scale, cudaStream_t st) {
     using namespace attn_tc_bwd;
     const int D = H * HD;
     const uint64_t BS = (uint64_t)B * S;
-    CUtensorMap tmq, tmkv, tmdo, tmdq;
+    CUtensorMap tmq, tmkv, tmdo, tmdq, tmout;
     RBK_TRY(tc::make_tmap(&tmq, qkv, 3 * (uint64_t)D, BS, 3 * (uint64_t)D, 64, BQ));
     RBK_TRY(tc::make_tmap(&tmkv, qkv, 3 * (uint64_t)D, BS, 3 * (uint64_t)D, 64, BK));
     RBK_TRY(tc::make_tmap(&tmdo, dout, (uint64_t)D, BS, (uint64_t)D, 64, BQ));
     RBK_TRY(tc::make_tmap(&tmdq, dq_acc, (uint64_t)D, BS, (uint64_t)D, 32, 128, CU_TENSOR_MAP_DATA_TYPE_FLOAT32));
+    RBK_TRY(tc::make_tmap(&tmout, dqkv, 3 * (uint64_t)D, BS, 3 * (uint64_t)D, 64, BK));
     static int set_dev = -1;
     if (set_dev != ctx->device) {
         RBK_CUDA(cudaFuncSetAttribute(flash_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
         set_dev = ctx->device;
     }
-    dim3 grid(B * H, S / BK);
-    flash_bwd_tc_kernel<<<grid, kThreads, SMEM, st>>>(tmq, tmkv, tmdo, tmdq, (half*)dqkv, dbias, NL2, Dot, S, H, scale,
+    const int items = B * H * (S / BK);
+    const int grid = items < ctx->num_sms ? items : ctx->num_sms;
+    flash_bwd_tc_kernel<<<grid, kThreads, SMEM, st>>>(tmq, tmkv, tmdo, tmdq, tmout, NL2, Dot, S, H, items, scale,
                                                       scale * 1.4426950408889634f, ctx->tickets + kGemmError);
     RBK_LAUNCHED("flash_bwd_tc_kernel");
     return RBK_OK;

@@ -71,6 +71,12 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
         "l"(src), "r"(bytes), "r"(bar)
         : "memory");
 }
+// Tiled 2-D store of a shared-memory box into global memory (bulk group).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* tm, uint32_t src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tm), "r"(src),
+                 "r"(x), "r"(y)
+                 : "memory");
+}
 // Tiled 2-D reduce-add (FP32) of a shared-memory box into global memory.
 __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* tm, uint32_t src, int x, int y) {
     asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
@@ -80,6 +86,7 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* tm, uint32_
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void named_sync(uint32_t id, uint32_t threads) {
