@@ -9,12 +9,15 @@
 // adjacent columns, and several teams share a CTA.  A thread keeps its
 // columns' dgamma / dbeta (/ dbias) partial sums in registers for every row
 // its team visits, instead of the reference's per-element half atomics
-// (src/cuda_kernels.cu:279-282).  Teams take kLnRows rows at a time (that
-// many 16-byte loads of dy and of x in flight per thread) and reduce their two
-// row sums through shared memory.  At the end the teams of a CTA fold their
-// partials in shared memory, and one small column-parallel launch sums the
-// per-CTA partials in a fixed order, so results are bitwise reproducible.
-#include "common.cuh"
+// (src/cuda_kernels.cu:279-282).  One persistent CTA per SM streams blocks of
+// consecutive rows of dy, x (and the residual gradient) into a shared-memory
+// ring with bulk copies issued by one producer thread, so 100+ KB per SM are
+// in flight while the teams work; each team reduces its two row sums through
+// shared memory behind its own named barrier.  At the end the teams of a CTA
+// fold their partials in shared memory, and one small column-parallel launch
+// sums the per-CTA partials in a fixed order, so results are bitwise
+// reproducible.
+#include "tc.cuh"
 
 namespace rbk {
 namespace {
@@ -68,7 +71,7 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(half* __restrict__ y, float
     }
 }
 
-constexpr int kLnRows = 4;       // rows per team iteration in the backward
+constexpr int kLnRows = 4;       // rows per team iteration in the backward (the butterfly assumes 4)
 constexpr int kLnMaxTeams = 8;
 
 // Dynamic shared memory: red[2][teams][2R][warps per team] then part[teams][3][D].
@@ -190,26 +193,238 @@ __global__ void __launch_bounds__(512) ln_bwd_kernel(half* __restrict__ dx, floa
 }
 
 // out_w[c] += sum_b part[b][w][c] for w in {dgamma, dbeta, dbias}: 32 columns per
-// CTA (one per lane), the 8 warps split the partial rows, fixed summation order.
-__global__ void __launch_bounds__(256) ln_bwd_reduce_kernel(float* __restrict__ dg, float* __restrict__ db,
-                                                            float* __restrict__ dbias,
-                                                            const float* __restrict__ part, int nblk, int D) {
-    __shared__ float s[8][33];
+// CTA (one per lane), the 32 warps split the partial rows (all their loads in
+// flight at once), fixed summation order.
+__global__ void __launch_bounds__(1024) ln_bwd_reduce_kernel(float* __restrict__ dg, float* __restrict__ db,
+                                                             float* __restrict__ dbias,
+                                                             const float* __restrict__ part, int nblk, int D) {
+    __shared__ float s[32][33];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int c = blockIdx.x * 32 + lane;
     const int which = blockIdx.y;
     float* out = which == 0 ? dg : which == 1 ? db : dbias;
-    float acc = 0.0f;
-    if (c < D)
-        for (int b = warp; b < nblk; b += 8) acc += part[(size_t)b * 3 * D + (size_t)which * D + c];
-    s[warp][lane] = acc;
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (c < D) {
+        int b = warp;
+        for (; b + 96 < nblk; b += 128) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) acc[u] += __ldg(part + (size_t)(b + 32 * u) * 3 * D + (size_t)which * D + c);
+        }
+        for (; b < nblk; b += 32) acc[0] += __ldg(part + (size_t)b * 3 * D + (size_t)which * D + c);
+    }
+    s[warp][lane] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
     __syncthreads();
     if (warp == 0 && c < D && out) {
         float t = 0.0f;
-#pragma unroll
-        for (int w = 0; w < 8; ++w) t += s[w][lane];
+#pragma unroll 8
+        for (int w = 0; w < 32; ++w) t += s[w][lane];
         out[c] += t;
     }
+}
+
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+    return v;
+}
+
+// ---------------------------------------------------------------------------
+// Backward with a bulk-copy ring.  Shared memory: stages x [dy | x | dres] row
+// blocks (RS = teams * kLnRows consecutive rows of D halves each, one bulk
+// copy per tensor), the teams' row-sum exchange red[teams][2][2 kLnRows][warps
+// per team], barriers; at the end the ring is reused for the teams' column
+// partials tpart[teams][3][D].
+// part (global) layout: [gridDim.x][3][D]  (dgamma | dbeta | dbias partials)
+template <bool kRefFormula, bool kRes, bool kBias>
+__global__ void __launch_bounds__(544, 1)
+    ln_bwd_ring_kernel(half* __restrict__ dx, float* __restrict__ part, const half* __restrict__ dy,
+                       const half* __restrict__ dres, const half* __restrict__ x, const half* __restrict__ g,
+                       const float* __restrict__ mean, const float* __restrict__ rstd, int N, int D, int teams,
+                       int tpt, int stages, int* err) {
+    using namespace tc;
+    constexpr int R = kLnRows;
+    static_assert(R == 4, "the row-sum butterfly below reduces 2 * 4 sums");
+    constexpr int NT = kRes ? 3 : 2;
+    extern __shared__ __align__(128) uint8_t lsm_raw[];
+    const int RS = teams * R;
+    const size_t row_bytes = (size_t)D * 2;
+    const size_t stage_bytes = (size_t)RS * row_bytes * NT;
+    const int wpt = tpt >> 5;
+    float* red = reinterpret_cast<float*>(lsm_raw + stages * stage_bytes);    // [teams][2][2R][wpt]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(red + (size_t)teams * 2 * 2 * R * wpt);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * stages);
+    auto full = [&](int s) { return su32(bars + s); };
+    auto empty = [&](int s) { return su32(bars + stages + s); };
+    const int consumers = teams * tpt;                  // consumer threads; one producer warp follows
+    const int nwc = consumers >> 5;
+    const int tid = threadIdx.x, lane = tid & 31;
+    if (tid == 0) {
+        for (int s = 0; s < stages; ++s) {
+            mbar_init(full(s), 1);
+            mbar_init(empty(s), nwc);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    const int nstage = (N + RS - 1) / RS;
+
+    if (tid >= consumers) {
+        // ------------------------------------------------------ producer ----
+        if (tid == consumers) {
+            int k = 0;
+            for (int gs = blockIdx.x; gs < nstage; gs += gridDim.x, ++k) {
+                const int s = k % stages;
+                if (!mbar_wait(empty(s), ((k / stages) & 1) ^ 1, abort_flag)) break;
+                const int rows = min(RS, N - gs * RS);
+                mbar_expect_tx(full(s), (uint32_t)(rows * row_bytes * NT));
+                const uint32_t dst = su32(lsm_raw + s * stage_bytes);
+                const size_t off = (size_t)gs * RS * D;
+                const uint32_t bytes = (uint32_t)(rows * row_bytes);   // consecutive rows: one copy per tensor
+                bulk_load(dst, dy + off, bytes, full(s));
+                bulk_load(dst + (uint32_t)(RS * row_bytes), x + off, bytes, full(s));
+                if (kRes) bulk_load(dst + (uint32_t)(2 * RS * row_bytes), dres + off, bytes, full(s));
+            }
+        }
+    } else {
+        // ------------------------------------------------------ consumers ----
+        const int team = tid / tpt, ttid = tid - team * tpt, twarp = ttid >> 5;
+        const int nvec = D >> 3;
+        const bool own = ttid < nvec;                   // columns [8 ttid, 8 ttid + 8)
+        const float invD = 1.0f / (float)D;
+        float gam[8], pg[8], pb[8], pd[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) { pg[j] = 0.0f; pb[j] = 0.0f; pd[j] = 0.0f; gam[j] = 0.0f; }
+        if (own) h8_to_f(__ldg(reinterpret_cast<const uint4*>(g) + ttid), gam);
+        bool ok = true;
+        int k = 0;
+        const uint32_t ring = su32(lsm_raw);
+        for (int gs = blockIdx.x; gs < nstage; gs += gridDim.x, ++k) {
+            const int s = k % stages;
+            const int row0 = gs * RS + team * R;
+            float mr[R], rr[R];                         // issued before the wait: their latency overlaps it
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                mr[r] = row0 + r < N ? __ldg(mean + row0 + r) : 0.0f;
+                rr[r] = row0 + r < N ? __ldg(rstd + row0 + r) : 0.0f;
+            }
+            ok = __all_sync(0xffffffffu, ok && mbar_wait(full(s), (k / stages) & 1, abort_flag));
+            const uint32_t sb = ring + (uint32_t)(s * stage_bytes);
+            // pass 1 over the staged rows: ts1 = sum dy*g, ts2 = sum dy*g*(x - mean)
+            float v8[2 * R];
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int lr = team * R + r;            // row inside the block
+                float s1 = 0.0f, s2 = 0.0f;
+                if (ok && own && row0 + r < N) {
+                    float d[8], xx[8];
+                    h8_to_f(lds128(sb + (uint32_t)(lr * row_bytes + 16 * ttid)), d);
+                    h8_to_f(lds128(sb + (uint32_t)((RS + lr) * row_bytes + 16 * ttid)), xx);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const float dg = d[j] * gam[j];
+                        s1 += dg;
+                        s2 = fmaf(dg, xx[j] - mr[r], s2);
+                    }
+                }
+                v8[2 * r] = s1;
+                v8[2 * r + 1] = s2;
+            }
+            // warp totals of the 8 sums with one transposed butterfly (9 shuffles): lane l ends with
+            // the total of sum index (l >> 2) & 7
+            float tot;
+            {
+                const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+                float a4[4], a2[2];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float keep = b4 ? v8[i + 4] : v8[i], send = b4 ? v8[i] : v8[i + 4];
+                    a4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+                }
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    const float keep = b3 ? a4[i + 2] : a4[i], send = b3 ? a4[i] : a4[i + 2];
+                    a2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+                }
+                tot = (b2 ? a2[1] : a2[0]) + __shfl_xor_sync(0xffffffffu, b2 ? a2[0] : a2[1], 4);
+                tot += __shfl_xor_sync(0xffffffffu, tot, 2);
+                tot += __shfl_xor_sync(0xffffffffu, tot, 1);
+            }
+            float* rb = red + ((size_t)team * 2 + (k & 1)) * 2 * R * wpt;
+            if ((lane & 3) == 0) rb[((lane >> 2) & 7) * wpt + twarp] = tot;
+            named_sync(1 + team, tpt);                  // this team's warps only
+            // lane q < 8 adds the team's warps for sum q; shuffles hand every lane all 8 totals
+            float mine = 0.0f;
+            if (lane < 2 * R)
+                for (int w = 0; w < wpt; ++w) mine += rb[lane * wpt + w];
+            float ts[2 * R];
+#pragma unroll
+            for (int q = 0; q < 2 * R; ++q) ts[q] = __shfl_sync(0xffffffffu, mine, q);
+            // pass 2: dx = A * dy*g + B * xhat + C per row, column partials
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int lr = team * R + r;
+                const int row = row0 + r;
+                if (ok && own && row < N) {
+                    float d[8], xx[8], o[8], rs[8];
+                    h8_to_f(lds128(sb + (uint32_t)(lr * row_bytes + 16 * ttid)), d);
+                    h8_to_f(lds128(sb + (uint32_t)((RS + lr) * row_bytes + 16 * ttid)), xx);
+                    if (kRes) h8_to_f(lds128(sb + (uint32_t)((2 * RS + lr) * row_bytes + 16 * ttid)), rs);
+                    const float inv = rr[r], m = mr[r];
+                    const float t1 = ts[2 * r], t2 = ts[2 * r + 1];
+                    // exact: dx = inv * (dg - (t1 + xm * inv^2 * t2) / D); the reference formula has
+                    // inv instead of inv^2 (one rstd factor short)
+                    const float A = inv, C = -inv * t1 * invD;
+                    const float B = -(kRefFormula ? inv : inv * inv) * t2 * invD;   // multiplies xhat = xm * inv
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const float xh = (xx[j] - m) * inv;
+                        const float dg = d[j] * gam[j];
+                        float v = fmaf(B, xh, fmaf(A, dg, C));
+                        if (kRes) v += rs[j];
+                        o[j] = v;
+                        pg[j] = fmaf(d[j], xh, pg[j]);
+                        pb[j] += d[j];
+                        if (kBias) pd[j] += v;
+                    }
+                    reinterpret_cast<uint4*>(dx + (size_t)row * D)[ttid] = f_to_h8(o);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty(s));      // this warp is done with the stage
+        }
+        if (!ok && tid == 0) atomicExch(err, RBK_ERR_TIMEOUT);
+        // park the partials until the ring is free (all copies were consumed)
+        __syncthreads();
+        float* tpart = reinterpret_cast<float*>(lsm_raw);   // [teams][3][D]
+        if (own) {
+            float* tp = tpart + (size_t)team * 3 * D + 8 * ttid;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                tp[j] = pg[j];
+                tp[D + j] = pb[j];
+                tp[2 * D + j] = pd[j];
+            }
+        }
+    }
+    if (tid >= consumers) __syncthreads();              // matches the consumers' barrier above
+    __syncthreads();
+    const float* tpart = reinterpret_cast<const float*>(lsm_raw);
+    for (int i = tid; i < 3 * D; i += blockDim.x) {
+        float v = 0.0f;
+        for (int t = 0; t < teams; ++t) v += tpart[(size_t)t * 3 * D + i];
+        part[(size_t)blockIdx.x * 3 * D + i] = v;
+    }
+}
+
+template <bool A, bool B, bool C>
+int launch_bwd_ring(int blocks, int threads, int teams, int tpt, int stages, size_t smem, cudaStream_t st, half* dx,
+                    float* part, const half* dy, const half* dres, const half* x, const half* g, const float* mean,
+                    const float* rstd, int N, int D, int* err) {
+    RBK_CUDA(cudaFuncSetAttribute(ln_bwd_ring_kernel<A, B, C>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    ln_bwd_ring_kernel<A, B, C><<<blocks, threads, smem, st>>>(dx, part, dy, dres, x, g, mean, rstd, N, D, teams, tpt,
+                                                               stages, err);
+    return RBK_OK;
 }
 
 template <int NV>
@@ -273,15 +488,21 @@ int rbk_ln_bwd(rbk_ctx* ctx, void* dx, float* dgamma, float* dbeta, float* dbias
     RBK_REQUIRE(N > 0 && D > 0 && D % 8 == 0 && D <= 4096, "rbk_ln_bwd: need D %% 8 == 0 and D <= 4096 (D=%d)", D);
     RBK_REQUIRE(aligned16(dx) && aligned16(dy) && aligned16(x) && aligned16(gamma) && (!dres || aligned16(dres)),
                 "rbk_ln_bwd: tensors must be 16-byte aligned");
+    RBK_REQUIRE(aligned16(mean) && aligned16(rstd), "rbk_ln_bwd: mean / rstd must be 16-byte aligned");
     const int tpt = ((D / 8 + 31) / 32) * 32;            // threads per team
     int teams = 512 / tpt;
     teams = teams < 1 ? 1 : teams > kLnMaxTeams ? kLnMaxTeams : teams;
-    const int threads = teams * tpt;
-    const int ngroups = (N + kLnRows - 1) / kLnRows;
-    int blocks = ctx->num_sms;                            // 512 threads x ~128 registers: one CTA per SM
-    const int need = (ngroups + teams - 1) / teams;
-    if (blocks > need) blocks = need;
-    const size_t smem = sizeof(float) * ((size_t)2 * teams * 2 * kLnRows * (tpt / 32) + (size_t)teams * 3 * D);
+    const int threads = teams * tpt + 32;                // + the producer warp
+    const int RS = teams * kLnRows;                      // rows per ring stage
+    const size_t stage_bytes = (size_t)RS * D * 2 * (dres ? 3 : 2);
+    int stages = (int)((200u << 10) / stage_bytes);
+    stages = stages > 4 ? 4 : stages;
+    RBK_REQUIRE(stages >= 2, "rbk_ln_bwd: row blocks too large for the shared-memory ring (D=%d)", D);
+    const size_t smem = stages * stage_bytes + sizeof(float) * (size_t)teams * 2 * 2 * kLnRows * (tpt / 32) +
+                        16 * (size_t)stages + 16;
+    const int nstage = (N + RS - 1) / RS;
+    int blocks = ctx->num_sms;                            // persistent: one CTA per SM
+    if (blocks > nstage) blocks = nstage;
     void* ws;
     RBK_TRY(ctx_scratch(ctx, sizeof(float) * 3 * (size_t)D * blocks, &ws));
     float* part = (float*)ws;
@@ -296,8 +517,10 @@ int rbk_ln_bwd(rbk_ctx* ctx, void* dx, float* dgamma, float* dbeta, float* dbias
     auto DR = (const half*)dres;
     auto X = (const half*)x;
     auto G = (const half*)gamma;
-#define RBK_LN_BWD(R_, S_, B_) \
-    RBK_TRY((launch_bwd<R_, S_, B_>(blocks, threads, teams, smem, st, DX, part, DY, DR, X, G, mean, rstd, N, D)))
+    int* err = ctx->tickets + kGemmError;
+#define RBK_LN_BWD(R_, S_, B_)                                                                                  \
+    RBK_TRY((launch_bwd_ring<R_, S_, B_>(blocks, threads, teams, tpt, stages, smem, st, DX, part, DY, DR, X, G, \
+                                         mean, rstd, N, D, err)))
     if (ref) {
         if (res) { if (bias) RBK_LN_BWD(true, true, true); else RBK_LN_BWD(true, true, false); }
         else { if (bias) RBK_LN_BWD(true, false, true); else RBK_LN_BWD(true, false, false); }
@@ -306,9 +529,9 @@ int rbk_ln_bwd(rbk_ctx* ctx, void* dx, float* dgamma, float* dbeta, float* dbias
         else { if (bias) RBK_LN_BWD(false, false, true); else RBK_LN_BWD(false, false, false); }
     }
 #undef RBK_LN_BWD
-    RBK_LAUNCHED("ln_bwd_kernel");
+    RBK_LAUNCHED("ln_bwd_ring_kernel");
     dim3 rg((D + 31) / 32, bias ? 3 : 2);
-    ln_bwd_reduce_kernel<<<rg, 256, 0, st>>>(dgamma, dbeta, dbias_out, part, blocks, D);
+    ln_bwd_reduce_kernel<<<rg, 1024, 0, st>>>(dgamma, dbeta, dbias_out, part, blocks, D);
     RBK_LAUNCHED("ln_bwd_reduce_kernel");
     return RBK_OK;
 }
@@ -417,7 +640,7 @@ extern "C" int rbk_ln_bwd_noalloc(void* dx, float* dgamma, float* dbeta, float* 
 #undef RBK_LN_BWD
     RBK_LAUNCHED("ln_bwd_kernel (no-alloc)");
     dim3 rg((D + 31) / 32, bias ? 3 : 2);
-    ln_bwd_reduce_kernel<<<rg, 256, 0, st>>>(dgamma, dbeta, dbias_out, part, blocks, D);
+    ln_bwd_reduce_kernel<<<rg, 1024, 0, st>>>(dgamma, dbeta, dbias_out, part, blocks, D);
     RBK_LAUNCHED("ln_bwd_reduce_kernel (no-alloc)");
     return RBK_OK;
 }

@@ -1,19 +1,20 @@
 // xent.cu — fused softmax-cross-entropy forward + backward (HBM-bound).
 //
-// One CTA owns a row at a time.  Pass 1 streams the row once from HBM with
-// 16-byte loads (4 in flight per thread) and keeps an online (max, sum of
-// exp) per thread, merged across the CTA; pass 2 re-reads the same row — a
-// few tens of KB that the CTA touched microseconds earlier, so it comes from
-// L2 — and writes (softmax - onehot) * scale, in place if the caller wishes.
-// DRAM therefore sees one read and one write per logit.  The number of rows in
-// flight (grid x row bytes) is capped well below the 126 MB L2 so pass 2 hits.
-// The reference instead rescans the whole row for every element
-// (src/cuda_kernels.cu:533-551, O(N V^2)); cpuops does three passes
-// (src/cpu_mat.h:220-236).  Per-row loss follows src/cpu_mat.h:213
+// Rows that fit twice in shared memory (V up to ~50K FP16) take the ring
+// kernel: one persistent CTA per SM, a producer thread bulk-copies whole rows
+// into a 2-4 deep shared-memory ring, and 16 warps make three passes over the
+// staged row (max, sum of exp, gradient) — DRAM sees exactly one read and one
+// write per logit, in place if the caller wishes, with the next rows already
+// in flight.  Wider rows take the streaming kernel: pass 1 reads the row once
+// with 16-byte loads and keeps an online (max, sum of exp) per thread; pass 2
+// re-reads it from L2 (rows in flight are capped well below the 126 MB L2)
+// and writes the gradient.  The reference instead rescans the whole row for
+// every element (src/cuda_kernels.cu:533-551, O(N V^2)); cpuops does three
+// passes (src/cpu_mat.h:220-236).  Per-row loss follows src/cpu_mat.h:213
 // (-log(p_t + 1e-10)).
 #include <cfloat>
 
-#include "common.cuh"
+#include "tc.cuh"
 
 namespace rbk {
 namespace {
@@ -116,6 +117,153 @@ __global__ void __launch_bounds__(kThreads) xent_kernel(half* dl, const half* lg
     }
 }
 
+constexpr int kRingConsumers = 512;
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+    return v;
+}
+
+// Ring kernel: shared memory = nbuf row buffers (rowb bytes each, V rounded up
+// to 8 halves), then per-row reduction scratch red[2][2][16] and barriers.
+__global__ void __launch_bounds__(kRingConsumers + 32, 1)
+    xent_ring_kernel(half* dl, const half* lg, int ld, const int* __restrict__ tgt, int N, int V, float scale,
+                     const float* __restrict__ dscale, float* __restrict__ row_loss, int nbuf, int rowb, int* err) {
+    using namespace tc;
+    extern __shared__ __align__(128) uint8_t xs[];
+    float* red = reinterpret_cast<float*>(xs + (size_t)nbuf * rowb);   // [2 parity][2 (max, sum)][16 warps]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(red + 64);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * nbuf);
+    auto full = [&](int b) { return su32(bars + b); };
+    auto empty = [&](int b) { return su32(bars + nbuf + b); };
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int NW = kRingConsumers / 32;
+    if (tid == 0) {
+        for (int b = 0; b < nbuf; ++b) {
+            mbar_init(full(b), 1);
+            mbar_init(empty(b), NW);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    const int nchunk = (V + 7) >> 3;                    // 16-byte chunks per row (tail masked)
+    if (tid >= kRingConsumers) {
+        // ------------------------------------------------------ producer ----
+        if (tid == kRingConsumers) {
+            int k = 0;
+            for (int row = blockIdx.x; row < N; row += gridDim.x, ++k) {
+                const int b = k % nbuf;
+                if (!mbar_wait(empty(b), ((k / nbuf) & 1) ^ 1, abort_flag)) break;
+                mbar_expect_tx(full(b), (uint32_t)(nchunk * 16));
+                bulk_load(su32(xs + (size_t)b * rowb), lg + (size_t)row * ld, (uint32_t)(nchunk * 16), full(b));
+            }
+        }
+        return;
+    }
+    // ---------------------------------------------------------- consumers ----
+    const float gs = scale * (dscale ? __ldg(dscale) : 1.0f);
+    constexpr float kL2e = 1.4426950408889634f;
+    bool ok = true;
+    int k = 0;
+    for (int row = blockIdx.x; row < N; row += gridDim.x, ++k) {
+        const int b = k % nbuf;
+        const int t = __ldg(tgt + row);
+        const bool tvalid = t >= 0 && t < V;
+        ok = __all_sync(0xffffffffu, ok && mbar_wait(full(b), (k / nbuf) & 1, abort_flag));
+        const uint32_t rb = su32(xs + (size_t)b * rowb);
+        float* rr = red + (k & 1) * 32;
+        const int full8 = V >> 3;                       // chunks without a tail
+        // the target logit is read before pass 2 overwrites the staged row
+        const float zt = (row_loss && tid == 0 && tvalid && ok)
+                             ? __half2float(reinterpret_cast<const half*>(xs + (size_t)b * rowb)[t])
+                             : 0.0f;
+        // pass 1: row max
+        float m = -INFINITY;
+        if (ok) {
+            for (int c = tid; c < nchunk; c += kRingConsumers) {
+                float f[8];
+                h8_to_f(lds128(rb + 16u * c), f);
+                if (c < full8) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) m = fmaxf(m, f[j]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) m = fmaxf(m, 8 * c + j < V ? f[j] : -INFINITY);
+                }
+            }
+        }
+        m = warp_max(m);
+        if (lane == 0) rr[warp] = m;
+        named_sync(1, kRingConsumers);
+        m = rr[0];
+#pragma unroll
+        for (int w = 1; w < NW; ++w) m = fmaxf(m, rr[w]);
+        // pass 2: p = exp(z - max) (exp2 of the log2e-scaled difference), summed in FP32 and
+        // written back over the staged row as FP16 (p <= 1) so pass 3 needs no second exp
+        const float mb = m * kL2e;
+        float sum = 0.0f;
+        if (ok) {
+            for (int c = tid; c < nchunk; c += kRingConsumers) {
+                float f[8];
+                h8_to_f(lds128(rb + 16u * c), f);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) f[j] = ex2(fmaf(f[j], kL2e, -mb));
+                if (c >= full8) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) f[j] = 8 * c + j < V ? f[j] : 0.0f;
+                }
+#pragma unroll
+                for (int j = 0; j < 8; ++j) sum += f[j];
+                const uint4 u = f_to_h8(f);
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rb + 16u * c), "r"(u.x), "r"(u.y),
+                             "r"(u.z), "r"(u.w)
+                             : "memory");
+            }
+        }
+        sum = warp_sum(sum);
+        if (lane == 0) rr[NW + warp] = sum;
+        named_sync(1, kRingConsumers);                  // also orders every thread's p stores before pass 3
+        sum = 0.0f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) sum += rr[NW + w];
+        const float inv = 1.0f / sum;
+        if (row_loss && tid == 0) {
+            float l = __int_as_float(0x7fc00000);       // NaN for an invalid target
+            if (tvalid) l = -logf(ex2(fmaf(zt, kL2e, -mb)) * inv + 1e-10f);
+            row_loss[row] = l;
+        }
+        // pass 3: gradient = (p / sum - onehot) * scale, 16-byte stores
+        if (dl && ok) {
+            const float g = tvalid ? gs : 0.0f, gi = g * inv;
+            half* d = dl + (size_t)row * ld;
+            for (int c = tid; c < nchunk; c += kRingConsumers) {
+                float f[8];
+                h8_to_f(lds128(rb + 16u * c), f);
+                const int tj = t - 8 * c;               // target column inside this chunk, if any
+#pragma unroll
+                for (int j = 0; j < 8; ++j) f[j] = fmaf(f[j], gi, j == tj ? -g : 0.0f);
+                if (c < full8) {
+                    reinterpret_cast<uint4*>(d)[c] = f_to_h8(f);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        if (8 * c + j < V) d[8 * c + j] = __float2half_rn(f[j]);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty(b));          // this warp is done with the buffer
+    }
+    if (!ok && tid == 0) atomicExch(err, RBK_ERR_TIMEOUT);
+}
+
 }  // namespace
 }  // namespace rbk
 
@@ -137,6 +285,24 @@ extern "C" int rbk_softmax_xent_bwd(rbk_ctx* ctx, void* dlogits, const void* log
     cudaStream_t st = as_stream(stream);
     ProfScope prof(ctx, st, kCatXent,
                    (double)N * V * (dlogits ? 4.0 : 2.0) + 4.0 * N + (row_loss ? 4.0 * N : 0.0));
+    // ring kernel when at least two rows fit in shared memory
+    const int rowb = ((V + 7) / 8) * 16;
+    int nbuf = (int)((200u << 10) / (unsigned)rowb);
+    nbuf = nbuf > 4 ? 4 : nbuf;
+    if (nbuf >= 2) {
+        const size_t smem = (size_t)nbuf * rowb + 64 * sizeof(float) + 16 * nbuf + 16;
+        static int set_dev = -1;
+        if (set_dev != ctx->device) {
+            RBK_CUDA(cudaFuncSetAttribute(xent_ring_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448));
+            set_dev = ctx->device;
+        }
+        const int rgrid = N < ctx->num_sms ? N : ctx->num_sms;
+        xent_ring_kernel<<<rgrid, kRingConsumers + 32, smem, st>>>((half*)dlogits, (const half*)logits, ld, targets,
+                                                                   N, V, scale, dscale, row_loss, nbuf, rowb,
+                                                                   ctx->tickets + kGemmError);
+        RBK_LAUNCHED("xent_ring_kernel");
+        return RBK_OK;
+    }
     xent_kernel<<<grid, kThreads, 0, st>>>((half*)dlogits, (const half*)logits, ld, targets, N, V, scale, dscale,
                                            row_loss);
     RBK_LAUNCHED("xent_kernel");
