@@ -299,14 +299,27 @@ __global__ void __launch_bounds__(544, 1)
         bool ok = true;
         int k = 0;
         const uint32_t ring = su32(lsm_raw);
+        // this team's row statistics are loaded one stage ahead, so their latency hides behind a stage
+        float nmr[R], nrr[R];
+        {
+            const int row0 = blockIdx.x * RS + team * R;
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                nmr[r] = row0 + r < N ? __ldg(mean + row0 + r) : 0.0f;
+                nrr[r] = row0 + r < N ? __ldg(rstd + row0 + r) : 0.0f;
+            }
+        }
         for (int gs = blockIdx.x; gs < nstage; gs += gridDim.x, ++k) {
             const int s = k % stages;
             const int row0 = gs * RS + team * R;
-            float mr[R], rr[R];                         // issued before the wait: their latency overlaps it
+            float mr[R], rr[R];
+            const int nrow0 = row0 + gridDim.x * RS;
 #pragma unroll
             for (int r = 0; r < R; ++r) {
-                mr[r] = row0 + r < N ? __ldg(mean + row0 + r) : 0.0f;
-                rr[r] = row0 + r < N ? __ldg(rstd + row0 + r) : 0.0f;
+                mr[r] = nmr[r];
+                rr[r] = nrr[r];
+                nmr[r] = nrow0 + r < N ? __ldg(mean + nrow0 + r) : 0.0f;
+                nrr[r] = nrow0 + r < N ? __ldg(rstd + nrow0 + r) : 0.0f;
             }
             ok = __all_sync(0xffffffffu, ok && mbar_wait(full(s), (k / stages) & 1, abort_flag));
             const uint32_t sb = ring + (uint32_t)(s * stage_bytes);
@@ -372,18 +385,17 @@ __global__ void __launch_bounds__(544, 1)
                     if (kRes) h8_to_f(lds128(sb + (uint32_t)((2 * RS + lr) * row_bytes + 16 * ttid)), rs);
                     const float inv = rr[r], m = mr[r];
                     const float t1 = ts[2 * r], t2 = ts[2 * r + 1];
-                    // exact: dx = inv * (dg - (t1 + xm * inv^2 * t2) / D); the reference formula has
-                    // inv instead of inv^2 (one rstd factor short)
-                    const float A = inv, C = -inv * t1 * invD;
-                    const float B = -(kRefFormula ? inv : inv * inv) * t2 * invD;   // multiplies xhat = xm * inv
+                    // exact: dx = inv * (dy g - (t1 + (x - m) * inv^2 * t2) / D); the reference formula
+                    // has inv instead of inv^2 (one rstd factor short).  Per row constants:
+                    // dx = (inv g) dy + Bx x + C
+                    const float Bx = -inv * (kRefFormula ? inv : inv * inv) * t2 * invD;
+                    const float C = -inv * t1 * invD - Bx * m;
 #pragma unroll
                     for (int j = 0; j < 8; ++j) {
-                        const float xh = (xx[j] - m) * inv;
-                        const float dg = d[j] * gam[j];
-                        float v = fmaf(B, xh, fmaf(A, dg, C));
+                        float v = fmaf(inv * gam[j], d[j], fmaf(Bx, xx[j], C));
                         if (kRes) v += rs[j];
                         o[j] = v;
-                        pg[j] = fmaf(d[j], xh, pg[j]);
+                        pg[j] = fmaf(d[j], (xx[j] - m) * inv, pg[j]);
                         pb[j] += d[j];
                         if (kBias) pd[j] += v;
                     }

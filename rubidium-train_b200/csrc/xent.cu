@@ -131,14 +131,14 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
 }
 
 // Ring kernel: shared memory = nbuf row buffers (rowb bytes each, V rounded up
-// to 8 halves), then per-row reduction scratch red[2][2][16] and barriers.
+// to 8 halves), then per-row reduction scratch red[2][2][32] and barriers.
 __global__ void __launch_bounds__(kRingConsumers + 32, 1)
     xent_ring_kernel(half* dl, const half* lg, int ld, const int* __restrict__ tgt, int N, int V, float scale,
                      const float* __restrict__ dscale, float* __restrict__ row_loss, int nbuf, int rowb, int* err) {
     using namespace tc;
     extern __shared__ __align__(128) uint8_t xs[];
-    float* red = reinterpret_cast<float*>(xs + (size_t)nbuf * rowb);   // [2 parity][2 (max, sum)][16 warps]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(red + 64);
+    float* red = reinterpret_cast<float*>(xs + (size_t)nbuf * rowb);   // [2 parity][2 (max, sum)][32]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(red + 128);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * nbuf);
     auto full = [&](int b) { return su32(bars + b); };
     auto empty = [&](int b) { return su32(bars + nbuf + b); };
@@ -178,7 +178,7 @@ __global__ void __launch_bounds__(kRingConsumers + 32, 1)
         const bool tvalid = t >= 0 && t < V;
         ok = __all_sync(0xffffffffu, ok && mbar_wait(full(b), (k / nbuf) & 1, abort_flag));
         const uint32_t rb = su32(xs + (size_t)b * rowb);
-        float* rr = red + (k & 1) * 32;
+        float* rr = red + (k & 1) * 64;
         const int full8 = V >> 3;                       // chunks without a tail
         // the target logit is read before pass 2 overwrites the staged row
         const float zt = (row_loss && tid == 0 && tvalid && ok)
@@ -202,9 +202,7 @@ __global__ void __launch_bounds__(kRingConsumers + 32, 1)
         m = warp_max(m);
         if (lane == 0) rr[warp] = m;
         named_sync(1, kRingConsumers);
-        m = rr[0];
-#pragma unroll
-        for (int w = 1; w < NW; ++w) m = fmaxf(m, rr[w]);
+        m = warp_max(lane < NW ? rr[lane] : -INFINITY);   // every warp folds the NW partials itself
         // pass 2: p = exp(z - max) (exp2 of the log2e-scaled difference), summed in FP32 and
         // written back over the staged row as FP16 (p <= 1) so pass 3 needs no second exp
         const float mb = m * kL2e;
@@ -228,11 +226,9 @@ __global__ void __launch_bounds__(kRingConsumers + 32, 1)
             }
         }
         sum = warp_sum(sum);
-        if (lane == 0) rr[NW + warp] = sum;
+        if (lane == 0) rr[32 + warp] = sum;
         named_sync(1, kRingConsumers);                  // also orders every thread's p stores before pass 3
-        sum = 0.0f;
-#pragma unroll
-        for (int w = 0; w < NW; ++w) sum += rr[NW + w];
+        sum = warp_sum(lane < NW ? rr[32 + lane] : 0.0f);
         const float inv = 1.0f / sum;
         if (row_loss && tid == 0) {
             float l = __int_as_float(0x7fc00000);       // NaN for an invalid target
@@ -246,9 +242,14 @@ __global__ void __launch_bounds__(kRingConsumers + 32, 1)
             for (int c = tid; c < nchunk; c += kRingConsumers) {
                 float f[8];
                 h8_to_f(lds128(rb + 16u * c), f);
-                const int tj = t - 8 * c;               // target column inside this chunk, if any
 #pragma unroll
-                for (int j = 0; j < 8; ++j) f[j] = fmaf(f[j], gi, j == tj ? -g : 0.0f);
+                for (int j = 0; j < 8; ++j) f[j] *= gi;
+                const int tj = t - 8 * c;               // the one chunk that holds the target
+                if ((unsigned)tj < 8u) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        if (j == tj) f[j] -= g;
+                }
                 if (c < full8) {
                     reinterpret_cast<uint4*>(d)[c] = f_to_h8(f);
                 } else {
@@ -290,7 +291,7 @@ extern "C" int rbk_softmax_xent_bwd(rbk_ctx* ctx, void* dlogits, const void* log
     int nbuf = (int)((200u << 10) / (unsigned)rowb);
     nbuf = nbuf > 4 ? 4 : nbuf;
     if (nbuf >= 2) {
-        const size_t smem = (size_t)nbuf * rowb + 64 * sizeof(float) + 16 * nbuf + 16;
+        const size_t smem = (size_t)nbuf * rowb + 128 * sizeof(float) + 16 * nbuf + 16;
         static int set_dev = -1;
         if (set_dev != ctx->device) {
             RBK_CUDA(cudaFuncSetAttribute(xent_ring_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448));
