@@ -1,6 +1,6 @@
 // xent.cu — fused softmax-cross-entropy forward + backward (HBM-bound).
 //
-// Rows that fit twice in shared memory (V up to ~50K FP16) take the ring
+// Rows that fit twice in shared memory (V up to ~56K FP16) take the ring
 // kernel: one persistent CTA per SM, a producer thread bulk-copies whole rows
 // into a 2-4 deep shared-memory ring, and 16 warps make three passes over the
 // staged row (max, sum of exp, gradient) — DRAM sees exactly one read and one
@@ -286,9 +286,9 @@ extern "C" int rbk_softmax_xent_bwd(rbk_ctx* ctx, void* dlogits, const void* log
     cudaStream_t st = as_stream(stream);
     ProfScope prof(ctx, st, kCatXent,
                    (double)N * V * (dlogits ? 4.0 : 2.0) + 4.0 * N + (row_loss ? 4.0 * N : 0.0));
-    // ring kernel when at least two rows fit in shared memory
+    // ring kernel when at least two rows fit in shared memory (two 50K-logit rows do)
     const int rowb = ((V + 7) / 8) * 16;
-    int nbuf = (int)((200u << 10) / (unsigned)rowb);
+    int nbuf = (int)((222u << 10) / (unsigned)rowb);
     nbuf = nbuf > 4 ? 4 : nbuf;
     if (nbuf >= 2) {
         const size_t smem = (size_t)nbuf * rowb + 128 * sizeof(float) + 16 * nbuf + 16;
