@@ -457,33 +457,54 @@ __global__ void __launch_bounds__(128) flash_bwd_kernel(half* __restrict__ dqkv,
 // (the tcgen05 path, whose main pass writes no bias terms) also
 // dbias[v block] += column sums of dO: sum_keys dV = sum_queries dO because
 // every row of P sums to 1 (the k block stays untouched: its gradient is 0).
-__global__ void flash_bwd_post_kernel(half* __restrict__ dqkv, float* __restrict__ dbias,
-                                      const float* __restrict__ dq_acc, const half* __restrict__ dO, int BS, int D,
-                                      int rows_per_block) {
-    const int c8 = blockIdx.x * blockDim.x + threadIdx.x;   // 8-column group
-    if (c8 * 8 >= D) return;
+// Block = 128 column groups of 8 x 4 row groups over rows_per_block rows; the
+// row groups fold in shared memory so each CTA adds one value per column.
+__global__ void __launch_bounds__(512) flash_bwd_post_kernel(half* __restrict__ dqkv, float* __restrict__ dbias,
+                                                             const float* __restrict__ dq_acc,
+                                                             const half* __restrict__ dO, int BS, int D,
+                                                             int rows_per_block) {
+    __shared__ float red[2][3][128][9];                 // [q|v][row groups 1..3][column group][8 (+1 pad)]
+    const int c8 = blockIdx.x * 128 + threadIdx.x;      // 8-column group
+    const bool col_ok = c8 * 8 < D;
     const int r0 = blockIdx.y * rows_per_block, r1 = min(BS, r0 + rows_per_block);
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0}, accv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int r = r0; r < r1; ++r) {
-        const float4* src = reinterpret_cast<const float4*>(dq_acc + (size_t)r * D + c8 * 8);
-        const float4 u = src[0], v = src[1];
-        float x[8] = {u.x, u.y, u.z, u.w, v.x, v.y, v.z, v.w};
+    if (col_ok) {
+#pragma unroll 4
+        for (int r = r0 + threadIdx.y; r < r1; r += 4) {
+            const float4* src = reinterpret_cast<const float4*>(dq_acc + (size_t)r * D + c8 * 8);
+            const float4 u = src[0], v = src[1];
+            float x[8] = {u.x, u.y, u.z, u.w, v.x, v.y, v.z, v.w};
 #pragma unroll
-        for (int k = 0; k < 8; ++k) acc[k] += x[k];
-        *reinterpret_cast<uint4*>(dqkv + (size_t)r * 3 * D + c8 * 8) = f_to_h8(x);
-        if (dO && dbias) {
-            float y[8];
-            h8_to_f(__ldg(reinterpret_cast<const uint4*>(dO + (size_t)r * D + c8 * 8)), y);
+            for (int k = 0; k < 8; ++k) acc[k] += x[k];
+            *reinterpret_cast<uint4*>(dqkv + (size_t)r * 3 * D + c8 * 8) = f_to_h8(x);
+            if (dO && dbias) {
+                float y[8];
+                h8_to_f(__ldg(reinterpret_cast<const uint4*>(dO + (size_t)r * D + c8 * 8)), y);
 #pragma unroll
-            for (int k = 0; k < 8; ++k) accv[k] += y[k];
+                for (int k = 0; k < 8; ++k) accv[k] += y[k];
+            }
         }
     }
-    if (dbias) {
+    if (!dbias) return;                                 // uniform across the CTA
+    if (threadIdx.y > 0) {
 #pragma unroll
-        for (int k = 0; k < 8; ++k) atomicAdd(dbias + c8 * 8 + k, acc[k]);
-        if (dO) {
+        for (int k = 0; k < 8; ++k) {
+            red[0][threadIdx.y - 1][threadIdx.x][k] = acc[k];
+            red[1][threadIdx.y - 1][threadIdx.x][k] = accv[k];
+        }
+    }
+    __syncthreads();
+    if (threadIdx.y == 0 && col_ok) {
 #pragma unroll
-            for (int k = 0; k < 8; ++k) atomicAdd(dbias + 2 * D + c8 * 8 + k, accv[k]);
+        for (int k = 0; k < 8; ++k) {
+            float q = acc[k], w = accv[k];
+#pragma unroll
+            for (int g = 0; g < 3; ++g) {
+                q += red[0][g][threadIdx.x][k];
+                w += red[1][g][threadIdx.x][k];
+            }
+            atomicAdd(dbias + c8 * 8 + k, q);
+            if (dO) atomicAdd(dbias + 2 * D + c8 * 8 + k, w);
         }
     }
 }
@@ -535,11 +556,12 @@ int bwd(rbk_ctx* ctx, void* dqkv, float* dbias, const void* qkv, const void* o, 
                                                       (const half*)dout, lse, Dot, S, H, scale, scale * kLog2e);
         RBK_LAUNCHED("flash_bwd_kernel");
     }
-    // enough CTAs to stream the FP32 accumulator at full bandwidth (>= 4 per SM)
-    const int rows_per_block = 32;
+    // 512-thread CTAs over 128 rows: enough in flight to stream the FP32 accumulator, and one
+    // bias atomic per column per CTA
+    const int rows_per_block = 128;
     dim3 pg((D / 8 + 127) / 128, (int)((BS + rows_per_block - 1) / rows_per_block));
-    flash_bwd_post_kernel<<<pg, 128, 0, st>>>((half*)dqkv, dbias, dq_acc, tc ? (const half*)dout : nullptr, (int)BS,
-                                              D, rows_per_block);
+    flash_bwd_post_kernel<<<pg, dim3(128, 4), 0, st>>>((half*)dqkv, dbias, dq_acc, tc ? (const half*)dout : nullptr,
+                                                       (int)BS, D, rows_per_block);
     RBK_LAUNCHED("flash_bwd_post_kernel");
     return RBK_OK;
 }

@@ -298,8 +298,13 @@ static int backward(rbk_model* m, const int* tokens, const int* targets, int B, 
     float* sk = a.sink;
     half* gcur = a.g0;
     half* gnext = a.g1;
+    // Bias gradients ride on the kernels that produce the bias's upstream gradient, so the W2, Wo
+    // and QKV weight gradients run on N = 256 tiles without the bias-gradient MMA: b2 of a layer
+    // is the column sum of the residual gradient the LayerNorm backward above it writes, bo the
+    // one LN2's backward writes, and bq|bk|bv come from the attention backward.
     RBK_TRY(rbk_ln_bwd(m->ctx, gcur, base ? m->w.g_ln_f_w : sk, base ? m->w.g_ln_f_b : sk + D,
-                       nullptr, a.dh, nullptr, a.x_out, m->w.ln_f_w, a.ln_f_mean, a.ln_f_inv_std, N, D, 0, st));
+                       base ? m->w.layers[L - 1].g_b2 : nullptr, a.dh, nullptr, a.x_out, m->w.ln_f_w, a.ln_f_mean,
+                       a.ln_f_inv_std, N, D, 0, st));
     if (m->dp.on) RBK_TRY(dp_unit_done(m, 0, st));
     for (int l = L - 1; l >= 0; --l) {
         LayerWeights& y = m->w.layers[l];
@@ -312,22 +317,22 @@ static int backward(rbk_model* m, const int* tokens, const int* targets, int B, 
             RBK_TRY(layer_attn_inputs(m, l, B, S, st));
         }
         // ---- FFN: x_out = x1 + gelu(h2 W1^T + b1) W2^T + b2 ----
-        if (base) RBK_TRY(g.wgrad(y.g_w2, y.g_b2, gcur, D, la.fi, F, N, F, D));
+        if (base) RBK_TRY(g.wgrad(y.g_w2, nullptr, gcur, D, la.fi, F, N, F, D));   // b2: see above
         RBK_TRY(g.dgrad(a.dpre, F, gcur, D, y.w2, N, F, D, la.fi_pre));
         if (base) RBK_TRY(g.wgrad(y.g_w1, y.g_b1, a.dpre, F, la.h2_checkpoint, D, N, D, F));
         RBK_TRY(g.dgrad(a.dh, D, a.dpre, F, y.w1, N, D, F));
         // ---- LN2: dx1 = g + LN2'(dh) ----
-        RBK_TRY(rbk_ln_bwd(m->ctx, gnext, base ? y.g_ln2_w : sk, base ? y.g_ln2_b : sk + D, nullptr,
+        RBK_TRY(rbk_ln_bwd(m->ctx, gnext, base ? y.g_ln2_w : sk, base ? y.g_ln2_b : sk + D, base ? y.g_bo : nullptr,
                            a.dh, gcur, la.x1_checkpoint, y.ln2_w, la.ln2_mean, la.ln2_inv_std, N, D, 0, st));
         std::swap(gcur, gnext);   // gcur = dx1
         // ---- attention output projection ----
-        if (base) RBK_TRY(g.wgrad(y.g_wo, y.g_bo, gcur, D, la.ao, D, N, D, D));
+        if (base) RBK_TRY(g.wgrad(y.g_wo, nullptr, gcur, D, la.ao, D, N, D, D));   // bo: from LN2's backward
         RBK_TRY(g.dgrad(a.dao, D, gcur, D, y.wo, N, D, D));
         // ---- attention core ----
-        RBK_TRY(rbk_attn_bwd(m->ctx, a.dqkv, nullptr, la.qkv, la.ao, a.dao, la.lse, B, S, H, m->cfg.hd,
-                             1.0f / sqrtf((float)m->cfg.hd), st));
+        RBK_TRY(rbk_attn_bwd(m->ctx, a.dqkv, base ? y.g_bq : nullptr, la.qkv, la.ao, a.dao, la.lse, B, S, H,
+                             m->cfg.hd, 1.0f / sqrtf((float)m->cfg.hd), st));
         // ---- QKV projection (one [3D, D] GEMM each way) ----
-        if (base) RBK_TRY(g.wgrad(y.g_wq, y.g_bq, a.dqkv, 3 * D, la.h1, D, N, D, 3 * D));
+        if (base) RBK_TRY(g.wgrad(y.g_wq, nullptr, a.dqkv, 3 * D, la.h1, D, N, D, 3 * D));   // bq|bk|bv: above
         RBK_TRY(g.dgrad(a.dh, D, a.dqkv, 3 * D, y.wq, N, D, 3 * D));
         if (m->lora.rank > 0) {
             LoraState& lo = m->lora;
@@ -353,8 +358,9 @@ static int backward(rbk_model* m, const int* tokens, const int* targets, int B, 
             }
         }
         // ---- LN1: g_prev = dx1 + LN1'(dh1) ----
-        RBK_TRY(rbk_ln_bwd(m->ctx, gnext, base ? y.g_ln1_w : sk, base ? y.g_ln1_b : sk + D, nullptr,
-                           a.dh, gcur, la.x_in, y.ln1_w, la.ln1_mean, la.ln1_inv_std, N, D, 0, st));
+        RBK_TRY(rbk_ln_bwd(m->ctx, gnext, base ? y.g_ln1_w : sk, base ? y.g_ln1_b : sk + D,
+                           base && l > 0 ? m->w.layers[l - 1].g_b2 : nullptr, a.dh, gcur, la.x_in, y.ln1_w,
+                           la.ln1_mean, la.ln1_inv_std, N, D, 0, st));
         std::swap(gcur, gnext);
         if (m->dp.on) RBK_TRY(dp_unit_done(m, L - l, st));
     }
