@@ -568,8 +568,8 @@ int bwd(rbk_ctx* ctx, void* dqkv, float* dbias, const void* qkv, const void* o, 
 
 }  // namespace attn
 
-// tcgen05 forward for d_head 64, S % 128 == 0 (attn_tc.cu).
-int attn_fwd_tc(rbk_ctx* ctx, void* o, float* lse, const void* qkv, int B, int S, int H, float scale,
+// tcgen05 forward for d_head 64 / 128, S % 128 == 0 (attn_tc.cu).
+int attn_fwd_tc(rbk_ctx* ctx, void* o, float* lse, const void* qkv, int B, int S, int H, int dh, float scale,
                 cudaStream_t st);
 
 }  // namespace rbk
@@ -596,8 +596,8 @@ int rbk_attn_fwd(rbk_ctx* ctx, void* o, float* lse, const void* qkv, int B, int 
     cudaStream_t st = as_stream(stream);
     // causal: QK^T and PV over S(S+1)/2 score entries per (b, h)
     ProfScope prof(ctx, st, kCatAttnFwd, 4.0 * B * H * ((double)S * (S + 1) / 2.0) * dh);
-    // tcgen05 kernel (attn_tc.cu) for d_head 64 and 128-multiple lengths
-    if (dh == 64 && S % 128 == 0 && !attn_legacy()) return attn_fwd_tc(ctx, o, lse, qkv, B, S, H, scale, st);
+    // tcgen05 kernel (attn_tc.cu) for 128-multiple lengths
+    if (S % 128 == 0 && !attn_legacy()) return attn_fwd_tc(ctx, o, lse, qkv, B, S, H, dh, scale, st);
     return dh == 64 ? attn::fwd<64>(ctx, o, lse, qkv, B, S, H, scale, st)
                     : attn::fwd<128>(ctx, o, lse, qkv, B, S, H, scale, st);
 }

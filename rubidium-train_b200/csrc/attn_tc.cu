@@ -1,9 +1,11 @@
 // attn_tc.cu — causal flash attention forward on the 5th-generation tensor
-// cores (d_head 64): the tcgen05 replacement of the mma.sync forward in
+// cores (d_head 64 or 128): the tcgen05 replacement of the mma.sync forward in
 // attn.cu for sequence lengths that are multiples of 128.
 //
-// One CTA = one (batch, head, 128-query block); two CTAs share an SM.  Keys
-// are consumed 64 at a time.  Roles (192 threads):
+// One CTA = one (batch, head, 128-query block); at d_head 64 two CTAs share an
+// SM.  Keys are consumed 64 at a time.  Q and K tiles are d_head/64 128B-swizzle
+// atoms wide (one TMA box each), V is d_head/64 MN-major column blocks, O is
+// d_head TMEM columns.  Roles (192 threads):
 //   warp 0     TMA: Q once (128 x 64 box), K through a 3-stage ring and V
 //              through a 2-stage ring (64 x 64 boxes), all from the fused
 //              q|k|v rows of the QKV projection
@@ -26,16 +28,22 @@ namespace attn_tc {
 
 using namespace tc;
 
-constexpr int BQ = 128, BKV = 64, HD = 64;
+constexpr int BQ = 128, BKV = 64;
 constexpr int kThreads = 192;
-constexpr int KS = 4, VS = 3;             // K / V ring depths
-constexpr int Q_BYTES = BQ * HD * 2;      // 16 KB
-constexpr int KV_BYTES = BKV * HD * 2;    // 8 KB
-constexpr int P_BYTES = BQ * BKV * 2;     // 16 KB: one 64-key K-major atom
-constexpr int OFF_Q = 0, OFF_K = OFF_Q + Q_BYTES, OFF_V = OFF_K + KS * KV_BYTES, OFF_P = OFF_V + VS * KV_BYTES;
-constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;   // P double-buffered
-constexpr int SMEM = 1024 + OFF_BAR + 256;
-constexpr uint32_t TMEM_COLS = 256;       // S0 [0, 64), S1 [64, 128), O [128, 192)
+template <int HD>
+struct FwdCfg {
+    static constexpr int NA = HD / 64;                  // 64-column atoms across d_head
+    static constexpr int KS = HD == 64 ? 4 : 3, VS = HD == 64 ? 3 : 3;   // K / V ring depths
+    static constexpr int Q_BYTES = BQ * HD * 2;         // NA atoms of 16 KB
+    static constexpr int KV_BYTES = BKV * HD * 2;       // NA atoms of 8 KB
+    static constexpr int P_BYTES = BQ * BKV * 2;        // 16 KB: one 64-key K-major atom
+    static constexpr int OFF_Q = 0, OFF_K = OFF_Q + Q_BYTES, OFF_V = OFF_K + KS * KV_BYTES,
+                         OFF_P = OFF_V + VS * KV_BYTES;
+    static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;   // P double-buffered
+    static constexpr int SMEM = 1024 + OFF_BAR + 256;
+    static constexpr int CTAS_PER_SM = HD == 64 ? 2 : 1;
+};
+constexpr uint32_t TMEM_COLS = 256;       // S0 [0, 64), S1 [64, 128), O [128, 128 + d_head)
 constexpr uint32_t O_COL = 128;
 
 __device__ __forceinline__ float ex2(float x) {
@@ -44,10 +52,14 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
-__global__ void __launch_bounds__(kThreads, 2) flash_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmq,
-                                                                    const __grid_constant__ CUtensorMap tmkv, half* O,
-                                                                    float* LSE, int S, int H, float scale_log2,
-                                                                    int* err) {
+template <int HD>
+__global__ void __launch_bounds__(kThreads, FwdCfg<HD>::CTAS_PER_SM)
+    flash_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmkv, half* O,
+                        float* LSE, int S, int H, float scale_log2, int* err) {
+    using Cf = FwdCfg<HD>;
+    constexpr int NA = Cf::NA, KS = Cf::KS, VS = Cf::VS, Q_BYTES = Cf::Q_BYTES, KV_BYTES = Cf::KV_BYTES,
+                  P_BYTES = Cf::P_BYTES, OFF_Q = Cf::OFF_Q, OFF_K = Cf::OFF_K, OFF_V = Cf::OFF_V, OFF_P = Cf::OFF_P,
+                  OFF_BAR = Cf::OFF_BAR;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = su32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -103,26 +115,31 @@ __global__ void __launch_bounds__(kThreads, 2) flash_fwd_tc_kernel(const __grid_
         // lane 0 streams Q then K, lane 16 streams V: the two rings refill independently
         if (lane == 0) {
             mbar_expect_tx(q_full, Q_BYTES);
-            tma_load_2d(sQ, &tmq, q_full, h * HD, row0 + qb * BQ);
+#pragma unroll
+            for (int a = 0; a < NA; ++a) tma_load_2d(sQ + a * (BQ * 128), &tmq, q_full, h * HD + 64 * a, row0 + qb * BQ);
             for (int j = 0; j < nkv; ++j) {
                 const int ks = j % KS;
                 if (!mbar_wait(k_empty(ks), ((j / KS) & 1) ^ 1, abort_flag)) break;
                 mbar_expect_tx(k_full(ks), KV_BYTES);
-                tma_load_2d(sK(ks), &tmkv, k_full(ks), D + h * HD, row0 + j * BKV);
+#pragma unroll
+                for (int a = 0; a < NA; ++a)
+                    tma_load_2d(sK(ks) + a * (BKV * 128), &tmkv, k_full(ks), D + h * HD + 64 * a, row0 + j * BKV);
             }
         } else if (lane == 16) {
             for (int j = 0; j < nkv; ++j) {
                 const int vs = j % VS;
                 if (!mbar_wait(v_empty(vs), ((j / VS) & 1) ^ 1, abort_flag)) break;
                 mbar_expect_tx(v_full(vs), KV_BYTES);
-                tma_load_2d(sV(vs), &tmkv, v_full(vs), 2 * D + h * HD, row0 + j * BKV);
+#pragma unroll
+                for (int a = 0; a < NA; ++a)
+                    tma_load_2d(sV(vs) + a * (BKV * 128), &tmkv, v_full(vs), 2 * D + h * HD + 64 * a, row0 + j * BKV);
             }
         }
     } else if (warp == 1) {
         // ---------------------------------------------------------- MMA ----
         if (lane == 0) {
             const uint32_t idesc_s = idesc_f16(BKV, 0, 0);   // Q (K-major) x K (K-major), N = 64
-            const uint32_t idesc_o = idesc_f16(HD, 0, 1);    // P (K-major) x V (MN-major), N = 64
+            const uint32_t idesc_o = idesc_f16(HD, 0, 1);    // P (K-major) x V (MN-major), N = d_head
             const uint32_t o_tm = tmem + O_COL;
             auto issue_s = [&](int j) -> bool {
                 const int ks = j % KS;
@@ -130,8 +147,9 @@ __global__ void __launch_bounds__(kThreads, 2) flash_fwd_tc_kernel(const __grid_
                 fence_after();
                 const uint32_t s_tm = tmem + (uint32_t)(j & 1) * BKV;
 #pragma unroll
-                for (int k = 0; k < HD / 16; ++k)
-                    mma_f16(s_tm, sdesc(sQ + k * 32, 16, 1024), sdesc(sK(ks) + k * 32, 16, 1024), idesc_s, k > 0);
+                for (int k = 0; k < HD / 16; ++k)   // K = d_head: atom k / 4, 32 B per step inside it
+                    mma_f16(s_tm, sdesc(sQ + (k >> 2) * (BQ * 128) + (k & 3) * 32, 16, 1024),
+                            sdesc(sK(ks) + (k >> 2) * (BKV * 128) + (k & 3) * 32, 16, 1024), idesc_s, k > 0);
                 mma_commit(s_full(j & 1));
                 mma_commit(k_empty(ks));
                 return true;
@@ -145,7 +163,8 @@ __global__ void __launch_bounds__(kThreads, 2) flash_fwd_tc_kernel(const __grid_
                 fence_after();
 #pragma unroll
                 for (int k = 0; k < BKV / 16; ++k)
-                    mma_f16(o_tm, sdesc(sP(j & 1) + k * 32, 16, 1024), sdesc(sV(vs) + k * 2048, KV_BYTES, 1024),
+                    mma_f16(o_tm, sdesc(sP(j & 1) + k * 32, 16, 1024),
+                            sdesc(sV(vs) + k * 2048, BKV * 128, 1024),   // N blocks of 64 columns, 8 KB apart
                             idesc_o, (j > 0 || k > 0) ? 1u : 0u);
                 mma_commit(o_done(j & 1));
                 mma_commit(v_empty(vs));
@@ -258,9 +277,10 @@ __global__ void __launch_bounds__(kThreads, 2) flash_fwd_tc_kernel(const __grid_
 
 }  // namespace attn_tc
 
-// Used by rbk_attn_fwd (attn.cu) when d_head == 64 and S % 128 == 0.
-int attn_fwd_tc(rbk_ctx* ctx, void* o, float* lse, const void* qkv, int B, int S, int H, float scale,
-                cudaStream_t st) {
+// Used by rbk_attn_fwd (attn.cu) when d_head is 64 or 128 and S % 128 == 0.
+template <int HD>
+static int attn_fwd_tc_hd(rbk_ctx* ctx, void* o, float* lse, const void* qkv, int B, int S, int H, float scale,
+                          cudaStream_t st) {
     using namespace attn_tc;
     const int D = H * HD;
     CUtensorMap tmq, tmkv;
@@ -268,14 +288,21 @@ int attn_fwd_tc(rbk_ctx* ctx, void* o, float* lse, const void* qkv, int B, int S
     RBK_TRY(tc::make_tmap(&tmkv, qkv, 3 * (uint64_t)D, (uint64_t)B * S, 3 * (uint64_t)D, 64, BKV));
     static int set_dev = -1;
     if (set_dev != ctx->device) {
-        RBK_CUDA(cudaFuncSetAttribute(flash_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+        RBK_CUDA(cudaFuncSetAttribute(flash_fwd_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      FwdCfg<HD>::SMEM));
         set_dev = ctx->device;
     }
     dim3 grid(S / BQ, B * H);
-    flash_fwd_tc_kernel<<<grid, kThreads, SMEM, st>>>(tmq, tmkv, (half*)o, lse, S, H, scale * 1.4426950408889634f,
-                                                      ctx->tickets + kGemmError);
+    flash_fwd_tc_kernel<HD><<<grid, kThreads, FwdCfg<HD>::SMEM, st>>>(
+        tmq, tmkv, (half*)o, lse, S, H, scale * 1.4426950408889634f, ctx->tickets + kGemmError);
     RBK_LAUNCHED("flash_fwd_tc_kernel");
     return RBK_OK;
+}
+
+int attn_fwd_tc(rbk_ctx* ctx, void* o, float* lse, const void* qkv, int B, int S, int H, int dh, float scale,
+                cudaStream_t st) {
+    return dh == 64 ? attn_fwd_tc_hd<64>(ctx, o, lse, qkv, B, S, H, scale, st)
+                    : attn_fwd_tc_hd<128>(ctx, o, lse, qkv, B, S, H, scale, st);
 }
 
 }  // namespace rbk
