@@ -198,6 +198,8 @@ __global__ void __launch_bounds__(512) ln_bwd_kernel(half* __restrict__ dx, floa
 __global__ void __launch_bounds__(1024) ln_bwd_reduce_kernel(float* __restrict__ dg, float* __restrict__ db,
                                                              float* __restrict__ dbias,
                                                              const float* __restrict__ part, int nblk, int D) {
+    // launched as a programmatic dependent of the main pass: wait for its partials
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     __shared__ float s[32][33];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int c = blockIdx.x * 32 + lane;
@@ -427,6 +429,8 @@ __global__ void __launch_bounds__(544, 1)
         for (int t = 0; t < teams; ++t) v += tpart[(size_t)t * 3 * D + i];
         part[(size_t)blockIdx.x * 3 * D + i] = v;
     }
+    // the column reduce may start launching (it waits for this grid's memory before reading)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 template <bool A, bool B, bool C>
@@ -542,8 +546,20 @@ int rbk_ln_bwd(rbk_ctx* ctx, void* dx, float* dgamma, float* dbeta, float* dbias
     }
 #undef RBK_LN_BWD
     RBK_LAUNCHED("ln_bwd_ring_kernel");
-    dim3 rg((D + 31) / 32, bias ? 3 : 2);
-    ln_bwd_reduce_kernel<<<rg, 1024, 0, st>>>(dgamma, dbeta, dbias_out, part, blocks, D);
+    {
+        // programmatic dependent launch: the reduce's launch overlaps the main pass's tail
+        cudaLaunchConfig_t lc = {};
+        lc.gridDim = dim3((D + 31) / 32, bias ? 3 : 2);
+        lc.blockDim = dim3(1024);
+        lc.stream = st;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[0].val.programmaticStreamSerializationAllowed = 1;
+        lc.attrs = at;
+        lc.numAttrs = 1;
+        const float* cpart = part;
+        RBK_CUDA(cudaLaunchKernelEx(&lc, ln_bwd_reduce_kernel, dgamma, dbeta, dbias_out, cpart, blocks, D));
+    }
     RBK_LAUNCHED("ln_bwd_reduce_kernel");
     return RBK_OK;
 }

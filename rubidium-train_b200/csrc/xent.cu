@@ -2,10 +2,10 @@
 //
 // Rows that fit twice in shared memory (V up to ~56K FP16) take the ring
 // kernel: one persistent CTA per SM, a producer thread bulk-copies whole rows
-// into a 2-4 deep shared-memory ring, and 16 warps make three passes over the
-// staged row (max, sum of exp, gradient) — DRAM sees exactly one read and one
-// write per logit, in place if the caller wishes, with the next rows already
-// in flight.  Wider rows take the streaming kernel: pass 1 reads the row once
+// into a 2-4 deep shared-memory ring, and two groups of 8 warps (alternate
+// rows) make three passes over each staged row (max, sum of exp, gradient) —
+// DRAM sees exactly one read and one write per logit, in place if the caller
+// wishes, with the next rows already in flight.  Wider rows take the streaming kernel: pass 1 reads the row once
 // with 16-byte loads and keeps an online (max, sum of exp) per thread; pass 2
 // re-reads it from L2 (rows in flight are capped well below the 126 MB L2)
 // and writes the gradient.  The reference instead rescans the whole row for
@@ -131,14 +131,14 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
 }
 
 // Ring kernel: shared memory = nbuf row buffers (rowb bytes each, V rounded up
-// to 8 halves), then per-row reduction scratch red[2][2][32] and barriers.
+// to 8 halves), then per-row reduction scratch red[2][2][2][32] and barriers.
 __global__ void __launch_bounds__(kRingConsumers + 32, 1)
     xent_ring_kernel(half* dl, const half* lg, int ld, const int* __restrict__ tgt, int N, int V, float scale,
                      const float* __restrict__ dscale, float* __restrict__ row_loss, int nbuf, int rowb, int* err) {
     using namespace tc;
     extern __shared__ __align__(128) uint8_t xs[];
-    float* red = reinterpret_cast<float*>(xs + (size_t)nbuf * rowb);   // [2 parity][2 (max, sum)][32]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(red + 128);
+    float* red = reinterpret_cast<float*>(xs + (size_t)nbuf * rowb);   // [2 groups][2 parity][2 (max, sum)][32]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(red + 256);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * nbuf);
     auto full = [&](int b) { return su32(bars + b); };
     auto empty = [&](int b) { return su32(bars + nbuf + b); };
@@ -147,7 +147,7 @@ __global__ void __launch_bounds__(kRingConsumers + 32, 1)
     if (tid == 0) {
         for (int b = 0; b < nbuf; ++b) {
             mbar_init(full(b), 1);
-            mbar_init(empty(b), NW);
+            mbar_init(empty(b), NW / 2);                 // the 8 warps of the group that took the row
         }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -168,26 +168,32 @@ __global__ void __launch_bounds__(kRingConsumers + 32, 1)
         return;
     }
     // ---------------------------------------------------------- consumers ----
+    // two groups of 8 warps take alternate rows: each row's passes and barriers involve half the
+    // CTA, and the two groups' rows overlap
     const float gs = scale * (dscale ? __ldg(dscale) : 1.0f);
     constexpr float kL2e = 1.4426950408889634f;
+    constexpr int GT = kRingConsumers / 2, GW = GT / 32;   // threads / warps per group
+    const int grp = warp / GW, gtid = tid - grp * GT;
     bool ok = true;
-    int k = 0;
+    int k = 0, kk = 0;
     for (int row = blockIdx.x; row < N; row += gridDim.x, ++k) {
+        if ((k & 1) != grp) continue;
         const int b = k % nbuf;
         const int t = __ldg(tgt + row);
         const bool tvalid = t >= 0 && t < V;
         ok = __all_sync(0xffffffffu, ok && mbar_wait(full(b), (k / nbuf) & 1, abort_flag));
         const uint32_t rb = su32(xs + (size_t)b * rowb);
-        float* rr = red + (k & 1) * 64;
+        float* rr = red + (grp * 2 + (kk & 1)) * 64;
+        ++kk;
         const int full8 = V >> 3;                       // chunks without a tail
         // the target logit is read before pass 2 overwrites the staged row
-        const float zt = (row_loss && tid == 0 && tvalid && ok)
+        const float zt = (row_loss && gtid == 0 && tvalid && ok)
                              ? __half2float(reinterpret_cast<const half*>(xs + (size_t)b * rowb)[t])
                              : 0.0f;
         // pass 1: row max
         float m = -INFINITY;
         if (ok) {
-            for (int c = tid; c < nchunk; c += kRingConsumers) {
+            for (int c = gtid; c < nchunk; c += GT) {
                 float f[8];
                 h8_to_f(lds128(rb + 16u * c), f);
                 if (c < full8) {
@@ -200,15 +206,15 @@ __global__ void __launch_bounds__(kRingConsumers + 32, 1)
             }
         }
         m = warp_max(m);
-        if (lane == 0) rr[warp] = m;
-        named_sync(1, kRingConsumers);
-        m = warp_max(lane < NW ? rr[lane] : -INFINITY);   // every warp folds the NW partials itself
+        if (lane == 0) rr[warp - grp * GW] = m;
+        named_sync(1 + grp, GT);
+        m = warp_max(lane < GW ? rr[lane] : -INFINITY);   // every warp folds the group's partials
         // pass 2: p = exp(z - max) (exp2 of the log2e-scaled difference), summed in FP32 and
         // written back over the staged row as FP16 (p <= 1) so pass 3 needs no second exp
         const float mb = m * kL2e;
         float sum = 0.0f;
         if (ok) {
-            for (int c = tid; c < nchunk; c += kRingConsumers) {
+            for (int c = gtid; c < nchunk; c += GT) {
                 float f[8];
                 h8_to_f(lds128(rb + 16u * c), f);
 #pragma unroll
@@ -226,11 +232,11 @@ __global__ void __launch_bounds__(kRingConsumers + 32, 1)
             }
         }
         sum = warp_sum(sum);
-        if (lane == 0) rr[32 + warp] = sum;
-        named_sync(1, kRingConsumers);                  // also orders every thread's p stores before pass 3
-        sum = warp_sum(lane < NW ? rr[32 + lane] : 0.0f);
+        if (lane == 0) rr[32 + warp - grp * GW] = sum;
+        named_sync(1 + grp, GT);                        // also orders the group's p stores before pass 3
+        sum = warp_sum(lane < GW ? rr[32 + lane] : 0.0f);
         const float inv = 1.0f / sum;
-        if (row_loss && tid == 0) {
+        if (row_loss && gtid == 0) {
             float l = __int_as_float(0x7fc00000);       // NaN for an invalid target
             if (tvalid) l = -logf(ex2(fmaf(zt, kL2e, -mb)) * inv + 1e-10f);
             row_loss[row] = l;
@@ -239,7 +245,7 @@ __global__ void __launch_bounds__(kRingConsumers + 32, 1)
         if (dl && ok) {
             const float g = tvalid ? gs : 0.0f, gi = g * inv;
             half* d = dl + (size_t)row * ld;
-            for (int c = tid; c < nchunk; c += kRingConsumers) {
+            for (int c = gtid; c < nchunk; c += GT) {
                 float f[8];
                 h8_to_f(lds128(rb + 16u * c), f);
 #pragma unroll
@@ -291,7 +297,7 @@ extern "C" int rbk_softmax_xent_bwd(rbk_ctx* ctx, void* dlogits, const void* log
     int nbuf = (int)((222u << 10) / (unsigned)rowb);
     nbuf = nbuf > 4 ? 4 : nbuf;
     if (nbuf >= 2) {
-        const size_t smem = (size_t)nbuf * rowb + 128 * sizeof(float) + 16 * nbuf + 16;
+        const size_t smem = (size_t)nbuf * rowb + 256 * sizeof(float) + 16 * nbuf + 16;
         static int set_dev = -1;
         if (set_dev != ctx->device) {
             RBK_CUDA(cudaFuncSetAttribute(xent_ring_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448));
