@@ -232,8 +232,9 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
 
 // ---------------------------------------------------------------------------
 // Backward with a bulk-copy ring.  Shared memory: stages x [dy | x | dres] row
-// blocks (RS = teams * kLnRows consecutive rows of D halves each, one bulk
-// copy per tensor), the teams' row-sum exchange red[teams][2][2 kLnRows][warps
+// blocks (kLnRows consecutive rows of D halves each, one bulk copy per tensor;
+// stage k belongs to team k % teams, so teams release their stages
+// independently), the teams' row-sum exchange red[teams][2][2 kLnRows][warps
 // per team], barriers; at the end the ring is reused for the teams' column
 // partials tpart[teams][3][D].
 // part (global) layout: [gridDim.x][3][D]  (dgamma | dbeta | dbias partials)
@@ -248,7 +249,7 @@ __global__ void __launch_bounds__(544, 1)
     static_assert(R == 4, "the row-sum butterfly below reduces 2 * 4 sums");
     constexpr int NT = kRes ? 3 : 2;
     extern __shared__ __align__(128) uint8_t lsm_raw[];
-    const int RS = teams * R;
+    const int RS = R;                                   // rows per stage: one team's rows
     const size_t row_bytes = (size_t)D * 2;
     const size_t stage_bytes = (size_t)RS * row_bytes * NT;
     const int wpt = tpt >> 5;
@@ -258,12 +259,11 @@ __global__ void __launch_bounds__(544, 1)
     auto full = [&](int s) { return su32(bars + s); };
     auto empty = [&](int s) { return su32(bars + stages + s); };
     const int consumers = teams * tpt;                  // consumer threads; one producer warp follows
-    const int nwc = consumers >> 5;
     const int tid = threadIdx.x, lane = tid & 31;
     if (tid == 0) {
         for (int s = 0; s < stages; ++s) {
             mbar_init(full(s), 1);
-            mbar_init(empty(s), nwc);
+            mbar_init(empty(s), tpt >> 5);              // the warps of the team that owns the stage
         }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -299,23 +299,24 @@ __global__ void __launch_bounds__(544, 1)
         for (int j = 0; j < 8; ++j) { pg[j] = 0.0f; pb[j] = 0.0f; pd[j] = 0.0f; gam[j] = 0.0f; }
         if (own) h8_to_f(__ldg(reinterpret_cast<const uint4*>(g) + ttid), gam);
         bool ok = true;
-        int k = 0;
         const uint32_t ring = su32(lsm_raw);
         // this team's row statistics are loaded one stage ahead, so their latency hides behind a stage
         float nmr[R], nrr[R];
         {
-            const int row0 = blockIdx.x * RS + team * R;
+            const int row0 = (blockIdx.x + team * gridDim.x) * RS;
 #pragma unroll
             for (int r = 0; r < R; ++r) {
                 nmr[r] = row0 + r < N ? __ldg(mean + row0 + r) : 0.0f;
                 nrr[r] = row0 + r < N ? __ldg(rstd + row0 + r) : 0.0f;
             }
         }
-        for (int gs = blockIdx.x; gs < nstage; gs += gridDim.x, ++k) {
+        int it = 0;
+        for (int k = team; blockIdx.x + k * gridDim.x < nstage; k += teams, ++it) {
+            const int gs = blockIdx.x + k * gridDim.x;
             const int s = k % stages;
-            const int row0 = gs * RS + team * R;
+            const int row0 = gs * RS;
             float mr[R], rr[R];
-            const int nrow0 = row0 + gridDim.x * RS;
+            const int nrow0 = (blockIdx.x + (k + teams) * gridDim.x) * RS;
 #pragma unroll
             for (int r = 0; r < R; ++r) {
                 mr[r] = nmr[r];
@@ -329,7 +330,7 @@ __global__ void __launch_bounds__(544, 1)
             float v8[2 * R];
 #pragma unroll
             for (int r = 0; r < R; ++r) {
-                const int lr = team * R + r;            // row inside the block
+                const int lr = r;                       // row inside the stage
                 float s1 = 0.0f, s2 = 0.0f;
                 if (ok && own && row0 + r < N) {
                     float d[8], xx[8];
@@ -365,7 +366,7 @@ __global__ void __launch_bounds__(544, 1)
                 tot += __shfl_xor_sync(0xffffffffu, tot, 2);
                 tot += __shfl_xor_sync(0xffffffffu, tot, 1);
             }
-            float* rb = red + ((size_t)team * 2 + (k & 1)) * 2 * R * wpt;
+            float* rb = red + ((size_t)team * 2 + (it & 1)) * 2 * R * wpt;
             if ((lane & 3) == 0) rb[((lane >> 2) & 7) * wpt + twarp] = tot;
             named_sync(1 + team, tpt);                  // this team's warps only
             // lane q < 8 adds the team's warps for sum q; shuffles hand every lane all 8 totals
@@ -378,7 +379,7 @@ __global__ void __launch_bounds__(544, 1)
             // pass 2: dx = A * dy*g + B * xhat + C per row, column partials
 #pragma unroll
             for (int r = 0; r < R; ++r) {
-                const int lr = team * R + r;
+                const int lr = r;
                 const int row = row0 + r;
                 if (ok && own && row < N) {
                     float d[8], xx[8], o[8], rs[8];
@@ -509,10 +510,10 @@ int rbk_ln_bwd(rbk_ctx* ctx, void* dx, float* dgamma, float* dbeta, float* dbias
     int teams = 512 / tpt;
     teams = teams < 1 ? 1 : teams > kLnMaxTeams ? kLnMaxTeams : teams;
     const int threads = teams * tpt + 32;                // + the producer warp
-    const int RS = teams * kLnRows;                      // rows per ring stage
+    const int RS = kLnRows;                              // rows per ring stage (one team's)
     const size_t stage_bytes = (size_t)RS * D * 2 * (dres ? 3 : 2);
     int stages = (int)((200u << 10) / stage_bytes);
-    stages = stages > 4 ? 4 : stages;
+    stages = stages > 16 ? 16 : stages;
     RBK_REQUIRE(stages >= 2, "rbk_ln_bwd: row blocks too large for the shared-memory ring (D=%d)", D);
     const size_t smem = stages * stage_bytes + sizeof(float) * (size_t)teams * 2 * 2 * kLnRows * (tpt / 32) +
                         16 * (size_t)stages + 16;
