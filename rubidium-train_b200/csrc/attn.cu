@@ -21,9 +21,9 @@
 
 namespace rbk {
 
-// tcgen05 main backward pass for d_head 64, S % 128 == 0 (attn_bwd_tc.cu).
+// tcgen05 main backward pass for d_head 64 / 128, S % 128 == 0 (attn_bwd_tc.cu).
 int attn_bwd_tc(rbk_ctx* ctx, void* dqkv, float* dq_acc, const void* qkv, const void* dout, const float* NL2,
-                const float* Dot, int B, int S, int H, float scale, cudaStream_t st);
+                const float* Dot, int B, int S, int H, int dh, float scale, cudaStream_t st);
 
 namespace attn {
 
@@ -543,7 +543,7 @@ int bwd(rbk_ctx* ctx, void* dqkv, float* dbias, const void* qkv, const void* o, 
         RBK_LAUNCHED("flash_bwd_pre_kernel");
     }
     if (tc) {
-        RBK_TRY(attn_bwd_tc(ctx, dqkv, dq_acc, qkv, dout, NL2, Dot, B, S, H, scale, st));
+        RBK_TRY(attn_bwd_tc(ctx, dqkv, dq_acc, qkv, dout, NL2, Dot, B, S, H, HD, scale, st));
     } else {
         constexpr int SMEM = 6 * BLK * HD * 2 + BLK * BLK * 2 + 4 * BLK * 4;
         static int set_dev = -1;
@@ -611,9 +611,9 @@ int rbk_attn_bwd(rbk_ctx* ctx, void* dqkv, float* dbias_qkv, const void* qkv, co
     cudaStream_t st = as_stream(stream);
     // algorithmic: dV, dP, dQ, dK products over the causal triangle (score recompute excluded)
     ProfScope prof(ctx, st, kCatAttnBwd, 8.0 * B * H * ((double)S * (S + 1) / 2.0) * dh);
-    const bool tc = dh == 64 && S % 128 == 0 && !attn_legacy();
+    const bool tc = S % 128 == 0 && !attn_legacy();
     return dh == 64 ? attn::bwd<64>(ctx, dqkv, dbias_qkv, qkv, o, dout, lse, B, S, H, scale, tc, st)
-                    : attn::bwd<128>(ctx, dqkv, dbias_qkv, qkv, o, dout, lse, B, S, H, scale, false, st);
+                    : attn::bwd<128>(ctx, dqkv, dbias_qkv, qkv, o, dout, lse, B, S, H, scale, tc, st);
 }
 
 }  // extern "C"

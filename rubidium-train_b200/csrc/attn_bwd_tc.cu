@@ -1,5 +1,5 @@
 // attn_bwd_tc.cu — causal flash attention backward on the 5th-generation
-// tensor cores (d_head 64, sequence length a multiple of 128): the tcgen05
+// tensor cores (d_head 64 or 128, sequence length a multiple of 128): the tcgen05
 // replacement of the mma.sync main kernel in attn.cu.  The pre pass (Dot =
 // rowsum(dO * O), -LSE * log2 e, zeroed FP32 dQ accumulator) and the post pass
 // (dQ -> FP16, q- and v-bias column sums) are shared with the mma.sync path.
@@ -465,14 +465,400 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace attn_tc_bwd
 
-// Main pass of rbk_attn_bwd (attn.cu) when d_head == 64 and S % 128 == 0.
-// dq_acc: FP32 [B*S, H*64], zeroed; NL2 / Dot: [B*H, S].  Writes the k and v
+// ---------------------------------------------------------------------------
+// d_head 128.  The same work items and P / dS computation, but the d_head-64
+// TMEM map does not fit: dK and dV alone take 256 of the 512 columns.  So
+//   * S^T and dP^T are single-buffered (64 + 64 columns); the P / dS warps free
+//     them as soon as they have loaded them, and the consumer-side MMAs of the
+//     previous sub-tile keep the tensor pipe busy meanwhile;
+//   * dQ is produced transposed per 64-query sub-tile,
+//       dQ^T_i = K^T dS^T_i   (M = 128 = d_head, N = 64 queries, K = 128 keys),
+//     with K read MN-major and dS^T_i as the MN-major B operand: 64 columns;
+//   * P^T stays double-buffered in TMEM (2 x 32 columns of FP16 pairs).
+// TMEM: S^T 0, dP^T 64, P^T[2] 128/160, dQ^T 192, dK 256, dV 384.
+// Shared memory (one CTA per SM): K, V (single-buffered, 32 KB each), Q / dO
+// ring of 4 (16 KB each), dS^T[2] (16 KB each), the per-query rows.  The drain
+// warps hold one d_head column of dQ^T per thread and add it into the FP32
+// accumulator with red.global (a warp covers 32 consecutive columns of one
+// query row: one 128-byte line per instruction); dK and dV leave straight from
+// registers, one key row per thread.
+namespace attn_tc_bwd128 {
+
+using namespace tc;
+using attn_tc_bwd::ex2;
+using attn_tc_bwd::pack_h2;
+using attn_tc_bwd::st_shared_v4;
+using attn_tc_bwd::ld_shared_f4;
+using attn_tc_bwd::Item;
+using attn_tc_bwd::item_of;
+using attn_tc_bwd::Masked;
+using attn_tc_bwd::Plain;
+
+constexpr int BK = 128, BQ = 64, HD = 128;
+constexpr int QS = 4;                       // Q / dO ring depth
+constexpr int NE = 16;                      // P / dS warps
+constexpr int WE = 3;                       // first P / dS warp
+constexpr int WD = WE + NE;                 // first drain warp
+constexpr int kThreads = (WD + 4) * 32;
+constexpr int KT_BYTES = BK * HD * 2;       // 32 KB  K or V block (two 64-column atoms of 16 KB)
+constexpr int KA_BYTES = BK * 128;          // one atom of K / V
+constexpr int QT_BYTES = BQ * HD * 2;       // 16 KB  Q or dO sub-tile (two atoms of 8 KB)
+constexpr int QA_BYTES = BQ * 128;
+constexpr int PT_BYTES = BK * BQ * 2;       // 16 KB  dS^T sub-tile
+constexpr int ROW_BYTES = 2 * BQ * 4;       // -LSE log2e | Dot of one sub-tile
+constexpr int OFF_K = 0, OFF_V = OFF_K + KT_BYTES, OFF_Q = OFF_V + KT_BYTES, OFF_DO = OFF_Q + QS * QT_BYTES,
+              OFF_DS = OFF_DO + QS * QT_BYTES, OFF_ROW = OFF_DS + 2 * PT_BYTES, OFF_BAR = OFF_ROW + QS * ROW_BYTES;
+constexpr int NBARS = 2 * QS + 2 + 2 + 2 * 2 + 2 + 2;
+constexpr int SMEM_USED = OFF_BAR + NBARS * 8 + 16;
+constexpr int SMEM = 232448;                // the per-CTA maximum; the base must come 1024-aligned
+static_assert(SMEM_USED <= SMEM, "shared memory budget");
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t S_COL = 0, DP_COL = 64, P_COL = 128, DQ_COL = 192, DK_COL = 256, DV_COL = 384;
+
+__device__ __forceinline__ void red_add(float* p, float v) {
+    asm volatile("red.relaxed.gpu.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    flash_bwd_tc128_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmkv,
+                           const __grid_constant__ CUtensorMap tmdo, half* __restrict__ dqkv,
+                           float* __restrict__ dq_acc, const float* __restrict__ NL2, const float* __restrict__ Dot,
+                           int S, int H, int num_items, float scale, float scale_log2, int* err) {
+    extern __shared__ __align__(1024) uint8_t smem128[];
+    const uint32_t raw = su32(smem128);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    if (base - raw + SMEM_USED > (uint32_t)SMEM) {   // uniform: no smem, TMEM or barrier touched yet
+        if (threadIdx.x == 0) atomicExch(err, RBK_ERR_UNSUPPORTED);
+        return;
+    }
+    uint8_t* gbase = smem128 + (base - raw);
+    const uint32_t sK = base + OFF_K, sV = base + OFF_V;
+    auto sQ = [&](int s) { return base + OFF_Q + (uint32_t)s * QT_BYTES; };
+    auto sdO = [&](int s) { return base + OFF_DO + (uint32_t)s * QT_BYTES; };
+    auto sRow = [&](int s) { return base + OFF_ROW + (uint32_t)s * ROW_BYTES; };
+    auto sdS = [&](int s) { return base + OFF_DS + (uint32_t)s * PT_BYTES; };
+    const uint32_t bars = base + OFF_BAR;
+    auto q_full = [&](int s) { return bars + 8 * s; };
+    auto q_empty = [&](int s) { return bars + 8 * QS + 8 * s; };
+    const uint32_t b2 = bars + 16 * QS;
+    const uint32_t kv_full = b2, kv_empty = b2 + 8;     // K, V of the item / released by both issuers
+    const uint32_t s_full = b2 + 16, s_free = b2 + 24;  // S^T, dP^T in TMEM / loaded by the P / dS warps
+    auto p_full = [&](int s) { return b2 + 32 + 8 * s; };   // P^T_i in TMEM, dS^T_i in shared memory
+    auto p_free = [&](int s) { return b2 + 48 + 8 * s; };   // dV_i, dK_i, dQ^T_i done: buffers i & 1 reusable
+    const uint32_t dq_full = b2 + 64, dq_free = b2 + 72, acc_done = b2 + 80, acc_free = b2 + 88;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + OFF_BAR + NBARS * 8);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + OFF_BAR + NBARS * 8 + 8);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int BH = num_items / (S / BK);
+    const int D = H * HD;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < QS; ++s) {
+            mbar_init(q_full(s), 1);
+            mbar_init(q_empty(s), NE + 2);
+        }
+        mbar_init(kv_full, 1);
+        mbar_init(kv_empty, 2);
+        mbar_init(s_full, 1);
+        mbar_init(s_free, NE);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(p_full(s), NE);
+            mbar_init(p_free(s), 1);
+        }
+        mbar_init(dq_full, 1);
+        mbar_init(dq_free, 4);
+        mbar_init(acc_done, 1);
+        mbar_init(acc_free, 4);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0 && lane == 0) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmq) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmkv) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmdo) : "memory");
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------- TMA ----
+        if (lane == 0) {
+            int g = 0;
+            bool ok = true;
+            for (int t = 0, u = blockIdx.x; ok && u < num_items; ++t, u += gridDim.x) {
+                const Item it = item_of(u, BH, H, S);
+                if (!mbar_wait(kv_empty, (t & 1) ^ 1, abort_flag)) break;
+                mbar_expect_tx(kv_full, 2 * KT_BYTES);
+#pragma unroll
+                for (int a = 0; a < 2; ++a) {
+                    tma_load_2d(sK + a * KA_BYTES, &tmkv, kv_full, D + it.h * HD + 64 * a, it.krow0);
+                    tma_load_2d(sV + a * KA_BYTES, &tmkv, kv_full, 2 * D + it.h * HD + 64 * a, it.krow0);
+                }
+                const float* nl2 = NL2 + (size_t)it.bh * S + it.kb * BK;
+                const float* dot = Dot + (size_t)it.bh * S + it.kb * BK;
+                for (int i = 0; i < it.n; ++i, ++g) {
+                    const int s = g % QS;
+                    if (!mbar_wait(q_empty(s), ((g / QS) & 1) ^ 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t fb = q_full(s);
+                    mbar_expect_tx(fb, 2 * QT_BYTES + ROW_BYTES);
+#pragma unroll
+                    for (int a = 0; a < 2; ++a) {
+                        tma_load_2d(sQ(s) + a * QA_BYTES, &tmq, fb, it.h * HD + 64 * a, it.krow0 + i * BQ);
+                        tma_load_2d(sdO(s) + a * QA_BYTES, &tmdo, fb, it.h * HD + 64 * a, it.krow0 + i * BQ);
+                    }
+                    bulk_load(sRow(s), nl2 + i * BQ, BQ * 4, fb);
+                    bulk_load(sRow(s) + BQ * 4, dot + i * BQ, BQ * 4, fb);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------- MMA: S^T, dP^T producer ----
+        if (lane == 0) {
+            const uint32_t id_s = idesc_f16(BQ, 0, 0);    // K (K-major) x Q^T (K-major): N = 64 queries
+            int g = 0;
+            bool ok = true;
+            for (int t = 0, u = blockIdx.x; ok && u < num_items; ++t, u += gridDim.x) {
+                const int n = item_of(u, BH, H, S).n;
+                if (!mbar_wait(kv_full, t & 1, abort_flag)) break;
+                for (int i = 0; i < n; ++i, ++g) {
+                    const int s = g % QS;
+                    ok = mbar_wait(q_full(s), (g / QS) & 1, abort_flag) &&
+                         (g == 0 || mbar_wait(s_free, (g - 1) & 1, abort_flag));
+                    if (!ok) break;
+                    fence_after();
+#pragma unroll
+                    for (int k = 0; k < HD / 16; ++k)
+                        mma_f16(tmem + S_COL, sdesc(sK + (k >> 2) * KA_BYTES + (k & 3) * 32, 16, 1024),
+                                sdesc(sQ(s) + (k >> 2) * QA_BYTES + (k & 3) * 32, 16, 1024), id_s, k > 0);
+#pragma unroll
+                    for (int k = 0; k < HD / 16; ++k)
+                        mma_f16(tmem + DP_COL, sdesc(sV + (k >> 2) * KA_BYTES + (k & 3) * 32, 16, 1024),
+                                sdesc(sdO(s) + (k >> 2) * QA_BYTES + (k & 3) * 32, 16, 1024), id_s, k > 0);
+                    mma_commit(s_full);
+                    mma_commit(q_empty(s));
+                }
+                if (ok) mma_commit(kv_empty);
+            }
+        }
+    } else if (warp == 2) {
+        // ------------------------------------------- MMA: dQ^T, dV, dK consumer ----
+        if (lane == 0) {
+            const uint32_t id_kv = idesc_f16(HD, 0, 1);   // P^T (TMEM) / dS^T (K-major) x dO / Q (MN-major): N = 128
+            const uint32_t id_q = idesc_f16(BQ, 1, 1);    // K^T (MN-major) x dS^T (MN-major): N = 64 queries
+            int g = 0;
+            bool ok = true;
+            for (int t = 0, u = blockIdx.x; ok && u < num_items; ++t, u += gridDim.x) {
+                const int n = item_of(u, BH, H, S).n;
+                // K is an operand of dQ^T; the accumulators must have been read out for the previous item
+                ok = mbar_wait(kv_full, t & 1, abort_flag) && (t == 0 || mbar_wait(acc_free, (t - 1) & 1, abort_flag));
+                if (!ok) break;
+                for (int i = 0; i < n; ++i, ++g) {
+                    const int s = g % QS, pb = g & 1;
+                    ok = mbar_wait(p_full(pb), (g >> 1) & 1, abort_flag) &&
+                         (g == 0 || mbar_wait(dq_free, (g - 1) & 1, abort_flag));   // dQ^T_{g-1} read out
+                    if (!ok) break;
+                    fence_after();
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k)
+                        mma_f16(tmem + DQ_COL, sdesc(sK + k * 2048, KA_BYTES, 1024), sdesc(sdS(pb) + k * 2048, PT_BYTES, 1024),
+                                id_q, k > 0);
+                    mma_commit(dq_full);
+#pragma unroll
+                    for (int k = 0; k < BQ / 16; ++k)
+                        mma_f16_ts(tmem + DV_COL, tmem + P_COL + (uint32_t)(pb * 32 + k * 8),
+                                   sdesc(sdO(s) + k * 2048, QA_BYTES, 1024), id_kv, (i > 0 || k > 0) ? 1u : 0u);
+#pragma unroll
+                    for (int k = 0; k < BQ / 16; ++k)
+                        mma_f16(tmem + DK_COL, sdesc(sdS(pb) + k * 32, 16, 1024), sdesc(sQ(s) + k * 2048, QA_BYTES, 1024),
+                                id_kv, (i > 0 || k > 0) ? 1u : 0u);
+                    mma_commit(q_empty(s));
+                    mma_commit(p_free(pb));
+                }
+                if (ok) {
+                    mma_commit(acc_done);
+                    mma_commit(kv_empty);
+                }
+            }
+        }
+    } else if (warp < WD) {
+        // ------------------------------------------------------ P / dS ----
+        const int lg = warp & 3, quarter = (warp - WE) >> 2;
+        const int r = lg * 32 + lane;                         // key row inside the block
+        const uint32_t lane_off = (uint32_t)(lg * 32) << 16;
+        const int c0 = quarter * 16;                          // first query column of this warp
+        int g = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; ok && u < num_items; u += gridDim.x) {
+            const int n = item_of(u, BH, H, S).n;
+            for (int i = 0; i < n; ++i, ++g) {
+                const int s = g % QS, pb = g & 1;
+                ok = mbar_wait(s_full, g & 1, abort_flag) && mbar_wait(q_full(s), (g / QS) & 1, abort_flag);
+                if (!__all_sync(0xffffffffu, ok)) {
+                    ok = false;
+                    break;
+                }
+                fence_after();
+                uint32_t sr[16], dr[16];
+                tmem_ld16(tmem + lane_off + S_COL + c0, sr);
+                tmem_ld16(tmem + lane_off + DP_COL + c0, dr);
+                tmem_wait_ld();
+                fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(s_free);           // the producer may compute the next sub-tile
+                const uint32_t rowp = sRow(s);
+                uint32_t pk[8], dk[8];
+                auto compute = [&](auto masked) {
+                    const int lim = r - BQ * i - c0;
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        const float4 nl = ld_shared_f4(rowp + (uint32_t)(c0 + 4 * q4) * 4);
+                        const float4 dt = ld_shared_f4(rowp + BQ * 4 + (uint32_t)(c0 + 4 * q4) * 4);
+                        const float nlv[4] = {nl.x, nl.y, nl.z, nl.w}, dtv[4] = {dt.x, dt.y, dt.z, dt.w};
+                        float pv[4], dv[4];
+#pragma unroll
+                        for (int e4 = 0; e4 < 4; ++e4) {
+                            const int e = 4 * q4 + e4;
+                            float p = ex2(fmaf(__uint_as_float(sr[e]), scale_log2, nlv[e4]));
+                            if (decltype(masked)::value) p = e < lim ? 0.0f : p;
+                            pv[e4] = p;
+                            dv[e4] = p * (__uint_as_float(dr[e]) - dtv[e4]);
+                        }
+                        pk[2 * q4] = pack_h2(pv[0], pv[1]);
+                        pk[2 * q4 + 1] = pack_h2(pv[2], pv[3]);
+                        dk[2 * q4] = pack_h2(dv[0], dv[1]);
+                        dk[2 * q4 + 1] = pack_h2(dv[2], dv[3]);
+                    }
+                };
+                if (i < 2) compute(Masked{});
+                else compute(Plain{});
+                // P^T buffer pb and dS^T buffer pb were last read by the MMAs of sub-tile g - 2
+                ok = g < 2 || mbar_wait(p_free(pb), ((g >> 1) & 1) ^ 1, abort_flag);
+                if (!__all_sync(0xffffffffu, ok)) {
+                    ok = false;
+                    break;
+                }
+                fence_after();
+                tmem_st8(tmem + lane_off + P_COL + (uint32_t)(pb * 32 + quarter * 8), pk);
+                const uint32_t drow = sdS(pb) + (uint32_t)r * 128u;
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {                 // 16-byte chunk = 8 queries, 128B swizzle
+                    const uint32_t sw = (uint32_t)((((c0 >> 3) + c) ^ (r & 7)) << 4);
+                    st_shared_v4(drow + sw, dk[4 * c], dk[4 * c + 1], dk[4 * c + 2], dk[4 * c + 3]);
+                }
+                tmem_wait_st();
+                fence_proxy_async();
+                fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(p_full(pb));
+                    mbar_arrive(q_empty(s));
+                }
+            }
+        }
+    } else {
+        // ------------------------------------------- dQ drain, dK / dV out ----
+        const int lg = warp & 3;
+        const int r = lg * 32 + lane;                         // d_head column of dQ^T / key row of the item
+        const uint32_t lane_off = (uint32_t)(lg * 32) << 16;
+        int g = 0;
+        bool ok = true;
+        for (int t = 0, u = blockIdx.x; ok && u < num_items; ++t, u += gridDim.x) {
+            const Item it = item_of(u, BH, H, S);
+            for (int i = 0; i < it.n; ++i, ++g) {
+                ok = __all_sync(0xffffffffu, mbar_wait(dq_full, g & 1, abort_flag));
+                if (!ok) break;
+                fence_after();
+                float* dst = dq_acc + (size_t)(it.krow0 + i * BQ) * D + it.h * HD + r;
+#pragma unroll 1
+                for (int hc = 0; hc < 2; ++hc) {              // 32 queries at a time
+                    uint32_t a[32];
+                    tmem_ld32(tmem + lane_off + DQ_COL + hc * 32, a);
+                    tmem_wait_ld();
+                    if (hc == 1) {
+                        fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(dq_free);
+                    }
+#pragma unroll
+                    for (int c = 0; c < 32; ++c) red_add(dst + (size_t)(hc * 32 + c) * D, __uint_as_float(a[c]) * scale);
+                }
+            }
+            if (!ok) break;
+            // dK (scaled) and dV: TMEM -> FP16 -> global, one key row per thread
+            ok = __all_sync(0xffffffffu, mbar_wait(acc_done, t & 1, abort_flag));
+            if (!ok) break;
+            fence_after();
+            half* krow = dqkv + (size_t)(it.krow0 + r) * 3 * D + D + it.h * HD;
+#pragma unroll 1
+            for (int q = 0; q < 8; ++q) {                     // dK in 4 x 32 columns, then dV
+                const int tv = q >> 2, hc = q & 3;
+                uint32_t a[32];
+                tmem_ld32(tmem + lane_off + (tv ? DV_COL : DK_COL) + hc * 32, a);
+                tmem_wait_ld();
+                if (q == 7) {
+                    fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(acc_free);     // the next item may accumulate again
+                }
+                const float f = tv ? 1.0f : scale;
+                uint4* out = reinterpret_cast<uint4*>(krow + tv * D + hc * 32);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    uint4 w;
+                    w.x = pack_h2(__uint_as_float(a[8 * c + 0]) * f, __uint_as_float(a[8 * c + 1]) * f);
+                    w.y = pack_h2(__uint_as_float(a[8 * c + 2]) * f, __uint_as_float(a[8 * c + 3]) * f);
+                    w.z = pack_h2(__uint_as_float(a[8 * c + 4]) * f, __uint_as_float(a[8 * c + 5]) * f);
+                    w.w = pack_h2(__uint_as_float(a[8 * c + 6]) * f, __uint_as_float(a[8 * c + 7]) * f);
+                    out[c] = w;
+                }
+            }
+        }
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    if (threadIdx.x == 0 && *abort_flag) atomicExch(err, RBK_ERR_TIMEOUT);
+    if (warp == 1) tmem_free(tmem, TMEM_COLS);
+}
+
+}  // namespace attn_tc_bwd128
+
+// Main pass of rbk_attn_bwd (attn.cu) when d_head is 64 or 128 and S % 128 == 0.
+// dq_acc: FP32 [B*S, H*dh], zeroed; NL2 / Dot: [B*H, S].  Writes the k and v
 // sections of dqkv and adds dQ into dq_acc.
 int attn_bwd_tc(rbk_ctx* ctx, void* dqkv, float* dq_acc, const void* qkv, const void* dout, const float* NL2,
-                const float* Dot, int B, int S, int H, float scale, cudaStream_t st) {
+                const float* Dot, int B, int S, int H, int dh, float scale, cudaStream_t st) {
+    const uint64_t BS = (uint64_t)B * S;
+    const int items = B * H * (S / 128);
+    const int grid = items < ctx->num_sms ? items : ctx->num_sms;
+    if (dh == 128) {
+        using namespace attn_tc_bwd128;
+        const int D = H * HD;
+        CUtensorMap tmq, tmkv, tmdo;
+        RBK_TRY(tc::make_tmap(&tmq, qkv, 3 * (uint64_t)D, BS, 3 * (uint64_t)D, 64, BQ));
+        RBK_TRY(tc::make_tmap(&tmkv, qkv, 3 * (uint64_t)D, BS, 3 * (uint64_t)D, 64, BK));
+        RBK_TRY(tc::make_tmap(&tmdo, dout, (uint64_t)D, BS, (uint64_t)D, 64, BQ));
+        static int set_dev = -1;
+        if (set_dev != ctx->device) {
+            RBK_CUDA(cudaFuncSetAttribute(flash_bwd_tc128_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+            set_dev = ctx->device;
+        }
+        flash_bwd_tc128_kernel<<<grid, kThreads, SMEM, st>>>(tmq, tmkv, tmdo, (half*)dqkv, dq_acc, NL2, Dot, S, H,
+                                                             items, scale, scale * 1.4426950408889634f,
+                                                             ctx->tickets + kGemmError);
+        RBK_LAUNCHED("flash_bwd_tc128_kernel");
+        return RBK_OK;
+    }
+    if (dh != 64) return RBK_ERR_UNSUPPORTED;
     using namespace attn_tc_bwd;
     const int D = H * HD;
-    const uint64_t BS = (uint64_t)B * S;
     CUtensorMap tmq, tmkv, tmdo, tmdq, tmout;
     RBK_TRY(tc::make_tmap(&tmq, qkv, 3 * (uint64_t)D, BS, 3 * (uint64_t)D, 64, BQ));
     RBK_TRY(tc::make_tmap(&tmkv, qkv, 3 * (uint64_t)D, BS, 3 * (uint64_t)D, 64, BK));
@@ -484,8 +870,6 @@ int attn_bwd_tc(rbk_ctx* ctx, void* dqkv, float* dq_acc, const void* qkv, const 
         RBK_CUDA(cudaFuncSetAttribute(flash_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
         set_dev = ctx->device;
     }
-    const int items = B * H * (S / BK);
-    const int grid = items < ctx->num_sms ? items : ctx->num_sms;
     flash_bwd_tc_kernel<<<grid, kThreads, SMEM, st>>>(tmq, tmkv, tmdo, tmdq, tmout, NL2, Dot, S, H, items, scale,
                                                       scale * 1.4426950408889634f, ctx->tickets + kGemmError);
     RBK_LAUNCHED("flash_bwd_tc_kernel");
