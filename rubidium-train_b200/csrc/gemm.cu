@@ -438,6 +438,183 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS));
 }
 
+// ------------------------------------------------------------ CTA pairs ----
+// The same GEMM on CTA pairs (a 2-CTA cluster per pair of SMs): a pair tile is
+// 256 rows x 256 columns.  Each CTA stages its 128 rows of A and its 128
+// columns of B per k-block (32 KB a stage instead of 48 KB for a 1-CTA
+// 128 x 256 tile), and the even CTA issues tcgen05.mma.cta_group::2 with
+// M = 256, N = 256, which reads A and B from both CTAs' shared memory and
+// leaves each CTA's 128 accumulator rows in its own TMEM.  Per SM and k-step
+// the tensor pipe then needs 8 KB of operands from shared memory and 8 KB
+// written by TMA, against 12 + 12 KB on a 1-CTA N = 256 tile: the 1-CTA tile
+// is bound by shared-memory bandwidth, the pair tile is not.
+// Barriers: full[s] lives in the even CTA and counts the TMA bytes of both
+// CTAs; empty[s] and tfull[b] exist in both CTAs and get one commit each from
+// the MMA thread; tempty[b] lives in the even CTA and takes the arrivals of
+// both CTAs' epilogue warps.  Bounded waits as in gemm_kernel.
+constexpr int kPairStages = 6;
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const Params p) {
+    constexpr int BN = 256, HALF_N = 128;
+    constexpr int A_BYTES = BM * BK * 2, B_BYTES = HALF_N * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
+    constexpr int STAGES = kPairStages;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = su32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t* gbase = smem_raw + (base - raw);
+    const uint32_t sA0 = base;
+    const uint32_t epi_stage = base + STAGES * STAGE_BYTES;
+    const uint32_t bars = epi_stage + kEpiWarps * kStageBytes;
+    uint8_t* gbars = gbase + (bars - base);
+    auto full_bar = [&](int s) { return bars + 8u * s; };
+    auto empty_bar = [&](int s) { return bars + 8u * (STAGES + s); };
+    auto tfull_bar = [&](int b) { return bars + 8u * (2 * STAGES + b); };
+    auto tempty_bar = [&](int b) { return bars + 8u * (2 * STAGES + 2 + b); };
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbars + 8 * (2 * STAGES + 4));
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(gbars + 8 * (2 * STAGES + 4) + 8);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(tfull_bar(b), 1);
+            mbar_init(tempty_bar(b), 2 * kEpiWarps);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0 && lane == 0) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
+    }
+    if (warp == 1) tmem_alloc_pair(tmem_slot, 512);
+    fence_before();
+    __syncthreads();
+    cluster_sync();                                  // the peer's barriers are initialised
+    fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------ TMA producer (both CTAs) -------------
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            for (int u = pair; u < p.units && !*abort_flag; u += num_pairs) {
+                int mb, nb, kb0, kb1;
+                decode_unit(p, u, mb, nb, kb0, kb1);
+                const int m0 = mb * 2 * BM + (int)rank * BM, n0 = nb * BN + (int)rank * HALF_N;
+                bool ok = true;
+                for (int kb = kb0; kb < kb1; ++kb) {
+                    if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag)) { ok = false; break; }
+                    if (leader) mbar_expect_tx(full_bar(stage), 2 * STAGE_BYTES);
+                    const uint32_t fb = mapa_shared(full_bar(stage), 0);
+                    const uint32_t sa = sA0 + stage * STAGE_BYTES;
+                    const uint32_t sb = sa + A_BYTES;
+                    const int k0 = kb * BK;
+                    if (!p.a_mn) {
+                        tma_load_2d_pair(sa, &tmA, fb, k0, m0);
+                    } else {
+                        tma_load_2d_pair(sa, &tmA, fb, m0, k0);
+                        tma_load_2d_pair(sa + 8192, &tmA, fb, m0 + 64, k0);
+                    }
+                    if (!p.b_mn) {
+                        tma_load_2d_pair(sb, &tmB, fb, k0, n0);
+                    } else {
+                        tma_load_2d_pair(sb, &tmB, fb, n0, k0);
+                        tma_load_2d_pair(sb + 8192, &tmB, fb, n0 + 64, k0);
+                    }
+                    if (++stage == STAGES) { stage = 0; phase ^= 1; }
+                }
+                if (!ok) break;
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------ MMA issuer (even CTA) ----------------
+        if (leader && lane == 0) {
+            const uint32_t idesc = idesc_f16_m256(BN, p.a_mn, p.b_mn);
+            const uint32_t a_lbo = p.a_mn ? 8192u : 16u, b_lbo = p.b_mn ? 8192u : 16u;
+            const uint32_t a_kstep = p.a_mn ? 2048u : 32u, b_kstep = p.b_mn ? 2048u : 32u;
+            int stage = 0, buf = 0;
+            uint32_t phase = 0, bphase = 0;
+            for (int u = pair; u < p.units && !*abort_flag; u += num_pairs) {
+                int mb, nb, kb0, kb1;
+                decode_unit(p, u, mb, nb, kb0, kb1);
+                if (!mbar_wait(tempty_bar(buf), bphase ^ 1, abort_flag)) break;
+                fence_after();
+                const uint32_t dacc = tmem + buf * BN;
+                bool ok = true;
+                for (int kb = kb0; kb < kb1; ++kb) {
+                    if (!mbar_wait(full_bar(stage), phase, abort_flag)) { ok = false; break; }
+                    fence_after();
+                    const uint32_t sa = sA0 + stage * STAGE_BYTES;
+                    const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+                    for (int k = 0; k < BK / UMMA_K; ++k)
+                        mma_f16_pair(dacc, sdesc(sa + k * a_kstep, a_lbo, 1024), sdesc(sb + k * b_kstep, b_lbo, 1024),
+                                     idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+                    mma_commit_pair(empty_bar(stage));
+                    mma_commit_pair(mapa_shared(empty_bar(stage), 1));
+                    if (++stage == STAGES) { stage = 0; phase ^= 1; }
+                }
+                if (!ok) break;
+                mma_commit_pair(tfull_bar(buf));
+                mma_commit_pair(mapa_shared(tfull_bar(buf), 1));
+                if (++buf == 2) { buf = 0; bphase ^= 1; }
+            }
+        }
+    } else {
+        // ------------------------------ epilogue (both CTAs) -----------------
+        const int q = warp & 3;
+        const int half_id = (warp - 2) / 4;
+        constexpr int kChunks = BN / 32;
+        const int c0 = half_id * (kChunks / 2), c1 = half_id ? kChunks : kChunks / 2;
+        uint8_t* my_stage = gbase + (epi_stage - base) + (warp - 2) * kStageBytes;
+        int buf = 0;
+        uint32_t bphase = 0;
+        for (int u = pair; u < p.units; u += num_pairs) {
+            int mb, nb, kb0, kb1;
+            decode_unit(p, u, mb, nb, kb0, kb1);
+            const int m0 = mb * 2 * BM + (int)rank * BM + q * 32;
+            constexpr bool kAux = EPI == RBK_EPI_STORE_F16 || EPI == RBK_EPI_BIAS_GELU || EPI == RBK_EPI_GELU_BWD;
+            const int lda = p.ld_aux ? p.ld_aux : p.ldc;
+            uint4 pf[4];
+            if (kAux && p.aux) prefetch_h(pf, p.aux, lda, m0, nb * BN + c0 * 32, p, lane);
+            if (!mbar_wait(tfull_bar(buf), bphase, abort_flag)) break;
+            fence_after();
+            const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + buf * BN;
+#pragma unroll 1
+            for (int c = c0; c < c1; ++c) {
+                uint32_t r[32];
+                tmem_ld32(tbase + c * 32, r);
+                uint4 cur[4] = {pf[0], pf[1], pf[2], pf[3]};
+                if (kAux && p.aux && c + 1 < c1) prefetch_h(pf, p.aux, lda, m0, nb * BN + (c + 1) * 32, p, lane);
+                tmem_wait_ld();
+                epilogue_chunk<EPI>(p, m0, nb * BN + c * 32, r, my_stage, lane, cur);
+            }
+            fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(buf), 0));
+            if (++buf == 2) { buf = 0; bphase ^= 1; }
+        }
+    }
+
+    fence_before();
+    __syncthreads();
+    cluster_sync();                                  // no remote arrival or commit is still in flight
+    fence_after();
+    if (threadIdx.x == 0 && *abort_flag) atomicExch(p.err, RBK_ERR_TIMEOUT);
+    if (warp == 1) tmem_free_pair(tmem, 512);
+}
+
 // ------------------------------------------------------------------- host ----
 template <int BN, int EPI>
 int launch(rbk_ctx* ctx, const rbk_gemm_desc* d, Params& p, cudaStream_t st) {
@@ -456,6 +633,52 @@ int launch(rbk_ctx* ctx, const rbk_gemm_desc* d, Params& p, cudaStream_t st) {
     gemm_kernel<BN, EPI><<<grid, kThreads, C::SMEM, st>>>(ta, tb, p);
     RBK_LAUNCHED("gemm_kernel");
     return RBK_OK;
+}
+
+// Launched as 2-CTA clusters; grid = 2 x min(units, pairs that fit at once).
+template <int EPI>
+int launch_pair(rbk_ctx* ctx, const rbk_gemm_desc* d, Params& p, cudaStream_t st) {
+    constexpr int SMEM = 1024 + kPairStages * (BM * BK * 2 + 128 * BK * 2) + kEpiWarps * kStageBytes + 256;
+    static_assert(SMEM <= 232448, "shared memory budget");
+    CUtensorMap ta, tb;
+    if (!d->a_major) RBK_TRY(make_tmap(&ta, d->A, d->K, d->M, d->lda, 64, 128));
+    else RBK_TRY(make_tmap(&ta, d->A, d->M, d->K, d->lda, 64, 64));
+    if (!d->b_major) RBK_TRY(make_tmap(&tb, d->B, d->K, d->N, d->ldb, 64, 128));
+    else RBK_TRY(make_tmap(&tb, d->B, d->N, d->K, d->ldb, 64, 64));
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = SMEM;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    static int configured_device = -1, max_pairs = 0;
+    if (configured_device != ctx->device) {
+        RBK_CUDA(cudaFuncSetAttribute(gemm_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+        cfg.gridDim = dim3(ctx->num_sms & ~1);
+        int n = 0;
+        RBK_CUDA(cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<EPI>, &cfg));
+        max_pairs = n > 0 ? n : ctx->num_sms / 2;
+        configured_device = ctx->device;
+    }
+    const int pairs = p.units < max_pairs ? p.units : max_pairs;
+    cfg.gridDim = dim3(2 * pairs);
+    RBK_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<EPI>, ta, tb, p));
+    RBK_LAUNCHED("gemm_pair_kernel");
+    return RBK_OK;
+}
+
+// CTA pairs unless RBK_GEMM_SINGLE=1 (the 1-CTA kernel for every N = 256 problem).
+static bool pair_tiles() {
+    static const int v = [] {
+        const char* e = getenv("RBK_GEMM_SINGLE");
+        return (e && e[0] == '1') ? 0 : 1;
+    }();
+    return v != 0;
 }
 
 }  // namespace gemm
@@ -489,9 +712,12 @@ int rbk_gemm(rbk_ctx* ctx, const rbk_gemm_desc* d, void* stream) {
         BN = d->N <= 128 ? 128 : (d->dbias_rows || d->N < 256) ? 192 : 256;
     else
         BN = d->N >= 512 ? 256 : 128;
+    // N = 256 problems run on CTA pairs (256 x 256 pair tiles)
+    const bool pair = BN == 256 && pair_tiles();
+    const int slots = pair ? ctx->num_sms / 2 : ctx->num_sms;
     Params p;
     p.M = d->M; p.N = d->N; p.K = d->K;
-    p.m_blocks = (d->M + BM - 1) / BM;
+    p.m_blocks = (d->M + (pair ? 2 * BM : BM) - 1) / (pair ? 2 * BM : BM);
     p.n_blocks = (d->N + BN - 1) / BN;
     p.k_blocks = (d->K + BK - 1) / BK;
     int splits = 1;
@@ -509,8 +735,8 @@ int rbk_gemm(rbk_ctx* ctx, const rbk_gemm_desc* d, void* stream) {
                 const int kbps = (p.k_blocks + s - 1) / s;
                 const int real = (p.k_blocks + kbps - 1) / kbps;
                 const long units = (long)tiles * real;
-                const long waves = (units + ctx->num_sms - 1) / ctx->num_sms;
-                const double eff = (double)units / (double)(waves * ctx->num_sms);
+                const long waves = (units + slots - 1) / slots;
+                const double eff = (double)units / (double)(waves * slots);
                 if (eff > best + 1e-9) { best = eff; splits = s; }
                 if (eff >= 0.9) break;
             }
@@ -533,6 +759,15 @@ int rbk_gemm(rbk_ctx* ctx, const rbk_gemm_desc* d, void* stream) {
     p.err = ctx->tickets + kGemmError;
     cudaStream_t st = as_stream(stream);
     ProfScope prof(ctx, st, kCatGemm, 2.0 * d->M * (double)d->N * d->K);
+    if (pair) {
+        switch (epi) {
+            case RBK_EPI_STORE_F16: return launch_pair<RBK_EPI_STORE_F16>(ctx, d, p, st);
+            case RBK_EPI_BIAS_GELU: return launch_pair<RBK_EPI_BIAS_GELU>(ctx, d, p, st);
+            case RBK_EPI_GELU_BWD: return launch_pair<RBK_EPI_GELU_BWD>(ctx, d, p, st);
+            case RBK_EPI_ACC_F32: return launch_pair<RBK_EPI_ACC_F32>(ctx, d, p, st);
+            default: return launch_pair<RBK_EPI_STORE_F32>(ctx, d, p, st);
+        }
+    }
     if (BN == 256) {
         switch (epi) {
             case RBK_EPI_STORE_F16: return launch<256, RBK_EPI_STORE_F16>(ctx, d, p, st);

@@ -290,6 +290,9 @@ def _mk(rng, rows, cols, ld=None):
     (256, 640, 128, 0, 0),     # BN=256 path
     (384, 1024, 320, 0, 1),    # BN=256 with MN-major B
     (128, 512, 64, 1, 0),      # A MN-major, BN=256
+    (300, 640, 256, 0, 0),     # CTA-pair tiles: last pair row half outside M
+    (200, 520, 136, 0, 1),     # CTA-pair tiles: ragged N, the odd CTA's columns wholly outside N
+    (100, 512, 64, 1, 1),      # CTA-pair tiles: the odd CTA's rows wholly outside M, both MN-major
 ])
 def test_gemm_store(ops, M, N, K, a_major, b_major):
     rng = np.random.default_rng(M * 7 + N + K)
@@ -351,3 +354,17 @@ def test_gemm_wgrad_with_bias_grad(ops, Ntok, fin, out):
     ref = dW0 + dY.astype(np.float64).T @ X.astype(np.float64)
     assert rel(dW.cpu().numpy(), ref) < F32_TOL
     assert rel(db.cpu().numpy(), db0 + dY.astype(np.float64).sum(0)) < F32_TOL
+
+
+@pytest.mark.parametrize("Ntok,fin,out", [(4096, 768, 2304), (1000, 520, 296)])
+def test_gemm_wgrad_split_k_pairs(ops, Ntok, fin, out):
+    """Weight gradient without a bias gradient: N = 256 CTA-pair tiles with split K, FP32 accumulate."""
+    rng = np.random.default_rng(Ntok + 3 * fin)
+    dY = _mk(rng, Ntok, out)
+    X = _mk(rng, Ntok, fin)
+    dW0 = rng.standard_normal((out, fin)).astype(np.float32)
+    dW = torch.from_numpy(dW0.copy()).cuda()
+    ops.gemm_wgrad(h(dY), h(X), dW=dW)
+    ref = dW0 + dY.astype(np.float64).T @ X.astype(np.float64)
+    assert rel(dW.cpu().numpy(), ref) < F32_TOL
+    assert ops.device_error() == 0
