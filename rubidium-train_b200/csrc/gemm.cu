@@ -438,6 +438,94 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS));
 }
 
+// ------------------------------------------------- TMA-store epilogue ----
+// FP16 outputs of the CTA-pair kernel leave through a tensor store: the warp
+// writes its 32 x 32 chunk into a 2 KB shared tile in the 64-byte swizzle
+// (16-byte piece pc of row r at r * 64 + ((pc ^ ((r >> 1) & 3)) << 4), free of
+// bank conflicts for a thread per row and for 2 rows x 4 pieces), and one lane
+// issues cp.async.bulk.tensor; the map's extents clip rows >= M and columns >= N.
+// Each warp owns two such tiles (4 KB).
+__device__ __forceinline__ int swoff(int r, int pc) { return r * 64 + ((pc ^ ((r >> 1) & 3)) << 4); }
+__device__ __forceinline__ void row_to_sw(uint8_t* st, int lane, const float* v) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) *reinterpret_cast<uint4*>(st + swoff(lane, k)) = f_to_h8(v + 8 * k);
+}
+__device__ __forceinline__ void stage_in_sw(uint8_t* st, const uint4* pf, int lane) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) *reinterpret_cast<uint4*>(st + swoff(i * 8 + (lane >> 2), lane & 3)) = pf[i];
+}
+__device__ __forceinline__ void row_from_sw(const uint8_t* st, int lane, float* v) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) h8_to_f(*reinterpret_cast<const uint4*>(st + swoff(lane, k)), v + 8 * k);
+}
+constexpr int kTmaStageBytes = 4096;            // per epilogue warp: two 2 KB tiles
+
+// FP16 epilogues (STORE_F16, BIAS_GELU, GELU_BWD) of one 32 x 32 chunk through
+// tensor stores.  st / st_s: the warp's two tiles (generic / shared address);
+// sc: the warp's chunk counter (single-output chunks alternate tiles).
+template <int EPI>
+__device__ __forceinline__ void epilogue_chunk_tma(const Params& p, int m0, int n, const uint32_t* r, uint8_t* st,
+                                                   uint32_t st_s, int lane, const uint4* pf, const CUtensorMap* tmC,
+                                                   const CUtensorMap* tmX, int& sc) {
+    if (n >= p.N || m0 >= p.M) return;                     // warp-uniform: nothing of this chunk is in C
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+    if constexpr (EPI == RBK_EPI_STORE_F16) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] *= p.alpha;
+    }
+    if (p.bias && EPI != RBK_EPI_GELU_BWD) {
+        if (n + 32 <= p.N) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+                float b[8];
+                h8_to_f(__ldg(reinterpret_cast<const uint4*>(p.bias + n + j)), b);
+#pragma unroll
+                for (int q = 0; q < 8; ++q) v[j + q] += b[q];
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (n + j < p.N) v[j] += __half2float(p.bias[n + j]);
+        }
+    }
+    constexpr bool kTwo = EPI == RBK_EPI_BIAS_GELU;
+    const int t = kTwo ? 0 : (sc & 1);
+    uint8_t* tile = st + t * 2048;
+    if (lane == 0) {                                       // the tile's previous tensor store has read it
+        if (kTwo) bulk_wait_read0();
+        else bulk_wait_read1();
+    }
+    __syncwarp();
+    if (p.aux) {                                           // residual or GELU pre-activation
+        stage_in_sw(tile, pf, lane);
+        __syncwarp();
+        float b[32];
+        row_from_sw(tile, lane, b);
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            if constexpr (EPI == RBK_EPI_GELU_BWD) v[j] *= gelu_grad_fast(b[j]);
+            else v[j] += b[j];
+        }
+    }
+    row_to_sw(tile, lane, v);
+    if constexpr (kTwo) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = gelu_fast(v[j]);
+        row_to_sw(st + 2048, lane, v);
+    }
+    fence_proxy_async();
+    __syncwarp();
+    if (lane == 0) {
+        tma_store_2d(tmC, st_s + t * 2048, n, m0);
+        if constexpr (kTwo) tma_store_2d(tmX, st_s + 2048, n, m0);
+        bulk_commit();
+    }
+    ++sc;
+}
+
 // ------------------------------------------------------------ CTA pairs ----
 // The same GEMM on CTA pairs (a 2-CTA cluster per pair of SMs): a pair tile is
 // 256 rows x 256 columns.  Each CTA stages its 128 rows of A and its 128
@@ -456,6 +544,7 @@ constexpr int kPairStages = 6;
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmX,
                      const Params p) {
     constexpr int BN = 256, HALF_N = 128;
     constexpr int A_BYTES = BM * BK * 2, B_BYTES = HALF_N * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
@@ -466,7 +555,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* gbase = smem_raw + (base - raw);
     const uint32_t sA0 = base;
     const uint32_t epi_stage = base + STAGES * STAGE_BYTES;
-    const uint32_t bars = epi_stage + kEpiWarps * kStageBytes;
+    const uint32_t bars = epi_stage + kEpiWarps * kTmaStageBytes;
     uint8_t* gbars = gbase + (bars - base);
     auto full_bar = [&](int s) { return bars + 8u * s; };
     auto empty_bar = [&](int s) { return bars + 8u * (STAGES + s); };
@@ -577,7 +666,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int half_id = (warp - 2) / 4;
         constexpr int kChunks = BN / 32;
         const int c0 = half_id * (kChunks / 2), c1 = half_id ? kChunks : kChunks / 2;
-        uint8_t* my_stage = gbase + (epi_stage - base) + (warp - 2) * kStageBytes;
+        uint8_t* my_stage = gbase + (epi_stage - base) + (warp - 2) * kTmaStageBytes;
+        const uint32_t my_stage_s = epi_stage + (warp - 2) * kTmaStageBytes;
+        constexpr bool kTma = EPI == RBK_EPI_STORE_F16 || EPI == RBK_EPI_BIAS_GELU || EPI == RBK_EPI_GELU_BWD;
+        int sc = 0;
         int buf = 0;
         uint32_t bphase = 0;
         for (int u = pair; u < p.units; u += num_pairs) {
@@ -598,13 +690,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint4 cur[4] = {pf[0], pf[1], pf[2], pf[3]};
                 if (kAux && p.aux && c + 1 < c1) prefetch_h(pf, p.aux, lda, m0, nb * BN + (c + 1) * 32, p, lane);
                 tmem_wait_ld();
-                epilogue_chunk<EPI>(p, m0, nb * BN + c * 32, r, my_stage, lane, cur);
+                if constexpr (kTma)
+                    epilogue_chunk_tma<EPI>(p, m0, nb * BN + c * 32, r, my_stage, my_stage_s, lane, cur, &tmC, &tmX, sc);
+                else
+                    epilogue_chunk<EPI>(p, m0, nb * BN + c * 32, r, my_stage, lane, cur);
             }
+            // the accumulator reads are complete (tcgen05.wait::ld); the tile's global stores need not
+            // drain before the MMAs may reuse the buffer, so the arrival is relaxed
             fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(buf), 0));
+            if (lane == 0) mbar_arrive_cluster_relaxed(mapa_shared(tempty_bar(buf), 0));
             if (++buf == 2) { buf = 0; bphase ^= 1; }
         }
+        if (kTma && lane == 0) bulk_wait0();               // tensor stores complete before exit
     }
 
     fence_before();
@@ -638,9 +736,21 @@ int launch(rbk_ctx* ctx, const rbk_gemm_desc* d, Params& p, cudaStream_t st) {
 // Launched as 2-CTA clusters; grid = 2 x min(units, pairs that fit at once).
 template <int EPI>
 int launch_pair(rbk_ctx* ctx, const rbk_gemm_desc* d, Params& p, cudaStream_t st) {
-    constexpr int SMEM = 1024 + kPairStages * (BM * BK * 2 + 128 * BK * 2) + kEpiWarps * kStageBytes + 256;
+    constexpr int SMEM = 1024 + kPairStages * (BM * BK * 2 + 128 * BK * 2) + kEpiWarps * kTmaStageBytes + 256;
     static_assert(SMEM <= 232448, "shared memory budget");
-    CUtensorMap ta, tb;
+    static_assert(kStageBytes <= kTmaStageBytes, "FP32 epilogues stage in the same per-warp tiles");
+    CUtensorMap ta, tb, tc_, tx;
+    // FP16 outputs: 32 x 32 store boxes over the logical [M, N] (ldc / ld_aux pitches)
+    constexpr bool kTma = EPI == RBK_EPI_STORE_F16 || EPI == RBK_EPI_BIAS_GELU || EPI == RBK_EPI_GELU_BWD;
+    memset(&tc_, 0, sizeof(tc_));
+    memset(&tx, 0, sizeof(tx));
+    if (kTma) {
+        RBK_TRY(make_tmap(&tc_, d->C, d->N, d->M, d->ldc, 32, 32, CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                          CU_TENSOR_MAP_SWIZZLE_64B));
+        if (EPI == RBK_EPI_BIAS_GELU)
+            RBK_TRY(make_tmap(&tx, d->aux_out, d->N, d->M, d->ld_aux ? d->ld_aux : d->ldc, 32, 32,
+                              CU_TENSOR_MAP_DATA_TYPE_FLOAT16, CU_TENSOR_MAP_SWIZZLE_64B));
+    }
     if (!d->a_major) RBK_TRY(make_tmap(&ta, d->A, d->K, d->M, d->lda, 64, 128));
     else RBK_TRY(make_tmap(&ta, d->A, d->M, d->K, d->lda, 64, 64));
     if (!d->b_major) RBK_TRY(make_tmap(&tb, d->B, d->K, d->N, d->ldb, 64, 128));
@@ -667,7 +777,7 @@ int launch_pair(rbk_ctx* ctx, const rbk_gemm_desc* d, Params& p, cudaStream_t st
     }
     const int pairs = p.units < max_pairs ? p.units : max_pairs;
     cfg.gridDim = dim3(2 * pairs);
-    RBK_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<EPI>, ta, tb, p));
+    RBK_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<EPI>, ta, tb, tc_, tx, p));
     RBK_LAUNCHED("gemm_pair_kernel");
     return RBK_OK;
 }

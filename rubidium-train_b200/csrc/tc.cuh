@@ -213,6 +213,12 @@ __device__ __forceinline__ void cluster_sync() {
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
 }
+// Relaxed form: orders nothing but the arrival itself.  For a consumer whose
+// reads are complete before it arrives (tcgen05.ld after tcgen05.wait::ld),
+// so its earlier global stores need not drain first.
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t bar_cluster) {
+    asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
 // Tile load into this CTA's shared memory whose completion is counted on the
 // pair leader's mbarrier (bar_cluster: shared::cluster address in CTA 0).
 __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* tm, uint32_t bar_cluster, int x,
@@ -270,11 +276,13 @@ inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// 2-D map with 128-byte swizzle: inner (contiguous) extent, outer extent, row
-// stride in elements, box in elements.  Elements outside the extents read 0.
-// FP16 by default; FP32 maps serve the tiled reduce-add.
+// 2-D map (128-byte swizzle unless told otherwise): inner (contiguous) extent,
+// outer extent, row stride in elements, box in elements.  Loads read 0 outside
+// the extents and stores skip those elements.  FP16 by default; FP32 maps serve
+// the tiled reduce-add.
 inline int make_tmap(CUtensorMap* tm, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_in,
-                     uint32_t box_out, CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_FLOAT16) {
+                     uint32_t box_out, CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                     CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
     auto fn = encode_fn();
     if (!fn) {
         set_error("cuTensorMapEncodeTiled unavailable from the driver");
@@ -285,8 +293,8 @@ inline int make_tmap(CUtensorMap* tm, const void* ptr, uint64_t inner, uint64_t 
     cuuint64_t strides[1] = {ld * esize};
     cuuint32_t box[2] = {box_in, box_out};
     cuuint32_t es[2] = {1, 1};
-    CUresult r = fn(tm, dtype, 2, const_cast<void*>(ptr), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = fn(tm, dtype, 2, const_cast<void*>(ptr), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         set_error("cuTensorMapEncodeTiled failed (%d): inner=%llu outer=%llu ld=%llu box=%ux%u", (int)r,
                   (unsigned long long)inner, (unsigned long long)outer, (unsigned long long)ld, box_in, box_out);

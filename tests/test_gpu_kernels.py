@@ -329,9 +329,10 @@ def test_gemm_bias_residual_gelu(ops):
     assert rel(f(act), oracle.act_fwd(f(pre))) < F16_TOL
 
 
-def test_gemm_dgrad_gelu_bwd(ops, ora):
-    rng = np.random.default_rng(12)
-    Ntok, fin, out = 260, 192, 320
+@pytest.mark.parametrize("Ntok,fin,out", [(260, 192, 320), (300, 640, 256), (777, 1024, 192)])
+def test_gemm_dgrad_gelu_bwd(ops, ora, Ntok, fin, out):
+    """dX = (dY W) * GELU'(pre); fin >= 512 runs on CTA-pair tiles with tensor stores."""
+    rng = np.random.default_rng(12 + Ntok)
     dY = _mk(rng, Ntok, out)
     W = _mk(rng, out, fin)
     pre = _mk(rng, Ntok, fin)
