@@ -4,20 +4,25 @@
 //
 // One CTA = one (batch, head, 128-query block); at d_head 64 two CTAs share an
 // SM.  Keys are consumed 64 at a time.  Q and K tiles are d_head/64 128B-swizzle
-// atoms wide (one TMA box each), V is d_head/64 MN-major column blocks, O is
-// d_head TMEM columns.  Roles (192 threads):
-//   warp 0     TMA: Q once (128 x 64 box), K through a 3-stage ring and V
-//              through a 2-stage ring (64 x 64 boxes), all from the fused
+// atoms wide (one TMA box each), V is d_head/64 MN-major column blocks.  Two
+// softmax warpgroups take alternate key blocks, each with its own running row
+// max / sum and its own O accumulator in TMEM; the two partial results are
+// merged at the end (O = O0 2^(m0-m) + O1 2^(m1-m), l likewise).  That doubles
+// the warps working through the exp / max / sum chains, which bound the
+// kernel, at the same TMEM budget.  Roles (320 threads):
+//   warp 0     TMA: Q once (128 x 64 box), K through a KS-stage ring and V
+//              through a VS-stage ring (64 x 64 boxes), all from the fused
 //              q|k|v rows of the QKV projection
-//   warp 1     MMA: S_j = Q K_j^T into one of two TMEM buffers (128 x 64 FP32),
-//              so S_{j+1} is computed while the softmax works on S_j; then
-//              O += P_j V_j into TMEM (128 x 64 FP32) with P_j from shared memory
-//   warps 2-5  softmax (P double-buffered: no wait on the PV just issued),
-//              one query row per thread (TMEM lane = row: the row max
-//              and sum need no cross-thread reduction); P = exp2(S*scale*log2e
-//              - m) goes to shared memory as FP16 in the 128B-swizzled K-major
-//              layout the PV MMA reads.  O is rescaled only when a row max grows
-//              by more than 2^8 (P stays <= 256, within FP16 range).
+//   warp 1     MMA: S_j = Q K_j^T into TMEM buffer j & 1 (128 x 64 FP32), then
+//              O_{j&1} += P_j V_j with P_j from shared memory
+//   warps 2-5  softmax, even key blocks; warps 6-9 odd key blocks.  One query
+//              row per thread (TMEM lane = row: the row max and sum need no
+//              cross-thread reduction); P = exp2(S*scale*log2e - m) is one FFMA
+//              and one ex2 per score and goes to shared memory as FP16 in the
+//              128B-swizzled K-major layout the PV MMA reads.  A group rescales
+//              its O only when its row max grows by more than 2^8 (P <= 256,
+//              within FP16 range).
+// TMEM: S0 [0, 64), S1 [64, 128), O0 [128, 128 + d_head), O1 after O0.
 // Causal masking applies to the two key blocks that overlap the query block;
 // blocks above the diagonal are never loaded.  Output O (FP16) and LSE
 // (natural log), as the mma.sync path.  Every wait is bounded; no multicast.
@@ -29,7 +34,6 @@ namespace attn_tc {
 using namespace tc;
 
 constexpr int BQ = 128, BKV = 64;
-constexpr int kThreads = 192;
 template <int HD>
 struct FwdCfg {
     static constexpr int NA = HD / 64;                  // 64-column atoms across d_head
@@ -39,11 +43,16 @@ struct FwdCfg {
     static constexpr int P_BYTES = BQ * BKV * 2;        // 16 KB: one 64-key K-major atom
     static constexpr int OFF_Q = 0, OFF_K = OFF_Q + Q_BYTES, OFF_V = OFF_K + KS * KV_BYTES,
                          OFF_P = OFF_V + VS * KV_BYTES;
-    static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;   // P double-buffered
+    static constexpr int OFF_ML = OFF_P + 2 * P_BYTES;    // P double-buffered; then (m, l) of both groups
+    static constexpr int OFF_BAR = OFF_ML + 2 * BQ * 8;
     static constexpr int SMEM = 1024 + OFF_BAR + 256;
     static constexpr int CTAS_PER_SM = HD == 64 ? 2 : 1;
+    // softmax groups: two at d_head 128 (one CTA per SM); one at d_head 64, where two CTAs share
+    // an SM and a second group's registers would not fit
+    static constexpr int NG = HD == 64 ? 1 : 2;
+    static constexpr int THREADS = 64 + 128 * NG;
+    static constexpr uint32_t TMEM_COLS = HD == 64 ? 256 : 512;   // S0, S1, O0 (, O1)
 };
-constexpr uint32_t TMEM_COLS = 256;       // S0 [0, 64), S1 [64, 128), O [128, 128 + d_head)
 constexpr uint32_t O_COL = 128;
 
 __device__ __forceinline__ float ex2(float x) {
@@ -51,12 +60,32 @@ __device__ __forceinline__ float ex2(float x) {
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
 }
+// Packed FP32 pairs (sm_100): one instruction for two lanes of arithmetic.
+__device__ __forceinline__ uint64_t pair_of(float a) {
+    return ((uint64_t)__float_as_uint(a) << 32) | __float_as_uint(a);
+}
+// (y0, y1) = (x0, x1) * a2 + b2
+__device__ __forceinline__ void ffma2(float& y0, float& y1, float x0, float x1, uint64_t a2, uint64_t b2) {
+    asm("{\n\t.reg .b64 xx, yy;\n\tmov.b64 xx, {%2, %3};\n\tfma.rn.f32x2 yy, xx, %4, %5;\n\tmov.b64 {%0, %1}, yy;\n\t}"
+        : "=f"(y0), "=f"(y1)
+        : "f"(x0), "f"(x1), "l"(a2), "l"(b2));
+}
+// acc += (x0, x1), lane-wise
+__device__ __forceinline__ void fadd2(uint64_t& acc, float x0, float x1) {
+    asm("{\n\t.reg .b64 xx;\n\tmov.b64 xx, {%1, %2};\n\tadd.rn.f32x2 %0, %0, xx;\n\t}" : "+l"(acc) : "f"(x0), "f"(x1));
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float y;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(y) : "f"(a), "f"(b), "f"(c));
+    return y;
+}
 
 template <int HD>
-__global__ void __launch_bounds__(kThreads, FwdCfg<HD>::CTAS_PER_SM)
+__global__ void __launch_bounds__(FwdCfg<HD>::THREADS, FwdCfg<HD>::CTAS_PER_SM)
     flash_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmkv, half* O,
                         float* LSE, int S, int H, float scale_log2, int* err) {
     using Cf = FwdCfg<HD>;
+    constexpr int NG = Cf::NG;
     constexpr int NA = Cf::NA, KS = Cf::KS, VS = Cf::VS, Q_BYTES = Cf::Q_BYTES, KV_BYTES = Cf::KV_BYTES,
                   P_BYTES = Cf::P_BYTES, OFF_Q = Cf::OFF_Q, OFF_K = Cf::OFF_K, OFF_V = Cf::OFF_V, OFF_P = Cf::OFF_P,
                   OFF_BAR = Cf::OFF_BAR;
@@ -104,7 +133,7 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<HD>::CTAS_PER_SM)
         asm volatile("prefetch.tensormap [%0];" ::"l"(&tmq) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(&tmkv) : "memory");
     }
-    if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+    if (warp == 1) tmem_alloc(tmem_slot, Cf::TMEM_COLS);
     fence_before();
     __syncthreads();
     fence_after();
@@ -140,7 +169,6 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<HD>::CTAS_PER_SM)
         if (lane == 0) {
             const uint32_t idesc_s = idesc_f16(BKV, 0, 0);   // Q (K-major) x K (K-major), N = 64
             const uint32_t idesc_o = idesc_f16(HD, 0, 1);    // P (K-major) x V (MN-major), N = d_head
-            const uint32_t o_tm = tmem + O_COL;
             auto issue_s = [&](int j) -> bool {
                 const int ks = j % KS;
                 if (!mbar_wait(k_full(ks), (j / KS) & 1, abort_flag)) return false;
@@ -161,11 +189,12 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<HD>::CTAS_PER_SM)
                     !mbar_wait(v_full(vs), (j / VS) & 1, abort_flag))
                     break;
                 fence_after();
+                const uint32_t o_tm = tmem + O_COL + (NG == 2 ? (uint32_t)(j & 1) * HD : 0u);   // the group's O
 #pragma unroll
                 for (int k = 0; k < BKV / 16; ++k)
                     mma_f16(o_tm, sdesc(sP(j & 1) + k * 32, 16, 1024),
                             sdesc(sV(vs) + k * 2048, BKV * 128, 1024),   // N blocks of 64 columns, 8 KB apart
-                            idesc_o, (j > 0 || k > 0) ? 1u : 0u);
+                            idesc_o, (j >= NG || k > 0) ? 1u : 0u);
                 mma_commit(o_done(j & 1));
                 mma_commit(v_empty(vs));
                 if (j + 2 < nkv && !issue_s(j + 2)) break;   // S buffer j&1 was released by p_full[j&1]
@@ -173,106 +202,143 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<HD>::CTAS_PER_SM)
         }
     } else {
         // ------------------------------------------------------ softmax ----
+        const int wg = NG == 2 ? (warp - 2) >> 2 : 0;    // two groups: even / odd key blocks
         const int q4 = warp & 3;
         const int row = q4 * 32 + lane;                   // query row inside the block
         const int qpos = qb * BQ + row;                   // query position in the sequence
         const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
-        float m = -INFINITY, l = 0.0f;
+        const uint32_t o_col = O_COL + (uint32_t)wg * HD;
+        float m = -INFINITY, l = 0.0f;                    // running max (log2 units) and sum of this group
         bool ok = true;
-        for (int j = 0; j < nkv; ++j) {
-            if (!mbar_wait(s_full(j & 1), (j >> 1) & 1, abort_flag)) { ok = false; break; }
+        int jl = 0;                                       // blocks of this group done
+        for (int j = wg; j < nkv; j += NG, ++jl) {
+            const int sb = j & 1;                         // S / P buffer of block j
+            if (!mbar_wait(s_full(sb), (j >> 1) & 1, abort_flag)) { ok = false; break; }
             fence_after();
             const bool mask = (j + 1) * BKV > qb * BQ;   // block overlaps the diagonal region
             uint32_t r[64];
-            tmem_ld32(tmem + lane_off + (uint32_t)(j & 1) * BKV, r);
-            tmem_ld32(tmem + lane_off + (uint32_t)(j & 1) * BKV + 32, r + 32);
+            tmem_ld32(tmem + lane_off + (uint32_t)sb * BKV, r);
+            tmem_ld32(tmem + lane_off + (uint32_t)sb * BKV + 32, r + 32);
             tmem_wait_ld();
-            // eight independent max / sum accumulators: no 64-long dependency chains
-            float x[64];
-            float mxp[8];
+            // four independent max accumulators, two scores per 3-input max
+            float mxp[4];
 #pragma unroll
-            for (int a = 0; a < 8; ++a) mxp[a] = -INFINITY;
-            const int lim = mask ? qpos - j * BKV : 1 << 30;   // keys e > lim are masked
+            for (int a = 0; a < 4; ++a) mxp[a] = -INFINITY;
+            if (mask) {
+                const int lim = qpos - j * BKV;           // keys e > lim are masked
 #pragma unroll
-            for (int e = 0; e < 64; ++e) {
-                const float v = e > lim ? -INFINITY : __uint_as_float(r[e]) * scale_log2;
-                x[e] = v;
-                mxp[e & 7] = fmaxf(mxp[e & 7], v);
+                for (int e = 0; e < 64; ++e)
+                    if (e > lim) r[e] = __float_as_uint(-INFINITY);
             }
-            const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
-                                   fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+#pragma unroll
+            for (int e = 0; e < 64; e += 2)
+                mxp[(e >> 1) & 3] = fmax3(mxp[(e >> 1) & 3], __uint_as_float(r[e]), __uint_as_float(r[e + 1]));
+            const float mx = scale_log2 * fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3]));
             float corr = 1.0f;
             bool rescale = false;
             if (mx > m + 8.0f) {                          // lazy rescale (first block: m = -inf)
-                if (j > 0) { corr = ex2(m - mx); rescale = true; }
+                if (jl > 0) { corr = ex2(m - mx); rescale = true; }
                 m = mx;
                 l *= corr;
             }
-            float p[64];
-            float rsp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            // p = 2^(s * scale * log2 e - m); a row with no visible key yet keeps m = -inf and p = 0
+            const float nm = m == -INFINITY ? 0.0f : -m;
+            const uint64_t c2 = pair_of(scale_log2), nm2 = pair_of(nm);
+            uint64_t rs2[2] = {0, 0};                     // two packed (even, odd) sum accumulators
+            uint32_t pk[32];                              // P as FP16 pairs
 #pragma unroll
-            for (int e = 0; e < 64; ++e) {
-                p[e] = ex2(x[e] - m);
-                rsp[e & 7] += p[e];
+            for (int e = 0; e < 64; e += 2) {
+                float x0, x1;
+                ffma2(x0, x1, __uint_as_float(r[e]), __uint_as_float(r[e + 1]), c2, nm2);
+                const float p0 = ex2(x0), p1 = ex2(x1);
+                fadd2(rs2[(e >> 1) & 1], p0, p1);
+                __half2 hp = __floats2half2_rn(p0, p1);
+                pk[e >> 1] = *reinterpret_cast<uint32_t*>(&hp);
             }
-            l += ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
-            // P buffer j&1 was last read by PV_{j-2}
+            l += (__uint_as_float((uint32_t)rs2[0]) + __uint_as_float((uint32_t)(rs2[0] >> 32))) +
+                 (__uint_as_float((uint32_t)rs2[1]) + __uint_as_float((uint32_t)(rs2[1] >> 32)));
+            // P buffer sb (and, with two groups, O_wg) was last read by PV_{j-2}
             if (j > 1) {
-                if (!mbar_wait(o_done(j & 1), ((j >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
+                if (!mbar_wait(o_done(sb), ((j >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
                 fence_after();
             }
             if (__any_sync(0xffffffffu, rescale)) {
-                // O must hold every earlier PV before it is rescaled: wait for PV_{j-1}
-                if (!mbar_wait(o_done((j - 1) & 1), ((j - 1) >> 1) & 1, abort_flag)) { ok = false; break; }
-                fence_after();
+                if constexpr (NG == 1) {                  // the single O must hold PV_{j-1} before its rescale
+                    if (!mbar_wait(o_done((j - 1) & 1), ((j - 1) >> 1) & 1, abort_flag)) { ok = false; break; }
+                    fence_after();
+                }
 #pragma unroll
                 for (int c = 0; c < HD / 32; ++c) {
                     uint32_t t[32];
-                    tmem_ld32(tmem + lane_off + O_COL + c * 32, t);
+                    tmem_ld32(tmem + lane_off + o_col + c * 32, t);
                     tmem_wait_ld();
 #pragma unroll
                     for (int e = 0; e < 32; ++e) t[e] = __float_as_uint(__uint_as_float(t[e]) * corr);
-                    tmem_st32(tmem + lane_off + O_COL + c * 32, t);
+                    tmem_st32(tmem + lane_off + o_col + c * 32, t);
                 }
                 tmem_wait_st();
             }
 #pragma unroll
             for (int c = 0; c < 8; ++c) {                 // 16-byte chunk = 8 keys, 128B swizzle
-                const uint32_t addr = sP(j & 1) + (uint32_t)row * 128u + (uint32_t)((c ^ (row & 7)) << 4);
-                const uint4 u = f_to_h8(p + 8 * c);
-                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(u.x), "r"(u.y), "r"(u.z),
-                             "r"(u.w)
+                const uint32_t addr = sP(sb) + (uint32_t)row * 128u + (uint32_t)((c ^ (row & 7)) << 4);
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk[4 * c]),
+                             "r"(pk[4 * c + 1]), "r"(pk[4 * c + 2]), "r"(pk[4 * c + 3])
                              : "memory");
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full(j & 1));
+            if (lane == 0) mbar_arrive(p_full(sb));
         }
-        // epilogue: O / l (FP16) and LSE
-        if (ok && mbar_wait(o_done((nkv - 1) & 1), ((nkv - 1) >> 1) & 1, abort_flag)) {
+        // epilogue.  One group: O / l.  Two groups: after each has seen its last PV, swap (m, l)
+        // and each writes half of the columns of
+        // O = (O0 2^(m0-M) + O1 2^(m1-M)) / (l0 2^(m0-M) + l1 2^(m1-M)).
+        const int jlast = nkv - NG + wg;                  // last block of this group (nkv is even)
+        ok = ok && mbar_wait(o_done(jlast & 1), (jlast >> 1) & 1, abort_flag);
+        float f0 = 0.0f, f1 = 0.0f, M = m, L = l;
+        if constexpr (NG == 2) {
+            float* ml = reinterpret_cast<float*>(gbase + Cf::OFF_ML);
+            ml[(wg * BQ + row) * 2] = m;
+            ml[(wg * BQ + row) * 2 + 1] = l;
+            fence_before();
+            named_sync(1, 256);
             fence_after();
-            const float inv = 1.0f / l;
+            ok = ok && !*abort_flag;
+            const float m0 = ml[row * 2], l0 = ml[row * 2 + 1];
+            const float m1 = ml[(BQ + row) * 2], l1 = ml[(BQ + row) * 2 + 1];
+            M = fmaxf(m0, m1);
+            const float a0 = m0 == -INFINITY ? 0.0f : ex2(m0 - M), a1 = m1 == -INFINITY ? 0.0f : ex2(m1 - M);
+            L = l0 * a0 + l1 * a1;
+            f0 = a0 / L;
+            f1 = a1 / L;
+        } else {
+            f0 = 1.0f / l;
+        }
+        if (ok) {
             half* orow = O + ((size_t)row0 + qpos) * D + h * HD;
-#pragma unroll
-            for (int c = 0; c < HD / 32; ++c) {
-                uint32_t t[32];
-                tmem_ld32(tmem + lane_off + O_COL + c * 32, t);
+#pragma unroll 1
+            for (int c = wg * (HD / 16 / NG); c < (wg + 1) * (HD / 16 / NG); ++c) {   // 16 columns at a time
+                uint32_t t0[16], t1[16];
+                tmem_ld16(tmem + lane_off + O_COL + c * 16, t0);
+                if constexpr (NG == 2) tmem_ld16(tmem + lane_off + O_COL + HD + c * 16, t1);
                 tmem_wait_ld();
-                float o[32];
+                float o[16];
 #pragma unroll
-                for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(t[e]) * inv;
+                for (int e = 0; e < 16; ++e) {
+                    o[e] = __uint_as_float(t0[e]) * f0;
+                    if constexpr (NG == 2) o[e] = fmaf(__uint_as_float(t1[e]), f1, o[e]);
+                }
 #pragma unroll
-                for (int g = 0; g < 4; ++g) reinterpret_cast<uint4*>(orow + c * 32)[g] = f_to_h8(o + 8 * g);
+                for (int g = 0; g < 2; ++g) reinterpret_cast<uint4*>(orow + c * 16)[g] = f_to_h8(o + 8 * g);
             }
-            LSE[(size_t)bh * S + qpos] = (m + __log2f(l)) * 0.6931471805599453f;
+            if (wg == 0) LSE[(size_t)bh * S + qpos] = (M + __log2f(L)) * 0.6931471805599453f;
         }
     }
     fence_before();
     __syncthreads();
     fence_after();
     if (threadIdx.x == 0 && *abort_flag) atomicExch(err, RBK_ERR_TIMEOUT);
-    if (warp == 1) tmem_free(tmem, TMEM_COLS);
+    if (warp == 1) tmem_free(tmem, Cf::TMEM_COLS);
 }
 
 }  // namespace attn_tc
@@ -293,7 +359,7 @@ static int attn_fwd_tc_hd(rbk_ctx* ctx, void* o, float* lse, const void* qkv, in
         set_dev = ctx->device;
     }
     dim3 grid(S / BQ, B * H);
-    flash_fwd_tc_kernel<HD><<<grid, kThreads, FwdCfg<HD>::SMEM, st>>>(
+    flash_fwd_tc_kernel<HD><<<grid, FwdCfg<HD>::THREADS, FwdCfg<HD>::SMEM, st>>>(
         tmq, tmkv, (half*)o, lse, S, H, scale * 1.4426950408889634f, ctx->tickets + kGemmError);
     RBK_LAUNCHED("flash_fwd_tc_kernel");
     return RBK_OK;
