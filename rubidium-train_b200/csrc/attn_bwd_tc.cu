@@ -1,24 +1,27 @@
 // attn_bwd_tc.cu — causal flash attention backward on the 5th-generation
-// tensor cores (d_head 64 or 128, sequence length a multiple of 128): the tcgen05
-// replacement of the mma.sync main kernel in attn.cu.  The pre pass (Dot =
-// rowsum(dO * O), -LSE * log2 e, zeroed FP32 dQ accumulator) and the post pass
-// (dQ -> FP16, q- and v-bias column sums) are shared with the mma.sync path.
+// tensor cores (d_head 64 or 128, sequence length a multiple of 128): the
+// tcgen05 replacement of the mma.sync main kernel in attn.cu.  The pre pass
+// (Dot = rowsum(dO * O), -LSE * log2 e, zeroed FP32 dQ accumulator) and the
+// post pass (dQ -> FP16, q- and v-bias column sums) are shared with the
+// mma.sync path.
 //
-// Work item = one (batch, head, 128-key block): it walks the 64-query
-// sub-tiles from the diagonal to the end of the sequence.  Per sub-tile i
-// (TMEM lane = key, column = query):
-//   S^T_i  = K Q_i^T          dP^T_i = V dO_i^T       (N = 64, double-buffered)
+// d_head 64.  Work item = one (batch, head, 128-key block): it walks the
+// 128-query sub-tiles from the diagonal to the end of the sequence.  Per
+// sub-tile i (TMEM lane = key, column = query):
+//   S^T_i  = K Q_i^T          dP^T_i = V dO_i^T       (M = N = 128, K = 64)
 //   P^T_i  = exp2(S^T * scale * log2 e - LSE * log2 e)     (0 above the diagonal)
 //   dS^T_i = P^T_i * (dP^T_i - Dot)
-//   dV    += P^T_i dO_i       dK    += dS^T_i Q_i     (TMEM accumulators)
-// and for every pair of sub-tiles (128 queries)
-//   dQ     = dS K            (M = 128 queries, K = 128 keys) -> TMA reduce-add
+//   dV    += P^T_i dO_i       dK    += dS^T_i Q_i     (K = 128 queries)
+//   dQ_i   = dS_i K           (M = 128 queries, K = 128 keys) -> TMA reduce-add
 // into the FP32 accumulator.  P^T goes back to TMEM as FP16 and is the A
 // operand of the dV product straight from there; dS^T goes to shared memory as
 // FP16 in the 128B-swizzled layout: K-major for the dK product and, read the
-// other way, MN-major for the dQ product, so one copy serves both.  Once dQ of
-// a pair is in TMEM, the pair's two dS^T tiles are the FP32 staging buffer of
-// its reduce-add.
+// other way, MN-major for the dQ product, so one copy serves both.  Once dQ_i
+// is in TMEM, the dS^T_i tile is the FP32 staging buffer of its reduce-add.
+// 128-query sub-tiles make every product an N = 128 or K = 128 MMA and halve
+// the hand-offs between the issuing threads and the P / dS warps per FLOP;
+// TMEM holds exactly one of each: S^T 0, dP^T 128, P^T 256 (FP16 pairs),
+// dK 320, dV 384, dQ 448.
 //
 // The kernel is persistent: one CTA per SM takes work items round-robin from
 // a longest-first order; K and V are double-buffered so the next item's tiles
@@ -29,23 +32,26 @@
 //
 // Roles (736 threads):
 //   warp 0       TMA: K and V per item, then Q_i, dO_i and the per-query rows
-//                (-LSE log2 e, Dot) through a 5-stage ring
+//                (-LSE log2 e, Dot) through a 2-stage ring
 //   warp 1       MMA issue, producer side: S^T_i and dP^T_i
 //   warp 2       MMA issue, consumer side: dV, dK and dQ.  Two issuing
 //                threads in different warps: a single issuer that also waits
 //                on barriers leaves the tensor pipe idle for each wait.
 //   warps 3-18   P / dS: warp w owns TMEM lanes 32 (w % 4) .. +31 and query
-//                columns 16 ((w - 3) / 4) .. +15 of each sub-tile
+//                columns 32 ((w - 3) / 4) .. +31 of each sub-tile, in two
+//                halves of 16
 //   warps 19-22  dQ drain (TMEM -> swizzled FP32 staging -> reduce-add), then
 //                the dK / dV epilogue of each item (TMEM -> K / V tiles -> TMA
 //                store)
-// TMEM (512 columns): S^T[2] 0/64, dP^T[2] 128/192, dK 256, dV 320, dQ 384,
-// P^T[2] (FP16 pairs) 448/480.  Every wait is bounded; no cluster multicast.
+// Every wait is bounded; no cluster multicast.
+//
+// d_head 128 (attn_tc_bwd128 below) keeps 64-query sub-tiles: dK and dV alone
+// take 256 TMEM columns there.
 //
 // Bias gradients: the key bias has an exactly zero gradient (it shifts every
 // score of a query row by the same amount, and sum_j dS_ij = Dot_i - Dot_i = 0),
 // and the value bias gradient is sum_j dV_j = sum_i dO_i (rows of P sum to 1);
-// the post pass adds the latter from dO, so this kernel writes no bias terms.
+// the post pass adds the latter from dO, so these kernels write no bias terms.
 #include "tc.cuh"
 
 namespace rbk {
@@ -53,22 +59,25 @@ namespace attn_tc_bwd {
 
 using namespace tc;
 
-constexpr int BK = 128, BQ = 64, HD = 64;
-constexpr int QS = 5;                       // Q / dO ring depth
+constexpr int BK = 128, BQ = 128, HD = 64;
+constexpr int QS = 3;                       // Q / dO ring depth
 constexpr int NE = 16;                      // P / dS warps
 constexpr int WE = 3;                       // first P / dS warp
 constexpr int WD = WE + NE;                 // first drain warp
 constexpr int kThreads = (WD + 4) * 32;
 constexpr int KT_BYTES = BK * HD * 2;       // 16 KB  K or V block
-constexpr int QT_BYTES = BQ * HD * 2;       // 8 KB   Q or dO sub-tile
-constexpr int PT_BYTES = BK * BQ * 2;       // 16 KB  dS^T sub-tile
+constexpr int QT_BYTES = BQ * HD * 2;       // 16 KB  Q or dO sub-tile
+constexpr int PT_BYTES = BK * BQ * 2;       // 32 KB  dS^T sub-tile: two 64-query atoms of 16 KB
+constexpr int PA_BYTES = BK * 128;          // one atom of dS^T
 constexpr int ROW_BYTES = 2 * BQ * 4;       // -LSE log2e | Dot of one sub-tile
+constexpr int STG_BYTES = BQ * 32 * 4;      // 16 KB  FP32 dQ staging: 128 queries x 32 columns (one box)
 constexpr int OFF_K = 0, OFF_V = OFF_K + 2 * KT_BYTES, OFF_Q = OFF_V + 2 * KT_BYTES, OFF_DO = OFF_Q + QS * QT_BYTES,
-              OFF_DS = OFF_DO + QS * QT_BYTES, OFF_ROW = OFF_DS + 4 * PT_BYTES, OFF_BAR = OFF_ROW + QS * ROW_BYTES;
-constexpr int NBARS = 2 * QS + 2 * 6 + 4 + 2 * 2;
+              OFF_DS = OFF_DO + QS * QT_BYTES, OFF_STG = OFF_DS + PT_BYTES, OFF_ROW = OFF_STG + STG_BYTES,
+              OFF_BAR = OFF_ROW + QS * ROW_BYTES;
+constexpr int NBARS = 2 * QS + 4 + 2 + 2 + 2 + 2 + 2;
 constexpr int SMEM = 1024 + OFF_BAR + NBARS * 8 + 16;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t S_COL = 0, DP_COL = 128, DK_COL = 256, DV_COL = 320, DQ_COL = 384, P_COL = 448;
+constexpr uint32_t S_COL = 0, DP_COL = 128, P_COL = 256, DK_COL = 320, DV_COL = 384, DQ_COL = 448;
 static_assert(SMEM <= 232448, "shared memory budget");
 
 __device__ __forceinline__ float ex2(float x) {
@@ -130,7 +139,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto sQ = [&](int s) { return base + OFF_Q + (uint32_t)s * QT_BYTES; };
     auto sdO = [&](int s) { return base + OFF_DO + (uint32_t)s * QT_BYTES; };
     auto sRow = [&](int s) { return base + OFF_ROW + (uint32_t)s * ROW_BYTES; };
-    auto sdS = [&](int s) { return base + OFF_DS + (uint32_t)s * PT_BYTES; };
+    const uint32_t sdS = base + OFF_DS, sStg = base + OFF_STG;
     // barriers
     const uint32_t bars = base + OFF_BAR;
     auto q_full = [&](int s) { return bars + 8 * s; };
@@ -138,18 +147,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t b2 = bars + 16 * QS;
     auto kv_full = [&](int s) { return b2 + 8 * s; };       // K, V of an item in buffer s
     auto kv_empty = [&](int s) { return b2 + 16 + 8 * s; }; // K / V buffer s free: producer done, dK / dV stored
-    auto s_full = [&](int s) { return b2 + 32 + 8 * s; };   // S^T_i, dP^T_i in TMEM buffer i & 1
-    auto s_free = [&](int s) { return b2 + 48 + 8 * s; };   // S^T_i, dP^T_i read out of TMEM buffer i & 1
-    auto p_full = [&](int s) { return b2 + 64 + 8 * s; };   // P^T_i in TMEM, dS^T_i in shared memory
-    auto p_free = [&](int s) { return b2 + 80 + 8 * s; };   // dV_i, dK_i done: P^T buffer i & 1 reusable
-    const uint32_t dq_full = b2 + 96, dq_free = b2 + 104, acc_done = b2 + 112, acc_free = b2 + 120;
-    auto ds_free = [&](int s) { return b2 + 128 + 8 * s; }; // pair's dS^T tiles (and staging) reusable
+    const uint32_t s_full = b2 + 32, s_free = b2 + 40;      // S^T, dP^T in TMEM / loaded by the P / dS warps
+    const uint32_t p_full = b2 + 48, p_free = b2 + 56;      // P^T in TMEM and dS^T in smem / P^T read by dV
+    const uint32_t ds_free = b2 + 64;                       // dS^T read by dK and dQ: reusable
+    const uint32_t dq_full = b2 + 72, dq_free = b2 + 80, acc_done = b2 + 88, acc_free = b2 + 96;
+    const uint32_t ds_full = b2 + 104;                      // dS^T in shared memory
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + OFF_BAR + NBARS * 8);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + OFF_BAR + NBARS * 8 + 8);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int BH = num_items / (S / BK);
+    const int nkb = S / BK;
+    const int BH = num_items / nkb;
     const int D = H * HD;
+    // sub-tiles of item u: 128-query blocks from the diagonal to the end
+    auto subtiles = [&](int u) { return nkb - u / BH; };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < QS; ++s) {
@@ -159,12 +170,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s = 0; s < 2; ++s) {
             mbar_init(kv_full(s), 1);
             mbar_init(kv_empty(s), 2);
-            mbar_init(s_full(s), 1);
-            mbar_init(s_free(s), NE);
-            mbar_init(p_full(s), NE);
-            mbar_init(p_free(s), 1);
-            mbar_init(ds_free(s), 1);
         }
+        mbar_init(ds_free, 1);
+        mbar_init(ds_full, NE);
+        mbar_init(s_full, 1);
+        mbar_init(s_free, NE);
+        mbar_init(p_full, NE);
+        mbar_init(p_free, 1);
         mbar_init(dq_full, 1);
         mbar_init(dq_free, 4);
         mbar_init(acc_done, 1);
@@ -192,6 +204,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             for (int t = 0, u = blockIdx.x; ok && u < num_items; ++t, u += gridDim.x) {
                 const Item it = item_of(u, BH, H, S);
+                const int n = subtiles(u);
                 const int kvb = t & 1;
                 if (!mbar_wait(kv_empty(kvb), ((t >> 1) & 1) ^ 1, abort_flag)) break;
                 mbar_expect_tx(kv_full(kvb), 2 * KT_BYTES);
@@ -199,7 +212,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tma_load_2d(sV(kvb), &tmkv, kv_full(kvb), 2 * D + it.h * HD, it.krow0);
                 const float* nl2 = NL2 + (size_t)it.bh * S + it.kb * BK;
                 const float* dot = Dot + (size_t)it.bh * S + it.kb * BK;
-                for (int i = 0; i < it.n; ++i, ++g) {
+                for (int i = 0; i < n; ++i, ++g) {
                     const int s = g % QS;
                     if (!mbar_wait(q_empty(s), ((g / QS) & 1) ^ 1, abort_flag)) {
                         ok = false;
@@ -217,29 +230,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ------------------------------------------- MMA: S^T, dP^T producer ----
         if (lane == 0) {
-            const uint32_t id_s = idesc_f16(BQ, 0, 0);    // K (K-major) x Q^T (K-major): N = 64 queries
+            const uint32_t id_s = idesc_f16(BQ, 0, 0);    // K (K-major) x Q^T (K-major): N = 128 queries
             int g = 0;
             bool ok = true;
             for (int t = 0, u = blockIdx.x; ok && u < num_items; ++t, u += gridDim.x) {
-                const int n = item_of(u, BH, H, S).n;
+                const int n = subtiles(u);
                 const int kvb = t & 1;
                 if (!mbar_wait(kv_full(kvb), (t >> 1) & 1, abort_flag)) break;
                 for (int i = 0; i < n; ++i, ++g) {
                     const int s = g % QS;
                     ok = mbar_wait(q_full(s), (g / QS) & 1, abort_flag) &&
-                         (g < 2 || mbar_wait(s_free(g & 1), ((g >> 1) & 1) ^ 1, abort_flag));
+                         (g == 0 || mbar_wait(s_free, (g - 1) & 1, abort_flag));
                     if (!ok) break;
                     fence_after();
-                    const uint32_t bcol = (uint32_t)(g & 1) * BQ;
 #pragma unroll
                     for (int k = 0; k < HD / 16; ++k)
-                        mma_f16(tmem + S_COL + bcol, sdesc(sK(kvb) + k * 32, 16, 1024), sdesc(sQ(s) + k * 32, 16, 1024),
+                        mma_f16(tmem + S_COL, sdesc(sK(kvb) + k * 32, 16, 1024), sdesc(sQ(s) + k * 32, 16, 1024), id_s,
+                                k > 0);
+#pragma unroll
+                    for (int k = 0; k < HD / 16; ++k)
+                        mma_f16(tmem + DP_COL, sdesc(sV(kvb) + k * 32, 16, 1024), sdesc(sdO(s) + k * 32, 16, 1024),
                                 id_s, k > 0);
-#pragma unroll
-                    for (int k = 0; k < HD / 16; ++k)
-                        mma_f16(tmem + DP_COL + bcol, sdesc(sV(kvb) + k * 32, 16, 1024),
-                                sdesc(sdO(s) + k * 32, 16, 1024), id_s, k > 0);
-                    mma_commit(s_full(g & 1));
+                    mma_commit(s_full);
                     mma_commit(q_empty(s));
                 }
                 if (ok) mma_commit(kv_empty(kvb));
@@ -253,121 +265,147 @@ __global__ void __launch_bounds__(kThreads, 1)
             int g = 0;
             bool ok = true;
             for (int t = 0, u = blockIdx.x; ok && u < num_items; ++t, u += gridDim.x) {
-                const int n = item_of(u, BH, H, S).n;
+                const int n = subtiles(u);
                 const int kvb = t & 1;
                 // K is an operand of dQ; the accumulators must have been read out for the previous item
                 ok = mbar_wait(kv_full(kvb), (t >> 1) & 1, abort_flag) &&
                      (t == 0 || mbar_wait(acc_free, (t - 1) & 1, abort_flag));
                 if (!ok) break;
                 for (int i = 0; i < n; ++i, ++g) {
-                    const int s = g % QS, pb = g & 1;
-                    if (!mbar_wait(p_full(pb), (g >> 1) & 1, abort_flag)) {
+                    const int s = g % QS;
+                    const uint32_t ds = sdS;
+                    // dK and dQ need only dS^T (shared memory): they run while P^T is still being stored
+                    if (!mbar_wait(ds_full, g & 1, abort_flag)) {
                         ok = false;
                         break;
                     }
                     fence_after();
 #pragma unroll
                     for (int k = 0; k < BQ / 16; ++k)
-                        mma_f16_ts(tmem + DV_COL, tmem + P_COL + (uint32_t)(pb * 32 + k * 8),
-                                   sdesc(sdO(s) + k * 2048, 8192, 1024), id_kv, (i > 0 || k > 0) ? 1u : 0u);
+                        mma_f16(tmem + DK_COL, sdesc(ds + (k >> 2) * PA_BYTES + (k & 3) * 32, 16, 1024),
+                                sdesc(sQ(s) + k * 2048, 8192, 1024), id_kv, (i > 0 || k > 0) ? 1u : 0u);
+                    if (g > 0 && !mbar_wait(dq_free, (g - 1) & 1, abort_flag)) {   // dQ_{g-1} read out of TMEM
+                        ok = false;
+                        break;
+                    }
+                    fence_after();
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k)
+                        mma_f16(tmem + DQ_COL, sdesc(ds + k * 2048, PA_BYTES, 1024), sdesc(sK(kvb) + k * 2048, 8192, 1024),
+                                id_q, k > 0);
+                    mma_commit(dq_full);
+                    mma_commit(ds_free);
+                    if (!mbar_wait(p_full, g & 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    fence_after();
 #pragma unroll
                     for (int k = 0; k < BQ / 16; ++k)
-                        mma_f16(tmem + DK_COL, sdesc(sdS(g & 3) + k * 32, 16, 1024),
-                                sdesc(sQ(s) + k * 2048, 8192, 1024), id_kv, (i > 0 || k > 0) ? 1u : 0u);
-                    mma_commit(p_free(pb));
+                        mma_f16_ts(tmem + DV_COL, tmem + P_COL + (uint32_t)(k * 8), sdesc(sdO(s) + k * 2048, 8192, 1024),
+                                   id_kv, (i > 0 || k > 0) ? 1u : 0u);
+                    mma_commit(p_free);
                     mma_commit(q_empty(s));
-                    if (g & 1) {
-                        const int p = g >> 1;
-                        if (!mbar_wait(dq_free, (p & 1) ^ 1, abort_flag)) {   // pair p-1 read out of TMEM
-                            ok = false;
-                            break;
-                        }
-                        fence_after();
-                        const uint32_t a0 = sdS((g - 1) & 3);                  // two adjacent 64-query blocks
-#pragma unroll
-                        for (int k = 0; k < BK / 16; ++k)
-                            mma_f16(tmem + DQ_COL, sdesc(a0 + k * 2048, PT_BYTES, 1024),
-                                    sdesc(sK(kvb) + k * 2048, 8192, 1024), id_q, k > 0);
-                        mma_commit(dq_full);
-                    }
                 }
                 if (ok) mma_commit(acc_done);
             }
         }
     } else if (warp < WD) {
         // ------------------------------------------------------ P / dS ----
-        const int lg = warp & 3, quarter = (warp - WE) >> 2;
+        const int lg = warp & 3, cg = (warp - WE) >> 2;
         const int r = lg * 32 + lane;                         // key row inside the block
         const uint32_t lane_off = (uint32_t)(lg * 32) << 16;
-        const int c0 = quarter * 16;                          // first query column of this warp
+        const int c0 = cg * 32;                               // first query column of this warp
+        const uint64_t c2 = pair_of(scale_log2);
         int g = 0;
         bool ok = true;
         for (int u = blockIdx.x; ok && u < num_items; u += gridDim.x) {
-            const int n = item_of(u, BH, H, S).n;
+            const int n = subtiles(u);
             for (int i = 0; i < n; ++i, ++g) {
-                const int s = g % QS, pb = g & 1;
-                ok = mbar_wait(s_full(pb), (g >> 1) & 1, abort_flag) && mbar_wait(q_full(s), (g / QS) & 1, abort_flag);
+                const int s = g % QS;
+                ok = mbar_wait(s_full, g & 1, abort_flag) && mbar_wait(q_full(s), (g / QS) & 1, abort_flag);
                 if (!__all_sync(0xffffffffu, ok)) {
                     ok = false;
                     break;
                 }
                 fence_after();
-                uint32_t sr[16], dr[16];
-                tmem_ld16(tmem + lane_off + S_COL + (uint32_t)pb * BQ + c0, sr);
-                tmem_ld16(tmem + lane_off + DP_COL + (uint32_t)pb * BQ + c0, dr);
-                tmem_wait_ld();
-                fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(s_free(pb));      // the producer may overwrite this buffer
                 const uint32_t rowp = sRow(s);
-                uint32_t pk[8], dk[8];
-                // masked: the two sub-tiles that overlap the diagonal; columns e < lim lie above it
-                auto compute = [&](auto masked) {
-                    const int lim = r - BQ * i - c0;
+                uint32_t pk[16], dk[16];
+                // columns c0 + 16 h .. +15; masked: the diagonal sub-tile, where columns e < lim lie above it
+                auto compute = [&](auto masked, int h, const uint32_t* sr, const uint32_t* dr) {
+                    const int lim = r - c0 - 16 * h;
 #pragma unroll
                     for (int q4 = 0; q4 < 4; ++q4) {
-                        const float4 nl = ld_shared_f4(rowp + (uint32_t)(c0 + 4 * q4) * 4);
-                        const float4 dt = ld_shared_f4(rowp + BQ * 4 + (uint32_t)(c0 + 4 * q4) * 4);
+                        const int cc = c0 + 16 * h + 4 * q4;
+                        const float4 nl = ld_shared_f4(rowp + (uint32_t)cc * 4);
+                        const float4 dt = ld_shared_f4(rowp + BQ * 4 + (uint32_t)cc * 4);
                         const float nlv[4] = {nl.x, nl.y, nl.z, nl.w}, dtv[4] = {dt.x, dt.y, dt.z, dt.w};
                         float pv[4], dv[4];
 #pragma unroll
-                        for (int e4 = 0; e4 < 4; ++e4) {
+                        for (int e4 = 0; e4 < 4; e4 += 2) {       // packed FP32 pairs
                             const int e = 4 * q4 + e4;
-                            float p = ex2(fmaf(__uint_as_float(sr[e]), scale_log2, nlv[e4]));
-                            if (decltype(masked)::value) p = e < lim ? 0.0f : p;
-                            pv[e4] = p;
-                            dv[e4] = p * (__uint_as_float(dr[e]) - dtv[e4]);
+                            float x0, x1;
+                            ffma2v(x0, x1, __uint_as_float(sr[e]), __uint_as_float(sr[e + 1]), c2, nlv[e4],
+                                   nlv[e4 + 1]);
+                            float p0 = ex2(x0), p1 = ex2(x1);
+                            if (decltype(masked)::value) {
+                                p0 = e < lim ? 0.0f : p0;
+                                p1 = e + 1 < lim ? 0.0f : p1;
+                            }
+                            pv[e4] = p0;
+                            pv[e4 + 1] = p1;
+                            float d0, d1;
+                            fsub2(d0, d1, __uint_as_float(dr[e]), __uint_as_float(dr[e + 1]), dtv[e4], dtv[e4 + 1]);
+                            fmul2(dv[e4], dv[e4 + 1], p0, p1, d0, d1);
                         }
-                        pk[2 * q4] = pack_h2(pv[0], pv[1]);
-                        pk[2 * q4 + 1] = pack_h2(pv[2], pv[3]);
-                        dk[2 * q4] = pack_h2(dv[0], dv[1]);
-                        dk[2 * q4 + 1] = pack_h2(dv[2], dv[3]);
+                        pk[8 * h + 2 * q4] = pack_h2(pv[0], pv[1]);
+                        pk[8 * h + 2 * q4 + 1] = pack_h2(pv[2], pv[3]);
+                        dk[8 * h + 2 * q4] = pack_h2(dv[0], dv[1]);
+                        dk[8 * h + 2 * q4 + 1] = pack_h2(dv[2], dv[3]);
                     }
                 };
-                if (i < 2) compute(Masked{});
-                else compute(Plain{});
-                // P^T buffer pb was last read by dV two sub-tiles back; the dS^T pair slot by the
-                // reduce-add of the pair two pairs back
-                ok = g < 2 || mbar_wait(p_free(pb), ((g >> 1) & 1) ^ 1, abort_flag);
-                if (ok && g >= 4 && !(g & 1)) ok = mbar_wait(ds_free((g >> 1) & 1), ((g >> 2) & 1) ^ 1, abort_flag);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    uint32_t sr[16], dr[16];
+                    tmem_ld16(tmem + lane_off + S_COL + c0 + 16 * h, sr);
+                    tmem_ld16(tmem + lane_off + DP_COL + c0 + 16 * h, dr);
+                    tmem_wait_ld();
+                    if (h == 1) {
+                        fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(s_free);   // the producer may overwrite S^T / dP^T
+                    }
+                    if (i == 0) compute(Masked{}, h, sr, dr);
+                    else compute(Plain{}, h, sr, dr);
+                }
+                // dS^T was last read by dK / dQ of the previous sub-tile, P^T by its dV
+                ok = g == 0 || mbar_wait(ds_free, (g - 1) & 1, abort_flag);
+                if (!__all_sync(0xffffffffu, ok)) {
+                    ok = false;
+                    break;
+                }
+                // dS^T row r, queries c0 .. c0 + 31: atom c0 / 64, 16-byte chunks (c0 % 64) / 8 .. +3
+                const uint32_t drow = sdS + (uint32_t)(c0 >> 6) * PA_BYTES + (uint32_t)r * 128u;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const uint32_t sw = (uint32_t)(((((c0 & 63) >> 3) + c) ^ (r & 7)) << 4);
+                    st_shared_v4(drow + sw, dk[4 * c], dk[4 * c + 1], dk[4 * c + 2], dk[4 * c + 3]);
+                }
+                fence_proxy_async();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(ds_full);
+                ok = g == 0 || mbar_wait(p_free, (g - 1) & 1, abort_flag);
                 if (!__all_sync(0xffffffffu, ok)) {
                     ok = false;
                     break;
                 }
                 fence_after();
-                tmem_st8(tmem + lane_off + P_COL + (uint32_t)(pb * 32 + quarter * 8), pk);
-                const uint32_t drow = sdS(g & 3) + (uint32_t)r * 128u;
-#pragma unroll
-                for (int c = 0; c < 2; ++c) {                 // 16-byte chunk = 8 queries, 128B swizzle
-                    const uint32_t sw = (uint32_t)((((c0 >> 3) + c) ^ (r & 7)) << 4);
-                    st_shared_v4(drow + sw, dk[4 * c], dk[4 * c + 1], dk[4 * c + 2], dk[4 * c + 3]);
-                }
+                tmem_st16(tmem + lane_off + P_COL + (uint32_t)(cg * 16), pk);
                 tmem_wait_st();
-                fence_proxy_async();
                 fence_before();
                 __syncwarp();
                 if (lane == 0) {
-                    mbar_arrive(p_full(pb));
+                    mbar_arrive(p_full);
                     mbar_arrive(q_empty(s));
                 }
             }
@@ -375,21 +413,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         // ------------------------------------------- dQ drain, dK / dV out ----
         const int lg = warp & 3;
-        const int r = lg * 32 + lane;                         // query row of the pair / key row of the item
+        const int r = lg * 32 + lane;                         // query row of the sub-tile / key row of the item
         const uint32_t lane_off = (uint32_t)(lg * 32) << 16;
         const bool elected = warp == WD && lane == 0;
-        int gp = 0;                                           // pair counter of this CTA
+        int g = 0;
         bool ok = true;
         for (int t = 0, u = blockIdx.x; u < num_items; ++t, u += gridDim.x) {
             const Item it = item_of(u, BH, H, S);
-            for (int p = 0; p < it.n / 2; ++p, ++gp) {
-                ok = __all_sync(0xffffffffu, ok && mbar_wait(dq_full, gp & 1, abort_flag));
-                const uint32_t stage = sdS(2 * (gp & 1));    // the pair's dS^T tiles: read by dQ, now free
-                if (ok) {
-                    fence_after();
+            const int n = subtiles(u);
+            for (int i = 0; i < n; ++i, ++g) {
+                ok = __all_sync(0xffffffffu, ok && mbar_wait(dq_full, g & 1, abort_flag));
+                if (ok) fence_after();
 #pragma unroll 1
-                    for (int hc = 0; hc < 2; ++hc) {          // 32 columns at a time
-                        uint32_t a[32];
+                for (int hc = 0; hc < 2; ++hc) {              // 32 columns at a time through the staging tile
+                    uint32_t a[32];
+                    if (ok) {
                         tmem_ld32(tmem + lane_off + DQ_COL + hc * 32, a);
                         tmem_wait_ld();
                         if (hc == 1) {
@@ -397,24 +435,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                             __syncwarp();
                             if (lane == 0) mbar_arrive(dq_free);
                         }
+                    }
+                    if (elected) bulk_wait_read0();           // the previous reduce-add has read the staging
+                    named_sync(1, 128);
+                    if (ok) {
 #pragma unroll
                         for (int c = 0; c < 8; ++c)
-                            st_shared_v4(stage_addr(stage, r, hc * 8 + c),
-                                         __float_as_uint(__uint_as_float(a[4 * c]) * scale),
+                            st_shared_v4(stage_addr(sStg, r, c), __float_as_uint(__uint_as_float(a[4 * c]) * scale),
                                          __float_as_uint(__uint_as_float(a[4 * c + 1]) * scale),
                                          __float_as_uint(__uint_as_float(a[4 * c + 2]) * scale),
                                          __float_as_uint(__uint_as_float(a[4 * c + 3]) * scale));
                     }
-                }
-                fence_proxy_async();
-                named_sync(1, 128);
-                if (elected && ok) {
-                    const int y = it.krow0 + p * 128;
-                    tma_reduce_add_2d(&tmdq, stage, it.h * HD, y);
-                    tma_reduce_add_2d(&tmdq, stage + 16384, it.h * HD + 32, y);
-                    bulk_commit();
-                    bulk_wait_read0();                        // staging read: the tiles may be rewritten
-                    mbar_arrive(ds_free(gp & 1));
+                    fence_proxy_async();
+                    named_sync(1, 128);
+                    if (elected && ok) {
+                        tma_reduce_add_2d(&tmdq, sStg, it.h * HD + hc * 32, it.krow0 + i * BQ);
+                        bulk_commit();
+                    }
                 }
             }
             // dK (scaled) and dV: TMEM -> FP16 in the item's K / V tiles (128B-swizzled rows, the
@@ -713,6 +750,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(s_free);           // the producer may compute the next sub-tile
                 const uint32_t rowp = sRow(s);
+                const uint64_t c2 = pair_of(scale_log2);
                 uint32_t pk[8], dk[8];
                 auto compute = [&](auto masked) {
                     const int lim = r - BQ * i - c0;
@@ -723,12 +761,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const float nlv[4] = {nl.x, nl.y, nl.z, nl.w}, dtv[4] = {dt.x, dt.y, dt.z, dt.w};
                         float pv[4], dv[4];
 #pragma unroll
-                        for (int e4 = 0; e4 < 4; ++e4) {
+                        for (int e4 = 0; e4 < 4; e4 += 2) {       // packed FP32 pairs
                             const int e = 4 * q4 + e4;
-                            float p = ex2(fmaf(__uint_as_float(sr[e]), scale_log2, nlv[e4]));
-                            if (decltype(masked)::value) p = e < lim ? 0.0f : p;
-                            pv[e4] = p;
-                            dv[e4] = p * (__uint_as_float(dr[e]) - dtv[e4]);
+                            float x0, x1;
+                            ffma2v(x0, x1, __uint_as_float(sr[e]), __uint_as_float(sr[e + 1]), c2, nlv[e4],
+                                   nlv[e4 + 1]);
+                            float p0 = ex2(x0), p1 = ex2(x1);
+                            if (decltype(masked)::value) {
+                                p0 = e < lim ? 0.0f : p0;
+                                p1 = e + 1 < lim ? 0.0f : p1;
+                            }
+                            pv[e4] = p0;
+                            pv[e4 + 1] = p1;
+                            float d0, d1;
+                            fsub2(d0, d1, __uint_as_float(dr[e]), __uint_as_float(dr[e + 1]), dtv[e4], dtv[e4 + 1]);
+                            fmul2(dv[e4], dv[e4 + 1], p0, p1, d0, d1);
                         }
                         pk[2 * q4] = pack_h2(pv[0], pv[1]);
                         pk[2 * q4 + 1] = pack_h2(pv[2], pv[3]);

@@ -60,26 +60,6 @@ __device__ __forceinline__ float ex2(float x) {
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
 }
-// Packed FP32 pairs (sm_100): one instruction for two lanes of arithmetic.
-__device__ __forceinline__ uint64_t pair_of(float a) {
-    return ((uint64_t)__float_as_uint(a) << 32) | __float_as_uint(a);
-}
-// (y0, y1) = (x0, x1) * a2 + b2
-__device__ __forceinline__ void ffma2(float& y0, float& y1, float x0, float x1, uint64_t a2, uint64_t b2) {
-    asm("{\n\t.reg .b64 xx, yy;\n\tmov.b64 xx, {%2, %3};\n\tfma.rn.f32x2 yy, xx, %4, %5;\n\tmov.b64 {%0, %1}, yy;\n\t}"
-        : "=f"(y0), "=f"(y1)
-        : "f"(x0), "f"(x1), "l"(a2), "l"(b2));
-}
-// acc += (x0, x1), lane-wise
-__device__ __forceinline__ void fadd2(uint64_t& acc, float x0, float x1) {
-    asm("{\n\t.reg .b64 xx;\n\tmov.b64 xx, {%1, %2};\n\tadd.rn.f32x2 %0, %0, xx;\n\t}" : "+l"(acc) : "f"(x0), "f"(x1));
-}
-__device__ __forceinline__ float fmax3(float a, float b, float c) {
-    float y;
-    asm("max.f32 %0, %1, %2, %3;" : "=f"(y) : "f"(a), "f"(b), "f"(c));
-    return y;
-}
-
 template <int HD>
 __global__ void __launch_bounds__(FwdCfg<HD>::THREADS, FwdCfg<HD>::CTAS_PER_SM)
     flash_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmkv, half* O,

@@ -167,6 +167,14 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
 }
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* r) {
     asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
                  "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
@@ -188,6 +196,46 @@ __device__ __forceinline__ void tmem_alloc(uint32_t* slot_smem, uint32_t cols) {
 }
 __device__ __forceinline__ void tmem_free(uint32_t taddr, uint32_t cols) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols));
+}
+
+// Packed FP32 pairs (sm_100): one instruction for two lanes of arithmetic.
+__device__ __forceinline__ uint64_t pair_of(float a) {
+    return ((uint64_t)__float_as_uint(a) << 32) | __float_as_uint(a);
+}
+// (y0, y1) = (x0, x1) * a2 + b2
+__device__ __forceinline__ void ffma2(float& y0, float& y1, float x0, float x1, uint64_t a2, uint64_t b2) {
+    asm("{\n\t.reg .b64 xx, yy;\n\tmov.b64 xx, {%2, %3};\n\tfma.rn.f32x2 yy, xx, %4, %5;\n\tmov.b64 {%0, %1}, yy;\n\t}"
+        : "=f"(y0), "=f"(y1)
+        : "f"(x0), "f"(x1), "l"(a2), "l"(b2));
+}
+// acc += (x0, x1), lane-wise
+__device__ __forceinline__ void fadd2(uint64_t& acc, float x0, float x1) {
+    asm("{\n\t.reg .b64 xx;\n\tmov.b64 xx, {%1, %2};\n\tadd.rn.f32x2 %0, %0, xx;\n\t}" : "+l"(acc) : "f"(x0), "f"(x1));
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float y;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(y) : "f"(a), "f"(b), "f"(c));
+    return y;
+}
+// (y0, y1) = (a0, a1) - (b0, b1) and (y0, y1) = (a0, a1) * (b0, b1), lane-wise
+__device__ __forceinline__ void fsub2(float& y0, float& y1, float a0, float a1, float b0, float b1) {
+    asm("{\n\t.reg .b64 aa, bb, yy;\n\tmov.b64 aa, {%2, %3};\n\tmov.b64 bb, {%4, %5};\n\tsub.rn.f32x2 yy, aa, bb;\n\t"
+        "mov.b64 {%0, %1}, yy;\n\t}"
+        : "=f"(y0), "=f"(y1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ void fmul2(float& y0, float& y1, float a0, float a1, float b0, float b1) {
+    asm("{\n\t.reg .b64 aa, bb, yy;\n\tmov.b64 aa, {%2, %3};\n\tmov.b64 bb, {%4, %5};\n\tmul.rn.f32x2 yy, aa, bb;\n\t"
+        "mov.b64 {%0, %1}, yy;\n\t}"
+        : "=f"(y0), "=f"(y1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+// (y0, y1) = (x0, x1) * a2 + (b0, b1)
+__device__ __forceinline__ void ffma2v(float& y0, float& y1, float x0, float x1, uint64_t a2, float b0, float b1) {
+    asm("{\n\t.reg .b64 xx, bb, yy;\n\tmov.b64 xx, {%2, %3};\n\tmov.b64 bb, {%5, %6};\n\tfma.rn.f32x2 yy, xx, %4, bb;\n\t"
+        "mov.b64 {%0, %1}, yy;\n\t}"
+        : "=f"(y0), "=f"(y1)
+        : "f"(x0), "f"(x1), "l"(a2), "f"(b0), "f"(b1));
 }
 
 // ------------------------------------------------ CTA pairs (cta_group::2) ----
