@@ -315,6 +315,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     __syncthreads();
     fence_after();
     const uint32_t tmem = *tmem_slot;
+    grid_dependency_sync();
 
     if (warp == 0) {
         // ------------------------------ TMA producer ------------------------
@@ -591,6 +592,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     cluster_sync();                                  // the peer's barriers are initialised
     fence_after();
     const uint32_t tmem = *tmem_slot;
+    grid_dependency_sync();
 
     if (warp == 0) {
         // ------------------------------ TMA producer (both CTAs) -------------
@@ -728,7 +730,15 @@ int launch(rbk_ctx* ctx, const rbk_gemm_desc* d, Params& p, cudaStream_t st) {
         configured_device = ctx->device;
     }
     int grid = p.units < ctx->num_sms ? p.units : ctx->num_sms;
-    gemm_kernel<BN, EPI><<<grid, kThreads, C::SMEM, st>>>(ta, tb, p);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = st;
+    cfg.numAttrs = set_pdl(attr, 0);
+    cfg.attrs = attr;
+    RBK_CUDA(cudaLaunchKernelEx(&cfg, gemm_kernel<BN, EPI>, ta, tb, p));
     RBK_LAUNCHED("gemm_kernel");
     return RBK_OK;
 }
@@ -756,7 +766,7 @@ int launch_pair(rbk_ctx* ctx, const rbk_gemm_desc* d, Params& p, cudaStream_t st
     if (!d->b_major) RBK_TRY(make_tmap(&tb, d->B, d->K, d->N, d->ldb, 64, 128));
     else RBK_TRY(make_tmap(&tb, d->B, d->N, d->K, d->ldb, 64, 64));
     cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
@@ -777,6 +787,7 @@ int launch_pair(rbk_ctx* ctx, const rbk_gemm_desc* d, Params& p, cudaStream_t st
     }
     const int pairs = p.units < max_pairs ? p.units : max_pairs;
     cfg.gridDim = dim3(2 * pairs);
+    cfg.numAttrs = set_pdl(attr, 1);
     RBK_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<EPI>, ta, tb, tc_, tx, p));
     RBK_LAUNCHED("gemm_pair_kernel");
     return RBK_OK;
