@@ -230,6 +230,7 @@ template <int HD>
 __global__ void flash_bwd_pre_kernel(float* __restrict__ Dot, float* __restrict__ dq_acc, float* __restrict__ NL2,
                                      const float* __restrict__ LSE, const half* __restrict__ O,
                                      const half* __restrict__ dO, int BS, int S, int H) {
+    grid_dependency_sync();
     constexpr int G = HD / 8;            // chunks per (row, head)
     const int D = H * HD;
     const long total = (long)BS * (D / 8);
@@ -463,6 +464,7 @@ __global__ void __launch_bounds__(512) flash_bwd_post_kernel(half* __restrict__ 
                                                              const float* __restrict__ dq_acc,
                                                              const half* __restrict__ dO, int BS, int D,
                                                              int rows_per_block) {
+    grid_dependency_sync();
     __shared__ float red[2][3][128][9];                 // [q|v][row groups 1..3][column group][8 (+1 pad)]
     const int c8 = blockIdx.x * 128 + threadIdx.x;      // 8-column group
     const bool col_ok = c8 * 8 < D;
@@ -538,8 +540,8 @@ int bwd(rbk_ctx* ctx, void* dqkv, float* dbias, const void* qkv, const void* o, 
         const long work = (long)BS * (D / 8);
         long gsz = (work + 255) / 256;
         if (gsz > ctx->num_sms * 16) gsz = ctx->num_sms * 16;
-        flash_bwd_pre_kernel<HD><<<(int)gsz, 256, 0, st>>>(Dot, dq_acc, tc ? NL2 : nullptr, lse, (const half*)o,
-                                                           (const half*)dout, (int)BS, S, H);
+        RBK_CUDA(launch_pdl(flash_bwd_pre_kernel<HD>, dim3((int)gsz), dim3(256), 0, st, Dot, dq_acc,
+                            tc ? NL2 : nullptr, lse, (const half*)o, (const half*)dout, (int)BS, S, H));
         RBK_LAUNCHED("flash_bwd_pre_kernel");
     }
     if (tc) {
@@ -560,8 +562,8 @@ int bwd(rbk_ctx* ctx, void* dqkv, float* dbias, const void* qkv, const void* o, 
     // bias atomic per column per CTA
     const int rows_per_block = 128;
     dim3 pg((D / 8 + 127) / 128, (int)((BS + rows_per_block - 1) / rows_per_block));
-    flash_bwd_post_kernel<<<pg, dim3(128, 4), 0, st>>>((half*)dqkv, dbias, dq_acc, tc ? (const half*)dout : nullptr,
-                                                       (int)BS, D, rows_per_block);
+    RBK_CUDA(launch_pdl(flash_bwd_post_kernel, pg, dim3(128, 4), 0, st, (half*)dqkv, dbias, (const float*)dq_acc,
+                        tc ? (const half*)dout : nullptr, (int)BS, D, rows_per_block));
     RBK_LAUNCHED("flash_bwd_post_kernel");
     return RBK_OK;
 }

@@ -196,6 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     fence_after();
     const uint32_t tmem = *tmem_slot;
+    grid_dependency_sync();
 
     if (warp == 0) {
         // ---------------------------------------------------------- TMA ----
@@ -620,6 +621,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     fence_after();
     const uint32_t tmem = *tmem_slot;
+    grid_dependency_sync();
 
     if (warp == 0) {
         // ---------------------------------------------------------- TMA ----
@@ -897,9 +899,9 @@ int attn_bwd_tc(rbk_ctx* ctx, void* dqkv, float* dq_acc, const void* qkv, const 
             RBK_CUDA(cudaFuncSetAttribute(flash_bwd_tc128_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
             set_dev = ctx->device;
         }
-        flash_bwd_tc128_kernel<<<grid, kThreads, SMEM, st>>>(tmq, tmkv, tmdo, (half*)dqkv, dq_acc, NL2, Dot, S, H,
-                                                             items, scale, scale * 1.4426950408889634f,
-                                                             ctx->tickets + kGemmError);
+        RBK_CUDA(launch_pdl(flash_bwd_tc128_kernel, dim3(grid), dim3(kThreads), SMEM, st, tmq, tmkv, tmdo, (half*)dqkv,
+                            dq_acc, NL2, Dot, S, H, items, scale, scale * 1.4426950408889634f,
+                            ctx->tickets + kGemmError));
         RBK_LAUNCHED("flash_bwd_tc128_kernel");
         return RBK_OK;
     }
@@ -917,8 +919,8 @@ int attn_bwd_tc(rbk_ctx* ctx, void* dqkv, float* dq_acc, const void* qkv, const 
         RBK_CUDA(cudaFuncSetAttribute(flash_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
         set_dev = ctx->device;
     }
-    flash_bwd_tc_kernel<<<grid, kThreads, SMEM, st>>>(tmq, tmkv, tmdo, tmdq, tmout, NL2, Dot, S, H, items, scale,
-                                                      scale * 1.4426950408889634f, ctx->tickets + kGemmError);
+    RBK_CUDA(launch_pdl(flash_bwd_tc_kernel, dim3(grid), dim3(kThreads), SMEM, st, tmq, tmkv, tmdo, tmdq, tmout, NL2,
+                        Dot, S, H, items, scale, scale * 1.4426950408889634f, ctx->tickets + kGemmError));
     RBK_LAUNCHED("flash_bwd_tc_kernel");
     return RBK_OK;
 }

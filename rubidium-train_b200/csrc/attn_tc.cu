@@ -118,6 +118,7 @@ __global__ void __launch_bounds__(FwdCfg<HD>::THREADS, FwdCfg<HD>::CTAS_PER_SM)
     __syncthreads();
     fence_after();
     const uint32_t tmem = *tmem_slot;
+    grid_dependency_sync();
 
     if (warp == 0) {
         // ---------------------------------------------------------- TMA ----
@@ -339,8 +340,8 @@ static int attn_fwd_tc_hd(rbk_ctx* ctx, void* o, float* lse, const void* qkv, in
         set_dev = ctx->device;
     }
     dim3 grid(S / BQ, B * H);
-    flash_fwd_tc_kernel<HD><<<grid, FwdCfg<HD>::THREADS, FwdCfg<HD>::SMEM, st>>>(
-        tmq, tmkv, (half*)o, lse, S, H, scale * 1.4426950408889634f, ctx->tickets + kGemmError);
+    RBK_CUDA(launch_pdl(flash_fwd_tc_kernel<HD>, grid, dim3(FwdCfg<HD>::THREADS), FwdCfg<HD>::SMEM, st, tmq, tmkv,
+                        (half*)o, lse, S, H, scale * 1.4426950408889634f, ctx->tickets + kGemmError));
     RBK_LAUNCHED("flash_fwd_tc_kernel");
     return RBK_OK;
 }

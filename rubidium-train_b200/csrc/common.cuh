@@ -7,6 +7,8 @@
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
+#include <utility>
 #include <vector>
 
 #include "rbk.h"
@@ -105,6 +107,38 @@ enum TicketSlot {
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ------------------------------------------------ programmatic dependent launch
+// A kernel launched with launch_pdl() may start while the previous kernel of its
+// stream is still finishing.  It may set up shared memory, barriers and TMEM,
+// but must call grid_dependency_wait() before its first global-memory access:
+// that blocks until the previous kernel has completed and its writes are
+// visible.  grid_dependents_launch() lets the next programmatic dependent start
+// its own setup (every CTA must have called it, or exited).
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dependents_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dependency_sync() {
+    grid_dependency_wait();
+    grid_dependents_launch();
+}
+// Adds the programmatic-stream-serialization attribute at attr[i] unless
+// RBK_NO_PDL=1; returns the attribute count.
+unsigned set_pdl(cudaLaunchAttribute* attr, unsigned i);
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = set_pdl(attr, 0);
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // ----------------------------------------------------------------------------
 // Device helpers

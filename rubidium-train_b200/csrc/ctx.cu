@@ -70,6 +70,17 @@ __global__ void column_reduce_kernel(float* __restrict__ out, const float* __res
     out[c] += s;
 }
 
+unsigned set_pdl(cudaLaunchAttribute* attr, unsigned i) {
+    static const bool off = [] {
+        const char* e = getenv("RBK_NO_PDL");
+        return e && e[0] == '1';
+    }();
+    if (off) return i;
+    attr[i].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[i].val.programmaticStreamSerializationAllowed = 1;
+    return i + 1;
+}
+
 int column_reduce(float* out, const float* part, int R, int C, cudaStream_t st) {
     column_reduce_kernel<<<(C + 255) / 256, 256, 0, st>>>(out, part, R, C);
     RBK_LAUNCHED("column_reduce_kernel");

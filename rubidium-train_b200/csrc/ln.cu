@@ -27,6 +27,7 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(half* __restrict__ y, float
                                                      float* __restrict__ rstd, const half* __restrict__ x,
                                                      const half* __restrict__ g, const half* __restrict__ b, int N,
                                                      int D, float eps) {
+    grid_dependency_sync();
     const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
     const int nvec = D >> 3;
     const float invD = 1.0f / (float)D;
@@ -199,7 +200,7 @@ __global__ void __launch_bounds__(1024) ln_bwd_reduce_kernel(float* __restrict__
                                                              float* __restrict__ dbias,
                                                              const float* __restrict__ part, int nblk, int D) {
     // launched as a programmatic dependent of the main pass: wait for its partials
-    asm volatile("griddepcontrol.wait;" ::: "memory");
+    grid_dependency_sync();
     __shared__ float s[32][33];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int c = blockIdx.x * 32 + lane;
@@ -269,6 +270,7 @@ __global__ void __launch_bounds__(544, 1)
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
+    grid_dependency_wait();                             // dependents are released at the end
     const int nstage = (N + RS - 1) / RS;
 
     if (tid >= consumers) {
@@ -439,15 +441,16 @@ int launch_bwd_ring(int blocks, int threads, int teams, int tpt, int stages, siz
                     float* part, const half* dy, const half* dres, const half* x, const half* g, const float* mean,
                     const float* rstd, int N, int D, int* err) {
     RBK_CUDA(cudaFuncSetAttribute(ln_bwd_ring_kernel<A, B, C>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    ln_bwd_ring_kernel<A, B, C><<<blocks, threads, smem, st>>>(dx, part, dy, dres, x, g, mean, rstd, N, D, teams, tpt,
-                                                               stages, err);
+    RBK_CUDA(launch_pdl(ln_bwd_ring_kernel<A, B, C>, dim3(blocks), dim3(threads), smem, st, dx, part, dy, dres, x, g,
+                        mean, rstd, N, D, teams, tpt, stages, err));
     return RBK_OK;
 }
 
 template <int NV>
-void launch_fwd(int blocks, cudaStream_t st, half* y, float* mean, float* rstd, const half* x, const half* g,
-                const half* b, int N, int D, float eps) {
-    ln_fwd_kernel<NV><<<blocks, 256, 0, st>>>(y, mean, rstd, x, g, b, N, D, eps);
+int launch_fwd(int blocks, cudaStream_t st, half* y, float* mean, float* rstd, const half* x, const half* g,
+               const half* b, int N, int D, float eps) {
+    RBK_CUDA(launch_pdl(ln_fwd_kernel<NV>, dim3(blocks), dim3(256), 0, st, y, mean, rstd, x, g, b, N, D, eps));
+    return RBK_OK;
 }
 
 template <bool A, bool B, bool C>
@@ -483,17 +486,19 @@ int rbk_ln_fwd(rbk_ctx* ctx, void* y, float* mean, float* rstd, const void* x, c
     auto X = (const half*)x;
     auto G = (const half*)gamma;
     auto Bt = (const half*)beta;
+    int rc;
     switch (nv) {
-        case 1: launch_fwd<1>(blocks, st, Y, mean, rstd, X, G, Bt, N, D, eps); break;
-        case 2: launch_fwd<2>(blocks, st, Y, mean, rstd, X, G, Bt, N, D, eps); break;
-        case 3: launch_fwd<3>(blocks, st, Y, mean, rstd, X, G, Bt, N, D, eps); break;
-        case 4: launch_fwd<4>(blocks, st, Y, mean, rstd, X, G, Bt, N, D, eps); break;
-        case 5: case 6: launch_fwd<6>(blocks, st, Y, mean, rstd, X, G, Bt, N, D, eps); break;
-        case 7: case 8: launch_fwd<8>(blocks, st, Y, mean, rstd, X, G, Bt, N, D, eps); break;
-        case 9: case 10: case 11: case 12: launch_fwd<12>(blocks, st, Y, mean, rstd, X, G, Bt, N, D, eps); break;
-        case 13: case 14: case 15: case 16: launch_fwd<16>(blocks, st, Y, mean, rstd, X, G, Bt, N, D, eps); break;
-        default: launch_fwd<32>(blocks, st, Y, mean, rstd, X, G, Bt, N, D, eps); break;
+        case 1: rc = launch_fwd<1>(blocks, st, Y, mean, rstd, X, G, Bt, N, D, eps); break;
+        case 2: rc = launch_fwd<2>(blocks, st, Y, mean, rstd, X, G, Bt, N, D, eps); break;
+        case 3: rc = launch_fwd<3>(blocks, st, Y, mean, rstd, X, G, Bt, N, D, eps); break;
+        case 4: rc = launch_fwd<4>(blocks, st, Y, mean, rstd, X, G, Bt, N, D, eps); break;
+        case 5: case 6: rc = launch_fwd<6>(blocks, st, Y, mean, rstd, X, G, Bt, N, D, eps); break;
+        case 7: case 8: rc = launch_fwd<8>(blocks, st, Y, mean, rstd, X, G, Bt, N, D, eps); break;
+        case 9: case 10: case 11: case 12: rc = launch_fwd<12>(blocks, st, Y, mean, rstd, X, G, Bt, N, D, eps); break;
+        case 13: case 14: case 15: case 16: rc = launch_fwd<16>(blocks, st, Y, mean, rstd, X, G, Bt, N, D, eps); break;
+        default: rc = launch_fwd<32>(blocks, st, Y, mean, rstd, X, G, Bt, N, D, eps); break;
     }
+    if (rc != RBK_OK) return rc;
     RBK_LAUNCHED("ln_fwd_kernel");
     return RBK_OK;
 }

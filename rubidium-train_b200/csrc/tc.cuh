@@ -310,29 +310,7 @@ __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, 
                  : "memory");
 }
 
-// Programmatic dependent launch.  A kernel launched with set_pdl() may start
-// while the previous kernel of its stream is still finishing: it sets up
-// shared memory, barriers and TMEM, then grid_dependency_sync() blocks until
-// that kernel has completed and its writes are visible, before any global
-// memory access, and lets the next such kernel start its own setup.
-__device__ __forceinline__ void grid_dependency_sync() {
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-
 // ---------------------------------------------------------------- host ----
-// Adds the programmatic-stream-serialization attribute at attr[i] unless
-// RBK_NO_PDL=1; returns the attribute count.
-inline unsigned set_pdl(cudaLaunchAttribute* attr, unsigned i) {
-    static const bool off = [] {
-        const char* e = getenv("RBK_NO_PDL");
-        return e && e[0] == '1';
-    }();
-    if (off) return i;
-    attr[i].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[i].val.programmaticStreamSerializationAllowed = 1;
-    return i + 1;
-}
 inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag once;

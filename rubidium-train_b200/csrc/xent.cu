@@ -153,6 +153,7 @@ __global__ void __launch_bounds__(kRingConsumers + 32, 1)
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
+    grid_dependency_sync();
     const int nchunk = (V + 7) >> 3;                    // 16-byte chunks per row (tail masked)
     if (tid >= kRingConsumers) {
         // ------------------------------------------------------ producer ----
@@ -304,9 +305,9 @@ extern "C" int rbk_softmax_xent_bwd(rbk_ctx* ctx, void* dlogits, const void* log
             set_dev = ctx->device;
         }
         const int rgrid = N < ctx->num_sms ? N : ctx->num_sms;
-        xent_ring_kernel<<<rgrid, kRingConsumers + 32, smem, st>>>((half*)dlogits, (const half*)logits, ld, targets,
-                                                                   N, V, scale, dscale, row_loss, nbuf, rowb,
-                                                                   ctx->tickets + kGemmError);
+        RBK_CUDA(launch_pdl(xent_ring_kernel, dim3(rgrid), dim3(kRingConsumers + 32), smem, st, (half*)dlogits,
+                            (const half*)logits, ld, targets, N, V, scale, dscale, row_loss, nbuf, rowb,
+                            ctx->tickets + kGemmError));
         RBK_LAUNCHED("xent_ring_kernel");
         return RBK_OK;
     }
