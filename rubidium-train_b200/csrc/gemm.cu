@@ -542,6 +542,16 @@ __device__ __forceinline__ void epilogue_chunk_tma(const Params& p, int m0, int 
 // the MMA thread; tempty[b] lives in the even CTA and takes the arrivals of
 // both CTAs' epilogue warps.  Bounded waits as in gemm_kernel.
 constexpr int kPairStages = 6;
+// Per-warp epilogue staging: two 2 KB tensor-store tiles for FP16 outputs; the
+// FP32 epilogues stage 32 x 80 B and keep a 2 KB ones tile for row sums.
+template <int EPI>
+struct PairEpi {
+    static constexpr bool TMA = EPI == RBK_EPI_STORE_F16 || EPI == RBK_EPI_BIAS_GELU || EPI == RBK_EPI_GELU_BWD;
+    static constexpr int WARP_STAGE = TMA ? kTmaStageBytes : kStageBytes;
+    static constexpr int ONES_BYTES = EPI == RBK_EPI_ACC_F32 ? 2048 : 0;
+    static constexpr int SMEM = 1024 + kPairStages * (BM * BK * 2 + 128 * BK * 2) + kEpiWarps * WARP_STAGE +
+                                ONES_BYTES + 256;
+};
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -550,13 +560,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int BN = 256, HALF_N = 128;
     constexpr int A_BYTES = BM * BK * 2, B_BYTES = HALF_N * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
     constexpr int STAGES = kPairStages;
+    constexpr bool kTma = EPI == RBK_EPI_STORE_F16 || EPI == RBK_EPI_BIAS_GELU || EPI == RBK_EPI_GELU_BWD;
+    constexpr int kWarpStage = PairEpi<EPI>::WARP_STAGE;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = su32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t* gbase = smem_raw + (base - raw);
     const uint32_t sA0 = base;
     const uint32_t epi_stage = base + STAGES * STAGE_BYTES;
-    const uint32_t bars = epi_stage + kEpiWarps * kTmaStageBytes;
+    const uint32_t ones = epi_stage + kEpiWarps * kWarpStage;       // FP32 epilogues: 2 KB of FP16 ones
+    const uint32_t bars = ones + PairEpi<EPI>::ONES_BYTES;
     uint8_t* gbars = gbase + (bars - base);
     auto full_bar = [&](int s) { return bars + 8u * s; };
     auto empty_bar = [&](int s) { return bars + 8u * (STAGES + s); };
@@ -569,6 +582,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t rank = cluster_rank();
     const bool leader = rank == 0;
     const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
+    // Row sums of A (the bias gradient of a weight gradient, A = dY^T): an extra N = 16 pair MMA per
+    // k-step against a ones tile, accumulated at TMEM column 256, so only one 256-column accumulator
+    // buffer remains (the K = tokens mainloops of weight gradients dwarf their epilogues).
+    constexpr bool kRowsumEpi = EPI == RBK_EPI_ACC_F32;
+    const bool rowsum_mode = kRowsumEpi && p.dbias_rows != nullptr;
+    const int nbuf = rowsum_mode ? 1 : 2;
+    if constexpr (kRowsumEpi) {
+        uint32_t* o = reinterpret_cast<uint32_t*>(gbase + (ones - base));
+        for (int i = threadIdx.x; i < PairEpi<EPI>::ONES_BYTES / 4; i += blockDim.x) o[i] = 0x3C003C00u;
+        fence_proxy_async();
+    }
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -632,6 +656,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------ MMA issuer (even CTA) ----------------
         if (leader && lane == 0) {
             const uint32_t idesc = idesc_f16_m256(BN, p.a_mn, p.b_mn);
+            const uint32_t idesc1 = idesc_f16_m256(16, p.a_mn, 0);
             const uint32_t a_lbo = p.a_mn ? 8192u : 16u, b_lbo = p.b_mn ? 8192u : 16u;
             const uint32_t a_kstep = p.a_mn ? 2048u : 32u, b_kstep = p.b_mn ? 2048u : 32u;
             int stage = 0, buf = 0;
@@ -639,6 +664,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int u = pair; u < p.units && !*abort_flag; u += num_pairs) {
                 int mb, nb, kb0, kb1;
                 decode_unit(p, u, mb, nb, kb0, kb1);
+                const bool rowsum = rowsum_mode && nb == 0;
                 if (!mbar_wait(tempty_bar(buf), bphase ^ 1, abort_flag)) break;
                 fence_after();
                 const uint32_t dacc = tmem + buf * BN;
@@ -649,9 +675,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t sa = sA0 + stage * STAGE_BYTES;
                     const uint32_t sb = sa + A_BYTES;
 #pragma unroll
-                    for (int k = 0; k < BK / UMMA_K; ++k)
-                        mma_f16_pair(dacc, sdesc(sa + k * a_kstep, a_lbo, 1024), sdesc(sb + k * b_kstep, b_lbo, 1024),
-                                     idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+                    for (int k = 0; k < BK / UMMA_K; ++k) {
+                        const uint64_t ad = sdesc(sa + k * a_kstep, a_lbo, 1024);
+                        const uint32_t acc = (kb > kb0 || k > 0) ? 1u : 0u;
+                        mma_f16_pair(dacc, ad, sdesc(sb + k * b_kstep, b_lbo, 1024), idesc, acc);
+                        if (kRowsumEpi && rowsum) mma_f16_pair(tmem + 256, ad, sdesc(ones + k * 32, 16, 1024), idesc1, acc);
+                    }
                     mma_commit_pair(empty_bar(stage));
                     mma_commit_pair(mapa_shared(empty_bar(stage), 1));
                     if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -659,7 +688,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!ok) break;
                 mma_commit_pair(tfull_bar(buf));
                 mma_commit_pair(mapa_shared(tfull_bar(buf), 1));
-                if (++buf == 2) { buf = 0; bphase ^= 1; }
+                if (++buf == nbuf) { buf = 0; bphase ^= 1; }
             }
         }
     } else {
@@ -668,9 +697,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int half_id = (warp - 2) / 4;
         constexpr int kChunks = BN / 32;
         const int c0 = half_id * (kChunks / 2), c1 = half_id ? kChunks : kChunks / 2;
-        uint8_t* my_stage = gbase + (epi_stage - base) + (warp - 2) * kTmaStageBytes;
-        const uint32_t my_stage_s = epi_stage + (warp - 2) * kTmaStageBytes;
-        constexpr bool kTma = EPI == RBK_EPI_STORE_F16 || EPI == RBK_EPI_BIAS_GELU || EPI == RBK_EPI_GELU_BWD;
+        uint8_t* my_stage = gbase + (epi_stage - base) + (warp - 2) * kWarpStage;
+        const uint32_t my_stage_s = epi_stage + (warp - 2) * kWarpStage;
         int sc = 0;
         int buf = 0;
         uint32_t bphase = 0;
@@ -697,12 +725,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 else
                     epilogue_chunk<EPI>(p, m0, nb * BN + c * 32, r, my_stage, lane, cur);
             }
+            if (kRowsumEpi && rowsum_mode && nb == 0 && c0 == 0) {   // one warp per lane quarter
+                const uint32_t v = tmem_ld1(tmem + ((uint32_t)(q * 32) << 16) + 256);
+                tmem_wait_ld();
+                const int m = m0 + lane;
+                if (m < p.M) atomicAdd(p.dbias_rows + m, p.alpha * __uint_as_float(v));
+            }
             // the accumulator reads are complete (tcgen05.wait::ld); the tile's global stores need not
             // drain before the MMAs may reuse the buffer, so the arrival is relaxed
             fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster_relaxed(mapa_shared(tempty_bar(buf), 0));
-            if (++buf == 2) { buf = 0; bphase ^= 1; }
+            if (++buf == nbuf) { buf = 0; bphase ^= 1; }
         }
         if (kTma && lane == 0) bulk_wait0();               // tensor stores complete before exit
     }
@@ -746,9 +780,8 @@ int launch(rbk_ctx* ctx, const rbk_gemm_desc* d, Params& p, cudaStream_t st) {
 // Launched as 2-CTA clusters; grid = 2 x min(units, pairs that fit at once).
 template <int EPI>
 int launch_pair(rbk_ctx* ctx, const rbk_gemm_desc* d, Params& p, cudaStream_t st) {
-    constexpr int SMEM = 1024 + kPairStages * (BM * BK * 2 + 128 * BK * 2) + kEpiWarps * kTmaStageBytes + 256;
+    constexpr int SMEM = PairEpi<EPI>::SMEM;
     static_assert(SMEM <= 232448, "shared memory budget");
-    static_assert(kStageBytes <= kTmaStageBytes, "FP32 epilogues stage in the same per-warp tiles");
     CUtensorMap ta, tb, tc_, tx;
     // FP16 outputs: 32 x 32 store boxes over the logical [M, N] (ldc / ld_aux pitches)
     constexpr bool kTma = EPI == RBK_EPI_STORE_F16 || EPI == RBK_EPI_BIAS_GELU || EPI == RBK_EPI_GELU_BWD;
@@ -830,7 +863,7 @@ int rbk_gemm(rbk_ctx* ctx, const rbk_gemm_desc* d, void* stream) {
     // the ones-MMA accumulator fit the 512 TMEM columns; narrow problems use 128.
     int BN;
     if (epi == RBK_EPI_ACC_F32)
-        BN = d->N <= 128 ? 128 : (d->dbias_rows || d->N < 256) ? 192 : 256;
+        BN = d->N <= 128 ? 128 : d->N < 256 ? 192 : (d->dbias_rows && !pair_tiles()) ? 192 : 256;
     else
         BN = d->N >= 512 ? 256 : 128;
     // N = 256 problems run on CTA pairs (256 x 256 pair tiles)

@@ -343,7 +343,7 @@ def test_gemm_dgrad_gelu_bwd(ops, ora, Ntok, fin, out):
     assert rel(f(dX2), dY.astype(np.float64) @ W.astype(np.float64)) < F16_TOL
 
 
-@pytest.mark.parametrize("Ntok,fin,out", [(1000, 160, 192), (4096, 768, 2304), (333, 64, 136)])
+@pytest.mark.parametrize("Ntok,fin,out", [(1000, 160, 192), (4096, 768, 2304), (333, 64, 136), (1000, 520, 296)])
 def test_gemm_wgrad_with_bias_grad(ops, Ntok, fin, out):
     rng = np.random.default_rng(Ntok + fin)
     dY = _mk(rng, Ntok, out)
