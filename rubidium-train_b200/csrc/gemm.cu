@@ -50,6 +50,52 @@ __device__ __forceinline__ float gelu_grad_fast(float x) {
     const float t = tanh_fast(c * (x + a * x * x * x));
     return 0.5f * (1.0f + t) + 0.5f * x * (1.0f - t * t) * c * (1.0f + 3.0f * a * x * x);
 }
+// Two lanes at once with packed FP32 pairs (sm_100 fma/mul.rn.f32x2); the same
+// formulas: gelu = x (0.5 + 0.5 t), gelu' = 0.5 (1 + t) + 0.5 x (1 - t^2) c (1 + 3 a x^2),
+// t = tanh(c x (1 + a x^2)).
+__device__ __forceinline__ uint64_t f2pack(float a, float b) {
+    return ((uint64_t)__float_as_uint(b) << 32) | __float_as_uint(a);
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float& a, float& b) {
+    a = __uint_as_float((uint32_t)v);
+    b = __uint_as_float((uint32_t)(v >> 32));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ void gelu2(float& x0, float& x1) {
+    const uint64_t c2 = f2pack(0.7978845608028654f, 0.7978845608028654f), a2 = f2pack(0.044715f, 0.044715f);
+    const uint64_t one2 = f2pack(1.0f, 1.0f), half2 = f2pack(0.5f, 0.5f);
+    const uint64_t x = f2pack(x0, x1);
+    const uint64_t u = mul2(mul2(x, c2), fma2(mul2(x, x), a2, one2));   // c x (1 + a x^2)
+    float u0, u1;
+    f2unpack(u, u0, u1);
+    const uint64_t t = f2pack(tanh_fast(u0), tanh_fast(u1));
+    f2unpack(mul2(x, fma2(t, half2, half2)), x0, x1);
+}
+// (g0, g1) *= gelu'(x0, x1)
+__device__ __forceinline__ void gelu_grad2(float& g0, float& g1, float x0, float x1) {
+    const float c = 0.7978845608028654f, a = 0.044715f;
+    const uint64_t c2 = f2pack(c, c), a2 = f2pack(a, a), a3c = f2pack(3.0f * a, 3.0f * a);
+    const uint64_t one2 = f2pack(1.0f, 1.0f), half2 = f2pack(0.5f, 0.5f), hc2 = f2pack(0.5f * c, 0.5f * c);
+    const uint64_t mone2 = f2pack(-1.0f, -1.0f);
+    const uint64_t x = f2pack(x0, x1), xx = mul2(x, x);
+    const uint64_t u = mul2(mul2(x, c2), fma2(xx, a2, one2));
+    float u0, u1;
+    f2unpack(u, u0, u1);
+    const uint64_t t = f2pack(tanh_fast(u0), tanh_fast(u1));
+    const uint64_t omt = fma2(mul2(t, t), mone2, one2);                 // 1 - t^2
+    const uint64_t r = mul2(mul2(x, hc2), mul2(omt, fma2(xx, a3c, one2)));   // 0.5 c x (1 - t^2)(1 + 3 a x^2)
+    const uint64_t d = fma2(t, half2, fma2(one2, half2, r));              // 0.5 + 0.5 t + r
+    f2unpack(mul2(f2pack(g0, g1), d), g0, g1);
+}
 
 template <int BN>
 struct Cfg {
@@ -506,15 +552,19 @@ __device__ __forceinline__ void epilogue_chunk_tma(const Params& p, int m0, int 
         row_from_sw(tile, lane, b);
         __syncwarp();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            if constexpr (EPI == RBK_EPI_GELU_BWD) v[j] *= gelu_grad_fast(b[j]);
-            else v[j] += b[j];
+        for (int j = 0; j < 32; j += 2) {
+            if constexpr (EPI == RBK_EPI_GELU_BWD) {
+                gelu_grad2(v[j], v[j + 1], b[j], b[j + 1]);
+            } else {
+                v[j] += b[j];
+                v[j + 1] += b[j + 1];
+            }
         }
     }
     row_to_sw(tile, lane, v);
     if constexpr (kTwo) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = gelu_fast(v[j]);
+        for (int j = 0; j < 32; j += 2) gelu2(v[j], v[j + 1]);
         row_to_sw(st + 2048, lane, v);
     }
     fence_proxy_async();
