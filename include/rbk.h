@@ -218,7 +218,8 @@ int rbk_adam_tail(rbk_ctx* ctx, const rbk_tail_args* args, void* stream);
 
 enum {
     RBK_EPI_STORE_F16 = 0,  /* C16 = alpha*acc [+ bias[n]] [+ aux[m,n]]              */
-    RBK_EPI_BIAS_GELU = 1,  /* C16 = acc + bias[n] (pre-activation); aux_out16 = gelu */
+    RBK_EPI_BIAS_GELU = 1,  /* C16 = acc + bias[n] (pre-activation); aux_out16 = gelu;
+                               C may be NULL: only the activation is stored        */
     RBK_EPI_GELU_BWD = 2,   /* C16 = acc * gelu'(aux[m,n])                           */
     RBK_EPI_ACC_F32 = 3,    /* C32[m,n] += alpha*acc   (gradient accumulation)       */
     RBK_EPI_STORE_F32 = 4   /* C32[m,n] = alpha*acc                                  */

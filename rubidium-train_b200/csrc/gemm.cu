@@ -294,7 +294,7 @@ __device__ __forceinline__ void epilogue_chunk(const Params& p, int m0, int n, c
         }
         row_to_stage_h(st, lane, v);
         __syncwarp();
-        stage_out_h(st, reinterpret_cast<half*>(p.C), p.ldc, m0, n, p, lane);
+        if (p.C) stage_out_h(st, reinterpret_cast<half*>(p.C), p.ldc, m0, n, p, lane);
         __syncwarp();
         if constexpr (EPI == RBK_EPI_BIAS_GELU) {
 #pragma unroll
@@ -561,7 +561,8 @@ __device__ __forceinline__ void epilogue_chunk_tma(const Params& p, int m0, int 
             }
         }
     }
-    row_to_sw(tile, lane, v);
+    const bool store_c = !kTwo || p.C != nullptr;       // BIAS_GELU may store the activation only
+    if (store_c) row_to_sw(tile, lane, v);
     if constexpr (kTwo) {
 #pragma unroll
         for (int j = 0; j < 32; j += 2) gelu2(v[j], v[j + 1]);
@@ -570,7 +571,7 @@ __device__ __forceinline__ void epilogue_chunk_tma(const Params& p, int m0, int 
     fence_proxy_async();
     __syncwarp();
     if (lane == 0) {
-        tma_store_2d(tmC, st_s + t * 2048, n, m0);
+        if (store_c) tma_store_2d(tmC, st_s + t * 2048, n, m0);
         if constexpr (kTwo) tma_store_2d(tmX, st_s + 2048, n, m0);
         bulk_commit();
     }
@@ -838,8 +839,9 @@ int launch_pair(rbk_ctx* ctx, const rbk_gemm_desc* d, Params& p, cudaStream_t st
     memset(&tc_, 0, sizeof(tc_));
     memset(&tx, 0, sizeof(tx));
     if (kTma) {
-        RBK_TRY(make_tmap(&tc_, d->C, d->N, d->M, d->ldc, 32, 32, CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                          CU_TENSOR_MAP_SWIZZLE_64B));
+        if (d->C)
+            RBK_TRY(make_tmap(&tc_, d->C, d->N, d->M, d->ldc, 32, 32, CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                              CU_TENSOR_MAP_SWIZZLE_64B));
         if (EPI == RBK_EPI_BIAS_GELU)
             RBK_TRY(make_tmap(&tx, d->aux_out, d->N, d->M, d->ld_aux ? d->ld_aux : d->ldc, 32, 32,
                               CU_TENSOR_MAP_DATA_TYPE_FLOAT16, CU_TENSOR_MAP_SWIZZLE_64B));
@@ -894,7 +896,8 @@ using namespace rbk::gemm;
 extern "C" {
 
 int rbk_gemm(rbk_ctx* ctx, const rbk_gemm_desc* d, void* stream) {
-    RBK_REQUIRE(ctx && d && d->A && d->B && d->C, "rbk_gemm: null pointer");
+    RBK_REQUIRE(ctx && d && d->A && d->B && (d->C || (d->epilogue == RBK_EPI_BIAS_GELU && d->aux_out)),
+                "rbk_gemm: null pointer");
     RBK_REQUIRE(d->M > 0 && d->N > 0 && d->K > 0, "rbk_gemm: empty problem (M=%d N=%d K=%d)", d->M, d->N, d->K);
     RBK_REQUIRE(d->epilogue >= RBK_EPI_STORE_F16 && d->epilogue <= RBK_EPI_STORE_F32, "rbk_gemm: bad epilogue");
     RBK_REQUIRE(d->lda % 8 == 0 && d->ldb % 8 == 0 && d->ldc % 8 == 0 && (d->ld_aux % 8 == 0),

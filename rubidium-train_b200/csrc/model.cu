@@ -216,13 +216,15 @@ static int layer_attn_inputs(rbk_model* m, int l, int B, int S, cudaStream_t st)
     return RBK_OK;
 }
 
-static int layer_ffn_inputs(rbk_model* m, int l, int N, cudaStream_t st) {
+// fi = gelu(h2 W1^T + b1), and the pre-activation when the backward will read it (with
+// checkpointing, the forward's pre-activation is dead: the backward recomputes both)
+static int layer_ffn_inputs(rbk_model* m, int l, int N, cudaStream_t st, bool store_pre) {
     const int D = m->cfg.D, F = m->cfg.FF;
     LayerWeights& y = m->w.layers[l];
     LayerActs& la = m->act.layers[l];
     G g{m->ctx, st};
-    return g.raw(N, F, D, la.h2_checkpoint, D, 0, y.w1, D, 0, la.fi_pre, F, RBK_EPI_BIAS_GELU, y.b1, nullptr, F,
-                 la.fi);
+    return g.raw(N, F, D, la.h2_checkpoint, D, 0, y.w1, D, 0, store_pre ? la.fi_pre : nullptr, F, RBK_EPI_BIAS_GELU,
+                 y.b1, nullptr, F, la.fi);
 }
 
 static int forward(rbk_model* m, const int* tokens, const int* targets, int B, int S, float* loss_dev,
@@ -238,7 +240,7 @@ static int forward(rbk_model* m, const int* tokens, const int* targets, int B, i
         RBK_TRY(g.fwd(la.x1_checkpoint, D, la.ao, D, y.wo, N, D, D, y.bo, la.x_in, D));
         RBK_TRY(rbk_ln_fwd(m->ctx, la.h2_checkpoint, la.ln2_mean, la.ln2_inv_std, la.x1_checkpoint, y.ln2_w, y.ln2_b,
                            N, D, 1e-5f, st));
-        RBK_TRY(layer_ffn_inputs(m, l, N, st));
+        RBK_TRY(layer_ffn_inputs(m, l, N, st, !m->cfg.use_activation_checkpointing));
         half* out = (l + 1 < L) ? m->act.layers[l + 1].x_in : m->act.x_out;
         RBK_TRY(g.fwd(out, D, la.fi, F, y.w2, N, F, D, y.b2, la.x1_checkpoint, D));
     }
@@ -311,7 +313,7 @@ static int backward(rbk_model* m, const int* tokens, const int* targets, int B, 
         LayerActs& la = a.layers[l];
         if (ckpt) {
             RBK_TRY(layer_attn_inputs(m, l, B, S, st));
-            RBK_TRY(layer_ffn_inputs(m, l, N, st));
+            RBK_TRY(layer_ffn_inputs(m, l, N, st, true));
         } else if (m->lora.rank > 0) {
             // LoRA projections are recomputed from the stored h1 (they are not kept)
             RBK_TRY(layer_attn_inputs(m, l, B, S, st));

@@ -183,8 +183,9 @@ def adam_tail(p32, g, m, v, p16, scaler_buf, lr, b1=0.9, b2=0.999, eps=1e-8, wd=
 # --------------------------------------------------------------------- GEMM --
 
 def gemm(A, B, M, N, K, a_major=0, b_major=0, C_out=None, epilogue=EPI_STORE_F16, bias=None, aux=None,
-         aux_out=None, dbias_rows=None, alpha=1.0, split_k=0, lda=None, ldb=None, ldc=None, ld_aux=0):
-    """C[M,N] = op(A)[M,K] op(B)[N,K]^T on tcgen05 (see rbk_gemm_desc)."""
+         aux_out=None, dbias_rows=None, alpha=1.0, split_k=0, lda=None, ldb=None, ldc=None, ld_aux=0, store_c=True):
+    """C[M,N] = op(A)[M,K] op(B)[N,K]^T on tcgen05 (see rbk_gemm_desc).  store_c=False with
+    EPI_BIAS_GELU stores only the activation (aux_out)."""
     d = GemmDesc()
     d.M, d.N, d.K = M, N, K
     d.A, d.lda, d.a_major = A.data_ptr(), lda or A.shape[-1], a_major
@@ -192,7 +193,7 @@ def gemm(A, B, M, N, K, a_major=0, b_major=0, C_out=None, epilogue=EPI_STORE_F16
     if C_out is None:
         dt = torch.float32 if epilogue in (EPI_ACC_F32, EPI_STORE_F32) else torch.float16
         C_out = (torch.zeros if epilogue == EPI_ACC_F32 else torch.empty)(M, N, dtype=dt, device=A.device)
-    d.C, d.ldc = C_out.data_ptr(), ldc or C_out.shape[-1]
+    d.C, d.ldc = (C_out.data_ptr() if store_c else None), ldc or C_out.shape[-1]
     d.epilogue = epilogue
     d.bias = bias.data_ptr() if bias is not None else None
     d.aux = aux.data_ptr() if aux is not None else None

@@ -327,6 +327,10 @@ def test_gemm_bias_residual_gelu(ops):
     assert rel(f(pre), ref) < F16_TOL
     import oracle
     assert rel(f(act), oracle.act_fwd(f(pre))) < F16_TOL
+    # activation only (no pre-activation store): the same activation, bit for bit
+    act2 = torch.empty(M, N, dtype=torch.float16, device="cuda")
+    ops.gemm(h(X), h(W), M, N, K, C_out=pre, epilogue=ops.EPI_BIAS_GELU, bias=h(b), aux_out=act2, store_c=False)
+    assert torch.equal(act2, act)
 
 
 @pytest.mark.parametrize("Ntok,fin,out", [(260, 192, 320), (300, 640, 256), (777, 1024, 192)])
