@@ -558,9 +558,11 @@ int bwd(rbk_ctx* ctx, void* dqkv, float* dbias, const void* qkv, const void* o, 
                                                       (const half*)dout, lse, Dot, S, H, scale, scale * kLog2e);
         RBK_LAUNCHED("flash_bwd_kernel");
     }
-    // 512-thread CTAs over 128 rows: enough in flight to stream the FP32 accumulator, and one
-    // bias atomic per column per CTA
-    const int rows_per_block = 128;
+    // 512-thread CTAs, about four per SM: enough loads in flight to stream the FP32 accumulator,
+    // and one bias atomic per column per CTA (rows per CTA: a power of two in [16, 256])
+    const int col_blocks = (D / 8 + 127) / 128;
+    int rows_per_block = 16;
+    while (rows_per_block < 256 && (long)rows_per_block * 4 * ctx->num_sms < (long)BS * col_blocks) rows_per_block *= 2;
     dim3 pg((D / 8 + 127) / 128, (int)((BS + rows_per_block - 1) / rows_per_block));
     RBK_CUDA(launch_pdl(flash_bwd_post_kernel, pg, dim3(128, 4), 0, st, (half*)dqkv, dbias, (const float*)dq_acc,
                         tc ? (const half*)dout : nullptr, (int)BS, D, rows_per_block));
