@@ -222,22 +222,6 @@ __global__ void __launch_bounds__(FwdCfg<HD>::THREADS, FwdCfg<HD>::CTAS_PER_SM)
                 m = mx;
                 l *= corr;
             }
-            // p = 2^(s * scale * log2 e - m); a row with no visible key yet keeps m = -inf and p = 0
-            const float nm = m == -INFINITY ? 0.0f : -m;
-            const uint64_t c2 = pair_of(scale_log2), nm2 = pair_of(nm);
-            uint64_t rs2[2] = {0, 0};                     // two packed (even, odd) sum accumulators
-            uint32_t pk[32];                              // P as FP16 pairs
-#pragma unroll
-            for (int e = 0; e < 64; e += 2) {
-                float x0, x1;
-                ffma2(x0, x1, __uint_as_float(r[e]), __uint_as_float(r[e + 1]), c2, nm2);
-                const float p0 = ex2(x0), p1 = ex2(x1);
-                fadd2(rs2[(e >> 1) & 1], p0, p1);
-                __half2 hp = __floats2half2_rn(p0, p1);
-                pk[e >> 1] = *reinterpret_cast<uint32_t*>(&hp);
-            }
-            l += (__uint_as_float((uint32_t)rs2[0]) + __uint_as_float((uint32_t)(rs2[0] >> 32))) +
-                 (__uint_as_float((uint32_t)rs2[1]) + __uint_as_float((uint32_t)(rs2[1] >> 32)));
             // P buffer sb (and, with two groups, O_wg) was last read by PV_{j-2}
             if (j > 1) {
                 if (!mbar_wait(o_done(sb), ((j >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
@@ -248,24 +232,42 @@ __global__ void __launch_bounds__(FwdCfg<HD>::THREADS, FwdCfg<HD>::CTAS_PER_SM)
                     if (!mbar_wait(o_done((j - 1) & 1), ((j - 1) >> 1) & 1, abort_flag)) { ok = false; break; }
                     fence_after();
                 }
-#pragma unroll
-                for (int c = 0; c < HD / 32; ++c) {
-                    uint32_t t[32];
-                    tmem_ld32(tmem + lane_off + o_col + c * 32, t);
+#pragma unroll 1
+                for (int c = 0; c < HD / 16; ++c) {
+                    uint32_t t[16];
+                    tmem_ld16(tmem + lane_off + o_col + c * 16, t);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) t[e] = __float_as_uint(__uint_as_float(t[e]) * corr);
-                    tmem_st32(tmem + lane_off + o_col + c * 32, t);
+                    for (int e = 0; e < 16; ++e) t[e] = __float_as_uint(__uint_as_float(t[e]) * corr);
+                    tmem_st16(tmem + lane_off + o_col + c * 16, t);
                 }
                 tmem_wait_st();
             }
+            // p = 2^(s * scale * log2 e - m); a row with no visible key yet keeps m = -inf and p = 0.
+            // Each 16-byte chunk of 8 keys goes to shared memory as soon as it is packed.
+            const float nm = m == -INFINITY ? 0.0f : -m;
+            const uint64_t c2 = pair_of(scale_log2), nm2 = pair_of(nm);
+            uint64_t rs2[2] = {0, 0};                     // two packed (even, odd) sum accumulators
 #pragma unroll
             for (int c = 0; c < 8; ++c) {                 // 16-byte chunk = 8 keys, 128B swizzle
+                uint32_t pk[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int e = 8 * c + 2 * q;
+                    float x0, x1;
+                    ffma2(x0, x1, __uint_as_float(r[e]), __uint_as_float(r[e + 1]), c2, nm2);
+                    const float p0 = ex2(x0), p1 = ex2(x1);
+                    fadd2(rs2[q & 1], p0, p1);
+                    __half2 hp = __floats2half2_rn(p0, p1);
+                    pk[q] = *reinterpret_cast<uint32_t*>(&hp);
+                }
                 const uint32_t addr = sP(sb) + (uint32_t)row * 128u + (uint32_t)((c ^ (row & 7)) << 4);
-                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk[4 * c]),
-                             "r"(pk[4 * c + 1]), "r"(pk[4 * c + 2]), "r"(pk[4 * c + 3])
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk[0]), "r"(pk[1]), "r"(pk[2]),
+                             "r"(pk[3])
                              : "memory");
             }
+            l += (__uint_as_float((uint32_t)rs2[0]) + __uint_as_float((uint32_t)(rs2[0] >> 32))) +
+                 (__uint_as_float((uint32_t)rs2[1]) + __uint_as_float((uint32_t)(rs2[1] >> 32)));
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             fence_before();
             __syncwarp();
