@@ -296,10 +296,11 @@ __global__ void __launch_bounds__(544, 1)
         const int nvec = D >> 3;
         const bool own = ttid < nvec;                   // columns [8 ttid, 8 ttid + 8)
         const float invD = 1.0f / (float)D;
-        float gam[8], pg[8], pb[8], pd[8];
+        // packed FP32 pairs (sm_100 f32x2 arithmetic) over the thread's 8 columns
+        uint64_t gam[4], pg[4], pb[4], pd[4];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) { pg[j] = 0.0f; pb[j] = 0.0f; pd[j] = 0.0f; gam[j] = 0.0f; }
-        if (own) h8_to_f(__ldg(reinterpret_cast<const uint4*>(g) + ttid), gam);
+        for (int j = 0; j < 4; ++j) { pg[j] = 0; pb[j] = 0; pd[j] = 0; gam[j] = 0; }
+        if (own) h8_to_p(__ldg(reinterpret_cast<const uint4*>(g) + ttid), gam);
         bool ok = true;
         const uint32_t ring = su32(lsm_raw);
         // this team's row statistics are loaded one stage ahead, so their latency hides behind a stage
@@ -335,15 +336,19 @@ __global__ void __launch_bounds__(544, 1)
                 const int lr = r;                       // row inside the stage
                 float s1 = 0.0f, s2 = 0.0f;
                 if (ok && own && row0 + r < N) {
-                    float d[8], xx[8];
-                    h8_to_f(lds128(sb + (uint32_t)(lr * row_bytes + 16 * ttid)), d);
-                    h8_to_f(lds128(sb + (uint32_t)((RS + lr) * row_bytes + 16 * ttid)), xx);
+                    uint64_t d[4], xx[4];
+                    h8_to_p(lds128(sb + (uint32_t)(lr * row_bytes + 16 * ttid)), d);
+                    h8_to_p(lds128(sb + (uint32_t)((RS + lr) * row_bytes + 16 * ttid)), xx);
+                    const uint64_t m2 = pk2(mr[r], mr[r]);
+                    uint64_t a1 = 0, a2 = 0;
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const float dg = d[j] * gam[j];
-                        s1 += dg;
-                        s2 = fmaf(dg, xx[j] - mr[r], s2);
+                    for (int j = 0; j < 4; ++j) {
+                        const uint64_t dg = pmul2(d[j], gam[j]);
+                        a1 = padd2(a1, dg);
+                        a2 = pfma2(dg, psub2(xx[j], m2), a2);
                     }
+                    s1 = lo2(a1) + hi2(a1);
+                    s2 = lo2(a2) + hi2(a2);
                 }
                 v8[2 * r] = s1;
                 v8[2 * r + 1] = s2;
@@ -384,10 +389,10 @@ __global__ void __launch_bounds__(544, 1)
                 const int lr = r;
                 const int row = row0 + r;
                 if (ok && own && row < N) {
-                    float d[8], xx[8], o[8], rs[8];
-                    h8_to_f(lds128(sb + (uint32_t)(lr * row_bytes + 16 * ttid)), d);
-                    h8_to_f(lds128(sb + (uint32_t)((RS + lr) * row_bytes + 16 * ttid)), xx);
-                    if (kRes) h8_to_f(lds128(sb + (uint32_t)((2 * RS + lr) * row_bytes + 16 * ttid)), rs);
+                    uint64_t d[4], xx[4], o[4], rs[4];
+                    h8_to_p(lds128(sb + (uint32_t)(lr * row_bytes + 16 * ttid)), d);
+                    h8_to_p(lds128(sb + (uint32_t)((RS + lr) * row_bytes + 16 * ttid)), xx);
+                    if (kRes) h8_to_p(lds128(sb + (uint32_t)((2 * RS + lr) * row_bytes + 16 * ttid)), rs);
                     const float inv = rr[r], m = mr[r];
                     const float t1 = ts[2 * r], t2 = ts[2 * r + 1];
                     // exact: dx = inv * (dy g - (t1 + (x - m) * inv^2 * t2) / D); the reference formula
@@ -395,16 +400,17 @@ __global__ void __launch_bounds__(544, 1)
                     // dx = (inv g) dy + Bx x + C
                     const float Bx = -inv * (kRefFormula ? inv : inv * inv) * t2 * invD;
                     const float C = -inv * t1 * invD - Bx * m;
+                    const uint64_t inv2 = pk2(inv, inv), m2 = pk2(m, m), bx2 = pk2(Bx, Bx), c2 = pk2(C, C);
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        float v = fmaf(inv * gam[j], d[j], fmaf(Bx, xx[j], C));
-                        if (kRes) v += rs[j];
+                    for (int j = 0; j < 4; ++j) {
+                        uint64_t v = pfma2(pmul2(inv2, gam[j]), d[j], pfma2(bx2, xx[j], c2));
+                        if (kRes) v = padd2(v, rs[j]);
                         o[j] = v;
-                        pg[j] = fmaf(d[j], (xx[j] - m) * inv, pg[j]);
-                        pb[j] += d[j];
-                        if (kBias) pd[j] += v;
+                        pg[j] = pfma2(d[j], pmul2(psub2(xx[j], m2), inv2), pg[j]);
+                        pb[j] = padd2(pb[j], d[j]);
+                        if (kBias) pd[j] = padd2(pd[j], v);
                     }
-                    reinterpret_cast<uint4*>(dx + (size_t)row * D)[ttid] = f_to_h8(o);
+                    reinterpret_cast<uint4*>(dx + (size_t)row * D)[ttid] = p_to_h8(o);
                 }
             }
             __syncwarp();
@@ -417,10 +423,13 @@ __global__ void __launch_bounds__(544, 1)
         if (own) {
             float* tp = tpart + (size_t)team * 3 * D + 8 * ttid;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                tp[j] = pg[j];
-                tp[D + j] = pb[j];
-                tp[2 * D + j] = pd[j];
+            for (int j = 0; j < 4; ++j) {
+                tp[2 * j] = lo2(pg[j]);
+                tp[2 * j + 1] = hi2(pg[j]);
+                tp[D + 2 * j] = lo2(pb[j]);
+                tp[D + 2 * j + 1] = hi2(pb[j]);
+                tp[2 * D + 2 * j] = lo2(pd[j]);
+                tp[2 * D + 2 * j + 1] = hi2(pd[j]);
             }
         }
     }

@@ -37,15 +37,28 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// try_wait that may suspend the thread (no issue slots used) until the phase
+// completes or about `ns` nanoseconds pass.
+__device__ __forceinline__ bool mbar_try_suspend(uint32_t bar, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
 // Bounded wait.  Returns false (and raises the CTA abort flag) on timeout or
-// when another role already aborted.
+// when another role already aborted.  Waiting threads sleep in try_wait
+// between checks rather than spinning, so they leave the issue slots to the
+// warps doing the work.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
     if (mbar_try(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     while (true) {
-#pragma unroll 1
-        for (int i = 0; i < 32; ++i)
-            if (mbar_try(bar, parity)) return true;
+        if (mbar_try_suspend(bar, parity, 20000u)) return true;
         if (*abort_flag) return false;
         if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
             *abort_flag = 1;
@@ -236,6 +249,51 @@ __device__ __forceinline__ void ffma2v(float& y0, float& y1, float x0, float x1,
         "mov.b64 {%0, %1}, yy;\n\t}"
         : "=f"(y0), "=f"(y1)
         : "f"(x0), "f"(x1), "l"(a2), "f"(b0), "f"(b1));
+}
+
+// Packed FP32 pairs as 64-bit values (low word = first lane).
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+    uint64_t v;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "f"(a), "f"(b));
+    return v;
+}
+__device__ __forceinline__ float lo2(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float hi2(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+__device__ __forceinline__ uint64_t padd2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t psub2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t pmul2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t pfma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+// 8 halves (one 16-byte vector) -> 4 packed FP32 pairs; 4 pairs -> 8 halves
+__device__ __forceinline__ void h8_to_p(const uint4& u, uint64_t* p) {
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 t = __half22float2(h[i]);
+        p[i] = pk2(t.x, t.y);
+    }
+}
+__device__ __forceinline__ uint4 p_to_h8(const uint64_t* p) {
+    uint4 u;
+    __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(lo2(p[i]), hi2(p[i]));
+    return u;
 }
 
 // ------------------------------------------------ CTA pairs (cta_group::2) ----
