@@ -478,9 +478,13 @@ def main():
     per_cat = {CAT_NAMES[c]: {"ms_per_step": cat_ms[c] / args.steps, "launches_per_step": cat_n[c] / args.steps,
                               "share": cat_ms[c] / max(sum(cat_ms), 1e-9)} for c in range(9) if cat_n[c]}
     gemm_tflops = cat_w[0] / (cat_ms[0] * 1e-3) / 1e12 if cat_ms[0] > 0 else 0.0
-    roofline = {"bound": "tensor", "kernel": "gemm_kernel (tcgen05, all GEMMs of the step)",
+    # DRAM bytes (read + write) per GEMM launch of the GPT-2-small step, averaged over the 372 GEMM
+    # launches of a one-pass ncu capture of two steps (dram__bytes_read.sum + dram__bytes_write.sum)
+    traffic = 137.9e6 if args.workload != "1.3b" else None
+    roofline = {"bound": "tensor", "kernel": "gemm_pair_kernel / gemm_kernel (tcgen05, all GEMMs of the step)",
                 "achieved": gemm_tflops, "peak": tc_sustained, "unit": "TFLOP/s",
-                "frac": gemm_tflops / tc_sustained, "traffic": None,
+                "frac": gemm_tflops / tc_sustained, "traffic": traffic,
+                "traffic_unit": "bytes per GEMM launch (ncu capture of the same command)",
                 "peak_source": f"{peak_kind} bf16_tflops_sustained (FP16 and BF16 share the dense tensor rate)",
                 "gemm_flops_per_launch": cat_w[0] / max(cat_n[0], 1),
                 "gemm_ms_per_launch": cat_ms[0] / max(cat_n[0], 1),
