@@ -22,6 +22,10 @@
 namespace rbk {
 namespace {
 
+// One warp per row, NV 16-byte vectors per lane.  For D <= 1024 (NV <= 4) each
+// warp walks its rows with the next row's vectors already in flight while it
+// reduces the current one, and keeps gamma / beta in registers; wider rows hold
+// too many registers for that and load each row when they reach it.
 template <int NV>
 __global__ void __launch_bounds__(256) ln_fwd_kernel(half* __restrict__ y, float* __restrict__ mean,
                                                      float* __restrict__ rstd, const half* __restrict__ x,
@@ -31,19 +35,38 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(half* __restrict__ y, float
     const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
     const int nvec = D >> 3;
     const float invD = 1.0f / (float)D;
-    for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < N; row += gridDim.x * warps) {
-        const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * D);
+    const int stride = gridDim.x * warps;
+    constexpr bool kPrefetch = NV <= 4;
+    uint4 gr[kPrefetch ? NV : 1], br[kPrefetch ? NV : 1], nx[NV];
+    if constexpr (kPrefetch) {
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int c = lane + 32 * i;
+            gr[i] = c < nvec ? __ldg(reinterpret_cast<const uint4*>(g) + c) : make_uint4(0, 0, 0, 0);
+            br[i] = c < nvec ? __ldg(reinterpret_cast<const uint4*>(b) + c) : make_uint4(0, 0, 0, 0);
+        }
+    }
+    int row = blockIdx.x * warps + (threadIdx.x >> 5);
+    auto load_row = [&](int r) {
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int c = lane + 32 * i;
+            nx[i] = (r < N && c < nvec) ? __ldg(reinterpret_cast<const uint4*>(x + (size_t)r * D) + c)
+                                        : make_uint4(0, 0, 0, 0);
+        }
+    };
+    if constexpr (kPrefetch) load_row(row);
+    for (; row < N; row += stride) {
+        if constexpr (!kPrefetch) load_row(row);
         float v[NV][8];
         float s = 0.0f;
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
-            const int c = lane + 32 * i;
-            if (c < nvec) {
-                h8_to_f(__ldg(xr + c), v[i]);
+            h8_to_f(nx[i], v[i]);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) s += v[i][j];
-            }
+            for (int j = 0; j < 8; ++j) s += v[i][j];
         }
+        if constexpr (kPrefetch) load_row(row + stride);   // next row in flight during the reductions
         const float m = warp_sum(s) * invD;
         float q = 0.0f;
 #pragma unroll
@@ -61,8 +84,13 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(half* __restrict__ y, float
             const int c = lane + 32 * i;
             if (c < nvec) {
                 float gf[8], bf[8], o[8];
-                h8_to_f(__ldg(reinterpret_cast<const uint4*>(g) + c), gf);
-                h8_to_f(__ldg(reinterpret_cast<const uint4*>(b) + c), bf);
+                if constexpr (kPrefetch) {
+                    h8_to_f(gr[i], gf);
+                    h8_to_f(br[i], bf);
+                } else {
+                    h8_to_f(__ldg(reinterpret_cast<const uint4*>(g) + c), gf);
+                    h8_to_f(__ldg(reinterpret_cast<const uint4*>(b) + c), bf);
+                }
 #pragma unroll
                 for (int j = 0; j < 8; ++j) o[j] = gf[j] * (v[i][j] - m) * r + bf[j];
                 yr[c] = f_to_h8(o);
@@ -458,6 +486,16 @@ int launch_bwd_ring(int blocks, int threads, int teams, int tpt, int stages, siz
 template <int NV>
 int launch_fwd(int blocks, cudaStream_t st, half* y, float* mean, float* rstd, const half* x, const half* g,
                const half* b, int N, int D, float eps) {
+    // the rows-in-flight variants (NV <= 4) walk rows with one wave of resident CTAs
+    static int resident = 0;
+    if (resident == 0) {
+        int occ = 0, dev = 0, sms = 0;
+        RBK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, ln_fwd_kernel<NV>, 256, 0));
+        RBK_CUDA(cudaGetDevice(&dev));
+        RBK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        resident = (occ > 0 ? occ : 1) * sms;
+    }
+    if (NV <= 4 && blocks > resident) blocks = resident;
     RBK_CUDA(launch_pdl(ln_fwd_kernel<NV>, dim3(blocks), dim3(256), 0, st, y, mean, rstd, x, g, b, N, D, eps));
     return RBK_OK;
 }
