@@ -222,46 +222,104 @@ __global__ void __launch_bounds__(128) flash_fwd_kernel(half* __restrict__ O, fl
 
 // ------------------------------------------------------------------ backward --
 
+// Pre and post passes share one row-block layout: block (TX, TY) with TX a
+// multiple of 32 (one warp never spans two row teams), thread (x, y) owns the
+// 8 columns c8 = blockIdx.x * TX + x and the rows r0 + y, r0 + y + TY, ... of
+// its CTA's row block [r0, r1).  Four rows are loaded before any is used, so a
+// thread keeps 4 x 32 bytes in flight.  Column sums (bias gradients) fold the
+// TY row teams in shared memory and leave one partial row per CTA in
+// part[blockIdx.y][0, D); attn_bias_reduce_kernel adds the partial rows in a
+// fixed order (no atomics: every CTA would otherwise add into the same D
+// addresses).
+constexpr int kRowUnroll = 4;
+
+// Fold acc[8] over the row teams of the CTA into part[c8 * 8, +8).  red holds
+// blockDim.x * blockDim.y * 8 floats.  Every thread of the CTA calls it.
+__device__ __forceinline__ void fold_column_sums(const float (&acc)[8], float* __restrict__ part, int c8, bool col_ok,
+                                                 float* red) {
+    const int t = threadIdx.y * blockDim.x + threadIdx.x;
+    float4* r4 = reinterpret_cast<float4*>(red);
+    r4[2 * t] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    r4[2 * t + 1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    __syncthreads();
+    if (threadIdx.y == 0 && col_ok) {
+        float4 a = r4[2 * t], b = r4[2 * t + 1];
+        for (int y = 1; y < (int)blockDim.y; ++y) {
+            const int u = y * blockDim.x + threadIdx.x;
+            const float4 c = r4[2 * u], d = r4[2 * u + 1];
+            a.x += c.x; a.y += c.y; a.z += c.z; a.w += c.w;
+            b.x += d.x; b.y += d.y; b.z += d.z; b.w += d.w;
+        }
+        float4* out = reinterpret_cast<float4*>(part + (size_t)c8 * 8);
+        out[0] = a;
+        out[1] = b;
+    }
+}
+
 // Dot[bh, s] = sum_d dO[s, d] O[s, d]  and zero the FP32 dQ accumulator; with
-// NL2 also NL2[bh, s] = -LSE[bh, s] * log2 e (the tcgen05 main pass reads it).
-// One thread per 16-byte chunk (coalesced); the HD/8 threads of a head reduce
-// by shuffles (they are adjacent lanes of one warp since HD/8 divides 32).
+// NL2 also NL2[bh, s] = -LSE[bh, s] * log2 e (the tcgen05 main pass reads it);
+// with vpart also the column sums of dO, one partial row per CTA (the v-bias
+// gradient of the tcgen05 path, whose main pass writes no bias terms:
+// sum_keys dV = sum_queries dO because every row of P sums to 1).  The HD/8
+// threads of a head reduce the dot by shuffles (adjacent lanes of one warp:
+// HD/8 divides 32 and TX is a multiple of 32).
 template <int HD>
-__global__ void flash_bwd_pre_kernel(float* __restrict__ Dot, float* __restrict__ dq_acc, float* __restrict__ NL2,
-                                     const float* __restrict__ LSE, const half* __restrict__ O,
-                                     const half* __restrict__ dO, int BS, int S, int H) {
+__global__ void __launch_bounds__(512, 2)
+    flash_bwd_pre_kernel(float* __restrict__ Dot, float* __restrict__ dq_acc, float* __restrict__ NL2,
+                         float* __restrict__ vpart, const float* __restrict__ LSE, const half* __restrict__ O,
+                         const half* __restrict__ dO, int BS, int S, int H, int rows_per_block) {
     grid_dependency_sync();
+    __shared__ __align__(16) float red[512 * 8];
     constexpr int G = HD / 8;            // chunks per (row, head)
     const int D = H * HD;
-    const long total = (long)BS * (D / 8);
-    const long stride = (long)gridDim.x * blockDim.x;
-    // every lane of a warp runs the same number of iterations (shuffles below)
-    const long iters = (total + stride - 1) / stride;
-    for (long it = 0; it < iters; ++it) {
-        const long i = it * stride + blockIdx.x * (long)blockDim.x + threadIdx.x;
-        const bool ok = i < total;
-        float acc = 0.0f;
-        if (ok) {
-            float a[8], bb[8];
-            h8_to_f(__ldg(reinterpret_cast<const uint4*>(O) + i), a);
-            h8_to_f(__ldg(reinterpret_cast<const uint4*>(dO) + i), bb);
+    const int TY = blockDim.y;
+    const int c8 = blockIdx.x * blockDim.x + threadIdx.x;
+    const bool col_ok = c8 * 8 < D;
+    const int h = c8 / G;
+    const int r0 = blockIdx.y * rows_per_block, r1 = min(BS, r0 + rows_per_block);
+    float accv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    // warp-uniform trip count (a warp lies in one row team)
+    for (int rb = r0 + threadIdx.y; rb < r1; rb += kRowUnroll * TY) {
+        uint4 a[kRowUnroll], d[kRowUnroll];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) acc += a[k] * bb[k];
-            float4* z = reinterpret_cast<float4*>(dq_acc) + 2 * i;
-            z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
-            z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int u = 0; u < kRowUnroll; ++u) {
+            const int r = rb + u * TY;
+            if (col_ok && r < r1) {
+                a[u] = __ldg(reinterpret_cast<const uint4*>(O + (size_t)r * D) + c8);
+                d[u] = __ldg(reinterpret_cast<const uint4*>(dO + (size_t)r * D) + c8);
+            } else {
+                a[u] = make_uint4(0u, 0u, 0u, 0u);
+                d[u] = make_uint4(0u, 0u, 0u, 0u);
+            }
         }
 #pragma unroll
-        for (int o = 1; o < G; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if (ok && (threadIdx.x & (G - 1)) == 0) {
-            const long n = i / (D / 8);
-            const int h = (int)((i % (D / 8)) / G);
-            const long b = n / S, s = n % S;
-            const size_t idx = ((size_t)b * H + h) * S + s;
-            Dot[idx] = acc;
-            if (NL2) NL2[idx] = -LSE[idx] * kLog2e;
+        for (int u = 0; u < kRowUnroll; ++u) {
+            const int r = rb + u * TY;
+            float fa[8], fd[8];
+            h8_to_f(a[u], fa);
+            h8_to_f(d[u], fd);
+            float acc = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                acc += fa[k] * fd[k];
+                accv[k] += fd[k];
+            }
+#pragma unroll
+            for (int o = 1; o < G; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            if (col_ok && r < r1) {
+                float4* z = reinterpret_cast<float4*>(dq_acc + (size_t)r * D) + 2 * c8;
+                z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+                z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if ((threadIdx.x & (G - 1)) == 0) {
+                    const int b = r / S, s = r % S;
+                    const size_t idx = ((size_t)b * H + h) * S + s;
+                    Dot[idx] = acc;
+                    if (NL2) NL2[idx] = -LSE[idx] * kLog2e;
+                }
+            }
         }
     }
+    if (vpart) fold_column_sums(accv, vpart + (size_t)blockIdx.y * D, c8, col_ok, red);
 }
 
 template <int HD>
@@ -454,60 +512,77 @@ __global__ void __launch_bounds__(128) flash_bwd_kernel(half* __restrict__ dqkv,
     }
 }
 
-// dqkv[:, q block] = half(dq_acc); dbias[q block] += column sums.  With dO
-// (the tcgen05 path, whose main pass writes no bias terms) also
-// dbias[v block] += column sums of dO: sum_keys dV = sum_queries dO because
-// every row of P sums to 1 (the k block stays untouched: its gradient is 0).
-// Block = 128 column groups of 8 x 4 row groups over rows_per_block rows; the
-// row groups fold in shared memory so each CTA adds one value per column.
-__global__ void __launch_bounds__(512) flash_bwd_post_kernel(half* __restrict__ dqkv, float* __restrict__ dbias,
-                                                             const float* __restrict__ dq_acc,
-                                                             const half* __restrict__ dO, int BS, int D,
-                                                             int rows_per_block) {
+// dqkv[:, q block] = half(dq_acc); with qpart also the column sums of dq_acc,
+// one partial row per CTA (the q-bias gradient).  Row-block layout as in the
+// pre pass.
+__global__ void __launch_bounds__(512, 2)
+    flash_bwd_post_kernel(half* __restrict__ dqkv, float* __restrict__ qpart, const float* __restrict__ dq_acc, int BS,
+                          int D, int rows_per_block) {
     grid_dependency_sync();
-    __shared__ float red[2][3][128][9];                 // [q|v][row groups 1..3][column group][8 (+1 pad)]
-    const int c8 = blockIdx.x * 128 + threadIdx.x;      // 8-column group
+    __shared__ __align__(16) float red[512 * 8];
+    const int TY = blockDim.y;
+    const int c8 = blockIdx.x * blockDim.x + threadIdx.x;
     const bool col_ok = c8 * 8 < D;
     const int r0 = blockIdx.y * rows_per_block, r1 = min(BS, r0 + rows_per_block);
-    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0}, accv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (col_ok) {
-#pragma unroll 4
-        for (int r = r0 + threadIdx.y; r < r1; r += 4) {
-            const float4* src = reinterpret_cast<const float4*>(dq_acc + (size_t)r * D + c8 * 8);
-            const float4 u = src[0], v = src[1];
-            float x[8] = {u.x, u.y, u.z, u.w, v.x, v.y, v.z, v.w};
+        for (int rb = r0 + threadIdx.y; rb < r1; rb += kRowUnroll * TY) {
+            float4 v[kRowUnroll][2];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) acc[k] += x[k];
-            *reinterpret_cast<uint4*>(dqkv + (size_t)r * 3 * D + c8 * 8) = f_to_h8(x);
-            if (dO && dbias) {
-                float y[8];
-                h8_to_f(__ldg(reinterpret_cast<const uint4*>(dO + (size_t)r * D + c8 * 8)), y);
+            for (int u = 0; u < kRowUnroll; ++u) {
+                const int r = rb + u * TY;
+                if (r < r1) {
+                    const float4* src = reinterpret_cast<const float4*>(dq_acc + (size_t)r * D) + 2 * c8;
+                    v[u][0] = __ldg(src);
+                    v[u][1] = __ldg(src + 1);
+                } else {
+                    v[u][0] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    v[u][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
 #pragma unroll
-                for (int k = 0; k < 8; ++k) accv[k] += y[k];
+            for (int u = 0; u < kRowUnroll; ++u) {
+                const int r = rb + u * TY;
+                const float x[8] = {v[u][0].x, v[u][0].y, v[u][0].z, v[u][0].w,
+                                    v[u][1].x, v[u][1].y, v[u][1].z, v[u][1].w};
+#pragma unroll
+                for (int k = 0; k < 8; ++k) acc[k] += x[k];
+                if (r < r1) *reinterpret_cast<uint4*>(dqkv + (size_t)r * 3 * D + c8 * 8) = f_to_h8(x);
             }
         }
     }
-    if (!dbias) return;                                 // uniform across the CTA
-    if (threadIdx.y > 0) {
+    if (qpart) fold_column_sums(acc, qpart + (size_t)blockIdx.y * D, c8, col_ok, red);
+}
+
+// dbias[off_w + c] += sum_b part[w][b][c] for w = 0 (q block, off 0) and, with
+// gridDim.y == 2, w = 1 (v block, off 2D): 32 columns per CTA (one per lane),
+// the 32 warps split the partial rows with four loads in flight, then fold in
+// shared memory; a fixed summation order, so the bias gradients are
+// deterministic.
+__global__ void __launch_bounds__(1024) attn_bias_reduce_kernel(float* __restrict__ dbias,
+                                                                const float* __restrict__ part, int nblk, int D) {
+    grid_dependency_sync();
+    __shared__ float s[32][33];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int c = blockIdx.x * 32 + lane;
+    const int w = blockIdx.y;
+    const float* pw = part + (size_t)w * nblk * D;
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (c < D) {
+        int b = warp;
+        for (; b + 96 < nblk; b += 128) {
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            red[0][threadIdx.y - 1][threadIdx.x][k] = acc[k];
-            red[1][threadIdx.y - 1][threadIdx.x][k] = accv[k];
+            for (int u = 0; u < 4; ++u) acc[u] += __ldg(pw + (size_t)(b + 32 * u) * D + c);
         }
+        for (; b < nblk; b += 32) acc[0] += __ldg(pw + (size_t)b * D + c);
     }
+    s[warp][lane] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
     __syncthreads();
-    if (threadIdx.y == 0 && col_ok) {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            float q = acc[k], w = accv[k];
-#pragma unroll
-            for (int g = 0; g < 3; ++g) {
-                q += red[0][g][threadIdx.x][k];
-                w += red[1][g][threadIdx.x][k];
-            }
-            atomicAdd(dbias + c8 * 8 + k, q);
-            if (dO) atomicAdd(dbias + 2 * D + c8 * 8 + k, w);
-        }
+    if (warp == 0 && c < D) {
+        float t = 0.0f;
+#pragma unroll 8
+        for (int k = 0; k < 32; ++k) t += s[k][lane];
+        dbias[(w ? 2 * D : 0) + c] += t;
     }
 }
 
@@ -531,19 +606,33 @@ int bwd(rbk_ctx* ctx, void* dqkv, float* dbias, const void* qkv, const void* o, 
     const int D = H * HD;
     const size_t BS = (size_t)B * S;
     const size_t dot_bytes = ((sizeof(float) * BS * H) + 255) & ~size_t(255);
+    // Row-block layout of the pre / post passes: TX threads of 8 columns (a
+    // warp multiple, at most 256, further column blocks beyond), TY row teams
+    // (TX * TY <= 512), about two CTAs per SM, each over one contiguous row block.
+    const int c8s = D / 8;
+    const int TX = c8s >= 256 ? 256 : (c8s + 31) / 32 * 32;
+    const int TY = 512 / TX;
+    const int col_blocks = (c8s + TX - 1) / TX;
+    int nrb = (2 * ctx->num_sms + col_blocks - 1) / col_blocks;
+    if (nrb > (int)BS) nrb = (int)BS;
+    const int rows_per_block = (int)((BS + nrb - 1) / nrb);
+    nrb = (int)((BS + rows_per_block - 1) / rows_per_block);
+    const size_t dq_bytes = (sizeof(float) * BS * D + 255) & ~size_t(255);
+    const size_t part_bytes = sizeof(float) * (size_t)nrb * D;   // one [nrb, D] block per bias part
     void* ws;
-    RBK_TRY(ctx_scratch(ctx, 2 * dot_bytes + sizeof(float) * BS * D, &ws));
+    RBK_TRY(ctx_scratch(ctx, 2 * dot_bytes + dq_bytes + 2 * part_bytes, &ws));
     float* Dot = (float*)ws;
     float* NL2 = (float*)((char*)ws + dot_bytes);
     float* dq_acc = (float*)((char*)ws + 2 * dot_bytes);
-    {
-        const long work = (long)BS * (D / 8);
-        long gsz = (work + 255) / 256;
-        if (gsz > ctx->num_sms * 16) gsz = ctx->num_sms * 16;
-        RBK_CUDA(launch_pdl(flash_bwd_pre_kernel<HD>, dim3((int)gsz), dim3(256), 0, st, Dot, dq_acc,
-                            tc ? NL2 : nullptr, lse, (const half*)o, (const half*)dout, (int)BS, S, H));
-        RBK_LAUNCHED("flash_bwd_pre_kernel");
-    }
+    float* qpart = (float*)((char*)ws + 2 * dot_bytes + dq_bytes);
+    float* vpart = (float*)((char*)qpart + part_bytes);
+    // the tcgen05 main pass writes no bias terms: the v block comes from dO's column sums
+    const bool vsum = dbias && tc;
+    const dim3 rgrid(col_blocks, nrb), rblock(TX, TY);
+    RBK_CUDA(launch_pdl(flash_bwd_pre_kernel<HD>, rgrid, rblock, 0, st, Dot, dq_acc, tc ? NL2 : nullptr,
+                        vsum ? vpart : nullptr, lse, (const half*)o, (const half*)dout, (int)BS, S, H,
+                        rows_per_block));
+    RBK_LAUNCHED("flash_bwd_pre_kernel");
     if (tc) {
         RBK_TRY(attn_bwd_tc(ctx, dqkv, dq_acc, qkv, dout, NL2, Dot, B, S, H, HD, scale, st));
     } else {
@@ -558,15 +647,14 @@ int bwd(rbk_ctx* ctx, void* dqkv, float* dbias, const void* qkv, const void* o, 
                                                       (const half*)dout, lse, Dot, S, H, scale, scale * kLog2e);
         RBK_LAUNCHED("flash_bwd_kernel");
     }
-    // 512-thread CTAs, about four per SM: enough loads in flight to stream the FP32 accumulator,
-    // and one bias atomic per column per CTA (rows per CTA: a power of two in [16, 256])
-    const int col_blocks = (D / 8 + 127) / 128;
-    int rows_per_block = 16;
-    while (rows_per_block < 256 && (long)rows_per_block * 4 * ctx->num_sms < (long)BS * col_blocks) rows_per_block *= 2;
-    dim3 pg((D / 8 + 127) / 128, (int)((BS + rows_per_block - 1) / rows_per_block));
-    RBK_CUDA(launch_pdl(flash_bwd_post_kernel, pg, dim3(128, 4), 0, st, (half*)dqkv, dbias, (const float*)dq_acc,
-                        tc ? (const half*)dout : nullptr, (int)BS, D, rows_per_block));
+    RBK_CUDA(launch_pdl(flash_bwd_post_kernel, rgrid, rblock, 0, st, (half*)dqkv, dbias ? qpart : nullptr,
+                        (const float*)dq_acc, (int)BS, D, rows_per_block));
     RBK_LAUNCHED("flash_bwd_post_kernel");
+    if (dbias) {
+        RBK_CUDA(launch_pdl(attn_bias_reduce_kernel, dim3((D + 31) / 32, vsum ? 2 : 1), dim3(1024), 0, st, dbias,
+                            (const float*)qpart, nrb, D));
+        RBK_LAUNCHED("attn_bias_reduce_kernel");
+    }
     return RBK_OK;
 }
 
