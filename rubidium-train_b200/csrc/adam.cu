@@ -63,7 +63,7 @@ __device__ __forceinline__ void chunk_range(const TailParams& P, int c, int64_t&
     }
 }
 
-__global__ void __launch_bounds__(512) adam_tail_kernel(TailParams P) {
+__global__ void __launch_bounds__(512, 2) adam_tail_kernel(TailParams P) {
     __shared__ float s_red[32];
     __shared__ int s_flag;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
@@ -83,9 +83,22 @@ __global__ void __launch_bounds__(512) adam_tail_kernel(TailParams P) {
         int len, seg;
         chunk_range(P, c, s, len, seg);
         const float4* g4 = reinterpret_cast<const float4*>(P.g + s);
+        const int nv = len >> 2;
         float ss = 0.0f;
-        for (int i = tid; i < (len >> 2); i += blockDim.x) {
-            const float4 x = g4[i];
+        // four independent 16-byte loads in flight per thread (one would leave HBM idle)
+        int i = tid;
+        for (; i + 3 * (int)blockDim.x < nv; i += 4 * blockDim.x) {
+            float4 x[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) x[u] = __ldcs(g4 + i + u * blockDim.x);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                bad |= !(isfinite(x[u].x) && isfinite(x[u].y) && isfinite(x[u].z) && isfinite(x[u].w));
+                ss += x[u].x * x[u].x + x[u].y * x[u].y + x[u].z * x[u].z + x[u].w * x[u].w;
+            }
+        }
+        for (; i < nv; i += blockDim.x) {
+            const float4 x = __ldcs(g4 + i);
             bad |= !(isfinite(x.x) && isfinite(x.y) && isfinite(x.z) && isfinite(x.w));
             ss += x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
         }

@@ -132,6 +132,12 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
 
 // Ring kernel: shared memory = nbuf row buffers (rowb bytes each, V rounded up
 // to 8 halves), then per-row reduction scratch red[2][2][2][32] and barriers.
+// ngrp consumer groups take rows in turn: two groups of 8 warps when the ring
+// holds three or more rows (each group's rows overlap the other's), one group
+// of all 16 warps when only two rows fit (a 50K-logit row is 100 KB): with two
+// groups there each group would wait for its own buffer's next load after every
+// row, whereas one group works on a row while the other buffer loads the next.
+template <int NGRP>
 __global__ void __launch_bounds__(kRingConsumers + 32, 1)
     xent_ring_kernel(half* dl, const half* lg, int ld, const int* __restrict__ tgt, int N, int V, float scale,
                      const float* __restrict__ dscale, float* __restrict__ row_loss, int nbuf, int rowb, int* err) {
@@ -147,7 +153,7 @@ __global__ void __launch_bounds__(kRingConsumers + 32, 1)
     if (tid == 0) {
         for (int b = 0; b < nbuf; ++b) {
             mbar_init(full(b), 1);
-            mbar_init(empty(b), NW / 2);                 // the 8 warps of the group that took the row
+            mbar_init(empty(b), NW / NGRP);              // the warps of the group that took the row
         }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -169,16 +175,15 @@ __global__ void __launch_bounds__(kRingConsumers + 32, 1)
         return;
     }
     // ---------------------------------------------------------- consumers ----
-    // two groups of 8 warps take alternate rows: each row's passes and barriers involve half the
-    // CTA, and the two groups' rows overlap
+    // ngrp groups take rows in turn: each row's passes and barriers involve its group only
     const float gs = scale * (dscale ? __ldg(dscale) : 1.0f);
     constexpr float kL2e = 1.4426950408889634f;
-    constexpr int GT = kRingConsumers / 2, GW = GT / 32;   // threads / warps per group
+    constexpr int GT = kRingConsumers / NGRP, GW = GT / 32;   // threads / warps per group
     const int grp = warp / GW, gtid = tid - grp * GT;
     bool ok = true;
     int k = 0, kk = 0;
     for (int row = blockIdx.x; row < N; row += gridDim.x, ++k) {
-        if ((k & 1) != grp) continue;
+        if (k % NGRP != grp) continue;
         const int b = k % nbuf;
         const int t = __ldg(tgt + row);
         const bool tvalid = t >= 0 && t < V;
@@ -301,13 +306,14 @@ extern "C" int rbk_softmax_xent_bwd(rbk_ctx* ctx, void* dlogits, const void* log
         const size_t smem = (size_t)nbuf * rowb + 256 * sizeof(float) + 16 * nbuf + 16;
         static int set_dev = -1;
         if (set_dev != ctx->device) {
-            RBK_CUDA(cudaFuncSetAttribute(xent_ring_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448));
+            RBK_CUDA(cudaFuncSetAttribute(xent_ring_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448));
+            RBK_CUDA(cudaFuncSetAttribute(xent_ring_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448));
             set_dev = ctx->device;
         }
         const int rgrid = N < ctx->num_sms ? N : ctx->num_sms;
-        RBK_CUDA(launch_pdl(xent_ring_kernel, dim3(rgrid), dim3(kRingConsumers + 32), smem, st, (half*)dlogits,
-                            (const half*)logits, ld, targets, N, V, scale, dscale, row_loss, nbuf, rowb,
-                            ctx->tickets + kGemmError));
+        RBK_CUDA(launch_pdl(nbuf >= 3 ? xent_ring_kernel<2> : xent_ring_kernel<1>, dim3(rgrid),
+                            dim3(kRingConsumers + 32), smem, st, (half*)dlogits, (const half*)logits, ld, targets, N,
+                            V, scale, dscale, row_loss, nbuf, rowb, ctx->tickets + kGemmError));
         RBK_LAUNCHED("xent_ring_kernel");
         return RBK_OK;
     }

@@ -106,7 +106,8 @@ def test_ln_bwd_config_2a_full_size(ops, ora):
 
 # ------------------------------------------------------------- cross entropy --
 
-@pytest.mark.parametrize("N,V,ld", [(64, 4096, 4096), (37, 1000, 1008), (16, 50257, 50264), (8, 65536, 65536)])
+@pytest.mark.parametrize("N,V,ld", [(64, 4096, 4096), (37, 1000, 1008), (16, 50257, 50264), (400, 50257, 50264),
+                                    (8, 65536, 65536)])
 def test_softmax_xent(ops, ora, N, V, ld):
     rng = np.random.default_rng(V)
     z = np.zeros((N, ld), np.float16)
