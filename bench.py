@@ -478,9 +478,9 @@ def main():
     per_cat = {CAT_NAMES[c]: {"ms_per_step": cat_ms[c] / args.steps, "launches_per_step": cat_n[c] / args.steps,
                               "share": cat_ms[c] / max(sum(cat_ms), 1e-9)} for c in range(9) if cat_n[c]}
     gemm_tflops = cat_w[0] / (cat_ms[0] * 1e-3) / 1e12 if cat_ms[0] > 0 else 0.0
-    # DRAM bytes (read + write) per GEMM launch of the GPT-2-small step, averaged over the 372 GEMM
-    # launches of a one-pass ncu capture of two steps (dram__bytes_read.sum + dram__bytes_write.sum)
-    traffic = 137.9e6 if args.workload != "1.3b" else None
+    # DRAM bytes (read + write) per GEMM launch of the GPT-2-small step, averaged over the 353 GEMM
+    # launches of a one-pass ncu capture of about two steps (dram__bytes_read.sum + dram__bytes_write.sum)
+    traffic = 143.4e6 if args.workload != "1.3b" else None
     roofline = {"bound": "tensor", "kernel": "gemm_pair_kernel / gemm_kernel (tcgen05, all GEMMs of the step)",
                 "achieved": gemm_tflops, "peak": tc_sustained, "unit": "TFLOP/s",
                 "frac": gemm_tflops / tc_sustained, "traffic": traffic,
