@@ -38,6 +38,7 @@ extern "C" {
 #define RBK_ERR_TIMEOUT (-4)      /* a bounded device-side wait ran out       */
 #define RBK_ERR_NCCL (-5)         /* an NCCL call failed                      */
 #define RBK_ERR_NOMEM (-6)        /* device allocation failed                 */
+#define RBK_ERR_IO (-7)           /* a file could not be opened, read or written */
 
 typedef struct rbk_ctx rbk_ctx;
 
@@ -320,6 +321,24 @@ int rbk_model_sync_fp16(rbk_model* m, void* stream);
 /* init_weights (src/model.cu:146-183): seeded N(0, std) matrices and
  * embeddings, LN gamma 1 / beta 0, biases 0; zero moments and gradients. */
 int rbk_model_init_weights(rbk_model* m, uint64_t seed, float std, void* stream);
+/* save / load (src/model.h:136-137, src/model.cu:585-679).  The file starts
+ * with the reference's RBN2 layout: "RBN2", V T D H L FF (int32), a 256-entry
+ * int32 character map (char_map, or zeros when NULL), then every FP16 weight
+ * in the reference's tensor order (token_emb, pos_emb; per layer ln1_w ln1_b
+ * ln2_w ln2_b wq bq wk bk wv bv wo bo w1 b1 w2 b2; ln_f_w ln_f_b lm_w lm_b),
+ * rows * cols elements each.  An extension block follows that the reference
+ * loader never reads: "RBKX", version 1 (int32), the element count of one
+ * family (int64), the rbk_scaler state, then the FP32 masters, Adam m and
+ * Adam v in the same order.  The reference passes device pointers to
+ * fwrite / fread and keeps no optimizer state; here a resumed run continues
+ * Adam and the loss-scale schedule exactly.  Both calls synchronise `stream`
+ * first.  load requires the file's config to equal the model's
+ * (RBK_ERR_INVALID otherwise); a file without the extension block (the
+ * reference's own) loads with masters = FP32(FP16 weights), zero moments and
+ * a fresh scaler.  Gradients are zeroed.  File errors return RBK_ERR_IO. */
+int rbk_model_save(rbk_model* m, const char* path, const int* char_map, void* stream);
+int rbk_model_load(rbk_model* m, const char* path, int* char_map_out, void* stream);
+
 
 /* forward (src/model.h:130): device tokens/targets [B*S] int32.  Writes the
  * mean loss to *loss_dev (device FP32) when non-NULL; targets may be NULL.

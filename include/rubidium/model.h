@@ -17,6 +17,7 @@
 
 #include <cuda_runtime.h>
 
+#include <cstdio>
 #include <stdexcept>
 #include <string>
 
@@ -56,6 +57,7 @@ struct RubidiumTransformer {
     cudaStream_t stream = nullptr;     // the reference runs on the legacy default stream
     float loss_scale = 65536.0f;       // mirrors the device scaler (src/model.h:120)
     bool overflow = false;             // last step skipped (src/model.h:121)
+    int applied_steps = 0;             // optimizer updates applied (device scaler)
     float pending_clip = 0.0f;
 
     // init (src/model.cu:17-24): allocate, seed (N(0, 0.02) / LN 1 / biases 0), FP16 copy.
@@ -107,6 +109,31 @@ struct RubidiumTransformer {
             throw Error(RBK_ERR_CUDA, "scaler read-back");
         loss_scale = s.scale;
         overflow = s.skipped != 0;
+        applied_steps = s.applied_steps;
+    }
+    // save / load (src/model.h:136-137): the reference's RBN2 file plus masters, Adam moments and
+    // the loss scaler (rbk_model_save / rbk_model_load).  char_map is the file's 256-entry
+    // character-to-token map (the reference stores its tokenizer's char_to_id there).  load on a
+    // model that was never init()ed takes the config from the file and sizes the activations for
+    // max_batch_on_load sequences of cfg.T tokens.
+    int char_map[256] = {};
+    int max_batch_on_load = 1;
+    void save(const char* path) {
+        check(rbk_model_save(handle, path, char_map, stream), "rbk_model_save");
+    }
+    void load(const char* path) {
+        if (!handle) {
+            int hdr[7] = {};                 // magic + V T D H L FF
+            FILE* f = std::fopen(path, "rb");
+            const bool ok = f && std::fread(hdr, sizeof(int), 7, f) == 7;
+            if (f) std::fclose(f);
+            if (!ok) throw Error(RBK_ERR_IO, std::string("cannot read the header of ") + path);
+            ModelConfig c;
+            c.init(hdr[1], hdr[2], hdr[3], hdr[4], hdr[5], hdr[6]);
+            init(c, max_batch_on_load);
+        }
+        check(rbk_model_load(handle, path, char_map, stream), "rbk_model_load");
+        update_loss_scale(false);
     }
     // LoRA hooks (src/lora.h:223-231).
     void init_lora(const LoRAConfig& lc, uint64_t seed = 7) {

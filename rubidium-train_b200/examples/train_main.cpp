@@ -3,6 +3,8 @@
 // librbk through the C++ drop-in header.  Synthetic tokens; prints one line
 // per step.  Build: make -C rubidium-train_b200 examples
 //   usage: train_main [steps] [ga] [V T D H L FF B]
+//   RBK_LOAD=<file> resumes from a checkpoint (weights, masters, Adam moments,
+//   loss scaler; the step count continues); RBK_SAVE=<file> writes one at the end.
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -25,15 +27,22 @@ int main(int argc, char** argv) {
     try {
         rubidium::RubidiumTransformer model;
         model.init(cfg, BS);
+        int start = 0;
+        if (const char* lp = getenv("RBK_LOAD")) {
+            model.load(lp);
+            start = model.applied_steps;
+            printf("loaded %s: %d steps applied, scale %.0f\n", lp, start, model.loss_scale);
+        }
         std::mt19937 gen(42);
         std::uniform_int_distribution<int> tokd(0, cfg.V - 1);
         std::vector<int> h_tok(BS * cfg.T), h_tgt(BS * cfg.T);
         int *d_tok = nullptr, *d_tgt = nullptr;
         cudaMalloc(&d_tok, sizeof(int) * BS * cfg.T);
         cudaMalloc(&d_tgt, sizeof(int) * BS * cfg.T);
-        for (int step = 1; step <= steps; ++step) {
+        for (int step = start + 1; step <= start + steps; ++step) {
             float lr_t = step < warmup ? lr * step / warmup
-                                       : lr * 0.5f * (1.0f + cosf(3.14159265f * (step - warmup) / (steps - warmup + 1)));
+                                       : lr * 0.5f * (1.0f + cosf(3.14159265f * (step - warmup) /
+                                                                    (start + steps - warmup + 1)));
             float loss_acc = 0.0f;
             for (int ga = 0; ga < GA; ++ga) {
                 for (int i = 0; i < BS * cfg.T; ++i) { h_tok[i] = tokd(gen); h_tgt[i] = tokd(gen); }
@@ -47,6 +56,10 @@ int main(int argc, char** argv) {
             model.update_loss_scale(false);
             printf("step %d loss %.4f lr %.2e scale %.0f skipped %d\n", step, loss_acc / GA, lr_t, model.loss_scale,
                    (int)model.overflow);
+        }
+        if (const char* sp = getenv("RBK_SAVE")) {
+            model.save(sp);
+            printf("saved %s\n", sp);
         }
         cudaFree(d_tok);
         cudaFree(d_tgt);

@@ -88,6 +88,8 @@ _SIGS = {
     "rbk_model_scaler": (i32, [vp, C.POINTER(vp)]),
     "rbk_model_sync_fp16": (i32, [vp, vp]),
     "rbk_model_init_weights": (i32, [vp, C.c_uint64, f32, vp]),
+    "rbk_model_save": (i32, [vp, C.c_char_p, vp, vp]),
+    "rbk_model_load": (i32, [vp, C.c_char_p, vp, vp]),
     "rbk_model_forward": (i32, [vp, vp, vp, i32, i32, vp, vp]),
     "rbk_model_backward": (i32, [vp, vp, vp, i32, i32, f32, vp]),
     "rbk_model_optimizer_step": (i32, [vp, i32, f32, f32, f32, f32, f32, f32, vp]),
@@ -112,6 +114,10 @@ def lib():
     """Load librbk.so; raise if it has not been built (no fallback exists)."""
     global _lib
     if _lib is None:
+        # torch first: librbk needs libnccl.so.2, and the NCCL that torch bundles must be the one the
+        # process loads under that name (torch's CUDA library does not start with an older system NCCL
+        # already in place)
+        import torch  # noqa: F401
         if not os.path.exists(LIB_PATH):
             raise FileNotFoundError(
                 f"{LIB_PATH} is missing: build it with `make -C rubidium-train_b200` "

@@ -145,6 +145,20 @@ class RubidiumTransformer:
     def convert_weights_fp32_to_fp16(self):
         call("rbk_model_sync_fp16", self.handle, _s())
 
+    def save(self, path: str, char_map=None):
+        """save (src/model.h:136): RBN2 file plus masters, Adam moments and scaler (rbk_model_save)."""
+        cm = None
+        if char_map is not None:
+            cm = C.cast((C.c_int * 256)(*[int(x) for x in char_map]), C.c_void_p)
+        call("rbk_model_save", self.handle, str(path).encode(), cm, _s())
+
+    def load(self, path: str):
+        """load (src/model.h:137): restores weights and, when the file has them, masters, moments
+        and scaler; returns the file's 256-entry character map."""
+        cm = (C.c_int * 256)()
+        call("rbk_model_load", self.handle, str(path).encode(), C.cast(cm, C.c_void_p), _s())
+        return list(cm)
+
     def init_weights(self, seed=42, std=0.02):
         call("rbk_model_init_weights", self.handle, C.c_uint64(seed), C.c_float(std), _s())
 

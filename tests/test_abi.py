@@ -21,6 +21,7 @@ def test_header_parses():
 
 
 def test_library_exports_every_declared_symbol():
+    import torch  # noqa: F401  (torch's bundled NCCL must be loaded before librbk's libnccl.so.2 need)
     from rbk import LIB_PATH
     if not os.path.exists(LIB_PATH):
         pytest.fail(f"{LIB_PATH} not built (run __graft_entry__.build())")
