@@ -336,6 +336,36 @@ int rbk_model_init_weights(rbk_model* m, uint64_t seed, float std, void* stream)
  * (RBK_ERR_INVALID otherwise); a file without the extension block (the
  * reference's own) loads with masters = FP32(FP16 weights), zero moments and
  * a fresh scaler.  Gradients are zeroed.  File errors return RBK_ERR_IO. */
+/* The trainer loop of src/main.cpp:125-175 on the device.  For each of
+ * `steps` steps (numbered first_step, first_step + 1, ...): `ga` micro-steps,
+ * each gathering B windows of T + 1 tokens from the device-resident token
+ * stream (tokens = stream[o + t], targets = stream[o + t + 1]), forward,
+ * backward with grad_scale (the reference passes 1/(B*ga), src/main.cpp:158);
+ * then the optimizer step with the reference's LR schedule (linear warm-up
+ * over `warmup` steps, then cosine to 0 at max_steps, src/main.cpp:127-131)
+ * and per-tensor clip `clip` (0: none); with LoRA enabled, the LoRA step
+ * (src/fine_tune.cu) instead.  Window starts come from `starts` (host,
+ * [steps * ga * B], each in [0, n_tokens - T - 1], uploaded once) or, when
+ * NULL, from a SplitMix64 hash of (seed, run-wide sample index), so a run
+ * resumed at first_step draws the windows it would have drawn.  The reference
+ * instead cudaMallocs and blocking-copies every micro-batch, reads every loss
+ * back and synchronises the device every step; this call enqueues the whole
+ * run and synchronises once, to read the losses back when `losses` (host,
+ * [steps], the mean over ga of the micro-step losses) is non-NULL.  Its
+ * buffers are stream-ordered allocations (cudaMallocAsync). */
+typedef struct rbk_train_args {
+    const int* tokens;       /* device int32 token stream [n_tokens]          */
+    int64_t n_tokens;
+    const int64_t* starts;   /* host window starts, or NULL (device-drawn)     */
+    uint64_t seed;
+    int steps, ga, B, T;
+    int first_step;          /* >= 1; Adam's t and the LR schedule's step       */
+    int max_steps, warmup;
+    float lr, b1, b2, eps, wd, clip;
+    float grad_scale;
+    float* losses;           /* host [steps] or NULL                           */
+} rbk_train_args;
+int rbk_model_train(rbk_model* m, const rbk_train_args* a, void* stream);
 int rbk_model_save(rbk_model* m, const char* path, const int* char_map, void* stream);
 int rbk_model_load(rbk_model* m, const char* path, int* char_map_out, void* stream);
 

@@ -135,6 +135,21 @@ struct RubidiumTransformer {
         check(rbk_model_load(handle, path, char_map, stream), "rbk_model_load");
         update_loss_scale(false);
     }
+    // The whole trainer loop of src/main.cpp:125-175 on the device (rbk_model_train): the token
+    // stream stays resident (d_stream, n tokens), windows are drawn on the device from `seed`,
+    // nothing synchronises until the per-step losses are read back at the end.
+    void train(const int* d_stream, int64_t n, int steps, int GA, int BS, int max_steps, int warmup, float lr,
+               float b1, float b2, float eps, float wd, float gc, float* losses, uint64_t seed = 1) {
+        rbk_train_args a{};
+        a.tokens = d_stream; a.n_tokens = n; a.starts = nullptr; a.seed = seed;
+        a.steps = steps; a.ga = GA; a.B = BS; a.T = cfg.T; a.first_step = applied_steps + 1;
+        a.max_steps = max_steps; a.warmup = warmup;
+        a.lr = lr; a.b1 = b1; a.b2 = b2; a.eps = eps; a.wd = wd; a.clip = gc;
+        a.grad_scale = 1.0f / (BS * GA);      // the reference's backward factor (src/main.cpp:158)
+        a.losses = losses;
+        check(rbk_model_train(handle, &a, stream), "rbk_model_train");
+        update_loss_scale(false);
+    }
     // LoRA hooks (src/lora.h:223-231).
     void init_lora(const LoRAConfig& lc, uint64_t seed = 7) {
         check(rbk_model_lora_enable(handle, lc.rank, lc.alpha, seed, stream), "rbk_model_lora_enable");

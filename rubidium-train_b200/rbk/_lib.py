@@ -57,6 +57,15 @@ class ModelOpts(C.Structure):
                 ("init_loss_scale", f32), ("growth_interval", i32), ("device", i32)]
 
 
+class TrainArgs(C.Structure):
+    """rbk_train_args (include/rbk.h)."""
+    _fields_ = [("tokens", C.c_void_p), ("n_tokens", C.c_int64), ("starts", C.c_void_p), ("seed", C.c_uint64),
+                ("steps", C.c_int), ("ga", C.c_int), ("B", C.c_int), ("T", C.c_int), ("first_step", C.c_int),
+                ("max_steps", C.c_int), ("warmup", C.c_int), ("lr", C.c_float), ("b1", C.c_float),
+                ("b2", C.c_float), ("eps", C.c_float), ("wd", C.c_float), ("clip", C.c_float),
+                ("grad_scale", C.c_float), ("losses", C.c_void_p)]
+
+
 _SIGS = {
     "rbk_last_error": (C.c_char_p, []),
     "rbk_version": (i32, []),
@@ -90,6 +99,7 @@ _SIGS = {
     "rbk_model_init_weights": (i32, [vp, C.c_uint64, f32, vp]),
     "rbk_model_save": (i32, [vp, C.c_char_p, vp, vp]),
     "rbk_model_load": (i32, [vp, C.c_char_p, vp, vp]),
+    "rbk_model_train": (i32, [vp, C.POINTER(TrainArgs), vp]),
     "rbk_model_forward": (i32, [vp, vp, vp, i32, i32, vp, vp]),
     "rbk_model_backward": (i32, [vp, vp, vp, i32, i32, f32, vp]),
     "rbk_model_optimizer_step": (i32, [vp, i32, f32, f32, f32, f32, f32, f32, vp]),

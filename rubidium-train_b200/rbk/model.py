@@ -19,7 +19,7 @@ from dataclasses import dataclass
 
 import torch
 
-from ._lib import Config, ModelOpts, Scaler, call, lib
+from ._lib import Config, ModelOpts, Scaler, TrainArgs, call, lib
 from .ops import _s
 
 BUF_P16, BUF_P32, BUF_GRAD, BUF_M, BUF_V, BUF_LOSS, BUF_LOGITS = range(7)
@@ -158,6 +158,31 @@ class RubidiumTransformer:
         cm = (C.c_int * 256)()
         call("rbk_model_load", self.handle, str(path).encode(), C.cast(cm, C.c_void_p), _s())
         return list(cm)
+
+    def train(self, tokens, steps, ga, B, T=None, starts=None, seed=0, first_step=1, max_steps=None, warmup=0,
+              lr=3e-4, b1=0.9, b2=0.999, eps=1e-8, wd=0.0, clip=0.0, grad_scale=None):
+        """The reference trainer loop (src/main.cpp:125-175) on the device (rbk_model_train).
+        tokens: device int32 token stream; starts: optional host int64 window starts
+        [steps * ga * B]; grad_scale defaults to 1 / ga (the mean of the micro-batch mean
+        losses; the reference passes 1 / (B * ga)).  Returns the per-step mean losses."""
+        import numpy as np
+        T = T or self.max_seq
+        a = TrainArgs()
+        a.tokens, a.n_tokens = tokens.data_ptr(), tokens.numel()
+        st = None
+        if starts is not None:
+            st = np.ascontiguousarray(np.asarray(starts, dtype=np.int64))
+            a.starts = st.ctypes.data
+        a.seed = seed
+        a.steps, a.ga, a.B, a.T, a.first_step = steps, ga, B, T, first_step
+        a.max_steps = max_steps if max_steps is not None else first_step + steps - 1
+        a.warmup = warmup
+        a.lr, a.b1, a.b2, a.eps, a.wd, a.clip = lr, b1, b2, eps, wd, clip
+        a.grad_scale = 1.0 / ga if grad_scale is None else grad_scale
+        out = (C.c_float * steps)()
+        a.losses = C.cast(out, C.c_void_p)
+        call("rbk_model_train", self.handle, C.byref(a), _s())
+        return list(out)
 
     def init_weights(self, seed=42, std=0.02):
         call("rbk_model_init_weights", self.handle, C.c_uint64(seed), C.c_float(std), _s())

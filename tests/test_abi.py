@@ -51,3 +51,23 @@ def test_gpu_free_ctx_create_fails_cleanly():
     st = lib().rbk_ctx_create(ctypes.byref(h), 0)
     assert st < 0
     assert len(lib().rbk_last_error()) > 0
+
+
+def test_train_args_layout_matches_header(tmp_path):
+    """The ctypes mirror of rbk_train_args has the C compiler's field offsets."""
+    import shutil
+    import subprocess
+    if shutil.which("gcc") is None:
+        pytest.skip("no gcc")
+    from rbk._lib import TrainArgs
+    names = [f for f, _ in TrainArgs._fields_]
+    src = tmp_path / "off.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "rbk.h"\nint main(void) {\n' +
+                   "".join(f'printf("%zu\\n", offsetof(rbk_train_args, {n}));\n' for n in names) +
+                   'printf("%zu\\n", sizeof(rbk_train_args));\nreturn 0;\n}\n')
+    exe = tmp_path / "off"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), "-I/usr/local/cuda/include", str(src), "-o",
+                    str(exe)], check=True)
+    got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    want = [getattr(TrainArgs, n).offset for n in names] + [ctypes.sizeof(TrainArgs)]
+    assert got == want
