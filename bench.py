@@ -43,6 +43,13 @@ WORKLOADS = {
                  name="1.3B decoder (L24 d2048 H16 FF8192 V50257), seq 2048, micro-batch 8/GPU"),
     "tiny": dict(cfg=dict(V=4096, T=128, D=256, H=4, L=4, FF=1024), batch=8, seq=128,
                  name="tiny decoder (L4 d256 H4 FF1024 V4096), seq 128, batch 8"),
+    # LoRA fine-tune of the GPT-2-small base: frozen FP16 base, rank-16 adapters on Q and V
+    # (A ~ N(0, 0.02), B = 0, alpha 32), gradients to A and B only; every 50th step +inf in 1 of
+    # every 1e5 dlogits elements exercises the fused inf check and skipped step
+    "lora": dict(cfg=dict(V=50257, T=1024, D=768, H=12, L=12, FF=3072), batch=32, seq=512,
+                 lora=dict(rank=16, alpha=32.0), inject_every=50, inject_stride=100000,
+                 name="LoRA r16 (Q, V; alpha 32) on the GPT-2-small base, seq 512, batch 32, "
+                      "+inf in 1e-5 of dlogits every 50th step"),
 }
 
 CAT_NAMES = ["gemm", "attn_fwd", "attn_bwd", "ln_fwd", "ln_bwd", "softmax_xent", "adam_tail", "embedding", "other"]
@@ -63,18 +70,21 @@ def mm_params(cfg):
     return L * (4 * D * D + 2 * D * F) + V * D
 
 
-def gemm_flops_per_step(cfg, ntok, ckpt=True):
-    """Algorithmic tensor-core FLOPs of the GEMMs in one step: forward 2 P, backward
-    4 P per token (P = matmul parameters), plus the checkpoint recompute of the
-    QKV and W1 projections."""
+def gemm_flops_per_step(cfg, ntok, ckpt=True, lora=False):
+    """Algorithmic tensor-core FLOPs of the base GEMMs in one step: forward 2 P, backward
+    4 P per token (2 P under LoRA: no weight gradients; P = matmul parameters), plus the
+    checkpoint recompute of the QKV and W1 projections."""
     D, F, L = cfg["D"], cfg["FF"], cfg["L"]
     P = mm_params(cfg)
     rec = L * (3 * D * D + D * F) if ckpt else 0
-    return 2.0 * ntok * (3 * P + rec)
+    return 2.0 * ntok * ((2 if lora else 3) * P + rec)
 
 
-def train_flops_per_token(cfg, seq):
-    """6 P + 6 L T D (causal attention), recompute excluded (the published convention)."""
+def train_flops_per_token(cfg, seq, lora_rank=0):
+    """6 P + 6 L T D (causal attention), recompute excluded (the published convention).  A
+    LoRA step has no base weight gradients: 4 P + 6 L T D + 16 L D r (Q and V adapters)."""
+    if lora_rank:
+        return 4.0 * mm_params(cfg) + 6.0 * cfg["L"] * seq * cfg["D"] + 16.0 * cfg["L"] * cfg["D"] * lora_rank
     return 6.0 * mm_params(cfg) + 6.0 * cfg["L"] * seq * cfg["D"]
 
 
@@ -124,11 +134,24 @@ def cpu_sample(workload, seq=128):
     at micro-batch 1 over `seq` tokens; returns (tokens/s, seconds, threads)."""
     import numpy as np
     import oracle
-    cfg = dict(WORKLOADS[workload]["cfg"])
+    wl = WORKLOADS[workload]
+    cfg = dict(wl["cfg"])
     rng = np.random.default_rng(0)
     params = oracle.init_params(cfg, seed=1)
     tok = rng.integers(0, cfg["V"], seq).astype(np.int32)
     tgt = rng.integers(0, cfg["V"], seq).astype(np.int32)
+    if wl.get("lora"):                                 # adapter gradients only, AdamW on the adapters
+        r, alpha, D, L = wl["lora"]["rank"], wl["lora"]["alpha"], cfg["D"], cfg["L"]
+        A = (0.02 * rng.standard_normal((2, L * D * r))).astype(np.float32)
+        Bz = np.zeros((2, L * r * D), np.float32)
+        t0 = time.perf_counter()
+        _, dAq, dBq, dAv, dBv = oracle.model_lora_grad(cfg, params, A[0], Bz[0], A[1], Bz[1], r, alpha, tok, tgt,
+                                                       1, seq)
+        ad = np.concatenate([A.ravel(), Bz.ravel()])
+        gd = np.concatenate([dAq, dAv, dBq, dBv]).astype(np.float32)
+        oracle.adamw(ad, gd, np.zeros_like(ad), np.zeros_like(ad), 3e-4, 0.9, 0.999, 1e-8, 0.0, 1)
+        dt = time.perf_counter() - t0
+        return seq / dt, dt, oracle.num_threads()
     m = np.zeros_like(params); v = np.zeros_like(params)
     t0 = time.perf_counter()
     _, g, _ = oracle.model_loss_grad(cfg, params, tok, tgt, 1, seq)
@@ -376,6 +399,9 @@ def main():
     ckpt = not args.no_ckpt
     model = RubidiumTransformer(ModelConfig(**cfg, use_activation_checkpointing=ckpt), max_batch=B, max_seq=S)
     model.init_weights(seed=42, std=0.02)
+    lora = wl.get("lora")
+    if lora:
+        model.init_lora(rank=lora["rank"], alpha=lora["alpha"])
     if world > 1:
         uid = [dp_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
@@ -386,10 +412,24 @@ def main():
     targets = torch.randint(0, cfg["V"], (B, S), device="cuda", dtype=torch.int32, generator=g)
     stream = torch.cuda.current_stream()
 
+    nstep = [0]   # steps run so far (warm-up included): the LoRA workload injects on every 50th
+
+    def backward(tok, tgt):
+        nstep[0] += 1
+        if lora and nstep[0] % wl["inject_every"] == 0:
+            model.inject_inf(offset=nstep[0] % wl["inject_stride"], stride=wl["inject_stride"])
+        model.backward(tok, tgt, B, S, 1.0)
+
+    def update():
+        if lora:
+            model.lora_optimizer_step(0, 3e-4, 0.9, 0.999, 1e-8, 0.0)
+        else:
+            model.optimizer_step(0, 3e-4, 0.9, 0.999, 1e-8, 0.0)
+
     def step(t):
         model.forward(tokens, targets, B, S)
-        model.backward(tokens, targets, B, S, 1.0)
-        model.optimizer_step(t, 3e-4, 0.9, 0.999, 1e-8, 0.0)
+        backward(tokens, targets)
+        update()
 
     for i in range(args.warmup):
         step(0)
@@ -416,9 +456,9 @@ def main():
     for i in range(args.steps):
         model.forward(tokens, targets, B, S)
         bw_s[i].record(stream)
-        model.backward(tokens, targets, B, S, 1.0)
+        backward(tokens, targets)
         bw_e[i].record(stream)
-        model.optimizer_step(0, 3e-4, 0.9, 0.999, 1e-8, 0.0)
+        update()
     t_end.record(stream)
     torch.cuda.synchronize()
     launches = lib().rbk_launch_count() - launches0
@@ -462,8 +502,8 @@ def main():
         d_tok.copy_(h_tok, non_blocking=True)
         d_tgt.copy_(h_tgt, non_blocking=True)
         loss = model.forward(d_tok, d_tgt, B, S)
-        model.backward(d_tok, d_tgt, B, S, 1.0)
-        model.optimizer_step(0, 3e-4, 0.9, 0.999, 1e-8, 0.0)
+        backward(d_tok, d_tgt)
+        update()
         h_loss.copy_(loss.view(1), non_blocking=True)
         torch.cuda.current_stream().synchronize()
         _ = float(h_loss[0])
@@ -501,7 +541,8 @@ def main():
     if rank == 0 and not args.no_cpu:
         tps, dt, cores = cpu_sample(args.workload, 128)
         cpu = {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port",
-               "sample": f"oracle fwd+bwd+AdamW of the same model over 1 x 128 tokens ({dt:.1f} s)"}
+               "sample": f"oracle fwd+bwd+AdamW{' (LoRA adapters)' if wl.get('lora') else ''} of the same model "
+                         f"over 1 x 128 tokens ({dt:.1f} s)"}
     if world > 1:
         dist.barrier()
     if rank == 0:
@@ -514,8 +555,9 @@ def main():
                        "loss_scale_init": 65536, "l2": "no flush: weights/activations/logits exceed 126 MB L2"},
             "tokens_per_s_per_gpu": value / world,
             "backward_ms_per_step": bwd_ms,
-            "train_tflops_per_gpu": train_flops_per_token(cfg, S) * ntok / (ms_step / 1000.0) / 1e12,
-            "gemm_flops_per_step": gemm_flops_per_step(cfg, ntok, ckpt),
+            "train_tflops_per_gpu": train_flops_per_token(cfg, S, lora["rank"] if lora else 0) * ntok /
+                                    (ms_step / 1000.0) / 1e12,
+            "gemm_flops_per_step": gemm_flops_per_step(cfg, ntok, ckpt, bool(lora)),
             "roofline": roofline,
             "kernels": per_cat,
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 2 * ntok * 4, "d2h_bytes_per_step": 4},
@@ -523,7 +565,12 @@ def main():
             "clocks": clk,
             "cpu_baseline": cpu,
             "loss_scale": model.loss_scale,
+            "skipped_steps": model.scaler().overflow_steps,
         }
+        if lora:
+            out["config"].update(lora_rank=lora["rank"], lora_alpha=lora["alpha"], lora_targets="q,v",
+                                 inf_injection=f"1 in {wl['inject_stride']} dlogits elements every "
+                                               f"{wl['inject_every']}th step")
         out.update(extra)
         print(json.dumps(out), flush=True)
     model.close()
