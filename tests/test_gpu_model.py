@@ -1,6 +1,6 @@
 """Attention and whole-model parity on the B200 against the CPU oracle.
 
-Acceptance (BASELINE): loss within 1e-3 relative; per-tensor gradient relative
+Acceptance: loss within 1e-3 relative; per-tensor gradient relative
 L2 error <= 2e-2 (FP16 path vs FP32 oracle, absolute floor for tensors whose
 exact gradient is ~0, e.g. the key bias); identical overflow / skip decisions.
 """
