@@ -134,6 +134,7 @@ __global__ void __launch_bounds__(512, 2) adam_tail_kernel(TailParams P) {
     // ---------------- phase 2: update ---------------------------------------
     int t = P.t > 0 ? P.t : P.sc->applied_steps + 1;
     const float c1 = 1.0f - powf(P.b1, (float)t), c2 = 1.0f - powf(P.b2, (float)t);
+    const float ic1 = 1.0f / c1, ic2 = 1.0f / c2;      // bias corrections as factors
     for (int c = blockIdx.x; c < P.nchunks; c += gridDim.x) {
         int64_t s;
         int len, seg;
@@ -161,8 +162,8 @@ __global__ void __launch_bounds__(512, 2) adam_tail_kernel(TailParams P) {
                     const float gi = gv[j] * f + P.wd * pv[j];
                     mv[j] = P.b1 * mv[j] + (1.0f - P.b1) * gi;
                     vw[j] = P.b2 * vw[j] + (1.0f - P.b2) * gi * gi;
-                    const float mh = mv[j] / c1, vh = vw[j] / c2;
-                    pv[j] -= P.lr * mh / (sqrtf(vh) + P.eps);
+                    const float mh = mv[j] * ic1, vh = vw[j] * ic2;
+                    pv[j] -= __fdividef(P.lr * mh, sqrtf(vh) + P.eps);
                 }
                 p4[i] = make_float4(pv[0], pv[1], pv[2], pv[3]);
                 m4[i] = make_float4(mv[0], mv[1], mv[2], mv[3]);
