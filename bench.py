@@ -520,7 +520,7 @@ def main():
     gemm_tflops = cat_w[0] / (cat_ms[0] * 1e-3) / 1e12 if cat_ms[0] > 0 else 0.0
     # DRAM bytes (read + write) per GEMM launch of the GPT-2-small step, averaged over the 353 GEMM
     # launches of a one-pass ncu capture of about two steps (dram__bytes_read.sum + dram__bytes_write.sum)
-    traffic = 143.4e6 if args.workload != "1.3b" else None
+    traffic = 141.8e6 if args.workload == "gpt2-small" else None
     roofline = {"bound": "tensor", "kernel": "gemm_pair_kernel / gemm_kernel (tcgen05, all GEMMs of the step)",
                 "achieved": gemm_tflops, "peak": tc_sustained, "unit": "TFLOP/s",
                 "frac": gemm_tflops / tc_sustained, "traffic": traffic,
