@@ -102,6 +102,7 @@ enum TicketSlot {
     kTicketSum = 0,
     kTailOverflow = 8, kTailBarrier = 9, kTailTicket = 10, kTailTimeout = 11,
     kGemmError = 16,
+    kAttnFwdTile = 20, kAttnFwdDone = 21,
 };
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
