@@ -335,7 +335,9 @@ int rbk_model_init_weights(rbk_model* m, uint64_t seed, float std, void* stream)
  * first.  load requires the file's config to equal the model's
  * (RBK_ERR_INVALID otherwise); a file without the extension block (the
  * reference's own) loads with masters = FP32(FP16 weights), zero moments and
- * a fresh scaler.  Gradients are zeroed.  File errors return RBK_ERR_IO. */
+ * a fresh scaler.  Gradients are zeroed.  File errors return RBK_ERR_IO.
+ * LoRA adapters and their moments are not part of the file (the base model
+ * and its optimizer state are). */
 /* The trainer loop of src/main.cpp:125-175 on the device.  For each of
  * `steps` steps (numbered first_step, first_step + 1, ...): `ga` micro-steps,
  * each gathering B windows of T + 1 tokens from the device-resident token
