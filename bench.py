@@ -129,13 +129,27 @@ class Clocks:
 
 # ---------------------------------------------------------------- CPU legs ----
 
-def cpu_sample(workload, seq=128):
+# CPU sample per workload: one micro-batch-1 sequence of this many tokens (the workload's
+# own sequence length where one step stays within about 10-30 s of host time).
+CPU_SEQ = {"gpt2-small": 1024, "lora": 512, "1.3b": 256, "tiny": 128}
+
+
+def cpu_threads():
+    """Every core this process may run on (torchrun exports OMP_NUM_THREADS=1 to each rank,
+    so the oracle's thread count is set explicitly)."""
+    import oracle
+    return oracle.set_threads()
+
+
+def cpu_sample(workload, seq=None):
     """The CPU restatement (oracle) of one fwd+bwd+AdamW step of the same model
     at micro-batch 1 over `seq` tokens; returns (tokens/s, seconds, threads)."""
     import numpy as np
     import oracle
     wl = WORKLOADS[workload]
     cfg = dict(wl["cfg"])
+    seq = seq or CPU_SEQ[workload]
+    threads = cpu_threads()
     rng = np.random.default_rng(0)
     params = oracle.init_params(cfg, seed=1)
     tok = rng.integers(0, cfg["V"], seq).astype(np.int32)
@@ -151,37 +165,123 @@ def cpu_sample(workload, seq=128):
         gd = np.concatenate([dAq, dAv, dBq, dBv]).astype(np.float32)
         oracle.adamw(ad, gd, np.zeros_like(ad), np.zeros_like(ad), 3e-4, 0.9, 0.999, 1e-8, 0.0, 1)
         dt = time.perf_counter() - t0
-        return seq / dt, dt, oracle.num_threads()
+        return seq / dt, dt, threads
     m = np.zeros_like(params); v = np.zeros_like(params)
     t0 = time.perf_counter()
     _, g, _ = oracle.model_loss_grad(cfg, params, tok, tgt, 1, seq)
     oracle.adamw(params, g, m, v, 3e-4, 0.9, 0.999, 1e-8, 0.0, 1)
     dt = time.perf_counter() - t0
-    return seq / dt, dt, oracle.num_threads()
+    return seq / dt, dt, threads
+
+
+def reference_ops():
+    """The reference's own CPU code (oracle/_ref/libref.so, compiled from its sources; it
+    builds only without OpenMP, so one core): cpuops::layer_norm_backward, softmax_backward,
+    cross_entropy_backward and adamw_step at the kernel-microbench shapes, and
+    CPUTransformer::forward on one sequence of the tiny decoder with V = D (its LM head is only
+    shape-correct then).  Inputs are staged first; only the reference call is timed."""
+    import ctypes as C
+
+    import numpy as np
+    import oracle
+    ref = oracle.ref_lib()
+    if ref is None:
+        return {"unavailable": "oracle/_ref/libref.so was not built (the reference tree was absent at build time)"}
+    F = lambda a: a.ctypes.data_as(C.POINTER(C.c_float))   # noqa: E731
+    I = lambda a: a.ctypes.data_as(C.POINTER(C.c_int))     # noqa: E731
+    rng = np.random.default_rng(0)
+    out = {"kind": "reference", "cores": 1,
+           "build": "g++ -O2 of src/cpu_mat.h + src/cpu_model.cpp without -fopenmp (oracle/Makefile target ref)"}
+    # LayerNorm backward [16384, 1024] (src/cpu_mat.h:126-153)
+    N, D = 16384, 1024
+    x = rng.standard_normal((N, D), dtype=np.float32)
+    dy = rng.standard_normal((N, D), dtype=np.float32)
+    g = (1 + 0.02 * rng.standard_normal(D)).astype(np.float32)
+    mean = x.mean(1).astype(np.float32)
+    rstd = (1 / np.sqrt(x.var(1) + 1e-5)).astype(np.float32)
+    s = ref.ref_time_layer_norm_backward(F(dy), F(x), F(g), F(mean), F(rstd), N, D)
+    by = N * D * 6 + N * 8 + D * 10       # the same algorithmic bytes as the GPU kernel (FP16 sizes)
+    out["layer_norm_backward_16384x1024"] = {"s": s, "GB/s": by / s / 1e9, "algorithmic_bytes": by}
+    del x, dy
+    # softmax backward over 8 * 16 * 1024 rows of 1024 (src/cpu_mat.h:190-200; it has no causal form)
+    rows, T = 8 * 16 * 1024, 1024
+    y = rng.random((rows, T), dtype=np.float32)
+    dyy = rng.standard_normal((rows, T), dtype=np.float32)
+    s = ref.ref_time_softmax_backward(F(dyy), F(y), rows, T)
+    out["softmax_backward_B8H16T1024"] = {"s": s, "elements": rows * T, "Gelem/s": rows * T / s / 1e9}
+    del y, dyy
+    # cross-entropy backward [8192, 32000] (src/cpu_mat.h:220-236)
+    N, V = 8192, 32000
+    z = (2.0 * rng.standard_normal((N, V), dtype=np.float32))
+    tg = rng.integers(0, V, N).astype(np.int32)
+    s = ref.ref_time_cross_entropy_backward(F(z), I(tg), N, V)
+    by = N * V * 4 + N * 4
+    out["cross_entropy_backward_8192x32000"] = {"s": s, "GB/s": by / s / 1e9, "algorithmic_bytes": by}
+    del z
+    # AdamW over 16M parameters (src/cpu_mat.h:280-292)
+    n = 1 << 24
+    p = rng.standard_normal(n, dtype=np.float32)
+    gg = rng.standard_normal(n, dtype=np.float32)
+    s = ref.ref_time_adamw_step(F(p), F(gg), n, C.c_float(3e-4), C.c_float(0.9), C.c_float(0.999),
+                                C.c_float(1e-8), C.c_float(0.01))
+    out["adamw_step_16M"] = {"s": s, "params_per_s": n / s, "GB/s": 34.0 * n / s / 1e9}
+    del p, gg
+    # CPUTransformer::forward (src/cpu_model.cpp:115-222): the tiny decoder (L4 D256 H4 FF1024) with
+    # V = D = 256, one sequence of 128 tokens, weights N(0, 0.02)
+    cfg = dict(V=256, T=128, D=256, H=4, L=4, FF=1024)
+    Vv, Tt, Dd, L, FF = cfg["V"], cfg["T"], cfg["D"], cfg["L"], cfg["FF"]
+    w = lambda *sh: (0.02 * rng.standard_normal(sh)).astype(np.float32)   # noqa: E731
+    blocks = []
+    for _ in range(L):
+        blocks += [np.ones(Dd), np.zeros(Dd), w(Dd, Dd), np.zeros(Dd), w(Dd, Dd), np.zeros(Dd), w(Dd, Dd),
+                   np.zeros(Dd), w(Dd, Dd), np.zeros(Dd), np.ones(Dd), np.zeros(Dd), w(Dd, FF), np.zeros(FF),
+                   w(FF, Dd), np.zeros(Dd)]
+    layers = np.concatenate([np.asarray(b, np.float32).ravel() for b in blocks])
+    tok = rng.integers(0, Vv, Tt).astype(np.int32)
+    tgt = rng.integers(0, Vv, Tt).astype(np.int32)
+    loss = C.c_float()
+    ones, zeros = np.ones(Dd, np.float32), np.zeros(Dd, np.float32)
+    te, pe, lw, lb = w(Vv, Dd), w(Tt, Dd), w(Dd, Vv), np.zeros(Vv, np.float32)
+    s = ref.ref_time_cpu_forward(Vv, Tt, Dd, cfg["H"], L, FF, F(te), F(pe), F(layers), F(ones), F(zeros), F(lw),
+                                 F(lb), I(tok), I(tgt), Tt, C.byref(loss))
+    out["cpu_transformer_forward_tiny_v256"] = {"s": s, "tokens_per_s": Tt / s, "loss": loss.value,
+                                                "config": "L4 D256 H4 FF1024 V256 T128, 1 sequence"}
+    return out
 
 
 def run_reference(args):
-    """--impl reference: the CPU restatement of the step on the host cores."""
+    """--impl reference: the CPU restatement of the step (the reference's own engine cannot run a
+    backward) on every host core, plus the reference's own CPU ops timed serially."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     wl = WORKLOADS[args.workload]
-    seq = 128
-    vals = []
-    for i in range(args.warmup + args.steps):
+    seq = CPU_SEQ[args.workload]
+    vals, cores = [], 1
+    budget_s, used = 90.0, 0.0
+    for _ in range(min(args.warmup, 1)):
+        cpu_sample(args.workload, seq)
+    for i in range(args.steps):
         tps, dt, cores = cpu_sample(args.workload, seq)
-        if i >= args.warmup:
-            vals.append(tps)
+        vals.append(tps)
+        used += dt
+        if used > budget_s:
+            break
     v = statistics.median(vals)
+    sample = (f"one fwd+bwd+AdamW{' (LoRA adapters)' if wl.get('lora') else ''} step of the same model over "
+              f"1 x {seq} tokens per timed step (oracle, {cores} threads)")
     out = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * seq / v, "higher_is_better": True,
+        "steps": len(vals), "steps_requested": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * seq / v, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-        "config": {"workload": wl["name"] + f"; CPU sample: micro-batch 1 x {seq} tokens per step"},
-        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"one fwd+bwd+AdamW step over 1 x {seq} tokens of the same model (oracle)"},
+        "config": {"workload": wl["name"] + f"; CPU sample: micro-batch 1 x {seq} tokens per step",
+                   "value_scope": "whole host (all cores of the node)"},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if args.workload != "tiny" and not args.no_ref_ops:
+        out["cpu_baseline"]["reference_ops"] = reference_ops()
     print(json.dumps(out), flush=True)
     return 0
 
@@ -265,45 +365,82 @@ def microbench(ops, torch, hbm_peak, reps=20):
     return res
 
 
+def r8(x):
+    return (x + 7) // 8 * 8
+
+
+def gemm_shapes(N=16384, D=768, F=3072, V=50257):
+    """The GEMMs of one GPT-2-small layer step and the LM head, as the model issues them:
+    name -> (M, N, K, a_major, b_major, epilogue, extra) with extra in {"", "bias", "res", "dbias"}."""
+    return {
+        "gemm_fwd_qkv": (N, 3 * D, D, 0, 0, 0, "bias"),
+        "gemm_fwd_wo": (N, D, D, 0, 0, 0, "res"),
+        "gemm_fwd_w1": (N, F, D, 0, 0, 1, "bias"),
+        "gemm_fwd_w2": (N, D, F, 0, 0, 0, "res"),
+        "gemm_lm_fwd": (N, V, D, 0, 0, 0, "bias"),
+        "gemm_dgrad_lm": (N, D, V, 0, 1, 0, ""),
+        "gemm_wgrad_lm": (V, D, N, 1, 1, 3, "dbias"),
+        "gemm_wgrad_w2": (D, F, N, 1, 1, 3, ""),
+        "gemm_dgrad_w2": (N, F, D, 0, 1, 2, ""),
+        "gemm_wgrad_w1": (F, D, N, 1, 1, 3, "dbias"),
+        "gemm_dgrad_w1": (N, D, F, 0, 1, 0, ""),
+        "gemm_wgrad_wo": (D, D, N, 1, 1, 3, ""),
+        "gemm_dgrad_wo": (N, D, D, 0, 1, 0, ""),
+        "gemm_wgrad_qkv": (3 * D, D, N, 1, 1, 3, ""),
+        "gemm_dgrad_qkv": (N, D, 3 * D, 0, 1, 0, ""),
+    }
+
+
 def kernel_loop(name, reps, torch, ops):
     """One kernel at a representative GPT-2-small shape, `reps` launches (for ncu
-    captures and tuning).  Prints per-launch time and the achieved rate."""
+    captures and tuning).  Prints per-launch time and the achieved rate.  GEMM inputs
+    rotate over enough sets (> 2x the 126 MB L2) that every launch reads them from DRAM."""
     g = torch.Generator(device="cuda").manual_seed(0)
     hbm, tc, tcs, _ = peaks()
     N, D, F, V = 16384, 768, 3072, 50257
     if name.startswith("gemm"):
-        shapes = {  # (M, N, K, a_major, b_major, epilogue)
-            "gemm_fwd_w1": (N, F, D, 0, 0, ops.EPI_BIAS_GELU),
-            "gemm_fwd_qkv": (N, 3 * D, D, 0, 0, ops.EPI_STORE_F16),
-            "gemm_dgrad_w2": (N, F, D, 0, 1, ops.EPI_GELU_BWD),
-            "gemm_dgrad_w1": (N, D, F, 0, 1, ops.EPI_STORE_F16),
-            "gemm_wgrad_w1": (F, D, N, 1, 1, ops.EPI_ACC_F32),
-            "gemm_lm_fwd": (N, V, D, 0, 0, ops.EPI_STORE_F16),
-        }
-        M, Nn, K, am, bm, epi = shapes[name]
-        A = torch.randn(K if am else M, M if am else K, device="cuda", generator=g).half()
-        B = torch.randn(K if bm else Nn, (Nn + 7) // 8 * 8 if bm else K, device="cuda", generator=g).half()
-        ldc = (Nn + 7) // 8 * 8
-        f32 = epi == ops.EPI_ACC_F32
-        Cm = torch.zeros(M, ldc, device="cuda", dtype=torch.float32 if f32 else torch.float16)
-        bias = torch.randn(ldc, device="cuda", generator=g).half()
-        aux = torch.randn(M, ldc, device="cuda", generator=g).half() if epi in (ops.EPI_GELU_BWD,) else None
-        aux_out = torch.empty(M, ldc, device="cuda", dtype=torch.float16) if epi == ops.EPI_BIAS_GELU else None
-        dbias = torch.zeros(M, device="cuda") if f32 else None
+        shapes = gemm_shapes(N, D, F, V)
+        if name not in shapes:
+            raise SystemExit(f"unknown GEMM {name}: one of {sorted(shapes)}")
+        M, Nn, K, am, bm, epi, extra = shapes[name]
+        lda, ldb, ldc = r8(M if am else K), r8(Nn if bm else K), r8(Nn)
+        f32 = epi in (ops.EPI_ACC_F32, ops.EPI_STORE_F32)
+        set_bytes = 2 * ((K if am else M) * lda + (K if bm else Nn) * ldb) + M * ldc * (4 if f32 else 2) * \
+            (2 if epi in (ops.EPI_GELU_BWD, ops.EPI_BIAS_GELU) or extra == "res" else 1)
+        nsets = max(1, min(16, -(-300_000_000 // set_bytes)))
+        sets = []
+        for _ in range(nsets):
+            A = (0.5 * torch.randn(K if am else M, lda, device="cuda", generator=g)).half()
+            B = (0.5 * torch.randn(K if bm else Nn, ldb, device="cuda", generator=g)).half()
+            Cm = torch.zeros(M, ldc, device="cuda", dtype=torch.float32 if f32 else torch.float16)
+            aux = torch.randn(M, ldc, device="cuda", generator=g).half() \
+                if epi == ops.EPI_GELU_BWD or extra == "res" else None
+            aux_out = torch.empty(M, ldc, device="cuda", dtype=torch.float16) if epi == ops.EPI_BIAS_GELU else None
+            sets.append((A, B, Cm, aux, aux_out))
+        bias = torch.randn(ldc, device="cuda", generator=g).half() if extra == "bias" or epi == ops.EPI_BIAS_GELU \
+            else None
+        dbias = torch.zeros(M, device="cuda") if extra == "dbias" else None
+        it = [0]
 
         def fn():
-            ops.gemm(A, B, M, Nn, K, am, bm, C_out=Cm, ldc=ldc, epilogue=epi,
-                     bias=bias if epi in (ops.EPI_BIAS_GELU,) else None, aux=aux, aux_out=aux_out,
-                     dbias_rows=dbias, ldb=B.shape[1])
+            A, B, Cm, aux, aux_out = sets[it[0] % nsets]
+            it[0] += 1
+            ops.gemm(A, B, M, Nn, K, am, bm, C_out=Cm, ldc=ldc, epilogue=epi, bias=bias, aux=aux, aux_out=aux_out,
+                     dbias_rows=dbias, lda=lda, ldb=ldb, store_c=epi != ops.EPI_BIAS_GELU)
         work, unit, peak = 2.0 * M * Nn * K, "TFLOP/s", tc
     elif name == "ln_bwd":
-        x = torch.randn(16384, 1024, device="cuda", generator=g).half()
-        dy = torch.randn(16384, 1024, device="cuda", generator=g).half()
-        gam = torch.ones(1024, device="cuda").half()
-        _, mean, rstd = ops.ln_fwd(x, gam, torch.zeros(1024, device="cuda").half())
+        # four input sets (256 MB) rotate, so x and dy come from DRAM as in the step
+        sets = [(torch.randn(16384, 1024, device="cuda", generator=g).half(),
+                 torch.randn(16384, 1024, device="cuda", generator=g).half()) for _ in range(4)]
+        gam = (1 + 0.02 * torch.randn(1024, device="cuda", generator=g)).half()
+        _, mean, rstd = ops.ln_fwd(sets[0][0], gam, torch.zeros(1024, device="cuda").half())
+        dgam, dbet = torch.zeros(1024, device="cuda"), torch.zeros(1024, device="cuda")
+        it = [0]
 
         def fn():
-            ops.ln_bwd(dy, x, gam, mean, rstd)
+            x, dy = sets[it[0] % 4]
+            it[0] += 1
+            ops.ln_bwd(dy, x, gam, mean, rstd, dgamma=dgam, dbeta=dbet)
         work, unit, peak = 16384 * 1024 * 6 + 16384 * 8 + 1024 * 10, "GB/s", hbm
     elif name == "xent":
         z = (2 * torch.randn(8192, 32000, device="cuda", generator=g)).half()
@@ -353,46 +490,63 @@ def kernel_loop(name, reps, torch, ops):
 
 # ------------------------------------------------------------------ GPU leg ----
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=40)
-    ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="rbk", choices=["rbk", "reference"])
-    ap.add_argument("--workload", default="gpt2-small", choices=sorted(WORKLOADS))
-    ap.add_argument("--no-ckpt", action="store_true", help="disable activation checkpointing")
-    ap.add_argument("--no-micro", action="store_true", help="skip the HBM-bound kernel microbench")
-    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--bucket-mb", type=float, default=25.0)
-    ap.add_argument("--kernel", default=None,
-                    help="loop one kernel instead of the training step (gemm_fwd_w1, gemm_fwd_qkv, gemm_dgrad_w2, "
-                         "gemm_dgrad_w1, gemm_wgrad_w1, gemm_lm_fwd, ln_bwd, xent, attn_fwd, attn_bwd, adam_tail)")
-    args = ap.parse_args()
-    if args.kernel:
-        import torch
-        from rbk import ops
-        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
-        return kernel_loop(args.kernel, args.steps, torch, ops)
-    assert args.warmup >= 3 or args.impl == "reference" or os.environ.get("RBK_BENCH_ALLOW_FEW_WARMUP"), \
-        "at least 3 warm-up steps"
-    if args.impl == "reference":
-        return run_reference(args)
+# Mean DRAM read + write bytes of one GEMM launch of the GPT-2-small step: every GEMM shape
+# of the step captured alone with ncu (dram__bytes_read.sum + dram__bytes_write.sum, one launch
+# each, inputs rotating over more than L2), weighted by that shape's launches per step.  The
+# per-shape figures and the command are in profiles/gemm_backward_shapes_ncu.md.
+GEMM_TRAFFIC_PER_LAUNCH = None
 
-    import torch
-    import torch.distributed as dist
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+def check_dp(model, tokens, targets, B, S, world, dist, torch):
+    """Cross-rank check of the data-parallel gradients at this world size, on the workload's
+    own model: (1) two micro-steps without all-reduce give this rank's local sum L; (2) the
+    same two micro-steps with the second all-reducing (gradient accumulation) give G.  G must
+    equal the plain sum over ranks of L (an independent NCCL all-reduce of L) and be
+    bit-identical on every rank (a checksum of its bits, gathered)."""
+    g2 = torch.roll(targets, 1, dims=1)               # a second micro-batch
+    model.grad.zero_()
+    with model.no_sync():
+        for t in (targets, g2):
+            model.forward(tokens, t, B, S)
+            model.backward(tokens, t, B, S, 0.5)
+    local = model.grad.clone()
+    model.grad.zero_()
+    with model.no_sync():
+        model.forward(tokens, targets, B, S)
+        model.backward(tokens, targets, B, S, 0.5)
+    model.forward(tokens, g2, B, S)
+    model.backward(tokens, g2, B, S, 0.5)
+    torch.cuda.synchronize()
+    G = model.grad
+    dist.all_reduce(local, op=dist.ReduceOp.SUM)
+    rel = float((G - local).norm() / local.norm().clamp_min(1e-30))
+    bits = G.view(torch.int32).to(torch.int64)
+    idx = torch.arange(bits.numel(), device=bits.device, dtype=torch.int64) % 1000003 + 1
+    cs = torch.stack([(bits * idx).sum(), G.double().sum().view(torch.int64)])
+    allcs = [torch.zeros_like(cs) for _ in range(world)]
+    dist.all_gather(allcs, cs)
+    agree = all(bool(torch.equal(c, allcs[0])) for c in allcs)
+    finite = bool(torch.isfinite(G).all())
+    model.grad.zero_()
+    del local
+    torch.cuda.synchronize()
+    return {"ga": 2, "ranks_bitwise_equal": agree, "checksum": int(allcs[0][0]), "finite": finite,
+            "rel_l2_vs_allreduce_of_local_sums": rel, "ok": agree and finite and rel < 1e-4,
+            "how": "grad after 2 micro-steps (the 1st without all-reduce) vs an independent all-reduce "
+                   "of each rank's 2-micro-step local sum; bit checksums gathered from every rank"}
 
-    from rbk import lib, ops
+
+def run_workload(name, args, world, rank, local, dist, torch, steps, warmup, e2e=True, profile=True,
+                 dp_check=False):
+    """Builds the workload's model, times `steps` training steps after `warmup`, then a profiled
+    pass (per-launch events) and an end-to-end pass.  Returns the result dict (rank 0 prints)."""
+    import ctypes
+
+    from rbk import lib
     from rbk.model import ModelConfig, RubidiumTransformer, dp_unique_id
 
     hbm_peak, tc_burst, tc_sustained, peak_kind = peaks()
-    wl = WORKLOADS[args.workload]
+    wl = WORKLOADS[name]
     cfg = wl["cfg"]
     B, S = wl["batch"], wl["seq"]
     ntok = B * S
@@ -426,34 +580,33 @@ def main():
         else:
             model.optimizer_step(0, 3e-4, 0.9, 0.999, 1e-8, 0.0)
 
-    def step(t):
+    def step():
         model.forward(tokens, targets, B, S)
         backward(tokens, targets)
         update()
 
-    for i in range(args.warmup):
-        step(0)
+    for _ in range(warmup):
+        step()
     torch.cuda.synchronize()
 
     # ---------------- timed region (device events, max over ranks) ----------
     # The headline pass records no per-kernel events (they cost ~4% of the step and
     # break launch overlap); a second pass of the same steps with an event pair around
     # every launch gives the per-kernel split and the GEMM roofline.
-    import ctypes
     mctx = ctypes.c_void_p()
     lib().rbk_model_ctx(model.handle, ctypes.byref(mctx))
     clocks = Clocks(local)
     clocks.start()
     time.sleep(0.5)   # let the sampler come up before the timed region
-    bw_s = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    bw_e = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    bw_s = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    bw_e = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     launches0 = lib().rbk_launch_count()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t_start.record(stream)
-    for i in range(args.steps):
+    for i in range(steps):
         model.forward(tokens, targets, B, S)
         bw_s[i].record(stream)
         backward(tokens, targets)
@@ -464,73 +617,151 @@ def main():
     launches = lib().rbk_launch_count() - launches0
     clk = clocks.stop()
     ms = t_start.elapsed_time(t_end)
-    bwd_ms = statistics.median(bw_s[i].elapsed_time(bw_e[i]) for i in range(args.steps))
-
-    # ---------------- profiled pass: per-launch events for the kernel split ----
-    lib().rbk_ctx_profile(mctx, 1)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    p_start, p_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    p_start.record(stream)
-    for i in range(args.steps):
-        step(0)
-    p_end.record(stream)
-    torch.cuda.synchronize()
-    prof_ms_step = p_start.elapsed_time(p_end) / args.steps
-    cat_ms = (ctypes.c_double * 9)(); cat_w = (ctypes.c_double * 9)(); cat_n = (ctypes.c_int * 9)()
-    lib().rbk_ctx_profile_read(mctx, cat_ms, cat_w, cat_n, 9)
-    lib().rbk_ctx_profile(mctx, 0)
+    bwd_ms = statistics.median(bw_s[i].elapsed_time(bw_e[i]) for i in range(steps))
     if world > 1:
         t = torch.tensor([ms, bwd_ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, bwd_ms = float(t[0]), float(t[1])
-    ms_step = ms / args.steps
-    value = world * ntok / (ms_step / 1000.0)
+    ms_step = ms / steps
+    res = {"workload": wl["name"], "value": world * ntok / (ms_step / 1000.0), "unit": "tokens/s",
+           "tokens_per_s_per_gpu": ntok / (ms_step / 1000.0), "ms_per_step": ms_step, "steps": steps,
+           "warmup": warmup, "backward_ms_per_step": bwd_ms, "gpu_launches": int(launches), "clocks": clk,
+           "global_batch": B * world, "seq_len": S, "activation_checkpointing": ckpt,
+           "train_tflops_per_gpu": train_flops_per_token(cfg, S, lora["rank"] if lora else 0) * ntok /
+                                   (ms_step / 1000.0) / 1e12,
+           "gemm_flops_per_step": gemm_flops_per_step(cfg, ntok, ckpt, bool(lora))}
+    if world > 1:
+        res["allreduce_bytes_per_step"] = 4 * (model.lora_tensors("grad")[0].numel() * 4 if lora else model.nparams)
+
+    # ---------------- profiled pass: per-launch events for the kernel split ----
+    if profile:
+        lib().rbk_ctx_profile(mctx, 1)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        p_start, p_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p_start.record(stream)
+        for _ in range(steps):
+            step()
+        p_end.record(stream)
+        torch.cuda.synchronize()
+        prof_ms_step = p_start.elapsed_time(p_end) / steps
+        cat_ms = (ctypes.c_double * 9)(); cat_w = (ctypes.c_double * 9)(); cat_n = (ctypes.c_int * 9)()
+        lib().rbk_ctx_profile_read(mctx, cat_ms, cat_w, cat_n, 9)
+        r_ms = (ctypes.c_double * 3)(); r_w = (ctypes.c_double * 3)(); r_n = (ctypes.c_int * 3)()
+        lib().rbk_ctx_profile_read_gemm(mctx, r_ms, r_w, r_n)
+        lib().rbk_ctx_profile(mctx, 0)
+        res["kernels"] = {CAT_NAMES[c]: {"ms_per_step": cat_ms[c] / steps, "launches_per_step": cat_n[c] / steps,
+                                         "share": cat_ms[c] / max(sum(cat_ms), 1e-9)} for c in range(9) if cat_n[c]}
+        gemm_tflops = cat_w[0] / (cat_ms[0] * 1e-3) / 1e12 if cat_ms[0] > 0 else 0.0
+        by_role = {}
+        for i, role in enumerate(("fwd", "dgrad", "wgrad")):
+            if r_n[i]:
+                a = r_w[i] / (r_ms[i] * 1e-3) / 1e12
+                by_role[role] = {"flops_per_step": r_w[i] / steps, "ms_per_step": r_ms[i] / steps,
+                                 "launches_per_step": r_n[i] / steps, "achieved": a, "frac": a / tc_sustained}
+        res["roofline"] = {
+            "bound": "tensor", "kernel": "gemm_pair_kernel / gemm_kernel (tcgen05, all GEMMs of the step)",
+            "achieved": gemm_tflops, "peak": tc_sustained, "unit": "TFLOP/s", "frac": gemm_tflops / tc_sustained,
+            "traffic": GEMM_TRAFFIC_PER_LAUNCH if name == "gpt2-small" else None,
+            "traffic_unit": "DRAM bytes per GEMM launch (ncu, each step shape captured alone, launch-weighted)",
+            "peak_source": f"{peak_kind} bf16_tflops_sustained (FP16 and BF16 share the dense tensor rate)",
+            "by_role": by_role,
+            "gemm_flops_per_launch": cat_w[0] / max(cat_n[0], 1),
+            "gemm_ms_per_launch": cat_ms[0] / max(cat_n[0], 1),
+            "measured": "CUDA events around every GEMM launch in a second pass of the same steps",
+            "profiled_pass_ms_per_step": prof_ms_step}
 
     # ---------------- end-to-end through the public API with host buffers ----
-    h_tok = torch.empty((B, S), dtype=torch.int32, pin_memory=True)
-    h_tgt = torch.empty((B, S), dtype=torch.int32, pin_memory=True)
-    h_tok.copy_(tokens.cpu()); h_tgt.copy_(targets.cpu())
-    d_tok = torch.empty_like(tokens); d_tgt = torch.empty_like(targets)
-    h_loss = torch.empty(1, dtype=torch.float32, pin_memory=True)
-    if world > 1:
-        dist.barrier()
+    if e2e:
+        h_tok = torch.empty((B, S), dtype=torch.int32, pin_memory=True)
+        h_tgt = torch.empty((B, S), dtype=torch.int32, pin_memory=True)
+        h_tok.copy_(tokens.cpu()); h_tgt.copy_(targets.cpu())
+        d_tok = torch.empty_like(tokens); d_tgt = torch.empty_like(targets)
+        h_loss = torch.empty(1, dtype=torch.float32, pin_memory=True)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        w0 = time.perf_counter()
+        for _ in range(steps):
+            d_tok.copy_(h_tok, non_blocking=True)
+            d_tgt.copy_(h_tgt, non_blocking=True)
+            loss = model.forward(d_tok, d_tgt, B, S)
+            backward(d_tok, d_tgt)
+            update()
+            h_loss.copy_(loss.view(1), non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+            _ = float(h_loss[0])
+        e2e_s = time.perf_counter() - w0
+        if world > 1:
+            t = torch.tensor([e2e_s], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_s = float(t[0])
+        res["e2e"] = {"value": world * ntok * steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 2 * ntok * 4,
+                      "d2h_bytes_per_step": 4}
+    if dp_check and world > 1 and not lora:
+        res["dp_check"] = check_dp(model, tokens, targets, B, S, world, dist, torch)
+    res["loss_scale"] = model.loss_scale
+    res["skipped_steps"] = model.scaler().overflow_steps
+    if lora:
+        res["lora"] = {"rank": lora["rank"], "alpha": lora["alpha"], "targets": "q,v",
+                       "inf_injection": f"1 in {wl['inject_stride']} dlogits elements every {wl['inject_every']}th step"}
+    model.close()
+    del tokens, targets
     torch.cuda.synchronize()
-    w0 = time.perf_counter()
-    for i in range(args.steps):
-        d_tok.copy_(h_tok, non_blocking=True)
-        d_tgt.copy_(h_tgt, non_blocking=True)
-        loss = model.forward(d_tok, d_tgt, B, S)
-        backward(d_tok, d_tgt)
-        update()
-        h_loss.copy_(loss.view(1), non_blocking=True)
-        torch.cuda.current_stream().synchronize()
-        _ = float(h_loss[0])
-    e2e_s = time.perf_counter() - w0
+    torch.cuda.empty_cache()
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=40)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="rbk", choices=["rbk", "reference"])
+    ap.add_argument("--workload", default="gpt2-small", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-ckpt", action="store_true", help="disable activation checkpointing")
+    ap.add_argument("--no-micro", action="store_true", help="skip the HBM-bound kernel microbench")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-ref-ops", action="store_true", help="skip timing the reference's own CPU ops")
+    ap.add_argument("--no-1p3b", action="store_true", help="skip the second (1.3B) workload pass")
+    ap.add_argument("--steps-1p3b", type=int, default=5)
+    ap.add_argument("--bucket-mb", type=float, default=25.0)
+    ap.add_argument("--kernel", default=None,
+                    help="loop one kernel instead of the training step (gemm_* of gemm_shapes(), ln_bwd, xent, "
+                         "attn_fwd, attn_bwd, adam_tail)")
+    args = ap.parse_args()
+    if args.kernel:
+        import torch
+        from rbk import ops
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        return kernel_loop(args.kernel, args.steps, torch, ops)
+    assert args.warmup >= 3 or args.impl == "reference" or os.environ.get("RBK_BENCH_ALLOW_FEW_WARMUP"), \
+        "at least 3 warm-up steps"
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
     if world > 1:
-        t = torch.tensor([e2e_s], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t[0])
-    e2e = world * ntok * args.steps / e2e_s
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
 
-    # ---------------- roofline of the dominant kernel (the tcgen05 GEMM) ----
-    per_cat = {CAT_NAMES[c]: {"ms_per_step": cat_ms[c] / args.steps, "launches_per_step": cat_n[c] / args.steps,
-                              "share": cat_ms[c] / max(sum(cat_ms), 1e-9)} for c in range(9) if cat_n[c]}
-    gemm_tflops = cat_w[0] / (cat_ms[0] * 1e-3) / 1e12 if cat_ms[0] > 0 else 0.0
-    # DRAM bytes (read + write) per GEMM launch of the GPT-2-small step, averaged over the 353 GEMM
-    # launches of a one-pass ncu capture of about two steps (dram__bytes_read.sum + dram__bytes_write.sum)
-    traffic = 141.8e6 if args.workload == "gpt2-small" else None
-    roofline = {"bound": "tensor", "kernel": "gemm_pair_kernel / gemm_kernel (tcgen05, all GEMMs of the step)",
-                "achieved": gemm_tflops, "peak": tc_sustained, "unit": "TFLOP/s",
-                "frac": gemm_tflops / tc_sustained, "traffic": traffic,
-                "traffic_unit": "bytes per GEMM launch (ncu capture of the same command)",
-                "peak_source": f"{peak_kind} bf16_tflops_sustained (FP16 and BF16 share the dense tensor rate)",
-                "gemm_flops_per_launch": cat_w[0] / max(cat_n[0], 1),
-                "gemm_ms_per_launch": cat_ms[0] / max(cat_n[0], 1),
-                "measured": "CUDA events around every GEMM launch in a second pass of the same steps",
-                "profiled_pass_ms_per_step": prof_ms_step}
+    from rbk import ops
 
+    hbm_peak, _, _, _ = peaks()
+    wl = WORKLOADS[args.workload]
+    head = run_workload(args.workload, args, world, rank, local, dist, torch, args.steps, args.warmup,
+                        dp_check=True)
+    others = {}
+    if args.workload == "gpt2-small" and not args.no_1p3b:
+        # the 1.3B decoder of the same step, a short pass (its scaling curve rides on every --gpus N run)
+        others["1.3b"] = run_workload("1.3b", args, world, rank, local, dist, torch, args.steps_1p3b, 3,
+                                      e2e=False)
     extra = {}
     if rank == 0 and not args.no_micro:
         try:
@@ -538,43 +769,48 @@ def main():
         except Exception as exc:   # report, never hide
             extra["microbench"] = {"error": repr(exc)}
     cpu = None
-    if rank == 0 and not args.no_cpu:
-        tps, dt, cores = cpu_sample(args.workload, 128)
+    if rank == 0 and world == 1 and not args.no_cpu:
+        tps, dt, cores = cpu_sample(args.workload)
+        seq = CPU_SEQ[args.workload]
         cpu = {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port",
                "sample": f"oracle fwd+bwd+AdamW{' (LoRA adapters)' if wl.get('lora') else ''} of the same model "
-                         f"over 1 x 128 tokens ({dt:.1f} s)"}
+                         f"over 1 x {seq} tokens ({dt:.1f} s, {cores} threads)"}
+        if not args.no_ref_ops and args.workload != "tiny":
+            cpu["reference_ops"] = reference_ops()
     if world > 1:
         dist.barrier()
     if rank == 0:
         out = {
-            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "metric": METRIC, "value": head["value"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp16", "data": "synthetic (uniform random tokens, N(0,0.02) weights)",
-            "config": {"workload": wl["name"], "global_batch": B * world, "seq_len": S,
-                       "parallelism": f"dp{world}", "activation_checkpointing": ckpt,
-                       "loss_scale_init": 65536, "l2": "no flush: weights/activations/logits exceed 126 MB L2"},
-            "tokens_per_s_per_gpu": value / world,
-            "backward_ms_per_step": bwd_ms,
-            "train_tflops_per_gpu": train_flops_per_token(cfg, S, lora["rank"] if lora else 0) * ntok /
-                                    (ms_step / 1000.0) / 1e12,
-            "gemm_flops_per_step": gemm_flops_per_step(cfg, ntok, ckpt, bool(lora)),
-            "roofline": roofline,
-            "kernels": per_cat,
-            "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 2 * ntok * 4, "d2h_bytes_per_step": 4},
-            "gpu_launches": int(launches),
-            "clocks": clk,
+            "config": {"workload": wl["name"], "global_batch": head["global_batch"], "seq_len": head["seq_len"],
+                       "parallelism": f"dp{world}", "activation_checkpointing": head["activation_checkpointing"],
+                       "loss_scale_init": 65536,
+                       "l2": "no flush: weights/activations/logits exceed 126 MB L2",
+                       "value_scope": "whole job: tokens/s summed over all N GPUs; tokens_per_s_per_gpu = value / N"},
+            "tokens_per_s_per_gpu": head["tokens_per_s_per_gpu"],
+            "backward_ms_per_step": head["backward_ms_per_step"],
+            "train_tflops_per_gpu": head["train_tflops_per_gpu"],
+            "gemm_flops_per_step": head["gemm_flops_per_step"],
+            "roofline": head.get("roofline"),
+            "kernels": head.get("kernels"),
+            "e2e": head.get("e2e"),
+            "gpu_launches": head["gpu_launches"],
+            "clocks": head["clocks"],
             "cpu_baseline": cpu,
-            "loss_scale": model.loss_scale,
-            "skipped_steps": model.scaler().overflow_steps,
+            "loss_scale": head["loss_scale"],
+            "skipped_steps": head["skipped_steps"],
         }
-        if lora:
-            out["config"].update(lora_rank=lora["rank"], lora_alpha=lora["alpha"], lora_targets="q,v",
-                                 inf_injection=f"1 in {wl['inject_stride']} dlogits elements every "
-                                               f"{wl['inject_every']}th step")
+        for k in ("dp_check", "allreduce_bytes_per_step", "lora"):
+            if k in head:
+                out[k] = head[k]
+        if others:
+            out["workloads"] = others
         out.update(extra)
         print(json.dumps(out), flush=True)
-    model.close()
     if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
     return 0
 

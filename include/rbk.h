@@ -70,6 +70,11 @@ int rbk_ctx_destroy(rbk_ctx* ctx);
 long long rbk_launch_count(void);
 int rbk_ctx_profile(rbk_ctx* ctx, int enable);
 int rbk_ctx_profile_read(rbk_ctx* ctx, double* ms, double* work, int* launches, int ncat);
+/* The GEMM category split by role (3 slots each): 0 forward (and checkpoint
+ * recompute), 1 data gradient (dgrad), 2 weight gradient (wgrad).  The model
+ * tags every GEMM it issues; a direct rbk_gemm call counts as wgrad when its
+ * epilogue accumulates / stores FP32, dgrad when B is MN-major, else forward. */
+int rbk_ctx_profile_read_gemm(rbk_ctx* ctx, double* ms, double* flops, int* launches);
 int rbk_ctx_device_error(rbk_ctx* ctx, int* status);
 
 /* ------------------------------------------------------------------------
@@ -101,14 +106,17 @@ int rbk_ln_bwd(rbk_ctx* ctx, void* dx, float* dgamma, float* dbeta, float* dbias
  * reference.  Meant for hosts whose device memory is all owned by their own
  * pool (as the reference trainer's fixed MemPool arena) or that cannot take
  * the device-wide synchronisation an allocation costs inside a step loop.
- * Same arguments and results as rbk_ln_bwd (identical launch shape).
+ * Same arguments and outputs as rbk_ln_bwd; it runs a different kernel (the
+ * non-ring LayerNorm backward), so the results agree with rbk_ln_bwd to
+ * rounding, not bit for bit.
  *   - Scratch: one fixed array of RBK_LN_BWD_NOALLOC_SCRATCH_BYTES (4 MiB) in
  *     device memory, reserved once by every GPU that loads the library and
  *     held until the process exits; enough for D <= 2048 on a 148-SM B200.
  *     Larger needs are rejected with RBK_ERR_INVALID (use rbk_ln_bwd).
  *   - The first call on each device looks up that array's device address
  *     (with the device current); make that first call before any stream
- *     capture.
+ *     capture.  `stream` must belong to the current device (RBK_ERR_INVALID
+ *     otherwise).
  *   - Every call shares the one array.  Each call overwrites the whole part it
  *     uses, so nothing carries over, but calls that overlap on the GPU (other
  *     streams, other threads) race on it: serialise them. */
@@ -430,6 +438,14 @@ int rbk_dp_plan(const rbk_config* cfg, int64_t bucket_bytes, int64_t* out, int m
 int rbk_dp_unique_id(void* id128);
 /* Join the communicator; bucket_bytes (25 MB) sets the all-reduce granularity. */
 int rbk_model_dp_init(rbk_model* m, const void* id128, int rank, int world, int64_t bucket_bytes);
+/* Gradient accumulation under data parallelism (the reference accumulates GA
+ * micro-steps per optimizer step, src/main.cpp:136-164).  sync = 0: following
+ * backwards only accumulate this rank's gradients, no all-reduce; sync = 1
+ * (the default): backward all-reduces the whole accumulated arena bucket by
+ * bucket.  Set 0 before the first GA - 1 micro-steps of a step and 1 before
+ * the last; rbk_model_train does this itself.  Each rank's micro-steps then
+ * enter the reduced sum exactly once. */
+int rbk_model_dp_set_sync(rbk_model* m, int sync);
 int rbk_model_dp_shutdown(rbk_model* m);
 
 #ifdef __cplusplus

@@ -33,13 +33,14 @@ def _p(a, ct=C.c_float):
 
 
 def build(ref: bool | None = None) -> None:
-    """Compile liboracle.so (and the reference shim when the reference tree exists)."""
+    """Compile liboracle.so, and the reference shim when RBK_REFERENCE names the reference
+    project's root (the directory holding its src/)."""
     subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    root = os.environ.get("RBK_REFERENCE", "")
     if ref is None:
-        ref = os.path.isdir(os.environ.get("RBK_REFERENCE", "/root/reference") + "/src")
+        ref = bool(root) and os.path.isdir(os.path.join(root, "src"))
     if ref:
-        subprocess.run(["make", "-s", "-C", _HERE, "ref",
-                        "REF=" + os.environ.get("RBK_REFERENCE", "/root/reference")], check=True)
+        subprocess.run(["make", "-s", "-C", _HERE, "ref", "REF=" + root], check=True)
 
 
 def lib():
@@ -70,6 +71,9 @@ def ref_lib():
         _REF.ref_cross_entropy.restype = C.c_float
         _REF.ref_clip_gradients.restype = C.c_float
         _REF.ref_cpu_forward.restype = C.c_float
+        for name in ("ref_time_layer_norm_backward", "ref_time_softmax_backward", "ref_time_cross_entropy_backward",
+                     "ref_time_adamw_step", "ref_time_cpu_forward"):
+            getattr(_REF, name).restype = C.c_double
     return _REF
 
 
@@ -83,6 +87,18 @@ def i32(a):
 
 def num_threads() -> int:
     return lib().ora_num_threads()
+
+
+def set_threads(n: int | None = None) -> int:
+    """Use n OpenMP threads (default: every core this process may run on) and return the count.
+    torchrun exports OMP_NUM_THREADS=1 to each rank; the CPU baseline sets its count explicitly."""
+    if n is None:
+        try:
+            n = len(os.sched_getaffinity(0))
+        except AttributeError:
+            n = os.cpu_count() or 1
+    lib().ora_set_threads(int(n))
+    return num_threads()
 
 
 # ------------------------------------------------------------------ ops ----

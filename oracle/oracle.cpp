@@ -640,5 +640,9 @@ int ora_param_table(const int* cfg6, long* off_rows_cols) {
 }
 
 int ora_num_threads(void) { return omp_get_max_threads(); }
+// Thread count for the following calls (torchrun exports OMP_NUM_THREADS=1 to every rank).
+void ora_set_threads(int n) {
+    if (n > 0) omp_set_num_threads(n);
+}
 
 }  // extern "C"

@@ -16,6 +16,7 @@
 //   cpuops::clip_gradients                     src/cpu_mat.h:295-306
 //   cpuops::matmul / matmul_tB / matmul_tA     src/cpu_mat.h:47-95
 //   CPUTransformer::forward                    src/cpu_model.cpp:115-222
+#include <chrono>
 #include <cstring>
 #include <vector>
 
@@ -28,6 +29,9 @@ Mat mk(const float* p, int r, int c) {
     return m;
 }
 void out(float* dst, const Mat& m) { std::memcpy(dst, m.data.data(), sizeof(float) * m.data.size()); }
+double secs(std::chrono::steady_clock::time_point t0) {
+    return std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+}
 }  // namespace
 
 extern "C" {
@@ -146,6 +150,74 @@ float ref_cpu_forward(int V, int T, int D, int H, int L, int FF, const float* to
     m.w.lm_b = mk(lm_b, 1, V);
     std::vector<int> tk(tokens, tokens + S), tg(targets, targets + S);
     return m.forward(tk, &tg);
+}
+
+// ---- timed variants for the CPU baseline: inputs are copied into the engine's
+// matrices first, then only the reference call itself is timed (seconds).
+double ref_time_layer_norm_backward(const float* dy, const float* x, const float* g, const float* mean,
+                                    const float* rstd, int N, int D) {
+    Mat DY = mk(dy, N, D), X = mk(x, N, D), G = mk(g, 1, D), M = mk(mean, N, 1), R = mk(rstd, N, 1);
+    Mat DX, DG, DB;
+    const auto t0 = std::chrono::steady_clock::now();
+    cpuops::layer_norm_backward(DX, DG, DB, DY, X, G, M, R);
+    return secs(t0);
+}
+
+double ref_time_softmax_backward(const float* dy, const float* y, int N, int C) {
+    Mat DY = mk(dy, N, C), Y = mk(y, N, C), DX;
+    const auto t0 = std::chrono::steady_clock::now();
+    cpuops::softmax_backward(DX, DY, Y);
+    return secs(t0);
+}
+
+double ref_time_cross_entropy_backward(const float* logits, const int* tgt, int N, int V) {
+    Mat Z = mk(logits, N, V), D;
+    std::vector<int> t(tgt, tgt + N);
+    const auto t0 = std::chrono::steady_clock::now();
+    cpuops::cross_entropy_backward(D, Z, t);
+    return secs(t0);
+}
+
+double ref_time_adamw_step(const float* p, const float* g, int n, float lr, float b1, float b2, float eps, float wd) {
+    Mat P = mk(p, 1, n), G = mk(g, 1, n), M(1, n), Vv(1, n);
+    const auto t0 = std::chrono::steady_clock::now();
+    cpuops::adamw_step(P, G, M, Vv, lr, b1, b2, eps, wd, 1);
+    return secs(t0);
+}
+
+// CPUTransformer::forward (with its loss) on one sequence of S tokens; the
+// same weight blocks as ref_cpu_forward (V == D), only the forward timed.
+double ref_time_cpu_forward(int V, int T, int D, int H, int L, int FF, const float* tok_emb, const float* pos_emb,
+                            const float* layers, const float* ln_f_w, const float* ln_f_b, const float* lm_w,
+                            const float* lm_b, const int* tokens, const int* targets, int S, float* loss) {
+    CPUConfig cfg;
+    cfg.init(V, T, D, H, L, FF);
+    CPUTransformer m;
+    m.init(cfg);
+    m.allocate_activations(S);
+    m.w.token_emb = mk(tok_emb, V, D);
+    m.w.pos_emb = mk(pos_emb, T, D);
+    const float* p = layers;
+    auto take = [&](Mat& dst, int r, int c) { dst = mk(p, r, c); p += (size_t)r * c; };
+    for (int l = 0; l < L; ++l) {
+        auto& ly = m.w.layers[l];
+        take(ly.ln1_w, 1, D); take(ly.ln1_b, 1, D);
+        take(ly.wq, D, D); take(ly.bq, 1, D);
+        take(ly.wk, D, D); take(ly.bk, 1, D);
+        take(ly.wv, D, D); take(ly.bv, 1, D);
+        take(ly.wo, D, D); take(ly.bo, 1, D);
+        take(ly.ln2_w, 1, D); take(ly.ln2_b, 1, D);
+        take(ly.w1, D, FF); take(ly.b1, 1, FF);
+        take(ly.w2, FF, D); take(ly.b2, 1, D);
+    }
+    m.w.ln_f_w = mk(ln_f_w, 1, D);
+    m.w.ln_f_b = mk(ln_f_b, 1, D);
+    m.w.lm_w = mk(lm_w, V, D);
+    m.w.lm_b = mk(lm_b, 1, V);
+    std::vector<int> tk(tokens, tokens + S), tg(targets, targets + S);
+    const auto t0 = std::chrono::steady_clock::now();
+    *loss = m.forward(tk, &tg);
+    return secs(t0);
 }
 
 }  // extern "C"

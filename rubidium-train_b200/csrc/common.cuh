@@ -59,7 +59,7 @@ void count_launch();   // every kernel launched by librbk is counted (rbk_launch
 struct rbk_prof {
     bool on = false;
     std::vector<cudaEvent_t> pool;     // start/stop pairs
-    struct Rec { int cat; double work; };
+    struct Rec { int cat; double work; int sub; };   // sub: GEMM role (0 fwd, 1 dgrad, 2 wgrad) or -1
     std::vector<Rec> recs;             // recs[i] uses pool[2i], pool[2i+1]
 };
 
@@ -73,6 +73,9 @@ struct rbk_ctx {
     static constexpr int kTickets = 64;
     int* err = nullptr;      // device error word written by bounded waits
     rbk_prof prof;
+    // Role of the next GEMMs for the profiler (0 forward, 1 dgrad, 2 wgrad); -1: derived from
+    // the descriptor (FP32-accumulating epilogues are weight gradients, an MN-major B a dgrad).
+    int gemm_role = -1;
 };
 
 namespace rbk {
@@ -86,7 +89,7 @@ struct ProfScope {
     rbk_ctx* ctx;
     cudaStream_t st;
     int idx = -1;
-    ProfScope(rbk_ctx* c, cudaStream_t s, int cat, double work);
+    ProfScope(rbk_ctx* c, cudaStream_t s, int cat, double work, int sub = -1);
     ~ProfScope();
 };
 

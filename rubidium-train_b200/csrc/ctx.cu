@@ -15,7 +15,7 @@ void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 constexpr int kProfPairs = 32768;   // ~130 timed steps of the 12-layer model
 
-ProfScope::ProfScope(rbk_ctx* c, cudaStream_t s, int cat, double work) : ctx(c), st(s) {
+ProfScope::ProfScope(rbk_ctx* c, cudaStream_t s, int cat, double work, int sub) : ctx(c), st(s) {
     if (!c || !c->prof.on) return;
     rbk_prof& p = c->prof;
     const int i = (int)p.recs.size();
@@ -27,7 +27,7 @@ ProfScope::ProfScope(rbk_ctx* c, cudaStream_t s, int cat, double work) : ctx(c),
             p.pool.push_back(e);
         }
     }
-    p.recs.push_back({cat, work});
+    p.recs.push_back({cat, work, sub});
     cudaEventRecord(p.pool[2 * i], s);
     idx = i;
 }
@@ -191,6 +191,22 @@ int rbk_ctx_profile_read(rbk_ctx* ctx, double* ms, double* work, int* launches, 
         ms[c] += t;
         work[c] += p.recs[i].work;
         launches[c] += 1;
+    }
+    return RBK_OK;
+}
+
+int rbk_ctx_profile_read_gemm(rbk_ctx* ctx, double* ms, double* flops, int* launches) {
+    RBK_REQUIRE(ctx && ms && flops && launches, "rbk_ctx_profile_read_gemm: bad arguments");
+    for (int c = 0; c < 3; ++c) { ms[c] = 0.0; flops[c] = 0.0; launches[c] = 0; }
+    rbk_prof& p = ctx->prof;
+    for (size_t i = 0; i < p.recs.size(); ++i) {
+        if (p.recs[i].cat != kCatGemm || p.recs[i].sub < 0 || p.recs[i].sub > 2) continue;
+        RBK_CUDA(cudaEventSynchronize(p.pool[2 * i + 1]));
+        float t = 0.0f;
+        RBK_CUDA(cudaEventElapsedTime(&t, p.pool[2 * i], p.pool[2 * i + 1]));
+        ms[p.recs[i].sub] += t;
+        flops[p.recs[i].sub] += p.recs[i].work;
+        launches[p.recs[i].sub] += 1;
     }
     return RBK_OK;
 }

@@ -965,7 +965,9 @@ int rbk_gemm(rbk_ctx* ctx, const rbk_gemm_desc* d, void* stream) {
     p.alpha = d->alpha;
     p.err = ctx->tickets + kGemmError;
     cudaStream_t st = as_stream(stream);
-    ProfScope prof(ctx, st, kCatGemm, 2.0 * d->M * (double)d->N * d->K);
+    const int role = ctx->gemm_role >= 0 ? ctx->gemm_role
+                     : (epi == RBK_EPI_ACC_F32 || epi == RBK_EPI_STORE_F32) ? 2 : d->b_major ? 1 : 0;
+    ProfScope prof(ctx, st, kCatGemm, 2.0 * d->M * (double)d->N * d->K, role);
     if (pair) {
         switch (epi) {
             case RBK_EPI_STORE_F16: return launch_pair<RBK_EPI_STORE_F16>(ctx, d, p, st);

@@ -684,7 +684,15 @@ extern "C" int rbk_ln_bwd_noalloc(void* dx, float* dgamma, float* dbeta, float* 
     int dev = 0, sms = 0;
     float* part = nullptr;
     RBK_TRY(noalloc_setup(&dev, &part, &sms));
-    // Same launch shape as rbk_ln_bwd, so both entry points give identical results.
+    if (stream) {
+        // the array's address is per device: a stream of another GPU would get the wrong one
+        int sdev = -1;
+        RBK_CUDA(cudaStreamGetDevice(as_stream(stream), &sdev));
+        RBK_REQUIRE(sdev == dev, "rbk_ln_bwd_noalloc: the stream belongs to device %d, the current device is %d",
+                    sdev, dev);
+    }
+    // A separate kernel from rbk_ln_bwd's ring (scalar FP32 arithmetic, one team per row group,
+    // no timeout word): the results agree with rbk_ln_bwd to rounding, not bit for bit.
     const int tpt = ((D / 8 + 31) / 32) * 32;
     int teams = 512 / tpt;
     teams = teams < 1 ? 1 : teams > kLnMaxTeams ? kLnMaxTeams : teams;

@@ -73,6 +73,15 @@ int grid_for(int64_t n, int sms) {
 }
 
 // ---------------------------------------------------------------- GEMMs ----
+// Tags the GEMMs issued in its scope for the profiler's forward / dgrad / wgrad split.
+struct Role {
+    rbk_ctx* ctx;
+    int saved;
+    Role(rbk_ctx* c, int r) : ctx(c), saved(c->gemm_role) { c->gemm_role = r; }
+    ~Role() { ctx->gemm_role = saved; }
+};
+enum { kFwd = 0, kDgrad = 1, kWgrad = 2 };
+
 struct G {
     rbk_ctx* ctx;
     cudaStream_t st;
@@ -93,16 +102,19 @@ struct G {
     // Y[Nt, out] = X[Nt, in] W^T  (+bias, +residual) ; ldx/ldy row strides
     int fwd(half* Y, int ldy, const half* X, int ldx, const half* W, int Nt, int in, int out, const half* bias,
             const half* res = nullptr, int ldres = 0) {
+        Role r(ctx, kFwd);
         return raw(Nt, out, in, X, ldx, 0, W, in, 0, Y, ldy, RBK_EPI_STORE_F16, bias, res, ldres);
     }
     // dX[Nt, in] = dY[Nt, out] W   (optionally * gelu'(pre))
     int dgrad(half* dX, int lddx, const half* dY, int lddy, const half* W, int Nt, int in, int out,
               const half* gelu_pre = nullptr) {
+        Role r(ctx, kDgrad);
         return raw(Nt, in, out, dY, lddy, 0, W, in, 1, dX, lddx, gelu_pre ? RBK_EPI_GELU_BWD : RBK_EPI_STORE_F16,
                    nullptr, gelu_pre, gelu_pre ? lddx : 0);
     }
     // dW[out, in] += dY^T X ; dbias[out] += colsum(dY)
     int wgrad(float* dW, float* dbias, const half* dY, int lddy, const half* X, int ldx, int Nt, int in, int out) {
+        Role r(ctx, kWgrad);
         return raw(out, in, Nt, dY, lddy, 1, X, ldx, 1, dW, in, RBK_EPI_ACC_F32, nullptr, nullptr, 0, nullptr, dbias);
     }
 };
@@ -193,6 +205,7 @@ static int layer_attn_inputs(rbk_model* m, int l, int B, int S, cudaStream_t st)
     LayerWeights& y = m->w.layers[l];
     LayerActs& la = m->act.layers[l];
     G g{m->ctx, st};
+    Role role(m->ctx, kFwd);
     // (in the backward's recompute this rewrites bit-identical statistics)
     RBK_TRY(rbk_ln_fwd(m->ctx, la.h1, la.ln1_mean, la.ln1_inv_std, la.x_in, y.ln1_w, y.ln1_b, N, D, 1e-5f, st));
     RBK_TRY(g.fwd(la.qkv, 3 * D, la.h1, D, y.wq, N, D, 3 * D, y.bq));
@@ -223,6 +236,7 @@ static int layer_ffn_inputs(rbk_model* m, int l, int N, cudaStream_t st, bool st
     LayerWeights& y = m->w.layers[l];
     LayerActs& la = m->act.layers[l];
     G g{m->ctx, st};
+    Role role(m->ctx, kFwd);
     return g.raw(N, F, D, la.h2_checkpoint, D, 0, y.w1, D, 0, store_pre ? la.fi_pre : nullptr, F, RBK_EPI_BIAS_GELU,
                  y.b1, nullptr, F, la.fi);
 }
@@ -264,6 +278,7 @@ static int forward(rbk_model* m, const int* tokens, const int* targets, int B, i
 
 // ------------------------------------------------------------ data parallel --
 static int dp_unit_done(rbk_model* m, int unit, cudaStream_t st);
+static int dp_reduce_all(rbk_model* m, float* buf, int64_t n, cudaStream_t st);
 
 // ------------------------------------------------------------- backward ----
 static int backward(rbk_model* m, const int* tokens, const int* targets, int B, int S, float grad_scale,
@@ -274,6 +289,12 @@ static int backward(rbk_model* m, const int* tokens, const int* targets, int B, 
     G g{m->ctx, st};
     Activations& a = m->act;
     const float world = m->dp.on ? (float)m->dp.world : 1.0f;
+    // Gradients accumulate across backward calls; only the last micro-step of an accumulation
+    // group all-reduces, so each rank's earlier micro-steps enter the sum exactly once.
+    // Under LoRA the frozen base has no gradients to exchange: the adapter arena is reduced once
+    // at the end instead (a few MB).
+    const bool reduce = m->dp.on && m->dp.sync && m->lora.rank == 0;
+    const bool reduce_lora = m->dp.on && m->dp.sync && m->lora.rank > 0;
     // dlogits = (softmax - onehot) * grad_scale / (N * world) * loss_scale, in place.  When the
     // forward already wrote it (training mode), grad_scale rides on the LM-head GEMMs' alpha.
     float head_alpha = 1.0f;
@@ -291,11 +312,16 @@ static int backward(rbk_model* m, const int* tokens, const int* targets, int B, 
         m->inject_pending = false;
     }
     // LM head
-    RBK_TRY(g.raw(N, D, V, a.logits, m->ldV, 0, m->w.lm_w, D, 1, a.dh, D, RBK_EPI_STORE_F16, nullptr, nullptr, 0,
-                  nullptr, nullptr, head_alpha));
-    if (base)
+    {
+        Role role(m->ctx, kDgrad);
+        RBK_TRY(g.raw(N, D, V, a.logits, m->ldV, 0, m->w.lm_w, D, 1, a.dh, D, RBK_EPI_STORE_F16, nullptr, nullptr, 0,
+                      nullptr, nullptr, head_alpha));
+    }
+    if (base) {
+        Role role(m->ctx, kWgrad);
         RBK_TRY(g.raw(V, D, N, a.logits, m->ldV, 1, a.hf, D, 1, m->w.g_lm_w, D, RBK_EPI_ACC_F32, nullptr, nullptr, 0,
                       nullptr, m->w.g_lm_b, head_alpha));
+    }
     // final LN (under LoRA the LN parameters are frozen: their gradients go to a sink)
     float* sk = a.sink;
     half* gcur = a.g0;
@@ -307,7 +333,7 @@ static int backward(rbk_model* m, const int* tokens, const int* targets, int B, 
     RBK_TRY(rbk_ln_bwd(m->ctx, gcur, base ? m->w.g_ln_f_w : sk, base ? m->w.g_ln_f_b : sk + D,
                        base ? m->w.layers[L - 1].g_b2 : nullptr, a.dh, nullptr, a.x_out, m->w.ln_f_w, a.ln_f_mean,
                        a.ln_f_inv_std, N, D, 0, st));
-    if (m->dp.on) RBK_TRY(dp_unit_done(m, 0, st));
+    if (reduce) RBK_TRY(dp_unit_done(m, 0, st));
     for (int l = L - 1; l >= 0; --l) {
         LayerWeights& y = m->w.layers[l];
         LayerActs& la = a.layers[l];
@@ -347,15 +373,20 @@ static int backward(rbk_model* m, const int* tokens, const int* targets, int B, 
                 float* dBl = lo.grad + (t ? 3 * szA : szA) + (int64_t)l * r * D;
                 const half* xa = lo.xa + (int64_t)t * N * r;
                 const half* dy = a.dqkv + (t ? 2 * D : 0);
+                Role wg(m->ctx, kWgrad);
                 // dB += s xa^T dy        [r, D]
                 RBK_TRY(g.raw(r, D, N, xa, r, 1, dy, 3 * D, 1, dBl, D, RBK_EPI_ACC_F32, nullptr, nullptr, 0, nullptr,
                               nullptr, lo.scaling));
                 // dyb = s dy B^T         [N, r]
-                RBK_TRY(g.raw(N, r, D, dy, 3 * D, 0, Bl, D, 0, lo.dyb, r, RBK_EPI_STORE_F16, nullptr, nullptr, 0,
-                              nullptr, nullptr, lo.scaling));
+                {
+                    Role dg(m->ctx, kDgrad);
+                    RBK_TRY(g.raw(N, r, D, dy, 3 * D, 0, Bl, D, 0, lo.dyb, r, RBK_EPI_STORE_F16, nullptr, nullptr, 0,
+                                  nullptr, nullptr, lo.scaling));
+                }
                 // dA += h1^T dyb         [D, r]
                 RBK_TRY(g.raw(D, r, N, la.h1, D, 1, lo.dyb, r, 1, dAl, r, RBK_EPI_ACC_F32));
                 // dh1 += dyb A^T         [N, D]  (A [D, r]: B(n=d, k=j) = A[d*r + j] -> K-major)
+                Role dg(m->ctx, kDgrad);
                 RBK_TRY(g.raw(N, D, r, lo.dyb, r, 0, Al, r, 0, a.dh, D, RBK_EPI_STORE_F16, nullptr, a.dh, D));
             }
         }
@@ -364,10 +395,11 @@ static int backward(rbk_model* m, const int* tokens, const int* targets, int B, 
                            base && l > 0 ? m->w.layers[l - 1].g_b2 : nullptr, a.dh, gcur, la.x_in, y.ln1_w,
                            la.ln1_mean, la.ln1_inv_std, N, D, 0, st));
         std::swap(gcur, gnext);
-        if (m->dp.on) RBK_TRY(dp_unit_done(m, L - l, st));
+        if (reduce) RBK_TRY(dp_unit_done(m, L - l, st));
     }
     if (base) RBK_TRY(rbk_embed_bwd(m->ctx, m->w.g_token_emb, m->w.g_pos_emb, gcur, tokens, B, S, D, V, st));
-    if (m->dp.on) RBK_TRY(dp_unit_done(m, L + 1, st));
+    if (reduce) RBK_TRY(dp_unit_done(m, L + 1, st));
+    if (reduce_lora) RBK_TRY(dp_reduce_all(m, m->lora.grad, m->lora.n, st));
     return RBK_OK;
 }
 
@@ -426,6 +458,22 @@ static int dp_unit_done(rbk_model* m, int u, cudaStream_t st) {
         RBK_CUDA(cudaEventRecord(d.all_done, d.stream));
         RBK_CUDA(cudaStreamWaitEvent(st, d.all_done, 0));
     }
+    return RBK_OK;
+}
+
+// One all-reduce of a whole gradient buffer on the communication stream, ordered after the work
+// on `st` so far, with `st` waiting for it (the LoRA adapter arena).
+static int dp_reduce_all(rbk_model* m, float* buf, int64_t n, cudaStream_t st) {
+    DpState& d = m->dp;
+    RBK_CUDA(cudaEventRecord(d.layer_done[0], st));
+    RBK_CUDA(cudaStreamWaitEvent(d.stream, d.layer_done[0], 0));
+    ncclResult_t r = ncclAllReduce(buf, buf, (size_t)n, ncclFloat32, ncclSum, d.comm, d.stream);
+    if (r != ncclSuccess) {
+        set_error("ncclAllReduce failed: %s", ncclGetErrorString(r));
+        return RBK_ERR_NCCL;
+    }
+    RBK_CUDA(cudaEventRecord(d.all_done, d.stream));
+    RBK_CUDA(cudaStreamWaitEvent(st, d.all_done, 0));
     return RBK_OK;
 }
 
@@ -701,6 +749,12 @@ int rbk_model_dp_init(rbk_model* m, const void* id128, int rank, int world, int6
     m->dp.rank = rank;
     m->dp.world = world;
     m->dp.on = true;
+    return RBK_OK;
+}
+
+int rbk_model_dp_set_sync(rbk_model* m, int sync) {
+    RBK_REQUIRE(m, "rbk_model_dp_set_sync: null model");
+    m->dp.sync = sync != 0;
     return RBK_OK;
 }
 

@@ -90,6 +90,9 @@ struct DpBucket {
 
 struct DpState {
     bool on = false;
+    // false: backward only accumulates this rank's gradients (the micro-steps of a gradient
+    // accumulation group before its last); true: buckets are all-reduced as they finish.
+    bool sync = true;
     int rank = 0, world = 1;
     ncclComm_t comm = nullptr;
     cudaStream_t stream = nullptr;

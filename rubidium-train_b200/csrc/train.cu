@@ -90,9 +90,14 @@ extern "C" int rbk_model_train(rbk_model* m, const rbk_train_args* a, void* stre
     }
     int rc = RBK_OK;
     const bool lora = m->lora.rank > 0;
+    // Data parallel: the micro-steps before the last of each step only accumulate this rank's
+    // gradients; the last one all-reduces the accumulated sum (src/main.cpp:136-164 runs GA
+    // micro-steps per optimizer step).
+    const bool sync_saved = m->dp.sync;
     for (int s = 0; s < a->steps && rc == RBK_OK; ++s) {
         const int step = a->first_step + s;
         for (int g = 0; g < a->ga && rc == RBK_OK; ++g) {
+            m->dp.sync = g == a->ga - 1;
             const int64_t k = (int64_t)s * a->ga + g;                 // micro-step of this call
             const int64_t sample0 = ((int64_t)(step - 1) * a->ga + g) * a->B;   // run-wide sample index
             gather_windows_kernel<<<(BT + 255) / 256, 256, 0, st>>>(tok, tgt, a->tokens, a->n_tokens,
@@ -109,6 +114,7 @@ extern "C" int rbk_model_train(rbk_model* m, const rbk_train_args* a, void* stre
         rc = lora ? rbk_model_lora_step(m, step, lr, a->b1, a->b2, a->eps, a->wd, stream)
                   : rbk_model_optimizer_step(m, step, lr, a->b1, a->b2, a->eps, a->wd, a->clip, stream);
     }
+    m->dp.sync = sync_saved;
     std::vector<float> h;
     if (rc == RBK_OK && a->losses) {
         h.resize((size_t)micro);

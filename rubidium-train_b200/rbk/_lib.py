@@ -74,6 +74,7 @@ _SIGS = {
     "rbk_launch_count": (C.c_longlong, []),
     "rbk_ctx_profile": (i32, [vp, i32]),
     "rbk_ctx_profile_read": (i32, [vp, C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(i32), i32]),
+    "rbk_ctx_profile_read_gemm": (i32, [vp, C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(i32)]),
     "rbk_ctx_device_error": (i32, [vp, C.POINTER(i32)]),
     "rbk_model_ctx": (i32, [vp, C.POINTER(vp)]),
     "rbk_ln_fwd": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, f32, vp]),
@@ -111,6 +112,7 @@ _SIGS = {
     "rbk_dp_unique_id": (i32, [vp]),
     "rbk_dp_plan": (i32, [C.POINTER(Config), i64, C.POINTER(i64), i32, C.POINTER(i32)]),
     "rbk_model_dp_init": (i32, [vp, vp, i32, i32, i64]),
+    "rbk_model_dp_set_sync": (i32, [vp, i32]),
     "rbk_model_dp_shutdown": (i32, [vp]),
 }
 

@@ -14,6 +14,7 @@ of the device arenas (include/rbk_layout.h order), by tensor name.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes as C
 from dataclasses import dataclass
 
@@ -254,6 +255,21 @@ class RubidiumTransformer:
     def dp_init(self, rank: int, world: int, unique_id: bytes, bucket_bytes: int = 25 << 20):
         buf = C.create_string_buffer(unique_id, 128)
         call("rbk_model_dp_init", self.handle, buf, rank, world, C.c_int64(bucket_bytes))
+
+    def dp_set_sync(self, sync: bool):
+        """sync False: following backwards only accumulate this rank's gradients (the first
+        GA - 1 micro-steps of a step); True (default): backward all-reduces the accumulated
+        arena bucket by bucket (the last micro-step)."""
+        call("rbk_model_dp_set_sync", self.handle, int(bool(sync)))
+
+    @contextlib.contextmanager
+    def no_sync(self):
+        """Backwards inside the block skip the all-reduce (gradient accumulation)."""
+        self.dp_set_sync(False)
+        try:
+            yield
+        finally:
+            self.dp_set_sync(True)
 
     def dp_shutdown(self):
         call("rbk_model_dp_shutdown", self.handle)

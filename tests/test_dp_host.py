@@ -7,7 +7,12 @@ the GPU path relies on, reproduced with gloo collectives on the same buckets:
   - summing the pre-divided (1/world) per-rank gradients bucket by bucket gives
     the gradient of the global mean loss;
   - a non-finite value on one rank reaches every rank through the sum, so the
-    overflow / skip decision is identical everywhere.
+    overflow / skip decision is identical everywhere;
+  - gradient accumulation (GA micro-steps per optimizer step, src/main.cpp:136-164):
+    with the schedule the library uses (micro-steps before the last only accumulate,
+    the last all-reduces the accumulated arena) the result is the mean gradient over
+    all ranks and micro-steps; all-reducing the accumulated arena after every
+    micro-step instead weights earlier micro-steps by world^(GA-1-k).
 """
 import os
 
@@ -101,3 +106,56 @@ def test_two_rank_gloo_bucketed_allreduce_semantics():
         assert same, "ranks derived different all-reduce plans"
         assert ok_sum, "bucketed sum of pre-divided gradients != mean gradient"
         assert skips == [1, 1], "overflow decision differs across ranks"
+
+
+def _ga_worker(rank, world, port, ga, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        cfg = TINY
+        plan = _plan(cfg, 1 << 20)
+        _, n = _arena(cfg)
+        rng = np.random.default_rng(200 + rank)
+        micro = [rng.standard_normal(n).astype(np.float32) for _ in range(ga)]   # per micro-step mean-loss grads
+
+        def bucketed_allreduce(g):
+            for _, b, e in plan:
+                seg = g[b:e].clone()
+                dist.all_reduce(seg, op=dist.ReduceOp.SUM)
+                g[b:e] = seg
+
+        def run(sync_of):
+            acc = torch.zeros(n)
+            for k in range(ga):
+                acc += torch.from_numpy(micro[k]) / (world * ga)   # backward factor 1/GA, seed pre-divided by world
+                if sync_of(k):
+                    bucketed_allreduce(acc)
+            return acc
+
+        fixed = run(lambda k: k == ga - 1)          # rbk_model_train: sync only on the last micro-step
+        every = run(lambda k: True)                 # the schedule without the sync switch
+        allm = [torch.zeros(ga, n) for _ in range(world)]
+        dist.all_gather(allm, torch.from_numpy(np.stack(micro)))
+        expect = torch.stack(allm).mean(dim=(0, 1))
+        q.put((rank, bool(torch.allclose(fixed, expect, rtol=1e-5, atol=1e-6)),
+               bool(torch.allclose(every, expect, rtol=1e-3, atol=1e-4))))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("ga", [2, 4])
+def test_two_rank_gloo_grad_accumulation_schedule(ga):
+    world = 2
+    port = 29700 + (os.getpid() % 1000) + ga
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_ga_worker, args=(r, world, port, ga, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, fixed_ok, every_ok in res:
+        assert fixed_ok, "sync-on-last-micro-step schedule does not give the mean gradient"
+        assert not every_ok, "the per-micro-step all-reduce should over-weight earlier micro-steps"

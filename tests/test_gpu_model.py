@@ -156,6 +156,30 @@ def test_config1_loss_and_grads_match_oracle(ora, ckpt):
     m.close()
 
 
+# Headline widths at depths the oracle finishes in seconds: the paths config 1 never reaches
+# (V = 50257 with the padded LM-head stride, 2048- and 16384-row pair tiles, split-K weight
+# gradients over thousands of tokens, the one-group CE ring for 100 KB rows, d_head 128
+# attention inside the model).
+HEADLINE = {
+    "gpt2-small-widths": (dict(V=50257, T=1024, D=768, H=12, L=2, FF=3072), 2, 1024),
+    "1.3b-layer": (dict(V=50257, T=2048, D=2048, H=16, L=1, FF=8192), 1, 2048),
+}
+
+
+@pytest.mark.parametrize("which", sorted(HEADLINE))
+def test_headline_widths_match_oracle(ora, which):
+    """GPT-2-small widths (L2, B2 x 1024) and one 1.3B layer (D2048 H16 dh128 FF8192, 1 x 2048):
+    one fwd+bwd, loss within 1e-3 and every tensor's gradient within 2e-2 of the FP32 oracle."""
+    cfg, B, S = HEADLINE[which]
+    ora.set_threads()
+    m, params, tok, tgt = _setup(ora, cfg, B, S, seed=3)
+    loss, el, errs = _grad_errors(ora, cfg, m, params, tok, tgt, B, S)
+    m.close()
+    assert abs(loss - el) <= LOSS_TOL * abs(el), (loss, el)
+    bad = {k: v for k, v in errs.items() if v > GRAD_TOL}
+    assert not bad, bad
+
+
 def test_config1_full_step_matches_oracle(ora):
     """fwd + bwd + fused Adam tail (lr 3e-4): post-step masters vs the oracle's."""
     B, S = 8, 128

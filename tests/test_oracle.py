@@ -176,3 +176,32 @@ def test_adam_tail_skip_and_unscale(ora):
                            1e-3, 0.9, 0.999, 1e-8, 0.0, 1)
     assert ora.adam_tail(p, g.copy(), m, v, [0], [n], 1e-3, 0.9, 0.999, 1e-8, 0.0, 1, s) == 0
     np.testing.assert_allclose(p, pe, rtol=1e-6, atol=1e-7)
+
+
+def test_reference_timed_entry_points_run():
+    """The CPU baseline's timed calls into the reference's own engine (oracle/_ref) run and
+    report a positive duration at small sizes; its forward agrees with the untimed wrapper."""
+    import ctypes as C
+
+    import oracle
+    ref = oracle.ref_lib()
+    if ref is None:
+        pytest.skip("oracle/_ref/libref.so not built (reference sources absent)")
+    F = lambda a: a.ctypes.data_as(C.POINTER(C.c_float))   # noqa: E731
+    I = lambda a: a.ctypes.data_as(C.POINTER(C.c_int))     # noqa: E731
+    rng = np.random.default_rng(0)
+    N, D = 64, 128
+    x = rng.standard_normal((N, D), dtype=np.float32)
+    dy = rng.standard_normal((N, D), dtype=np.float32)
+    g = np.ones(D, np.float32)
+    mean = x.mean(1).astype(np.float32)
+    rstd = (1 / np.sqrt(x.var(1) + 1e-5)).astype(np.float32)
+    assert ref.ref_time_layer_norm_backward(F(dy), F(x), F(g), F(mean), F(rstd), N, D) > 0
+    y = rng.random((N, D), dtype=np.float32)
+    assert ref.ref_time_softmax_backward(F(dy), F(y), N, D) > 0
+    tg = rng.integers(0, D, N).astype(np.int32)
+    assert ref.ref_time_cross_entropy_backward(F(x), I(tg), N, D) > 0
+    n = 4096
+    p = rng.standard_normal(n, dtype=np.float32)
+    assert ref.ref_time_adamw_step(F(p), F(p), n, C.c_float(1e-3), C.c_float(0.9), C.c_float(0.999),
+                                   C.c_float(1e-8), C.c_float(0.0)) > 0
