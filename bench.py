@@ -369,26 +369,34 @@ def r8(x):
     return (x + 7) // 8 * 8
 
 
-def gemm_shapes(N=16384, D=768, F=3072, V=50257):
+def gemm_shapes(N=16384, D=768, F=3072, V=50257, prefix="gemm"):
     """The GEMMs of one GPT-2-small layer step and the LM head, as the model issues them:
     name -> (M, N, K, a_major, b_major, epilogue, extra) with extra in {"", "bias", "res", "dbias"}."""
-    return {
-        "gemm_fwd_qkv": (N, 3 * D, D, 0, 0, 0, "bias"),
-        "gemm_fwd_wo": (N, D, D, 0, 0, 0, "res"),
-        "gemm_fwd_w1": (N, F, D, 0, 0, 1, "bias"),
-        "gemm_fwd_w2": (N, D, F, 0, 0, 0, "res"),
-        "gemm_lm_fwd": (N, V, D, 0, 0, 0, "bias"),
-        "gemm_dgrad_lm": (N, D, V, 0, 1, 0, ""),
-        "gemm_wgrad_lm": (V, D, N, 1, 1, 3, "dbias"),
-        "gemm_wgrad_w2": (D, F, N, 1, 1, 3, ""),
-        "gemm_dgrad_w2": (N, F, D, 0, 1, 2, ""),
-        "gemm_wgrad_w1": (F, D, N, 1, 1, 3, "dbias"),
-        "gemm_dgrad_w1": (N, D, F, 0, 1, 0, ""),
-        "gemm_wgrad_wo": (D, D, N, 1, 1, 3, ""),
-        "gemm_dgrad_wo": (N, D, D, 0, 1, 0, ""),
-        "gemm_wgrad_qkv": (3 * D, D, N, 1, 1, 3, ""),
-        "gemm_dgrad_qkv": (N, D, 3 * D, 0, 1, 0, ""),
+    s = {
+        "fwd_qkv": (N, 3 * D, D, 0, 0, 0, "bias"),
+        "fwd_wo": (N, D, D, 0, 0, 0, "res"),
+        "fwd_w1": (N, F, D, 0, 0, 1, "bias"),
+        "fwd_w2": (N, D, F, 0, 0, 0, "res"),
+        "lm_fwd": (N, V, D, 0, 0, 0, "bias"),
+        "dgrad_lm": (N, D, V, 0, 1, 0, ""),
+        "wgrad_lm": (V, D, N, 1, 1, 3, "dbias"),
+        "wgrad_w2": (D, F, N, 1, 1, 3, ""),
+        "dgrad_w2": (N, F, D, 0, 1, 2, ""),
+        "wgrad_w1": (F, D, N, 1, 1, 3, "dbias"),
+        "dgrad_w1": (N, D, F, 0, 1, 0, ""),
+        "wgrad_wo": (D, D, N, 1, 1, 3, ""),
+        "dgrad_wo": (N, D, D, 0, 1, 0, ""),
+        "wgrad_qkv": (3 * D, D, N, 1, 1, 3, ""),
+        "dgrad_qkv": (N, D, 3 * D, 0, 1, 0, ""),
     }
+    return {f"{prefix}_{k}": v for k, v in s.items()}
+
+
+def all_gemm_shapes():
+    """GPT-2-small shapes as gemm_*, the 1.3B decoder's (N = 8 x 2048, D 2048, FF 8192) as gemm13_*."""
+    out = gemm_shapes()
+    out.update(gemm_shapes(16384, 2048, 8192, 50257, prefix="gemm13"))
+    return out
 
 
 def kernel_loop(name, reps, torch, ops):
@@ -399,7 +407,7 @@ def kernel_loop(name, reps, torch, ops):
     hbm, tc, tcs, _ = peaks()
     N, D, F, V = 16384, 768, 3072, 50257
     if name.startswith("gemm"):
-        shapes = gemm_shapes(N, D, F, V)
+        shapes = all_gemm_shapes()
         if name not in shapes:
             raise SystemExit(f"unknown GEMM {name}: one of {sorted(shapes)}")
         M, Nn, K, am, bm, epi, extra = shapes[name]
@@ -530,8 +538,10 @@ def check_dp(model, tokens, targets, B, S, world, dist, torch):
     model.grad.zero_()
     del local
     torch.cuda.synchronize()
+    # tolerance: two backwards of the same inputs differ by FP32 accumulation-order noise that FP16
+    # roundings carry forward (measured ~2e-4); the schedule error this guards against is O(1)
     return {"ga": 2, "ranks_bitwise_equal": agree, "checksum": int(allcs[0][0]), "finite": finite,
-            "rel_l2_vs_allreduce_of_local_sums": rel, "ok": agree and finite and rel < 1e-4,
+            "rel_l2_vs_allreduce_of_local_sums": rel, "tolerance": 2e-3, "ok": agree and finite and rel < 2e-3,
             "how": "grad after 2 micro-steps (the 1st without all-reduce) vs an independent all-reduce "
                    "of each rank's 2-micro-step local sum; bit checksums gathered from every rank"}
 

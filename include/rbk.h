@@ -436,8 +436,31 @@ int rbk_model_inject_inf(rbk_model* m, int64_t offset, int64_t stride);
 int rbk_dp_plan(const rbk_config* cfg, int64_t bucket_bytes, int64_t* out, int max, int* count);
 /* Fill a 128-byte NCCL unique id on the root rank (ncclGetUniqueId). */
 int rbk_dp_unique_id(void* id128);
-/* Join the communicator; bucket_bytes (25 MB) sets the all-reduce granularity. */
+/* Join the communicator; bucket_bytes (25 MB) sets the all-reduce granularity.
+ * Defaults of rbk_model_dp_init_ex, overridable through the environment:
+ * RBK_NCCL_MAX_CTAS (0), RBK_NCCL_TIMEOUT_S (300). */
 int rbk_model_dp_init(rbk_model* m, const void* id128, int rank, int world, int64_t bucket_bytes);
+typedef struct rbk_dp_opts {
+    int64_t bucket_bytes;   /* all-reduce granularity (25 MB)                            */
+    int max_ctas;           /* NCCL CTA cap for the buckets that overlap the backward, so
+                               NCCL leaves SMs to the GEMM grids (0: NCCL's default); the
+                               last bucket, reduced after the backward, is not capped  */
+    double timeout_s;       /* watchdog deadline per collective (<= 0: 300 s)            */
+} rbk_dp_opts;
+/* rbk_model_dp_init with explicit options.  The communicators are non-blocking
+ * (ncclCommInitRankConfig, blocking = 0) and watched by a host thread: a
+ * collective still incomplete after timeout_s (a peer that left, a hung link)
+ * or an asynchronous NCCL error aborts them (ncclCommAbort, which ends NCCL
+ * kernels waiting on a peer).  From then on rbk_model_dp_status, backward and
+ * the optimizer steps return RBK_ERR_TIMEOUT / RBK_ERR_NCCL (nothing is
+ * applied); the model must be shut down (rbk_model_dp_shutdown) and rebuilt. */
+int rbk_model_dp_init_ex(rbk_model* m, const void* id128, int rank, int world, const rbk_dp_opts* o);
+/* RBK_OK, or the status that made the watchdog abort the communicators. */
+int rbk_model_dp_status(rbk_model* m);
+/* Abort this rank's communicators now (local, not collective): a rank that
+ * leaves the job calls it instead of a shutdown its peers would have to join;
+ * afterwards the model behaves as after a watchdog abort (RBK_ERR_NCCL). */
+int rbk_model_dp_abort(rbk_model* m);
 /* Gradient accumulation under data parallelism (the reference accumulates GA
  * micro-steps per optimizer step, src/main.cpp:136-164).  sync = 0: following
  * backwards only accumulate this rank's gradients, no all-reduce; sync = 1

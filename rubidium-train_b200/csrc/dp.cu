@@ -1,0 +1,351 @@
+// dp.cu — data parallelism for the training step: one process per GPU, the
+// gradient arena all-reduced (sum) over NCCL in buckets that are launched on a
+// high-priority communication stream as soon as the backward has finished
+// their layers, so the exchange overlaps the rest of the backward.  The
+// reference is single-GPU (src/main.cpp:54); this has no counterpart there.
+//
+// Communicators are created non-blocking (ncclCommInitRankConfig with
+// blocking = 0) and watched: a host thread checks every enqueued collective
+// against a deadline and polls ncclCommGetAsyncError; on a timeout (a peer that
+// left, a hung link) or an asynchronous NCCL error it aborts the communicators
+// (ncclCommAbort ends NCCL kernels still waiting on a peer), and every later
+// call on the model returns RBK_ERR_TIMEOUT / RBK_ERR_NCCL instead of hanging.
+//
+// Two communicators share the ranks: the buckets that overlap the backward use
+// one whose CTA count is capped (NCCL's CTAs otherwise take SMs from the
+// persistent tcgen05 GEMM grids), the last bucket — the embeddings, reduced
+// after the backward has ended, with nothing left to overlap — uses one
+// without the cap.
+#include <chrono>
+#include <cstring>
+#include <deque>
+#include <mutex>
+#include <thread>
+
+#include "model.h"
+
+namespace rbk {
+
+using Clock = std::chrono::steady_clock;
+
+struct DpWatch {
+    std::thread th;
+    std::mutex mu;
+    bool stop = false;
+    int device = 0;
+    double timeout_s = 300.0;
+    int failed = RBK_OK;                       // guarded by mu
+    ncclComm_t comms[2] = {nullptr, nullptr};  // guarded by mu; nulled after an abort
+    std::deque<std::pair<cudaEvent_t, Clock::time_point>> pending;
+    std::vector<cudaEvent_t> spare;
+    std::vector<cudaEvent_t> all;
+
+    // Under mu: abort both communicators (NCCL kernels waiting on a peer exit).
+    void abort_locked(int why) {
+        if (failed == RBK_OK) failed = why;
+        if (comms[1] && comms[1] != comms[0]) ncclCommAbort(comms[1]);
+        if (comms[0]) ncclCommAbort(comms[0]);
+        comms[0] = comms[1] = nullptr;
+    }
+
+    void loop() {
+        cudaSetDevice(device);
+        while (true) {
+            {
+                std::lock_guard<std::mutex> lk(mu);
+                if (stop) return;
+                if (failed == RBK_OK) {
+                    const auto now = Clock::now();
+                    while (!pending.empty()) {
+                        const cudaError_t q = cudaEventQuery(pending.front().first);
+                        if (q == cudaSuccess) {
+                            spare.push_back(pending.front().first);
+                            pending.pop_front();
+                            continue;
+                        }
+                        if (q != cudaErrorNotReady) {           // a sticky CUDA error: stop waiting on it
+                            abort_locked(RBK_ERR_CUDA);
+                            break;
+                        }
+                        const double waited = std::chrono::duration<double>(now - pending.front().second).count();
+                        if (waited > timeout_s) abort_locked(RBK_ERR_TIMEOUT);
+                        break;
+                    }
+                    for (int i = 0; i < 2 && failed == RBK_OK; ++i) {
+                        if (!comms[i]) continue;
+                        ncclResult_t ae = ncclSuccess;
+                        if (ncclCommGetAsyncError(comms[i], &ae) != ncclSuccess ||
+                            (ae != ncclSuccess && ae != ncclInProgress))
+                            abort_locked(RBK_ERR_NCCL);
+                    }
+                }
+            }
+            std::this_thread::sleep_for(std::chrono::milliseconds(20));
+        }
+    }
+};
+
+namespace {
+
+double env_double(const char* name, double dflt) {
+    const char* e = getenv(name);
+    return e && *e ? atof(e) : dflt;
+}
+
+// Wait (host) until a non-blocking communicator has finished its pending work.
+ncclResult_t settle(ncclComm_t c, double timeout_s) {
+    const auto t0 = Clock::now();
+    ncclResult_t st = ncclInProgress;
+    while (true) {
+        if (ncclCommGetAsyncError(c, &st) != ncclSuccess) return ncclInternalError;
+        if (st != ncclInProgress) return st;
+        if (std::chrono::duration<double>(Clock::now() - t0).count() > timeout_s) return ncclInProgress;
+        std::this_thread::sleep_for(std::chrono::microseconds(200));
+    }
+}
+
+// Units in backward order: 0 = ln_f + lm head (end of the arena), 1..L =
+// layers L-1..0, L+1 = embeddings (start of the arena).  Each unit's range is
+// contiguous.
+void unit_range(const std::vector<rbk_tensor>& tab, int64_t n, const rbk_config* c, int u, int64_t* b, int64_t* e) {
+    const int L = c->L;
+    if (u == 0) { *b = tab[rbk_tail_tensor(c, 0)].offset; *e = n; return; }
+    if (u == L + 1) { *b = 0; *e = tab[rbk_layer_tensor(0, 0)].offset; return; }
+    const int l = L - u;
+    *b = tab[rbk_layer_tensor(l, 0)].offset;
+    *e = (l + 1 < L) ? tab[rbk_layer_tensor(l + 1, 0)].offset : tab[rbk_tail_tensor(c, 0)].offset;
+}
+
+// Enqueue one all-reduce on the communication stream and register it with the watchdog.
+int allreduce(rbk_model* m, float* buf, size_t n, bool tail) {
+    DpState& d = m->dp;
+    DpWatch& w = *d.watch;
+    std::lock_guard<std::mutex> lk(w.mu);
+    if (w.failed != RBK_OK) {
+        set_error("data parallel: the communicator was aborted (%s)",
+                  w.failed == RBK_ERR_TIMEOUT ? "a collective timed out" : "an NCCL / CUDA error");
+        return w.failed;
+    }
+    ncclComm_t c = w.comms[tail ? 1 : 0];
+    ncclResult_t r = ncclAllReduce(buf, buf, n, ncclFloat32, ncclSum, c, d.stream);
+    if (r == ncclInProgress) r = settle(c, w.timeout_s);
+    if (r != ncclSuccess) {
+        set_error("ncclAllReduce failed: %s", ncclGetErrorString(r));
+        w.abort_locked(r == ncclInProgress ? RBK_ERR_TIMEOUT : RBK_ERR_NCCL);
+        return w.failed;
+    }
+    cudaEvent_t ev;
+    if (!w.spare.empty()) {
+        ev = w.spare.back();
+        w.spare.pop_back();
+    } else {
+        RBK_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+        w.all.push_back(ev);
+    }
+    RBK_CUDA(cudaEventRecord(ev, d.stream));
+    w.pending.emplace_back(ev, Clock::now());
+    return RBK_OK;
+}
+
+}  // namespace
+
+// Bucket plan: walk the units in backward order, growing a pending range
+// downwards through the arena, and close a bucket once it holds at least
+// bucket_elems (the embeddings unit always closes the last one).  Pure host
+// code: identical on every rank for the same configuration.
+std::vector<DpBucket> dp_plan(const rbk_config* c, int64_t bucket_elems) {
+    std::vector<rbk_tensor> tab(rbk_num_tensors(c));
+    const int64_t n = rbk_param_table(c, tab.data());
+    std::vector<DpBucket> out;
+    int64_t pend_end = n;
+    for (int u = 0; u <= c->L + 1; ++u) {
+        int64_t b, e;
+        unit_range(tab, n, c, u, &b, &e);
+        if (pend_end - b >= bucket_elems || u == c->L + 1) {
+            out.push_back(DpBucket{u, b, pend_end});
+            pend_end = b;
+        }
+    }
+    return out;
+}
+
+// Called by the backward after unit u's gradients are final on stream st.
+int dp_unit_done(rbk_model* m, int u, cudaStream_t st) {
+    DpState& d = m->dp;
+    for (const DpBucket& bk : d.plan) {
+        if (bk.unit != u) continue;
+        RBK_CUDA(cudaEventRecord(d.layer_done[u], st));
+        RBK_CUDA(cudaStreamWaitEvent(d.stream, d.layer_done[u], 0));
+        RBK_TRY(allreduce(m, m->grad + bk.begin, (size_t)(bk.end - bk.begin), u == m->cfg.L + 1));
+    }
+    if (u == m->cfg.L + 1) {
+        RBK_CUDA(cudaEventRecord(d.all_done, d.stream));
+        RBK_CUDA(cudaStreamWaitEvent(st, d.all_done, 0));
+    }
+    return RBK_OK;
+}
+
+// One all-reduce of a whole gradient buffer, ordered after the work on st so far, with st
+// waiting for it (the LoRA adapter arena).
+int dp_reduce_all(rbk_model* m, float* buf, int64_t n, cudaStream_t st) {
+    DpState& d = m->dp;
+    RBK_CUDA(cudaEventRecord(d.layer_done[0], st));
+    RBK_CUDA(cudaStreamWaitEvent(d.stream, d.layer_done[0], 0));
+    RBK_TRY(allreduce(m, buf, (size_t)n, true));
+    RBK_CUDA(cudaEventRecord(d.all_done, d.stream));
+    RBK_CUDA(cudaStreamWaitEvent(st, d.all_done, 0));
+    return RBK_OK;
+}
+
+int dp_status(rbk_model* m) {
+    if (!m->dp.on || !m->dp.watch) return RBK_OK;
+    std::lock_guard<std::mutex> lk(m->dp.watch->mu);
+    return m->dp.watch->failed;
+}
+
+}  // namespace rbk
+
+using namespace rbk;
+
+extern "C" {
+
+int rbk_dp_plan(const rbk_config* cfg, int64_t bucket_bytes, int64_t* out, int max, int* count) {
+    RBK_REQUIRE(cfg && count && rbk_config_check(cfg) == 0 && bucket_bytes > 0, "rbk_dp_plan: bad arguments");
+    const std::vector<DpBucket> p = dp_plan(cfg, std::max<int64_t>(bucket_bytes / 4, 1));
+    *count = (int)p.size();
+    for (int i = 0; i < (int)p.size() && i < max && out; ++i) {
+        out[3 * i] = p[i].unit;
+        out[3 * i + 1] = p[i].begin;
+        out[3 * i + 2] = p[i].end;
+    }
+    return RBK_OK;
+}
+
+int rbk_dp_unique_id(void* id128) {
+    RBK_REQUIRE(id128, "rbk_dp_unique_id: null pointer");
+    static_assert(sizeof(ncclUniqueId) == RBK_NCCL_ID_BYTES, "NCCL unique id size");
+    ncclResult_t r = ncclGetUniqueId(reinterpret_cast<ncclUniqueId*>(id128));
+    if (r != ncclSuccess) {
+        set_error("ncclGetUniqueId failed: %s", ncclGetErrorString(r));
+        return RBK_ERR_NCCL;
+    }
+    return RBK_OK;
+}
+
+int rbk_model_dp_init_ex(rbk_model* m, const void* id128, int rank, int world, const rbk_dp_opts* o) {
+    RBK_REQUIRE(m && id128 && o && world >= 1 && rank >= 0 && rank < world && o->bucket_bytes > 0,
+                "rbk_model_dp_init_ex: bad arguments");
+    RBK_REQUIRE(!m->dp.on, "rbk_model_dp_init_ex: already initialised");
+    RBK_CUDA(cudaSetDevice(m->ctx->device));
+    const double timeout_s = o->timeout_s > 0 ? o->timeout_s : 300.0;
+    ncclUniqueId id;
+    std::memcpy(&id, id128, sizeof(id));
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    ncclComm_t comm = nullptr, tail = nullptr;
+    ncclResult_t r = ncclCommInitRankConfig(&comm, world, id, rank, &cfg);
+    if (r == ncclInProgress || r == ncclSuccess) r = settle(comm, timeout_s);
+    if (r != ncclSuccess) {
+        set_error("ncclCommInitRankConfig failed: %s", r == ncclInProgress ? "timed out" : ncclGetErrorString(r));
+        if (comm) ncclCommAbort(comm);
+        return r == ncclInProgress ? RBK_ERR_TIMEOUT : RBK_ERR_NCCL;
+    }
+    if (o->max_ctas > 0) {
+        // the capped communicator for the overlapped buckets; `comm` (uncapped) keeps the tail
+        ncclConfig_t capped = NCCL_CONFIG_INITIALIZER;
+        capped.blocking = 0;
+        capped.maxCTAs = o->max_ctas;
+        capped.minCTAs = 1;
+        ncclComm_t c2 = nullptr;
+        r = ncclCommSplit(comm, 0, rank, &c2, &capped);
+        if (r == ncclInProgress || r == ncclSuccess) r = settle(comm, timeout_s);
+        if (r == ncclSuccess && c2) r = settle(c2, timeout_s);
+        if (r != ncclSuccess || !c2) {
+            set_error("ncclCommSplit (capped communicator) failed: %s",
+                      r == ncclInProgress ? "timed out" : ncclGetErrorString(r));
+            if (c2) ncclCommAbort(c2);
+            ncclCommAbort(comm);
+            return r == ncclInProgress ? RBK_ERR_TIMEOUT : RBK_ERR_NCCL;
+        }
+        tail = comm;
+        comm = c2;
+    } else {
+        tail = comm;
+    }
+    DpState& d = m->dp;
+    int lo = 0, hi = 0;
+    RBK_CUDA(cudaDeviceGetStreamPriorityRange(&lo, &hi));
+    RBK_CUDA(cudaStreamCreateWithPriority(&d.stream, cudaStreamNonBlocking, hi));
+    d.layer_done.resize(m->cfg.L + 2);
+    for (auto& e : d.layer_done) RBK_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    RBK_CUDA(cudaEventCreateWithFlags(&d.all_done, cudaEventDisableTiming));
+    d.bucket_elems = std::max<int64_t>(o->bucket_bytes / 4, 1);
+    d.plan = dp_plan(&m->lay, d.bucket_elems);
+    d.rank = rank;
+    d.world = world;
+    d.max_ctas = o->max_ctas;
+    d.watch = new DpWatch();
+    d.watch->device = m->ctx->device;
+    d.watch->timeout_s = timeout_s;
+    d.watch->comms[0] = comm;
+    d.watch->comms[1] = tail;
+    d.watch->th = std::thread([w = d.watch] { w->loop(); });
+    d.on = true;
+    return RBK_OK;
+}
+
+int rbk_model_dp_init(rbk_model* m, const void* id128, int rank, int world, int64_t bucket_bytes) {
+    rbk_dp_opts o = {};
+    o.bucket_bytes = bucket_bytes;
+    o.max_ctas = (int)env_double("RBK_NCCL_MAX_CTAS", 0.0);
+    o.timeout_s = env_double("RBK_NCCL_TIMEOUT_S", 300.0);
+    return rbk_model_dp_init_ex(m, id128, rank, world, &o);
+}
+
+int rbk_model_dp_set_sync(rbk_model* m, int sync) {
+    RBK_REQUIRE(m, "rbk_model_dp_set_sync: null model");
+    m->dp.sync = sync != 0;
+    return RBK_OK;
+}
+
+int rbk_model_dp_status(rbk_model* m) {
+    RBK_REQUIRE(m, "rbk_model_dp_status: null model");
+    const int s = dp_status(m);
+    if (s != RBK_OK) set_error("data parallel: the communicator was aborted (%s)",
+                               s == RBK_ERR_TIMEOUT ? "a collective timed out" : "an NCCL / CUDA error");
+    return s;
+}
+
+int rbk_model_dp_abort(rbk_model* m) {
+    RBK_REQUIRE(m, "rbk_model_dp_abort: null model");
+    if (!m->dp.on || !m->dp.watch) return RBK_OK;
+    std::lock_guard<std::mutex> lk(m->dp.watch->mu);
+    m->dp.watch->abort_locked(RBK_ERR_NCCL);
+    return RBK_OK;
+}
+
+int rbk_model_dp_shutdown(rbk_model* m) {
+    RBK_REQUIRE(m, "rbk_model_dp_shutdown: null model");
+    DpState& d = m->dp;
+    if (!d.on) return RBK_OK;
+    DpWatch* w = d.watch;
+    // Wait for the collectives in flight; the watchdog keeps running meanwhile, so a hung one
+    // is aborted after the timeout and this returns.
+    cudaStreamSynchronize(d.stream);
+    {
+        std::lock_guard<std::mutex> lk(w->mu);
+        w->stop = true;
+    }
+    w->th.join();
+    if (w->comms[1] && w->comms[1] != w->comms[0]) ncclCommDestroy(w->comms[1]);
+    if (w->comms[0]) ncclCommDestroy(w->comms[0]);
+    for (cudaEvent_t e : w->all) cudaEventDestroy(e);
+    delete w;
+    for (auto& e : d.layer_done) cudaEventDestroy(e);
+    cudaEventDestroy(d.all_done);
+    cudaStreamDestroy(d.stream);
+    d = DpState();
+    return RBK_OK;
+}
+
+}  // extern "C"

@@ -276,9 +276,6 @@ static int forward(rbk_model* m, const int* tokens, const int* targets, int B, i
     return RBK_OK;
 }
 
-// ------------------------------------------------------------ data parallel --
-static int dp_unit_done(rbk_model* m, int unit, cudaStream_t st);
-static int dp_reduce_all(rbk_model* m, float* buf, int64_t n, cudaStream_t st);
 
 // ------------------------------------------------------------- backward ----
 static int backward(rbk_model* m, const int* tokens, const int* targets, int B, int S, float grad_scale,
@@ -400,80 +397,6 @@ static int backward(rbk_model* m, const int* tokens, const int* targets, int B, 
     if (base) RBK_TRY(rbk_embed_bwd(m->ctx, m->w.g_token_emb, m->w.g_pos_emb, gcur, tokens, B, S, D, V, st));
     if (reduce) RBK_TRY(dp_unit_done(m, L + 1, st));
     if (reduce_lora) RBK_TRY(dp_reduce_all(m, m->lora.grad, m->lora.n, st));
-    return RBK_OK;
-}
-
-// --------------------------------------------------------- data parallel ----
-// Units in backward order: 0 = ln_f + lm head (end of the arena), 1..L =
-// layers L-1..0, L+1 = embeddings (start of the arena).  Each unit's range is
-// contiguous; consecutive units are grouped into buckets of >= bucket_elems
-// and all-reduced on the communication stream as soon as the last unit of the
-// bucket has its gradients final.
-static void unit_range(rbk_model* m, int u, int64_t* b, int64_t* e) {
-    const int L = m->cfg.L;
-    if (u == 0) { *b = m->tab[rbk_tail_tensor(&m->lay, 0)].offset; *e = m->n; return; }
-    if (u == L + 1) { *b = 0; *e = m->tab[rbk_layer_tensor(0, 0)].offset; return; }
-    const int l = L - u;
-    *b = m->tab[rbk_layer_tensor(l, 0)].offset;
-    *e = (l + 1 < L) ? m->tab[rbk_layer_tensor(l + 1, 0)].offset : m->tab[rbk_tail_tensor(&m->lay, 0)].offset;
-}
-
-// Bucket plan: walk the units in backward order, growing a pending range
-// downwards through the arena, and close a bucket once it holds at least
-// bucket_elems (the embeddings unit always closes the last one).  Pure host
-// code: identical on every rank for the same configuration.
-std::vector<DpBucket> dp_plan(const rbk_config* c, int64_t bucket_elems) {
-    rbk_model tmp;
-    tmp.lay = *c;
-    tmp.cfg.L = c->L;
-    tmp.tab.resize(rbk_num_tensors(c));
-    tmp.n = rbk_param_table(c, tmp.tab.data());
-    std::vector<DpBucket> out;
-    int64_t pend_end = tmp.n;
-    for (int u = 0; u <= c->L + 1; ++u) {
-        int64_t b, e;
-        unit_range(&tmp, u, &b, &e);
-        if (pend_end - b >= bucket_elems || u == c->L + 1) {
-            out.push_back(DpBucket{u, b, pend_end});
-            pend_end = b;
-        }
-    }
-    return out;
-}
-
-static int dp_unit_done(rbk_model* m, int u, cudaStream_t st) {
-    DpState& d = m->dp;
-    for (const DpBucket& bk : d.plan) {
-        if (bk.unit != u) continue;
-        RBK_CUDA(cudaEventRecord(d.layer_done[u], st));
-        RBK_CUDA(cudaStreamWaitEvent(d.stream, d.layer_done[u], 0));
-        ncclResult_t r = ncclAllReduce(m->grad + bk.begin, m->grad + bk.begin, (size_t)(bk.end - bk.begin),
-                                       ncclFloat32, ncclSum, d.comm, d.stream);
-        if (r != ncclSuccess) {
-            set_error("ncclAllReduce failed: %s", ncclGetErrorString(r));
-            return RBK_ERR_NCCL;
-        }
-    }
-    if (u == m->cfg.L + 1) {
-        RBK_CUDA(cudaEventRecord(d.all_done, d.stream));
-        RBK_CUDA(cudaStreamWaitEvent(st, d.all_done, 0));
-    }
-    return RBK_OK;
-}
-
-// One all-reduce of a whole gradient buffer on the communication stream, ordered after the work
-// on `st` so far, with `st` waiting for it (the LoRA adapter arena).
-static int dp_reduce_all(rbk_model* m, float* buf, int64_t n, cudaStream_t st) {
-    DpState& d = m->dp;
-    RBK_CUDA(cudaEventRecord(d.layer_done[0], st));
-    RBK_CUDA(cudaStreamWaitEvent(d.stream, d.layer_done[0], 0));
-    ncclResult_t r = ncclAllReduce(buf, buf, (size_t)n, ncclFloat32, ncclSum, d.comm, d.stream);
-    if (r != ncclSuccess) {
-        set_error("ncclAllReduce failed: %s", ncclGetErrorString(r));
-        return RBK_ERR_NCCL;
-    }
-    RBK_CUDA(cudaEventRecord(d.all_done, d.stream));
-    RBK_CUDA(cudaStreamWaitEvent(st, d.all_done, 0));
     return RBK_OK;
 }
 
@@ -617,6 +540,7 @@ int rbk_model_forward(rbk_model* m, const int* tokens, const int* targets, int B
 int rbk_model_backward(rbk_model* m, const int* tokens, const int* targets, int B, int S, float grad_scale,
                        void* stream) {
     RBK_REQUIRE(m && tokens && targets, "rbk_model_backward: null pointer");
+    if (m->dp.on) RBK_TRY(rbk_model_dp_status(m));   // an aborted communicator fails fast
     RBK_REQUIRE(B > 0 && B <= m->opts.max_batch && S > 0 && S <= m->opts.max_seq && S % 64 == 0,
                 "rbk_model_backward: bad B/S");
     return backward(m, tokens, targets, B, S, grad_scale, as_stream(stream));
@@ -625,6 +549,7 @@ int rbk_model_backward(rbk_model* m, const int* tokens, const int* targets, int 
 int rbk_model_optimizer_step(rbk_model* m, int t, float lr, float b1, float b2, float eps, float wd, float max_norm,
                              void* stream) {
     RBK_REQUIRE(m, "rbk_model_optimizer_step: null model");
+    if (m->dp.on) RBK_TRY(rbk_model_dp_status(m));   // never apply a partially reduced gradient
     rbk_tail_args a = {};
     a.p32 = m->p32; a.g = m->grad; a.m = m->m; a.v = m->v; a.p16 = m->p16; a.n = m->n;
     a.seg_off = m->seg_off.data(); a.seg_len = m->seg_len.data(); a.nseg = (int)m->seg_off.size();
@@ -681,6 +606,7 @@ int rbk_model_lora_buffer(rbk_model* m, int which, void** ptr, int64_t* n) {
 
 int rbk_model_lora_step(rbk_model* m, int t, float lr, float b1, float b2, float eps, float wd, void* stream) {
     RBK_REQUIRE(m && m->lora.rank > 0, "rbk_model_lora_step: LoRA not enabled");
+    if (m->dp.on) RBK_TRY(rbk_model_dp_status(m));
     rbk_tail_args a = {};
     a.p32 = m->lora.p32; a.g = m->lora.grad; a.m = m->lora.m; a.v = m->lora.v; a.p16 = m->lora.p16;
     a.n = m->lora.n;
@@ -701,72 +627,6 @@ int rbk_model_inject_inf(rbk_model* m, int64_t offset, int64_t stride) {
     m->inject_offset = offset;
     m->inject_stride = stride;
     m->inject_pending = stride > 0;
-    return RBK_OK;
-}
-
-int rbk_dp_plan(const rbk_config* cfg, int64_t bucket_bytes, int64_t* out, int max, int* count) {
-    RBK_REQUIRE(cfg && count && rbk_config_check(cfg) == 0 && bucket_bytes > 0, "rbk_dp_plan: bad arguments");
-    const std::vector<DpBucket> p = dp_plan(cfg, std::max<int64_t>(bucket_bytes / 4, 1));
-    *count = (int)p.size();
-    for (int i = 0; i < (int)p.size() && i < max && out; ++i) {
-        out[3 * i] = p[i].unit;
-        out[3 * i + 1] = p[i].begin;
-        out[3 * i + 2] = p[i].end;
-    }
-    return RBK_OK;
-}
-
-int rbk_dp_unique_id(void* id128) {
-    RBK_REQUIRE(id128, "rbk_dp_unique_id: null pointer");
-    static_assert(sizeof(ncclUniqueId) == RBK_NCCL_ID_BYTES, "NCCL unique id size");
-    ncclResult_t r = ncclGetUniqueId(reinterpret_cast<ncclUniqueId*>(id128));
-    if (r != ncclSuccess) {
-        set_error("ncclGetUniqueId failed: %s", ncclGetErrorString(r));
-        return RBK_ERR_NCCL;
-    }
-    return RBK_OK;
-}
-
-int rbk_model_dp_init(rbk_model* m, const void* id128, int rank, int world, int64_t bucket_bytes) {
-    RBK_REQUIRE(m && id128 && world >= 1 && rank >= 0 && rank < world, "rbk_model_dp_init: bad arguments");
-    RBK_REQUIRE(!m->dp.on, "rbk_model_dp_init: already initialised");
-    cudaSetDevice(m->ctx->device);
-    ncclUniqueId id;
-    std::memcpy(&id, id128, sizeof(id));
-    ncclResult_t r = ncclCommInitRank(&m->dp.comm, world, id, rank);
-    if (r != ncclSuccess) {
-        set_error("ncclCommInitRank failed: %s", ncclGetErrorString(r));
-        return RBK_ERR_NCCL;
-    }
-    int lo = 0, hi = 0;
-    RBK_CUDA(cudaDeviceGetStreamPriorityRange(&lo, &hi));
-    RBK_CUDA(cudaStreamCreateWithPriority(&m->dp.stream, cudaStreamNonBlocking, hi));
-    m->dp.layer_done.resize(m->cfg.L + 2);
-    for (auto& e : m->dp.layer_done) RBK_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
-    RBK_CUDA(cudaEventCreateWithFlags(&m->dp.all_done, cudaEventDisableTiming));
-    m->dp.bucket_elems = std::max<int64_t>(bucket_bytes / 4, 1);
-    m->dp.plan = dp_plan(&m->lay, m->dp.bucket_elems);
-    m->dp.rank = rank;
-    m->dp.world = world;
-    m->dp.on = true;
-    return RBK_OK;
-}
-
-int rbk_model_dp_set_sync(rbk_model* m, int sync) {
-    RBK_REQUIRE(m, "rbk_model_dp_set_sync: null model");
-    m->dp.sync = sync != 0;
-    return RBK_OK;
-}
-
-int rbk_model_dp_shutdown(rbk_model* m) {
-    RBK_REQUIRE(m, "rbk_model_dp_shutdown: null model");
-    if (!m->dp.on) return RBK_OK;
-    cudaStreamSynchronize(m->dp.stream);
-    ncclCommDestroy(m->dp.comm);
-    for (auto& e : m->dp.layer_done) cudaEventDestroy(e);
-    cudaEventDestroy(m->dp.all_done);
-    cudaStreamDestroy(m->dp.stream);
-    m->dp = DpState();
     return RBK_OK;
 }
 

@@ -88,20 +88,33 @@ struct DpBucket {
     int64_t begin, end;
 };
 
+struct DpWatch;   // the communicators' watchdog (dp.cu)
+
 struct DpState {
     bool on = false;
     // false: backward only accumulates this rank's gradients (the micro-steps of a gradient
     // accumulation group before its last); true: buckets are all-reduced as they finish.
     bool sync = true;
     int rank = 0, world = 1;
-    ncclComm_t comm = nullptr;
     cudaStream_t stream = nullptr;
     int64_t bucket_elems = 0;
     std::vector<DpBucket> plan;
     std::vector<cudaEvent_t> layer_done;   // recorded after each layer's grads are final
     cudaEvent_t head_done = nullptr, all_done = nullptr;
+    int max_ctas = 0;                      // NCCL CTA cap of the overlapped buckets (0: NCCL's default)
+    DpWatch* watch = nullptr;              // owns the communicators
 };
 
+}  // namespace rbk
+
+struct rbk_model;
+
+namespace rbk {
+// dp.cu
+std::vector<DpBucket> dp_plan(const rbk_config* c, int64_t bucket_elems);
+int dp_unit_done(rbk_model* m, int unit, cudaStream_t st);
+int dp_reduce_all(rbk_model* m, float* buf, int64_t n, cudaStream_t st);
+int dp_status(rbk_model* m);
 }  // namespace rbk
 
 struct rbk_model {

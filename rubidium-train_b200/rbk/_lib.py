@@ -57,6 +57,11 @@ class ModelOpts(C.Structure):
                 ("init_loss_scale", f32), ("growth_interval", i32), ("device", i32)]
 
 
+class DpOpts(C.Structure):
+    """rbk_dp_opts (include/rbk.h)."""
+    _fields_ = [("bucket_bytes", C.c_int64), ("max_ctas", C.c_int), ("timeout_s", C.c_double)]
+
+
 class TrainArgs(C.Structure):
     """rbk_train_args (include/rbk.h)."""
     _fields_ = [("tokens", C.c_void_p), ("n_tokens", C.c_int64), ("starts", C.c_void_p), ("seed", C.c_uint64),
@@ -113,6 +118,9 @@ _SIGS = {
     "rbk_dp_plan": (i32, [C.POINTER(Config), i64, C.POINTER(i64), i32, C.POINTER(i32)]),
     "rbk_model_dp_init": (i32, [vp, vp, i32, i32, i64]),
     "rbk_model_dp_set_sync": (i32, [vp, i32]),
+    "rbk_model_dp_init_ex": (i32, [vp, vp, i32, i32, C.POINTER(DpOpts)]),
+    "rbk_model_dp_status": (i32, [vp]),
+    "rbk_model_dp_abort": (i32, [vp]),
     "rbk_model_dp_shutdown": (i32, [vp]),
 }
 

@@ -20,7 +20,7 @@ from dataclasses import dataclass
 
 import torch
 
-from ._lib import Config, ModelOpts, Scaler, TrainArgs, call, lib
+from ._lib import Config, DpOpts, ModelOpts, Scaler, TrainArgs, call, lib
 from .ops import _s
 
 BUF_P16, BUF_P32, BUF_GRAD, BUF_M, BUF_V, BUF_LOSS, BUF_LOGITS = range(7)
@@ -252,9 +252,26 @@ class RubidiumTransformer:
         call("rbk_model_inject_inf", self.handle, C.c_int64(offset), C.c_int64(stride))
 
     # ------------------------------------------------------ data parallel --
-    def dp_init(self, rank: int, world: int, unique_id: bytes, bucket_bytes: int = 25 << 20):
+    def dp_init(self, rank: int, world: int, unique_id: bytes, bucket_bytes: int = 25 << 20, max_ctas=None,
+                timeout_s=None):
+        """Join the NCCL communicator (rbk_model_dp_init_ex).  max_ctas caps NCCL's CTAs for the
+        buckets that overlap the backward; timeout_s is the watchdog's deadline per collective.
+        None: the library defaults (environment RBK_NCCL_MAX_CTAS / RBK_NCCL_TIMEOUT_S)."""
+        import os
         buf = C.create_string_buffer(unique_id, 128)
-        call("rbk_model_dp_init", self.handle, buf, rank, world, C.c_int64(bucket_bytes))
+        o = DpOpts()
+        o.bucket_bytes = bucket_bytes
+        o.max_ctas = int(os.environ.get("RBK_NCCL_MAX_CTAS", "0")) if max_ctas is None else int(max_ctas)
+        o.timeout_s = float(os.environ.get("RBK_NCCL_TIMEOUT_S", "300")) if timeout_s is None else float(timeout_s)
+        call("rbk_model_dp_init_ex", self.handle, buf, rank, world, C.byref(o))
+
+    def dp_abort(self):
+        """Abort this rank's communicators locally (a rank leaving the job)."""
+        call("rbk_model_dp_abort", self.handle)
+
+    def dp_status(self) -> int:
+        """0, or the status (RBK_ERR_TIMEOUT -4 / RBK_ERR_NCCL -5) after the watchdog aborted."""
+        return lib().rbk_model_dp_status(self.handle)
 
     def dp_set_sync(self, sync: bool):
         """sync False: following backwards only accumulate this rank's gradients (the first
