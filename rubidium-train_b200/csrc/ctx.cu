@@ -61,6 +61,20 @@ int ctx_scratch(rbk_ctx* ctx, size_t bytes, void** out) {
     return RBK_OK;
 }
 
+int ctx_counters(rbk_ctx* ctx, int n, int** out) {
+    if (n > ctx->counters_n) {
+        if (ctx->counters) RBK_CUDA(cudaFree(ctx->counters));
+        ctx->counters = nullptr;
+        ctx->counters_n = 0;
+        const int want = n < 4096 ? 4096 : n;
+        RBK_CUDA(cudaMalloc(&ctx->counters, sizeof(int) * (size_t)want));
+        RBK_CUDA(cudaMemset(ctx->counters, 0, sizeof(int) * (size_t)want));
+        ctx->counters_n = want;
+    }
+    *out = ctx->counters;
+    return RBK_OK;
+}
+
 // out[c] += sum_r part[r*C + c]   (deterministic, fixed order over r)
 __global__ void column_reduce_kernel(float* __restrict__ out, const float* __restrict__ part, int R, int C) {
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
@@ -150,6 +164,8 @@ int rbk_ctx_create(rbk_ctx** out, int device) {
     e = cudaMemset(c->tickets, 0, sizeof(int) * (rbk_ctx::kTickets + 1));
     if (e != cudaSuccess) { cudaFree(c->tickets); delete c; return cuda_fail(e, "cudaMemset", __FILE__, __LINE__); }
     c->err = c->tickets + rbk_ctx::kTickets;
+    const char* det = getenv("RBK_DETERMINISTIC");
+    c->deterministic = det && det[0] == '1';
     *out = c;
     return RBK_OK;
 }
@@ -159,6 +175,7 @@ int rbk_ctx_destroy(rbk_ctx* ctx) {
     cudaSetDevice(ctx->device);
     if (ctx->scratch) cudaFree(ctx->scratch);
     if (ctx->tickets) cudaFree(ctx->tickets);
+    if (ctx->counters) cudaFree(ctx->counters);
     for (cudaEvent_t e : ctx->prof.pool) cudaEventDestroy(e);
     delete ctx;
     return RBK_OK;
@@ -208,6 +225,12 @@ int rbk_ctx_profile_read_gemm(rbk_ctx* ctx, double* ms, double* flops, int* laun
         flops[p.recs[i].sub] += p.recs[i].work;
         launches[p.recs[i].sub] += 1;
     }
+    return RBK_OK;
+}
+
+int rbk_ctx_set_deterministic(rbk_ctx* ctx, int on) {
+    RBK_REQUIRE(ctx, "rbk_ctx_set_deterministic: null ctx");
+    ctx->deterministic = on != 0;
     return RBK_OK;
 }
 

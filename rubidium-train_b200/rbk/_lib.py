@@ -81,6 +81,7 @@ _SIGS = {
     "rbk_ctx_profile_read": (i32, [vp, C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(i32), i32]),
     "rbk_ctx_profile_read_gemm": (i32, [vp, C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(i32)]),
     "rbk_ctx_device_error": (i32, [vp, C.POINTER(i32)]),
+    "rbk_ctx_set_deterministic": (i32, [vp, i32]),
     "rbk_model_ctx": (i32, [vp, C.POINTER(vp)]),
     "rbk_ln_fwd": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, f32, vp]),
     "rbk_ln_bwd": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, vp]),

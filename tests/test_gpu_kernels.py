@@ -205,7 +205,9 @@ def test_attn_softmax_bwd_config_2c_full_size(ops, ora):
 
 # --------------------------------------------------------------- embeddings --
 
-def test_embeddings(ops):
+def test_embeddings(ops, ora):
+    """Forward gather and backward scatter against the oracle (src/cpu_mat.h:265-277); pos_emb's
+    gradient (which the reference does not compute) against the batch sum."""
     rng = np.random.default_rng(5)
     V, T, D, B, S = 97, 40, 64, 3, 32
     tok_emb = rng.standard_normal((V, D)).astype(np.float16)
@@ -216,10 +218,26 @@ def test_embeddings(ops):
     assert rel(f(x), ex) < F16_TOL
     dx = rng.standard_normal((B * S, D)).astype(np.float16)
     dtok, dpos = ops.embed_bwd(h(dx), torch.from_numpy(tokens).cuda(), B, S, V)
-    et = np.zeros((V, D), np.float32)
-    np.add.at(et, tokens, dx.astype(np.float32))
+    et = ora.embed_bwd(dx.astype(np.float32), tokens, V)
     ep = dx.astype(np.float32).reshape(B, S, D).sum(0)
     assert rel(dtok.cpu().numpy(), et) < 1e-6 and rel(dpos.cpu().numpy(), ep) < 1e-6
+
+
+@pytest.mark.parametrize("N,V,D", [(16384, 50, 768), (16384, 50257, 768), (1000, 7, 2048), (40000, 300, 64)])
+def test_embed_bwd_reruns_bitwise(ops, ora, N, V, D):
+    """The token gradient is summed per token in position order (sorted keys), so two runs give
+    identical bits, with many repeats of each token; 40000 positions take the reduction path
+    (above the sort's 32768), checked against the oracle only."""
+    rng = np.random.default_rng(N + V)
+    tokens = rng.integers(0, V, N).astype(np.int32)
+    dx = rng.standard_normal((N, D)).astype(np.float16)
+    tt, hdx = torch.from_numpy(tokens).cuda(), h(dx)
+    a, _ = ops.embed_bwd(hdx, tt, 1, N, V)
+    b, _ = ops.embed_bwd(hdx, tt, 1, N, V)
+    if N <= 32768:
+        assert torch.equal(a, b)
+    et = ora.embed_bwd(dx.astype(np.float32), tokens, V)
+    assert rel(a.cpu().numpy(), et) < 1e-6
 
 
 # --------------------------------------------------------------------- tail --
@@ -373,4 +391,40 @@ def test_gemm_wgrad_split_k_pairs(ops, Ntok, fin, out):
     ops.gemm_wgrad(h(dY), h(X), dW=dW)
     ref = dW0 + dY.astype(np.float64).T @ X.astype(np.float64)
     assert rel(dW.cpu().numpy(), ref) < F32_TOL
+    assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("Ntok,fin,out,bias", [
+    (16384, 768, 768, False),     # the GPT-2-small Wo weight gradient: 3 x 3 pair tiles, 8 splits
+    (16384, 768, 2304, True),     # QKV shape with a bias row sum (pair tiles, one accumulator)
+    (8192, 192, 200, True),       # single-CTA N = 192 tiles with the ones-MMA row sums, ragged M
+    (5000, 136, 130, False),      # ragged N tail columns
+])
+def test_gemm_wgrad_deterministic_split_k(ops, Ntok, fin, out, bias):
+    """Deterministic mode: split-K partial tiles are added by the last arriving split in split
+    order, so repeated weight gradients are bitwise identical (and equal to the atomic mode
+    within FP32 rounding)."""
+    from rbk import lib
+    rng = np.random.default_rng(Ntok + out)
+    dY = h(_mk(rng, Ntok, out))
+    X = h(_mk(rng, Ntok, fin))
+    dW0 = torch.from_numpy(rng.standard_normal((out, fin)).astype(np.float32)).cuda()
+    db0 = torch.from_numpy(rng.standard_normal(out).astype(np.float32)).cuda()
+    lib().rbk_ctx_set_deterministic(ops.ctx().handle, 1)
+    try:
+        runs = []
+        for _ in range(2):
+            dW, db = dW0.clone(), db0.clone()
+            ops.gemm_wgrad(dY, X, dW=dW, dbias=db if bias else None)
+            runs.append((dW, db))
+    finally:
+        lib().rbk_ctx_set_deterministic(ops.ctx().handle, 0)
+    assert torch.equal(runs[0][0], runs[1][0]) and torch.equal(runs[0][1], runs[1][1])
+    dW, db = dW0.clone(), db0.clone()
+    ops.gemm_wgrad(dY, X, dW=dW, dbias=db if bias else None)
+    assert rel(runs[0][0].cpu().numpy(), dW.cpu().numpy()) < 1e-6
+    ref = dW0.double() + dY.double().t() @ X.double()
+    assert rel(runs[0][0].cpu().numpy(), ref.cpu().numpy()) < F32_TOL
+    if bias:
+        assert rel(runs[0][1].cpu().numpy(), (db0.double() + dY.double().sum(0)).cpu().numpy()) < F32_TOL
     assert ops.device_error() == 0
