@@ -77,10 +77,13 @@ int rbk_ctx_profile_read(rbk_ctx* ctx, double* ms, double* work, int* launches, 
 int rbk_ctx_profile_read_gemm(rbk_ctx* ctx, double* ms, double* flops, int* launches);
 int rbk_ctx_device_error(rbk_ctx* ctx, int* status);
 /* Bitwise-reproducible gradients (default off, or on for every new context when
- * RBK_DETERMINISTIC=1): split-K weight-gradient GEMMs write partial tiles that
- * the last arriving split adds in split order, instead of FP32 atomics, so two
- * runs on the same inputs give identical bits.  The token-embedding gradient is
- * reproducible in both modes.  No counterpart in the reference. */
+ * RBK_DETERMINISTIC=1), so two runs on the same inputs give identical bits:
+ *   - split-K weight-gradient GEMMs write partial tiles that the last arriving
+ *     split adds in split order, instead of FP32 atomics;
+ *   - the tcgen05 attention backward (S % 128 == 0) adds each query block's dQ
+ *     contributions in ascending key-block order (per-block counters).
+ * The token-embedding gradient is reproducible in both modes.  No counterpart
+ * in the reference. */
 int rbk_ctx_set_deterministic(rbk_ctx* ctx, int on);
 
 /* ------------------------------------------------------------------------

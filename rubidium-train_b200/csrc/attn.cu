@@ -22,8 +22,9 @@
 namespace rbk {
 
 // tcgen05 main backward pass for d_head 64 / 128, S % 128 == 0 (attn_bwd_tc.cu).
+// dq_sem (deterministic mode): zeroed ints [B*H, S/64] that order the dQ additions.
 int attn_bwd_tc(rbk_ctx* ctx, void* dqkv, float* dq_acc, const void* qkv, const void* dout, const float* NL2,
-                const float* Dot, int B, int S, int H, int dh, float scale, cudaStream_t st);
+                const float* Dot, int B, int S, int H, int dh, float scale, cudaStream_t st, int* dq_sem);
 
 namespace attn {
 
@@ -267,8 +268,14 @@ template <int HD>
 __global__ void __launch_bounds__(512, 2)
     flash_bwd_pre_kernel(float* __restrict__ Dot, float* __restrict__ dq_acc, float* __restrict__ NL2,
                          float* __restrict__ vpart, const float* __restrict__ LSE, const half* __restrict__ O,
-                         const half* __restrict__ dO, int BS, int S, int H, int rows_per_block) {
+                         const half* __restrict__ dO, int BS, int S, int H, int rows_per_block, int* __restrict__ sem,
+                         int nsem) {
     grid_dependency_sync();
+    if (sem) {                           // the main pass's dQ ordering counters start at zero
+        const int nt = blockDim.x * blockDim.y * gridDim.x * gridDim.y;
+        const int id = ((blockIdx.y * gridDim.x + blockIdx.x) * blockDim.y + threadIdx.y) * blockDim.x + threadIdx.x;
+        for (int i = id; i < nsem; i += nt) sem[i] = 0;
+    }
     __shared__ __align__(16) float red[512 * 8];
     constexpr int G = HD / 8;            // chunks per (row, head)
     const int D = H * HD;
@@ -619,8 +626,12 @@ int bwd(rbk_ctx* ctx, void* dqkv, float* dbias, const void* qkv, const void* o, 
     nrb = (int)((BS + rows_per_block - 1) / rows_per_block);
     const size_t dq_bytes = (sizeof(float) * BS * D + 255) & ~size_t(255);
     const size_t part_bytes = sizeof(float) * (size_t)nrb * D;   // one [nrb, D] block per bias part
+    const bool det = tc && ctx->deterministic;
+    const int nsem = det ? (int)((size_t)B * H * (S / 64)) : 0;
+    const size_t sem_bytes = ((sizeof(int) * (size_t)nsem) + 255) & ~size_t(255);
     void* ws;
-    RBK_TRY(ctx_scratch(ctx, 2 * dot_bytes + dq_bytes + 2 * part_bytes, &ws));
+    RBK_TRY(ctx_scratch(ctx, 2 * dot_bytes + dq_bytes + 2 * part_bytes + sem_bytes, &ws));
+    int* sem = det ? (int*)((char*)ws + 2 * dot_bytes + dq_bytes + 2 * part_bytes) : nullptr;
     float* Dot = (float*)ws;
     float* NL2 = (float*)((char*)ws + dot_bytes);
     float* dq_acc = (float*)((char*)ws + 2 * dot_bytes);
@@ -631,10 +642,10 @@ int bwd(rbk_ctx* ctx, void* dqkv, float* dbias, const void* qkv, const void* o, 
     const dim3 rgrid(col_blocks, nrb), rblock(TX, TY);
     RBK_CUDA(launch_pdl(flash_bwd_pre_kernel<HD>, rgrid, rblock, 0, st, Dot, dq_acc, tc ? NL2 : nullptr,
                         vsum ? vpart : nullptr, lse, (const half*)o, (const half*)dout, (int)BS, S, H,
-                        rows_per_block));
+                        rows_per_block, sem, nsem));
     RBK_LAUNCHED("flash_bwd_pre_kernel");
     if (tc) {
-        RBK_TRY(attn_bwd_tc(ctx, dqkv, dq_acc, qkv, dout, NL2, Dot, B, S, H, HD, scale, st));
+        RBK_TRY(attn_bwd_tc(ctx, dqkv, dq_acc, qkv, dout, NL2, Dot, B, S, H, HD, scale, st, sem));
     } else {
         constexpr int SMEM = 6 * BLK * HD * 2 + BLK * BLK * 2 + 4 * BLK * 4;
         static int set_dev = -1;

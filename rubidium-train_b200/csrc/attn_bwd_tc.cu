@@ -103,6 +103,33 @@ __device__ __forceinline__ uint32_t stage_addr(uint32_t s, int row, int chunk /*
     return s + (uint32_t)(chunk >> 3) * 16384u + (uint32_t)row * 128u + (uint32_t)(((chunk & 7) ^ (row & 7)) << 4);
 }
 
+// Deterministic dQ (dq_sem != nullptr): the contributions to a query block are added in
+// ascending key-block order.  dq_sem counts, per (batch * head, 64-query block), the
+// contributions already added; an item waits until the count shows every lower key block done.
+// Items are dispatched key-block-major (lower key blocks first) to CTAs that are all resident,
+// so the item waited on is already running or done; every wait is bounded.
+__device__ __forceinline__ int ld_acquire(const int* p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __noinline__ bool wait_count(const int* p, int want, volatile int* abort_flag) {
+    if (ld_acquire(p) >= want) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire(p) < want) {
+        if (*abort_flag) return false;
+        if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+            *abort_flag = 1;
+            return false;
+        }
+        __nanosleep(128);
+    }
+    return true;
+}
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // Work item u (longest first: all diagonal-0 key blocks, then 1, ...).
 struct Item {
     int kb, bh, h, n, krow0;
@@ -129,7 +156,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const __grid_constant__ CUtensorMap tmdo, const __grid_constant__ CUtensorMap tmdq,
                         const __grid_constant__ CUtensorMap tmout, const float* __restrict__ NL2,
                         const float* __restrict__ Dot, int S, int H, int num_items, float scale, float scale_log2,
-                        int* err) {
+                        int* err, int* __restrict__ dq_sem) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = su32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -449,9 +476,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     fence_proxy_async();
                     named_sync(1, 128);
+                    // query block kb + i (128 rows) is entry 2 (kb + i) of the item's 64-row counters
+                    int* sem = dq_sem ? dq_sem + (size_t)it.bh * (S / 64) + 2 * (it.kb + i) : nullptr;
+                    if (elected && ok && sem && hc == 0) {
+                        ok = wait_count(sem, it.kb, abort_flag);   // key blocks 0 .. kb-1 have added
+                        fence_proxy_async_global();
+                    }
                     if (elected && ok) {
                         tma_reduce_add_2d(&tmdq, sStg, it.h * HD + hc * 32, it.krow0 + i * BQ);
                         bulk_commit();
+                        if (sem && hc == 1) {                      // both halves complete: count this one
+                            bulk_wait0();
+                            fence_proxy_async_global();
+                            __threadfence();
+                            atomicAdd(sem, 1);
+                        }
                     }
                 }
             }
@@ -528,6 +567,8 @@ using attn_tc_bwd::pack_h2;
 using attn_tc_bwd::st_shared_v4;
 using attn_tc_bwd::ld_shared_f4;
 using attn_tc_bwd::Item;
+using attn_tc_bwd::ld_acquire;
+using attn_tc_bwd::wait_count;
 using attn_tc_bwd::item_of;
 using attn_tc_bwd::Masked;
 using attn_tc_bwd::Plain;
@@ -561,7 +602,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     flash_bwd_tc128_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmkv,
                            const __grid_constant__ CUtensorMap tmdo, half* __restrict__ dqkv,
                            float* __restrict__ dq_acc, const float* __restrict__ NL2, const float* __restrict__ Dot,
-                           int S, int H, int num_items, float scale, float scale_log2, int* err) {
+                           int S, int H, int num_items, float scale, float scale_log2, int* err,
+                           int* __restrict__ dq_sem) {
     extern __shared__ __align__(1024) uint8_t smem128[];
     const uint32_t raw = su32(smem128);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -824,6 +866,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ok = __all_sync(0xffffffffu, mbar_wait(dq_full, g & 1, abort_flag));
                 if (!ok) break;
                 fence_after();
+                // deterministic dQ: 64-query block 2 kb + i takes the key blocks in ascending order; each
+                // of the 4 drain warps counts its own part, so key block kb waits for 4 kb arrivals
+                int* sem = dq_sem ? dq_sem + (size_t)it.bh * (S / 64) + 2 * it.kb + i : nullptr;
+                if (sem) {
+                    bool w = true;
+                    if (lane == 0) w = wait_count(sem, 4 * it.kb, abort_flag);
+                    ok = __shfl_sync(0xffffffffu, w, 0);
+                    if (!ok) break;
+                    (void)ld_acquire(sem);                    // every lane orders its adds after the count
+                }
                 float* dst = dq_acc + (size_t)(it.krow0 + i * BQ) * D + it.h * HD + r;
 #pragma unroll 1
                 for (int hc = 0; hc < 2; ++hc) {              // 32 queries at a time
@@ -837,6 +889,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
 #pragma unroll
                     for (int c = 0; c < 32; ++c) red_add(dst + (size_t)(hc * 32 + c) * D, __uint_as_float(a[c]) * scale);
+                }
+                if (sem) {
+                    __threadfence();
+                    __syncwarp();
+                    if (lane == 0) {
+                        __threadfence();
+                        atomicAdd(sem, 1);
+                    }
                 }
             }
             if (!ok) break;
@@ -883,7 +943,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // dq_acc: FP32 [B*S, H*dh], zeroed; NL2 / Dot: [B*H, S].  Writes the k and v
 // sections of dqkv and adds dQ into dq_acc.
 int attn_bwd_tc(rbk_ctx* ctx, void* dqkv, float* dq_acc, const void* qkv, const void* dout, const float* NL2,
-                const float* Dot, int B, int S, int H, int dh, float scale, cudaStream_t st) {
+                const float* Dot, int B, int S, int H, int dh, float scale, cudaStream_t st, int* dq_sem) {
     const uint64_t BS = (uint64_t)B * S;
     const int items = B * H * (S / 128);
     const int grid = items < ctx->num_sms ? items : ctx->num_sms;
@@ -901,7 +961,7 @@ int attn_bwd_tc(rbk_ctx* ctx, void* dqkv, float* dq_acc, const void* qkv, const 
         }
         RBK_CUDA(launch_pdl(flash_bwd_tc128_kernel, dim3(grid), dim3(kThreads), SMEM, st, tmq, tmkv, tmdo, (half*)dqkv,
                             dq_acc, NL2, Dot, S, H, items, scale, scale * 1.4426950408889634f,
-                            ctx->tickets + kGemmError));
+                            ctx->tickets + kGemmError, dq_sem));
         RBK_LAUNCHED("flash_bwd_tc128_kernel");
         return RBK_OK;
     }
@@ -920,7 +980,7 @@ int attn_bwd_tc(rbk_ctx* ctx, void* dqkv, float* dq_acc, const void* qkv, const 
         set_dev = ctx->device;
     }
     RBK_CUDA(launch_pdl(flash_bwd_tc_kernel, dim3(grid), dim3(kThreads), SMEM, st, tmq, tmkv, tmdo, tmdq, tmout, NL2,
-                        Dot, S, H, items, scale, scale * 1.4426950408889634f, ctx->tickets + kGemmError));
+                        Dot, S, H, items, scale, scale * 1.4426950408889634f, ctx->tickets + kGemmError, dq_sem));
     RBK_LAUNCHED("flash_bwd_tc_kernel");
     return RBK_OK;
 }

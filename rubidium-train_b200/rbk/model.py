@@ -203,6 +203,13 @@ class RubidiumTransformer:
         call("rbk_model_backward", self.handle, C.c_void_p(tokens.data_ptr()), C.c_void_p(targets.data_ptr()), B, T,
              C.c_float(loss_scale), _s())
 
+    def set_deterministic(self, on: bool = True):
+        """Bitwise-reproducible backward on this model's context (rbk_ctx_set_deterministic):
+        ordered split-K weight gradients and ordered dQ additions in the attention backward."""
+        ctx = C.c_void_p()
+        call("rbk_model_ctx", self.handle, C.byref(ctx))
+        call("rbk_ctx_set_deterministic", ctx, int(bool(on)))
+
     def set_training(self, training: bool = True):
         """Training mode: forward also writes dlogits (one pass over the logits);
         eval mode keeps the logits intact."""

@@ -180,6 +180,27 @@ def test_headline_widths_match_oracle(ora, which):
     assert not bad, bad
 
 
+@pytest.mark.parametrize("which", ["config1", "gpt2-small-widths"])
+def test_backward_bitwise_reproducible(ora, which):
+    """Deterministic mode: two forward + backward passes on the same inputs give identical
+    gradient arenas, bit for bit (ordered split-K weight gradients, ordered dQ additions in the
+    attention backward, the sorted token-embedding gradient), and stay within the oracle bound."""
+    cfg, B, S = (CFG1, 8, 128) if which == "config1" else HEADLINE["gpt2-small-widths"]
+    m, params, tok, tgt = _setup(ora, cfg, B, S, seed=4)
+    m.set_deterministic(True)
+    tt = torch.from_numpy(tok).cuda().view(B, S)
+    tg = torch.from_numpy(tgt).cuda().view(B, S)
+    grads = []
+    for _ in range(2):
+        m.grad.zero_()
+        m.forward(tt, tg, B, S)
+        m.backward(tt, tg, B, S, loss_scale=1.0)
+        torch.cuda.synchronize()
+        grads.append(m.grad.clone())
+    m.close()
+    assert torch.equal(grads[0], grads[1]), "deterministic backward differs between two runs"
+
+
 def test_config1_full_step_matches_oracle(ora):
     """fwd + bwd + fused Adam tail (lr 3e-4): post-step masters vs the oracle's."""
     B, S = 8, 128
