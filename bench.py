@@ -399,43 +399,63 @@ def all_gemm_shapes():
     return out
 
 
+def gemm_case(name, torch, ops, g):
+    """(launch function, FLOPs per launch) of one step GEMM shape; inputs rotate over enough sets
+    (> 2x the 126 MB L2) that every launch reads them from DRAM."""
+    shapes = all_gemm_shapes()
+    if name not in shapes:
+        raise SystemExit(f"unknown GEMM {name}: one of {sorted(shapes)}")
+    M, Nn, K, am, bm, epi, extra = shapes[name]
+    lda, ldb, ldc = r8(M if am else K), r8(Nn if bm else K), r8(Nn)
+    f32 = epi in (ops.EPI_ACC_F32, ops.EPI_STORE_F32)
+    set_bytes = 2 * ((K if am else M) * lda + (K if bm else Nn) * ldb) + M * ldc * (4 if f32 else 2) * \
+        (2 if epi in (ops.EPI_GELU_BWD, ops.EPI_BIAS_GELU) or extra == "res" else 1)
+    nsets = max(1, min(16, -(-300_000_000 // set_bytes)))
+    sets = []
+    for _ in range(nsets):
+        A = (0.5 * torch.randn(K if am else M, lda, device="cuda", generator=g)).half()
+        B = (0.5 * torch.randn(K if bm else Nn, ldb, device="cuda", generator=g)).half()
+        Cm = torch.zeros(M, ldc, device="cuda", dtype=torch.float32 if f32 else torch.float16)
+        aux = torch.randn(M, ldc, device="cuda", generator=g).half() \
+            if epi == ops.EPI_GELU_BWD or extra == "res" else None
+        aux_out = torch.empty(M, ldc, device="cuda", dtype=torch.float16) if epi == ops.EPI_BIAS_GELU else None
+        sets.append((A, B, Cm, aux, aux_out))
+    bias = torch.randn(ldc, device="cuda", generator=g).half() if extra == "bias" or epi == ops.EPI_BIAS_GELU \
+        else None
+    dbias = torch.zeros(M, device="cuda") if extra == "dbias" else None
+    it = [0]
+
+    def fn():
+        A, B, Cm, aux, aux_out = sets[it[0] % nsets]
+        it[0] += 1
+        ops.gemm(A, B, M, Nn, K, am, bm, C_out=Cm, ldc=ldc, epilogue=epi, bias=bias, aux=aux, aux_out=aux_out,
+                 dbias_rows=dbias, lda=lda, ldb=ldb, store_c=epi != ops.EPI_BIAS_GELU)
+    return fn, 2.0 * M * Nn * K
+
+
 def kernel_loop(name, reps, torch, ops):
     """One kernel at a representative GPT-2-small shape, `reps` launches (for ncu
     captures and tuning).  Prints per-launch time and the achieved rate.  GEMM inputs
-    rotate over enough sets (> 2x the 126 MB L2) that every launch reads them from DRAM."""
+    rotate over enough sets (> 2x the 126 MB L2) that every launch reads them from DRAM.
+    gemm_all: every GEMM shape of the step in turn (no timing line)."""
     g = torch.Generator(device="cuda").manual_seed(0)
     hbm, tc, tcs, _ = peaks()
     N, D, F, V = 16384, 768, 3072, 50257
+    if name == "gemm_all":
+        # every GEMM shape of the GPT-2-small step, `reps` launches each, one shape resident at a
+        # time (for one ncu capture of their DRAM traffic)
+        for k in gemm_shapes():
+            fn, _ = gemm_case(k, torch, ops, g)
+            for _ in range(reps):
+                fn()
+            torch.cuda.synchronize()
+            del fn
+            torch.cuda.empty_cache()
+        print(json.dumps({"kernel": name, "shapes": len(gemm_shapes()), "launches_each": reps}), flush=True)
+        return 0
     if name.startswith("gemm"):
-        shapes = all_gemm_shapes()
-        if name not in shapes:
-            raise SystemExit(f"unknown GEMM {name}: one of {sorted(shapes)}")
-        M, Nn, K, am, bm, epi, extra = shapes[name]
-        lda, ldb, ldc = r8(M if am else K), r8(Nn if bm else K), r8(Nn)
-        f32 = epi in (ops.EPI_ACC_F32, ops.EPI_STORE_F32)
-        set_bytes = 2 * ((K if am else M) * lda + (K if bm else Nn) * ldb) + M * ldc * (4 if f32 else 2) * \
-            (2 if epi in (ops.EPI_GELU_BWD, ops.EPI_BIAS_GELU) or extra == "res" else 1)
-        nsets = max(1, min(16, -(-300_000_000 // set_bytes)))
-        sets = []
-        for _ in range(nsets):
-            A = (0.5 * torch.randn(K if am else M, lda, device="cuda", generator=g)).half()
-            B = (0.5 * torch.randn(K if bm else Nn, ldb, device="cuda", generator=g)).half()
-            Cm = torch.zeros(M, ldc, device="cuda", dtype=torch.float32 if f32 else torch.float16)
-            aux = torch.randn(M, ldc, device="cuda", generator=g).half() \
-                if epi == ops.EPI_GELU_BWD or extra == "res" else None
-            aux_out = torch.empty(M, ldc, device="cuda", dtype=torch.float16) if epi == ops.EPI_BIAS_GELU else None
-            sets.append((A, B, Cm, aux, aux_out))
-        bias = torch.randn(ldc, device="cuda", generator=g).half() if extra == "bias" or epi == ops.EPI_BIAS_GELU \
-            else None
-        dbias = torch.zeros(M, device="cuda") if extra == "dbias" else None
-        it = [0]
-
-        def fn():
-            A, B, Cm, aux, aux_out = sets[it[0] % nsets]
-            it[0] += 1
-            ops.gemm(A, B, M, Nn, K, am, bm, C_out=Cm, ldc=ldc, epilogue=epi, bias=bias, aux=aux, aux_out=aux_out,
-                     dbias_rows=dbias, lda=lda, ldb=ldb, store_c=epi != ops.EPI_BIAS_GELU)
-        work, unit, peak = 2.0 * M * Nn * K, "TFLOP/s", tc
+        fn, work = gemm_case(name, torch, ops, g)
+        unit, peak = "TFLOP/s", tc
     elif name == "ln_bwd":
         # four input sets (256 MB) rotate, so x and dy come from DRAM as in the step
         sets = [(torch.randn(16384, 1024, device="cuda", generator=g).half(),

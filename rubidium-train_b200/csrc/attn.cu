@@ -21,7 +21,7 @@
 
 namespace rbk {
 
-// tcgen05 main backward pass for d_head 64 / 128, S % 128 == 0 (attn_bwd_tc.cu).
+// tcgen05 main backward pass for d_head 64 / 128, S % 64 == 0 (attn_bwd_tc.cu).
 // dq_sem (deterministic mode): zeroed ints [B*H, S/64] that order the dQ additions.
 int attn_bwd_tc(rbk_ctx* ctx, void* dqkv, float* dq_acc, const void* qkv, const void* dout, const float* NL2,
                 const float* Dot, int B, int S, int H, int dh, float scale, cudaStream_t st, int* dq_sem);
@@ -671,7 +671,7 @@ int bwd(rbk_ctx* ctx, void* dqkv, float* dbias, const void* qkv, const void* o, 
 
 }  // namespace attn
 
-// tcgen05 forward for d_head 64 / 128, S % 128 == 0 (attn_tc.cu).
+// tcgen05 forward for d_head 64 / 128, S % 64 == 0 (attn_tc.cu).
 int attn_fwd_tc(rbk_ctx* ctx, void* o, float* lse, const void* qkv, int B, int S, int H, int dh, float scale,
                 cudaStream_t st);
 
@@ -699,8 +699,8 @@ int rbk_attn_fwd(rbk_ctx* ctx, void* o, float* lse, const void* qkv, int B, int 
     cudaStream_t st = as_stream(stream);
     // causal: QK^T and PV over S(S+1)/2 score entries per (b, h)
     ProfScope prof(ctx, st, kCatAttnFwd, 4.0 * B * H * ((double)S * (S + 1) / 2.0) * dh);
-    // tcgen05 kernel (attn_tc.cu) for 128-multiple lengths
-    if (S % 128 == 0 && !attn_legacy()) return attn_fwd_tc(ctx, o, lse, qkv, B, S, H, dh, scale, st);
+    // tcgen05 kernel (attn_tc.cu); the mma.sync kernels only under RBK_ATTN_LEGACY=1
+    if (!attn_legacy()) return attn_fwd_tc(ctx, o, lse, qkv, B, S, H, dh, scale, st);
     return dh == 64 ? attn::fwd<64>(ctx, o, lse, qkv, B, S, H, scale, st)
                     : attn::fwd<128>(ctx, o, lse, qkv, B, S, H, scale, st);
 }
@@ -714,7 +714,7 @@ int rbk_attn_bwd(rbk_ctx* ctx, void* dqkv, float* dbias_qkv, const void* qkv, co
     cudaStream_t st = as_stream(stream);
     // algorithmic: dV, dP, dQ, dK products over the causal triangle (score recompute excluded)
     ProfScope prof(ctx, st, kCatAttnBwd, 8.0 * B * H * ((double)S * (S + 1) / 2.0) * dh);
-    const bool tc = S % 128 == 0 && !attn_legacy();
+    const bool tc = !attn_legacy();
     return dh == 64 ? attn::bwd<64>(ctx, dqkv, dbias_qkv, qkv, o, dout, lse, B, S, H, scale, tc, st)
                     : attn::bwd<128>(ctx, dqkv, dbias_qkv, qkv, o, dout, lse, B, S, H, scale, tc, st);
 }

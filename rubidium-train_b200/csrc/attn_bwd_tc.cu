@@ -139,7 +139,7 @@ __device__ __forceinline__ Item item_of(int u, int BH, int H, int S) {
     it.kb = u / BH;
     it.bh = u % BH;
     it.h = it.bh % H;
-    it.n = 2 * (S / BK - it.kb);
+    it.n = (S - it.kb * BK) / 64;         // 64-query sub-tiles from the diagonal to S (d_head 128)
     it.krow0 = (it.bh / H) * S + it.kb * BK;
     return it;
 }
@@ -156,7 +156,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const __grid_constant__ CUtensorMap tmdo, const __grid_constant__ CUtensorMap tmdq,
                         const __grid_constant__ CUtensorMap tmout, const float* __restrict__ NL2,
                         const float* __restrict__ Dot, int S, int H, int num_items, float scale, float scale_log2,
-                        int* err, int* __restrict__ dq_sem) {
+                        int* err, int* __restrict__ dq_sem, const __grid_constant__ CUtensorMap tmdq64,
+                        const __grid_constant__ CUtensorMap tmout64) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = su32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -183,8 +184,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + OFF_BAR + NBARS * 8 + 8);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nkb = S / BK;
+    const int nkb = (S + BK - 1) / BK;
     const int BH = num_items / nkb;
+    const bool half_tail = S % BK != 0;     // the last key / query block holds 64 rows
     const int D = H * HD;
     // sub-tiles of item u: 128-query blocks from the diagonal to the end
     auto subtiles = [&](int u) { return nkb - u / BH; };
@@ -349,6 +351,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (int u = blockIdx.x; ok && u < num_items; u += gridDim.x) {
             const int n = subtiles(u);
+            const int kbu = u / BH;                            // the item's key block
             for (int i = 0; i < n; ++i, ++g) {
                 const int s = g % QS;
                 ok = mbar_wait(s_full, g & 1, abort_flag) && mbar_wait(q_full(s), (g / QS) & 1, abort_flag);
@@ -359,9 +362,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 fence_after();
                 const uint32_t rowp = sRow(s);
                 uint32_t pk[16], dk[16];
+                // query columns at or beyond qmax lie past the sequence end (a half last block): P = 0
+                const int qmax = S - (kbu * BK + i * BQ) - c0;
                 // columns c0 + 16 h .. +15; masked: the diagonal sub-tile, where columns e < lim lie above it
-                auto compute = [&](auto masked, int h, const uint32_t* sr, const uint32_t* dr) {
+                auto compute = [&](auto masked, auto tail, int h, const uint32_t* sr, const uint32_t* dr) {
                     const int lim = r - c0 - 16 * h;
+                    const int qm = qmax - 16 * h;
 #pragma unroll
                     for (int q4 = 0; q4 < 4; ++q4) {
                         const int cc = c0 + 16 * h + 4 * q4;
@@ -379,6 +385,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                             if (decltype(masked)::value) {
                                 p0 = e < lim ? 0.0f : p0;
                                 p1 = e + 1 < lim ? 0.0f : p1;
+                            }
+                            if (decltype(tail)::value) {
+                                p0 = e >= qm ? 0.0f : p0;
+                                p1 = e + 1 >= qm ? 0.0f : p1;
                             }
                             pv[e4] = p0;
                             pv[e4 + 1] = p1;
@@ -403,8 +413,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                         __syncwarp();
                         if (lane == 0) mbar_arrive(s_free);   // the producer may overwrite S^T / dP^T
                     }
-                    if (i == 0) compute(Masked{}, h, sr, dr);
-                    else compute(Plain{}, h, sr, dr);
+                    const bool tail = half_tail && i == n - 1;   // the sub-tile that ends at S
+                    if (i == 0) {
+                        if (tail) compute(Masked{}, Masked{}, h, sr, dr);
+                        else compute(Masked{}, Plain{}, h, sr, dr);
+                    } else {
+                        if (tail) compute(Plain{}, Masked{}, h, sr, dr);
+                        else compute(Plain{}, Plain{}, h, sr, dr);
+                    }
                 }
                 // dS^T was last read by dK / dQ of the previous sub-tile, P^T by its dV
                 ok = g == 0 || mbar_wait(ds_free, (g - 1) & 1, abort_flag);
@@ -483,7 +499,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         fence_proxy_async_global();
                     }
                     if (elected && ok) {
-                        tma_reduce_add_2d(&tmdq, sStg, it.h * HD + hc * 32, it.krow0 + i * BQ);
+                        // the sub-tile that ends at a half block adds only its 64 rows inside the sequence
+                        const bool tail = half_tail && i == n - 1;
+                        tma_reduce_add_2d(tail ? &tmdq64 : &tmdq, sStg, it.h * HD + hc * 32, it.krow0 + i * BQ);
                         bulk_commit();
                         if (sem && hc == 1) {                      // both halves complete: count this one
                             bulk_wait0();
@@ -524,8 +542,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             fence_proxy_async();
             named_sync(1, 128);
             if (elected && ok) {
-                tma_store_2d(&tmout, sK(kvb), D + it.h * HD, it.krow0);
-                tma_store_2d(&tmout, sV(kvb), 2 * D + it.h * HD, it.krow0);
+                // a half last key block stores its 64 rows inside the sequence only
+                const CUtensorMap* to = (half_tail && it.kb == nkb - 1) ? &tmout64 : &tmout;
+                tma_store_2d(to, sK(kvb), D + it.h * HD, it.krow0);
+                tma_store_2d(to, sV(kvb), 2 * D + it.h * HD, it.krow0);
                 bulk_commit();
                 bulk_wait_read0();                            // tiles read: the buffer may take new K / V
                 mbar_arrive(kv_empty(kvb));
@@ -630,7 +650,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + OFF_BAR + NBARS * 8 + 8);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int BH = num_items / (S / BK);
+    const int BH = num_items / ((S + BK - 1) / BK);
     const int D = H * HD;
 
     if (threadIdx.x == 0) {
@@ -918,6 +938,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 const float f = tv ? 1.0f : scale;
                 uint4* out = reinterpret_cast<uint4*>(krow + tv * D + hc * 32);
+                const bool inside = it.kb * BK + r < S;       // key rows of a half last block beyond S: none
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     uint4 w;
@@ -925,7 +946,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     w.y = pack_h2(__uint_as_float(a[8 * c + 2]) * f, __uint_as_float(a[8 * c + 3]) * f);
                     w.z = pack_h2(__uint_as_float(a[8 * c + 4]) * f, __uint_as_float(a[8 * c + 5]) * f);
                     w.w = pack_h2(__uint_as_float(a[8 * c + 6]) * f, __uint_as_float(a[8 * c + 7]) * f);
-                    out[c] = w;
+                    if (inside) out[c] = w;
                 }
             }
         }
@@ -939,13 +960,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace attn_tc_bwd128
 
-// Main pass of rbk_attn_bwd (attn.cu) when d_head is 64 or 128 and S % 128 == 0.
+// Main pass of rbk_attn_bwd (attn.cu) for d_head 64 or 128 and S % 64 == 0 (a sequence that ends in
+// a half 128-row block: the tail sub-tile masks its queries beyond S, and the stores and dQ
+// additions of the last blocks cover only their rows inside the sequence).
 // dq_acc: FP32 [B*S, H*dh], zeroed; NL2 / Dot: [B*H, S].  Writes the k and v
 // sections of dqkv and adds dQ into dq_acc.
 int attn_bwd_tc(rbk_ctx* ctx, void* dqkv, float* dq_acc, const void* qkv, const void* dout, const float* NL2,
                 const float* Dot, int B, int S, int H, int dh, float scale, cudaStream_t st, int* dq_sem) {
     const uint64_t BS = (uint64_t)B * S;
-    const int items = B * H * (S / 128);
+    const int items = B * H * ((S + 127) / 128);
     const int grid = items < ctx->num_sms ? items : ctx->num_sms;
     if (dh == 128) {
         using namespace attn_tc_bwd128;
@@ -968,19 +991,23 @@ int attn_bwd_tc(rbk_ctx* ctx, void* dqkv, float* dq_acc, const void* qkv, const 
     if (dh != 64) return RBK_ERR_UNSUPPORTED;
     using namespace attn_tc_bwd;
     const int D = H * HD;
-    CUtensorMap tmq, tmkv, tmdo, tmdq, tmout;
+    CUtensorMap tmq, tmkv, tmdo, tmdq, tmout, tmdq64, tmout64;
     RBK_TRY(tc::make_tmap(&tmq, qkv, 3 * (uint64_t)D, BS, 3 * (uint64_t)D, 64, BQ));
     RBK_TRY(tc::make_tmap(&tmkv, qkv, 3 * (uint64_t)D, BS, 3 * (uint64_t)D, 64, BK));
     RBK_TRY(tc::make_tmap(&tmdo, dout, (uint64_t)D, BS, (uint64_t)D, 64, BQ));
     RBK_TRY(tc::make_tmap(&tmdq, dq_acc, (uint64_t)D, BS, (uint64_t)D, 32, 128, CU_TENSOR_MAP_DATA_TYPE_FLOAT32));
     RBK_TRY(tc::make_tmap(&tmout, dqkv, 3 * (uint64_t)D, BS, 3 * (uint64_t)D, 64, BK));
+    // the 64 rows of a half last block (sequences of 128 k + 64)
+    RBK_TRY(tc::make_tmap(&tmdq64, dq_acc, (uint64_t)D, BS, (uint64_t)D, 32, 64, CU_TENSOR_MAP_DATA_TYPE_FLOAT32));
+    RBK_TRY(tc::make_tmap(&tmout64, dqkv, 3 * (uint64_t)D, BS, 3 * (uint64_t)D, 64, 64));
     static int set_dev = -1;
     if (set_dev != ctx->device) {
         RBK_CUDA(cudaFuncSetAttribute(flash_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
         set_dev = ctx->device;
     }
     RBK_CUDA(launch_pdl(flash_bwd_tc_kernel, dim3(grid), dim3(kThreads), SMEM, st, tmq, tmkv, tmdo, tmdq, tmout, NL2,
-                        Dot, S, H, items, scale, scale * 1.4426950408889634f, ctx->tickets + kGemmError, dq_sem));
+                        Dot, S, H, items, scale, scale * 1.4426950408889634f, ctx->tickets + kGemmError, dq_sem,
+                        tmdq64, tmout64));
     RBK_LAUNCHED("flash_bwd_tc_kernel");
     return RBK_OK;
 }

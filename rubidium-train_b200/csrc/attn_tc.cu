@@ -31,6 +31,10 @@
 // Causal masking applies to the two key blocks that overlap the query block;
 // blocks above the diagonal are never loaded.  Output O (FP16) and LSE
 // (natural log), as the mma.sync path.  Every wait is bounded; no multicast.
+// Sequence lengths that are 64 more than a multiple of 128 end in a half query
+// block: its Q rows beyond the sequence are the next sequence's (or TMA's zero
+// fill after the last), computed but never stored; the keys beyond the
+// sequence are above every stored query, so the causal mask zeroes them.
 #include "tc.cuh"
 
 namespace rbk {
@@ -119,7 +123,7 @@ __global__ void __launch_bounds__(FwdCfg<HD>::THREADS, FwdCfg<HD>::CTAS_PER_SM)
     volatile int* tile_slot = reinterpret_cast<volatile int*>(misc + 8);   // [2]: the tile ring
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nqb = S / BQ;
+    const int nqb = (S + BQ - 1) / BQ;
     const int ntiles = nqb * BH;
     const int D = H * HD;
 
@@ -428,10 +432,12 @@ __global__ void __launch_bounds__(FwdCfg<HD>::THREADS, FwdCfg<HD>::CTAS_PER_SM)
                     o[e] = __uint_as_float(t0[e]) * f0;
                     if constexpr (NG == 2) o[e] = fmaf(__uint_as_float(t1[e]), f1, o[e]);
                 }
+                if (qpos < S) {                           // rows of a half last block beyond S are not stored
 #pragma unroll
-                for (int g = 0; g < 2; ++g) reinterpret_cast<uint4*>(orow + c * 16)[g] = f_to_h8(o + 8 * g);
+                    for (int g = 0; g < 2; ++g) reinterpret_cast<uint4*>(orow + c * 16)[g] = f_to_h8(o + 8 * g);
+                }
             }
-            if (wg == 0) LSE[(size_t)bh * S + qpos] = (M + __log2f(L)) * 0.6931471805599453f;
+            if (wg == 0 && qpos < S) LSE[(size_t)bh * S + qpos] = (M + __log2f(L)) * 0.6931471805599453f;
             // O is out of TMEM: the next tile's first PV may overwrite it
             fence_before();
             __syncwarp();
@@ -448,7 +454,7 @@ __global__ void __launch_bounds__(FwdCfg<HD>::THREADS, FwdCfg<HD>::CTAS_PER_SM)
 
 }  // namespace attn_tc
 
-// Used by rbk_attn_fwd (attn.cu) when d_head is 64 or 128 and S % 128 == 0.
+// Used by rbk_attn_fwd (attn.cu) for d_head 64 or 128 and S % 64 == 0.
 template <int HD>
 static int attn_fwd_tc_hd(rbk_ctx* ctx, void* o, float* lse, const void* qkv, int B, int S, int H, float scale,
                           cudaStream_t st) {
@@ -468,7 +474,7 @@ static int attn_fwd_tc_hd(rbk_ctx* ctx, void* o, float* lse, const void* qkv, in
     }
     // persistent: one CTA per resident slot (CTAS_PER_SM per SM, the launch bound), tiles from a
     // device counter that the last CTA re-arms; a CTA that cannot be resident only starts late
-    const int BH = B * H, nqb = S / BQ;
+    const int BH = B * H, nqb = (S + BQ - 1) / BQ;
     const long ntiles = (long)nqb * BH;
     const long slots = (long)ctx->num_sms * FwdCfg<HD>::CTAS_PER_SM;
     const int grid = (int)(ntiles < slots ? ntiles : slots);

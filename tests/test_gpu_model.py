@@ -26,7 +26,9 @@ def rel(a, b, floor=0.0):
 # ------------------------------------------------------------------ attention --
 
 @pytest.mark.parametrize("B,S,H,dh", [(2, 128, 3, 64), (1, 256, 2, 128), (3, 64, 1, 64), (2, 384, 2, 64),
-                                       (1, 512, 3, 64), (2, 384, 2, 128), (1, 192, 2, 128)])
+                                       (1, 512, 3, 64), (2, 384, 2, 128), (1, 192, 2, 128),
+                                       # lengths of 128 k + 64: a half last block (rows past S never stored)
+                                       (2, 320, 2, 64), (3, 64, 2, 128), (2, 576, 3, 128), (4, 192, 1, 64)])
 def test_flash_attention_fwd_bwd(ora, B, S, H, dh):
     from rbk import ops
     rng = np.random.default_rng(S + dh)
@@ -163,6 +165,9 @@ def test_config1_loss_and_grads_match_oracle(ora, ckpt):
 HEADLINE = {
     "gpt2-small-widths": (dict(V=50257, T=1024, D=768, H=12, L=2, FF=3072), 2, 1024),
     "1.3b-layer": (dict(V=50257, T=2048, D=2048, H=16, L=1, FF=8192), 1, 2048),
+    # sequences of 128 k + 64 tokens: the attention kernels' half last block, at both head sizes
+    "tail-192-dh64": (dict(V=4096, T=192, D=256, H=4, L=2, FF=1024), 4, 192),
+    "tail-320-dh128": (dict(V=4096, T=320, D=256, H=2, L=2, FF=1024), 3, 320),
 }
 
 
