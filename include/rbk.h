@@ -78,8 +78,9 @@ int rbk_ctx_profile_read_gemm(rbk_ctx* ctx, double* ms, double* flops, int* laun
 int rbk_ctx_device_error(rbk_ctx* ctx, int* status);
 /* Bitwise-reproducible gradients (default off, or on for every new context when
  * RBK_DETERMINISTIC=1), so two runs on the same inputs give identical bits:
- *   - split-K weight-gradient GEMMs write partial tiles that the last arriving
- *     split adds in split order, instead of FP32 atomics;
+ *   - split-K weight-gradient GEMMs write one FP32 partial plane per split
+ *     (ctx scratch), and a reduction launch adds them to C in split order,
+ *     instead of FP32 atomics;
  *   - the tcgen05 attention backward (S % 128 == 0) adds each query block's dQ
  *     contributions in ascending key-block order (per-block counters).
  * The token-embedding gradient is reproducible in both modes.  No counterpart

@@ -77,10 +77,9 @@ struct rbk_ctx {
     // the descriptor (FP32-accumulating epilogues are weight gradients, an MN-major B a dgrad).
     int gemm_role = -1;
     // Bitwise-reproducible accumulation (rbk_ctx_set_deterministic / RBK_DETERMINISTIC=1):
-    // split-K weight gradients add their partial tiles in split order.
+    // split-K weight gradients add their partial planes in split order, the attention backward
+    // adds dQ in key-block order.
     int deterministic = 0;
-    int* counters = nullptr;   // zeroed device ints for per-tile arrival counts
-    int counters_n = 0;
 };
 
 namespace rbk {
@@ -101,8 +100,6 @@ struct ProfScope {
 // Scratch of at least `bytes` (256-byte aligned); grows (cudaFree + cudaMalloc)
 // only when the current arena is too small.
 int ctx_scratch(rbk_ctx* ctx, size_t bytes, void** out);
-// At least n zeroed device ints that every user leaves zeroed again (grown on demand).
-int ctx_counters(rbk_ctx* ctx, int n, int** out);
 
 // out[c] += sum_r part[r*C + c], deterministic (ctx.cu).
 int column_reduce(float* out, const float* part, int R, int C, cudaStream_t st);

@@ -61,20 +61,6 @@ int ctx_scratch(rbk_ctx* ctx, size_t bytes, void** out) {
     return RBK_OK;
 }
 
-int ctx_counters(rbk_ctx* ctx, int n, int** out) {
-    if (n > ctx->counters_n) {
-        if (ctx->counters) RBK_CUDA(cudaFree(ctx->counters));
-        ctx->counters = nullptr;
-        ctx->counters_n = 0;
-        const int want = n < 4096 ? 4096 : n;
-        RBK_CUDA(cudaMalloc(&ctx->counters, sizeof(int) * (size_t)want));
-        RBK_CUDA(cudaMemset(ctx->counters, 0, sizeof(int) * (size_t)want));
-        ctx->counters_n = want;
-    }
-    *out = ctx->counters;
-    return RBK_OK;
-}
-
 // out[c] += sum_r part[r*C + c]   (deterministic, fixed order over r)
 __global__ void column_reduce_kernel(float* __restrict__ out, const float* __restrict__ part, int R, int C) {
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
@@ -175,7 +161,6 @@ int rbk_ctx_destroy(rbk_ctx* ctx) {
     cudaSetDevice(ctx->device);
     if (ctx->scratch) cudaFree(ctx->scratch);
     if (ctx->tickets) cudaFree(ctx->tickets);
-    if (ctx->counters) cudaFree(ctx->counters);
     for (cudaEvent_t e : ctx->prof.pool) cudaEventDestroy(e);
     delete ctx;
     return RBK_OK;

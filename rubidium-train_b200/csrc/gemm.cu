@@ -126,13 +126,11 @@ struct Params {
     float alpha;
     int* err;
     // Deterministic split K (FP32 accumulating epilogues with splits > 1): every unit stores its
-    // partial tile slab (alpha applied) instead of adding into C; the last unit of a tile to
-    // arrive (per-tile counter) adds the tile's slabs to C in split order.
-    float* part;        // [units][ctas][BM][slab_ld]
-    float* part_rows;   // [units][ctas][BM] row-sum partials (dbias_rows)
-    int* tile_cnt;      // [tiles][ctas], zero between launches (the last arrival resets it)
-    int ctas;           // CTAs per tile: 1, or 2 for CTA pairs
-    int slab_ld;        // columns of a slab (the tile width)
+    // partial tile (alpha applied) into the plane of its split instead of adding into C, and
+    // splitk_reduce_kernel adds the planes to C in split order.
+    float* part;        // [splits][M][ldp]
+    float* part_rows;   // [splits][M] row-sum partials (dbias_rows)
+    int ldp;            // row pitch of a plane (N rounded up to 4)
 };
 
 // PTX helpers (mbarriers, TMA, tcgen05, descriptors) come from tc.cuh.
@@ -224,8 +222,7 @@ __device__ __forceinline__ void row_from_stage_h(const uint8_t* st, int lane, fl
 // pf: this chunk's aux pieces (prefetch_h), used when p.aux is set.
 template <int EPI>
 __device__ __forceinline__ void epilogue_chunk(const Params& p, int m0, int n, const uint32_t* r, uint8_t* st,
-                                               int lane, const uint4* pf, float* slab = nullptr, int mt0 = 0,
-                                               int nt0 = 0) {
+                                               int lane, const uint4* pf, float* plane = nullptr) {
     if (n >= p.N || m0 >= p.M) return;                     // warp-uniform: nothing of this chunk is in C
     float v[32];
 #pragma unroll
@@ -249,16 +246,16 @@ __device__ __forceinline__ void epilogue_chunk(const Params& p, int m0, int n, c
                 const int m = m0 + rr, col = n + 16 * hh + 4 * pc;
                 if (m < p.M && col < p.N) {
                     const float4 f = *reinterpret_cast<const float4*>(st + rr * kStageRow + pc * 16);
-                    float* dst = slab ? slab + (size_t)(m - mt0) * p.slab_ld + (col - nt0) : C + (size_t)m * p.ldc + col;
+                    float* dst = plane ? plane + (size_t)m * p.ldp + col : C + (size_t)m * p.ldc + col;
                     if (col + 4 <= p.N) {
-                        if (EPI == RBK_EPI_ACC_F32 && !slab) red_add_v4(dst, f.x, f.y, f.z, f.w);
+                        if (EPI == RBK_EPI_ACC_F32 && !plane) red_add_v4(dst, f.x, f.y, f.z, f.w);
                         else *reinterpret_cast<float4*>(dst) = f;
                     } else {
                         const float fv[4] = {f.x, f.y, f.z, f.w};
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
                             if (col + e < p.N) {
-                                if (EPI == RBK_EPI_ACC_F32 && !slab) atomicAdd(dst + e, fv[e]);
+                                if (EPI == RBK_EPI_ACC_F32 && !plane) atomicAdd(dst + e, fv[e]);
                                 else dst[e] = fv[e];
                             }
                         }
@@ -316,67 +313,50 @@ __device__ __forceinline__ void epilogue_chunk(const Params& p, int m0, int n, c
     }
 }
 
-// Deterministic split K: after this CTA's 8 epilogue warps have stored unit u's slab, count the
-// arrival; the last of the tile's splits adds every slab to C (and the row-sum partials to
-// dbias_rows) in split order, then resets the counter.  No thread waits on another CTA.  The
-// epilogue warps meet at two mbarriers (8 arrivals each, bounded waits: a warp that left the
-// unit loop on a timeout cannot hang the others).  Returns false on a timeout.
-__device__ bool epi_meet(uint32_t bar, uint32_t parity, int lane, volatile int* abort_flag) {
-    __syncwarp();
-    if (lane == 0) mbar_arrive(bar);
-    return mbar_wait(bar, parity, abort_flag);
-}
-__device__ __noinline__ bool split_finish(const Params& p, int u, int rank, int mt0, int nt0, bool rowsum_tile,
-                                          int eth, volatile int* s_last, uint32_t bar_a, uint32_t bar_b,
-                                          uint32_t parity, volatile int* abort_flag) {
-    const int lane = eth & 31;
-    __threadfence();
-    if (!epi_meet(bar_a, parity, lane, abort_flag)) return false;
-    const int tile = u / p.splits;
-    int* cnt = p.tile_cnt + tile * p.ctas + rank;
-    if (eth == 0) *s_last = atomicAdd(cnt, 1) == p.splits - 1;
-    if (!epi_meet(bar_b, parity, lane, abort_flag)) return false;
-    if (*s_last) {
-        __threadfence();
-        const int ld = p.slab_ld;
-        const size_t sstride = (size_t)p.ctas * BM * ld;           // between the splits of one tile
-        const float* base = p.part + ((size_t)tile * p.splits * p.ctas + rank) * BM * ld;
-        float* C = reinterpret_cast<float*>(p.C);
-        const int q4 = ld >> 2;
-        for (int i = eth; i < BM * q4; i += 256) {
-            const int r = i / q4, c = (i - r * q4) * 4;
-            const int m = mt0 + r, col = nt0 + c;
-            if (m >= p.M || col >= p.N) continue;
-            const float* src = base + (size_t)r * ld + c;
-            float* dst = C + (size_t)m * p.ldc + col;
-            if (col + 4 <= p.N) {
-                float4 a = __ldcg(reinterpret_cast<const float4*>(dst));
-                for (int sp = 0; sp < p.splits; ++sp) {
-                    const float4 b = __ldcg(reinterpret_cast<const float4*>(src + sp * sstride));
-                    a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
-                }
-                *reinterpret_cast<float4*>(dst) = a;
-            } else {
-                for (int e = 0; col + e < p.N; ++e) {
-                    float a = __ldcg(dst + e);
-                    for (int sp = 0; sp < p.splits; ++sp) a += __ldcg(src + sp * sstride + e);
-                    dst[e] = a;
-                }
+// Deterministic split K: C[m, n] += part[0][m][n] + part[1][m][n] + ... in split order (and
+// dbias_rows[m] += the row-sum planes), one thread per 4 columns, all split loads in flight.
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(float* __restrict__ C, int ldc, const float* __restrict__ part,
+                                                            int M, int N, int ldp, int splits, float* __restrict__ dbias,
+                                                            const float* __restrict__ part_rows) {
+    grid_dependency_sync();
+    const size_t plane = (size_t)M * ldp;
+    const int q4 = (N + 3) >> 2;
+    const size_t total = (size_t)M * q4;
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += stride) {
+        const int m = (int)(i / q4), c = (int)(i - (size_t)m * q4) * 4;
+        const float* src = part + (size_t)m * ldp + c;
+        float* dst = C + (size_t)m * ldc + c;
+        if (c + 4 <= N) {
+            float4 a = *reinterpret_cast<const float4*>(dst);
+            int sp = 0;
+            for (; sp + 4 <= splits; sp += 4) {                 // four planes' loads in flight at once
+                float4 b[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) b[j] = __ldcs(reinterpret_cast<const float4*>(src + (sp + j) * plane));
+#pragma unroll
+                for (int j = 0; j < 4; ++j) { a.x += b[j].x; a.y += b[j].y; a.z += b[j].z; a.w += b[j].w; }
+            }
+            for (; sp < splits; ++sp) {
+                const float4 b = __ldcs(reinterpret_cast<const float4*>(src + sp * plane));
+                a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+            }
+            *reinterpret_cast<float4*>(dst) = a;
+        } else {
+            for (int e = 0; c + e < N; ++e) {
+                float a = dst[e];
+                for (int sp = 0; sp < splits; ++sp) a += src[sp * plane + e];
+                dst[e] = a;
             }
         }
-        if (rowsum_tile) {
-            const float* rb = p.part_rows + ((size_t)tile * p.splits * p.ctas + rank) * BM;
-            for (int r = eth; r < BM; r += 256) {
-                const int m = mt0 + r;
-                if (m >= p.M) continue;
-                float a = p.dbias_rows[m];
-                for (int sp = 0; sp < p.splits; ++sp) a += __ldcg(rb + (size_t)sp * p.ctas * BM + r);
-                p.dbias_rows[m] = a;
-            }
-        }
-        if (eth == 0) *cnt = 0;
     }
-    return true;
+    if (dbias) {
+        for (size_t m = blockIdx.x * (size_t)blockDim.x + threadIdx.x; m < (size_t)M; m += stride) {
+            float a = dbias[m];
+            for (int sp = 0; sp < splits; ++sp) a += part_rows[(size_t)sp * M + m];
+            dbias[m] = a;
+        }
+    }
 }
 
 // ----------------------------------------------------------------- kernel ----
@@ -399,8 +379,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     auto tempty_bar = [&](int b) { return bars + 8u * (2 * C::STAGES + 2 + b); };
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbars + 8 * (2 * C::STAGES + 4));
     volatile int* abort_flag = reinterpret_cast<volatile int*>(gbars + 8 * (2 * C::STAGES + 4) + 8);
-    auto split_bar = [&](int i) { return bars + 8u * (2 * C::STAGES + 4) + 16u + 8u * i; };   // 2, after the flag
-    static_assert(8 * (2 * C::STAGES + 4) + 32 <= C::BAR_BYTES, "barrier area");
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -420,8 +398,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             mbar_init(tempty_bar(b), kEpiWarps);
         }
         *abort_flag = 0;
-        mbar_init(split_bar(0), kEpiWarps);
-        mbar_init(split_bar(1), kEpiWarps);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0 && lane == 0) {
@@ -521,13 +497,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         int buf = 0;
         uint32_t bphase = 0;
         const bool det = EPI == RBK_EPI_ACC_F32 && p.part != nullptr;
-        __shared__ int s_last;
-        uint32_t split_phase = 0;
         for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
             int mb, nb, kb0, kb1;
             decode_unit(p, u, mb, nb, kb0, kb1);
             const int m0 = mb * BM + q * 32;
-            float* slab = det ? p.part + (size_t)u * BM * p.slab_ld : nullptr;
+            const int split = u % p.splits;
+            float* plane = det ? p.part + (size_t)split * p.M * p.ldp : nullptr;
             // residual / pre-activation of the first chunk: fetched while the MMAs run
             constexpr bool kAux = EPI == RBK_EPI_STORE_F16 || EPI == RBK_EPI_BIAS_GELU || EPI == RBK_EPI_GELU_BWD;
             const int lda = p.ld_aux ? p.ld_aux : p.ldc;
@@ -544,14 +519,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 uint4 cur[4] = {pf[0], pf[1], pf[2], pf[3]};
                 if (kAux && p.aux && c + 1 < c1) prefetch_h(pf, p.aux, lda, m0, nb * BN + (c + 1) * 32, p, lane);
                 tmem_wait_ld();
-                epilogue_chunk<EPI>(p, m0, nb * BN + c * 32, r, my_stage, lane, cur, slab, mb * BM, nb * BN);
+                epilogue_chunk<EPI>(p, m0, nb * BN + c * 32, r, my_stage, lane, cur, plane);
             }
             const bool rowsum_tile = EPI == RBK_EPI_ACC_F32 && C::ROWSUM_OK && p.dbias_rows && nb == 0;
             if (rowsum_tile && half_id == 0) {
                 const uint32_t v = tmem_ld1(tmem + ((uint32_t)(q * 32) << 16) + C::ACC2_COL + buf * 16);
                 tmem_wait_ld();
                 if (m < p.M) {
-                    if (det) p.part_rows[(size_t)u * BM + q * 32 + lane] = p.alpha * __uint_as_float(v);
+                    if (det) p.part_rows[(size_t)split * p.M + m] = p.alpha * __uint_as_float(v);
                     else atomicAdd(p.dbias_rows + m, p.alpha * __uint_as_float(v));
                 }
             }
@@ -559,10 +534,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             __syncwarp();
             if (lane == 0) mbar_arrive(tempty_bar(buf));
             if (++buf == 2) { buf = 0; bphase ^= 1; }
-            if (det && !split_finish(p, u, 0, mb * BM, nb * BN, rowsum_tile, threadIdx.x - 64, &s_last,
-                                     split_bar(0), split_bar(1), split_phase, abort_flag))
-                break;
-            split_phase ^= 1;
         }
     }
 
@@ -716,8 +687,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto tempty_bar = [&](int b) { return bars + 8u * (2 * STAGES + 2 + b); };
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbars + 8 * (2 * STAGES + 4));
     volatile int* abort_flag = reinterpret_cast<volatile int*>(gbars + 8 * (2 * STAGES + 4) + 8);
-    auto split_bar = [&](int i) { return bars + 8u * (2 * STAGES + 4) + 16u + 8u * i; };   // 2, after the flag
-    static_assert(8 * (2 * STAGES + 4) + 32 <= 256, "barrier area");
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_rank();
@@ -745,8 +714,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(tempty_bar(b), 2 * kEpiWarps);
         }
         *abort_flag = 0;
-        mbar_init(split_bar(0), kEpiWarps);
-        mbar_init(split_bar(1), kEpiWarps);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0 && lane == 0) {
@@ -846,14 +813,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         int buf = 0;
         uint32_t bphase = 0;
         const bool det = EPI == RBK_EPI_ACC_F32 && p.part != nullptr;
-        __shared__ int s_last;
-        uint32_t split_phase = 0;
         for (int u = pair; u < p.units; u += num_pairs) {
             int mb, nb, kb0, kb1;
             decode_unit(p, u, mb, nb, kb0, kb1);
             const int m0 = mb * 2 * BM + (int)rank * BM + q * 32;
-            const int mt0 = mb * 2 * BM + (int)rank * BM;
-            float* slab = det ? p.part + ((size_t)u * 2 + rank) * BM * p.slab_ld : nullptr;
+            const int split = u % p.splits;
+            float* plane = det ? p.part + (size_t)split * p.M * p.ldp : nullptr;
             constexpr bool kAux = EPI == RBK_EPI_STORE_F16 || EPI == RBK_EPI_BIAS_GELU || EPI == RBK_EPI_GELU_BWD;
             const int lda = p.ld_aux ? p.ld_aux : p.ldc;
             uint4 pf[4];
@@ -871,7 +836,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if constexpr (kTma)
                     epilogue_chunk_tma<EPI>(p, m0, nb * BN + c * 32, r, my_stage, my_stage_s, lane, cur, &tmC, &tmX, sc);
                 else
-                    epilogue_chunk<EPI>(p, m0, nb * BN + c * 32, r, my_stage, lane, cur, slab, mt0, nb * BN);
+                    epilogue_chunk<EPI>(p, m0, nb * BN + c * 32, r, my_stage, lane, cur, plane);
             }
             const bool rowsum_tile = kRowsumEpi && rowsum_mode && nb == 0;
             if (rowsum_tile && c0 == 0) {   // one warp per lane quarter
@@ -879,7 +844,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_wait_ld();
                 const int m = m0 + lane;
                 if (m < p.M) {
-                    if (det) p.part_rows[((size_t)u * 2 + rank) * BM + q * 32 + lane] = p.alpha * __uint_as_float(v);
+                    if (det) p.part_rows[(size_t)split * p.M + m] = p.alpha * __uint_as_float(v);
                     else atomicAdd(p.dbias_rows + m, p.alpha * __uint_as_float(v));
                 }
             }
@@ -889,10 +854,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster_relaxed(mapa_shared(tempty_bar(buf), 0));
             if (++buf == nbuf) { buf = 0; bphase ^= 1; }
-            if (det && !split_finish(p, u, (int)rank, mt0, nb * BN, rowsum_tile, threadIdx.x - 64, &s_last,
-                                     split_bar(0), split_bar(1), split_phase, abort_flag))
-                break;
-            split_phase ^= 1;
         }
         if (kTma && lane == 0) bulk_wait0();               // tensor stores complete before exit
     }
@@ -1071,48 +1032,59 @@ int rbk_gemm(rbk_ctx* ctx, const rbk_gemm_desc* d, void* stream) {
     p.err = ctx->tickets + kGemmError;
     p.part = nullptr;
     p.part_rows = nullptr;
-    p.tile_cnt = nullptr;
-    p.ctas = pair ? 2 : 1;
-    p.slab_ld = BN;
-    if (epi == RBK_EPI_ACC_F32 && p.splits > 1 && ctx->deterministic) {
-        // partial slabs of every unit (+ their row sums) and one arrival counter per tile and CTA
-        const size_t slabs = (size_t)p.units * p.ctas;
+    p.ldp = (d->N + 3) & ~3;
+    const bool det = epi == RBK_EPI_ACC_F32 && p.splits > 1 && ctx->deterministic;
+    if (det) {
+        // one FP32 plane per split (+ its row sums), added to C in split order after the GEMM
+        const size_t plane = (size_t)d->M * p.ldp;
         void* ws;
-        RBK_TRY(ctx_scratch(ctx, slabs * BM * (size_t)BN * sizeof(float) + slabs * BM * sizeof(float), &ws));
+        RBK_TRY(ctx_scratch(ctx, sizeof(float) * (p.splits * plane + (size_t)p.splits * d->M), &ws));
         p.part = static_cast<float*>(ws);
-        p.part_rows = p.part + slabs * BM * (size_t)BN;
-        RBK_TRY(ctx_counters(ctx, p.m_blocks * p.n_blocks * p.ctas, &p.tile_cnt));
+        p.part_rows = p.part + p.splits * plane;
     }
     cudaStream_t st = as_stream(stream);
     const int role = ctx->gemm_role >= 0 ? ctx->gemm_role
                      : (epi == RBK_EPI_ACC_F32 || epi == RBK_EPI_STORE_F32) ? 2 : d->b_major ? 1 : 0;
     ProfScope prof(ctx, st, kCatGemm, 2.0 * d->M * (double)d->N * d->K, role);
-    if (pair) {
-        switch (epi) {
-            case RBK_EPI_STORE_F16: return launch_pair<RBK_EPI_STORE_F16>(ctx, d, p, st);
-            case RBK_EPI_BIAS_GELU: return launch_pair<RBK_EPI_BIAS_GELU>(ctx, d, p, st);
-            case RBK_EPI_GELU_BWD: return launch_pair<RBK_EPI_GELU_BWD>(ctx, d, p, st);
-            case RBK_EPI_ACC_F32: return launch_pair<RBK_EPI_ACC_F32>(ctx, d, p, st);
-            default: return launch_pair<RBK_EPI_STORE_F32>(ctx, d, p, st);
+    auto run = [&]() -> int {
+        if (pair) {
+            switch (epi) {
+                case RBK_EPI_STORE_F16: return launch_pair<RBK_EPI_STORE_F16>(ctx, d, p, st);
+                case RBK_EPI_BIAS_GELU: return launch_pair<RBK_EPI_BIAS_GELU>(ctx, d, p, st);
+                case RBK_EPI_GELU_BWD: return launch_pair<RBK_EPI_GELU_BWD>(ctx, d, p, st);
+                case RBK_EPI_ACC_F32: return launch_pair<RBK_EPI_ACC_F32>(ctx, d, p, st);
+                default: return launch_pair<RBK_EPI_STORE_F32>(ctx, d, p, st);
+            }
         }
-    }
-    if (BN == 256) {
-        switch (epi) {
-            case RBK_EPI_STORE_F16: return launch<256, RBK_EPI_STORE_F16>(ctx, d, p, st);
-            case RBK_EPI_BIAS_GELU: return launch<256, RBK_EPI_BIAS_GELU>(ctx, d, p, st);
-            case RBK_EPI_GELU_BWD: return launch<256, RBK_EPI_GELU_BWD>(ctx, d, p, st);
-            case RBK_EPI_ACC_F32: return launch<256, RBK_EPI_ACC_F32>(ctx, d, p, st);
-            default: return launch<256, RBK_EPI_STORE_F32>(ctx, d, p, st);
+        if (BN == 256) {
+            switch (epi) {
+                case RBK_EPI_STORE_F16: return launch<256, RBK_EPI_STORE_F16>(ctx, d, p, st);
+                case RBK_EPI_BIAS_GELU: return launch<256, RBK_EPI_BIAS_GELU>(ctx, d, p, st);
+                case RBK_EPI_GELU_BWD: return launch<256, RBK_EPI_GELU_BWD>(ctx, d, p, st);
+                case RBK_EPI_ACC_F32: return launch<256, RBK_EPI_ACC_F32>(ctx, d, p, st);
+                default: return launch<256, RBK_EPI_STORE_F32>(ctx, d, p, st);
+            }
         }
+        if (BN == 192) return launch<192, RBK_EPI_ACC_F32>(ctx, d, p, st);
+        switch (epi) {
+            case RBK_EPI_STORE_F16: return launch<128, RBK_EPI_STORE_F16>(ctx, d, p, st);
+            case RBK_EPI_BIAS_GELU: return launch<128, RBK_EPI_BIAS_GELU>(ctx, d, p, st);
+            case RBK_EPI_GELU_BWD: return launch<128, RBK_EPI_GELU_BWD>(ctx, d, p, st);
+            case RBK_EPI_ACC_F32: return launch<128, RBK_EPI_ACC_F32>(ctx, d, p, st);
+            default: return launch<128, RBK_EPI_STORE_F32>(ctx, d, p, st);
+        }
+    };
+    RBK_TRY(run());
+    if (det) {
+        const size_t work = (size_t)d->M * ((d->N + 3) / 4);
+        const size_t want = (work + 255) / 256;
+        const int blocks = (int)(want < (size_t)ctx->num_sms * 8 ? want : (size_t)ctx->num_sms * 8);
+        RBK_CUDA(launch_pdl(splitk_reduce_kernel, dim3(blocks), dim3(256), 0, st, (float*)d->C, d->ldc,
+                            (const float*)p.part, d->M, d->N, p.ldp, p.splits, d->dbias_rows,
+                            (const float*)p.part_rows));
+        RBK_LAUNCHED("splitk_reduce_kernel");
     }
-    if (BN == 192) return launch<192, RBK_EPI_ACC_F32>(ctx, d, p, st);
-    switch (epi) {
-        case RBK_EPI_STORE_F16: return launch<128, RBK_EPI_STORE_F16>(ctx, d, p, st);
-        case RBK_EPI_BIAS_GELU: return launch<128, RBK_EPI_BIAS_GELU>(ctx, d, p, st);
-        case RBK_EPI_GELU_BWD: return launch<128, RBK_EPI_GELU_BWD>(ctx, d, p, st);
-        case RBK_EPI_ACC_F32: return launch<128, RBK_EPI_ACC_F32>(ctx, d, p, st);
-        default: return launch<128, RBK_EPI_STORE_F32>(ctx, d, p, st);
-    }
+    return RBK_OK;
 }
 
 int rbk_linear_fwd(rbk_ctx* ctx, void* Y, const void* X, const void* W, const void* bias, const void* residual,

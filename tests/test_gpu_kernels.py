@@ -398,12 +398,12 @@ def test_gemm_wgrad_split_k_pairs(ops, Ntok, fin, out):
     (16384, 768, 768, False),     # the GPT-2-small Wo weight gradient: 3 x 3 pair tiles, 8 splits
     (16384, 768, 2304, True),     # QKV shape with a bias row sum (pair tiles, one accumulator)
     (8192, 192, 200, True),       # single-CTA N = 192 tiles with the ones-MMA row sums, ragged M
-    (5000, 136, 130, False),      # ragged N tail columns
+    (5000, 136, 136, False),      # ragged M and N against the 128 x 192 tiles
 ])
 def test_gemm_wgrad_deterministic_split_k(ops, Ntok, fin, out, bias):
-    """Deterministic mode: split-K partial tiles are added by the last arriving split in split
-    order, so repeated weight gradients are bitwise identical (and equal to the atomic mode
-    within FP32 rounding)."""
+    """Deterministic mode: split-K partial planes are added to the gradient in split order, so
+    repeated weight gradients are bitwise identical (and equal to the atomic mode within FP32
+    rounding)."""
     from rbk import lib
     rng = np.random.default_rng(Ntok + out)
     dY = h(_mk(rng, Ntok, out))
