@@ -81,10 +81,12 @@ int rbk_ctx_device_error(rbk_ctx* ctx, int* status);
  *   - split-K weight-gradient GEMMs write one FP32 partial plane per split
  *     (ctx scratch), and a reduction launch adds them to C in split order,
  *     instead of FP32 atomics;
- *   - the tcgen05 attention backward (S % 128 == 0) adds each query block's dQ
- *     contributions in ascending key-block order (per-block counters).
- * The token-embedding gradient is reproducible in both modes.  No counterpart
- * in the reference. */
+ *   - the tcgen05 attention backward adds each query block's dQ contributions
+ *     in ascending key-block order (per-block counters);
+ *   - the token-embedding gradient sums each token's rows in position order
+ *     after a key sort (up to 32768 positions per call).
+ * Measured cost on the GPT-2-small step: about 7% (the ordered dQ additions
+ * and the split-K reductions).  No counterpart in the reference. */
 int rbk_ctx_set_deterministic(rbk_ctx* ctx, int on);
 
 /* ------------------------------------------------------------------------

@@ -3,12 +3,12 @@
 // Forward fuses embedding_fp16_forward with the per-batch pos_emb scale_add of
 // the reference (src/model.cu:246-248).  Backward: the reference scatters dx
 // into the token table with one atomicAdd per element (src/cuda_kernels.cu:
-// 345-361), whose summation order changes from run to run.  Here the (token,
+// 345-361), whose summation order changes from run to run; so does the default
+// path here (16-byte vector reductions).  In deterministic mode the (token,
 // position) pairs are sorted first and each distinct token's rows are summed in
-// position order by one warp, so the token gradient is bitwise reproducible
-// (up to 32768 positions per call; beyond that, vector reductions as the
-// reference).  pos_emb's gradient (which the reference never computes) is
-// summed over the batch in a fixed order.
+// position order by one warp, so the token gradient is bitwise reproducible (up
+// to 32768 positions per call).  pos_emb's gradient (which the reference never
+// computes) is summed over the batch in a fixed order in both modes.
 #include "common.cuh"
 
 namespace rbk {
@@ -177,8 +177,8 @@ int rbk_embed_bwd(rbk_ctx* ctx, float* dtok, float* dpos, const void* dx, const 
     const int N = B * S;
     cudaStream_t st = as_stream(stream);
     ProfScope prof(ctx, st, kCatEmbed, (double)N * D * (2.0 + 8.0));
-    if (dtok && N <= kSortMaxN && V <= (1 << (32 - kSortIdxBits)) - 1) {
-        // deterministic: sort (token, position), then one writer per table row
+    if (dtok && ctx->deterministic && N <= kSortMaxN && V <= (1 << (32 - kSortIdxBits)) - 1) {
+        // deterministic mode: sort (token, position), then one writer per table row
         int P = 1;
         while (P < N) P <<= 1;
         void* ws;
@@ -192,7 +192,7 @@ int rbk_embed_bwd(rbk_ctx* ctx, float* dtok, float* dpos, const void* dx, const 
                                                                           (const uint32_t*)ws, N, D);
         RBK_LAUNCHED("embed_tok_bwd_sorted_kernel");
     } else if (dtok) {
-        // more than 32768 positions: vector reductions into the table (summation order not fixed)
+        // vector reductions into the table (summation order not fixed; about 4x faster than sorting)
         embed_tok_bwd_kernel<<<grid_for((long)N * (D / 8), ctx->num_sms), 256, 0, st>>>(dtok, (const half*)dx,
                                                                                        tokens, N, D, V);
         RBK_LAUNCHED("embed_tok_bwd_kernel");

@@ -125,13 +125,22 @@ struct Params {
     float* dbias_rows;
     float alpha;
     int* err;
-    // Deterministic split K (FP32 accumulating epilogues with splits > 1): every unit stores its
-    // partial tile (alpha applied) into the plane of its split instead of adding into C, and
-    // splitk_reduce_kernel adds the planes to C in split order.
-    float* part;        // [splits][M][ldp]
-    float* part_rows;   // [splits][M] row-sum partials (dbias_rows)
+    // FP32 accumulation (ACC_F32) without atomics where possible: the units of split 0 own C and
+    // add their tile with plain loads and stores when no other unit writes it concurrently (one
+    // split, or deterministic mode); in deterministic mode the units of split s >= 1 store their
+    // partial tile (alpha applied) into plane s - 1, and splitk_reduce_kernel adds the planes to C
+    // in split order.  Otherwise (several splits, atomic mode) every unit reduce-adds into C.
+    float* part;        // [splits - 1][M][ldp], or nullptr (atomic mode)
+    float* part_rows;   // [splits - 1][M] row-sum partials (dbias_rows)
     int ldp;            // row pitch of a plane (N rounded up to 4)
 };
+
+// How an ACC_F32 unit of split `split` writes its tile.
+enum AccMode { kAccAtomic = 0, kAccOwner = 1, kAccPlane = 2 };
+__device__ __forceinline__ int acc_mode(const Params& p, int split) {
+    if (split == 0 && (p.splits == 1 || p.part)) return kAccOwner;
+    return p.part ? kAccPlane : kAccAtomic;
+}
 
 // PTX helpers (mbarriers, TMA, tcgen05, descriptors) come from tc.cuh.
 using namespace tc;
@@ -222,7 +231,8 @@ __device__ __forceinline__ void row_from_stage_h(const uint8_t* st, int lane, fl
 // pf: this chunk's aux pieces (prefetch_h), used when p.aux is set.
 template <int EPI>
 __device__ __forceinline__ void epilogue_chunk(const Params& p, int m0, int n, const uint32_t* r, uint8_t* st,
-                                               int lane, const uint4* pf, float* plane = nullptr) {
+                                               int lane, const uint4* pf, int mode = kAccAtomic,
+                                               float* plane = nullptr) {
     if (n >= p.N || m0 >= p.M) return;                     // warp-uniform: nothing of this chunk is in C
     float v[32];
 #pragma unroll
@@ -246,16 +256,25 @@ __device__ __forceinline__ void epilogue_chunk(const Params& p, int m0, int n, c
                 const int m = m0 + rr, col = n + 16 * hh + 4 * pc;
                 if (m < p.M && col < p.N) {
                     const float4 f = *reinterpret_cast<const float4*>(st + rr * kStageRow + pc * 16);
-                    float* dst = plane ? plane + (size_t)m * p.ldp + col : C + (size_t)m * p.ldc + col;
+                    const bool pl = EPI == RBK_EPI_ACC_F32 && mode == kAccPlane;
+                    float* dst = pl ? plane + (size_t)m * p.ldp + col : C + (size_t)m * p.ldc + col;
                     if (col + 4 <= p.N) {
-                        if (EPI == RBK_EPI_ACC_F32 && !plane) red_add_v4(dst, f.x, f.y, f.z, f.w);
-                        else *reinterpret_cast<float4*>(dst) = f;
+                        if (EPI == RBK_EPI_ACC_F32 && mode == kAccAtomic) {
+                            red_add_v4(dst, f.x, f.y, f.z, f.w);
+                        } else if (EPI == RBK_EPI_ACC_F32 && mode == kAccOwner) {
+                            float4 o = *reinterpret_cast<const float4*>(dst);
+                            o.x += f.x; o.y += f.y; o.z += f.z; o.w += f.w;
+                            *reinterpret_cast<float4*>(dst) = o;
+                        } else {
+                            *reinterpret_cast<float4*>(dst) = f;
+                        }
                     } else {
                         const float fv[4] = {f.x, f.y, f.z, f.w};
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
                             if (col + e < p.N) {
-                                if (EPI == RBK_EPI_ACC_F32 && !plane) atomicAdd(dst + e, fv[e]);
+                                if (EPI == RBK_EPI_ACC_F32 && mode == kAccAtomic) atomicAdd(dst + e, fv[e]);
+                                else if (EPI == RBK_EPI_ACC_F32 && mode == kAccOwner) dst[e] += fv[e];
                                 else dst[e] = fv[e];
                             }
                         }
@@ -313,8 +332,9 @@ __device__ __forceinline__ void epilogue_chunk(const Params& p, int m0, int n, c
     }
 }
 
-// Deterministic split K: C[m, n] += part[0][m][n] + part[1][m][n] + ... in split order (and
-// dbias_rows[m] += the row-sum planes), one thread per 4 columns, all split loads in flight.
+// Deterministic split K: C[m, n] += part[0][m][n] + part[1][m][n] + ... in plane (split) order,
+// after split 0 has added its own tile (and dbias_rows[m] += the row-sum planes), one thread per
+// 4 columns, four planes' loads in flight.
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(float* __restrict__ C, int ldc, const float* __restrict__ part,
                                                             int M, int N, int ldp, int splits, float* __restrict__ dbias,
                                                             const float* __restrict__ part_rows) {
@@ -496,13 +516,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         uint8_t* my_stage = gbase + (epi_stage - base) + (warp - 2) * kStageBytes;
         int buf = 0;
         uint32_t bphase = 0;
-        const bool det = EPI == RBK_EPI_ACC_F32 && p.part != nullptr;
         for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
             int mb, nb, kb0, kb1;
             decode_unit(p, u, mb, nb, kb0, kb1);
             const int m0 = mb * BM + q * 32;
             const int split = u % p.splits;
-            float* plane = det ? p.part + (size_t)split * p.M * p.ldp : nullptr;
+            const int mode = acc_mode(p, split);
+            float* plane = mode == kAccPlane ? p.part + (size_t)(split - 1) * p.M * p.ldp : nullptr;
             // residual / pre-activation of the first chunk: fetched while the MMAs run
             constexpr bool kAux = EPI == RBK_EPI_STORE_F16 || EPI == RBK_EPI_BIAS_GELU || EPI == RBK_EPI_GELU_BWD;
             const int lda = p.ld_aux ? p.ld_aux : p.ldc;
@@ -519,15 +539,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 uint4 cur[4] = {pf[0], pf[1], pf[2], pf[3]};
                 if (kAux && p.aux && c + 1 < c1) prefetch_h(pf, p.aux, lda, m0, nb * BN + (c + 1) * 32, p, lane);
                 tmem_wait_ld();
-                epilogue_chunk<EPI>(p, m0, nb * BN + c * 32, r, my_stage, lane, cur, plane);
+                epilogue_chunk<EPI>(p, m0, nb * BN + c * 32, r, my_stage, lane, cur, mode, plane);
             }
             const bool rowsum_tile = EPI == RBK_EPI_ACC_F32 && C::ROWSUM_OK && p.dbias_rows && nb == 0;
             if (rowsum_tile && half_id == 0) {
                 const uint32_t v = tmem_ld1(tmem + ((uint32_t)(q * 32) << 16) + C::ACC2_COL + buf * 16);
                 tmem_wait_ld();
                 if (m < p.M) {
-                    if (det) p.part_rows[(size_t)split * p.M + m] = p.alpha * __uint_as_float(v);
-                    else atomicAdd(p.dbias_rows + m, p.alpha * __uint_as_float(v));
+                    const float bv = p.alpha * __uint_as_float(v);
+                    if (mode == kAccPlane) p.part_rows[(size_t)(split - 1) * p.M + m] = bv;
+                    else if (mode == kAccOwner) p.dbias_rows[m] += bv;
+                    else atomicAdd(p.dbias_rows + m, bv);
                 }
             }
             fence_before();
@@ -637,6 +659,71 @@ __device__ __forceinline__ void epilogue_chunk_tma(const Params& p, int m0, int 
     ++sc;
 }
 
+// FP32 epilogues (ACC_F32, STORE_F32) of one 32 x 32 chunk through bulk tensor operations: two
+// 32-row x 16-column halves (64-byte rows, the same 64-byte swizzle as the FP16 tiles) leave
+// through the warp's 2 KB tile, each half as one tensor reduce-add into C (ACC_F32) or one tensor
+// store (STORE_F32, and the split planes of deterministic mode: tmP, a 3-D map [splits][M][ldp]
+// whose z coordinate is the split).  One bulk request per 2 KB instead of 128 per-lane vector
+// reductions; the map's extents clip rows >= M and columns >= N.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* tm, uint32_t src, int x, int y, int z) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(tm),
+                 "r"(src), "r"(x), "r"(y), "r"(z)
+                 : "memory");
+}
+// Row m0 + lane of C, columns n .. n + 31 (the owner's read of the values it adds to), 16 B at a
+// time; rows >= M and columns >= N read as zero.
+__device__ __forceinline__ void load_c_row(float4* cv, const Params& p, int m0, int n, int lane) {
+    const int m = m0 + lane;
+    const float* src = reinterpret_cast<const float*>(p.C) + (size_t)m * p.ldc + n;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int col = n + 4 * k;
+        cv[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (m < p.M && col < p.N) {
+            if (col + 4 <= p.N) {
+                cv[k] = __ldcg(reinterpret_cast<const float4*>(src + 4 * k));
+            } else {
+                float t[4] = {0.f, 0.f, 0.f, 0.f};
+                for (int e = 0; col + e < p.N; ++e) t[e] = src[4 * k + e];
+                cv[k] = make_float4(t[0], t[1], t[2], t[3]);
+            }
+        }
+    }
+}
+
+template <int EPI>
+__device__ __forceinline__ void epilogue_chunk_f32_tma(const Params& p, int m0, int n, const uint32_t* r,
+                                                       uint8_t* st, uint32_t st_s, int lane, const CUtensorMap* tmC,
+                                                       const CUtensorMap* tmP, int split, int mode, const float4* cv) {
+    if (n >= p.N || m0 >= p.M) return;                     // warp-uniform: nothing of this chunk is in C
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {                       // half hh uses tile hh: one operation may stay in flight
+        if (lane == 0) bulk_wait_read1();                  // the tile's previous bulk operation has read it
+        __syncwarp();
+        uint8_t* tile = st + hh * 2048;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int j = 16 * hh + 4 * k;
+            float4 v = make_float4(__uint_as_float(r[j]) * p.alpha, __uint_as_float(r[j + 1]) * p.alpha,
+                                   __uint_as_float(r[j + 2]) * p.alpha, __uint_as_float(r[j + 3]) * p.alpha);
+            if (EPI == RBK_EPI_ACC_F32 && mode == kAccOwner) {
+                const float4 c = cv[4 * hh + k];
+                v.x += c.x; v.y += c.y; v.z += c.z; v.w += c.w;
+            }
+            *reinterpret_cast<float4*>(tile + swoff(lane, k)) = v;
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+            const uint32_t ts = st_s + hh * 2048;
+            if (EPI == RBK_EPI_ACC_F32 && mode == kAccPlane) tma_store_3d(tmP, ts, n + 16 * hh, m0, split - 1);
+            else if (EPI == RBK_EPI_ACC_F32 && mode == kAccAtomic) tma_reduce_add_2d(tmC, ts, n + 16 * hh, m0);
+            else tma_store_2d(tmC, ts, n + 16 * hh, m0);
+            bulk_commit();
+        }
+    }
+}
+
 // ------------------------------------------------------------ CTA pairs ----
 // The same GEMM on CTA pairs (a 2-CTA cluster per pair of SMs): a pair tile is
 // 256 rows x 256 columns.  Each CTA stages its 128 rows of A and its 128
@@ -652,24 +739,26 @@ __device__ __forceinline__ void epilogue_chunk_tma(const Params& p, int m0, int 
 // the MMA thread; tempty[b] lives in the even CTA and takes the arrivals of
 // both CTAs' epilogue warps.  Bounded waits as in gemm_kernel.
 constexpr int kPairStages = 6;
-// Per-warp epilogue staging: two 2 KB tensor-store tiles for FP16 outputs; the
-// FP32 epilogues stage 32 x 80 B and keep a 2 KB ones tile for row sums.
+// Per-warp epilogue staging: two 2 KB tiles for the tensor stores / reduce-adds; the FP32
+// epilogues also keep a 2 KB ones tile for row sums and run one operand stage fewer (their
+// K = tokens mainloops are long).
 template <int EPI>
 struct PairEpi {
     static constexpr bool TMA = EPI == RBK_EPI_STORE_F16 || EPI == RBK_EPI_BIAS_GELU || EPI == RBK_EPI_GELU_BWD;
-    static constexpr int WARP_STAGE = TMA ? kTmaStageBytes : kStageBytes;
+    static constexpr int STAGES = TMA ? kPairStages : kPairStages - 1;
+    static constexpr int WARP_STAGE = kTmaStageBytes;
     static constexpr int ONES_BYTES = EPI == RBK_EPI_ACC_F32 ? 2048 : 0;
-    static constexpr int SMEM = 1024 + kPairStages * (BM * BK * 2 + 128 * BK * 2) + kEpiWarps * WARP_STAGE +
+    static constexpr int SMEM = 1024 + STAGES * (BM * BK * 2 + 128 * BK * 2) + kEpiWarps * WARP_STAGE +
                                 ONES_BYTES + 256;
 };
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmX,
-                     const Params p) {
+                     const __grid_constant__ CUtensorMap tmP, const Params p) {
     constexpr int BN = 256, HALF_N = 128;
     constexpr int A_BYTES = BM * BK * 2, B_BYTES = HALF_N * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
-    constexpr int STAGES = kPairStages;
+    constexpr int STAGES = PairEpi<EPI>::STAGES;
     constexpr bool kTma = EPI == RBK_EPI_STORE_F16 || EPI == RBK_EPI_BIAS_GELU || EPI == RBK_EPI_GELU_BWD;
     constexpr int kWarpStage = PairEpi<EPI>::WARP_STAGE;
     extern __shared__ uint8_t smem_raw[];
@@ -812,17 +901,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         int sc = 0;
         int buf = 0;
         uint32_t bphase = 0;
-        const bool det = EPI == RBK_EPI_ACC_F32 && p.part != nullptr;
         for (int u = pair; u < p.units; u += num_pairs) {
             int mb, nb, kb0, kb1;
             decode_unit(p, u, mb, nb, kb0, kb1);
             const int m0 = mb * 2 * BM + (int)rank * BM + q * 32;
             const int split = u % p.splits;
-            float* plane = det ? p.part + (size_t)split * p.M * p.ldp : nullptr;
+            const int mode = acc_mode(p, split);
             constexpr bool kAux = EPI == RBK_EPI_STORE_F16 || EPI == RBK_EPI_BIAS_GELU || EPI == RBK_EPI_GELU_BWD;
+            constexpr bool kOwn = EPI == RBK_EPI_ACC_F32;        // C values the owner adds to, one chunk ahead
+            const bool own = kOwn && mode == kAccOwner;
             const int lda = p.ld_aux ? p.ld_aux : p.ldc;
             uint4 pf[4];
+            float4 cpf[kOwn ? 8 : 1];
             if (kAux && p.aux) prefetch_h(pf, p.aux, lda, m0, nb * BN + c0 * 32, p, lane);
+            if constexpr (kOwn) {
+                if (own) load_c_row(cpf, p, m0, nb * BN + c0 * 32, lane);
+            }
             if (!mbar_wait(tfull_bar(buf), bphase, abort_flag)) break;
             fence_after();
             const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + buf * BN;
@@ -833,10 +927,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint4 cur[4] = {pf[0], pf[1], pf[2], pf[3]};
                 if (kAux && p.aux && c + 1 < c1) prefetch_h(pf, p.aux, lda, m0, nb * BN + (c + 1) * 32, p, lane);
                 tmem_wait_ld();
-                if constexpr (kTma)
+                if constexpr (kTma) {
                     epilogue_chunk_tma<EPI>(p, m0, nb * BN + c * 32, r, my_stage, my_stage_s, lane, cur, &tmC, &tmX, sc);
-                else
-                    epilogue_chunk<EPI>(p, m0, nb * BN + c * 32, r, my_stage, lane, cur, plane);
+                } else {
+                    float4 cv[kOwn ? 8 : 1];
+                    if constexpr (kOwn) {
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) cv[k] = cpf[k];
+                        if (own && c + 1 < c1) load_c_row(cpf, p, m0, nb * BN + (c + 1) * 32, lane);
+                    }
+                    epilogue_chunk_f32_tma<EPI>(p, m0, nb * BN + c * 32, r, my_stage, my_stage_s, lane, &tmC, &tmP,
+                                                split, mode, cv);
+                }
             }
             const bool rowsum_tile = kRowsumEpi && rowsum_mode && nb == 0;
             if (rowsum_tile && c0 == 0) {   // one warp per lane quarter
@@ -844,8 +946,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_wait_ld();
                 const int m = m0 + lane;
                 if (m < p.M) {
-                    if (det) p.part_rows[(size_t)split * p.M + m] = p.alpha * __uint_as_float(v);
-                    else atomicAdd(p.dbias_rows + m, p.alpha * __uint_as_float(v));
+                    const float bv = p.alpha * __uint_as_float(v);
+                    if (mode == kAccPlane) p.part_rows[(size_t)(split - 1) * p.M + m] = bv;
+                    else if (mode == kAccOwner) p.dbias_rows[m] += bv;
+                    else atomicAdd(p.dbias_rows + m, bv);
                 }
             }
             // the accumulator reads are complete (tcgen05.wait::ld); the tile's global stores need not
@@ -855,7 +959,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) mbar_arrive_cluster_relaxed(mapa_shared(tempty_bar(buf), 0));
             if (++buf == nbuf) { buf = 0; bphase ^= 1; }
         }
-        if (kTma && lane == 0) bulk_wait0();               // tensor stores complete before exit
+        if (lane == 0) bulk_wait0();                       // tensor stores / reduce-adds complete before exit
     }
 
     fence_before();
@@ -899,11 +1003,13 @@ template <int EPI>
 int launch_pair(rbk_ctx* ctx, const rbk_gemm_desc* d, Params& p, cudaStream_t st) {
     constexpr int SMEM = PairEpi<EPI>::SMEM;
     static_assert(SMEM <= 232448, "shared memory budget");
-    CUtensorMap ta, tb, tc_, tx;
-    // FP16 outputs: 32 x 32 store boxes over the logical [M, N] (ldc / ld_aux pitches)
+    CUtensorMap ta, tb, tc_, tx, tp;
+    // FP16 outputs: 32 x 32 store boxes over the logical [M, N] (ldc / ld_aux pitches); FP32
+    // outputs: 16 x 32 boxes (64-byte rows), the split planes of deterministic mode a 3-D map
     constexpr bool kTma = EPI == RBK_EPI_STORE_F16 || EPI == RBK_EPI_BIAS_GELU || EPI == RBK_EPI_GELU_BWD;
     memset(&tc_, 0, sizeof(tc_));
     memset(&tx, 0, sizeof(tx));
+    memset(&tp, 0, sizeof(tp));
     if (kTma) {
         if (d->C)
             RBK_TRY(make_tmap(&tc_, d->C, d->N, d->M, d->ldc, 32, 32, CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
@@ -911,6 +1017,10 @@ int launch_pair(rbk_ctx* ctx, const rbk_gemm_desc* d, Params& p, cudaStream_t st
         if (EPI == RBK_EPI_BIAS_GELU)
             RBK_TRY(make_tmap(&tx, d->aux_out, d->N, d->M, d->ld_aux ? d->ld_aux : d->ldc, 32, 32,
                               CU_TENSOR_MAP_DATA_TYPE_FLOAT16, CU_TENSOR_MAP_SWIZZLE_64B));
+    } else {
+        RBK_TRY(make_tmap(&tc_, d->C, d->N, d->M, d->ldc, 16, 32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                          CU_TENSOR_MAP_SWIZZLE_64B));
+        if (p.part) RBK_TRY(make_tmap_3d(&tp, p.part, d->N, d->M, p.splits - 1, p.ldp, 16, 32));
     }
     if (!d->a_major) RBK_TRY(make_tmap(&ta, d->A, d->K, d->M, d->lda, 64, 128));
     else RBK_TRY(make_tmap(&ta, d->A, d->M, d->K, d->lda, 64, 64));
@@ -939,7 +1049,7 @@ int launch_pair(rbk_ctx* ctx, const rbk_gemm_desc* d, Params& p, cudaStream_t st
     const int pairs = p.units < max_pairs ? p.units : max_pairs;
     cfg.gridDim = dim3(2 * pairs);
     cfg.numAttrs = set_pdl(attr, 1);
-    RBK_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<EPI>, ta, tb, tc_, tx, p));
+    RBK_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<EPI>, ta, tb, tc_, tx, tp, p));
     RBK_LAUNCHED("gemm_pair_kernel");
     return RBK_OK;
 }
@@ -1035,12 +1145,13 @@ int rbk_gemm(rbk_ctx* ctx, const rbk_gemm_desc* d, void* stream) {
     p.ldp = (d->N + 3) & ~3;
     const bool det = epi == RBK_EPI_ACC_F32 && p.splits > 1 && ctx->deterministic;
     if (det) {
-        // one FP32 plane per split (+ its row sums), added to C in split order after the GEMM
+        // one FP32 plane per split after the first (+ its row sums), added to C in split order
+        // after the GEMM; split 0 adds its tile to C itself
         const size_t plane = (size_t)d->M * p.ldp;
         void* ws;
-        RBK_TRY(ctx_scratch(ctx, sizeof(float) * (p.splits * plane + (size_t)p.splits * d->M), &ws));
+        RBK_TRY(ctx_scratch(ctx, sizeof(float) * ((p.splits - 1) * plane + (size_t)(p.splits - 1) * d->M), &ws));
         p.part = static_cast<float*>(ws);
-        p.part_rows = p.part + p.splits * plane;
+        p.part_rows = p.part + (p.splits - 1) * plane;
     }
     cudaStream_t st = as_stream(stream);
     const int role = ctx->gemm_role >= 0 ? ctx->gemm_role
@@ -1080,7 +1191,7 @@ int rbk_gemm(rbk_ctx* ctx, const rbk_gemm_desc* d, void* stream) {
         const size_t want = (work + 255) / 256;
         const int blocks = (int)(want < (size_t)ctx->num_sms * 8 ? want : (size_t)ctx->num_sms * 8);
         RBK_CUDA(launch_pdl(splitk_reduce_kernel, dim3(blocks), dim3(256), 0, st, (float*)d->C, d->ldc,
-                            (const float*)p.part, d->M, d->N, p.ldp, p.splits, d->dbias_rows,
+                            (const float*)p.part, d->M, d->N, p.ldp, p.splits - 1, d->dbias_rows,
                             (const float*)p.part_rows));
         RBK_LAUNCHED("splitk_reduce_kernel");
     }

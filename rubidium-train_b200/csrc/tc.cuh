@@ -409,5 +409,29 @@ inline int make_tmap(CUtensorMap* tm, const void* ptr, uint64_t inner, uint64_t 
     return RBK_OK;
 }
 
+// FP32 [z][y][x] planes of pitch ld (elements) and y extent `rows`: box (box_x, box_y, 1), 64-byte
+// swizzle (the FP32 epilogue tiles).
+inline int make_tmap_3d(CUtensorMap* tm, const void* ptr, uint64_t x, uint64_t rows, uint64_t planes, uint64_t ld,
+                        uint32_t box_x, uint32_t box_y) {
+    auto fn = encode_fn();
+    if (!fn) {
+        set_error("cuTensorMapEncodeTiled unavailable from the driver");
+        return RBK_ERR_CUDA;
+    }
+    cuuint64_t dims[3] = {x, rows, planes};
+    cuuint64_t strides[2] = {ld * 4, ld * 4 * rows};
+    cuuint32_t box[3] = {box_x, box_y, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(ptr), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled (3-D) failed (%d): x=%llu rows=%llu planes=%llu ld=%llu", (int)r,
+                  (unsigned long long)x, (unsigned long long)rows, (unsigned long long)planes, (unsigned long long)ld);
+        return RBK_ERR_CUDA;
+    }
+    return RBK_OK;
+}
+
 }  // namespace tc
 }  // namespace rbk

@@ -225,15 +225,20 @@ def test_embeddings(ops, ora):
 
 @pytest.mark.parametrize("N,V,D", [(16384, 50, 768), (16384, 50257, 768), (1000, 7, 2048), (40000, 300, 64)])
 def test_embed_bwd_reruns_bitwise(ops, ora, N, V, D):
-    """The token gradient is summed per token in position order (sorted keys), so two runs give
-    identical bits, with many repeats of each token; 40000 positions take the reduction path
-    (above the sort's 32768), checked against the oracle only."""
+    """Deterministic mode: the token gradient is summed per token in position order (sorted
+    keys), so two runs give identical bits, with many repeats of each token; 40000 positions take
+    the reduction path (above the sort's 32768), checked against the oracle only."""
+    from rbk import lib
     rng = np.random.default_rng(N + V)
     tokens = rng.integers(0, V, N).astype(np.int32)
     dx = rng.standard_normal((N, D)).astype(np.float16)
     tt, hdx = torch.from_numpy(tokens).cuda(), h(dx)
-    a, _ = ops.embed_bwd(hdx, tt, 1, N, V)
-    b, _ = ops.embed_bwd(hdx, tt, 1, N, V)
+    lib().rbk_ctx_set_deterministic(ops.ctx().handle, 1)
+    try:
+        a, _ = ops.embed_bwd(hdx, tt, 1, N, V)
+        b, _ = ops.embed_bwd(hdx, tt, 1, N, V)
+    finally:
+        lib().rbk_ctx_set_deterministic(ops.ctx().handle, 0)
     if N <= 32768:
         assert torch.equal(a, b)
     et = ora.embed_bwd(dx.astype(np.float32), tokens, V)
