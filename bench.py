@@ -519,10 +519,10 @@ def kernel_loop(name, reps, torch, ops):
 # ------------------------------------------------------------------ GPU leg ----
 
 # Mean DRAM read + write bytes of one GEMM launch of the GPT-2-small step: every GEMM shape
-# of the step captured alone with ncu (dram__bytes_read.sum + dram__bytes_write.sum, one launch
-# each, inputs rotating over more than L2), weighted by that shape's launches per step.  The
-# per-shape figures and the command are in profiles/gemm_backward_shapes_ncu.md.
-GEMM_TRAFFIC_PER_LAUNCH = None
+# of the step captured alone with ncu (dram__bytes_read.sum + dram__bytes_write.sum, inputs
+# rotating over more than L2), weighted by that shape's launches per step (171).  The per-shape
+# figures and the command are in profiles/gemm_shapes_dram.md.
+GEMM_TRAFFIC_PER_LAUNCH = 141.3e6
 
 
 def check_dp(model, tokens, targets, B, S, world, dist, torch):
