@@ -288,22 +288,48 @@ def run_reference(args):
 
 # ------------------------------------------------------------- microbench ----
 
+def graph_time(torch, fn, n):
+    """ms per call of fn(i), i = 0..n-1, from one replay of a CUDA graph holding the n calls, so the
+    host's per-call cost (ctypes, launch) does not pace kernels of a few tens of microseconds.  Three
+    eager warm-up calls first; an eager loop if the calls cannot be captured."""
+    for i in range(3):
+        fn(i)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    try:
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(graph, stream=side):
+                for i in range(n):
+                    fn(i)
+        torch.cuda.current_stream().wait_stream(side)
+        graph.replay()                                  # warm
+        torch.cuda.synchronize()
+        s.record()
+        graph.replay()
+        e.record()
+        torch.cuda.synchronize()
+        del graph
+        return s.elapsed_time(e) / n
+    except RuntimeError:
+        torch.cuda.synchronize()
+    s.record()
+    for i in range(n):
+        fn(i)
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / n
+
+
 def microbench(ops, torch, hbm_peak, reps=20):
     """HBM-bound backward kernels at their configured shapes (GB/s of algorithmic bytes)."""
     res = {}
     dev = "cuda"
 
     def timeit(fn, n=reps):
-        for _ in range(3):
-            fn(0)
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        s.record()
-        for i in range(n):
-            fn(i)
-        e.record()
-        torch.cuda.synchronize()
-        return s.elapsed_time(e) / n
+        return graph_time(torch, fn, n)
 
     g = torch.Generator(device=dev).manual_seed(0)
     # (a) LN backward [16384, 1024]: 4 input sets rotate so the 64 MB per set is not L2-resident
@@ -456,20 +482,23 @@ def kernel_loop(name, reps, torch, ops):
     if name.startswith("gemm"):
         fn, work = gemm_case(name, torch, ops, g)
         unit, peak = "TFLOP/s", tc
-    elif name == "ln_bwd":
-        # four input sets (256 MB) rotate, so x and dy come from DRAM as in the step
-        sets = [(torch.randn(16384, 1024, device="cuda", generator=g).half(),
-                 torch.randn(16384, 1024, device="cuda", generator=g).half()) for _ in range(4)]
-        gam = (1 + 0.02 * torch.randn(1024, device="cuda", generator=g)).half()
-        _, mean, rstd = ops.ln_fwd(sets[0][0], gam, torch.zeros(1024, device="cuda").half())
-        dgam, dbet = torch.zeros(1024, device="cuda"), torch.zeros(1024, device="cuda")
+    elif name == "ln_bwd" or name.startswith("ln_bwd_"):
+        # ln_bwd: [16384, 1024]; ln_bwd_<D>: 2^24 elements of width D.  Four input sets (256 MB)
+        # rotate, so x and dy come from DRAM as in the step.
+        Dl = int(name[7:]) if name != "ln_bwd" else 1024
+        Nl = ((1 << 24) // Dl) // 4 * 4
+        sets = [(torch.randn(Nl, Dl, device="cuda", generator=g).half(),
+                 torch.randn(Nl, Dl, device="cuda", generator=g).half()) for _ in range(4)]
+        gam = (1 + 0.02 * torch.randn(Dl, device="cuda", generator=g)).half()
+        _, mean, rstd = ops.ln_fwd(sets[0][0], gam, torch.zeros(Dl, device="cuda").half())
+        dgam, dbet = torch.zeros(Dl, device="cuda"), torch.zeros(Dl, device="cuda")
         it = [0]
 
         def fn():
             x, dy = sets[it[0] % 4]
             it[0] += 1
             ops.ln_bwd(dy, x, gam, mean, rstd, dgamma=dgam, dbeta=dbet)
-        work, unit, peak = 16384 * 1024 * 6 + 16384 * 8 + 1024 * 10, "GB/s", hbm
+        work, unit, peak = Nl * Dl * 6 + Nl * 8 + Dl * 10, "GB/s", hbm
     elif name == "xent":
         z = (2 * torch.randn(8192, 32000, device="cuda", generator=g)).half()
         t = torch.randint(0, 32000, (8192,), device="cuda", dtype=torch.int32, generator=g)
@@ -500,16 +529,19 @@ def kernel_loop(name, reps, torch, ops):
         work, unit, peak = 34.0 * n, "GB/s", hbm
     else:
         raise SystemExit(f"unknown kernel {name}")
-    for _ in range(3):
-        fn()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    s.record()
-    for _ in range(reps):
-        fn()
-    e.record()
-    torch.cuda.synchronize()
-    ms = s.elapsed_time(e) / reps
+    if os.environ.get("RBK_BENCH_EAGER") == "1" or name.startswith("attn") or name == "adam_tail":
+        for _ in range(3):
+            fn()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        s.record()
+        for _ in range(reps):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e) / reps
+    else:
+        ms = graph_time(torch, lambda i: fn(), reps)
     rate = work / (ms * 1e-3) / (1e12 if unit == "TFLOP/s" else 1e9)
     print(json.dumps({"kernel": name, "ms_per_launch": ms, "achieved": rate, "unit": unit, "peak": peak,
                       "frac": rate / peak}), flush=True)

@@ -473,11 +473,503 @@ __global__ void __launch_bounds__(544, 1)
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// ---------------------------------------------------------------------------
+// The ring backward specialised for D = 2048 (every column owned: D / 8 threads per
+// team, a multiple of 32) with mixed-precision arithmetic, about half the instructions per
+// element of the generic ring kernel, which is issue-bound:
+//   - row sums t1 = sum dy g (exact products: fma.rn.f32.f16) and sum (dy g) x with FP32
+//     accumulation, t2 = sum (dy g)(x - m) = that - m t1 per row (the (dy g) products rounded to
+//     FP16 first; t1 and t2 enter dx only through their row means);
+//   - dx = inv (dy g) - (inv^2 t2 / D) xhat - inv t1 / D in packed FP16 (the output is FP16; every
+//     term is within a small factor of the output's magnitude), xhat = (x - m_hi - m_lo) inv with
+//     the row mean split into two FP16 parts, so x - m keeps full precision for any mean;
+//   - column sums dgamma += dy xhat and dbeta += dy in FP32 from FP32 dy and xhat (the same
+//     arithmetic as the generic kernel, so the weight gradients agree with it to FP32 rounding);
+//     dbias += dx accumulates the FP16 dx in FP32 (add.rn.f32.f16).
+// Same ring, teams, barriers, butterfly and outputs as ln_bwd_ring_kernel.
+__device__ __forceinline__ void mfma2(float& c0, float& c1, uint32_t a, uint32_t b) {
+    asm("{.reg .f16 al, ah, bl, bh;\n\t"
+        "mov.b32 {al, ah}, %2;\n\t"
+        "mov.b32 {bl, bh}, %3;\n\t"
+        "fma.rn.f32.f16 %0, al, bl, %0;\n\t"
+        "fma.rn.f32.f16 %1, ah, bh, %1;}"
+        : "+f"(c0), "+f"(c1)
+        : "r"(a), "r"(b));
+}
+__device__ __forceinline__ void madd2(float& c0, float& c1, uint32_t a) {
+    asm("{.reg .f16 al, ah;\n\t"
+        "mov.b32 {al, ah}, %2;\n\t"
+        "add.rn.f32.f16 %0, al, %0;\n\t"
+        "add.rn.f32.f16 %1, ah, %1;}"
+        : "+f"(c0), "+f"(c1)
+        : "r"(a));
+}
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+template <int D, bool kRefFormula, bool kRes, bool kBias>
+__global__ void __launch_bounds__(D / 8 * (512 / (D / 8) > kLnMaxTeams ? kLnMaxTeams : 512 / (D / 8)) + 32, 1)
+    ln_bwd_mx_kernel(half* __restrict__ dx, float* __restrict__ part, const half* __restrict__ dy,
+                     const half* __restrict__ dres, const half* __restrict__ x, const half* __restrict__ g,
+                     const float* __restrict__ mean, const float* __restrict__ rstd, int N, int stages, int* err) {
+    using namespace tc;
+    constexpr int R = kLnRows;
+    static_assert(R == 4, "the row-sum butterfly below reduces 2 * 4 sums");
+    constexpr int TPT = D / 8;                          // threads per team, one per 8 columns
+    static_assert(TPT % 32 == 0, "whole warps per team");
+    constexpr int TEAMS = 512 / TPT > kLnMaxTeams ? kLnMaxTeams : 512 / TPT;
+    constexpr int WPT = TPT / 32;
+    constexpr int NT = kRes ? 3 : 2;
+    constexpr uint32_t ROW_BYTES = D * 2;
+    constexpr uint32_t STAGE_BYTES = R * ROW_BYTES * NT;
+    constexpr float kInvD = 1.0f / (float)D;
+    extern __shared__ __align__(128) uint8_t lsm_raw[];
+    float* red = reinterpret_cast<float*>(lsm_raw + (size_t)stages * STAGE_BYTES);   // [TEAMS][2][2R][WPT]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(red + TEAMS * 2 * 2 * R * WPT);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * stages);
+    auto full = [&](int s) { return su32(bars + s); };
+    auto empty = [&](int s) { return su32(bars + stages + s); };
+    constexpr int CONSUMERS = TEAMS * TPT;
+    const int tid = threadIdx.x, lane = tid & 31;
+    if (tid == 0) {
+        for (int s = 0; s < stages; ++s) {
+            mbar_init(full(s), 1);
+            mbar_init(empty(s), WPT);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    grid_dependency_wait();
+    const int nstage = (N + R - 1) / R;
+
+    if (tid >= CONSUMERS) {
+        if (tid == CONSUMERS) {                         // producer: one bulk copy per tensor per stage
+            int k = 0;
+            for (int gs = blockIdx.x; gs < nstage; gs += gridDim.x, ++k) {
+                const int s = k % stages;
+                if (!mbar_wait(empty(s), ((k / stages) & 1) ^ 1, abort_flag)) break;
+                const int rows = min(R, N - gs * R);
+                mbar_expect_tx(full(s), (uint32_t)rows * ROW_BYTES * NT);
+                const uint32_t dst = su32(lsm_raw + (size_t)s * STAGE_BYTES);
+                const size_t off = (size_t)gs * R * D;
+                const uint32_t bytes = (uint32_t)rows * ROW_BYTES;
+                bulk_load(dst, dy + off, bytes, full(s));
+                bulk_load(dst + R * ROW_BYTES, x + off, bytes, full(s));
+                if (kRes) bulk_load(dst + 2 * R * ROW_BYTES, dres + off, bytes, full(s));
+            }
+        }
+    } else {
+        const int team = tid / TPT, ttid = tid - team * TPT, twarp = ttid >> 5;
+        uint32_t gam[4];                                // gamma of the thread's 8 columns, FP16 pairs
+        {
+            const uint4 gv = __ldg(reinterpret_cast<const uint4*>(g) + ttid);
+            gam[0] = gv.x; gam[1] = gv.y; gam[2] = gv.z; gam[3] = gv.w;
+        }
+        uint64_t pg[4], pb[4];                          // FP32 pairs: dgamma, dbeta
+        float pd[8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) { pg[j] = 0; pb[j] = 0; }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) pd[j] = 0.f;
+        bool ok = true;
+        const uint32_t ring = su32(lsm_raw);
+        float nmr[R], nrr[R];
+        {
+            const int row0 = (blockIdx.x + team * gridDim.x) * R;
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                nmr[r] = row0 + r < N ? __ldg(mean + row0 + r) : 0.0f;
+                nrr[r] = row0 + r < N ? __ldg(rstd + row0 + r) : 0.0f;
+            }
+        }
+        int it = 0;
+        for (int k = team; blockIdx.x + k * gridDim.x < nstage; k += TEAMS, ++it) {
+            const int gs = blockIdx.x + k * gridDim.x;
+            const int s = k % stages;
+            const int row0 = gs * R;
+            const int nrows = min(R, N - row0);
+            float mr[R], rr[R];
+            const int nrow0 = (blockIdx.x + (k + TEAMS) * gridDim.x) * R;
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                mr[r] = nmr[r];
+                rr[r] = nrr[r];
+                nmr[r] = nrow0 + r < N ? __ldg(mean + nrow0 + r) : 0.0f;
+                nrr[r] = nrow0 + r < N ? __ldg(rstd + nrow0 + r) : 0.0f;
+            }
+            ok = __all_sync(0xffffffffu, ok && mbar_wait(full(s), (k / stages) & 1, abort_flag));
+            const uint32_t sb = ring + (uint32_t)s * STAGE_BYTES + 16u * ttid;
+            // pass 1: per row, t1 = sum dy g and sum (dy g) x over the thread's 8 columns
+            float v8[2 * R];
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                float s1a = 0.f, s1b = 0.f, s2a = 0.f, s2b = 0.f;
+                if (ok && r < nrows) {
+                    const uint4 d = lds128(sb + r * ROW_BYTES);
+                    const uint4 xv = lds128(sb + (R + r) * ROW_BYTES);
+                    const uint32_t dd[4] = {d.x, d.y, d.z, d.w}, xx[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        mfma2(s1a, s1b, dd[j], gam[j]);
+                        mfma2(s2a, s2b, h2u(__hmul2(u2h(dd[j]), u2h(gam[j]))), xx[j]);
+                    }
+                }
+                v8[2 * r] = s1a + s1b;
+                v8[2 * r + 1] = s2a + s2b;
+            }
+            float tot;
+            {
+                const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+                float a4[4], a2[2];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float keep = b4 ? v8[i + 4] : v8[i], send = b4 ? v8[i] : v8[i + 4];
+                    a4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+                }
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    const float keep = b3 ? a4[i + 2] : a4[i], send = b3 ? a4[i] : a4[i + 2];
+                    a2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+                }
+                tot = (b2 ? a2[1] : a2[0]) + __shfl_xor_sync(0xffffffffu, b2 ? a2[0] : a2[1], 4);
+                tot += __shfl_xor_sync(0xffffffffu, tot, 2);
+                tot += __shfl_xor_sync(0xffffffffu, tot, 1);
+            }
+            float* rb = red + ((size_t)team * 2 + (it & 1)) * 2 * R * WPT;
+            if ((lane & 3) == 0) rb[((lane >> 2) & 7) * WPT + twarp] = tot;
+            named_sync(1 + team, TPT);
+            float mine = 0.0f;
+            if (lane < 2 * R) {
+#pragma unroll
+                for (int w = 0; w < WPT; ++w) mine += rb[lane * WPT + w];
+            }
+            float ts[2 * R];
+#pragma unroll
+            for (int q = 0; q < 2 * R; ++q) ts[q] = __shfl_sync(0xffffffffu, mine, q);
+            // pass 2
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                if (ok && r < nrows) {
+                    const float inv = rr[r], m = mr[r];
+                    const float t1 = ts[2 * r], t2 = ts[2 * r + 1] - m * t1;   // sum (dy g)(x - m)
+                    // dx = inv (dy g) + bh xhat + c,  xhat = (x - m) inv
+                    const float bh = -(kRefFormula ? inv : inv * inv) * t2 * kInvD;
+                    const float c = -inv * t1 * kInvD;
+                    const __half mhi = __float2half_rn(m);
+                    const __half mlo = __float2half_rn(m - __half2float(mhi));
+                    const __half2 mhi2 = __halves2half2(mhi, mhi), mlo2 = __halves2half2(mlo, mlo);
+                    const __half2 inv2 = __float2half2_rn(inv), bh2 = __float2half2_rn(bh), c2 = __float2half2_rn(c);
+                    const uint64_t iv2 = pk2(inv, inv), nmi2 = pk2(-m * inv, -m * inv);
+                    const uint4 d = lds128(sb + r * ROW_BYTES);
+                    const uint4 xv = lds128(sb + (R + r) * ROW_BYTES);
+                    uint4 rv = make_uint4(0u, 0u, 0u, 0u);
+                    if (kRes) rv = lds128(sb + (2 * R + r) * ROW_BYTES);
+                    const uint32_t dd[4] = {d.x, d.y, d.z, d.w}, xx[4] = {xv.x, xv.y, xv.z, xv.w};
+                    const uint32_t rs[4] = {rv.x, rv.y, rv.z, rv.w};
+                    uint64_t df[4], xf[4];
+                    h8_to_p(d, df);
+                    h8_to_p(xv, xf);
+                    uint32_t o[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const __half2 xh = __hmul2(__hsub2(__hsub2(u2h(xx[j]), mhi2), mlo2), inv2);
+                        const __half2 dg = __hmul2(u2h(dd[j]), u2h(gam[j]));
+                        __half2 v = __hfma2(inv2, dg, __hfma2(bh2, xh, c2));
+                        if (kRes) v = __hadd2(v, u2h(rs[j]));
+                        o[j] = h2u(v);
+                        pg[j] = pfma2(df[j], pfma2(xf[j], iv2, nmi2), pg[j]);   // dy (x inv - m inv)
+                        pb[j] = padd2(pb[j], df[j]);
+                        if (kBias) madd2(pd[2 * j], pd[2 * j + 1], o[j]);
+                    }
+                    reinterpret_cast<uint4*>(dx + (size_t)(row0 + r) * D)[ttid] = make_uint4(o[0], o[1], o[2], o[3]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty(s));
+        }
+        if (!ok && tid == 0) atomicExch(err, RBK_ERR_TIMEOUT);
+        __syncthreads();
+        float* tpart = reinterpret_cast<float*>(lsm_raw);   // [TEAMS][3][D]
+        float* tp = tpart + (size_t)team * 3 * D + 8 * ttid;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            tp[2 * j] = lo2(pg[j]);
+            tp[2 * j + 1] = hi2(pg[j]);
+            tp[D + 2 * j] = lo2(pb[j]);
+            tp[D + 2 * j + 1] = hi2(pb[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) tp[2 * D + j] = pd[j];
+    }
+    if (tid >= CONSUMERS) __syncthreads();
+    __syncthreads();
+    const float* tpart = reinterpret_cast<const float*>(lsm_raw);
+    for (int i = tid; i < 3 * D; i += blockDim.x) {
+        float v = 0.0f;
+#pragma unroll
+        for (int t = 0; t < TEAMS; ++t) v += tpart[(size_t)t * 3 * D + i];
+        part[(size_t)blockIdx.x * 3 * D + i] = v;
+    }
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// One warp per team for D = 768 and 1024: lane l owns the 8-column groups l, l + 32, ... (CPT =
+// D / 32 columns; consecutive lanes read consecutive 16-byte pieces of a row), so a row's sums
+// reduce inside the warp (no shared-memory exchange, no named barrier) and the per-row scalar
+// work is spread over D / 32 columns per lane instead of 8.  Eight teams take alternate stages of
+// a 4-row ring fed by one producer thread, as in ln_bwd_ring_kernel.  Arithmetic as
+// ln_bwd_mx_kernel (row sums and dx with FP16 operands, FP32 accumulation) except the column sums:
+// dgamma += dy xhat and dbeta += dy in FP32 from FP32 dy and xhat, so they match the FP32 column
+// sums of the generic kernel; dbias += dx from the FP16 dx.
+constexpr int kLnWarpTeams = 8;
+template <int D, bool kRefFormula, bool kRes, bool kBias>
+__global__ void __launch_bounds__(32 * kLnWarpTeams + 32, 1)
+    ln_bwd_warp_kernel(half* __restrict__ dx, float* __restrict__ part, const half* __restrict__ dy,
+                       const half* __restrict__ dres, const half* __restrict__ x, const half* __restrict__ g,
+                       const float* __restrict__ mean, const float* __restrict__ rstd, int N, int stages, int* err) {
+    using namespace tc;
+    constexpr int R = kLnRows;
+    static_assert(R == 4, "the row-sum butterfly below reduces 2 * 4 sums");
+    constexpr int G = D / 256;                          // 8-column groups per lane
+    static_assert(D % 256 == 0 && G <= 4, "D = 256 k, k <= 4");
+    constexpr int TEAMS = kLnWarpTeams;
+    constexpr int NT = kRes ? 3 : 2;
+    constexpr uint32_t ROW_BYTES = D * 2;
+    constexpr uint32_t STAGE_BYTES = R * ROW_BYTES * NT;
+    constexpr float kInvD = 1.0f / (float)D;
+    extern __shared__ __align__(128) uint8_t lsm_raw[];
+    uint64_t* bars = reinterpret_cast<uint64_t*>(lsm_raw + (size_t)stages * STAGE_BYTES);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * stages);
+    auto full = [&](int s) { return su32(bars + s); };
+    auto empty = [&](int s) { return su32(bars + stages + s); };
+    const int tid = threadIdx.x, lane = tid & 31, team = tid >> 5;
+    if (tid == 0) {
+        for (int s = 0; s < stages; ++s) {
+            mbar_init(full(s), 1);
+            mbar_init(empty(s), 1);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    grid_dependency_wait();
+    const int nstage = (N + R - 1) / R;
+
+    if (team == TEAMS) {
+        if (lane == 0) {                                // producer
+            int k = 0;
+            for (int gs = blockIdx.x; gs < nstage; gs += gridDim.x, ++k) {
+                const int s = k % stages;
+                if (!mbar_wait(empty(s), ((k / stages) & 1) ^ 1, abort_flag)) break;
+                const int rows = min(R, N - gs * R);
+                mbar_expect_tx(full(s), (uint32_t)rows * ROW_BYTES * NT);
+                const uint32_t dst = su32(lsm_raw + (size_t)s * STAGE_BYTES);
+                const size_t off = (size_t)gs * R * D;
+                const uint32_t bytes = (uint32_t)rows * ROW_BYTES;
+                bulk_load(dst, dy + off, bytes, full(s));
+                bulk_load(dst + R * ROW_BYTES, x + off, bytes, full(s));
+                if (kRes) bulk_load(dst + 2 * R * ROW_BYTES, dres + off, bytes, full(s));
+            }
+        }
+    } else {
+        uint32_t gam[G][4];
+#pragma unroll
+        for (int q = 0; q < G; ++q) {
+            const uint4 gv = __ldg(reinterpret_cast<const uint4*>(g) + lane + 32 * q);
+            gam[q][0] = gv.x; gam[q][1] = gv.y; gam[q][2] = gv.z; gam[q][3] = gv.w;
+        }
+        uint64_t pg[G][4], pb[G][4];
+        float pd[G][8];
+#pragma unroll
+        for (int q = 0; q < G; ++q) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) { pg[q][j] = 0; pb[q][j] = 0; }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) pd[q][j] = 0.f;
+        }
+        bool ok = true;
+        const uint32_t ring = su32(lsm_raw);
+        float nmr[R], nrr[R];
+        {
+            const int row0 = (blockIdx.x + team * gridDim.x) * R;
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                nmr[r] = row0 + r < N ? __ldg(mean + row0 + r) : 0.0f;
+                nrr[r] = row0 + r < N ? __ldg(rstd + row0 + r) : 0.0f;
+            }
+        }
+        for (int k = team; blockIdx.x + k * gridDim.x < nstage; k += TEAMS) {
+            const int gs = blockIdx.x + k * gridDim.x;
+            const int s = k % stages;
+            const int row0 = gs * R;
+            const int nrows = min(R, N - row0);
+            float mr[R], rr[R];
+            const int nrow0 = (blockIdx.x + (k + TEAMS) * gridDim.x) * R;
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                mr[r] = nmr[r];
+                rr[r] = nrr[r];
+                nmr[r] = nrow0 + r < N ? __ldg(mean + nrow0 + r) : 0.0f;
+                nrr[r] = nrow0 + r < N ? __ldg(rstd + nrow0 + r) : 0.0f;
+            }
+            ok = __all_sync(0xffffffffu, ok && mbar_wait(full(s), (k / stages) & 1, abort_flag));
+            const uint32_t sb = ring + (uint32_t)s * STAGE_BYTES + 16u * lane;
+            float v8[2 * R];
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                float s1a = 0.f, s1b = 0.f, s2a = 0.f, s2b = 0.f;
+                if (ok && r < nrows) {
+#pragma unroll
+                    for (int q = 0; q < G; ++q) {
+                        const uint4 d = lds128(sb + r * ROW_BYTES + 512u * q);
+                        const uint4 xv = lds128(sb + (R + r) * ROW_BYTES + 512u * q);
+                        const uint32_t dd[4] = {d.x, d.y, d.z, d.w}, xx[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            mfma2(s1a, s1b, dd[j], gam[q][j]);
+                            mfma2(s2a, s2b, h2u(__hmul2(u2h(dd[j]), u2h(gam[q][j]))), xx[j]);
+                        }
+                    }
+                }
+                v8[2 * r] = s1a + s1b;
+                v8[2 * r + 1] = s2a + s2b;
+            }
+            // warp totals of the 8 sums (transposed butterfly): lane l ends with sum (l >> 2) & 7
+            float tot;
+            {
+                const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+                float a4[4], a2[2];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float keep = b4 ? v8[i + 4] : v8[i], send = b4 ? v8[i] : v8[i + 4];
+                    a4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+                }
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    const float keep = b3 ? a4[i + 2] : a4[i], send = b3 ? a4[i] : a4[i + 2];
+                    a2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+                }
+                tot = (b2 ? a2[1] : a2[0]) + __shfl_xor_sync(0xffffffffu, b2 ? a2[0] : a2[1], 4);
+                tot += __shfl_xor_sync(0xffffffffu, tot, 2);
+                tot += __shfl_xor_sync(0xffffffffu, tot, 1);
+            }
+            float ts[2 * R];
+#pragma unroll
+            for (int q = 0; q < 2 * R; ++q) ts[q] = __shfl_sync(0xffffffffu, tot, 4 * q);
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                if (ok && r < nrows) {
+                    const float inv = rr[r], m = mr[r];
+                    const float t1 = ts[2 * r], t2 = ts[2 * r + 1] - m * t1;
+                    const float bh = -(kRefFormula ? inv : inv * inv) * t2 * kInvD;
+                    const float c = -inv * t1 * kInvD;
+                    const __half mhi = __float2half_rn(m);
+                    const __half mlo = __float2half_rn(m - __half2float(mhi));
+                    const __half2 mhi2 = __halves2half2(mhi, mhi), mlo2 = __halves2half2(mlo, mlo);
+                    const __half2 inv2 = __float2half2_rn(inv), bh2 = __float2half2_rn(bh), c2 = __float2half2_rn(c);
+                    const uint64_t iv2 = pk2(inv, inv), nmi2 = pk2(-m * inv, -m * inv);
+                    half* dxr = dx + (size_t)(row0 + r) * D;
+#pragma unroll
+                    for (int q = 0; q < G; ++q) {
+                        const uint4 d = lds128(sb + r * ROW_BYTES + 512u * q);
+                        const uint4 xv = lds128(sb + (R + r) * ROW_BYTES + 512u * q);
+                        uint4 rv = make_uint4(0u, 0u, 0u, 0u);
+                        if (kRes) rv = lds128(sb + (2 * R + r) * ROW_BYTES + 512u * q);
+                        const uint32_t dd[4] = {d.x, d.y, d.z, d.w}, xx[4] = {xv.x, xv.y, xv.z, xv.w};
+                        const uint32_t rs[4] = {rv.x, rv.y, rv.z, rv.w};
+                        uint64_t df[4], xf[4];
+                        h8_to_p(d, df);
+                        h8_to_p(xv, xf);
+                        uint32_t o[4];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const __half2 xh = __hmul2(__hsub2(__hsub2(u2h(xx[j]), mhi2), mlo2), inv2);
+                            const __half2 dg = __hmul2(u2h(dd[j]), u2h(gam[q][j]));
+                            __half2 v = __hfma2(inv2, dg, __hfma2(bh2, xh, c2));
+                            if (kRes) v = __hadd2(v, u2h(rs[j]));
+                            o[j] = h2u(v);
+                            pg[q][j] = pfma2(df[j], pfma2(xf[j], iv2, nmi2), pg[q][j]);   // dy (x inv - m inv)
+                            pb[q][j] = padd2(pb[q][j], df[j]);
+                            if (kBias) madd2(pd[q][2 * j], pd[q][2 * j + 1], o[j]);
+                        }
+                        reinterpret_cast<uint4*>(dxr)[lane + 32 * q] = make_uint4(o[0], o[1], o[2], o[3]);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty(s));
+        }
+        if (!ok && lane == 0) atomicExch(err, RBK_ERR_TIMEOUT);
+        __syncthreads();                                // the ring is consumed: reuse it for the partials
+        float* tp = reinterpret_cast<float*>(lsm_raw) + (size_t)team * 3 * D;
+#pragma unroll
+        for (int q = 0; q < G; ++q) {
+            const int c0 = 8 * (lane + 32 * q);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                tp[c0 + 2 * j] = lo2(pg[q][j]);
+                tp[c0 + 2 * j + 1] = hi2(pg[q][j]);
+                tp[D + c0 + 2 * j] = lo2(pb[q][j]);
+                tp[D + c0 + 2 * j + 1] = hi2(pb[q][j]);
+                tp[2 * D + c0 + 2 * j] = pd[q][2 * j];
+                tp[2 * D + c0 + 2 * j + 1] = pd[q][2 * j + 1];
+            }
+        }
+    }
+    if (team == TEAMS) __syncthreads();
+    __syncthreads();
+    const float* tpart = reinterpret_cast<const float*>(lsm_raw);
+    for (int i = tid; i < 3 * D; i += blockDim.x) {
+        float v = 0.0f;
+#pragma unroll
+        for (int t = 0; t < TEAMS; ++t) v += tpart[(size_t)t * 3 * D + i];
+        part[(size_t)blockIdx.x * 3 * D + i] = v;
+    }
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// cudaFuncSetAttribute once per (kernel, device, size): on every launch it would cost host time
+// comparable to these kernels' own duration.
+int ensure_smem(const void* fn, size_t smem) {
+    static std::mutex mu;
+    static std::vector<std::tuple<const void*, int, size_t>> done;
+    int dev = 0;
+    RBK_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(mu);
+    for (const auto& t : done)
+        if (std::get<0>(t) == fn && std::get<1>(t) == dev && std::get<2>(t) >= smem) return RBK_OK;
+    RBK_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    done.emplace_back(fn, dev, smem);
+    return RBK_OK;
+}
+
+template <int D, bool A, bool B, bool C>
+int launch_bwd_warp(int blocks, int stages, size_t smem, cudaStream_t st, half* dx, float* part, const half* dy,
+                    const half* dres, const half* x, const half* g, const float* mean, const float* rstd, int N,
+                    int* err) {
+    RBK_TRY(ensure_smem((const void*)ln_bwd_warp_kernel<D, A, B, C>, smem));
+    RBK_CUDA(launch_pdl(ln_bwd_warp_kernel<D, A, B, C>, dim3(blocks), dim3(32 * kLnWarpTeams + 32), smem, st, dx, part,
+                        dy, dres, x, g, mean, rstd, N, stages, err));
+    return RBK_OK;
+}
+
+template <int D, bool A, bool B, bool C>
+int launch_bwd_mx(int blocks, int threads, int stages, size_t smem, cudaStream_t st, half* dx, float* part,
+                  const half* dy, const half* dres, const half* x, const half* g, const float* mean, const float* rstd,
+                  int N, int* err) {
+    RBK_TRY(ensure_smem((const void*)ln_bwd_mx_kernel<D, A, B, C>, smem));
+    RBK_CUDA(launch_pdl(ln_bwd_mx_kernel<D, A, B, C>, dim3(blocks), dim3(threads), smem, st, dx, part, dy, dres, x, g,
+                        mean, rstd, N, stages, err));
+    return RBK_OK;
+}
+
 template <bool A, bool B, bool C>
 int launch_bwd_ring(int blocks, int threads, int teams, int tpt, int stages, size_t smem, cudaStream_t st, half* dx,
                     float* part, const half* dy, const half* dres, const half* x, const half* g, const float* mean,
                     const float* rstd, int N, int D, int* err) {
-    RBK_CUDA(cudaFuncSetAttribute(ln_bwd_ring_kernel<A, B, C>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    RBK_TRY(ensure_smem((const void*)ln_bwd_ring_kernel<A, B, C>, smem));
     RBK_CUDA(launch_pdl(ln_bwd_ring_kernel<A, B, C>, dim3(blocks), dim3(threads), smem, st, dx, part, dy, dres, x, g,
                         mean, rstd, N, D, teams, tpt, stages, err));
     return RBK_OK;
@@ -587,6 +1079,50 @@ int rbk_ln_bwd(rbk_ctx* ctx, void* dx, float* dgamma, float* dbeta, float* dbias
     auto X = (const half*)x;
     auto G = (const half*)gamma;
     int* err = ctx->tickets + kGemmError;
+    static const bool generic_only = [] {
+        const char* e = getenv("RBK_LN_GENERIC");
+        return e && e[0] == '1';
+    }();
+    if (!generic_only && (D == 768 || D == 1024)) {
+        // one warp per team: its own ring depth (the stage is 4 rows of every tensor)
+        const size_t wstage = (size_t)kLnRows * D * 2 * (dres ? 3 : 2);
+        int wst = (int)((200u << 10) / wstage);
+        wst = wst > 16 ? 16 : wst;
+        const size_t wsmem = wst * wstage + 16 * (size_t)wst + 16;
+        RBK_REQUIRE(wsmem >= sizeof(float) * 3 * (size_t)D * kLnWarpTeams, "rbk_ln_bwd: partial area");
+#define RBK_LN_W(D_, R_, S_, B_) \
+    RBK_TRY((launch_bwd_warp<D_, R_, S_, B_>(blocks, wst, wsmem, st, DX, part, DY, DR, X, G, mean, rstd, N, err)))
+#define RBK_LN_W_D(D_)                                                                                        \
+    if (ref) {                                                                                                \
+        if (res) { if (bias) RBK_LN_W(D_, true, true, true); else RBK_LN_W(D_, true, true, false); }           \
+        else { if (bias) RBK_LN_W(D_, true, false, true); else RBK_LN_W(D_, true, false, false); }            \
+    } else {                                                                                                  \
+        if (res) { if (bias) RBK_LN_W(D_, false, true, true); else RBK_LN_W(D_, false, true, false); }         \
+        else { if (bias) RBK_LN_W(D_, false, false, true); else RBK_LN_W(D_, false, false, false); }          \
+    }
+        if (D == 768) { RBK_LN_W_D(768) }
+        else { RBK_LN_W_D(1024) }
+#undef RBK_LN_W_D
+#undef RBK_LN_W
+        RBK_LAUNCHED("ln_bwd_warp_kernel");
+    } else if (!generic_only && D == 2048) {
+        // the specialised mixed-precision kernel: same teams, ring and launch shape
+#define RBK_LN_MX(D_, R_, S_, B_)                                                                                \
+    RBK_TRY((launch_bwd_mx<D_, R_, S_, B_>(blocks, threads, stages, smem, st, DX, part, DY, DR, X, G, mean, rstd, N, \
+                                           err)))
+#define RBK_LN_MX_D(D_)                                                                                       \
+    if (ref) {                                                                                                \
+        if (res) { if (bias) RBK_LN_MX(D_, true, true, true); else RBK_LN_MX(D_, true, true, false); }         \
+        else { if (bias) RBK_LN_MX(D_, true, false, true); else RBK_LN_MX(D_, true, false, false); }          \
+    } else {                                                                                                  \
+        if (res) { if (bias) RBK_LN_MX(D_, false, true, true); else RBK_LN_MX(D_, false, true, false); }       \
+        else { if (bias) RBK_LN_MX(D_, false, false, true); else RBK_LN_MX(D_, false, false, false); }        \
+    }
+        RBK_LN_MX_D(2048)
+#undef RBK_LN_MX_D
+#undef RBK_LN_MX
+        RBK_LAUNCHED("ln_bwd_mx_kernel");
+    } else {
 #define RBK_LN_BWD(R_, S_, B_)                                                                                  \
     RBK_TRY((launch_bwd_ring<R_, S_, B_>(blocks, threads, teams, tpt, stages, smem, st, DX, part, DY, DR, X, G, \
                                          mean, rstd, N, D, err)))
@@ -599,6 +1135,7 @@ int rbk_ln_bwd(rbk_ctx* ctx, void* dx, float* dgamma, float* dbeta, float* dbias
     }
 #undef RBK_LN_BWD
     RBK_LAUNCHED("ln_bwd_ring_kernel");
+    }
     {
         // programmatic dependent launch: the reduce's launch overlaps the main pass's tail
         cudaLaunchConfig_t lc = {};

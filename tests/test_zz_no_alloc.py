@@ -74,7 +74,9 @@ def test_noalloc_ln_bwd_matches_ctx_entry_point_twice():
         assert rel(got[0].float(), ref[0].float()) < F16_TOL, f"dx, call {call}"
         assert rel(got[1], ref[1]) < F32_TOL and rel(got[2], ref[2]) < F32_TOL, f"dgamma/dbeta, call {call}"
         if bias:
-            assert rel(got[3], ref[3]) < F32_TOL, f"dbias, call {call}"
+            # dbias sums the FP16 dx that each kernel rounds on its own (the ctx entry point computes
+            # dx in FP16 arithmetic at D = 768 / 1024 / 2048), and the rows' dx cancel in the sum
+            assert rel(got[3], ref[3]) < 2e-3, f"dbias, call {call}"
         if call == 0:
             # the CPU oracle (src/cpu_mat.h:126-153 with the exact dx) on the same FP16 inputs
             import oracle
