@@ -499,6 +499,19 @@ def kernel_loop(name, reps, torch, ops):
             it[0] += 1
             ops.ln_bwd(dy, x, gam, mean, rstd, dgamma=dgam, dbeta=dbet)
         work, unit, peak = Nl * Dl * 6 + Nl * 8 + Dl * 10, "GB/s", hbm
+    elif name.startswith("ln_fwd_"):
+        # LayerNorm forward over 2^24 elements of width D, four input sets rotating (256 MB)
+        Dl = int(name[7:])
+        Nl = ((1 << 24) // Dl) // 4 * 4
+        xs = [torch.randn(Nl, Dl, device="cuda", generator=g).half() for _ in range(4)]
+        gam = (1 + 0.02 * torch.randn(Dl, device="cuda", generator=g)).half()
+        bet = (0.02 * torch.randn(Dl, device="cuda", generator=g)).half()
+        it = [0]
+
+        def fn():
+            ops.ln_fwd(xs[it[0] % 4], gam, bet)
+            it[0] += 1
+        work, unit, peak = Nl * Dl * 4 + Nl * 8 + Dl * 4, "GB/s", hbm
     elif name == "xent":
         z = (2 * torch.randn(8192, 32000, device="cuda", generator=g)).half()
         t = torch.randint(0, 32000, (8192,), device="cuda", dtype=torch.int32, generator=g)
@@ -562,7 +575,9 @@ def check_dp(model, tokens, targets, B, S, world, dist, torch):
     own model: (1) two micro-steps without all-reduce give this rank's local sum L; (2) the
     same two micro-steps with the second all-reducing (gradient accumulation) give G.  G must
     equal the plain sum over ranks of L (an independent NCCL all-reduce of L) and be
-    bit-identical on every rank (a checksum of its bits, gathered)."""
+    bit-identical on every rank (a checksum of its bits, gathered).  Under the sharded optimizer
+    each rank holds the sum on its own slices only (the rest is zero): G is compared there, and
+    the ranks must agree bit for bit on the weights after one optimizer step."""
     g2 = torch.roll(targets, 1, dims=1)               # a second micro-batch
     model.grad.zero_()
     with model.no_sync():
@@ -579,23 +594,41 @@ def check_dp(model, tokens, targets, B, S, world, dist, torch):
     torch.cuda.synchronize()
     G = model.grad
     dist.all_reduce(local, op=dist.ReduceOp.SUM)
-    rel = float((G - local).norm() / local.norm().clamp_min(1e-30))
-    bits = G.view(torch.int32).to(torch.int64)
+    ranges = model.dp_shard_ranges()
+    if ranges:
+        own = torch.zeros(G.numel(), dtype=torch.bool, device=G.device)
+        for b, e in ranges:
+            own[b:e] = True
+        err2 = torch.stack([((G - local) * own).norm() ** 2, (local * own).norm() ** 2])
+        dist.all_reduce(err2, op=dist.ReduceOp.SUM)       # over the union of the slices: the arena
+        rel = float(err2[0].sqrt() / err2[1].sqrt().clamp_min(1e-30))
+        finite = bool(torch.isfinite(G).all()) and int(torch.count_nonzero(G * ~own)) == 0
+        model.optimizer_step(0, 1e-4)
+        model.dp_gather_state()
+        torch.cuda.synchronize()
+        what = torch.cat([model.p16.view(torch.int16).to(torch.int32), model.p32.view(torch.int32)])
+        del own
+    else:
+        rel = float((G - local).norm() / local.norm().clamp_min(1e-30))
+        finite = bool(torch.isfinite(G).all())
+        what = G.view(torch.int32)
+    bits = what.to(torch.int64)
     idx = torch.arange(bits.numel(), device=bits.device, dtype=torch.int64) % 1000003 + 1
-    cs = torch.stack([(bits * idx).sum(), G.double().sum().view(torch.int64)])
+    cs = torch.stack([(bits * idx).sum(), bits.sum()])
     allcs = [torch.zeros_like(cs) for _ in range(world)]
     dist.all_gather(allcs, cs)
     agree = all(bool(torch.equal(c, allcs[0])) for c in allcs)
-    finite = bool(torch.isfinite(G).all())
     model.grad.zero_()
-    del local
+    del local, bits, idx, what
     torch.cuda.synchronize()
     # tolerance: two backwards of the same inputs differ by FP32 accumulation-order noise that FP16
     # roundings carry forward (measured ~2e-4); the schedule error this guards against is O(1)
     return {"ga": 2, "ranks_bitwise_equal": agree, "checksum": int(allcs[0][0]), "finite": finite,
             "rel_l2_vs_allreduce_of_local_sums": rel, "tolerance": 2e-3, "ok": agree and finite and rel < 2e-3,
+            "sharded_optimizer": bool(ranges),
             "how": "grad after 2 micro-steps (the 1st without all-reduce) vs an independent all-reduce "
-                   "of each rank's 2-micro-step local sum; bit checksums gathered from every rank"}
+                   "of each rank's 2-micro-step local sum (sharded: on each rank's slices); bit checksums "
+                   "gathered from every rank (sharded: of the FP16 and FP32 weights after one optimizer step)"}
 
 
 def run_workload(name, args, world, rank, local, dist, torch, steps, warmup, e2e=True, profile=True,
@@ -621,7 +654,7 @@ def run_workload(name, args, world, rank, local, dist, torch, steps, warmup, e2e
     if world > 1:
         uid = [dp_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
-        model.dp_init(rank, world, uid[0], int(args.bucket_mb * (1 << 20)))
+        model.dp_init(rank, world, uid[0], int(args.bucket_mb * (1 << 20)), shard=args.dp_shard and not lora)
 
     g = torch.Generator(device="cuda").manual_seed(1234 + rank)
     tokens = torch.randint(0, cfg["V"], (B, S), device="cuda", dtype=torch.int32, generator=g)
@@ -694,6 +727,11 @@ def run_workload(name, args, world, rank, local, dist, torch, steps, warmup, e2e
            "gemm_flops_per_step": gemm_flops_per_step(cfg, ntok, ckpt, bool(lora))}
     if world > 1:
         res["allreduce_bytes_per_step"] = 4 * (model.lora_tensors("grad")[0].numel() * 4 if lora else model.nparams)
+        res["sharded_optimizer"] = bool(args.dp_shard and not lora)
+        if res["sharded_optimizer"]:   # FP32 gradients reduce-scattered, FP16 weights all-gathered
+            res["allreduce_bytes_per_step"] = 0
+            res["reduce_scatter_bytes_per_step"] = 4 * model.nparams
+            res["all_gather_bytes_per_step"] = 2 * model.nparams
 
     # ---------------- profiled pass: per-launch events for the kernel split ----
     if profile:
@@ -789,6 +827,9 @@ def main():
     ap.add_argument("--no-1p3b", action="store_true", help="skip the second (1.3B) workload pass")
     ap.add_argument("--steps-1p3b", type=int, default=5)
     ap.add_argument("--bucket-mb", type=float, default=25.0)
+    ap.add_argument("--dp-shard", type=int, default=int(os.environ.get("RBK_DP_SHARD", "0")),
+                    help="1: sharded optimizer under data parallelism (reduce-scatter, the tail on each rank's "
+                         "slices, FP16 all-gather); 0: all-reduce and the whole tail on every rank")
     ap.add_argument("--kernel", default=None,
                     help="loop one kernel instead of the training step (gemm_* of gemm_shapes(), ln_bwd, xent, "
                          "attn_fwd, attn_bwd, adam_tail)")
@@ -864,7 +905,8 @@ def main():
             "loss_scale": head["loss_scale"],
             "skipped_steps": head["skipped_steps"],
         }
-        for k in ("dp_check", "allreduce_bytes_per_step", "lora"):
+        for k in ("dp_check", "allreduce_bytes_per_step", "reduce_scatter_bytes_per_step", "all_gather_bytes_per_step",
+                  "sharded_optimizer", "lora"):
             if k in head:
                 out[k] = head[k]
         if others:

@@ -89,6 +89,18 @@ int rbk_ctx_device_error(rbk_ctx* ctx, int* status);
  * and the split-K reductions).  No counterpart in the reference. */
 int rbk_ctx_set_deterministic(rbk_ctx* ctx, int on);
 
+/* Test only: arms the next rbk_adam_tail launch on this context (one launch; the
+ * setting is cleared when it is used).  Its grid-barrier wait gives up after
+ * limit_s seconds (1e-4 .. 2; the default is 2 s) and CTA `withheld_cta` does
+ * not arrive at the barrier (-1: every CTA arrives; larger than the grid: the
+ * last CTA), so that the bounded wait runs out on a healthy GPU.  The launch
+ * then returns as for a timeout in production: the step is skipped like an
+ * overflow step (masters and moments untouched, gradients zeroed, scale halved)
+ * and rbk_scaler.status = RBK_ERR_TIMEOUT; the next launch runs normally.
+ * It exercises the failure path of the bounded device waits without a GPU
+ * fault.  No counterpart in the reference. */
+int rbk_ctx_arm_tail_timeout_test(rbk_ctx* ctx, double limit_s, int withheld_cta);
+
 /* ------------------------------------------------------------------------
  * LayerNorm
  * ------------------------------------------------------------------------ */
@@ -404,9 +416,17 @@ int rbk_model_forward(rbk_model* m, const int* tokens, const int* targets, int B
  *   loss * grad_scale * scaler.scale
  * into the gradient arena (grad_scale is the reference's loss_scale argument,
  * 1/(BS*GA) in src/main.cpp:158; pass 1 for the plain mean).  Must follow a
- * forward on the same tokens. */
+ * forward on the same tokens.  The arena is the library's between calls: while
+ * it is known to hold zeros (after rbk_model_create, rbk_model_init_weights,
+ * rbk_model_zero_grad or an optimizer step, which zeroes it) the weight-gradient
+ * GEMMs store their tiles instead of reading and adding, so values written into
+ * it through rbk_model_buffer after one of those calls are overwritten, not
+ * added to.  A caller that zeroes the arena itself uses rbk_model_zero_grad. */
 int rbk_model_backward(rbk_model* m, const int* tokens, const int* targets, int B, int S, float grad_scale,
                        void* stream);
+/* Zero the gradient arena on `stream` (what the reference's backward does at
+ * entry, src/model.cu:325-340; here the optimizer step already does it). */
+int rbk_model_zero_grad(rbk_model* m, void* stream);
 /* Training (1, default) / eval (0) mode, see rbk_model_forward. */
 int rbk_model_set_training(rbk_model* m, int training);
 /* optimizer_step (src/model.h:132) fused with the overflow check, unscale,
@@ -458,6 +478,17 @@ typedef struct rbk_dp_opts {
                                NCCL leaves SMs to the GEMM grids (0: NCCL's default); the
                                last bucket, reduced after the backward, is not capped  */
     double timeout_s;       /* watchdog deadline per collective (<= 0: 300 s)            */
+    int shard_optimizer;    /* 1: sharded optimizer.  Each bucket is reduce-scattered (not
+                               all-reduced): rank r receives the summed gradients of the r-th
+                               1/world slice of every bucket and runs the optimizer tail on
+                               those slices only; the updated FP16 weights are all-gathered
+                               bucket by bucket, overlapped with the next forward, which waits
+                               for each bucket before its first use.  FP32 masters and Adam
+                               moments then hold this rank's slices only until
+                               rbk_model_dp_gather_state (called by rbk_model_save and
+                               rbk_model_sync_fp16).  Needs every bucket length to divide into
+                               world slices of a multiple of 4 elements (world = 1, 2, 4, 8, 16).
+                               0: every rank all-reduces and updates the whole arena.          */
 } rbk_dp_opts;
 /* rbk_model_dp_init with explicit options.  The communicators are non-blocking
  * (ncclCommInitRankConfig, blocking = 0) and watched by a host thread: a
@@ -473,6 +504,12 @@ int rbk_model_dp_status(rbk_model* m);
  * leaves the job calls it instead of a shutdown its peers would have to join;
  * afterwards the model behaves as after a watchdog abort (RBK_ERR_NCCL). */
 int rbk_model_dp_abort(rbk_model* m);
+/* Sharded optimizer: *count = number of [begin, end) arena ranges this rank
+ * updates (0 when not sharded); out[2i], out[2i+1] = range i, for i < max. */
+int rbk_model_dp_shard_ranges(rbk_model* m, int64_t* out, int max, int* count);
+/* Sharded optimizer: all-gather the FP32 masters and Adam moments on `stream`
+ * so every rank holds all of them again (a no-op when they are whole). */
+int rbk_model_dp_gather_state(rbk_model* m, void* stream);
 /* Gradient accumulation under data parallelism (the reference accumulates GA
  * micro-steps per optimizer step, src/main.cpp:136-164).  sync = 0: following
  * backwards only accumulate this rank's gradients, no all-reduce; sync = 1

@@ -47,6 +47,15 @@ struct TailParams {
     int t;
     rbk_scaler* sc;
     int* flags;               // ctx tickets
+    uint64_t wait_ns;         // grid-barrier wait limit
+    int withheld_cta;         // test only: this CTA does not arrive (-1: none)
+    // 3: both phases in one cooperative launch (grid barrier between them).  1 / 2: one phase
+    // per launch, for the sharded optimizer: phase 1 leaves its results in xbuf ([0] = 1 if a
+    // gradient was non-finite, [1 + s] = segment s's sum of squares), the caller sums xbuf
+    // over the ranks, phase 2 reads the sums.
+    int phases;
+    float* xbuf;
+    int nseg;
 };
 
 __device__ __forceinline__ void chunk_range(const TailParams& P, int c, int64_t& s, int& len, int& seg) {
@@ -78,7 +87,7 @@ __global__ void __launch_bounds__(512, 2) adam_tail_kernel(TailParams P) {
     if (tid == 0) s_flag = 0;
     __syncthreads();
     int bad = 0;
-    for (int c = blockIdx.x; c < P.nchunks; c += gridDim.x) {
+    for (int c = blockIdx.x; (P.phases & 1) && c < P.nchunks; c += gridDim.x) {
         int64_t s;
         int len, seg;
         chunk_range(P, c, s, len, seg);
@@ -116,13 +125,39 @@ __global__ void __launch_bounds__(512, 2) adam_tail_kernel(TailParams P) {
     }
     if (__syncthreads_or(bad) && tid == 0) atomicOr(overflow, 1);
 
-    // ---------------- bounded grid barrier ----------------------------------
-    if (tid == 0) {
+    if (P.phases == 1) {
+        // the last CTA out folds the chunk sums into per-segment sums for the exchange
+        __shared__ int s_last;
+        if (tid == 0) {
+            __threadfence();
+            s_last = atomicAdd(ticket, 1) == (int)gridDim.x - 1;
+        }
+        __syncthreads();
+        if (!s_last) return;
         __threadfence();
-        atomicAdd(barrier, 1);
+        if (tid == 0) P.xbuf[0] = atomicAdd(overflow, 0) ? 1.0f : 0.0f;
+        for (int sg = tid; P.clip && sg < P.nseg; sg += blockDim.x) {
+            float ss = 0.0f;
+            for (int k = P.seg_begin[sg]; k < P.seg_begin[sg + 1]; ++k) ss += P.chunk_sumsq[k];
+            P.xbuf[1 + sg] = ss;
+        }
+        if (tid == 0) {
+            *overflow = 0;
+            __threadfence();
+            *ticket = 0;
+        }
+        return;
+    }
+
+    // ---------------- bounded grid barrier ----------------------------------
+    if (P.phases == 2) {
+        if (tid == 0) s_flag = P.xbuf[0] != 0.0f;
+    } else if (tid == 0) {
+        __threadfence();
+        if ((int)blockIdx.x != P.withheld_cta) atomicAdd(barrier, 1);
         const uint64_t t0 = globaltimer_ns();
         while (atomicAdd(barrier, 0) < (int)gridDim.x) {
-            if (globaltimer_ns() - t0 > kWaitTimeoutNs) { atomicOr(timeout, 1); break; }
+            if (globaltimer_ns() - t0 > P.wait_ns) { atomicOr(timeout, 1); break; }
             __nanosleep(64);
         }
         __threadfence();
@@ -145,7 +180,8 @@ __global__ void __launch_bounds__(512, 2) adam_tail_kernel(TailParams P) {
             float f = inv_scale;
             if (P.clip) {
                 float ss = 0.0f;
-                for (int k = P.seg_begin[seg]; k < P.seg_begin[seg + 1]; ++k) ss += P.chunk_sumsq[k];
+                if (P.phases == 2) ss = P.xbuf[1 + seg];
+                else for (int k = P.seg_begin[seg]; k < P.seg_begin[seg + 1]; ++k) ss += P.chunk_sumsq[k];
                 const float norm = sqrtf(ss) * inv_scale;
                 if (norm > P.max_norm) f *= P.max_norm / norm;
             }
@@ -214,7 +250,7 @@ __global__ void __launch_bounds__(512, 2) adam_tail_kernel(TailParams P) {
 }
 
 struct TailCache {
-    std::vector<int64_t> off, len;
+    std::vector<int64_t> off, len, own;
     int64_t n = -1;
     Chunk* chunks = nullptr;
     int* seg_begin = nullptr;
@@ -223,24 +259,32 @@ struct TailCache {
     int device = -1;
 };
 
-// One cached chunk table per ctx (keyed by the segment list).
-int tail_table(rbk_ctx* ctx, const rbk_tail_args* a, TailCache** out) {
-    static thread_local TailCache cache;
-    TailCache& c = cache;
+// Cached chunk tables, keyed by the segment list and (sharded optimizer) the ranges this rank
+// owns: one for the full arena, one for a shard.  Chunks are ordered by segment, each the part
+// of a segment inside one owned range (the whole arena when `own` is empty), at most kChunk long.
+int tail_table(rbk_ctx* ctx, const rbk_tail_args* a, const std::vector<int64_t>& own, TailCache** out) {
+    static thread_local TailCache caches[2];
+    TailCache& c = caches[own.empty() ? 0 : 1];
     const bool same = c.device == ctx->device && c.n == a->n && (int)c.off.size() == a->nseg &&
                       std::memcmp(c.off.data(), a->seg_off, sizeof(int64_t) * a->nseg) == 0 &&
-                      std::memcmp(c.len.data(), a->seg_len, sizeof(int64_t) * a->nseg) == 0;
+                      std::memcmp(c.len.data(), a->seg_len, sizeof(int64_t) * a->nseg) == 0 && c.own == own;
     if (!same) {
         std::vector<Chunk> ch;
         std::vector<int> sb(a->nseg + 1);
+        const std::vector<int64_t> whole = {0, a->n};
+        const std::vector<int64_t>& rg = own.empty() ? whole : own;     // [begin, end) pairs, ascending
         for (int s = 0; s < a->nseg; ++s) {
             sb[s] = (int)ch.size();
             RBK_REQUIRE(a->seg_off[s] % 4 == 0 && a->seg_len[s] % 4 == 0 && a->seg_off[s] >= 0 &&
                             a->seg_off[s] + a->seg_len[s] <= a->n,
                         "rbk_adam_tail: segment %d must be 4-element aligned and inside [0, n)", s);
-            for (int64_t o = 0; o < a->seg_len[s]; o += kChunk) {
-                const int64_t l = a->seg_len[s] - o < kChunk ? a->seg_len[s] - o : kChunk;
-                ch.push_back(Chunk{a->seg_off[s] + o, (int32_t)l, s});
+            for (size_t r = 0; r + 1 < rg.size(); r += 2) {
+                const int64_t b = std::max(rg[r], a->seg_off[s]);
+                const int64_t e = std::min(rg[r + 1], a->seg_off[s] + a->seg_len[s]);
+                for (int64_t o = b; o < e; o += kChunk) {
+                    const int64_t l = e - o < kChunk ? e - o : kChunk;
+                    ch.push_back(Chunk{o, (int32_t)l, s});
+                }
             }
         }
         sb[a->nseg] = (int)ch.size();
@@ -256,6 +300,7 @@ int tail_table(rbk_ctx* ctx, const rbk_tail_args* a, TailCache** out) {
         RBK_CUDA(cudaMemcpy(c.seg_begin, sb.data(), sizeof(int) * sb.size(), cudaMemcpyHostToDevice));
         c.off.assign(a->seg_off, a->seg_off + a->nseg);
         c.len.assign(a->seg_len, a->seg_len + a->nseg);
+        c.own = own;
         c.nchunks = (int)ch.size();
         c.n = a->n;
         c.device = ctx->device;
@@ -265,11 +310,12 @@ int tail_table(rbk_ctx* ctx, const rbk_tail_args* a, TailCache** out) {
 }
 
 }  // namespace
-}  // namespace rbk
 
-using namespace rbk;
-
-extern "C" int rbk_adam_tail(rbk_ctx* ctx, const rbk_tail_args* a, void* stream) {
+// One tail launch.  own: [begin, end) pairs this rank updates (empty: the whole arena);
+// phases 3 = the fused cooperative launch, 1 / 2 = one phase of the sharded optimizer with
+// its exchange buffer xbuf.
+int tail_launch(rbk_ctx* ctx, const rbk_tail_args* a, const std::vector<int64_t>& own, int phases, float* xbuf,
+                cudaStream_t st) {
     RBK_REQUIRE(ctx && a && a->p32 && a->g && a->m && a->v && a->scaler, "rbk_adam_tail: null pointer");
     RBK_REQUIRE(a->n > 0 && a->n % 4 == 0, "rbk_adam_tail: n must be a positive multiple of 4");
     RBK_REQUIRE(aligned16(a->p32) && aligned16(a->g) && aligned16(a->m) && aligned16(a->v) &&
@@ -284,19 +330,39 @@ extern "C" int rbk_adam_tail(rbk_ctx* ctx, const rbk_tail_args* a, void* stream)
     P.t = a->t;
     P.sc = a->scaler;
     P.flags = ctx->tickets;
-    if (clip) {
+    P.wait_ns = ctx->test_tail_wait_ns ? ctx->test_tail_wait_ns : kWaitTimeoutNs;
+    P.withheld_cta = ctx->test_tail_withheld_cta;
+    ctx->test_tail_wait_ns = 0;                        // the test setting covers one launch
+    ctx->test_tail_withheld_cta = -1;
+    P.phases = phases;
+    P.xbuf = xbuf;
+    P.nseg = clip ? a->nseg : 1;
+    int64_t whole_off = 0, whole_len = a->n;
+    rbk_tail_args one = *a;
+    if (!clip) {                                       // chunks of the owned ranges, one segment
+        one.seg_off = &whole_off;
+        one.seg_len = &whole_len;
+        one.nseg = 1;
+    }
+    int64_t work = a->n;
+    if (clip || !own.empty()) {
         TailCache* tc;
-        RBK_TRY(tail_table(ctx, a, &tc));
+        RBK_TRY(tail_table(ctx, &one, own, &tc));
         P.chunks = tc->chunks;
         P.nchunks = tc->nchunks;
         P.seg_begin = tc->seg_begin;
         P.chunk_sumsq = tc->sumsq;
+        if (!own.empty()) {
+            work = 0;
+            for (size_t r = 0; r + 1 < own.size(); r += 2) work += own[r + 1] - own[r];
+        }
     } else {
         P.chunks = nullptr;
         P.nchunks = (int)((a->n + kChunk - 1) / kChunk);
         P.seg_begin = nullptr;
         P.chunk_sumsq = nullptr;
     }
+    RBK_REQUIRE(P.nchunks > 0, "rbk_adam_tail: nothing to update");
     static thread_local int occ = 0, occ_dev = -1;
     if (occ_dev != ctx->device) {
         RBK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, adam_tail_kernel, 512, 0));
@@ -304,11 +370,23 @@ extern "C" int rbk_adam_tail(rbk_ctx* ctx, const rbk_tail_args* a, void* stream)
     }
     int grid = ctx->num_sms * (occ > 0 ? occ : 1);
     if (grid > P.nchunks) grid = P.nchunks;
+    if (P.withheld_cta >= grid) P.withheld_cta = grid - 1;
     void* args[] = {&P};
-    // algorithmic bytes: read g, p, m, v; write p, m, v, g (zero), p16
-    ProfScope prof(ctx, as_stream(stream), kCatTail, (double)a->n * (a->p16 ? 34.0 : 32.0));
-    RBK_CUDA(cudaLaunchCooperativeKernel((const void*)adam_tail_kernel, dim3(grid), dim3(512), args, 0,
-                                         as_stream(stream)));
+    // algorithmic bytes: read g, p, m, v; write p, m, v, g (zero), p16 (phase 1: read g)
+    const double per = phases == 1 ? 4.0 : phases == 2 ? (a->p16 ? 30.0 : 28.0) : (a->p16 ? 34.0 : 32.0);
+    ProfScope prof(ctx, st, kCatTail, (double)work * per);
+    if (phases == 3)
+        RBK_CUDA(cudaLaunchCooperativeKernel((const void*)adam_tail_kernel, dim3(grid), dim3(512), args, 0, st));
+    else
+        RBK_CUDA(cudaLaunchKernel((const void*)adam_tail_kernel, dim3(grid), dim3(512), args, 0, st));
     count_launch();
     return RBK_OK;
+}
+
+}  // namespace rbk
+
+using namespace rbk;
+
+extern "C" int rbk_adam_tail(rbk_ctx* ctx, const rbk_tail_args* a, void* stream) {
+    return tail_launch(ctx, a, std::vector<int64_t>(), 3, nullptr, as_stream(stream));
 }

@@ -101,6 +101,8 @@ using namespace rbk;
 extern "C" int rbk_model_save(rbk_model* m, const char* path, const int* char_map, void* stream) {
     RBK_REQUIRE(m && path, "rbk_model_save: null pointer");
     RBK_CUDA(cudaSetDevice(m->ctx->device));
+    RBK_TRY(dp_gather_state(m, as_stream(stream)));       // sharded optimizer: whole masters / moments
+    RBK_TRY(dp_wait_weights(m, -1, as_stream(stream)));
     RBK_CUDA(cudaStreamSynchronize(as_stream(stream)));   // the last optimizer step has landed
     File fh;
     fh.f = fopen(path, "wb");
@@ -134,6 +136,7 @@ extern "C" int rbk_model_load(rbk_model* m, const char* path, int* char_map_out,
     RBK_REQUIRE(m && path, "rbk_model_load: null pointer");
     RBK_CUDA(cudaSetDevice(m->ctx->device));
     cudaStream_t st = as_stream(stream);
+    RBK_TRY(dp_wait_weights(m, -1, st));                  // no all-gather still writes the weights
     RBK_CUDA(cudaStreamSynchronize(st));                  // no kernel still reads the arenas
     File fh;
     fh.f = fopen(path, "rb");
@@ -175,6 +178,7 @@ extern "C" int rbk_model_load(rbk_model* m, const char* path, int* char_map_out,
         sc.scale = m->opts.init_loss_scale > 0 ? m->opts.init_loss_scale : 65536.0f;
         sc.interval = m->opts.growth_interval > 0 ? m->opts.growth_interval : 2000;
         RBK_CUDA(cudaMemcpy(m->scaler, &sc, sizeof(sc), cudaMemcpyHostToDevice));
+        m->dp.masters_partial = false;
         return RBK_OK;
     }
     RBK_REQUIRE(got == 4 && std::memcmp(xm, "RBKX", 4) == 0,
@@ -193,5 +197,6 @@ extern "C" int rbk_model_load(rbk_model* m, const char* path, int* char_map_out,
     RBK_TRY(read_family(f, m, order, m->v, sizeof(float), buf, path));
     sc.status = 0;
     RBK_CUDA(cudaMemcpy(m->scaler, &sc, sizeof(sc), cudaMemcpyHostToDevice));
+    m->dp.masters_partial = false;                        // every rank holds the whole state again
     return RBK_OK;
 }

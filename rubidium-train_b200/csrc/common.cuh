@@ -76,10 +76,18 @@ struct rbk_ctx {
     // Role of the next GEMMs for the profiler (0 forward, 1 dgrad, 2 wgrad); -1: derived from
     // the descriptor (FP32-accumulating epilogues are weight gradients, an MN-major B a dgrad).
     int gemm_role = -1;
+    // Set by a caller that knows the C of its next ACC_F32 GEMMs holds zeros (the model's weight
+    // gradients after an optimizer step): their single-split tiles are stored, not read and added.
+    int gemm_c_zero = 0;
     // Bitwise-reproducible accumulation (rbk_ctx_set_deterministic / RBK_DETERMINISTIC=1):
     // split-K weight gradients add their partial planes in split order, the attention backward
     // adds dQ in key-block order.
     int deterministic = 0;
+    // One-shot test setting of the next rbk_adam_tail launch (rbk_ctx_arm_tail_timeout_test):
+    // its grid-barrier wait limit in ns (0: the default kWaitTimeoutNs) and a CTA that does not
+    // arrive at the barrier (-1: none).
+    uint64_t test_tail_wait_ns = 0;
+    int test_tail_withheld_cta = -1;
 };
 
 namespace rbk {

@@ -219,6 +219,15 @@ int rbk_ctx_set_deterministic(rbk_ctx* ctx, int on) {
     return RBK_OK;
 }
 
+int rbk_ctx_arm_tail_timeout_test(rbk_ctx* ctx, double limit_s, int withheld_cta) {
+    RBK_REQUIRE(ctx, "rbk_ctx_arm_tail_timeout_test: null ctx");
+    RBK_REQUIRE(limit_s >= 1e-4 && limit_s <= 2.0, "rbk_ctx_arm_tail_timeout_test: limit_s must be in [1e-4, 2]");
+    RBK_REQUIRE(withheld_cta >= -1, "rbk_ctx_arm_tail_timeout_test: withheld_cta must be >= -1");
+    ctx->test_tail_wait_ns = (uint64_t)(limit_s * 1e9);
+    ctx->test_tail_withheld_cta = withheld_cta;
+    return RBK_OK;
+}
+
 int rbk_ctx_device_error(rbk_ctx* ctx, int* status) {
     RBK_REQUIRE(ctx && status, "rbk_ctx_device_error: bad arguments");
     int v[rbk_ctx::kTickets] = {};

@@ -16,6 +16,7 @@
 // persistent tcgen05 GEMM grids), the last bucket — the embeddings, reduced
 // after the backward has ended, with nothing left to overlap — uses one
 // without the cap.
+#include <algorithm>
 #include <chrono>
 #include <cstring>
 #include <deque>
@@ -92,6 +93,11 @@ double env_double(const char* name, double dflt) {
     return e && *e ? atof(e) : dflt;
 }
 
+// Host-side bound for a non-blocking communicator's own setup work: creation, the split, and
+// the first collectives, which connect the ranks' channels (seconds on a large job).  The
+// watchdog's deadline bounds collectives on the GPU, which may be much shorter.
+constexpr double kSetupBoundS = 120.0;
+
 // Wait (host) until a non-blocking communicator has finished its pending work.
 ncclResult_t settle(ncclComm_t c, double timeout_s) {
     const auto t0 = Clock::now();
@@ -116,10 +122,11 @@ void unit_range(const std::vector<rbk_tensor>& tab, int64_t n, const rbk_config*
     *e = (l + 1 < L) ? tab[rbk_layer_tensor(l + 1, 0)].offset : tab[rbk_tail_tensor(c, 0)].offset;
 }
 
-// Enqueue one all-reduce on the communication stream and register it with the watchdog.
-int allreduce(rbk_model* m, float* buf, size_t n, bool tail) {
-    DpState& d = m->dp;
-    DpWatch& w = *d.watch;
+// Enqueue one collective on stream st through communicator `tail ? uncapped : capped` and
+// register it with the watchdog.  issue(comm) makes the NCCL call.
+template <typename F>
+int collective(rbk_model* m, bool tail, cudaStream_t st, const char* what, F issue) {
+    DpWatch& w = *m->dp.watch;
     std::lock_guard<std::mutex> lk(w.mu);
     if (w.failed != RBK_OK) {
         set_error("data parallel: the communicator was aborted (%s)",
@@ -127,10 +134,10 @@ int allreduce(rbk_model* m, float* buf, size_t n, bool tail) {
         return w.failed;
     }
     ncclComm_t c = w.comms[tail ? 1 : 0];
-    ncclResult_t r = ncclAllReduce(buf, buf, n, ncclFloat32, ncclSum, c, d.stream);
-    if (r == ncclInProgress) r = settle(c, w.timeout_s);
+    ncclResult_t r = issue(c);
+    if (r == ncclInProgress) r = settle(c, std::max(w.timeout_s, kSetupBoundS));
     if (r != ncclSuccess) {
-        set_error("ncclAllReduce failed: %s", ncclGetErrorString(r));
+        set_error("%s failed: %s", what, ncclGetErrorString(r));
         w.abort_locked(r == ncclInProgress ? RBK_ERR_TIMEOUT : RBK_ERR_NCCL);
         return w.failed;
     }
@@ -142,9 +149,43 @@ int allreduce(rbk_model* m, float* buf, size_t n, bool tail) {
         RBK_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
         w.all.push_back(ev);
     }
-    RBK_CUDA(cudaEventRecord(ev, d.stream));
+    RBK_CUDA(cudaEventRecord(ev, st));
     w.pending.emplace_back(ev, Clock::now());
     return RBK_OK;
+}
+
+int allreduce(rbk_model* m, float* buf, size_t n, bool tail) {
+    return collective(m, tail, m->dp.stream, "ncclAllReduce", [&](ncclComm_t c) {
+        return ncclAllReduce(buf, buf, n, ncclFloat32, ncclSum, c, m->dp.stream);
+    });
+}
+
+// Sharded optimizer: reduce-scatter bucket [b, e) of the gradients in place (this rank's slice
+// receives the sum over ranks), then clear the rest of the bucket, which still holds this
+// rank's own unreduced gradients and must be zero for the next accumulation.
+int reduce_scatter(rbk_model* m, int64_t b, int64_t e, bool tail) {
+    DpState& d = m->dp;
+    const size_t cnt = (size_t)((e - b) / d.world);
+    float* base = m->grad + b;
+    RBK_TRY(collective(m, tail, d.stream, "ncclReduceScatter", [&](ncclComm_t c) {
+        return ncclReduceScatter(base, base + (size_t)d.rank * cnt, cnt, ncclFloat32, ncclSum, c, d.stream);
+    }));
+    if (d.rank > 0) RBK_CUDA(cudaMemsetAsync(base, 0, sizeof(float) * cnt * d.rank, d.stream));
+    if (d.rank + 1 < d.world)
+        RBK_CUDA(cudaMemsetAsync(base + cnt * (d.rank + 1), 0, sizeof(float) * cnt * (d.world - 1 - d.rank),
+                                 d.stream));
+    return RBK_OK;
+}
+
+// In-place all-gather of bucket [b, e) of an arena on stream st (each rank contributes its slice).
+template <typename T>
+int all_gather(rbk_model* m, T* arena, int64_t b, int64_t e, ncclDataType_t type, bool tail, cudaStream_t st) {
+    DpState& d = m->dp;
+    const size_t cnt = (size_t)((e - b) / d.world);
+    T* base = arena + b;
+    return collective(m, tail, st, "ncclAllGather", [&](ncclComm_t c) {
+        return ncclAllGather(base + (size_t)d.rank * cnt, base, cnt, type, c, st);
+    });
 }
 
 }  // namespace
@@ -176,7 +217,10 @@ int dp_unit_done(rbk_model* m, int u, cudaStream_t st) {
         if (bk.unit != u) continue;
         RBK_CUDA(cudaEventRecord(d.layer_done[u], st));
         RBK_CUDA(cudaStreamWaitEvent(d.stream, d.layer_done[u], 0));
-        RBK_TRY(allreduce(m, m->grad + bk.begin, (size_t)(bk.end - bk.begin), u == m->cfg.L + 1));
+        if (d.shard)
+            RBK_TRY(reduce_scatter(m, bk.begin, bk.end, u == m->cfg.L + 1));
+        else
+            RBK_TRY(allreduce(m, m->grad + bk.begin, (size_t)(bk.end - bk.begin), u == m->cfg.L + 1));
     }
     if (u == m->cfg.L + 1) {
         RBK_CUDA(cudaEventRecord(d.all_done, d.stream));
@@ -194,6 +238,57 @@ int dp_reduce_all(rbk_model* m, float* buf, int64_t n, cudaStream_t st) {
     RBK_TRY(allreduce(m, buf, (size_t)n, true));
     RBK_CUDA(cudaEventRecord(d.all_done, d.stream));
     RBK_CUDA(cudaStreamWaitEvent(st, d.all_done, 0));
+    return RBK_OK;
+}
+
+// Sharded optimizer step on stream st: phase 1 of the tail over this rank's slices (overflow
+// flag and per-tensor sums of squares into xbuf), one small all-reduce of xbuf so every rank
+// takes the same skip decision and clip factors, phase 2 over the slices, then the FP16
+// weights all-gathered bucket by bucket on the communication stream, in forward order
+// (embeddings first), each bucket's completion recorded for dp_wait_weights.
+int dp_optimizer_step(rbk_model* m, const rbk_tail_args* a, cudaStream_t st) {
+    DpState& d = m->dp;
+    const int nx = 1 + (a->max_norm > 0.0f ? a->nseg : 0);
+    RBK_TRY(tail_launch(m->ctx, a, d.own, 1, d.xbuf, st));
+    RBK_TRY(collective(m, true, st, "ncclAllReduce", [&](ncclComm_t c) {
+        return ncclAllReduce(d.xbuf, d.xbuf, (size_t)nx, ncclFloat32, ncclSum, c, st);
+    }));
+    RBK_TRY(tail_launch(m->ctx, a, d.own, 2, d.xbuf, st));
+    d.masters_partial = true;
+    RBK_CUDA(cudaEventRecord(d.tail_done, st));
+    RBK_CUDA(cudaStreamWaitEvent(d.stream, d.tail_done, 0));
+    for (int i = (int)d.plan.size() - 1; i >= 0; --i) {
+        const DpBucket& bk = d.plan[i];
+        RBK_TRY(all_gather(m, m->p16, bk.begin, bk.end, ncclFloat16, false, d.stream));
+        RBK_CUDA(cudaEventRecord(d.weights_ready[i], d.stream));
+    }
+    d.ag_pending = true;
+    return RBK_OK;
+}
+
+// Order stream st after the FP16 all-gather of the bucket holding backward unit `unit`
+// (-1: all buckets).  The forward calls it before each unit's first use of its weights.
+int dp_wait_weights(rbk_model* m, int unit, cudaStream_t st) {
+    DpState& d = m->dp;
+    if (!d.on || !d.ag_pending) return RBK_OK;
+    if (unit < 0) {
+        for (cudaEvent_t e : d.weights_ready) RBK_CUDA(cudaStreamWaitEvent(st, e, 0));
+        d.ag_pending = false;
+        return RBK_OK;
+    }
+    RBK_CUDA(cudaStreamWaitEvent(st, d.weights_ready[d.unit_bucket[unit]], 0));
+    if (unit == 0) d.ag_pending = false;           // the head is the forward's last unit
+    return RBK_OK;
+}
+
+// All-gather the FP32 masters and both moments on st, so every rank holds all of them.
+int dp_gather_state(rbk_model* m, cudaStream_t st) {
+    DpState& d = m->dp;
+    if (!d.on || !d.shard || !d.masters_partial) return RBK_OK;
+    RBK_TRY(dp_wait_weights(m, -1, st));
+    for (float* arena : {m->p32, m->m, m->v})
+        for (const DpBucket& bk : d.plan) RBK_TRY(all_gather(m, arena, bk.begin, bk.end, ncclFloat32, true, st));
+    d.masters_partial = false;
     return RBK_OK;
 }
 
@@ -236,15 +331,23 @@ int rbk_model_dp_init_ex(rbk_model* m, const void* id128, int rank, int world, c
     RBK_REQUIRE(m && id128 && o && world >= 1 && rank >= 0 && rank < world && o->bucket_bytes > 0,
                 "rbk_model_dp_init_ex: bad arguments");
     RBK_REQUIRE(!m->dp.on, "rbk_model_dp_init_ex: already initialised");
+    if (o->shard_optimizer) {
+        for (const DpBucket& bk : dp_plan(&m->lay, std::max<int64_t>(o->bucket_bytes / 4, 1)))
+            RBK_REQUIRE((bk.end - bk.begin) % (4 * (int64_t)world) == 0,
+                        "rbk_model_dp_init_ex: the sharded optimizer needs every bucket to split into %d slices of a "
+                        "multiple of 4 elements (bucket [%lld, %lld))", world, (long long)bk.begin, (long long)bk.end);
+        RBK_REQUIRE(m->lora.rank == 0, "rbk_model_dp_init_ex: the sharded optimizer covers the base model, not LoRA");
+    }
     RBK_CUDA(cudaSetDevice(m->ctx->device));
     const double timeout_s = o->timeout_s > 0 ? o->timeout_s : 300.0;
+    const double setup_s = std::max(timeout_s, kSetupBoundS);
     ncclUniqueId id;
     std::memcpy(&id, id128, sizeof(id));
     ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
     cfg.blocking = 0;
     ncclComm_t comm = nullptr, tail = nullptr;
     ncclResult_t r = ncclCommInitRankConfig(&comm, world, id, rank, &cfg);
-    if (r == ncclInProgress || r == ncclSuccess) r = settle(comm, timeout_s);
+    if (r == ncclInProgress || r == ncclSuccess) r = settle(comm, setup_s);
     if (r != ncclSuccess) {
         set_error("ncclCommInitRankConfig failed: %s", r == ncclInProgress ? "timed out" : ncclGetErrorString(r));
         if (comm) ncclCommAbort(comm);
@@ -258,8 +361,8 @@ int rbk_model_dp_init_ex(rbk_model* m, const void* id128, int rank, int world, c
         capped.minCTAs = 1;
         ncclComm_t c2 = nullptr;
         r = ncclCommSplit(comm, 0, rank, &c2, &capped);
-        if (r == ncclInProgress || r == ncclSuccess) r = settle(comm, timeout_s);
-        if (r == ncclSuccess && c2) r = settle(c2, timeout_s);
+        if (r == ncclInProgress || r == ncclSuccess) r = settle(comm, setup_s);
+        if (r == ncclSuccess && c2) r = settle(c2, setup_s);
         if (r != ncclSuccess || !c2) {
             set_error("ncclCommSplit (capped communicator) failed: %s",
                       r == ncclInProgress ? "timed out" : ncclGetErrorString(r));
@@ -284,6 +387,28 @@ int rbk_model_dp_init_ex(rbk_model* m, const void* id128, int rank, int world, c
     d.rank = rank;
     d.world = world;
     d.max_ctas = o->max_ctas;
+    if (o->shard_optimizer) {
+        d.shard = true;
+        d.unit_bucket.assign(m->cfg.L + 2, 0);
+        int first = 0;                                  // units first..bk.unit belong to bucket i
+        for (int i = 0; i < (int)d.plan.size(); ++i) {
+            const DpBucket& bk = d.plan[i];
+            for (int u = first; u <= bk.unit; ++u) d.unit_bucket[u] = i;
+            first = bk.unit + 1;
+            d.own.push_back(bk.begin + (bk.end - bk.begin) / world * rank);
+            d.own.push_back(bk.begin + (bk.end - bk.begin) / world * (rank + 1));
+        }
+        std::vector<int64_t> asc;                       // ascending address order
+        for (int i = (int)d.own.size() - 2; i >= 0; i -= 2) {
+            asc.push_back(d.own[i]);
+            asc.push_back(d.own[i + 1]);
+        }
+        d.own = asc;
+        RBK_CUDA(cudaMalloc(&d.xbuf, sizeof(float) * (2 + m->seg_off.size())));
+        d.weights_ready.resize(d.plan.size());
+        for (auto& e : d.weights_ready) RBK_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        RBK_CUDA(cudaEventCreateWithFlags(&d.tail_done, cudaEventDisableTiming));
+    }
     d.watch = new DpWatch();
     d.watch->device = m->ctx->device;
     d.watch->timeout_s = timeout_s;
@@ -316,6 +441,23 @@ int rbk_model_dp_status(rbk_model* m) {
     return s;
 }
 
+int rbk_model_dp_shard_ranges(rbk_model* m, int64_t* out, int max, int* count) {
+    RBK_REQUIRE(m && count, "rbk_model_dp_shard_ranges: bad arguments");
+    const DpState& d = m->dp;
+    *count = d.shard ? (int)d.own.size() / 2 : 0;
+    for (int i = 0; i < *count && i < max && out; ++i) {
+        out[2 * i] = d.own[2 * i];
+        out[2 * i + 1] = d.own[2 * i + 1];
+    }
+    return RBK_OK;
+}
+
+int rbk_model_dp_gather_state(rbk_model* m, void* stream) {
+    RBK_REQUIRE(m, "rbk_model_dp_gather_state: null model");
+    if (m->dp.on) RBK_TRY(rbk_model_dp_status(m));
+    return dp_gather_state(m, as_stream(stream));
+}
+
 int rbk_model_dp_abort(rbk_model* m) {
     RBK_REQUIRE(m, "rbk_model_dp_abort: null model");
     if (!m->dp.on || !m->dp.watch) return RBK_OK;
@@ -343,6 +485,9 @@ int rbk_model_dp_shutdown(rbk_model* m) {
     delete w;
     for (auto& e : d.layer_done) cudaEventDestroy(e);
     cudaEventDestroy(d.all_done);
+    for (auto& e : d.weights_ready) cudaEventDestroy(e);
+    if (d.tail_done) cudaEventDestroy(d.tail_done);
+    if (d.xbuf) cudaFree(d.xbuf);
     cudaStreamDestroy(d.stream);
     d = DpState();
     return RBK_OK;

@@ -133,12 +133,14 @@ struct Params {
     float* part;        // [splits - 1][M][ldp], or nullptr (atomic mode)
     float* part_rows;   // [splits - 1][M] row-sum partials (dbias_rows)
     int ldp;            // row pitch of a plane (N rounded up to 4)
+    int c_zero;         // ACC_F32 into a C known to hold zeros: the owner stores without reading C
 };
 
-// How an ACC_F32 unit of split `split` writes its tile.
-enum AccMode { kAccAtomic = 0, kAccOwner = 1, kAccPlane = 2 };
+// How an ACC_F32 unit of split `split` writes its tile.  kAccStore: the owner of a tile whose C
+// holds zeros stores its values (C + acc = acc) instead of reading C first.
+enum AccMode { kAccAtomic = 0, kAccOwner = 1, kAccPlane = 2, kAccStore = 3 };
 __device__ __forceinline__ int acc_mode(const Params& p, int split) {
-    if (split == 0 && (p.splits == 1 || p.part)) return kAccOwner;
+    if (split == 0 && (p.splits == 1 || p.part)) return p.c_zero ? kAccStore : kAccOwner;
     return p.part ? kAccPlane : kAccAtomic;
 }
 
@@ -1143,6 +1145,7 @@ int rbk_gemm(rbk_ctx* ctx, const rbk_gemm_desc* d, void* stream) {
     p.part = nullptr;
     p.part_rows = nullptr;
     p.ldp = (d->N + 3) & ~3;
+    p.c_zero = epi == RBK_EPI_ACC_F32 && ctx->gemm_c_zero;
     const bool det = epi == RBK_EPI_ACC_F32 && p.splits > 1 && ctx->deterministic;
     if (det) {
         // one FP32 plane per split after the first (+ its row sums), added to C in split order

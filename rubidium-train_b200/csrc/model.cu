@@ -81,6 +81,13 @@ struct Role {
     ~Role() { ctx->gemm_role = saved; }
 };
 enum { kFwd = 0, kDgrad = 1, kWgrad = 2 };
+// The destination of the GEMMs in scope is known to hold zeros.
+struct CZero {
+    rbk_ctx* ctx;
+    int saved;
+    CZero(rbk_ctx* c, bool z) : ctx(c), saved(c->gemm_c_zero) { c->gemm_c_zero = z ? 1 : 0; }
+    ~CZero() { ctx->gemm_c_zero = saved; }
+};
 
 struct G {
     rbk_ctx* ctx;
@@ -115,8 +122,10 @@ struct G {
     // dW[out, in] += dY^T X ; dbias[out] += colsum(dY)
     int wgrad(float* dW, float* dbias, const half* dY, int lddy, const half* X, int ldx, int Nt, int in, int out) {
         Role r(ctx, kWgrad);
+        CZero z(ctx, c_zero);
         return raw(out, in, Nt, dY, lddy, 1, X, ldx, 1, dW, in, RBK_EPI_ACC_F32, nullptr, nullptr, 0, nullptr, dbias);
     }
+    bool c_zero = false;   // the weight gradients are known to hold zeros (each is written once per backward)
 };
 
 }  // namespace
@@ -245,10 +254,13 @@ static int forward(rbk_model* m, const int* tokens, const int* targets, int B, i
                    cudaStream_t st) {
     const int N = B * S, D = m->cfg.D, F = m->cfg.FF, L = m->cfg.L, V = m->cfg.V;
     G g{m->ctx, st};
+    // After a sharded optimizer step each unit waits for the all-gather of its FP16 weights.
+    RBK_TRY(dp_wait_weights(m, L + 1, st));
     RBK_TRY(rbk_embed_fwd(m->ctx, m->act.layers[0].x_in, m->w.token_emb, m->w.pos_emb, tokens, B, S, D, V, st));
     for (int l = 0; l < L; ++l) {
         LayerWeights& y = m->w.layers[l];
         LayerActs& la = m->act.layers[l];
+        RBK_TRY(dp_wait_weights(m, L - l, st));
         RBK_TRY(layer_attn_inputs(m, l, B, S, st));
         // x1 = x + ao Wo^T + bo
         RBK_TRY(g.fwd(la.x1_checkpoint, D, la.ao, D, y.wo, N, D, D, y.bo, la.x_in, D));
@@ -258,6 +270,7 @@ static int forward(rbk_model* m, const int* tokens, const int* targets, int B, i
         half* out = (l + 1 < L) ? m->act.layers[l + 1].x_in : m->act.x_out;
         RBK_TRY(g.fwd(out, D, la.fi, F, y.w2, N, F, D, y.b2, la.x1_checkpoint, D));
     }
+    RBK_TRY(dp_wait_weights(m, 0, st));
     RBK_TRY(rbk_ln_fwd(m->ctx, m->act.hf, m->act.ln_f_mean, m->act.ln_f_inv_std, m->act.x_out, m->w.ln_f_w,
                        m->w.ln_f_b, N, D, 1e-5f, st));
     RBK_TRY(g.fwd(m->act.logits, m->ldV, m->act.hf, D, m->w.lm_w, N, D, V, m->w.lm_b));
@@ -314,10 +327,15 @@ static int backward(rbk_model* m, const int* tokens, const int* targets, int B, 
         RBK_TRY(g.raw(N, D, V, a.logits, m->ldV, 0, m->w.lm_w, D, 1, a.dh, D, RBK_EPI_STORE_F16, nullptr, nullptr, 0,
                       nullptr, nullptr, head_alpha));
     }
+    // Each weight gradient is written by one GEMM per backward: right after an optimizer step (or
+    // zeroing) its tiles are stored instead of read and added.
+    g.c_zero = base && m->grads_zero;
     if (base) {
         Role role(m->ctx, kWgrad);
+        CZero z(m->ctx, g.c_zero);
         RBK_TRY(g.raw(V, D, N, a.logits, m->ldV, 1, a.hf, D, 1, m->w.g_lm_w, D, RBK_EPI_ACC_F32, nullptr, nullptr, 0,
                       nullptr, m->w.g_lm_b, head_alpha));
+        m->grads_zero = false;
     }
     // final LN (under LoRA the LN parameters are frozen: their gradients go to a sink)
     float* sk = a.sink;
@@ -495,6 +513,8 @@ int rbk_model_scaler(rbk_model* m, rbk_scaler** dev) {
 
 int rbk_model_sync_fp16(rbk_model* m, void* stream) {
     RBK_REQUIRE(m, "rbk_model_sync_fp16: null model");
+    RBK_TRY(dp_gather_state(m, as_stream(stream)));   // sharded optimizer: whole masters first
+    RBK_TRY(dp_wait_weights(m, -1, as_stream(stream)));
     cast_f32_f16_kernel<<<grid_for(m->n, m->ctx->num_sms), 256, 0, as_stream(stream)>>>(m->p16, m->p32, m->n);
     RBK_LAUNCHED("cast_f32_f16_kernel");
     return RBK_OK;
@@ -526,6 +546,8 @@ int rbk_model_init_weights(rbk_model* m, uint64_t seed, float std, void* stream)
     RBK_CUDA(cudaMemsetAsync(m->grad, 0, sizeof(float) * m->n, st));
     RBK_CUDA(cudaMemsetAsync(m->m, 0, sizeof(float) * m->n, st));
     RBK_CUDA(cudaMemsetAsync(m->v, 0, sizeof(float) * m->n, st));
+    m->dp.masters_partial = false;                   // every rank holds the whole state again
+    m->grads_zero = true;
     return rbk_model_sync_fp16(m, stream);
 }
 
@@ -543,6 +565,7 @@ int rbk_model_backward(rbk_model* m, const int* tokens, const int* targets, int 
     if (m->dp.on) RBK_TRY(rbk_model_dp_status(m));   // an aborted communicator fails fast
     RBK_REQUIRE(B > 0 && B <= m->opts.max_batch && S > 0 && S <= m->opts.max_seq && S % 64 == 0,
                 "rbk_model_backward: bad B/S");
+    RBK_TRY(dp_wait_weights(m, -1, as_stream(stream)));
     return backward(m, tokens, targets, B, S, grad_scale, as_stream(stream));
 }
 
@@ -556,12 +579,24 @@ int rbk_model_optimizer_step(rbk_model* m, int t, float lr, float b1, float b2, 
     a.max_norm = max_norm;
     a.lr = lr; a.beta1 = b1; a.beta2 = b2; a.eps = eps; a.weight_decay = wd; a.t = t;
     a.scaler = m->scaler;
-    return rbk_adam_tail(m->ctx, &a, stream);
+    // the tail zeroes every gradient it updates (and a sharded step the rest of each bucket)
+    const int st = m->dp.on && m->dp.shard ? dp_optimizer_step(m, &a, as_stream(stream))
+                                           : rbk_adam_tail(m->ctx, &a, stream);
+    if (st == RBK_OK) m->grads_zero = true;
+    return st;
+}
+
+int rbk_model_zero_grad(rbk_model* m, void* stream) {
+    RBK_REQUIRE(m, "rbk_model_zero_grad: null model");
+    RBK_CUDA(cudaMemsetAsync(m->grad, 0, sizeof(float) * m->n, as_stream(stream)));
+    m->grads_zero = true;
+    return RBK_OK;
 }
 
 int rbk_model_lora_enable(rbk_model* m, int rank, float alpha, uint64_t seed, void* stream) {
     RBK_REQUIRE(m && rank > 0 && rank % 8 == 0 && rank <= 64, "rbk_model_lora_enable: rank must be 8..64, %% 8 == 0");
     RBK_REQUIRE(m->lora.rank == 0, "rbk_model_lora_enable: already enabled");
+    RBK_REQUIRE(!m->dp.shard, "rbk_model_lora_enable: not with the sharded optimizer (it covers the base model)");
     LoraState& lo = m->lora;
     const int64_t szA = (int64_t)m->cfg.L * m->cfg.D * rank;
     lo.n = 4 * szA;

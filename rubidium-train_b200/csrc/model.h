@@ -103,6 +103,16 @@ struct DpState {
     cudaEvent_t head_done = nullptr, all_done = nullptr;
     int max_ctas = 0;                      // NCCL CTA cap of the overlapped buckets (0: NCCL's default)
     DpWatch* watch = nullptr;              // owns the communicators
+    // Sharded optimizer: buckets reduce-scattered, this rank updates `own` ([begin, end) pairs,
+    // ascending: slice `rank` of every bucket), FP16 weights all-gathered per bucket.
+    bool shard = false;
+    std::vector<int64_t> own;
+    float* xbuf = nullptr;                 // [1 + segments] overflow flag + clip sums, summed over ranks
+    std::vector<int> unit_bucket;          // backward unit -> index into plan
+    std::vector<cudaEvent_t> weights_ready;// per bucket: its FP16 all-gather finished
+    cudaEvent_t tail_done = nullptr;
+    bool ag_pending = false;               // all-gathers enqueued that no forward has waited for yet
+    bool masters_partial = false;          // p32 / m / v hold this rank's slices only
 };
 
 }  // namespace rbk
@@ -115,6 +125,13 @@ std::vector<DpBucket> dp_plan(const rbk_config* c, int64_t bucket_elems);
 int dp_unit_done(rbk_model* m, int unit, cudaStream_t st);
 int dp_reduce_all(rbk_model* m, float* buf, int64_t n, cudaStream_t st);
 int dp_status(rbk_model* m);
+int dp_optimizer_step(rbk_model* m, const rbk_tail_args* a, cudaStream_t st);
+int dp_wait_weights(rbk_model* m, int unit, cudaStream_t st);   // unit -1: every bucket
+int dp_gather_state(rbk_model* m, cudaStream_t st);
+// adam.cu: one optimizer-tail launch over `own` ([begin, end) pairs; empty: the whole arena),
+// phases 3 (fused) or 1 / 2 (sharded, with the exchange buffer xbuf).
+int tail_launch(rbk_ctx* ctx, const rbk_tail_args* a, const std::vector<int64_t>& own, int phases, float* xbuf,
+                cudaStream_t st);
 }  // namespace rbk
 
 struct rbk_model {
@@ -138,5 +155,10 @@ struct rbk_model {
     bool inject_pending = false;
     bool fused_ce = true;           // forward writes dlogits in place (training mode)
     bool dlogits_ready = false;     // set by a training-mode forward, consumed by backward
+    // The gradient arena holds zeros (after creation, rbk_model_init_weights, rbk_model_zero_grad
+    // or an optimizer step, which zeroes it): the next backward's weight-gradient GEMMs store
+    // their single-split tiles instead of reading and adding.  Cleared by a backward that writes
+    // base gradients.
+    bool grads_zero = true;
     std::vector<void*> allocs;
 };

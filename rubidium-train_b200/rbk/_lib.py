@@ -59,7 +59,8 @@ class ModelOpts(C.Structure):
 
 class DpOpts(C.Structure):
     """rbk_dp_opts (include/rbk.h)."""
-    _fields_ = [("bucket_bytes", C.c_int64), ("max_ctas", C.c_int), ("timeout_s", C.c_double)]
+    _fields_ = [("bucket_bytes", C.c_int64), ("max_ctas", C.c_int), ("timeout_s", C.c_double),
+                ("shard_optimizer", C.c_int)]
 
 
 class TrainArgs(C.Structure):
@@ -82,6 +83,7 @@ _SIGS = {
     "rbk_ctx_profile_read_gemm": (i32, [vp, C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(i32)]),
     "rbk_ctx_device_error": (i32, [vp, C.POINTER(i32)]),
     "rbk_ctx_set_deterministic": (i32, [vp, i32]),
+    "rbk_ctx_arm_tail_timeout_test": (i32, [vp, C.c_double, i32]),
     "rbk_model_ctx": (i32, [vp, C.POINTER(vp)]),
     "rbk_ln_fwd": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, f32, vp]),
     "rbk_ln_bwd": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, vp]),
@@ -122,6 +124,9 @@ _SIGS = {
     "rbk_model_dp_init_ex": (i32, [vp, vp, i32, i32, C.POINTER(DpOpts)]),
     "rbk_model_dp_status": (i32, [vp]),
     "rbk_model_dp_abort": (i32, [vp]),
+    "rbk_model_dp_shard_ranges": (i32, [vp, C.POINTER(C.c_int64), i32, C.POINTER(i32)]),
+    "rbk_model_dp_gather_state": (i32, [vp, vp]),
+    "rbk_model_zero_grad": (i32, [vp, vp]),
     "rbk_model_dp_shutdown": (i32, [vp]),
 }
 

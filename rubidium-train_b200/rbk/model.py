@@ -260,17 +260,37 @@ class RubidiumTransformer:
 
     # ------------------------------------------------------ data parallel --
     def dp_init(self, rank: int, world: int, unique_id: bytes, bucket_bytes: int = 25 << 20, max_ctas=None,
-                timeout_s=None):
+                timeout_s=None, shard=None):
         """Join the NCCL communicator (rbk_model_dp_init_ex).  max_ctas caps NCCL's CTAs for the
-        buckets that overlap the backward; timeout_s is the watchdog's deadline per collective.
-        None: the library defaults (environment RBK_NCCL_MAX_CTAS / RBK_NCCL_TIMEOUT_S)."""
+        buckets that overlap the backward; timeout_s is the watchdog's deadline per collective;
+        shard selects the sharded optimizer (reduce-scatter, the tail on this rank's slices, FP16
+        all-gather).  None: the library defaults (environment RBK_NCCL_MAX_CTAS /
+        RBK_NCCL_TIMEOUT_S / RBK_DP_SHARD)."""
         import os
         buf = C.create_string_buffer(unique_id, 128)
         o = DpOpts()
         o.bucket_bytes = bucket_bytes
         o.max_ctas = int(os.environ.get("RBK_NCCL_MAX_CTAS", "0")) if max_ctas is None else int(max_ctas)
         o.timeout_s = float(os.environ.get("RBK_NCCL_TIMEOUT_S", "300")) if timeout_s is None else float(timeout_s)
+        o.shard_optimizer = int(os.environ.get("RBK_DP_SHARD", "0")) if shard is None else int(bool(shard))
         call("rbk_model_dp_init_ex", self.handle, buf, rank, world, C.byref(o))
+
+    def dp_shard_ranges(self):
+        """[(begin, end), ...] arena ranges this rank updates under the sharded optimizer ([] if not)."""
+        n = C.c_int()
+        call("rbk_model_dp_shard_ranges", self.handle, None, 0, C.byref(n))
+        out = (C.c_int64 * (2 * n.value + 2))()
+        call("rbk_model_dp_shard_ranges", self.handle, out, n.value, C.byref(n))
+        return [(out[2 * i], out[2 * i + 1]) for i in range(n.value)]
+
+    def zero_grad(self):
+        """Zero the gradient arena (rbk_model_zero_grad); the next backward then stores its weight
+        gradients instead of adding to them."""
+        call("rbk_model_zero_grad", self.handle, _s())
+
+    def dp_gather_state(self):
+        """Sharded optimizer: all-gather the FP32 masters and Adam moments (every rank whole again)."""
+        call("rbk_model_dp_gather_state", self.handle, _s())
 
     def dp_abort(self):
         """Abort this rank's communicators locally (a rank leaving the job)."""

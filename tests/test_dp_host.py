@@ -159,3 +159,103 @@ def test_two_rank_gloo_grad_accumulation_schedule(ga):
     for rank, fixed_ok, every_ok in res:
         assert fixed_ok, "sync-on-last-micro-step schedule does not give the mean gradient"
         assert not every_ok, "the per-micro-step all-reduce should over-weight earlier micro-steps"
+
+
+GPT13 = dict(V=50257, T=2048, D=2048, H=16, L=24, FF=8192)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8, 16])
+@pytest.mark.parametrize("cfg,bucket_mb", [(GPT2S, 25), (GPT13, 25), (TINY, 1)])
+def test_plan_buckets_split_into_optimizer_shards(cfg, bucket_mb, world):
+    """The sharded optimizer gives rank r the r-th 1/world slice of every bucket; the slices
+    must start and end on 4-element boundaries (16-byte vectors of the tail kernel)."""
+    plan = _plan(cfg, bucket_mb << 20)
+    assert all((e - b) % (4 * world) == 0 for _, b, e in plan)
+
+
+def _adam(p, g, m, v, f, lr=1e-3, b1=0.9, b2=0.999, eps=1e-8, wd=0.1, t=1):
+    """L2-coupled AdamW as the tail applies it (src/cpu_mat.h:280-292), gradient factor f."""
+    gi = g * f + wd * p
+    m = b1 * m + (1 - b1) * gi
+    v = b2 * v + (1 - b2) * gi * gi
+    return p - lr * (m / (1 - b1 ** t)) / (np.sqrt(v / (1 - b2 ** t)) + eps), m, v
+
+
+def _shard_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        cfg = TINY
+        plan = _plan(cfg, 1 << 20)
+        table, n = _arena(cfg)
+        rng = np.random.default_rng(7)
+        p0 = rng.standard_normal(n).astype(np.float64) * 0.02
+        grads = [np.random.default_rng(50 + r).standard_normal(n) for r in range(world)]
+        full = np.sum(grads, axis=0)                          # what the all-reduce gives every rank
+        max_norm = 0.5
+        # the plain path: every rank clips each tensor by its own norm and updates everything
+        fac = np.ones(n)
+        for _, off, r, c in table:
+            nrm = np.linalg.norm(full[off:off + r * c])
+            if nrm > max_norm:
+                fac[off:off + r * c] = max_norm / nrm
+        ref, _, _ = _adam(p0, full, np.zeros(n), np.zeros(n), fac)
+        # the sharded path: reduce-scatter per bucket (this rank's slice of the sum), per-tensor
+        # sums of squares over the slice, one all-reduce of those sums, the update on the slice,
+        # then an all-gather of the slices
+        own = []
+        g = torch.from_numpy(grads[rank].copy())
+        for _, b, e in plan:
+            seg = g[b:e].clone()
+            dist.all_reduce(seg, op=dist.ReduceOp.SUM)             # stands in for reduce-scatter
+            cnt = (e - b) // world
+            own.append((b + rank * cnt, b + (rank + 1) * cnt))
+            g[b:e] = 0
+            g[b + rank * cnt:b + (rank + 1) * cnt] = seg[rank * cnt:(rank + 1) * cnt]
+        g = g.numpy()
+        sums = np.zeros(len(table))
+        for k, (_, off, r, c) in enumerate(table):
+            for b, e in own:
+                lo, hi = max(b, off), min(e, off + r * c)
+                if lo < hi:
+                    sums[k] += float(np.sum(g[lo:hi] ** 2))
+        ts = torch.from_numpy(sums)
+        dist.all_reduce(ts, op=dist.ReduceOp.SUM)
+        fac = np.ones(n)
+        for k, (_, off, r, c) in enumerate(table):
+            nrm = np.sqrt(float(ts[k]))
+            if nrm > max_norm:
+                fac[off:off + r * c] = max_norm / nrm
+        p = p0.copy()
+        for b, e in own:
+            p[b:e], _, _ = _adam(p0[b:e], g[b:e], np.zeros(e - b), np.zeros(e - b), fac[b:e])
+        mine = torch.zeros(n, dtype=torch.float64)
+        for b, e in own:
+            mine[b:e] = torch.from_numpy(p[b:e])
+        allp = [torch.zeros(n, dtype=torch.float64) for _ in range(world)]
+        dist.all_gather(allp, mine)                               # stands in for the all-gather
+        gathered = torch.stack(allp).sum(0).numpy()               # the slices are disjoint
+        q.put((rank, float(np.max(np.abs(gathered - ref)))))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_gloo_sharded_optimizer_schedule():
+    """The sharded optimizer's schedule (bucketed reduce-scatter, per-tensor clip sums exchanged,
+    the update on each rank's slices, all-gather) gives the same weights as all-reducing and
+    updating the whole arena on every rank."""
+    import socket
+    world = 2
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_shard_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for _, err in res:
+        assert err < 1e-12

@@ -433,3 +433,37 @@ def test_gemm_wgrad_deterministic_split_k(ops, Ntok, fin, out, bias):
     if bias:
         assert rel(runs[0][1].cpu().numpy(), (db0.double() + dY.double().sum(0)).cpu().numpy()) < F32_TOL
     assert ops.device_error() == 0
+
+
+def test_adam_tail_barrier_timeout_is_reported_and_recovers(ops, ora):
+    """The tail's bounded grid-barrier wait runs out on a healthy GPU: one CTA is told not to
+    arrive and the limit is 1 ms.  Every CTA gives up, the step is skipped (masters and moments
+    untouched, gradients zeroed, scale halved), rbk_scaler.status reports RBK_ERR_TIMEOUT, and the
+    next launch on the same context is a normal step that matches the oracle."""
+    from rbk._lib import lib
+    rng = np.random.default_rng(21)
+    n = 1 << 20
+    p = (0.02 * rng.standard_normal(n)).astype(np.float32)
+    m = (1e-3 * rng.standard_normal(n)).astype(np.float32)
+    v = np.abs(1e-6 * rng.standard_normal(n)).astype(np.float32)
+    g = (1024.0 * 1e-3 * rng.standard_normal(n)).astype(np.float32)
+    sc = ops.new_scaler(1024.0, 2000)
+    tp, tg, tm, tv = (torch.from_numpy(a.copy()).cuda() for a in (p, g, m, v))
+    assert lib().rbk_ctx_arm_tail_timeout_test(ops.ctx().handle, 1e-3, 5) == 0
+    ops.adam_tail(tp, tg, tm, tv, None, sc, lr=1e-3, wd=0.1, t=1)
+    st = ops.read_scaler(sc)
+    assert st.status == -4                                # RBK_ERR_TIMEOUT
+    assert st.skipped == 1 and st.scale == 512.0 and st.applied_steps == 0
+    assert np.array_equal(tp.cpu().numpy(), p) and np.array_equal(tm.cpu().numpy(), m)
+    assert np.array_equal(tv.cpu().numpy(), v)
+    assert torch.count_nonzero(tg).item() == 0
+    torch.cuda.synchronize()                              # the context is intact
+    # the next launch is a normal step
+    tg.copy_(torch.from_numpy(g))
+    ops.adam_tail(tp, tg, tm, tv, None, sc, lr=1e-3, wd=0.1, t=1)
+    st = ops.read_scaler(sc)
+    assert st.status == 0 and st.skipped == 0 and st.applied_steps == 1
+    osc = ora.Scaler(512.0, 0, 2000)
+    ep, eg, em, ev = p.copy(), g.copy(), m.copy(), v.copy()
+    ora.adam_tail(ep, eg, em, ev, [0], [n], 1e-3, 0.9, 0.999, 1e-8, 0.1, 1, osc, 0.0)
+    assert rel(tp.cpu().numpy(), ep) < 1e-6 and rel(tm.cpu().numpy(), em) < 1e-5
