@@ -827,9 +827,9 @@ def main():
     ap.add_argument("--no-1p3b", action="store_true", help="skip the second (1.3B) workload pass")
     ap.add_argument("--steps-1p3b", type=int, default=5)
     ap.add_argument("--bucket-mb", type=float, default=25.0)
-    ap.add_argument("--dp-shard", type=int, default=int(os.environ.get("RBK_DP_SHARD", "0")),
-                    help="1: sharded optimizer under data parallelism (reduce-scatter, the tail on each rank's "
-                         "slices, FP16 all-gather); 0: all-reduce and the whole tail on every rank")
+    ap.add_argument("--dp-shard", type=int, default=int(os.environ.get("RBK_DP_SHARD", "1")),
+                    help="1 (default): sharded optimizer under data parallelism (reduce-scatter, the tail on each "
+                         "rank's slices, FP16 all-gather); 0: all-reduce and the whole tail on every rank")
     ap.add_argument("--kernel", default=None,
                     help="loop one kernel instead of the training step (gemm_* of gemm_shapes(), ln_bwd, xent, "
                          "attn_fwd, attn_bwd, adam_tail)")

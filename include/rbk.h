@@ -470,7 +470,7 @@ int rbk_dp_plan(const rbk_config* cfg, int64_t bucket_bytes, int64_t* out, int m
 int rbk_dp_unique_id(void* id128);
 /* Join the communicator; bucket_bytes (25 MB) sets the all-reduce granularity.
  * Defaults of rbk_model_dp_init_ex, overridable through the environment:
- * RBK_NCCL_MAX_CTAS (0), RBK_NCCL_TIMEOUT_S (300). */
+ * RBK_NCCL_MAX_CTAS (0), RBK_NCCL_TIMEOUT_S (300), RBK_DP_SHARD (0). */
 int rbk_model_dp_init(rbk_model* m, const void* id128, int rank, int world, int64_t bucket_bytes);
 typedef struct rbk_dp_opts {
     int64_t bucket_bytes;   /* all-reduce granularity (25 MB)                            */

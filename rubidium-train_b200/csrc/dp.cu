@@ -424,6 +424,7 @@ int rbk_model_dp_init(rbk_model* m, const void* id128, int rank, int world, int6
     o.bucket_bytes = bucket_bytes;
     o.max_ctas = (int)env_double("RBK_NCCL_MAX_CTAS", 0.0);
     o.timeout_s = env_double("RBK_NCCL_TIMEOUT_S", 300.0);
+    o.shard_optimizer = (int)env_double("RBK_DP_SHARD", 0.0);
     return rbk_model_dp_init_ex(m, id128, rank, world, &o);
 }
 

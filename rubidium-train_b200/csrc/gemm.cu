@@ -23,6 +23,8 @@
 // Every mbarrier wait is bounded (globaltimer); on expiry the kernel records
 // RBK_ERR_TIMEOUT, drains, frees TMEM and returns.
 // No cluster multicast is used anywhere.
+#include <type_traits>
+
 #include "tc.cuh"
 
 namespace rbk {
@@ -486,23 +488,30 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 fence_after();
                 const uint32_t dacc = tmem + buf * BN;
                 const uint32_t dacc2 = tmem + C::ACC2_COL + buf * 16;
-                bool ok = true;
-                for (int kb = kb0; kb < kb1; ++kb) {
-                    if (!mbar_wait(full_bar(stage), phase, abort_flag)) { ok = false; break; }
-                    fence_after();
-                    const uint32_t sa = sA0 + stage * C::STAGE_BYTES;
-                    const uint32_t sb = sa + C::A_BYTES;
+                // two versions of the k-loop: no per-MMA branch in the issuing thread
+                auto mainloop = [&](auto with_rows) -> bool {
+                    constexpr bool kRows = decltype(with_rows)::value;
+                    for (int kb = kb0; kb < kb1; ++kb) {
+                        if (!mbar_wait(full_bar(stage), phase, abort_flag)) return false;
+                        fence_after();
+                        const uint32_t sa = sA0 + stage * C::STAGE_BYTES;
+                        const uint32_t sb = sa + C::A_BYTES;
 #pragma unroll
-                    for (int k = 0; k < BK / UMMA_K; ++k) {
-                        const uint64_t ad = sdesc(sa + k * a_kstep, a_lbo, 1024);
-                        const uint64_t bd = sdesc(sb + k * b_kstep, b_lbo, 1024);
-                        const uint32_t acc = (kb > kb0 || k > 0) ? 1u : 0u;
-                        mma_f16(dacc, ad, bd, idesc, acc);
-                        if (rowsum) mma_f16(dacc2, ad, sdesc(ones + k * 32, 16, 1024), idesc1, acc);
+                        for (int k = 0; k < BK / UMMA_K; ++k) {
+                            const uint64_t ad = sdesc(sa + k * a_kstep, a_lbo, 1024);
+                            const uint64_t bd = sdesc(sb + k * b_kstep, b_lbo, 1024);
+                            const uint32_t acc = (kb > kb0 || k > 0) ? 1u : 0u;
+                            mma_f16(dacc, ad, bd, idesc, acc);
+                            if constexpr (kRows) mma_f16(dacc2, ad, sdesc(ones + k * 32, 16, 1024), idesc1, acc);
+                        }
+                        mma_commit(empty_bar(stage));
+                        if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
                     }
-                    mma_commit(empty_bar(stage));
-                    if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
-                }
+                    return true;
+                };
+                bool ok;
+                if constexpr (EPI == RBK_EPI_ACC_F32) ok = rowsum ? mainloop(std::true_type{}) : mainloop(std::false_type{});
+                else ok = mainloop(std::false_type{});
                 if (!ok) break;
                 mma_commit(tfull_bar(buf));
                 if (++buf == 2) { buf = 0; bphase ^= 1; }
@@ -744,25 +753,27 @@ constexpr int kPairStages = 6;
 // Per-warp epilogue staging: two 2 KB tiles for the tensor stores / reduce-adds; the FP32
 // epilogues also keep a 2 KB ones tile for row sums and run one operand stage fewer (their
 // K = tokens mainloops are long).
-template <int EPI>
+template <int EPI, bool ROW>
 struct PairEpi {
     static constexpr bool TMA = EPI == RBK_EPI_STORE_F16 || EPI == RBK_EPI_BIAS_GELU || EPI == RBK_EPI_GELU_BWD;
     static constexpr int STAGES = TMA ? kPairStages : kPairStages - 1;
     static constexpr int WARP_STAGE = kTmaStageBytes;
-    static constexpr int ONES_BYTES = EPI == RBK_EPI_ACC_F32 ? 2048 : 0;
+    static constexpr int ONES_BYTES = EPI == RBK_EPI_ACC_F32 && ROW ? 2048 : 0;
     static constexpr int SMEM = 1024 + STAGES * (BM * BK * 2 + 128 * BK * 2) + kEpiWarps * WARP_STAGE +
                                 ONES_BYTES + 256;
 };
-template <int EPI>
+// ROW: the ACC_F32 variant that can also produce row sums (bias gradients, dbias_rows); the
+// variant without keeps the ones tile and the extra MMA out of the kernel.
+template <int EPI, bool ROW>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmX,
                      const __grid_constant__ CUtensorMap tmP, const Params p) {
     constexpr int BN = 256, HALF_N = 128;
     constexpr int A_BYTES = BM * BK * 2, B_BYTES = HALF_N * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
-    constexpr int STAGES = PairEpi<EPI>::STAGES;
+    constexpr int STAGES = PairEpi<EPI, ROW>::STAGES;
     constexpr bool kTma = EPI == RBK_EPI_STORE_F16 || EPI == RBK_EPI_BIAS_GELU || EPI == RBK_EPI_GELU_BWD;
-    constexpr int kWarpStage = PairEpi<EPI>::WARP_STAGE;
+    constexpr int kWarpStage = PairEpi<EPI, ROW>::WARP_STAGE;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = su32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -770,7 +781,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t sA0 = base;
     const uint32_t epi_stage = base + STAGES * STAGE_BYTES;
     const uint32_t ones = epi_stage + kEpiWarps * kWarpStage;       // FP32 epilogues: 2 KB of FP16 ones
-    const uint32_t bars = ones + PairEpi<EPI>::ONES_BYTES;
+    const uint32_t bars = ones + PairEpi<EPI, ROW>::ONES_BYTES;
     uint8_t* gbars = gbase + (bars - base);
     auto full_bar = [&](int s) { return bars + 8u * s; };
     auto empty_bar = [&](int s) { return bars + 8u * (STAGES + s); };
@@ -786,12 +797,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Row sums of A (the bias gradient of a weight gradient, A = dY^T): an extra N = 16 pair MMA per
     // k-step against a ones tile, accumulated at TMEM column 256, so only one 256-column accumulator
     // buffer remains (the K = tokens mainloops of weight gradients dwarf their epilogues).
-    constexpr bool kRowsumEpi = EPI == RBK_EPI_ACC_F32;
+    constexpr bool kRowsumEpi = EPI == RBK_EPI_ACC_F32 && ROW;
     const bool rowsum_mode = kRowsumEpi && p.dbias_rows != nullptr;
     const int nbuf = rowsum_mode ? 1 : 2;
     if constexpr (kRowsumEpi) {
         uint32_t* o = reinterpret_cast<uint32_t*>(gbase + (ones - base));
-        for (int i = threadIdx.x; i < PairEpi<EPI>::ONES_BYTES / 4; i += blockDim.x) o[i] = 0x3C003C00u;
+        for (int i = threadIdx.x; i < PairEpi<EPI, ROW>::ONES_BYTES / 4; i += blockDim.x) o[i] = 0x3C003C00u;
         fence_proxy_async();
     }
 
@@ -869,23 +880,32 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!mbar_wait(tempty_bar(buf), bphase ^ 1, abort_flag)) break;
                 fence_after();
                 const uint32_t dacc = tmem + buf * BN;
-                bool ok = true;
-                for (int kb = kb0; kb < kb1; ++kb) {
-                    if (!mbar_wait(full_bar(stage), phase, abort_flag)) { ok = false; break; }
-                    fence_after();
-                    const uint32_t sa = sA0 + stage * STAGE_BYTES;
-                    const uint32_t sb = sa + A_BYTES;
+                // The k-loop comes in two versions, so the issuing thread's stream of MMAs carries no
+                // per-MMA branch: a test between back-to-back MMAs cost the accumulating GEMMs about
+                // 20% of their rate even when no row sums were asked for.
+                auto mainloop = [&](auto with_rows) -> bool {
+                    constexpr bool kRows = decltype(with_rows)::value;
+                    for (int kb = kb0; kb < kb1; ++kb) {
+                        if (!mbar_wait(full_bar(stage), phase, abort_flag)) return false;
+                        fence_after();
+                        const uint32_t sa = sA0 + stage * STAGE_BYTES;
+                        const uint32_t sb = sa + A_BYTES;
 #pragma unroll
-                    for (int k = 0; k < BK / UMMA_K; ++k) {
-                        const uint64_t ad = sdesc(sa + k * a_kstep, a_lbo, 1024);
-                        const uint32_t acc = (kb > kb0 || k > 0) ? 1u : 0u;
-                        mma_f16_pair(dacc, ad, sdesc(sb + k * b_kstep, b_lbo, 1024), idesc, acc);
-                        if (kRowsumEpi && rowsum) mma_f16_pair(tmem + 256, ad, sdesc(ones + k * 32, 16, 1024), idesc1, acc);
+                        for (int k = 0; k < BK / UMMA_K; ++k) {
+                            const uint64_t ad = sdesc(sa + k * a_kstep, a_lbo, 1024);
+                            const uint32_t acc = (kb > kb0 || k > 0) ? 1u : 0u;
+                            mma_f16_pair(dacc, ad, sdesc(sb + k * b_kstep, b_lbo, 1024), idesc, acc);
+                            if constexpr (kRows) mma_f16_pair(tmem + 256, ad, sdesc(ones + k * 32, 16, 1024), idesc1, acc);
+                        }
+                        mma_commit_pair(empty_bar(stage));
+                        mma_commit_pair(mapa_shared(empty_bar(stage), 1));
+                        if (++stage == STAGES) { stage = 0; phase ^= 1; }
                     }
-                    mma_commit_pair(empty_bar(stage));
-                    mma_commit_pair(mapa_shared(empty_bar(stage), 1));
-                    if (++stage == STAGES) { stage = 0; phase ^= 1; }
-                }
+                    return true;
+                };
+                bool ok;
+                if constexpr (kRowsumEpi) ok = rowsum ? mainloop(std::true_type{}) : mainloop(std::false_type{});
+                else ok = mainloop(std::false_type{});
                 if (!ok) break;
                 mma_commit_pair(tfull_bar(buf));
                 mma_commit_pair(mapa_shared(tfull_bar(buf), 1));
@@ -1001,9 +1021,9 @@ int launch(rbk_ctx* ctx, const rbk_gemm_desc* d, Params& p, cudaStream_t st) {
 }
 
 // Launched as 2-CTA clusters; grid = 2 x min(units, pairs that fit at once).
-template <int EPI>
+template <int EPI, bool ROW = false>
 int launch_pair(rbk_ctx* ctx, const rbk_gemm_desc* d, Params& p, cudaStream_t st) {
-    constexpr int SMEM = PairEpi<EPI>::SMEM;
+    constexpr int SMEM = PairEpi<EPI, ROW>::SMEM;
     static_assert(SMEM <= 232448, "shared memory budget");
     CUtensorMap ta, tb, tc_, tx, tp;
     // FP16 outputs: 32 x 32 store boxes over the logical [M, N] (ldc / ld_aux pitches); FP32
@@ -1041,17 +1061,17 @@ int launch_pair(rbk_ctx* ctx, const rbk_gemm_desc* d, Params& p, cudaStream_t st
     cfg.numAttrs = 1;
     static int configured_device = -1, max_pairs = 0;
     if (configured_device != ctx->device) {
-        RBK_CUDA(cudaFuncSetAttribute(gemm_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+        RBK_CUDA(cudaFuncSetAttribute(gemm_pair_kernel<EPI, ROW>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
         cfg.gridDim = dim3(ctx->num_sms & ~1);
         int n = 0;
-        RBK_CUDA(cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<EPI>, &cfg));
+        RBK_CUDA(cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<EPI, ROW>, &cfg));
         max_pairs = n > 0 ? n : ctx->num_sms / 2;
         configured_device = ctx->device;
     }
     const int pairs = p.units < max_pairs ? p.units : max_pairs;
     cfg.gridDim = dim3(2 * pairs);
     cfg.numAttrs = set_pdl(attr, 1);
-    RBK_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<EPI>, ta, tb, tc_, tx, tp, p));
+    RBK_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<EPI, ROW>, ta, tb, tc_, tx, tp, p));
     RBK_LAUNCHED("gemm_pair_kernel");
     return RBK_OK;
 }
@@ -1088,7 +1108,7 @@ int rbk_gemm(rbk_ctx* ctx, const rbk_gemm_desc* d, void* stream) {
     RBK_REQUIRE(d->epilogue != RBK_EPI_BIAS_GELU || (d->bias && d->aux_out), "rbk_gemm: BIAS_GELU needs bias and aux_out");
     RBK_REQUIRE(d->epilogue != RBK_EPI_GELU_BWD || d->aux, "rbk_gemm: GELU_BWD needs aux (pre-activation)");
     RBK_REQUIRE(!d->dbias_rows || d->epilogue == RBK_EPI_ACC_F32, "rbk_gemm: dbias_rows needs ACC_F32");
-    const int epi = d->epilogue;
+    int epi = d->epilogue;
     // Tile width: N=256 tiles amortise each A tile over the most MMA columns; the
     // wgrad with a fused bias gradient uses N=192 so that two accumulators plus
     // the ones-MMA accumulator fit the 512 TMEM columns; narrow problems use 128.
@@ -1112,8 +1132,17 @@ int rbk_gemm(rbk_ctx* ctx, const rbk_gemm_desc* d, void* stream) {
         // efficiency units / (ceil(units / SMs) * SMs) is >= 90%, else the best.
         const int tiles = p.m_blocks * p.n_blocks;
         const int max_split = p.k_blocks / 8 > 0 ? p.k_blocks / 8 : 1;
+        // A destination known to hold zeros (and no row sums) is written by one unit per tile
+        // with the plain FP32 store epilogue: about 1.1-1.35x the rate of reduce-added split-K
+        // partials on the 1.3B weight gradients, so it keeps one split unless the grid's last
+        // wave would be less than 80% full.
+        const long w1 = (tiles + slots - 1) / slots;
+        const bool store_one = ctx->gemm_c_zero && !d->dbias_rows && BN != 192 &&
+                               (double)tiles / (double)(w1 * slots) >= 0.8;
         if (d->split_k > 0) {
             splits = d->split_k;
+        } else if (store_one) {
+            splits = 1;
         } else {
             double best = -1.0;
             for (int s = 1; s <= max_split && s <= 64; ++s) {
@@ -1131,6 +1160,9 @@ int rbk_gemm(rbk_ctx* ctx, const rbk_gemm_desc* d, void* stream) {
     }
     p.kb_per_split = (p.k_blocks + splits - 1) / splits;
     p.splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;
+    // C + acc = acc: the store epilogue (no read of C, fewer registers than the accumulating one)
+    if (epi == RBK_EPI_ACC_F32 && ctx->gemm_c_zero && p.splits == 1 && !d->dbias_rows && BN != 192)
+        epi = RBK_EPI_STORE_F32;
     p.units = p.m_blocks * p.n_blocks * p.splits;
     p.a_mn = d->a_major ? 1 : 0;
     p.b_mn = d->b_major ? 1 : 0;
@@ -1166,7 +1198,9 @@ int rbk_gemm(rbk_ctx* ctx, const rbk_gemm_desc* d, void* stream) {
                 case RBK_EPI_STORE_F16: return launch_pair<RBK_EPI_STORE_F16>(ctx, d, p, st);
                 case RBK_EPI_BIAS_GELU: return launch_pair<RBK_EPI_BIAS_GELU>(ctx, d, p, st);
                 case RBK_EPI_GELU_BWD: return launch_pair<RBK_EPI_GELU_BWD>(ctx, d, p, st);
-                case RBK_EPI_ACC_F32: return launch_pair<RBK_EPI_ACC_F32>(ctx, d, p, st);
+                case RBK_EPI_ACC_F32:
+                    return d->dbias_rows ? launch_pair<RBK_EPI_ACC_F32, true>(ctx, d, p, st)
+                                         : launch_pair<RBK_EPI_ACC_F32, false>(ctx, d, p, st);
                 default: return launch_pair<RBK_EPI_STORE_F32>(ctx, d, p, st);
             }
         }

@@ -22,10 +22,12 @@
 namespace rbk {
 namespace {
 
-// One warp per row, NV 16-byte vectors per lane.  For D <= 1024 (NV <= 4) each
-// warp walks its rows with the next row's vectors already in flight while it
-// reduces the current one, and keeps gamma / beta in registers; wider rows hold
-// too many registers for that and load each row when they reach it.
+// One warp per row, NV 16-byte vectors per lane.  Each warp walks its rows with the next
+// row's vectors already in flight while it works on the current one.  For D <= 1024
+// (NV <= 4) the current row is held as FP32 and gamma / beta stay in registers; for
+// 1024 < D <= 2048 the row stays FP16 and is converted again in each of the three passes
+// (sum, centred sum of squares, output), gamma / beta come from L1, so two rows fit the
+// registers of two CTAs per SM; wider rows load each row when they reach it.
 template <int NV>
 __global__ void __launch_bounds__(256) ln_fwd_kernel(half* __restrict__ y, float* __restrict__ mean,
                                                      float* __restrict__ rstd, const half* __restrict__ x,
@@ -37,6 +39,60 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(half* __restrict__ y, float
     const float invD = 1.0f / (float)D;
     const int stride = gridDim.x * warps;
     constexpr bool kPrefetch = NV <= 4;
+    if constexpr (NV > 4 && NV <= 8) {
+        uint4 cur[NV], nxt[NV];
+        int row = blockIdx.x * warps + (threadIdx.x >> 5);
+        auto load = [&](uint4* dst, int r) {
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                const int c = lane + 32 * i;
+                dst[i] = (r < N && c < nvec) ? __ldg(reinterpret_cast<const uint4*>(x + (size_t)r * D) + c)
+                                             : make_uint4(0, 0, 0, 0);
+            }
+        };
+        load(nxt, row);
+        for (; row < N; row += stride) {
+#pragma unroll
+            for (int i = 0; i < NV; ++i) cur[i] = nxt[i];
+            load(nxt, row + stride);                         // next row in flight during this one
+            float s = 0.0f;
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                float v[8];
+                h8_to_f(cur[i], v);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) s += v[j];
+            }
+            const float m = warp_sum(s) * invD;
+            float q = 0.0f;
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                if (lane + 32 * i < nvec) {
+                    float v[8];
+                    h8_to_f(cur[i], v);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) { const float d = v[j] - m; q += d * d; }
+                }
+            }
+            const float r = 1.0f / sqrtf(warp_sum(q) * invD + eps);
+            uint4* yr = reinterpret_cast<uint4*>(y + (size_t)row * D);
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                const int c = lane + 32 * i;
+                if (c < nvec) {
+                    float v[8], gf[8], bf[8], o[8];
+                    h8_to_f(cur[i], v);
+                    h8_to_f(__ldg(reinterpret_cast<const uint4*>(g) + c), gf);
+                    h8_to_f(__ldg(reinterpret_cast<const uint4*>(b) + c), bf);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) o[j] = gf[j] * (v[j] - m) * r + bf[j];
+                    yr[c] = f_to_h8(o);
+                }
+            }
+            if (lane == 0) { mean[row] = m; rstd[row] = r; }
+        }
+        return;
+    }
     uint4 gr[kPrefetch ? NV : 1], br[kPrefetch ? NV : 1], nx[NV];
     if constexpr (kPrefetch) {
 #pragma unroll
@@ -987,7 +1043,7 @@ int launch_fwd(int blocks, cudaStream_t st, half* y, float* mean, float* rstd, c
         RBK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
         resident = (occ > 0 ? occ : 1) * sms;
     }
-    if (NV <= 4 && blocks > resident) blocks = resident;
+    if (NV <= 8 && blocks > resident) blocks = resident;
     RBK_CUDA(launch_pdl(ln_fwd_kernel<NV>, dim3(blocks), dim3(256), 0, st, y, mean, rstd, x, g, b, N, D, eps));
     return RBK_OK;
 }
