@@ -314,6 +314,10 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
     asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
     return v;
 }
+__device__ __forceinline__ float4 lds128f(uint32_t addr) {
+    const uint4 u = lds128(addr);
+    return make_float4(__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z), __uint_as_float(u.w));
+}
 
 // ---------------------------------------------------------------------------
 // Backward with a bulk-copy ring.  Shared memory: stages x [dy | x | dres] row
@@ -793,7 +797,11 @@ __global__ void __launch_bounds__(32 * kLnWarpTeams + 32, 1)
     constexpr int TEAMS = kLnWarpTeams;
     constexpr int NT = kRes ? 3 : 2;
     constexpr uint32_t ROW_BYTES = D * 2;
-    constexpr uint32_t STAGE_BYTES = R * ROW_BYTES * NT;
+    // At D = 1024 a stage also carries its rows' mean[R], rstd[R] (the consumers' own loads of them
+    // were the leading stall); at D = 768 the consumers load them one stage ahead (measured faster).
+    constexpr bool kStats = D >= 1024;
+    constexpr uint32_t STATS_OFF = R * ROW_BYTES * NT;
+    constexpr uint32_t STAGE_BYTES = STATS_OFF + (kStats ? 8 * R : 0);
     constexpr float kInvD = 1.0f / (float)D;
     extern __shared__ __align__(128) uint8_t lsm_raw[];
     uint64_t* bars = reinterpret_cast<uint64_t*>(lsm_raw + (size_t)stages * STAGE_BYTES);
@@ -820,13 +828,19 @@ __global__ void __launch_bounds__(32 * kLnWarpTeams + 32, 1)
                 const int s = k % stages;
                 if (!mbar_wait(empty(s), ((k / stages) & 1) ^ 1, abort_flag)) break;
                 const int rows = min(R, N - gs * R);
-                mbar_expect_tx(full(s), (uint32_t)rows * ROW_BYTES * NT);
+                // a whole stage also brings its rows' mean and rstd (16 bytes each); a partial last
+                // stage leaves them to the consumers' own loads
+                mbar_expect_tx(full(s), (uint32_t)rows * ROW_BYTES * NT + (kStats && rows == R ? 8u * R : 0u));
                 const uint32_t dst = su32(lsm_raw + (size_t)s * STAGE_BYTES);
                 const size_t off = (size_t)gs * R * D;
                 const uint32_t bytes = (uint32_t)rows * ROW_BYTES;
                 bulk_load(dst, dy + off, bytes, full(s));
                 bulk_load(dst + R * ROW_BYTES, x + off, bytes, full(s));
                 if (kRes) bulk_load(dst + 2 * R * ROW_BYTES, dres + off, bytes, full(s));
+                if (kStats && rows == R) {
+                    bulk_load(dst + STATS_OFF, mean + (size_t)gs * R, 4u * R, full(s));
+                    bulk_load(dst + STATS_OFF + 4u * R, rstd + (size_t)gs * R, 4u * R, full(s));
+                }
             }
         }
     } else {
@@ -848,7 +862,7 @@ __global__ void __launch_bounds__(32 * kLnWarpTeams + 32, 1)
         bool ok = true;
         const uint32_t ring = su32(lsm_raw);
         float nmr[R], nrr[R];
-        {
+        if constexpr (!kStats) {
             const int row0 = (blockIdx.x + team * gridDim.x) * R;
 #pragma unroll
             for (int r = 0; r < R; ++r) {
@@ -862,15 +876,30 @@ __global__ void __launch_bounds__(32 * kLnWarpTeams + 32, 1)
             const int row0 = gs * R;
             const int nrows = min(R, N - row0);
             float mr[R], rr[R];
-            const int nrow0 = (blockIdx.x + (k + TEAMS) * gridDim.x) * R;
+            if constexpr (!kStats) {
+                const int nrow0 = (blockIdx.x + (k + TEAMS) * gridDim.x) * R;
 #pragma unroll
-            for (int r = 0; r < R; ++r) {
-                mr[r] = nmr[r];
-                rr[r] = nrr[r];
-                nmr[r] = nrow0 + r < N ? __ldg(mean + nrow0 + r) : 0.0f;
-                nrr[r] = nrow0 + r < N ? __ldg(rstd + nrow0 + r) : 0.0f;
+                for (int r = 0; r < R; ++r) {
+                    mr[r] = nmr[r];
+                    rr[r] = nrr[r];
+                    nmr[r] = nrow0 + r < N ? __ldg(mean + nrow0 + r) : 0.0f;
+                    nrr[r] = nrow0 + r < N ? __ldg(rstd + nrow0 + r) : 0.0f;
+                }
             }
             ok = __all_sync(0xffffffffu, ok && mbar_wait(full(s), (k / stages) & 1, abort_flag));
+            if (!kStats) {
+            } else if (nrows == R) {
+                const float4 m4 = lds128f(ring + (uint32_t)s * STAGE_BYTES + STATS_OFF);
+                const float4 r4 = lds128f(ring + (uint32_t)s * STAGE_BYTES + STATS_OFF + 4u * R);
+                mr[0] = m4.x; mr[1] = m4.y; mr[2] = m4.z; mr[3] = m4.w;
+                rr[0] = r4.x; rr[1] = r4.y; rr[2] = r4.z; rr[3] = r4.w;
+            } else {
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    mr[r] = r < nrows ? __ldg(mean + row0 + r) : 0.0f;
+                    rr[r] = r < nrows ? __ldg(rstd + row0 + r) : 0.0f;
+                }
+            }
             const uint32_t sb = ring + (uint32_t)s * STAGE_BYTES + 16u * lane;
             float v8[2 * R];
 #pragma unroll
@@ -1141,7 +1170,7 @@ int rbk_ln_bwd(rbk_ctx* ctx, void* dx, float* dgamma, float* dbeta, float* dbias
     }();
     if (!generic_only && (D == 768 || D == 1024)) {
         // one warp per team: its own ring depth (the stage is 4 rows of every tensor)
-        const size_t wstage = (size_t)kLnRows * D * 2 * (dres ? 3 : 2);
+        const size_t wstage = (size_t)kLnRows * D * 2 * (dres ? 3 : 2) + (D >= 1024 ? 8 * kLnRows : 0);   // + stats
         int wst = (int)((200u << 10) / wstage);
         wst = wst > 16 ? 16 : wst;
         const size_t wsmem = wst * wstage + 16 * (size_t)wst + 16;
