@@ -302,6 +302,30 @@ int rbk_gemm_wgrad(rbk_ctx* ctx, float* dW, float* dbias, const void* dY, const 
                    void* stream);
 
 /* ------------------------------------------------------------------------
+ * LoRA adapters, kernel level (the model level runs the same GEMMs inside
+ * rbk_model_forward / _backward once rbk_model_lora_enable has been called)
+ * ------------------------------------------------------------------------ */
+
+/* One adapter on one projection, W' = W + scaling A B, A [in, r] and B [r, out]
+ * row-major FP16 (the per-target step of lora_forward_all, src/lora.h:224-226):
+ *   xa[N, r] = x A   (FP16, kept for the backward);   y[N, out] += scaling xa B
+ * x, y FP16 with row strides ldx, ldy (y updated in place, e.g. the q or v
+ * columns of a fused qkv).  in, out, r and the strides are multiples of 8. */
+int rbk_lora_fwd(rbk_ctx* ctx, void* y, int ldy, void* xa, const void* x, int ldx, const void* A, const void* B,
+                 int N, int in, int r, int out, float scaling, void* stream);
+/* Its backward (lora_backward_all, src/lora.h:227-229):
+ *   dB[r, out] += scaling xa^T dy;   dyb[N, r] = scaling dy B^T (caller's FP16
+ *   workspace);   dA[in, r] += x^T dyb;   dx[N, in] += dyb A^T (FP16, in place,
+ *   row stride lddx; NULL skips it).  dA, dB FP32. */
+int rbk_lora_bwd(rbk_ctx* ctx, float* dA, float* dB, void* dx, int lddx, void* dyb, const void* dy, int lddy,
+                 const void* x, int ldx, const void* xa, const void* A, const void* B, int N, int in, int r, int out,
+                 float scaling, void* stream);
+/* lora_optimizer_step (src/lora.h:230): the fused AdamW tail (rbk_adam_tail)
+ * over an adapter arena: FP32 masters / grads / moments, the FP16 copy the
+ * adapter GEMMs read, the shared loss scaler. */
+int rbk_lora_adam(rbk_ctx* ctx, const rbk_tail_args* args, void* stream);
+
+/* ------------------------------------------------------------------------
  * Causal flash attention (d_head 64 or 128)
  * ------------------------------------------------------------------------ */
 
@@ -504,6 +528,24 @@ int rbk_model_dp_status(rbk_model* m);
  * leaves the job calls it instead of a shutdown its peers would have to join;
  * afterwards the model behaves as after a watchdog abort (RBK_ERR_NCCL). */
 int rbk_model_dp_abort(rbk_model* m);
+/* Kernel-level data parallelism for callers that keep their own orchestration
+ * (no rbk_model): the same non-blocking communicators, high-priority
+ * communication stream and watchdog as rbk_model_dp_init_ex (opts: max_ctas,
+ * timeout_s; NULL for the defaults; bucket_bytes and shard_optimizer unused).
+ *   rbk_dp_bucket_ready: sum-all-reduce buf[0, n) FP32 in place over the ranks,
+ *     on the communication stream, after the work enqueued on `stream` so far
+ *     (call it as soon as a bucket's gradients are final; it overlaps what
+ *     follows on `stream`);
+ *   rbk_dp_finish: `stream` waits for every bucket enqueued so far;
+ *   rbk_dp_status / rbk_dp_abort / rbk_dp_destroy: as the rbk_model_dp_* ones.
+ * No counterpart in the reference (single GPU, src/main.cpp:54). */
+typedef struct rbk_dp rbk_dp;
+int rbk_dp_init(rbk_dp** out, int device, const void* id128, int rank, int world, const rbk_dp_opts* opts);
+int rbk_dp_bucket_ready(rbk_dp* dp, float* buf, int64_t n, void* stream);
+int rbk_dp_finish(rbk_dp* dp, void* stream);
+int rbk_dp_status(rbk_dp* dp);
+int rbk_dp_abort(rbk_dp* dp);
+int rbk_dp_destroy(rbk_dp* dp);
 /* Sharded optimizer: *count = number of [begin, end) arena ranges this rank
  * updates (0 when not sharded); out[2i], out[2i+1] = range i, for i < max. */
 int rbk_model_dp_shard_ranges(rbk_model* m, int64_t* out, int max, int* count);

@@ -125,8 +125,8 @@ void unit_range(const std::vector<rbk_tensor>& tab, int64_t n, const rbk_config*
 // Enqueue one collective on stream st through communicator `tail ? uncapped : capped` and
 // register it with the watchdog.  issue(comm) makes the NCCL call.
 template <typename F>
-int collective(rbk_model* m, bool tail, cudaStream_t st, const char* what, F issue) {
-    DpWatch& w = *m->dp.watch;
+int collective(DpState& d, bool tail, cudaStream_t st, const char* what, F issue) {
+    DpWatch& w = *d.watch;
     std::lock_guard<std::mutex> lk(w.mu);
     if (w.failed != RBK_OK) {
         set_error("data parallel: the communicator was aborted (%s)",
@@ -154,9 +154,9 @@ int collective(rbk_model* m, bool tail, cudaStream_t st, const char* what, F iss
     return RBK_OK;
 }
 
-int allreduce(rbk_model* m, float* buf, size_t n, bool tail) {
-    return collective(m, tail, m->dp.stream, "ncclAllReduce", [&](ncclComm_t c) {
-        return ncclAllReduce(buf, buf, n, ncclFloat32, ncclSum, c, m->dp.stream);
+int allreduce(DpState& d, float* buf, size_t n, bool tail) {
+    return collective(d, tail, d.stream, "ncclAllReduce", [&](ncclComm_t c) {
+        return ncclAllReduce(buf, buf, n, ncclFloat32, ncclSum, c, d.stream);
     });
 }
 
@@ -167,7 +167,7 @@ int reduce_scatter(rbk_model* m, int64_t b, int64_t e, bool tail) {
     DpState& d = m->dp;
     const size_t cnt = (size_t)((e - b) / d.world);
     float* base = m->grad + b;
-    RBK_TRY(collective(m, tail, d.stream, "ncclReduceScatter", [&](ncclComm_t c) {
+    RBK_TRY(collective(d, tail, d.stream, "ncclReduceScatter", [&](ncclComm_t c) {
         return ncclReduceScatter(base, base + (size_t)d.rank * cnt, cnt, ncclFloat32, ncclSum, c, d.stream);
     }));
     if (d.rank > 0) RBK_CUDA(cudaMemsetAsync(base, 0, sizeof(float) * cnt * d.rank, d.stream));
@@ -183,7 +183,7 @@ int all_gather(rbk_model* m, T* arena, int64_t b, int64_t e, ncclDataType_t type
     DpState& d = m->dp;
     const size_t cnt = (size_t)((e - b) / d.world);
     T* base = arena + b;
-    return collective(m, tail, st, "ncclAllGather", [&](ncclComm_t c) {
+    return collective(d, tail, st, "ncclAllGather", [&](ncclComm_t c) {
         return ncclAllGather(base + (size_t)d.rank * cnt, base, cnt, type, c, st);
     });
 }
@@ -220,7 +220,7 @@ int dp_unit_done(rbk_model* m, int u, cudaStream_t st) {
         if (d.shard)
             RBK_TRY(reduce_scatter(m, bk.begin, bk.end, u == m->cfg.L + 1));
         else
-            RBK_TRY(allreduce(m, m->grad + bk.begin, (size_t)(bk.end - bk.begin), u == m->cfg.L + 1));
+            RBK_TRY(allreduce(d, m->grad + bk.begin, (size_t)(bk.end - bk.begin), u == m->cfg.L + 1));
     }
     if (u == m->cfg.L + 1) {
         RBK_CUDA(cudaEventRecord(d.all_done, d.stream));
@@ -235,7 +235,7 @@ int dp_reduce_all(rbk_model* m, float* buf, int64_t n, cudaStream_t st) {
     DpState& d = m->dp;
     RBK_CUDA(cudaEventRecord(d.layer_done[0], st));
     RBK_CUDA(cudaStreamWaitEvent(d.stream, d.layer_done[0], 0));
-    RBK_TRY(allreduce(m, buf, (size_t)n, true));
+    RBK_TRY(allreduce(d, buf, (size_t)n, true));
     RBK_CUDA(cudaEventRecord(d.all_done, d.stream));
     RBK_CUDA(cudaStreamWaitEvent(st, d.all_done, 0));
     return RBK_OK;
@@ -250,7 +250,7 @@ int dp_optimizer_step(rbk_model* m, const rbk_tail_args* a, cudaStream_t st) {
     DpState& d = m->dp;
     const int nx = 1 + (a->max_norm > 0.0f ? a->nseg : 0);
     RBK_TRY(tail_launch(m->ctx, a, d.own, 1, d.xbuf, st));
-    RBK_TRY(collective(m, true, st, "ncclAllReduce", [&](ncclComm_t c) {
+    RBK_TRY(collective(d, true, st, "ncclAllReduce", [&](ncclComm_t c) {
         return ncclAllReduce(d.xbuf, d.xbuf, (size_t)nx, ncclFloat32, ncclSum, c, st);
     }));
     RBK_TRY(tail_launch(m->ctx, a, d.own, 2, d.xbuf, st));
@@ -292,13 +292,106 @@ int dp_gather_state(rbk_model* m, cudaStream_t st) {
     return RBK_OK;
 }
 
-int dp_status(rbk_model* m) {
-    if (!m->dp.on || !m->dp.watch) return RBK_OK;
-    std::lock_guard<std::mutex> lk(m->dp.watch->mu);
-    return m->dp.watch->failed;
+int dp_state_status(DpState& d);
+int dp_status(rbk_model* m) { return dp_state_status(m->dp); }
+
+// Create the communicators (non-blocking; a second one with a CTA cap when max_ctas > 0),
+// the high-priority communication stream and the watchdog, on `device`.
+int dp_open(DpState& d, int device, const void* id128, int rank, int world, int max_ctas, double timeout_in) {
+    RBK_CUDA(cudaSetDevice(device));
+    const double timeout_s = timeout_in > 0 ? timeout_in : 300.0;
+    const double setup_s = std::max(timeout_s, kSetupBoundS);
+    ncclUniqueId id;
+    std::memcpy(&id, id128, sizeof(id));
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    ncclComm_t comm = nullptr, tail = nullptr;
+    ncclResult_t r = ncclCommInitRankConfig(&comm, world, id, rank, &cfg);
+    if (r == ncclInProgress || r == ncclSuccess) r = settle(comm, setup_s);
+    if (r != ncclSuccess) {
+        set_error("ncclCommInitRankConfig failed: %s", r == ncclInProgress ? "timed out" : ncclGetErrorString(r));
+        if (comm) ncclCommAbort(comm);
+        return r == ncclInProgress ? RBK_ERR_TIMEOUT : RBK_ERR_NCCL;
+    }
+    if (max_ctas > 0) {
+        // the capped communicator for the overlapped buckets; `comm` (uncapped) keeps the tail
+        ncclConfig_t capped = NCCL_CONFIG_INITIALIZER;
+        capped.blocking = 0;
+        capped.maxCTAs = max_ctas;
+        capped.minCTAs = 1;
+        ncclComm_t c2 = nullptr;
+        r = ncclCommSplit(comm, 0, rank, &c2, &capped);
+        if (r == ncclInProgress || r == ncclSuccess) r = settle(comm, setup_s);
+        if (r == ncclSuccess && c2) r = settle(c2, setup_s);
+        if (r != ncclSuccess || !c2) {
+            set_error("ncclCommSplit (capped communicator) failed: %s",
+                      r == ncclInProgress ? "timed out" : ncclGetErrorString(r));
+            if (c2) ncclCommAbort(c2);
+            ncclCommAbort(comm);
+            return r == ncclInProgress ? RBK_ERR_TIMEOUT : RBK_ERR_NCCL;
+        }
+        tail = comm;
+        comm = c2;
+    } else {
+        tail = comm;
+    }
+    int lo = 0, hi = 0;
+    RBK_CUDA(cudaDeviceGetStreamPriorityRange(&lo, &hi));
+    RBK_CUDA(cudaStreamCreateWithPriority(&d.stream, cudaStreamNonBlocking, hi));
+    RBK_CUDA(cudaEventCreateWithFlags(&d.all_done, cudaEventDisableTiming));
+    d.rank = rank;
+    d.world = world;
+    d.max_ctas = max_ctas;
+    d.watch = new DpWatch();
+    d.watch->device = device;
+    d.watch->timeout_s = timeout_s;
+    d.watch->comms[0] = comm;
+    d.watch->comms[1] = tail;
+    d.watch->th = std::thread([w = d.watch] { w->loop(); });
+    d.on = true;
+    return RBK_OK;
+}
+
+// Drain, stop the watchdog and release the communicators and every event / buffer of d.
+int dp_close(DpState& d) {
+    if (!d.on) return RBK_OK;
+    DpWatch* w = d.watch;
+    // Wait for the collectives in flight; the watchdog keeps running meanwhile, so a hung one
+    // is aborted after the timeout and this returns.
+    cudaStreamSynchronize(d.stream);
+    {
+        std::lock_guard<std::mutex> lk(w->mu);
+        w->stop = true;
+    }
+    w->th.join();
+    if (w->comms[1] && w->comms[1] != w->comms[0]) ncclCommDestroy(w->comms[1]);
+    if (w->comms[0]) ncclCommDestroy(w->comms[0]);
+    for (cudaEvent_t e : w->all) cudaEventDestroy(e);
+    delete w;
+    for (auto& e : d.layer_done) cudaEventDestroy(e);
+    cudaEventDestroy(d.all_done);
+    for (auto& e : d.weights_ready) cudaEventDestroy(e);
+    if (d.tail_done) cudaEventDestroy(d.tail_done);
+    if (d.xbuf) cudaFree(d.xbuf);
+    cudaStreamDestroy(d.stream);
+    d = DpState();
+    return RBK_OK;
+}
+
+int dp_state_status(DpState& d) {
+    if (!d.on || !d.watch) return RBK_OK;
+    std::lock_guard<std::mutex> lk(d.watch->mu);
+    return d.watch->failed;
 }
 
 }  // namespace rbk
+
+// Kernel-level data parallelism: the communicators, stream and watchdog of the model-level
+// path without a model (the caller names the buffers).
+struct rbk_dp {
+    rbk::DpState d;
+    cudaEvent_t ready = nullptr;
+};
 
 using namespace rbk;
 
@@ -338,55 +431,12 @@ int rbk_model_dp_init_ex(rbk_model* m, const void* id128, int rank, int world, c
                         "multiple of 4 elements (bucket [%lld, %lld))", world, (long long)bk.begin, (long long)bk.end);
         RBK_REQUIRE(m->lora.rank == 0, "rbk_model_dp_init_ex: the sharded optimizer covers the base model, not LoRA");
     }
-    RBK_CUDA(cudaSetDevice(m->ctx->device));
-    const double timeout_s = o->timeout_s > 0 ? o->timeout_s : 300.0;
-    const double setup_s = std::max(timeout_s, kSetupBoundS);
-    ncclUniqueId id;
-    std::memcpy(&id, id128, sizeof(id));
-    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
-    cfg.blocking = 0;
-    ncclComm_t comm = nullptr, tail = nullptr;
-    ncclResult_t r = ncclCommInitRankConfig(&comm, world, id, rank, &cfg);
-    if (r == ncclInProgress || r == ncclSuccess) r = settle(comm, setup_s);
-    if (r != ncclSuccess) {
-        set_error("ncclCommInitRankConfig failed: %s", r == ncclInProgress ? "timed out" : ncclGetErrorString(r));
-        if (comm) ncclCommAbort(comm);
-        return r == ncclInProgress ? RBK_ERR_TIMEOUT : RBK_ERR_NCCL;
-    }
-    if (o->max_ctas > 0) {
-        // the capped communicator for the overlapped buckets; `comm` (uncapped) keeps the tail
-        ncclConfig_t capped = NCCL_CONFIG_INITIALIZER;
-        capped.blocking = 0;
-        capped.maxCTAs = o->max_ctas;
-        capped.minCTAs = 1;
-        ncclComm_t c2 = nullptr;
-        r = ncclCommSplit(comm, 0, rank, &c2, &capped);
-        if (r == ncclInProgress || r == ncclSuccess) r = settle(comm, setup_s);
-        if (r == ncclSuccess && c2) r = settle(c2, setup_s);
-        if (r != ncclSuccess || !c2) {
-            set_error("ncclCommSplit (capped communicator) failed: %s",
-                      r == ncclInProgress ? "timed out" : ncclGetErrorString(r));
-            if (c2) ncclCommAbort(c2);
-            ncclCommAbort(comm);
-            return r == ncclInProgress ? RBK_ERR_TIMEOUT : RBK_ERR_NCCL;
-        }
-        tail = comm;
-        comm = c2;
-    } else {
-        tail = comm;
-    }
+    RBK_TRY(dp_open(m->dp, m->ctx->device, id128, rank, world, o->max_ctas, o->timeout_s));
     DpState& d = m->dp;
-    int lo = 0, hi = 0;
-    RBK_CUDA(cudaDeviceGetStreamPriorityRange(&lo, &hi));
-    RBK_CUDA(cudaStreamCreateWithPriority(&d.stream, cudaStreamNonBlocking, hi));
     d.layer_done.resize(m->cfg.L + 2);
     for (auto& e : d.layer_done) RBK_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
-    RBK_CUDA(cudaEventCreateWithFlags(&d.all_done, cudaEventDisableTiming));
     d.bucket_elems = std::max<int64_t>(o->bucket_bytes / 4, 1);
     d.plan = dp_plan(&m->lay, d.bucket_elems);
-    d.rank = rank;
-    d.world = world;
-    d.max_ctas = o->max_ctas;
     if (o->shard_optimizer) {
         d.shard = true;
         d.unit_bucket.assign(m->cfg.L + 2, 0);
@@ -409,13 +459,6 @@ int rbk_model_dp_init_ex(rbk_model* m, const void* id128, int rank, int world, c
         for (auto& e : d.weights_ready) RBK_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
         RBK_CUDA(cudaEventCreateWithFlags(&d.tail_done, cudaEventDisableTiming));
     }
-    d.watch = new DpWatch();
-    d.watch->device = m->ctx->device;
-    d.watch->timeout_s = timeout_s;
-    d.watch->comms[0] = comm;
-    d.watch->comms[1] = tail;
-    d.watch->th = std::thread([w = d.watch] { w->loop(); });
-    d.on = true;
     return RBK_OK;
 }
 
@@ -469,29 +512,66 @@ int rbk_model_dp_abort(rbk_model* m) {
 
 int rbk_model_dp_shutdown(rbk_model* m) {
     RBK_REQUIRE(m, "rbk_model_dp_shutdown: null model");
-    DpState& d = m->dp;
-    if (!d.on) return RBK_OK;
-    DpWatch* w = d.watch;
-    // Wait for the collectives in flight; the watchdog keeps running meanwhile, so a hung one
-    // is aborted after the timeout and this returns.
-    cudaStreamSynchronize(d.stream);
-    {
-        std::lock_guard<std::mutex> lk(w->mu);
-        w->stop = true;
+    return dp_close(m->dp);
+}
+
+// ---------------------------------------------------------------- kernel level --
+int rbk_dp_init(rbk_dp** out, int device, const void* id128, int rank, int world, const rbk_dp_opts* o) {
+    RBK_REQUIRE(out && id128 && world >= 1 && rank >= 0 && rank < world, "rbk_dp_init: bad arguments");
+    *out = nullptr;
+    rbk_dp* p = new rbk_dp();
+    int st = dp_open(p->d, device, id128, rank, world, o ? o->max_ctas : 0, o ? o->timeout_s : 0.0);
+    if (st == RBK_OK && cudaEventCreateWithFlags(&p->ready, cudaEventDisableTiming) != cudaSuccess) {
+        set_error("rbk_dp_init: cudaEventCreate failed");
+        dp_close(p->d);
+        st = RBK_ERR_CUDA;
     }
-    w->th.join();
-    if (w->comms[1] && w->comms[1] != w->comms[0]) ncclCommDestroy(w->comms[1]);
-    if (w->comms[0]) ncclCommDestroy(w->comms[0]);
-    for (cudaEvent_t e : w->all) cudaEventDestroy(e);
-    delete w;
-    for (auto& e : d.layer_done) cudaEventDestroy(e);
-    cudaEventDestroy(d.all_done);
-    for (auto& e : d.weights_ready) cudaEventDestroy(e);
-    if (d.tail_done) cudaEventDestroy(d.tail_done);
-    if (d.xbuf) cudaFree(d.xbuf);
-    cudaStreamDestroy(d.stream);
-    d = DpState();
+    if (st != RBK_OK) {
+        delete p;
+        return st;
+    }
+    *out = p;
     return RBK_OK;
+}
+
+int rbk_dp_bucket_ready(rbk_dp* dp, float* buf, int64_t n, void* stream) {
+    RBK_REQUIRE(dp && dp->d.on && buf && n > 0, "rbk_dp_bucket_ready: bad arguments");
+    RBK_TRY(rbk_dp_status(dp));
+    RBK_CUDA(cudaEventRecord(dp->ready, as_stream(stream)));
+    RBK_CUDA(cudaStreamWaitEvent(dp->d.stream, dp->ready, 0));
+    return allreduce(dp->d, buf, (size_t)n, false);
+}
+
+int rbk_dp_finish(rbk_dp* dp, void* stream) {
+    RBK_REQUIRE(dp && dp->d.on, "rbk_dp_finish: bad arguments");
+    RBK_TRY(rbk_dp_status(dp));
+    RBK_CUDA(cudaEventRecord(dp->d.all_done, dp->d.stream));
+    RBK_CUDA(cudaStreamWaitEvent(as_stream(stream), dp->d.all_done, 0));
+    return RBK_OK;
+}
+
+int rbk_dp_status(rbk_dp* dp) {
+    RBK_REQUIRE(dp, "rbk_dp_status: null handle");
+    const int s = dp_state_status(dp->d);
+    if (s != RBK_OK) set_error("data parallel: the communicator was aborted (%s)",
+                               s == RBK_ERR_TIMEOUT ? "a collective timed out" : "an NCCL / CUDA error");
+    return s;
+}
+
+int rbk_dp_abort(rbk_dp* dp) {
+    RBK_REQUIRE(dp, "rbk_dp_abort: null handle");
+    if (!dp->d.on || !dp->d.watch) return RBK_OK;
+    std::lock_guard<std::mutex> lk(dp->d.watch->mu);
+    dp->d.watch->abort_locked(RBK_ERR_NCCL);
+    return RBK_OK;
+}
+
+int rbk_dp_destroy(rbk_dp* dp) {
+    if (!dp) return RBK_OK;
+    const int st = dp_close(dp->d);
+    if (dp->ready) cudaEventDestroy(dp->ready);
+    delete dp;
+    return st;
 }
 
 }  // extern "C"

@@ -226,12 +226,9 @@ static int layer_attn_inputs(rbk_model* m, int l, int B, int S, cudaStream_t st)
             const half* Al = lo.p16 + (t ? 2 * szA : 0) + (int64_t)l * D * r;
             const half* Bl = lo.p16 + (t ? 3 * szA : szA) + (int64_t)l * r * D;
             half* xa = lo.xa + (int64_t)t * N * r;
-            // xa = h1 A  (A [D, r] row-major: B(n=j, k=d) = A[d*r + j] -> MN-major)
-            RBK_TRY(g.raw(N, r, D, la.h1, D, 0, Al, r, 1, xa, r, RBK_EPI_STORE_F16));
-            // q|v += scaling * xa B   (B [r, D]: B(n=d, k=j) = B[j*D + d] -> MN-major), in place
+            // xa = h1 A;  q|v += scaling * xa B, in place in the fused qkv rows
             half* col = la.qkv + (t ? 2 * D : 0);
-            RBK_TRY(g.raw(N, D, r, xa, r, 0, Bl, D, 1, col, 3 * D, RBK_EPI_STORE_F16, nullptr, col, 3 * D, nullptr,
-                          nullptr, lo.scaling));
+            RBK_TRY(rbk_lora_fwd(m->ctx, col, 3 * D, xa, la.h1, D, Al, Bl, N, D, r, D, lo.scaling, st));
         }
     }
     RBK_TRY(rbk_attn_fwd(m->ctx, la.ao, la.lse, la.qkv, B, S, H, m->cfg.hd, 1.0f / sqrtf((float)m->cfg.hd), st));
@@ -388,21 +385,9 @@ static int backward(rbk_model* m, const int* tokens, const int* targets, int B, 
                 float* dBl = lo.grad + (t ? 3 * szA : szA) + (int64_t)l * r * D;
                 const half* xa = lo.xa + (int64_t)t * N * r;
                 const half* dy = a.dqkv + (t ? 2 * D : 0);
-                Role wg(m->ctx, kWgrad);
-                // dB += s xa^T dy        [r, D]
-                RBK_TRY(g.raw(r, D, N, xa, r, 1, dy, 3 * D, 1, dBl, D, RBK_EPI_ACC_F32, nullptr, nullptr, 0, nullptr,
-                              nullptr, lo.scaling));
-                // dyb = s dy B^T         [N, r]
-                {
-                    Role dg(m->ctx, kDgrad);
-                    RBK_TRY(g.raw(N, r, D, dy, 3 * D, 0, Bl, D, 0, lo.dyb, r, RBK_EPI_STORE_F16, nullptr, nullptr, 0,
-                                  nullptr, nullptr, lo.scaling));
-                }
-                // dA += h1^T dyb         [D, r]
-                RBK_TRY(g.raw(D, r, N, la.h1, D, 1, lo.dyb, r, 1, dAl, r, RBK_EPI_ACC_F32));
-                // dh1 += dyb A^T         [N, D]  (A [D, r]: B(n=d, k=j) = A[d*r + j] -> K-major)
-                Role dg(m->ctx, kDgrad);
-                RBK_TRY(g.raw(N, D, r, lo.dyb, r, 0, Al, r, 0, a.dh, D, RBK_EPI_STORE_F16, nullptr, a.dh, D));
+                // dB += s xa^T dy;  dyb = s dy B^T;  dA += h1^T dyb;  dh1 += dyb A^T
+                RBK_TRY(rbk_lora_bwd(m->ctx, dAl, dBl, a.dh, D, lo.dyb, dy, 3 * D, la.h1, D, xa, Al, Bl, N, D, r, D,
+                                     lo.scaling, st));
             }
         }
         // ---- LN1: g_prev = dx1 + LN1'(dh1) ----

@@ -94,6 +94,9 @@ _SIGS = {
     "rbk_embed_fwd": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
     "rbk_embed_bwd": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
     "rbk_adam_tail": (i32, [vp, C.POINTER(TailArgs), vp]),
+    "rbk_lora_fwd": (i32, [vp, vp, i32, vp, vp, i32, vp, vp, i32, i32, i32, i32, f32, vp]),
+    "rbk_lora_bwd": (i32, [vp, vp, vp, vp, i32, vp, vp, i32, vp, i32, vp, vp, vp, i32, i32, i32, i32, f32, vp]),
+    "rbk_lora_adam": (i32, [vp, C.POINTER(TailArgs), vp]),
     "rbk_gemm": (i32, [vp, C.POINTER(GemmDesc), vp]),
     "rbk_linear_fwd": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, vp]),
     "rbk_gemm_dgrad": (i32, [vp, vp, vp, vp, i32, i32, i32, vp, vp]),
@@ -124,6 +127,12 @@ _SIGS = {
     "rbk_model_dp_init_ex": (i32, [vp, vp, i32, i32, C.POINTER(DpOpts)]),
     "rbk_model_dp_status": (i32, [vp]),
     "rbk_model_dp_abort": (i32, [vp]),
+    "rbk_dp_init": (i32, [C.POINTER(vp), i32, vp, i32, i32, C.POINTER(DpOpts)]),
+    "rbk_dp_bucket_ready": (i32, [vp, vp, i64, vp]),
+    "rbk_dp_finish": (i32, [vp, vp]),
+    "rbk_dp_status": (i32, [vp]),
+    "rbk_dp_abort": (i32, [vp]),
+    "rbk_dp_destroy": (i32, [vp]),
     "rbk_model_dp_shard_ranges": (i32, [vp, C.POINTER(C.c_int64), i32, C.POINTER(i32)]),
     "rbk_model_dp_gather_state": (i32, [vp, vp]),
     "rbk_model_zero_grad": (i32, [vp, vp]),

@@ -180,6 +180,29 @@ def adam_tail(p32, g, m, v, p16, scaler_buf, lr, b1=0.9, b2=0.999, eps=1e-8, wd=
     call("rbk_adam_tail", ctx().handle, C.byref(a), _s())
 
 
+# --------------------------------------------------------------------- LoRA --
+
+def lora_fwd(x, A, B, y, scaling, xa=None):
+    """One LoRA adapter (rbk_lora_fwd): xa = x A, y += scaling xa B (y in place, any row
+    stride).  x [N, in], A [in, r], B [r, out] FP16.  Returns xa."""
+    N, in_ = x.shape[0], A.shape[0]
+    r, out = B.shape
+    xa = torch.empty(N, r, dtype=torch.float16, device=x.device) if xa is None else xa
+    call("rbk_lora_fwd", ctx().handle, _p(y), y.stride(0), _p(xa), _p(x), x.stride(0), _p(A), _p(B), N, in_, r, out,
+         C.c_float(scaling), _s())
+    return xa
+
+
+def lora_bwd(dy, x, xa, A, B, scaling, dA, dB, dx=None):
+    """Its backward (rbk_lora_bwd): dB += s xa^T dy, dA += x^T (s dy B^T), dx += (s dy B^T) A^T."""
+    N, in_ = x.shape[0], A.shape[0]
+    r, out = B.shape
+    dyb = torch.empty(N, r, dtype=torch.float16, device=x.device)
+    call("rbk_lora_bwd", ctx().handle, _p(dA), _p(dB), _p(dx) if dx is not None else None,
+         dx.stride(0) if dx is not None else 0, _p(dyb), _p(dy), dy.stride(0), _p(x), x.stride(0), _p(xa), _p(A), _p(B),
+         N, in_, r, out, C.c_float(scaling), _s())
+
+
 # --------------------------------------------------------------------- GEMM --
 
 def gemm(A, B, M, N, K, a_major=0, b_major=0, C_out=None, epilogue=EPI_STORE_F16, bias=None, aux=None,

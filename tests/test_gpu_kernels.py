@@ -467,3 +467,60 @@ def test_adam_tail_barrier_timeout_is_reported_and_recovers(ops, ora):
     ep, eg, em, ev = p.copy(), g.copy(), m.copy(), v.copy()
     ora.adam_tail(ep, eg, em, ev, [0], [n], 1e-3, 0.9, 0.999, 1e-8, 0.1, 1, osc, 0.0)
     assert rel(tp.cpu().numpy(), ep) < 1e-6 and rel(tm.cpu().numpy(), em) < 1e-5
+
+
+# -------------------------------------------------------- LoRA (kernel level) --
+
+def test_lora_kernel_level_fwd_bwd_adam(ops):
+    """rbk_lora_fwd / _bwd on a q-column slice of a fused qkv (row stride 3D) against a float64
+    restatement of the adapter math (src/lora.h:223-229) on the same FP16 inputs, with xa and dyb
+    rounded to FP16 where the kernels store them; rbk_lora_adam equals rbk_adam_tail."""
+    import ctypes
+
+    from rbk._lib import TailArgs, lib
+    rng = np.random.default_rng(31)
+    N, D, r, s = 512, 768, 16, 2.0
+    f16 = lambda a: torch.from_numpy(a.astype(np.float16)).cuda()  # noqa: E731
+    x = f16(rng.standard_normal((N, D)))
+    A = f16(0.02 * rng.standard_normal((D, r)))
+    Bm = f16(0.05 * rng.standard_normal((r, D)))
+    qkv = f16(rng.standard_normal((N, 3 * D)))
+    y0 = qkv[:, :D].double().cpu().numpy()
+    kv0 = qkv[:, D:].clone()
+    xa = ops.lora_fwd(x, A, Bm, qkv[:, :D], s)
+    torch.cuda.synchronize()
+    X, Am, Bd = (t.double().cpu().numpy() for t in (x, A, Bm))
+    xa_ref = X @ Am
+    assert rel(xa.double().cpu().numpy(), xa_ref) < 2e-3
+    xa16 = xa.double().cpu().numpy()
+    y_ref = y0 + s * xa16 @ Bd
+    assert rel(qkv[:, :D].double().cpu().numpy(), y_ref) < 2e-3
+    assert torch.equal(qkv[:, D:], kv0)                       # the k and v columns are untouched
+    dy = f16(rng.standard_normal((N, 3 * D)))[:, :D]
+    dx = f16(rng.standard_normal((N, D)))
+    dx0 = dx.double().cpu().numpy()
+    dA = torch.zeros(D, r, device="cuda")
+    dB = torch.zeros(r, D, device="cuda")
+    ops.lora_bwd(dy, x, xa, A, Bm, s, dA, dB, dx)
+    torch.cuda.synchronize()
+    DY = dy.double().cpu().numpy()
+    assert rel(dB.double().cpu().numpy(), s * xa16.T @ DY) < 1e-4
+    dyb = (s * DY @ Bd.T).astype(np.float16).astype(np.float64)
+    assert rel(dA.double().cpu().numpy(), X.T @ dyb) < 1e-3
+    assert rel(dx.double().cpu().numpy(), dx0 + dyb @ Am.T) < 2e-3
+    # lora_optimizer_step: the fused tail over an adapter arena
+    n = 4 * D * r
+    p = (0.02 * rng.standard_normal(n)).astype(np.float32)
+    g = (rng.standard_normal(n)).astype(np.float32)
+    outs = []
+    for fn in ("rbk_adam_tail", "rbk_lora_adam"):
+        tp, tg = torch.from_numpy(p.copy()).cuda(), torch.from_numpy(g.copy()).cuda()
+        tm, tv = torch.zeros(n, device="cuda"), torch.zeros(n, device="cuda")
+        sc = ops.new_scaler(1.0, 2000)
+        a = TailArgs()
+        a.p32, a.g, a.m, a.v, a.p16, a.n = tp.data_ptr(), tg.data_ptr(), tm.data_ptr(), tv.data_ptr(), None, n
+        a.lr, a.beta1, a.beta2, a.eps, a.weight_decay, a.t, a.scaler = 1e-3, 0.9, 0.999, 1e-8, 0.0, 1, sc.data_ptr()
+        assert getattr(lib(), fn)(ops.ctx().handle, ctypes.byref(a), ops._s()) == 0
+        torch.cuda.synchronize()
+        outs.append(tp.cpu())
+    assert torch.equal(outs[0], outs[1])
