@@ -18,8 +18,9 @@
 //   warps 2..5  epilogue: tcgen05.ld 32x32b (one TMEM lane quarter per warp,
 //               one output row per thread), fused bias / residual / GELU /
 //               GELU' / FP32 accumulation, direct 16-byte global stores.
-// Bias gradients (row sums of A over K when A = dY^T) come from one extra
-// N=16 MMA per k-step against a constant ones tile, issued by the n=0 tiles.
+// Bias gradients (row sums of A over K when A = dY^T): in this 1-CTA kernel one
+// extra N=16 MMA per k-step against a constant ones tile, issued by the n=0
+// tiles; in the CTA-pair kernel below an extra warp sums A from shared memory.
 // Every mbarrier wait is bounded (globaltimer); on expiry the kernel records
 // RBK_ERR_TIMEOUT, drains, frees TMEM and returns.
 // No cluster multicast is used anywhere.
@@ -750,22 +751,49 @@ __device__ __forceinline__ void epilogue_chunk_f32_tma(const Params& p, int m0, 
 // the MMA thread; tempty[b] lives in the even CTA and takes the arrivals of
 // both CTAs' epilogue warps.  Bounded waits as in gemm_kernel.
 constexpr int kPairStages = 6;
+// Shared-memory loads and FP32 += FP16 pair additions for the row warp.
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+    uint2 v;
+    asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ void add_f16x2(float& c0, float& c1, uint32_t a) {
+    asm("{.reg .f16 al, ah;\n\t"
+        "mov.b32 {al, ah}, %2;\n\t"
+        "add.rn.f32.f16 %0, al, %0;\n\t"
+        "add.rn.f32.f16 %1, ah, %1;}"
+        : "+f"(c0), "+f"(c1)
+        : "r"(a));
+}
+
 // Per-warp epilogue staging: two 2 KB tiles for the tensor stores / reduce-adds; the FP32
-// epilogues also keep a 2 KB ones tile for row sums and run one operand stage fewer (their
-// K = tokens mainloops are long).
+// epilogues run one operand stage fewer (their K = tokens mainloops are long).
+constexpr int kRowWarps = 4;                    // ROW: warp w owns the operand stages s with s % 4 == w
 template <int EPI, bool ROW>
 struct PairEpi {
     static constexpr bool TMA = EPI == RBK_EPI_STORE_F16 || EPI == RBK_EPI_BIAS_GELU || EPI == RBK_EPI_GELU_BWD;
     static constexpr int STAGES = TMA ? kPairStages : kPairStages - 1;
     static constexpr int WARP_STAGE = kTmaStageBytes;
-    static constexpr int ONES_BYTES = EPI == RBK_EPI_ACC_F32 && ROW ? 2048 : 0;
+    static constexpr int PART_BYTES = ROW ? kRowWarps * BM * 4 : 0;     // per-warp row partials
     static constexpr int SMEM = 1024 + STAGES * (BM * BK * 2 + 128 * BK * 2) + kEpiWarps * WARP_STAGE +
-                                ONES_BYTES + 256;
+                                PART_BYTES + 256;
+    static constexpr int THREADS = kThreads + (ROW ? 32 * kRowWarps : 0);
 };
-// ROW: the ACC_F32 variant that can also produce row sums (bias gradients, dbias_rows); the
-// variant without keeps the ones tile and the extra MMA out of the kernel.
+// ROW: the ACC_F32 instance that also produces the row sums of A (the bias gradient of a weight
+// gradient, A = dY^T, into dbias_rows).  Four row warps per CTA (warp w owns the stages
+// s % 4 == w) sum the CTA's 128 rows of A of the n = 0 tiles from shared memory after the MMAs
+// have consumed a stage: for those tiles the MMA thread's commits go to a per-stage `consumed`
+// barrier in each CTA, and the stage's row warp frees it for the producer; the other tiles free
+// their stages directly.  At the end of an n = 0 tile the four partials are added in warp
+// order (bounded mbarrier hand-off), so the result does not depend on timing.  The tensor pipe
+// does no row-sum work and both TMEM accumulator buffers stay in use.
 template <int EPI, bool ROW>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(PairEpi<EPI, ROW>::THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmX,
                      const __grid_constant__ CUtensorMap tmP, const Params p) {
@@ -780,36 +808,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* gbase = smem_raw + (base - raw);
     const uint32_t sA0 = base;
     const uint32_t epi_stage = base + STAGES * STAGE_BYTES;
-    const uint32_t ones = epi_stage + kEpiWarps * kWarpStage;       // FP32 epilogues: 2 KB of FP16 ones
-    const uint32_t bars = ones + PairEpi<EPI, ROW>::ONES_BYTES;
+    const uint32_t part_s = epi_stage + kEpiWarps * kWarpStage;      // ROW: float [kRowWarps][BM]
+    const uint32_t bars = part_s + PairEpi<EPI, ROW>::PART_BYTES;
     uint8_t* gbars = gbase + (bars - base);
     auto full_bar = [&](int s) { return bars + 8u * s; };
     auto empty_bar = [&](int s) { return bars + 8u * (STAGES + s); };
     auto tfull_bar = [&](int b) { return bars + 8u * (2 * STAGES + b); };
     auto tempty_bar = [&](int b) { return bars + 8u * (2 * STAGES + 2 + b); };
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbars + 8 * (2 * STAGES + 4));
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(gbars + 8 * (2 * STAGES + 4) + 8);
+    auto consumed_bar = [&](int s) { return bars + 8u * (2 * STAGES + 4 + s); };   // ROW only
+    const uint32_t parts_rdy = bars + 8u * (3 * STAGES + 4);                   // ROW: partials written
+    const uint32_t parts_free = parts_rdy + 8u;                                 // ROW: partials read
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbars + 8 * (3 * STAGES + 6));
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(gbars + 8 * (3 * STAGES + 6) + 8);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_rank();
     const bool leader = rank == 0;
     const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
-    // Row sums of A (the bias gradient of a weight gradient, A = dY^T): an extra N = 16 pair MMA per
-    // k-step against a ones tile, accumulated at TMEM column 256, so only one 256-column accumulator
-    // buffer remains (the K = tokens mainloops of weight gradients dwarf their epilogues).
-    constexpr bool kRowsumEpi = EPI == RBK_EPI_ACC_F32 && ROW;
-    const bool rowsum_mode = kRowsumEpi && p.dbias_rows != nullptr;
-    const int nbuf = rowsum_mode ? 1 : 2;
-    if constexpr (kRowsumEpi) {
-        uint32_t* o = reinterpret_cast<uint32_t*>(gbase + (ones - base));
-        for (int i = threadIdx.x; i < PairEpi<EPI, ROW>::ONES_BYTES / 4; i += blockDim.x) o[i] = 0x3C003C00u;
-        fence_proxy_async();
-    }
+    constexpr bool kRowWarp = EPI == RBK_EPI_ACC_F32 && ROW;
+    constexpr int nbuf = 2;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(full_bar(s), 1);
             mbar_init(empty_bar(s), 1);
+            if (kRowWarp) mbar_init(consumed_bar(s), 1);
+        }
+        if (kRowWarp) {
+            mbar_init(parts_rdy, kRowWarps);
+            mbar_init(parts_free, 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(tfull_bar(b), 1);
@@ -868,7 +895,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------ MMA issuer (even CTA) ----------------
         if (leader && lane == 0) {
             const uint32_t idesc = idesc_f16_m256(BN, p.a_mn, p.b_mn);
-            const uint32_t idesc1 = idesc_f16_m256(16, p.a_mn, 0);
             const uint32_t a_lbo = p.a_mn ? 8192u : 16u, b_lbo = p.b_mn ? 8192u : 16u;
             const uint32_t a_kstep = p.a_mn ? 2048u : 32u, b_kstep = p.b_mn ? 2048u : 32u;
             int stage = 0, buf = 0;
@@ -876,41 +902,145 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int u = pair; u < p.units && !*abort_flag; u += num_pairs) {
                 int mb, nb, kb0, kb1;
                 decode_unit(p, u, mb, nb, kb0, kb1);
-                const bool rowsum = rowsum_mode && nb == 0;
+                const bool rows_tile = kRowWarp && p.dbias_rows != nullptr && nb == 0;
                 if (!mbar_wait(tempty_bar(buf), bphase ^ 1, abort_flag)) break;
                 fence_after();
                 const uint32_t dacc = tmem + buf * BN;
-                // The k-loop comes in two versions, so the issuing thread's stream of MMAs carries no
-                // per-MMA branch: a test between back-to-back MMAs cost the accumulating GEMMs about
-                // 20% of their rate even when no row sums were asked for.
-                auto mainloop = [&](auto with_rows) -> bool {
-                    constexpr bool kRows = decltype(with_rows)::value;
-                    for (int kb = kb0; kb < kb1; ++kb) {
-                        if (!mbar_wait(full_bar(stage), phase, abort_flag)) return false;
-                        fence_after();
-                        const uint32_t sa = sA0 + stage * STAGE_BYTES;
-                        const uint32_t sb = sa + A_BYTES;
+                bool ok = true;
+                for (int kb = kb0; kb < kb1; ++kb) {
+                    if (!mbar_wait(full_bar(stage), phase, abort_flag)) { ok = false; break; }
+                    fence_after();
+                    const uint32_t sa = sA0 + stage * STAGE_BYTES;
+                    const uint32_t sb = sa + A_BYTES;
 #pragma unroll
-                        for (int k = 0; k < BK / UMMA_K; ++k) {
-                            const uint64_t ad = sdesc(sa + k * a_kstep, a_lbo, 1024);
-                            const uint32_t acc = (kb > kb0 || k > 0) ? 1u : 0u;
-                            mma_f16_pair(dacc, ad, sdesc(sb + k * b_kstep, b_lbo, 1024), idesc, acc);
-                            if constexpr (kRows) mma_f16_pair(tmem + 256, ad, sdesc(ones + k * 32, 16, 1024), idesc1, acc);
-                        }
-                        mma_commit_pair(empty_bar(stage));
-                        mma_commit_pair(mapa_shared(empty_bar(stage), 1));
-                        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+                    for (int k = 0; k < BK / UMMA_K; ++k) {
+                        const uint32_t acc = (kb > kb0 || k > 0) ? 1u : 0u;
+                        mma_f16_pair(dacc, sdesc(sa + k * a_kstep, a_lbo, 1024), sdesc(sb + k * b_kstep, b_lbo, 1024),
+                                     idesc, acc);
                     }
-                    return true;
-                };
-                bool ok;
-                if constexpr (kRowsumEpi) ok = rowsum ? mainloop(std::true_type{}) : mainloop(std::false_type{});
-                else ok = mainloop(std::false_type{});
+                    // the stage is consumed: free it (row-sum tiles: the stage's row warp in each CTA
+                    // reads it first)
+                    const uint32_t rel = rows_tile ? consumed_bar(stage) : empty_bar(stage);
+                    mma_commit_pair(rel);
+                    mma_commit_pair(mapa_shared(rel, 1));
+                    if (++stage == STAGES) { stage = 0; phase ^= 1; }
+                }
                 if (!ok) break;
                 mma_commit_pair(tfull_bar(buf));
                 mma_commit_pair(mapa_shared(tfull_bar(buf), 1));
                 if (++buf == nbuf) { buf = 0; bphase ^= 1; }
             }
+        }
+    } else if (kRowWarp && warp >= 2 + kEpiWarps) {
+        // ------------------------------ row sums of A (both CTAs) ------------
+        // Row warp rw owns the operand stages s % 4 == rw.  On the tiles of n block 0 every use of
+        // them passes through here after the MMAs have read it: the CTA's 128 rows of A over the
+        // stage's 64 k are added into FP32 sums, then the stage is freed for the producer.
+        const int rw = warp - 2 - kEpiWarps;
+        float* part = reinterpret_cast<float*>(gbase + (part_s - base));
+        uint32_t j = 0;                                  // k blocks of this pair so far (all tiles)
+        static_assert(STAGES <= 2 * kRowWarps, "a row warp owns at most two stages");
+        uint32_t uses0 = 0, uses1 = 0;                   // row-tile uses of the two owned stages
+        uint32_t rphase = 0;                             // row-sum tiles so far (hand-off parity)
+        bool ok = true;
+        for (int u = pair; ok && u < p.units; u += num_pairs) {
+            int mb, nb, kb0, kb1;
+            decode_unit(p, u, mb, nb, kb0, kb1);
+            const bool rows = p.dbias_rows != nullptr && nb == 0;
+            if (!rows) {                                 // its stages are freed by the MMA thread
+                j += (uint32_t)(kb1 - kb0);
+                continue;
+            }
+            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            for (int kb = kb0; kb < kb1; ++kb, ++j) {
+                const int stage = (int)(j % STAGES);
+                if (stage % kRowWarps != rw) continue;
+                const bool second = stage >= kRowWarps;
+                const uint32_t n = second ? uses1++ : uses0++;
+                // the MMAs have read the stage (their commit follows the TMA's completion of it)
+                ok = __all_sync(0xffffffffu, mbar_wait(consumed_bar(stage), n & 1, abort_flag));
+                if (!ok) break;
+                {
+                    fence_proxy_async();                    // the TMA (async proxy) wrote the stage
+                    const uint32_t sa = sA0 + stage * STAGE_BYTES;
+                    if (p.a_mn) {
+                        // two boxes of 64 rows (k) x 128 B (64 m); 16-byte chunk c of row k sits at
+                        // c ^ (k & 7).  Lane l: the 8 m of chunk l % 8 of box (l / 8) % 2, rows
+                        // k = 32 (l / 16) .. + 31
+                        const uint32_t box = sa + (uint32_t)((lane >> 3) & 1) * 8192u;
+                        const uint32_t c = (uint32_t)(lane & 7), k0 = (uint32_t)(lane >> 4) * 32u;
+#pragma unroll 8
+                        for (uint32_t k = k0; k < k0 + 32u; ++k) {
+                            const uint4 v = lds128(box + k * 128u + ((c ^ (k & 7u)) << 4));
+                            add_f16x2(acc[0], acc[1], v.x);
+                            add_f16x2(acc[2], acc[3], v.y);
+                            add_f16x2(acc[4], acc[5], v.z);
+                            add_f16x2(acc[6], acc[7], v.w);
+                        }
+                    } else {
+                        // 128 rows (m) x 128 B (64 k); chunk c of row m at c ^ (m & 7).  Lane l: rows
+                        // l + 32 i, i < 4 (sums in acc[i])
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const uint32_t m = (uint32_t)(lane + 32 * i);
+                            float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+                            for (uint32_t c = 0; c < 8; ++c) {
+                                const uint4 v = lds128(sa + m * 128u + ((c ^ (m & 7u)) << 4));
+                                add_f16x2(s0, s1, v.x);
+                                add_f16x2(s0, s1, v.y);
+                                add_f16x2(s0, s1, v.z);
+                                add_f16x2(s0, s1, v.w);
+                            }
+                            acc[i] += s0 + s1;
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(empty_bar(stage));   // the producer may refill the stage
+            }
+            if (!ok) break;
+            // this warp's partial sums of the tile's 128 rows -> part[rw][*]
+            if (p.a_mn) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], 16);   // both k halves
+            }
+            ok = __all_sync(0xffffffffu, mbar_wait(parts_free, (rphase & 1) ^ 1, abort_flag));
+            if (!ok) break;
+            if (p.a_mn) {
+                if (lane < 16) {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) part[rw * BM + 8 * lane + e] = acc[e];
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) part[rw * BM + lane + 32 * i] = acc[i];
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(parts_rdy);
+            if (rw == 0) {
+                // the four partials in warp order, then this rank's 128 rows of dbias
+                ok = __all_sync(0xffffffffu, mbar_wait(parts_rdy, rphase & 1, abort_flag));
+                if (ok) {
+                    const int split = u % p.splits;
+                    const int mode = acc_mode(p, split);
+                    const int mbase = mb * 2 * BM + (int)rank * BM;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int r = lane + 32 * i, m = mbase + r;
+                        const float v = ((part[r] + part[BM + r]) + part[2 * BM + r]) + part[3 * BM + r];
+                        if (m < p.M) {
+                            const float bv = p.alpha * v;
+                            if (mode == kAccPlane) p.part_rows[(size_t)(split - 1) * p.M + m] = bv;
+                            else if (mode == kAccOwner) p.dbias_rows[m] += bv;
+                            else atomicAdd(p.dbias_rows + m, bv);
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(parts_free);
+                }
+            }
+            ++rphase;
         }
     } else {
         // ------------------------------ epilogue (both CTAs) -----------------
@@ -960,18 +1090,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     epilogue_chunk_f32_tma<EPI>(p, m0, nb * BN + c * 32, r, my_stage, my_stage_s, lane, &tmC, &tmP,
                                                 split, mode, cv);
-                }
-            }
-            const bool rowsum_tile = kRowsumEpi && rowsum_mode && nb == 0;
-            if (rowsum_tile && c0 == 0) {   // one warp per lane quarter
-                const uint32_t v = tmem_ld1(tmem + ((uint32_t)(q * 32) << 16) + 256);
-                tmem_wait_ld();
-                const int m = m0 + lane;
-                if (m < p.M) {
-                    const float bv = p.alpha * __uint_as_float(v);
-                    if (mode == kAccPlane) p.part_rows[(size_t)(split - 1) * p.M + m] = bv;
-                    else if (mode == kAccOwner) p.dbias_rows[m] += bv;
-                    else atomicAdd(p.dbias_rows + m, bv);
                 }
             }
             // the accumulator reads are complete (tcgen05.wait::ld); the tile's global stores need not
@@ -1054,7 +1172,7 @@ int launch_pair(rbk_ctx* ctx, const rbk_gemm_desc* d, Params& p, cudaStream_t st
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(PairEpi<EPI, ROW>::THREADS);
     cfg.dynamicSmemBytes = SMEM;
     cfg.stream = st;
     cfg.attrs = attr;

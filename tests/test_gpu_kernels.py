@@ -524,3 +524,24 @@ def test_lora_kernel_level_fwd_bwd_adam(ops):
         torch.cuda.synchronize()
         outs.append(tp.cpu())
     assert torch.equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("M,N,K,splits", [(300, 512, 1000, 0), (520, 768, 4096, 3)])
+def test_gemm_row_sums_k_major_a(ops, M, N, K, splits):
+    """dbias_rows with a K-major A on the CTA-pair tiles (the row warp reads 128-byte rows of A);
+    split K adds the partial row sums atomically."""
+    rng = np.random.default_rng(M + K)
+    A = _mk(rng, M, K)
+    B = _mk(rng, N, K)
+    C0 = rng.standard_normal((M, N)).astype(np.float32)
+    r0 = rng.standard_normal(M).astype(np.float32)
+    C = torch.from_numpy(C0.copy()).cuda()
+    rows = torch.from_numpy(r0.copy()).cuda()
+    ops.gemm(h(A), h(B), M, N, K, 0, 0, C_out=C, epilogue=ops.EPI_ACC_F32, dbias_rows=rows, alpha=0.5,
+             split_k=splits)
+    torch.cuda.synchronize()
+    A64 = A.astype(np.float16).astype(np.float64)
+    ref = C0 + 0.5 * A64 @ B.astype(np.float16).astype(np.float64).T
+    assert rel(C.cpu().numpy(), ref) < F32_TOL
+    assert rel(rows.cpu().numpy(), r0 + 0.5 * A64.sum(1)) < F32_TOL
+    assert ops.device_error() == 0
