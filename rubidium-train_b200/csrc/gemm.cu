@@ -773,7 +773,7 @@ __device__ __forceinline__ void add_f16x2(float& c0, float& c1, uint32_t a) {
 
 // Per-warp epilogue staging: two 2 KB tiles for the tensor stores / reduce-adds; the FP32
 // epilogues run one operand stage fewer (their K = tokens mainloops are long).
-constexpr int kRowWarps = 4;                    // ROW: warp w owns the operand stages s with s % 4 == w
+constexpr int kRowWarps = 5;                    // ROW: row warp w owns operand stage w
 template <int EPI, bool ROW>
 struct PairEpi {
     static constexpr bool TMA = EPI == RBK_EPI_STORE_F16 || EPI == RBK_EPI_BIAS_GELU || EPI == RBK_EPI_GELU_BWD;
@@ -785,11 +785,11 @@ struct PairEpi {
     static constexpr int THREADS = kThreads + (ROW ? 32 * kRowWarps : 0);
 };
 // ROW: the ACC_F32 instance that also produces the row sums of A (the bias gradient of a weight
-// gradient, A = dY^T, into dbias_rows).  Four row warps per CTA (warp w owns the stages
-// s % 4 == w) sum the CTA's 128 rows of A of the n = 0 tiles from shared memory after the MMAs
-// have consumed a stage: for those tiles the MMA thread's commits go to a per-stage `consumed`
+// gradient, A = dY^T, into dbias_rows).  One row warp per operand stage (kRowWarps per CTA)
+// sums the CTA's 128 rows of A of the n = 0 tiles from shared memory after the MMAs have
+// consumed a stage: for those tiles the MMA thread's commits go to a per-stage `consumed`
 // barrier in each CTA, and the stage's row warp frees it for the producer; the other tiles free
-// their stages directly.  At the end of an n = 0 tile the four partials are added in warp
+// their stages directly.  At the end of an n = 0 tile the warps' partials are added in warp
 // order (bounded mbarrier hand-off), so the result does not depend on timing.  The tensor pipe
 // does no row-sum work and both TMEM accumulator buffers stay in use.
 template <int EPI, bool ROW>
@@ -933,7 +933,7 @@ __global__ void __launch_bounds__(PairEpi<EPI, ROW>::THREADS, 1)
         }
     } else if (kRowWarp && warp >= 2 + kEpiWarps) {
         // ------------------------------ row sums of A (both CTAs) ------------
-        // Row warp rw owns the operand stages s % 4 == rw.  On the tiles of n block 0 every use of
+        // Row warp rw owns the operand stages s % kRowWarps == rw.  On the tiles of n block 0 every use of
         // them passes through here after the MMAs have read it: the CTA's 128 rows of A over the
         // stage's 64 k are added into FP32 sums, then the stage is freed for the producer.
         const int rw = warp - 2 - kEpiWarps;
@@ -1019,7 +1019,7 @@ __global__ void __launch_bounds__(PairEpi<EPI, ROW>::THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(parts_rdy);
             if (rw == 0) {
-                // the four partials in warp order, then this rank's 128 rows of dbias
+                // the partials in warp order, then this rank's 128 rows of dbias
                 ok = __all_sync(0xffffffffu, mbar_wait(parts_rdy, rphase & 1, abort_flag));
                 if (ok) {
                     const int split = u % p.splits;
@@ -1028,7 +1028,9 @@ __global__ void __launch_bounds__(PairEpi<EPI, ROW>::THREADS, 1)
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         const int r = lane + 32 * i, m = mbase + r;
-                        const float v = ((part[r] + part[BM + r]) + part[2 * BM + r]) + part[3 * BM + r];
+                        float v = part[r];
+#pragma unroll
+                        for (int w = 1; w < kRowWarps; ++w) v += part[w * BM + r];
                         if (m < p.M) {
                             const float bv = p.alpha * v;
                             if (mode == kAccPlane) p.part_rows[(size_t)(split - 1) * p.M + m] = bv;
