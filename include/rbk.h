@@ -532,6 +532,7 @@ int rbk_model_dp_abort(rbk_model* m);
  * (no rbk_model): the same non-blocking communicators, high-priority
  * communication stream and watchdog as rbk_model_dp_init_ex (opts: max_ctas,
  * timeout_s; NULL for the defaults; bucket_bytes and shard_optimizer unused).
+ * rbk_dp_init makes `device` the calling thread's current device.
  *   rbk_dp_bucket_ready: sum-all-reduce buf[0, n) FP32 in place over the ranks,
  *     on the communication stream, after the work enqueued on `stream` so far
  *     (call it as soon as a bucket's gradients are final; it overlaps what
