@@ -391,6 +391,105 @@ def microbench(ops, torch, hbm_peak, reps=20):
     return res
 
 
+def tokenizer_bench(torch, hbm_peak, cpu=True):
+    """The GPU BPE tokenizer (rbk_bpe_*, the data path of src/tokenizer_cuda.cu:90-203) on a
+    GPT-2-sized synthetic tokenizer (50257 ids, 49996 rules; seeded Zipf text, no dataset offline):
+      encode_2048: 16384 strings x 2047 bytes -> rows of 2048 tokens, inputs resident (value) and
+                   from host strings through rbk_bpe_encode_batch (e2e: packing + H2D + kernel);
+      encode_256:  65536 strings x 254 bytes at max_seq_len 256, the reference kernel's domain (one
+                   block of 256 threads per string), with the reference's own algorithm (its kernels
+                   compiled for the CPU, serial) and the oracle port timed on bounded samples;
+      decode_2048: the encode_2048 rows back to strings of up to 4096 bytes.
+    Algorithmic bytes: text + offsets (8) + lengths (4) in, rows (4 x max_seq_len) + lengths (4) out."""
+    import numpy as np
+
+    import oracle
+    from rbk.tokenizer import GPUTokenizer, pack_strings, synthetic_batch, synthetic_corpus, synthetic_tables
+    vocab, merges, words = synthetic_tables()
+    corpus = synthetic_corpus(words, 1 << 25, seed=9)
+    tk = GPUTokenizer(vocab, merges)
+    res = {"tokenizer": "synthetic GPT-2-sized: 50257 ids, %d rules, Zipf(1.1) pseudo-words" % tk.num_rules}
+    st = torch.cuda.current_stream()
+
+    def dev_time(fn, n):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(st)
+        for _ in range(n):
+            fn()
+        e.record(st)
+        torch.cuda.synchronize()
+        return s.elapsed_time(e) / n
+
+    for name, B, L, ms in (("encode_2048", 16384, 2047, 2048), ("encode_256", 65536, 254, 256)):
+        strs = synthetic_batch(corpus, B, L, seed=4)
+        data, offs, lens = pack_strings(strs)
+        d_data, d_offs, d_lens = (torch.from_numpy(a.copy()).cuda() for a in (data, offs, lens))
+        rows = torch.empty(B, ms, dtype=torch.int32, device="cuda")
+        rl = torch.empty(B, dtype=torch.int32, device="cuda")
+        ms_launch = dev_time(lambda: tk.encode(d_data, d_offs, d_lens, ms, out=rows, out_lengths=rl), 10)
+        n_tok = int(rl.sum().item()) - B
+        by = data.size + 12 * B + 4 * B * ms + 4 * B
+        gbs = by / ms_launch / 1e6
+        ent = {"strings": B, "bytes_per_string": L, "max_seq_len": ms, "ms_per_launch": ms_launch,
+               "text_MB_per_s": data.size / ms_launch / 1e3, "tokens_per_s": n_tok / ms_launch * 1e3,
+               "strings_per_s": B / ms_launch * 1e3, "tokens_per_string": n_tok / B,
+               "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
+                            "frac": gbs / hbm_peak, "algorithmic_bytes_per_launch": by,
+                            "note": "the pair lookups hit L1/L2 (a 4 MB table); DRAM carries only text in and rows out"}}
+        if name == "encode_2048":
+            # e2e: host strings -> device rows, through the reference-facing entry
+            for _ in range(2):
+                tk.encode_batch(strs, ms, out=rows, out_lengths=rl)
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            reps = 5
+            for _ in range(reps):
+                tk.encode_batch(strs, ms, out=rows, out_lengths=rl)
+            lh = rl.cpu()
+            dt = (time.perf_counter() - t0) / reps
+            ent["e2e"] = {"text_MB_per_s": data.size / dt / 1e6, "strings_per_s": B / dt, "ms_per_call": dt * 1e3,
+                          "h2d_bytes_per_call": int(data.size + 12 * B), "d2h_bytes": int(lh.numel() * 4),
+                          "path": "rbk_bpe_encode_batch (host strings: pack into pinned staging, one H2D, kernel)"}
+            # decode the rows back
+            out = torch.empty(B, 4096, dtype=torch.uint8, device="cuda")
+            ms_dec = dev_time(lambda: tk.decode_batch(rows, rl, 4096, out=out), 10)
+            dby = 4 * (n_tok + B) + 4 * B + data.size + B   # tokens read up to the EOS, text + NULs written
+            ent_dec = {"strings": B, "ms_per_launch": ms_dec, "text_MB_per_s": data.size / ms_dec / 1e3,
+                       "roofline": {"bound": "hbm", "achieved": dby / ms_dec / 1e6, "peak": hbm_peak, "unit": "GB/s",
+                                    "frac": dby / ms_dec / 1e6 / hbm_peak, "algorithmic_bytes_per_launch": dby}}
+            ok = bytes(out[7].cpu().numpy()).split(b"\0", 1)[0] == strs[7]
+            ent_dec["round_trip_row7"] = bool(ok)
+            res["decode_2048"] = ent_dec
+            del out
+        if cpu:
+            # oracle port (hash-map restatement, 1 thread) on a bounded sample
+            k = 256 if ms == 2048 else 2048
+            sd, so, sl = pack_strings(strs[:k])
+            t0 = time.perf_counter()
+            orow, orl, _ = oracle.bpe_encode(merges, sd, so, sl, ms)
+            dt = time.perf_counter() - t0
+            same = bool(np.array_equal(orl, rl[:k].cpu().numpy()) and np.array_equal(orow, rows[:k].cpu().numpy()))
+            ent["cpu_baseline_port"] = {"value": sd.size / dt / 1e6, "unit": "text MB/s", "cores": 1, "kind": "port",
+                                        "sample": f"first {k} strings", "rows_equal_gpu": same}
+            if ms == 256 and oracle.reftok_lib() is not None:
+                kr = 24
+                sd, so, sl = pack_strings(strs[:kr])
+                dt = oracle.ref_bpe_time_encode(merges, sd, so, sl, ms, 1)
+                ent["cpu_baseline_reference"] = {
+                    "value": sd.size / dt / 1e6, "unit": "text MB/s", "cores": 1, "kind": "reference",
+                    "sample": f"first {kr} strings ({dt:.1f} s)",
+                    "note": "encode_kernel's algorithm (thread 0 merges serially, find_merge scans every rule "
+                            "per pair) compiled for the CPU; on a GPU it runs the same loop on one thread per block"}
+        res[name] = ent
+        del d_data, d_offs, d_lens, rows, rl
+    tk.close()
+    torch.cuda.empty_cache()
+    return res
+
+
 def r8(x):
     return (x + 7) // 8 * 8
 
@@ -540,9 +639,34 @@ def kernel_loop(name, reps, torch, ops):
         def fn():
             ops.adam_tail(p, gr, m, v, p16, sc, lr=1e-4)
         work, unit, peak = 34.0 * n, "GB/s", hbm
+    elif name in ("bpe_encode", "bpe_decode"):
+        # the GPU tokenizer: 16384 strings x 2047 bytes of synthetic text -> rows of 2048 tokens
+        # (33 MB in, 134 MB out), GPT-2-sized synthetic rule table; decode turns the rows back
+        from rbk.tokenizer import GPUTokenizer, pack_strings, synthetic_batch, synthetic_corpus, synthetic_tables
+        vocab, merges, words = synthetic_tables()
+        tk = GPUTokenizer(vocab, merges)
+        strs = synthetic_batch(synthetic_corpus(words, 1 << 25, seed=9), 16384, 2047, seed=4)
+        data, offs, lens = pack_strings(strs)
+        dd, do, dl = (torch.from_numpy(a.copy()).cuda() for a in (data, offs, lens))
+        rows = torch.empty(16384, 2048, dtype=torch.int32, device="cuda")
+        rl = torch.empty(16384, dtype=torch.int32, device="cuda")
+        tk.encode(dd, do, dl, 2048, out=rows, out_lengths=rl)
+        sout = torch.empty(16384, 4096, dtype=torch.uint8, device="cuda")
+
+        def fn():
+            if name == "bpe_encode":
+                tk.encode(dd, do, dl, 2048, out=rows, out_lengths=rl)
+            else:
+                tk.decode_batch(rows, rl, 4096, out=sout)
+        # algorithmic bytes: text + offsets + lengths in, full rows + lengths out (encode); tokens up
+        # to the EOS + lengths in, text + NULs out (decode)
+        work = data.size + 16384 * (12 + 4 * 2048 + 4) if name == "bpe_encode" else \
+            4 * int(rl.sum().item()) + 16384 * 5 + data.size
+        unit, peak = "GB/s", hbm
     else:
         raise SystemExit(f"unknown kernel {name}")
-    if os.environ.get("RBK_BENCH_EAGER") == "1" or name.startswith("attn") or name == "adam_tail":
+    if os.environ.get("RBK_BENCH_EAGER") == "1" or name.startswith("attn") or name == "adam_tail" or \
+            name.startswith("bpe_"):
         for _ in range(3):
             fn()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -822,6 +946,7 @@ def main():
     ap.add_argument("--workload", default="gpt2-small", choices=sorted(WORKLOADS))
     ap.add_argument("--no-ckpt", action="store_true", help="disable activation checkpointing")
     ap.add_argument("--no-micro", action="store_true", help="skip the HBM-bound kernel microbench")
+    ap.add_argument("--no-tokenizer", action="store_true", help="skip the GPU BPE tokenizer bench (N = 1 only)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-ref-ops", action="store_true", help="skip timing the reference's own CPU ops")
     ap.add_argument("--no-1p3b", action="store_true", help="skip the second (1.3B) workload pass")
@@ -832,7 +957,7 @@ def main():
                          "rank's slices, FP16 all-gather); 0: all-reduce and the whole tail on every rank")
     ap.add_argument("--kernel", default=None,
                     help="loop one kernel instead of the training step (gemm_* of gemm_shapes(), ln_bwd, xent, "
-                         "attn_fwd, attn_bwd, adam_tail)")
+                         "attn_fwd, attn_bwd, adam_tail, bpe_encode, bpe_decode)")
     args = ap.parse_args()
     if args.kernel:
         import torch
@@ -871,6 +996,11 @@ def main():
             extra["microbench"] = microbench(ops, torch, hbm_peak)
         except Exception as exc:   # report, never hide
             extra["microbench"] = {"error": repr(exc)}
+    if rank == 0 and world == 1 and not args.no_tokenizer:
+        try:
+            extra["tokenizer"] = tokenizer_bench(torch, hbm_peak, cpu=not args.no_cpu)
+        except Exception as exc:   # report, never hide
+            extra["tokenizer"] = {"error": repr(exc)}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         tps, dt, cores = cpu_sample(args.workload)

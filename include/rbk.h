@@ -563,6 +563,63 @@ int rbk_model_dp_gather_state(rbk_model* m, void* stream);
 int rbk_model_dp_set_sync(rbk_model* m, int sync);
 int rbk_model_dp_shutdown(rbk_model* m);
 
+/* ------------------------------------------------------------------------
+ * GPU BPE tokenizer (src/tokenizer_cuda.h:120-164, src/tokenizer_cuda.cu:90-348)
+ * ------------------------------------------------------------------------
+ * Special ids as the reference's: PAD 0, UNK 1, BOS 2, EOS 3, SEP 4; byte c
+ * encodes as c + 5.  A pair merges into the result of the first rule, in
+ * rule order, with that pair; merges run in greedy left-to-right passes until
+ * a pass merges nothing; EOS ends every row.  Results equal the reference's
+ * encode_kernel / decode_kernel wherever those are defined; the contract
+ * where they are not is stated at each call.  A handle serves one device and
+ * one host thread at a time. */
+typedef struct rbk_bpe rbk_bpe;
+/* tokenizer_copy_to_device / tokenizer_init_gpu (src/tokenizer_cuda.cu:205-272,
+ * 391-394).  The tables are the ones the reference's builders produce:
+ *   inverse vocabulary: id i's string is inv_bytes[inv_offsets[i] ..
+ *     + inv_lengths[i]) for i < vocab_size (build_inv_vocab_arrays, :488-505);
+ *   merge rules in merge order: (merge_first[j], merge_second[j]) ->
+ *     merge_result[j] (the rules array of build_merge_trie, :408-454).
+ * vocab_size >= 261 (specials + bytes); results inside the vocabulary.  A
+ * rule whose pair holds an id outside [0, vocab_size) can never fire and is
+ * dropped; a repeated pair keeps its first rule.  Fails with
+ * RBK_ERR_UNSUPPORTED on a device other than sm_100. */
+int rbk_bpe_create(rbk_bpe** out, int device, int vocab_size, const char* inv_bytes, int64_t inv_bytes_size,
+                   const int* inv_offsets, const int* inv_lengths, const int* merge_first, const int* merge_second,
+                   const int* merge_result, int num_merges);
+/* tokenizer_free_gpu (:274-285).  Waits for the handle's staging copies. */
+int rbk_bpe_destroy(rbk_bpe* t);
+/* Distinct rules the handle's pair table holds. */
+int rbk_bpe_num_rules(const rbk_bpe* t);
+/* encode_batch (src/tokenizer_cuda.cu:287-332): `batch` NUL-terminated host
+ * strings -> device rows out_tokens[b * max_seq_len ..] and out_lengths[b]
+ * (tokens + 1, the EOS included).  Asynchronous on `stream` (the strings may
+ * be reused once the call returns).  Row b holds the tokens, EOS, then PAD up
+ * to max_seq_len (the reference leaves pass scratch there).  An empty string
+ * gives [EOS], length 1 (the reference writes nothing).  A string of more
+ * than max_seq_len - 1 bytes is rejected with RBK_ERR_INVALID before anything
+ * runs (the reference writes past its row); one of exactly max_seq_len - 1
+ * bytes is merged like any other (the reference skips its merges).
+ * 2 <= max_seq_len <= 8193. */
+int rbk_bpe_encode_batch(rbk_bpe* t, const char* const* strings, int batch, int* out_tokens, int* out_lengths,
+                         int max_seq_len, void* stream);
+/* The same encode over strings already on the device: string b is
+ * bytes[offsets[b] .. offsets[b] + lengths[b]) (any byte values, NUL
+ * included).  A string longer than max_seq_len - 1 bytes is cut to its first
+ * max_seq_len - 1 bytes and counted into *n_truncated (device int, may be
+ * NULL). */
+int rbk_bpe_encode(rbk_bpe* t, const uint8_t* bytes, const int64_t* offsets, const int* lengths, int batch,
+                   int* out_tokens, int* out_lengths, int max_seq_len, int* n_truncated, void* stream);
+/* decode_batch (src/tokenizer_cuda.cu:334-348): device token rows -> device
+ * strings out[b * max_string_len ..], NUL-terminated, the bytes after the NUL
+ * untouched.  Row b has lengths[b] tokens; rows sit ld tokens apart (at most
+ * ld read), or with ld == 0 row b starts at b * lengths[b] as in the
+ * reference (:182).  A token id outside [0, vocab_size) adds no bytes and is
+ * counted into *n_bad (device int, may be NULL); the reference reads outside
+ * its tables there. */
+int rbk_bpe_decode_batch(rbk_bpe* t, const int* tokens, int64_t ld, const int* lengths, int batch, char* out,
+                         int max_string_len, int* n_bad, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

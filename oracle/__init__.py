@@ -303,3 +303,112 @@ def model_lora_grad(cfg, params, Aq, Bq, Av, Bv, r, alpha, tok, tgt, B, S, grad_
                                      _p(dAq), _p(dBq), _p(dAv), _p(dBv), r, C.c_float(alpha),
                                      _p(i32(tok), C.c_int), _p(i32(tgt), C.c_int), B, S, C.c_float(grad_scale))
     return float(loss), dAq, dBq, dAv, dBv
+
+
+# ---------------------------------------------------------------------------
+# BPE tokenizer (oracle/bpe.cpp; the reference's kernels in _ref/libreftok.so)
+# ---------------------------------------------------------------------------
+_REFTOK = None
+
+
+def _merge_cols(merges):
+    m = np.ascontiguousarray(np.asarray(merges, dtype=np.int32).reshape(-1, 3))
+    return [np.ascontiguousarray(m[:, i]) for i in range(3)]
+
+
+def bpe_encode(merges, data, offsets, lengths, max_seq_len):
+    """Restated encode: (int32 [B, max_seq_len] rows, int32 [B] lengths, truncated count)."""
+    mf, ms, mr = _merge_cols(merges)
+    data = np.ascontiguousarray(data, np.uint8)
+    offsets = np.ascontiguousarray(offsets, np.int64)
+    lengths = np.ascontiguousarray(lengths, np.int32)
+    B = lengths.size
+    out = np.empty((B, max_seq_len), np.int32)
+    out_len = np.empty(B, np.int32)
+    cut = C.c_int(0)
+    rc = lib().ora_bpe_encode(_p(mf, C.c_int), _p(ms, C.c_int), _p(mr, C.c_int), len(mf),
+                              data.ctypes.data_as(C.c_void_p), _p(offsets, C.c_int64), _p(lengths, C.c_int), B,
+                              _p(out, C.c_int), _p(out_len, C.c_int), max_seq_len, C.byref(cut))
+    assert rc == 0, "ora_bpe_encode rejected its arguments"
+    return out, out_len, cut.value
+
+
+def bpe_decode(vocab, tokens, ld, lengths, max_string_len, out=None):
+    """Restated decode: (uint8 [B, max_string_len] rows, bad-id count).  `out` (optional) is the
+    initial buffer content (bytes after each NUL are left as they are)."""
+    inv = b"".join(vocab)
+    offs = np.zeros(len(vocab), np.int64)
+    lens = np.array([len(s) for s in vocab], np.int32)
+    offs[1:] = np.cumsum(lens[:-1])
+    tokens = np.ascontiguousarray(tokens, np.int32)
+    lengths = np.ascontiguousarray(lengths, np.int32)
+    B = lengths.size
+    out = np.zeros((B, max_string_len), np.uint8) if out is None else np.ascontiguousarray(out, np.uint8).copy()
+    bad = C.c_int(0)
+    invb = np.frombuffer(inv, np.uint8) if inv else np.zeros(1, np.uint8)
+    rc = lib().ora_bpe_decode(invb.ctypes.data_as(C.c_void_p), _p(offs, C.c_int64), _p(lens, C.c_int), len(vocab),
+                              _p(tokens, C.c_int), C.c_int64(ld), _p(lengths, C.c_int), B,
+                              out.ctypes.data_as(C.c_void_p), max_string_len, C.byref(bad))
+    assert rc == 0, "ora_bpe_decode rejected its arguments"
+    return out, bad.value
+
+
+def reftok_lib():
+    """The reference's tokenizer kernels compiled for the CPU, or None when not built here."""
+    global _REFTOK
+    if _REFTOK is None:
+        path = os.path.join(_HERE, "_ref", "libreftok.so")
+        if not os.path.exists(path):
+            return None
+        _REFTOK = C.CDLL(path)
+        _REFTOK.reftok_time_encode.restype = C.c_double
+    return _REFTOK
+
+
+def ref_bpe_encode(merges, data, offsets, lengths, max_seq_len, fill=-7):
+    """The reference's encode_kernel (strings of 1..256 bytes, at most max_seq_len - 2):
+    (rows as the kernel leaves them, starting from `fill`, and lengths), or None outside
+    its defined domain."""
+    mf, ms, mr = _merge_cols(merges)
+    data = np.ascontiguousarray(data, np.uint8)
+    offs32 = np.ascontiguousarray(offsets, np.int32)
+    lengths = np.ascontiguousarray(lengths, np.int32)
+    B = lengths.size
+    out = np.full((B, max_seq_len), fill, np.int32)
+    out_len = np.full(B, fill, np.int32)
+    rc = reftok_lib().reftok_encode(_p(mf, C.c_int), _p(ms, C.c_int), _p(mr, C.c_int), len(mf),
+                                    data.ctypes.data_as(C.c_void_p), _p(offs32, C.c_int), _p(lengths, C.c_int), B,
+                                    _p(out, C.c_int), _p(out_len, C.c_int), max_seq_len)
+    return None if rc != 0 else (out, out_len)
+
+
+def ref_bpe_decode(vocab, tokens_ref_layout, lengths, max_string_len, out=None):
+    """The reference's decode_kernel; row b at b * lengths[b] of the flat token array."""
+    inv = b"".join(vocab)
+    lens = np.array([len(s) for s in vocab], np.int32)
+    offs = np.zeros(len(vocab), np.int32)
+    offs[1:] = np.cumsum(lens[:-1])
+    tokens = np.ascontiguousarray(tokens_ref_layout, np.int32)
+    lengths = np.ascontiguousarray(lengths, np.int32)
+    B = lengths.size
+    out = np.zeros((B, max_string_len), np.uint8) if out is None else np.ascontiguousarray(out, np.uint8).copy()
+    invb = np.frombuffer(inv, np.uint8) if inv else np.zeros(1, np.uint8)
+    rc = reftok_lib().reftok_decode(invb.ctypes.data_as(C.c_void_p), _p(offs, C.c_int), _p(lens, C.c_int),
+                                    len(vocab), _p(tokens, C.c_int), _p(lengths, C.c_int), B,
+                                    out.ctypes.data_as(C.c_void_p), max_string_len)
+    return None if rc != 0 else out
+
+
+def ref_bpe_time_encode(merges, data, offsets, lengths, max_seq_len, reps=1):
+    """Seconds the reference's encode algorithm takes for `reps` passes over the batch."""
+    mf, ms, mr = _merge_cols(merges)
+    data = np.ascontiguousarray(data, np.uint8)
+    offs32 = np.ascontiguousarray(offsets, np.int32)
+    lengths = np.ascontiguousarray(lengths, np.int32)
+    B = lengths.size
+    out = np.empty((B, max_seq_len), np.int32)
+    out_len = np.empty(B, np.int32)
+    return reftok_lib().reftok_time_encode(_p(mf, C.c_int), _p(ms, C.c_int), _p(mr, C.c_int), len(mf),
+                                           data.ctypes.data_as(C.c_void_p), _p(offs32, C.c_int),
+                                           _p(lengths, C.c_int), B, _p(out, C.c_int), _p(out_len, C.c_int),
+                                           max_seq_len, reps)

@@ -133,6 +133,12 @@ _SIGS = {
     "rbk_dp_status": (i32, [vp]),
     "rbk_dp_abort": (i32, [vp]),
     "rbk_dp_destroy": (i32, [vp]),
+    "rbk_bpe_create": (i32, [C.POINTER(vp), i32, i32, vp, i64, vp, vp, vp, vp, vp, i32]),
+    "rbk_bpe_destroy": (i32, [vp]),
+    "rbk_bpe_num_rules": (i32, [vp]),
+    "rbk_bpe_encode_batch": (i32, [vp, vp, i32, vp, vp, i32, vp]),
+    "rbk_bpe_encode": (i32, [vp, vp, vp, vp, i32, vp, vp, i32, vp, vp]),
+    "rbk_bpe_decode_batch": (i32, [vp, vp, i64, vp, i32, vp, i32, vp, vp]),
     "rbk_model_dp_shard_ranges": (i32, [vp, C.POINTER(C.c_int64), i32, C.POINTER(i32)]),
     "rbk_model_dp_gather_state": (i32, [vp, vp]),
     "rbk_model_zero_grad": (i32, [vp, vp]),
