@@ -16,9 +16,10 @@
 //
 // Design.  The reference runs every pass serially on thread 0 of a block and scans the whole
 // rule array for every pair (O(rules) per lookup).  Here:
-//   - the rules live in an open-addressed hash table of 16-byte slots {first, second, result,
-//     0} (load <= 1/4, linear probing, MurmurHash3's 64-bit finalizer on the packed pair):
-//     one 128-bit L2/L1 load answers almost every lookup, and duplicate pairs keep the first
+//   - the rules live in an open-addressed hash table (load <= 1/4, linear probing) of 8-byte
+//     slots {first | second << 16, result} for vocabularies of up to 65535 ids (the reference's
+//     MAX_VOCAB_SIZE range; 2 MB for 50K rules) or 16-byte slots {first, second, result, 0}
+//     above that: one L1/L2 load answers almost every lookup, and duplicate pairs keep the first
 //     rule because the host inserts in rule order and skips pairs already present;
 //   - one CTA of 256 threads owns a string; each pass is data-parallel: every thread looks
 //     up the pairs of its chunk of positions, and the greedy left-to-right choice becomes a
@@ -42,7 +43,8 @@ struct rbk_bpe {
     int vocab_size = 0;
     int n_rules = 0;        // distinct usable pairs in the table
     uint32_t mask = 0;      // table slots - 1
-    int4* table = nullptr;  // device: {first, second, result, 0}, first = -1 for an empty slot
+    bool wide = false;      // 16-byte slots (vocabularies above 65535 ids), else 8-byte slots
+    void* table = nullptr;  // device pair table (PairSlot<wide>)
     int2* inv = nullptr;    // device: {offset, length} of every id's string
     uint8_t* inv_bytes = nullptr;
     // host-string staging of rbk_bpe_encode_batch, double-buffered
@@ -76,13 +78,40 @@ __host__ __device__ __forceinline__ uint32_t pair_hash(int a, int b) {
     return h;
 }
 
-// The rest of a probe sequence whose first slot `e` (at index i) neither matched nor was empty.
-__device__ __noinline__ int probe_rest(const int4* __restrict__ table, uint32_t mask, uint32_t i, int a, int b) {
+// Pair-table slots.  Narrow (vocabularies of at most 65535 ids, the reference's
+// MAX_VOCAB_SIZE range): 8 bytes {first | second << 16, result}, key 0xffffffff empty.  Wide:
+// 16 bytes {first, second, result, 0}, first = -1 empty.
+template <bool kWide>
+struct PairSlot;
+template <>
+struct PairSlot<false> {
+    using T = uint2;
+    static __host__ __device__ T vacant() { return make_uint2(0xffffffffu, 0u); }
+    static __host__ __device__ T make(int a, int b, int r) { return make_uint2((uint32_t)a | ((uint32_t)b << 16), (uint32_t)r); }
+    static __host__ __device__ bool is_vacant(T e) { return e.x == 0xffffffffu; }
+    static __host__ __device__ bool holds(T e, int a, int b) { return e.x == ((uint32_t)a | ((uint32_t)b << 16)); }
+    static __host__ __device__ int result(T e) { return (int)e.y; }
+};
+template <>
+struct PairSlot<true> {
+    using T = int4;
+    static __host__ __device__ T vacant() { return make_int4(-1, -1, -1, 0); }
+    static __host__ __device__ T make(int a, int b, int r) { return make_int4(a, b, r, 0); }
+    static __host__ __device__ bool is_vacant(T e) { return e.x < 0; }
+    static __host__ __device__ bool holds(T e, int a, int b) { return e.x == a && e.y == b; }
+    static __host__ __device__ int result(T e) { return e.z; }
+};
+
+// The rest of a probe sequence whose first slot (at index i) neither matched nor was vacant.
+template <bool kWide>
+__device__ __noinline__ int probe_rest(const typename PairSlot<kWide>::T* __restrict__ table, uint32_t mask, uint32_t i,
+                                       int a, int b) {
+    using S = PairSlot<kWide>;
     for (uint32_t n = 0; n < mask; ++n) {  // bounded by the table size; the table is never full
         i = (i + 1) & mask;
-        const int4 e = __ldg(table + i);
-        if (e.x == a && e.y == b) return e.z;
-        if (e.x < 0) return -1;
+        const typename S::T e = __ldg(table + i);
+        if (S::holds(e, a, b)) return S::result(e);
+        if (S::is_vacant(e)) return -1;
     }
     return -1;
 }
@@ -105,9 +134,10 @@ __device__ __forceinline__ uint32_t map_then(uint32_t lo, uint32_t hi) {
 
 // One merge pass over the len tokens in s_tok, C positions per thread (256 C >= len); returns
 // the new length (len when nothing merged).  Ends with a barrier: s_tok holds the new string.
-template <int C>
-__device__ __forceinline__ int merge_pass(int* s_tok, uint32_t* s_warp, int len, const int4* __restrict__ table,
-                                          uint32_t mask) {
+template <int C, bool kWide>
+__device__ __forceinline__ int merge_pass(int* s_tok, uint32_t* s_warp, int len,
+                                          const typename PairSlot<kWide>::T* __restrict__ table, uint32_t mask) {
+    using S = PairSlot<kWide>;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int p0 = tid * C;
     int t[C], m[C];
@@ -139,14 +169,14 @@ __device__ __forceinline__ int merge_pass(int* s_tok, uint32_t* s_warp, int len,
 #pragma unroll
     for (int g = 0; g < C; g += 8) {
         constexpr int G = C < 8 ? C : 8;
-        int4 e[G];
+        typename S::T e[G];
         uint32_t idx[G];
 #pragma unroll
         for (int j = 0; j < G; ++j) {
             const int k = g + j;
             const int second = (k + 1 < C) ? t[k + 1] : after;
             idx[j] = pair_hash(t[k], second) & mask;
-            e[j] = (p0 + k + 1 < len) ? __ldg(table + idx[j]) : make_int4(-1, -1, -1, 0);
+            e[j] = (p0 + k + 1 < len) ? __ldg(table + idx[j]) : S::vacant();
         }
 #pragma unroll
         for (int j = 0; j < G; ++j) {
@@ -154,8 +184,8 @@ __device__ __forceinline__ int merge_pass(int* s_tok, uint32_t* s_warp, int len,
             const int second = (k + 1 < C) ? t[k + 1] : after;
             int r = -1;
             if (p0 + k + 1 < len) {
-                if (e[j].x == t[k] && e[j].y == second) r = e[j].z;
-                else if (e[j].x >= 0) r = probe_rest(table, mask, idx[j], t[k], second);
+                if (S::holds(e[j], t[k], second)) r = S::result(e[j]);
+                else if (!S::is_vacant(e[j])) r = probe_rest<kWide>(table, mask, idx[j], t[k], second);
             }
             m[k] = r;
         }
@@ -209,9 +239,9 @@ __device__ __forceinline__ int merge_pass(int* s_tok, uint32_t* s_warp, int len,
 
 // Strings of up to 256 K tokens (max_seq_len - 1 <= 256 K).  Each pass runs with the fewest
 // positions per thread that cover the current length, so later, shorter passes cost less.
-template <int K>
+template <int K, bool kWide>
 __global__ void __launch_bounds__(kBpeThreads, K <= 8 ? 4 : 1) bpe_encode_kernel(
-    const int4* __restrict__ table, uint32_t mask, const uint8_t* __restrict__ bytes,
+    const typename PairSlot<kWide>::T* __restrict__ table, uint32_t mask, const uint8_t* __restrict__ bytes,
     const int64_t* __restrict__ offsets, const int* __restrict__ lengths, int* __restrict__ out,
     int* __restrict__ out_len, int max_seq_len, int* __restrict__ n_truncated) {
     __shared__ __align__(16) int s_tok[kBpeThreads * K];
@@ -231,12 +261,13 @@ __global__ void __launch_bounds__(kBpeThreads, K <= 8 ? 4 : 1) bpe_encode_kernel
     // Every pass that continues shortens the string, so at most len passes run.
     while (len > 1) {
         int nl;
-        if (len <= kBpeThreads) nl = merge_pass<1>(s_tok, s_warp, len, table, mask);
-        else if (K < 4 || len <= 2 * kBpeThreads) nl = merge_pass<(K < 2 ? 1 : 2)>(s_tok, s_warp, len, table, mask);
-        else if (K < 8 || len <= 4 * kBpeThreads) nl = merge_pass<(K < 4 ? 1 : 4)>(s_tok, s_warp, len, table, mask);
-        else if (K < 16 || len <= 8 * kBpeThreads) nl = merge_pass<(K < 8 ? 1 : 8)>(s_tok, s_warp, len, table, mask);
-        else if (K < 32 || len <= 16 * kBpeThreads) nl = merge_pass<(K < 16 ? 1 : 16)>(s_tok, s_warp, len, table, mask);
-        else nl = merge_pass<K>(s_tok, s_warp, len, table, mask);
+        if (len <= kBpeThreads) nl = merge_pass<1, kWide>(s_tok, s_warp, len, table, mask);
+        else if (K < 4 || len <= 2 * kBpeThreads) nl = merge_pass<(K < 2 ? 1 : 2), kWide>(s_tok, s_warp, len, table, mask);
+        else if (K < 8 || len <= 4 * kBpeThreads) nl = merge_pass<(K < 4 ? 1 : 4), kWide>(s_tok, s_warp, len, table, mask);
+        else if (K < 16 || len <= 8 * kBpeThreads) nl = merge_pass<(K < 8 ? 1 : 8), kWide>(s_tok, s_warp, len, table, mask);
+        else if (K < 32 || len <= 16 * kBpeThreads)
+            nl = merge_pass<(K < 16 ? 1 : 16), kWide>(s_tok, s_warp, len, table, mask);
+        else nl = merge_pass<K, kWide>(s_tok, s_warp, len, table, mask);
         if (nl == len) break;
         len = nl;
     }
@@ -339,14 +370,17 @@ int encode_items(int max_seq_len) {
     return k;
 }
 
-int launch_encode(const rbk_bpe* t, const uint8_t* bytes, const int64_t* offsets, const int* lengths, int batch,
-                  int* out, int* out_len, int max_seq_len, int* n_truncated, cudaStream_t st) {
+template <bool kWide>
+int launch_encode_as(const rbk_bpe* t, const uint8_t* bytes, const int64_t* offsets, const int* lengths, int batch,
+                     int* out, int* out_len, int max_seq_len, int* n_truncated, cudaStream_t st) {
+    using T = typename PairSlot<kWide>::T;
+    const T* table = static_cast<const T*>(t->table);
     const dim3 grid(batch), block(kBpeThreads);
     switch (encode_items(max_seq_len)) {
-#define RBK_BPE_CASE(K)                                                                                        \
-    case K:                                                                                                    \
-        bpe_encode_kernel<K><<<grid, block, 0, st>>>(t->table, t->mask, bytes, offsets, lengths, out, out_len, \
-                                                    max_seq_len, n_truncated);                                 \
+#define RBK_BPE_CASE(K)                                                                                          \
+    case K:                                                                                                      \
+        bpe_encode_kernel<K, kWide><<<grid, block, 0, st>>>(table, t->mask, bytes, offsets, lengths, out, out_len, \
+                                                           max_seq_len, n_truncated);                            \
         break;
         RBK_BPE_CASE(1)
         RBK_BPE_CASE(2)
@@ -360,6 +394,43 @@ int launch_encode(const rbk_bpe* t, const uint8_t* bytes, const int64_t* offsets
             return RBK_ERR_INVALID;
     }
     RBK_LAUNCHED("bpe_encode_kernel");
+    return RBK_OK;
+}
+
+int launch_encode(const rbk_bpe* t, const uint8_t* bytes, const int64_t* offsets, const int* lengths, int batch,
+                  int* out, int* out_len, int max_seq_len, int* n_truncated, cudaStream_t st) {
+    return t->wide ? launch_encode_as<true>(t, bytes, offsets, lengths, batch, out, out_len, max_seq_len, n_truncated, st)
+                   : launch_encode_as<false>(t, bytes, offsets, lengths, batch, out, out_len, max_seq_len, n_truncated,
+                                             st);
+}
+
+// Insert the rules in rule order (a pair already present keeps its earlier rule; a rule whose
+// pair holds an id no token can carry never fires and is dropped) and upload the table.
+template <bool kWide>
+int build_table(rbk_bpe* t, const int* f, const int* s2, const int* r, int n, uint32_t slots) {
+    using S = PairSlot<kWide>;
+    std::vector<typename S::T> table(slots, S::vacant());
+    const uint32_t mask = slots - 1;
+    int n_rules = 0;
+    for (int i = 0; i < n; ++i) {
+        const int a = f[i], b = s2[i];
+        if (a < 0 || b < 0 || a >= t->vocab_size || b >= t->vocab_size) continue;
+        uint32_t j = pair_hash(a, b) & mask;
+        while (!S::is_vacant(table[j]) && !S::holds(table[j], a, b)) j = (j + 1) & mask;
+        if (!S::is_vacant(table[j])) continue;
+        table[j] = S::make(a, b, r[i]);
+        ++n_rules;
+    }
+    t->n_rules = n_rules;
+    t->mask = mask;
+    t->wide = kWide;
+    if (cudaMalloc(&t->table, sizeof(typename S::T) * slots) != cudaSuccess) {
+        cudaGetLastError();
+        t->table = nullptr;
+        set_error("rbk_bpe_create: device allocation of the pair table failed");
+        return RBK_ERR_NOMEM;
+    }
+    RBK_CUDA(cudaMemcpy(t->table, table.data(), sizeof(typename S::T) * slots, cudaMemcpyHostToDevice));
     return RBK_OK;
 }
 
@@ -420,22 +491,6 @@ int rbk_bpe_create(rbk_bpe** out, int device, int vocab_size, const char* inv_by
         RBK_REQUIRE(merge_result[i] >= 0 && merge_result[i] < vocab_size,
                     "rbk_bpe_create: rule %d yields id %d outside the vocabulary of %d", i, merge_result[i],
                     vocab_size);
-    // hash table: load <= 1/4; a pair already present keeps its earlier rule; a rule whose pair
-    // holds an id no token can carry (negative, or outside the vocabulary) never fires and is dropped
-    uint32_t slots = 1024;
-    while (slots < 4ull * (uint64_t)num_merges) slots *= 2;
-    std::vector<int4> table(slots, make_int4(-1, -1, -1, 0));
-    const uint32_t mask = slots - 1;
-    int n_rules = 0;
-    for (int i = 0; i < num_merges; ++i) {
-        const int a = merge_first[i], b = merge_second[i];
-        if (a < 0 || b < 0 || a >= vocab_size || b >= vocab_size) continue;
-        uint32_t j = pair_hash(a, b) & mask;
-        while (table[j].x >= 0 && !(table[j].x == a && table[j].y == b)) j = (j + 1) & mask;
-        if (table[j].x >= 0) continue;  // an earlier rule owns the pair
-        table[j] = make_int4(a, b, merge_result[i], 0);
-        ++n_rules;
-    }
     cudaDeviceProp prop;
     RBK_CUDA(cudaGetDeviceProperties(&prop, device));
     if (prop.major != 10 || prop.minor != 0) {
@@ -446,18 +501,24 @@ int rbk_bpe_create(rbk_bpe** out, int device, int vocab_size, const char* inv_by
     rbk_bpe* t = new rbk_bpe;
     t->device = device;
     t->vocab_size = vocab_size;
-    t->n_rules = n_rules;
-    t->mask = mask;
+    // the pair table: load <= 1/4
+    uint32_t slots = 1024;
+    while (slots < 4ull * (uint64_t)num_merges) slots *= 2;
+    const int rc = vocab_size <= 65535
+                       ? build_table<false>(t, merge_first, merge_second, merge_result, num_merges, slots)
+                       : build_table<true>(t, merge_first, merge_second, merge_result, num_merges, slots);
+    if (rc != RBK_OK) {
+        free_bpe(t);
+        return rc;
+    }
     const size_t nb = (size_t)std::max<int64_t>(inv_bytes_size, 1);
-    if (cudaMalloc(&t->table, sizeof(int4) * slots) != cudaSuccess ||
-        cudaMalloc(&t->inv, sizeof(int2) * vocab_size) != cudaSuccess || cudaMalloc(&t->inv_bytes, nb) != cudaSuccess) {
+    if (cudaMalloc(&t->inv, sizeof(int2) * vocab_size) != cudaSuccess || cudaMalloc(&t->inv_bytes, nb) != cudaSuccess) {
         cudaGetLastError();
         free_bpe(t);
         set_error("rbk_bpe_create: device allocation of the tables failed");
         return RBK_ERR_NOMEM;
     }
-    cudaError_t e = cudaMemcpy(t->table, table.data(), sizeof(int4) * slots, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = cudaMemcpy(t->inv, inv.data(), sizeof(int2) * vocab_size, cudaMemcpyHostToDevice);
+    cudaError_t e = cudaMemcpy(t->inv, inv.data(), sizeof(int2) * vocab_size, cudaMemcpyHostToDevice);
     if (e == cudaSuccess && inv_bytes_size > 0)
         e = cudaMemcpy(t->inv_bytes, inv_bytes, (size_t)inv_bytes_size, cudaMemcpyHostToDevice);
     for (auto& s : t->slot)

@@ -120,6 +120,27 @@ def test_random_rule_sets_match_oracle():
         assert np.array_equal(rows, want), it
 
 
+def test_wide_pair_table_matches_oracle(tk):
+    """Vocabularies above 65535 ids use the 16-byte pair slots: the golden tokenizer with every
+    merged id moved up by 65000 encodes to the same rows, ids moved likewise."""
+    from rbk.tokenizer import GPUTokenizer, pack_strings
+    _, vocab, merges = tk
+    sh = lambda i: i + 65000 if i >= 261 else i  # noqa: E731
+    wide_vocab = vocab[:261] + [b"?"] * 65000 + vocab[261:]
+    wide_merges = [(sh(a), sh(b), sh(r)) for a, b, r in merges]
+    t = GPUTokenizer(wide_vocab, wide_merges)
+    g, _, _ = golden()
+    corpus = g["enc_a_data"].tobytes()
+    strs = [corpus[i:i + L] for i, L in zip(range(0, 4000, 97), range(1, 2000, 47))]
+    data, offs, lens = pack_strings(strs)
+    rows, rl = encode_dev(t, data, offs, lens, 2048)
+    nrows, nrl = encode_dev(tk[0], data, offs, lens, 2048)
+    want, wl, _ = oracle.bpe_encode(wide_merges, data, offs, lens, 2048)
+    t.close()
+    assert np.array_equal(rl, wl) and np.array_equal(rows, want)
+    assert np.array_equal(rl, nrl) and np.array_equal(rows, np.where(nrows >= 261, nrows + 65000, nrows))
+
+
 def test_truncation_and_rejection(tk):
     from rbk._lib import RbkError
     from rbk.tokenizer import pack_strings
