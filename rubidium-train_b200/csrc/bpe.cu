@@ -21,7 +21,8 @@
 //     MAX_VOCAB_SIZE range; 2 MB for 50K rules) or 16-byte slots {first, second, result, 0}
 //     above that: one L1/L2 load answers almost every lookup, and duplicate pairs keep the first
 //     rule because the host inserts in rule order and skips pairs already present;
-//   - one CTA of 256 threads owns a string; each pass is data-parallel: every thread looks
+//   - one CTA of 256 threads owns a string (one warp, for rows of at most 257 tokens); each
+//     pass is data-parallel: every thread looks
 //     up the pairs of its chunk of positions, and the greedy left-to-right choice becomes a
 //     prefix computation.  Whether position p is consumed depends only on whether the pair
 //     at p-1 merged, so a chunk is a map of that one-bit state (2 bits) together with how
@@ -67,6 +68,7 @@ constexpr int kEosId = 3;
 constexpr int kByteBase = 5;
 constexpr int kMaxItems = 32;  // positions per thread: strings of up to 256 * 32 tokens
 constexpr int kDecodeWarps = 8;
+constexpr int kWarpTokens = 256;  // longest string of the warp-per-string encode
 
 // The pair hash: both ids multiplied by xxHash32's primes 1 and 2 (plus prime 5), then a
 // xorshift-multiply avalanche; 32-bit arithmetic only (a few instructions per lookup).
@@ -132,13 +134,15 @@ __device__ __forceinline__ uint32_t map_then(uint32_t lo, uint32_t hi) {
     return ((hi >> o0) & 1u) | (((hi >> o1) & 1u) << 1) | (c0 << 2) | (c1 << 17);
 }
 
-// One merge pass over the len tokens in s_tok, C positions per thread (256 C >= len); returns
-// the new length (len when nothing merged).  Ends with a barrier: s_tok holds the new string.
-template <int C, bool kWide>
+// One merge pass over the len tokens in s_tok, C positions per thread, on NT threads (the
+// block, or one warp; NT C >= len); returns the new length (len when nothing merged).  Ends
+// with a barrier of the NT threads: s_tok holds the new string.
+template <int C, int NT, bool kWide>
 __device__ __forceinline__ int merge_pass(int* s_tok, uint32_t* s_warp, int len,
                                           const typename PairSlot<kWide>::T* __restrict__ table, uint32_t mask) {
     using S = PairSlot<kWide>;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    static_assert(NT == 32 || NT == kBpeThreads, "a pass runs on one warp or on the whole block");
+    const int tid = threadIdx.x % NT, lane = tid & 31, warp = tid >> 5;
     const int p0 = tid * C;
     int t[C], m[C];
     // the chunk, as 16- or 8-byte vectors (p0 is a multiple of C; every vector that starts below
@@ -164,7 +168,10 @@ __device__ __forceinline__ int merge_pass(int* s_tok, uint32_t* s_warp, int len,
 #pragma unroll
     for (int k = 0; k < C; ++k)
         if (p0 + k >= len) t[k] = -1;
-    const int after = (p0 + C < len) ? s_tok[p0 + C] : -1;
+    // the token after the chunk is the next thread's first (a shuffle: s_tok read at stride C
+    // would be a C-way bank conflict); the warp's last lane reads it
+    int after = __shfl_down_sync(0xffffffffu, t[0], 1);
+    if (lane == 31) after = (p0 + C < len) ? s_tok[p0 + C] : -1;
     // pair lookups: the first probes of up to 8 positions in flight together
 #pragma unroll
     for (int g = 0; g < C; g += 8) {
@@ -211,17 +218,23 @@ __device__ __forceinline__ int merge_pass(int* s_tok, uint32_t* s_warp, int len,
     }
     uint32_t excl = __shfl_up_sync(0xffffffffu, v, 1);
     if (lane == 0) excl = kMapIdentity;
-    if (lane == 31) s_warp[warp] = v;
-    __syncthreads();
-    uint32_t x = lane < kBpeThreads / 32 ? s_warp[lane] : kMapIdentity;
+    uint32_t total;
+    if constexpr (NT == 32) {
+        total = __shfl_sync(0xffffffffu, v, 31);
+        __syncwarp();
+    } else {
+        if (lane == 31) s_warp[warp] = v;
+        __syncthreads();
+        uint32_t x = lane < NT / 32 ? s_warp[lane] : kMapIdentity;
 #pragma unroll
-    for (int d = 1; d < kBpeThreads / 32; d <<= 1) {
-        const uint32_t o = __shfl_up_sync(0xffffffffu, x, d);
-        if (lane >= d) x = map_then(o, x);
+        for (int d = 1; d < NT / 32; d <<= 1) {
+            const uint32_t o = __shfl_up_sync(0xffffffffu, x, d);
+            if (lane >= d) x = map_then(o, x);
+        }
+        const uint32_t pre = __shfl_sync(0xffffffffu, x, warp > 0 ? warp - 1 : 0);  // used from warp 1 on
+        total = __shfl_sync(0xffffffffu, x, NT / 32 - 1);
+        if (warp > 0) excl = map_then(pre, excl);
     }
-    const uint32_t pre = __shfl_sync(0xffffffffu, x, warp > 0 ? warp - 1 : 0);  // used from warp 1 on
-    const uint32_t total = __shfl_sync(0xffffffffu, x, kBpeThreads / 32 - 1);
-    if (warp > 0) excl = map_then(pre, excl);
     // compact in place: every read of s_tok happened before the barrier above
     uint32_t st = excl & 1u;
     int o = (int)map_count(excl, 0);
@@ -233,7 +246,8 @@ __device__ __forceinline__ int merge_pass(int* s_tok, uint32_t* s_warp, int len,
             st = chosen;
         }
     }
-    __syncthreads();
+    if constexpr (NT == 32) __syncwarp();
+    else __syncthreads();
     return (int)map_count(total, 0);
 }
 
@@ -261,13 +275,13 @@ __global__ void __launch_bounds__(kBpeThreads, K <= 8 ? 4 : 1) bpe_encode_kernel
     // Every pass that continues shortens the string, so at most len passes run.
     while (len > 1) {
         int nl;
-        if (len <= kBpeThreads) nl = merge_pass<1, kWide>(s_tok, s_warp, len, table, mask);
-        else if (K < 4 || len <= 2 * kBpeThreads) nl = merge_pass<(K < 2 ? 1 : 2), kWide>(s_tok, s_warp, len, table, mask);
-        else if (K < 8 || len <= 4 * kBpeThreads) nl = merge_pass<(K < 4 ? 1 : 4), kWide>(s_tok, s_warp, len, table, mask);
-        else if (K < 16 || len <= 8 * kBpeThreads) nl = merge_pass<(K < 8 ? 1 : 8), kWide>(s_tok, s_warp, len, table, mask);
+        if (len <= kBpeThreads) nl = merge_pass<1, kBpeThreads, kWide>(s_tok, s_warp, len, table, mask);
+        else if (K < 4 || len <= 2 * kBpeThreads) nl = merge_pass<(K < 2 ? 1 : 2), kBpeThreads, kWide>(s_tok, s_warp, len, table, mask);
+        else if (K < 8 || len <= 4 * kBpeThreads) nl = merge_pass<(K < 4 ? 1 : 4), kBpeThreads, kWide>(s_tok, s_warp, len, table, mask);
+        else if (K < 16 || len <= 8 * kBpeThreads) nl = merge_pass<(K < 8 ? 1 : 8), kBpeThreads, kWide>(s_tok, s_warp, len, table, mask);
         else if (K < 32 || len <= 16 * kBpeThreads)
-            nl = merge_pass<(K < 16 ? 1 : 16), kWide>(s_tok, s_warp, len, table, mask);
-        else nl = merge_pass<K, kWide>(s_tok, s_warp, len, table, mask);
+            nl = merge_pass<(K < 16 ? 1 : 16), kBpeThreads, kWide>(s_tok, s_warp, len, table, mask);
+        else nl = merge_pass<K, kBpeThreads, kWide>(s_tok, s_warp, len, table, mask);
         if (nl == len) break;
         len = nl;
     }
@@ -290,6 +304,53 @@ __global__ void __launch_bounds__(kBpeThreads, K <= 8 ? 4 : 1) bpe_encode_kernel
             row[i] = i < len ? s_tok[i] : (i == len ? kEosId : kPadId);
     }
     if (tid == 0) out_len[b] = len + 1;
+}
+
+// Strings of at most 256 tokens (max_seq_len <= 257, the reference kernel's one-block domain):
+// one warp per string, 8 strings per block; passes synchronise the warp only.
+template <bool kWide>
+__global__ void __launch_bounds__(kBpeThreads, 4) bpe_encode_warp_kernel(
+    const typename PairSlot<kWide>::T* __restrict__ table, uint32_t mask, const uint8_t* __restrict__ bytes,
+    const int64_t* __restrict__ offsets, const int* __restrict__ lengths, int batch, int* __restrict__ out,
+    int* __restrict__ out_len, int max_seq_len, int* __restrict__ n_truncated) {
+    __shared__ __align__(16) int s_all[kBpeThreads / 32][kWarpTokens];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int b = blockIdx.x * (kBpeThreads / 32) + warp;
+    if (b >= batch) return;
+    int* s_tok = s_all[warp];
+    int len = max(lengths[b], 0);
+    if (len > max_seq_len - 1) {
+        if (lane == 0 && n_truncated) atomicAdd(n_truncated, 1);
+        len = max_seq_len - 1;
+    }
+    const uint8_t* src = bytes + offsets[b];
+    for (int i = lane; i < len; i += 32) s_tok[i] = (int)src[i] + kByteBase;
+    __syncwarp();
+    while (len > 1) {
+        int nl;
+        if (len <= 32) nl = merge_pass<1, 32, kWide>(s_tok, nullptr, len, table, mask);
+        else if (len <= 64) nl = merge_pass<2, 32, kWide>(s_tok, nullptr, len, table, mask);
+        else if (len <= 128) nl = merge_pass<4, 32, kWide>(s_tok, nullptr, len, table, mask);
+        else nl = merge_pass<8, 32, kWide>(s_tok, nullptr, len, table, mask);
+        if (nl == len) break;
+        len = nl;
+    }
+    int* row = out + (int64_t)b * max_seq_len;
+    if ((max_seq_len & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+        int4* row4 = reinterpret_cast<int4*>(row);
+        for (int q = lane; q < max_seq_len / 4; q += 32) {
+            int v4[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int i = 4 * q + j;
+                v4[j] = i < len ? s_tok[i] : (i == len ? kEosId : kPadId);
+            }
+            row4[q] = make_int4(v4[0], v4[1], v4[2], v4[3]);
+        }
+    } else {
+        for (int i = lane; i < max_seq_len; i += 32) row[i] = i < len ? s_tok[i] : (i == len ? kEosId : kPadId);
+    }
+    if (lane == 0) out_len[b] = len + 1;
 }
 
 // One warp per row.  ld > 0: rows ld tokens apart, at most ld read; ld == 0: row r at
@@ -375,6 +436,13 @@ int launch_encode_as(const rbk_bpe* t, const uint8_t* bytes, const int64_t* offs
                      int* out, int* out_len, int max_seq_len, int* n_truncated, cudaStream_t st) {
     using T = typename PairSlot<kWide>::T;
     const T* table = static_cast<const T*>(t->table);
+    if (max_seq_len - 1 <= kWarpTokens) {
+        const int per = kBpeThreads / 32;
+        bpe_encode_warp_kernel<kWide><<<(batch + per - 1) / per, kBpeThreads, 0, st>>>(
+            table, t->mask, bytes, offsets, lengths, batch, out, out_len, max_seq_len, n_truncated);
+        RBK_LAUNCHED("bpe_encode_warp_kernel");
+        return RBK_OK;
+    }
     const dim3 grid(batch), block(kBpeThreads);
     switch (encode_items(max_seq_len)) {
 #define RBK_BPE_CASE(K)                                                                                          \
@@ -382,7 +450,6 @@ int launch_encode_as(const rbk_bpe* t, const uint8_t* bytes, const int64_t* offs
         bpe_encode_kernel<K, kWide><<<grid, block, 0, st>>>(table, t->mask, bytes, offsets, lengths, out, out_len, \
                                                            max_seq_len, n_truncated);                            \
         break;
-        RBK_BPE_CASE(1)
         RBK_BPE_CASE(2)
         RBK_BPE_CASE(4)
         RBK_BPE_CASE(8)
