@@ -95,7 +95,7 @@ class GPUTokenizer:
 
     def encode_batch(self, strings, max_seq_len: int = MAX_SEQ_LEN, out=None, out_lengths=None):
         """Host strings -> (int32 [B, max_seq_len] rows, int32 [B] lengths) on the device."""
-        bs = [s.encode() if isinstance(s, str) else bytes(s) for s in strings]
+        bs = [s if isinstance(s, bytes) else (s.encode() if isinstance(s, str) else bytes(s)) for s in strings]
         B = len(bs)
         out = torch.empty(B, max_seq_len, dtype=torch.int32, device=f"cuda:{self.device}") if out is None else out
         out_lengths = torch.empty(B, dtype=torch.int32, device=out.device) if out_lengths is None else out_lengths
