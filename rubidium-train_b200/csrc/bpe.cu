@@ -255,7 +255,7 @@ __device__ __forceinline__ int merge_pass(int* s_tok, uint32_t* s_warp, int len,
 // Strings of up to 256 K tokens (max_seq_len - 1 <= 256 K).  Each pass runs with the fewest
 // positions per thread that cover the current length, so later, shorter passes cost less.
 template <int K, bool kWide>
-__global__ void __launch_bounds__(kBpeThreads, K <= 8 ? 4 : 1) bpe_encode_kernel(
+__global__ void __launch_bounds__(kBpeThreads, K <= 8 ? 5 : 1) bpe_encode_kernel(
     const typename PairSlot<kWide>::T* __restrict__ table, uint32_t mask, const uint8_t* __restrict__ bytes,
     const int64_t* __restrict__ offsets, const int* __restrict__ lengths, int* __restrict__ out,
     int* __restrict__ out_len, int max_seq_len, int* __restrict__ n_truncated) {
