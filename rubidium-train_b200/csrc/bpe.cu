@@ -175,8 +175,8 @@ __device__ __forceinline__ int merge_pass(int* s_tok, uint32_t* s_warp, int len,
     if (lane == 31) after = (p0 + C < len) ? s_tok[p0 + C] : -1;
     // pair lookups: the first probes of up to 8 positions in flight together
 #pragma unroll
-    for (int g = 0; g < C; g += 8) {
-        constexpr int G = C < 8 ? C : 8;
+    for (int g = 0; g < C; g += (C < 4 ? C : 4)) {
+        constexpr int G = C < 4 ? C : 4;
         typename S::T e[G];
         uint32_t idx[G];
 #pragma unroll
@@ -255,7 +255,7 @@ __device__ __forceinline__ int merge_pass(int* s_tok, uint32_t* s_warp, int len,
 // Strings of up to 256 K tokens (max_seq_len - 1 <= 256 K).  Each pass runs with the fewest
 // positions per thread that cover the current length, so later, shorter passes cost less.
 template <int K, bool kWide>
-__global__ void __launch_bounds__(kBpeThreads, K <= 8 ? 5 : 1) bpe_encode_kernel(
+__global__ void __launch_bounds__(kBpeThreads, K <= 8 ? 6 : 1) bpe_encode_kernel(
     const typename PairSlot<kWide>::T* __restrict__ table, uint32_t mask, const uint8_t* __restrict__ bytes,
     const int64_t* __restrict__ offsets, const int* __restrict__ lengths, int* __restrict__ out,
     int* __restrict__ out_len, int max_seq_len, int* __restrict__ n_truncated) {
@@ -310,7 +310,7 @@ __global__ void __launch_bounds__(kBpeThreads, K <= 8 ? 5 : 1) bpe_encode_kernel
 // Strings of at most 256 tokens (max_seq_len <= 257, the reference kernel's one-block domain):
 // one warp per string, 8 strings per block; passes synchronise the warp only.
 template <bool kWide>
-__global__ void __launch_bounds__(kBpeThreads, 4) bpe_encode_warp_kernel(
+__global__ void __launch_bounds__(kBpeThreads, 5) bpe_encode_warp_kernel(
     const typename PairSlot<kWide>::T* __restrict__ table, uint32_t mask, const uint8_t* __restrict__ bytes,
     const int64_t* __restrict__ offsets, const int* __restrict__ lengths, int batch, int* __restrict__ out,
     int* __restrict__ out_len, int max_seq_len, int* __restrict__ n_truncated) {
