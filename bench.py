@@ -466,7 +466,7 @@ def tokenizer_bench(torch, hbm_peak, cpu=True):
             del out
         if cpu:
             # oracle port (hash-map restatement, 1 thread) on a bounded sample
-            k = 256 if ms == 2048 else 2048
+            k = 2048 if ms == 2048 else 16384
             sd, so, sl = pack_strings(strs[:k])
             t0 = time.perf_counter()
             orow, orl, _ = oracle.bpe_encode(merges, sd, so, sl, ms)
@@ -475,7 +475,7 @@ def tokenizer_bench(torch, hbm_peak, cpu=True):
             ent["cpu_baseline_port"] = {"value": sd.size / dt / 1e6, "unit": "text MB/s", "cores": 1, "kind": "port",
                                         "sample": f"first {k} strings", "rows_equal_gpu": same}
             if ms == 256 and oracle.reftok_lib() is not None:
-                kr = 24
+                kr = 256
                 sd, so, sl = pack_strings(strs[:kr])
                 dt = oracle.ref_bpe_time_encode(merges, sd, so, sl, ms, 1)
                 ent["cpu_baseline_reference"] = {
@@ -639,29 +639,31 @@ def kernel_loop(name, reps, torch, ops):
         def fn():
             ops.adam_tail(p, gr, m, v, p16, sc, lr=1e-4)
         work, unit, peak = 34.0 * n, "GB/s", hbm
-    elif name in ("bpe_encode", "bpe_decode"):
+    elif name in ("bpe_encode", "bpe_encode_256", "bpe_decode"):
         # the GPU tokenizer: 16384 strings x 2047 bytes of synthetic text -> rows of 2048 tokens
-        # (33 MB in, 134 MB out), GPT-2-sized synthetic rule table; decode turns the rows back
+        # (33 MB in, 134 MB out), or 65536 x 254 bytes -> rows of 256 (bpe_encode_256, one warp
+        # per string), GPT-2-sized synthetic rule table; decode turns the 2048-token rows back
         from rbk.tokenizer import GPUTokenizer, pack_strings, synthetic_batch, synthetic_corpus, synthetic_tables
         vocab, merges, words = synthetic_tables()
         tk = GPUTokenizer(vocab, merges)
-        strs = synthetic_batch(synthetic_corpus(words, 1 << 25, seed=9), 16384, 2047, seed=4)
+        B, L, ms = (65536, 254, 256) if name == "bpe_encode_256" else (16384, 2047, 2048)
+        strs = synthetic_batch(synthetic_corpus(words, 1 << 25, seed=9), B, L, seed=4)
         data, offs, lens = pack_strings(strs)
         dd, do, dl = (torch.from_numpy(a.copy()).cuda() for a in (data, offs, lens))
-        rows = torch.empty(16384, 2048, dtype=torch.int32, device="cuda")
-        rl = torch.empty(16384, dtype=torch.int32, device="cuda")
-        tk.encode(dd, do, dl, 2048, out=rows, out_lengths=rl)
-        sout = torch.empty(16384, 4096, dtype=torch.uint8, device="cuda")
+        rows = torch.empty(B, ms, dtype=torch.int32, device="cuda")
+        rl = torch.empty(B, dtype=torch.int32, device="cuda")
+        tk.encode(dd, do, dl, ms, out=rows, out_lengths=rl)
+        sout = torch.empty(B, 4096, dtype=torch.uint8, device="cuda") if name == "bpe_decode" else None
 
         def fn():
-            if name == "bpe_encode":
-                tk.encode(dd, do, dl, 2048, out=rows, out_lengths=rl)
-            else:
+            if name == "bpe_decode":
                 tk.decode_batch(rows, rl, 4096, out=sout)
+            else:
+                tk.encode(dd, do, dl, ms, out=rows, out_lengths=rl)
         # algorithmic bytes: text + offsets + lengths in, full rows + lengths out (encode); tokens up
         # to the EOS + lengths in, text + NULs out (decode)
-        work = data.size + 16384 * (12 + 4 * 2048 + 4) if name == "bpe_encode" else \
-            4 * int(rl.sum().item()) + 16384 * 5 + data.size
+        work = data.size + B * (12 + 4 * ms + 4) if name != "bpe_decode" else \
+            4 * int(rl.sum().item()) + B * 5 + data.size
         unit, peak = "GB/s", hbm
     else:
         raise SystemExit(f"unknown kernel {name}")
@@ -957,7 +959,7 @@ def main():
                          "rank's slices, FP16 all-gather); 0: all-reduce and the whole tail on every rank")
     ap.add_argument("--kernel", default=None,
                     help="loop one kernel instead of the training step (gemm_* of gemm_shapes(), ln_bwd, xent, "
-                         "attn_fwd, attn_bwd, adam_tail, bpe_encode, bpe_decode)")
+                         "attn_fwd, attn_bwd, adam_tail, bpe_encode, bpe_encode_256, bpe_decode)")
     args = ap.parse_args()
     if args.kernel:
         import torch
