@@ -173,7 +173,8 @@ __device__ __forceinline__ int merge_pass(int* s_tok, uint32_t* s_warp, int len,
     // would be a C-way bank conflict); the warp's last lane reads it
     int after = __shfl_down_sync(0xffffffffu, t[0], 1);
     if (lane == 31) after = (p0 + C < len) ? s_tok[p0 + C] : -1;
-    // pair lookups: the first probes of up to 8 positions in flight together
+    // pair lookups: the first probes of up to 4 positions in flight together (more costs registers,
+    // and so blocks per SM)
 #pragma unroll
     for (int g = 0; g < C; g += (C < 4 ? C : 4)) {
         constexpr int G = C < 4 ? C : 4;
