@@ -600,7 +600,9 @@ int rbk_bpe_num_rules(const rbk_bpe* t);
  * than max_seq_len - 1 bytes is rejected with RBK_ERR_INVALID before anything
  * runs (the reference writes past its row); one of exactly max_seq_len - 1
  * bytes is merged like any other (the reference skips its merges).
- * 2 <= max_seq_len <= 8193. */
+ * 2 <= max_seq_len <= 8193.  Large batches (>= 4096 strings, >= 8 MiB of text) are
+ * staged and encoded in four parts, each part's copy and launch overlapping the host
+ * packing of the next. */
 int rbk_bpe_encode_batch(rbk_bpe* t, const char* const* strings, int batch, int* out_tokens, int* out_lengths,
                          int max_seq_len, void* stream);
 /* The same encode over strings already on the device: string b is

@@ -635,15 +635,34 @@ int rbk_bpe_encode_batch(rbk_bpe* t, const char* const* strings, int batch, int*
     RBK_REQUIRE(out_tokens && out_lengths, "rbk_bpe_encode_batch: null output");
     RBK_TRY(check_device(t));
     // staging layout: offsets (int64) | lengths (int32, padded to 8 bytes) | bytes
+    for (int b = 0; b < batch; ++b) RBK_REQUIRE(strings[b], "rbk_bpe_encode_batch: string %d is null", b);
+    // String lengths, then (below) the copy into pinned memory: both in slices on several host
+    // threads for large batches (one core scans or copies ~10 GB/s, below what the copy engine
+    // takes).  A length above the row is kept as -1 and rejected before anything is staged.
+    const int nthr = batch >= 1024 ? (int)std::min<unsigned>(8u, std::max(1u, std::thread::hardware_concurrency())) : 1;
+    auto in_slices = [&](auto&& fn) {
+        if (nthr == 1) {
+            fn(0, batch);
+            return;
+        }
+        std::vector<std::thread> pool;
+        for (int k = 1; k < nthr; ++k)
+            pool.emplace_back(fn, (int)((int64_t)batch * k / nthr), (int)((int64_t)batch * (k + 1) / nthr));
+        fn(0, (int)((int64_t)batch / nthr));
+        for (auto& th : pool) th.join();
+    };
     std::vector<int> len(batch);
+    in_slices([&](int b0, int b1) {
+        for (int b = b0; b < b1; ++b) {
+            const size_t l = strlen(strings[b]);
+            len[b] = l <= (size_t)max_seq_len - 1 ? (int)l : -1;
+        }
+    });
     size_t total = 0;
     for (int b = 0; b < batch; ++b) {
-        RBK_REQUIRE(strings[b], "rbk_bpe_encode_batch: string %d is null", b);
-        const size_t l = strlen(strings[b]);
-        RBK_REQUIRE(l <= (size_t)max_seq_len - 1, "rbk_bpe_encode_batch: string %d has %zu bytes, above max_seq_len - 1 = %d",
-                    b, l, max_seq_len - 1);
-        len[b] = (int)l;
-        total += l;
+        RBK_REQUIRE(len[b] >= 0, "rbk_bpe_encode_batch: string %d has %zu bytes, above max_seq_len - 1 = %d", b,
+                    strlen(strings[b]), max_seq_len - 1);
+        total += len[b];
     }
     const size_t off_bytes = sizeof(int64_t) * batch, len_bytes = (sizeof(int) * batch + 7) / 8 * 8;
     const size_t need = off_bytes + len_bytes + std::max<size_t>(total, 1);
@@ -676,26 +695,38 @@ int rbk_bpe_encode_batch(rbk_bpe* t, const char* const* strings, int batch, int*
         h_len[b] = len[b];
         pos += len[b];
     }
-    // the text into pinned memory: in slices on several host threads when there is a lot of it
-    // (one core copies ~10 GB/s, below what the copy engine takes)
-    auto pack = [&](int b0, int b1) {
-        for (int b = b0; b < b1; ++b) memcpy(h_bytes + h_off[b], strings[b], len[b]);
-    };
-    const int nthr = total >= ((size_t)8 << 20) ? (int)std::min<unsigned>(8u, std::max(1u, std::thread::hardware_concurrency())) : 1;
-    if (nthr > 1) {
-        std::vector<std::thread> pool;
-        for (int k = 1; k < nthr; ++k)
-            pool.emplace_back(pack, (int)((int64_t)batch * k / nthr), (int)((int64_t)batch * (k + 1) / nthr));
-        pack(0, (int)((int64_t)batch / nthr));
-        for (auto& th : pool) th.join();
-    } else {
-        pack(0, batch);
-    }
+    // Offsets and lengths first; then the text in up to four parts: part p + 1 is packed on the
+    // host while part p is copied and encoded (strings are independent: each part is one launch).
     cudaStream_t st = as_stream(stream);
-    RBK_CUDA(cudaMemcpyAsync(s.dev, s.host, off_bytes + len_bytes + total, cudaMemcpyHostToDevice, st));
-    const int rc = launch_encode(t, s.dev + off_bytes + len_bytes, reinterpret_cast<const int64_t*>(s.dev),
-                                 reinterpret_cast<const int*>(s.dev + off_bytes), batch, out_tokens, out_lengths,
-                                 max_seq_len, nullptr, st);
+    RBK_CUDA(cudaMemcpyAsync(s.dev, s.host, off_bytes + len_bytes, cudaMemcpyHostToDevice, st));
+    const int parts = (batch >= 4096 && total >= ((size_t)8 << 20)) ? 4 : 1;
+    const int64_t* d_off = reinterpret_cast<const int64_t*>(s.dev);
+    const int* d_len = reinterpret_cast<const int*>(s.dev + off_bytes);
+    int rc = RBK_OK;
+    for (int p = 0; p < parts && rc == RBK_OK; ++p) {
+        const int b0 = (int)((int64_t)batch * p / parts), b1 = (int)((int64_t)batch * (p + 1) / parts);
+        if (b1 == b0) continue;
+        const int n = b1 - b0;
+        const int pthr = n >= 1024 ? nthr : 1;
+        auto copy = [&](int c0, int c1) {
+            for (int b = b0 + c0; b < b0 + c1; ++b) memcpy(h_bytes + h_off[b], strings[b], len[b]);
+        };
+        if (pthr == 1) {
+            copy(0, n);
+        } else {
+            std::vector<std::thread> pool;
+            for (int k = 1; k < pthr; ++k)
+                pool.emplace_back(copy, (int)((int64_t)n * k / pthr), (int)((int64_t)n * (k + 1) / pthr));
+            copy(0, (int)((int64_t)n / pthr));
+            for (auto& th : pool) th.join();
+        }
+        const size_t lo = (size_t)h_off[b0], hi = (size_t)h_off[b1 - 1] + len[b1 - 1];
+        if (hi > lo)
+            RBK_CUDA(cudaMemcpyAsync(s.dev + off_bytes + len_bytes + lo, h_bytes + lo, hi - lo, cudaMemcpyHostToDevice,
+                                     st));
+        rc = launch_encode(t, s.dev + off_bytes + len_bytes, d_off + b0, d_len + b0, n,
+                           out_tokens + (int64_t)b0 * max_seq_len, out_lengths + b0, max_seq_len, nullptr, st);
+    }
     RBK_CUDA(cudaEventRecord(s.done, st));
     s.live = true;
     return rc;

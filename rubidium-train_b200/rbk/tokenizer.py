@@ -94,12 +94,13 @@ class GPUTokenizer:
             pass
 
     def encode_batch(self, strings, max_seq_len: int = MAX_SEQ_LEN, out=None, out_lengths=None):
-        """Host strings -> (int32 [B, max_seq_len] rows, int32 [B] lengths) on the device."""
-        bs = [s if isinstance(s, bytes) else (s.encode() if isinstance(s, str) else bytes(s)) for s in strings]
-        B = len(bs)
+        """Host strings -> (int32 [B, max_seq_len] rows, int32 [B] lengths) on the device.
+        `strings`: a list of str/bytes, or the array host_strings() made from one (building
+        that array of 16K C pointers costs Python several ms; reuse it when encoding again)."""
+        arr = strings if isinstance(strings, C.Array) else host_strings(strings)
+        B = len(arr) if len(arr) != 1 or arr[0] is not None else 0
         out = torch.empty(B, max_seq_len, dtype=torch.int32, device=f"cuda:{self.device}") if out is None else out
         out_lengths = torch.empty(B, dtype=torch.int32, device=out.device) if out_lengths is None else out_lengths
-        arr = (C.c_char_p * max(B, 1))(*bs)
         call("rbk_bpe_encode_batch", self._h, arr, B, _vp(out), _vp(out_lengths), max_seq_len, _stream())
         return out, out_lengths
 
@@ -133,6 +134,14 @@ class GPUTokenizer:
         n = torch.tensor([t.shape[1]], dtype=torch.int32, device=t.device)
         raw = self.decode_batch(t, n, DECODE_STRING_LEN, ld=max(t.shape[1], 1)).cpu().numpy()[0].tobytes()
         return raw.split(b"\0", 1)[0].decode(errors="replace")
+
+
+def host_strings(strings):
+    """The char** a C caller of rbk_bpe_encode_batch holds: a ctypes array of C pointers to
+    the strings (str is UTF-8 encoded; the array keeps the bytes objects alive).  An empty
+    list gives a one-entry array holding NULL."""
+    bs = [s if isinstance(s, bytes) else (s.encode() if isinstance(s, str) else bytes(s)) for s in strings]
+    return (C.c_char_p * max(len(bs), 1))(*bs) if bs else (C.c_char_p * 1)(None)
 
 
 def strings_from_rows(raw: np.ndarray):

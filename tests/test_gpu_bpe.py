@@ -206,6 +206,25 @@ def test_full_size_round_trip_and_oracle_sample(big):
     assert np.array_equal(rl[sample], wl) and np.array_equal(rows[sample], want)
 
 
+def test_host_string_entry_in_parts_matches_device_entry(big):
+    """A host-string batch large enough (4200 strings, 8.6 MB) to be staged and encoded in four
+    parts, the text of part p + 1 packed while part p is copied and encoded: rows and lengths
+    equal the device entry's, and a reused pointer array gives the same again."""
+    from rbk.tokenizer import host_strings, pack_strings, synthetic_batch
+    t, _, _, corpus = big
+    strs = synthetic_batch(corpus, 4200, 2047, seed=5)
+    strs[7] = b""
+    strs[3000] = strs[3000][:5]
+    data, offs, lens = pack_strings(strs)
+    assert data.size >= 8 << 20           # the size at which the entry stages in parts
+    want, wl = encode_dev(t, data, offs, lens, 2048)
+    arr = host_strings(strs)
+    for _ in range(2):
+        rows, rl = t.encode_batch(arr, 2048)
+        torch.cuda.synchronize()
+        assert np.array_equal(rl.cpu().numpy(), wl) and np.array_equal(rows.cpu().numpy(), want)
+
+
 def test_encode_string_decode_tokens(big):
     """The single-string helpers (encode_string / decode_tokens, tokenizer_cuda.cu:350-389)."""
     t, _, _, corpus = big
