@@ -22,9 +22,8 @@
 //     above that: one L1/L2 load answers almost every lookup, and duplicate pairs keep the first
 //     rule because the host inserts in rule order and skips pairs already present;
 //   - one CTA of 256 threads owns a string (one warp, for rows of at most 257 tokens); each
-//     pass is data-parallel: every thread looks
-//     up the pairs of its chunk of positions, and the greedy left-to-right choice becomes a
-//     prefix computation.  Whether position p is consumed depends only on whether the pair
+//     pass is data-parallel: every thread looks up the pairs of its chunk of positions, and
+//     the greedy left-to-right choice becomes a prefix computation.  Whether position p is consumed depends only on whether the pair
 //     at p-1 merged, so a chunk is a map of that one-bit state (2 bits) together with how
 //     many tokens it emits for either input state; composing these maps is associative, so
 //     one block-wide scan of a packed 32-bit value gives every thread its input state and
