@@ -34,10 +34,68 @@
 // lengths gives every token its output position, and each lane copies its token's bytes.
 // Only if a token would overflow the row does the rest of the row fall back to one lane
 // (the reference's skip-and-continue rule is inherently sequential).
+#include <condition_variable>
+#include <functional>
+#include <memory>
+#include <mutex>
 #include <thread>
 #include <vector>
 
 #include "common.cuh"
+
+// Host threads that pack the strings of large rbk_bpe_encode_batch calls, started on the first
+// such call and kept until the handle is destroyed (spawning threads per call costs ~0.1-0.3 ms
+// a round).  run(fn) calls fn(k) for k = 0 .. workers, the calling thread taking the last one.
+struct rbk_bpe_pool {
+    std::vector<std::thread> threads;
+    std::mutex mu;
+    std::condition_variable wake, idle;
+    std::function<void(int)> job;
+    unsigned gen = 0;
+    int pending = 0;
+    bool stop = false;
+
+    explicit rbk_bpe_pool(int workers) {
+        for (int k = 0; k < workers; ++k)
+            threads.emplace_back([this, k] {
+                unsigned seen = 0;
+                for (;;) {
+                    std::function<void(int)> fn;
+                    {
+                        std::unique_lock<std::mutex> lk(mu);
+                        wake.wait(lk, [&] { return stop || gen != seen; });
+                        if (stop) return;
+                        seen = gen;
+                        fn = job;
+                    }
+                    fn(k);
+                    std::lock_guard<std::mutex> lk(mu);
+                    if (--pending == 0) idle.notify_one();
+                }
+            });
+    }
+    int workers() const { return (int)threads.size(); }
+    void run(const std::function<void(int)>& fn) {
+        {
+            std::lock_guard<std::mutex> lk(mu);
+            job = fn;
+            pending = workers();
+            ++gen;
+        }
+        wake.notify_all();
+        fn(workers());
+        std::unique_lock<std::mutex> lk(mu);
+        idle.wait(lk, [&] { return pending == 0; });
+    }
+    ~rbk_bpe_pool() {
+        {
+            std::lock_guard<std::mutex> lk(mu);
+            stop = true;
+        }
+        wake.notify_all();
+        for (auto& t : threads) t.join();
+    }
+};
 
 struct rbk_bpe {
     int device = 0;
@@ -57,6 +115,7 @@ struct rbk_bpe {
         bool live = false;
     } slot[2];
     int next_slot = 0;
+    std::unique_ptr<rbk_bpe_pool> pool;  // host packing threads (large batches)
 };
 
 namespace rbk {
@@ -521,6 +580,7 @@ void free_slot(rbk_bpe::Slot& s) {
 }
 
 void free_bpe(rbk_bpe* t) {
+    t->pool.reset();
     for (auto& s : t->slot) free_slot(s);
     if (t->table) cudaFree(t->table);
     if (t->inv) cudaFree(t->inv);
@@ -635,21 +695,26 @@ int rbk_bpe_encode_batch(rbk_bpe* t, const char* const* strings, int batch, int*
     RBK_TRY(check_device(t));
     // staging layout: offsets (int64) | lengths (int32, padded to 8 bytes) | bytes
     for (int b = 0; b < batch; ++b) RBK_REQUIRE(strings[b], "rbk_bpe_encode_batch: string %d is null", b);
-    // String lengths, then (below) the copy into pinned memory: both in slices on several host
-    // threads for large batches (one core scans or copies ~10 GB/s, below what the copy engine
+    // String lengths, then (below) the copy into pinned memory: both in slices on the handle's
+    // host threads for large batches (one core scans or copies ~10 GB/s, below what the copy engine
     // takes).  A length above the row is kept as -1 and rejected before anything is staged.
-    const int nthr = batch >= 1024 ? (int)std::min<unsigned>(8u, std::max(1u, std::thread::hardware_concurrency())) : 1;
-    auto in_slices = [&](auto&& fn) {
-        if (nthr == 1) {
-            fn(0, batch);
+    int nthr = 1;
+    if (batch >= 1024) {
+        if (!t->pool) {
+            const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+            t->pool.reset(new rbk_bpe_pool((int)std::min<unsigned>(8u, hw) - 1));
+        }
+        nthr = t->pool->workers() + 1;
+    }
+    // fn(b0, b1) over nthr slices of [0, n), on the pool when there is more than one
+    auto slices = [&](int n, const std::function<void(int, int)>& fn) {
+        if (nthr == 1 || n < 1024) {
+            fn(0, n);
             return;
         }
-        std::vector<std::thread> pool;
-        for (int k = 1; k < nthr; ++k)
-            pool.emplace_back(fn, (int)((int64_t)batch * k / nthr), (int)((int64_t)batch * (k + 1) / nthr));
-        fn(0, (int)((int64_t)batch / nthr));
-        for (auto& th : pool) th.join();
+        t->pool->run([&](int k) { fn((int)((int64_t)n * k / nthr), (int)((int64_t)n * (k + 1) / nthr)); });
     };
+    auto in_slices = [&](const std::function<void(int, int)>& fn) { slices(batch, fn); };
     std::vector<int> len(batch);
     in_slices([&](int b0, int b1) {
         for (int b = b0; b < b1; ++b) {
@@ -706,19 +771,9 @@ int rbk_bpe_encode_batch(rbk_bpe* t, const char* const* strings, int batch, int*
         const int b0 = (int)((int64_t)batch * p / parts), b1 = (int)((int64_t)batch * (p + 1) / parts);
         if (b1 == b0) continue;
         const int n = b1 - b0;
-        const int pthr = n >= 1024 ? nthr : 1;
-        auto copy = [&](int c0, int c1) {
+        slices(n, [&](int c0, int c1) {
             for (int b = b0 + c0; b < b0 + c1; ++b) memcpy(h_bytes + h_off[b], strings[b], len[b]);
-        };
-        if (pthr == 1) {
-            copy(0, n);
-        } else {
-            std::vector<std::thread> pool;
-            for (int k = 1; k < pthr; ++k)
-                pool.emplace_back(copy, (int)((int64_t)n * k / pthr), (int)((int64_t)n * (k + 1) / pthr));
-            copy(0, (int)((int64_t)n / pthr));
-            for (auto& th : pool) th.join();
-        }
+        });
         const size_t lo = (size_t)h_off[b0], hi = (size_t)h_off[b1 - 1] + len[b1 - 1];
         if (hi > lo)
             RBK_CUDA(cudaMemcpyAsync(s.dev + off_bytes + len_bytes + lo, h_bytes + lo, hi - lo, cudaMemcpyHostToDevice,
