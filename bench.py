@@ -473,15 +473,24 @@ def tokenizer_bench(torch, hbm_peak, cpu=True):
             res["decode_2048"] = ent_dec
             del out
         if cpu:
-            # oracle port (hash-map restatement, 1 thread) on a bounded sample
+            # oracle port (hash-map restatement) on bounded samples: one thread, then every core
+            # (strings in parallel); its rows are checked against the GPU's
             k = 2048 if ms == 2048 else 16384
             sd, so, sl = pack_strings(strs[:k])
+            oracle.set_threads(1)
             t0 = time.perf_counter()
             orow, orl, _ = oracle.bpe_encode(merges, sd, so, sl, ms)
             dt = time.perf_counter() - t0
             same = bool(np.array_equal(orl, rl[:k].cpu().numpy()) and np.array_equal(orow, rows[:k].cpu().numpy()))
             ent["cpu_baseline_port"] = {"value": sd.size / dt / 1e6, "unit": "text MB/s", "cores": 1, "kind": "port",
                                         "sample": f"first {k} strings", "rows_equal_gpu": same}
+            cores = cpu_threads()
+            sd, so, sl = pack_strings(strs)
+            t0 = time.perf_counter()
+            oracle.bpe_encode(merges, sd, so, sl, ms)
+            dt = time.perf_counter() - t0
+            ent["cpu_baseline_port_all_cores"] = {"value": sd.size / dt / 1e6, "unit": "text MB/s", "cores": cores,
+                                                  "kind": "port", "sample": f"all {B} strings ({dt:.1f} s)"}
             if ms == 256 and oracle.reftok_lib() is not None:
                 kr = 256
                 sd, so, sl = pack_strings(strs[:kr])

@@ -97,23 +97,30 @@ int ora_bpe_encode(const int* m_first, const int* m_second, const int* m_result,
                    const unsigned char* bytes, const int64_t* offsets, const int* lengths, int batch, int* out,
                    int* out_len, int max_seq_len, int* n_truncated) {
     if (max_seq_len < 2 || batch < 0 || n_merges < 0) return -1;
+    for (int b = 0; b < batch; ++b)
+        if (lengths[b] < 0) return -1;
     const Rules rules(m_first, m_second, m_result, n_merges);
-    std::vector<int> tok, nxt;
     int cut = 0;
-    for (int b = 0; b < batch; ++b) {
-        int len = lengths[b];
-        if (len < 0) return -1;
-        if (len > max_seq_len - 1) {
-            len = max_seq_len - 1;
-            ++cut;
+    // strings are independent: one per OpenMP iteration (the thread count follows OMP_NUM_THREADS
+    // or ora_set_threads)
+#pragma omp parallel reduction(+ : cut)
+    {
+        std::vector<int> tok, nxt;
+#pragma omp for schedule(dynamic, 16)
+        for (int b = 0; b < batch; ++b) {
+            int len = lengths[b];
+            if (len > max_seq_len - 1) {
+                len = max_seq_len - 1;
+                ++cut;
+            }
+            encode_one(rules, bytes + offsets[b], len, tok, nxt);
+            int* row = out + (size_t)b * max_seq_len;
+            const int n = (int)tok.size();
+            std::memcpy(row, tok.data(), sizeof(int) * n);
+            row[n] = kEos;
+            for (int i = n + 1; i < max_seq_len; ++i) row[i] = kPad;
+            out_len[b] = n + 1;
         }
-        encode_one(rules, bytes + offsets[b], len, tok, nxt);
-        int* row = out + (size_t)b * max_seq_len;
-        const int n = (int)tok.size();
-        std::memcpy(row, tok.data(), sizeof(int) * n);
-        row[n] = kEos;
-        for (int i = n + 1; i < max_seq_len; ++i) row[i] = kPad;
-        out_len[b] = n + 1;
     }
     if (n_truncated) *n_truncated = cut;
     return 0;
