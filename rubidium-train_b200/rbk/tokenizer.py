@@ -3,6 +3,7 @@ reference's host API names (src/tokenizer_cuda.h:120-164):
 
     tok = GPUTokenizer(vocab, merges)            # tokenizer_copy_to_device
     toks, lens = tok.encode_batch(strings, 2048) # encode_batch (host strings -> device rows)
+    arr = host_strings(strings)                  # the char** once, reused by later encode_batch calls
     toks, lens = tok.encode(bytes, offs, lens_in, 2048)  # the same, inputs already on the device
     out = tok.decode_batch(toks, lens, 1024)     # decode_batch (device rows -> device strings)
     ids = tok.encode_string("text")              # encode_string
