@@ -55,24 +55,33 @@ struct rbk_bpe_pool {
     int pending = 0;
     bool stop = false;
 
+    // as many workers as the system grants, up to `workers` (none: the caller packs alone)
     explicit rbk_bpe_pool(int workers) {
-        for (int k = 0; k < workers; ++k)
-            threads.emplace_back([this, k] {
-                unsigned seen = 0;
-                for (;;) {
-                    std::function<void(int)> fn;
-                    {
-                        std::unique_lock<std::mutex> lk(mu);
-                        wake.wait(lk, [&] { return stop || gen != seen; });
-                        if (stop) return;
-                        seen = gen;
-                        fn = job;
-                    }
-                    fn(k);
-                    std::lock_guard<std::mutex> lk(mu);
-                    if (--pending == 0) idle.notify_one();
+        for (int k = 0; k < workers; ++k) {
+            try {
+                spawn(k);
+            } catch (...) {
+                break;
+            }
+        }
+    }
+    void spawn(int k) {
+        threads.emplace_back([this, k] {
+            unsigned seen = 0;
+            for (;;) {
+                std::function<void(int)> fn;
+                {
+                    std::unique_lock<std::mutex> lk(mu);
+                    wake.wait(lk, [&] { return stop || gen != seen; });
+                    if (stop) return;
+                    seen = gen;
+                    fn = job;
                 }
-            });
+                fn(k);
+                std::lock_guard<std::mutex> lk(mu);
+                if (--pending == 0) idle.notify_one();
+            }
+        });
     }
     int workers() const { return (int)threads.size(); }
     void run(const std::function<void(int)>& fn) {
